@@ -1,0 +1,233 @@
+"""CPU oracle for the block-quantized linear path (TEST INFRASTRUCTURE ONLY).
+
+Wraps ``liboracle.so`` (qlinear_oracle.c, a C restatement of the reference's
+CUDA arithmetic) and, when built, ``_ref/libref_local_llm.so`` (the reference's
+own CUDA kernels compiled from its sources for sm_100a).  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may import
+this package; the product library never does.
+
+Parity status: pinned by the reference's known-answer tests
+(test/LaunchAddTest.cpp), by gguf-py 0.19.0 vectors, and on a GPU bit for bit
+against the reference's own kernels.  Q4_0 is pinned by gguf-py only (the
+reference has no Q4_0 arithmetic).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_LIB_PATH = os.path.join(HERE, "_ref", "libref_local_llm.so")
+
+# GGML type codes (reference src/tensor/TensorCommon.h:15-33)
+F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 6, 8, 12, 14
+BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q5_0: (32, 22), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+NAMES = {Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", F16: "F16", F32: "F32"}
+
+
+def row_bytes(t: int, k: int) -> int:
+    be, bb = BLOCK[t]
+    assert k % be == 0, (t, k)
+    return k // be * bb
+
+
+def build() -> None:
+    """Compile liboracle.so (and _ref when the reference sources are present)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        P, I, I64, U64, SZ, F = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
+        sig = {
+            "orc_f16_to_f32": (F, [C.c_uint16]),
+            "orc_f32_to_f16": (C.c_uint16, [F]),
+            "orc_dequant_rows_f32": (I, [I, P, SZ, I64, I, P]),
+            "orc_dequant_f16": (I, [I, P, I64, P]),
+            "orc_gemv": (I, [I, P, SZ, P, P, I, I, I, I]),
+            "orc_gemv_add": (I, [I, P, SZ, P, P, I, I, I]),
+            "orc_swiglu": (I, [I, P, P, SZ, SZ, P, P, I, I, I]),
+            "orc_swiglu_indexed": (I, [I, P, P, SZ, SZ, SZ, SZ, P, P, P, I, I, I, I]),
+            "orc_down_indexed_ordered": (I, [I, P, SZ, SZ, P, P, P, P, I, I, I, I]),
+            "orc_router_topk": (I, [P, P, P, I, I, I, F]),
+            "orc_argmax": (I, [P, I]),
+            "orc_rmsnorm": (None, [P, P, P, I, I, F]),
+            "orc_embedding": (I, [I, P, P, P, SZ, I, I]),
+            "orc_quantize_rows": (I, [I, P, I64, I, P]),
+            "orc_randn": (None, [U64, U64, I64, F, P]),
+            "orc_num_threads": (I, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _ok(rc):
+    if rc != 0:
+        raise ValueError(f"oracle call rejected its arguments (rc={rc})")
+
+
+def randn(seed: int, n: int, std: float = 1.0, offset: int = 0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().orc_randn(seed, offset, n, std, _p(out))
+    return out
+
+
+def quantize(t: int, x: np.ndarray) -> np.ndarray:
+    x = _c(x, np.float32)
+    rows, k = x.shape
+    out = np.empty((rows, row_bytes(t, k)), np.uint8)
+    _ok(lib().orc_quantize_rows(t, _p(x), rows, k, _p(out)))
+    return out
+
+
+def dequant_rows(t: int, w: np.ndarray, k: int, rb: int | None = None) -> np.ndarray:
+    w = _c(w, np.uint8)
+    rb = rb if rb is not None else row_bytes(t, k)
+    rows = w.size // rb
+    out = np.empty((rows, k), np.float32)
+    _ok(lib().orc_dequant_rows_f32(t, _p(w), rb, rows, k, _p(out)))
+    return out
+
+
+def dequant_f16(t: int, src: np.ndarray, n: int) -> np.ndarray:
+    src = _c(src, np.uint8)
+    out = np.empty(n, np.uint16)
+    _ok(lib().orc_dequant_f16(t, _p(src), n, _p(out)))
+    return out
+
+
+def gemv(t, w, rb, x, n, k, m, order=0):
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.empty((m, n), np.float32)
+    _ok(lib().orc_gemv(t, _p(w), rb, _p(x), _p(y), n, k, m, order))
+    return y
+
+
+def gemv_add(t, w, rb, x, y, n, k, order=0):
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.array(y, np.float32, copy=True)
+    _ok(lib().orc_gemv_add(t, _p(w), rb, _p(x), _p(y), n, k, order))
+    return y
+
+
+def swiglu(t, g, u, grb, urb, x, f, k, order=0):
+    g, u, x = _c(g, np.uint8), _c(u, np.uint8), _c(x, np.float32)
+    act = np.empty(f, np.float32)
+    _ok(lib().orc_swiglu(t, _p(g), _p(u), grb, urb, _p(x), _p(act), f, k, order))
+    return act
+
+
+def swiglu_indexed(t, g, u, geb, ueb, grb, urb, x, ids, k, f, kin, order=0):
+    g, u, x = _c(g, np.uint8), _c(u, np.uint8), _c(x, np.float32)
+    ids = _c(ids, np.int32)
+    act = np.empty((k, f), np.float32)
+    _ok(lib().orc_swiglu_indexed(t, _p(g), _p(u), geb, ueb, grb, urb, _p(x), _p(ids), _p(act), k, f, kin, order))
+    return act
+
+
+def down_indexed_ordered(t, d, deb, drb, act, ids, rw, out, k, h, f, order=0):
+    d, act = _c(d, np.uint8), _c(act, np.float32)
+    ids, rw = _c(ids, np.int32), _c(rw, np.float32)
+    out = np.array(out, np.float32, copy=True)
+    _ok(lib().orc_down_indexed_ordered(t, _p(d), deb, drb, _p(act), _p(ids), _p(rw), _p(out), k, h, f, order))
+    return out
+
+
+def router_topk(logits, k, scale):
+    logits = _c(logits, np.float32)
+    t, e = logits.shape
+    idx = np.empty((t, k), np.int32)
+    w = np.empty((t, k), np.float32)
+    _ok(lib().orc_router_topk(_p(logits), _p(idx), _p(w), t, e, k, scale))
+    return idx, w
+
+
+def argmax(v) -> int:
+    v = _c(v, np.float32)
+    return int(lib().orc_argmax(_p(v), v.size))
+
+
+def rmsnorm(x, gamma, eps):
+    x = _c(x, np.float32)
+    rows, h = x.reshape(-1, x.shape[-1]).shape
+    y = np.empty_like(x)
+    g = _c(gamma, np.float32) if gamma is not None else None
+    lib().orc_rmsnorm(_p(x), _p(y), _p(g) if g is not None else None, rows, h, eps)
+    return y
+
+
+def embedding(t, ids, table, rb, h):
+    ids, table = _c(ids, np.int32), _c(table, np.uint8)
+    out = np.empty((ids.size, h), np.float32)
+    _ok(lib().orc_embedding(t, _p(ids), _p(out), _p(table), rb, h, ids.size))
+    return out
+
+
+def num_threads() -> int:
+    return int(lib().orc_num_threads())
+
+
+def f16_bits_to_f32(bits) -> np.ndarray:
+    return np.asarray(bits, np.uint16).view(np.float16).astype(np.float32)
+
+
+# ----------------------------------------------------------------------------
+# The reference's own CUDA kernels (GPU only; built into _ref/ from the
+# reference sources).  Arguments are raw device pointers (ints).
+# ----------------------------------------------------------------------------
+_ref = None
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_LIB_PATH):
+            return None
+        L = C.CDLL(REF_LIB_PATH)
+        P, I, I64, SZ, F = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
+        sig = {
+            "ref_set_stream": (I, [P]),
+            "ref_last_error": (I, []),
+            "ref_quant_gemv": (None, [I, P, SZ, P, P, I, I, I]),
+            "ref_quant_gemv_add": (None, [I, P, SZ, P, P, I, I]),
+            "ref_quant_matmul": (None, [I, P, SZ, P, P, I, I, I]),
+            "ref_quant_swiglu": (None, [I, P, P, SZ, SZ, P, P, I, I]),
+            "ref_quant_swiglu_indexed": (None, [I, P, P, SZ, SZ, SZ, SZ, P, P, P, I, I, I]),
+            "ref_quant_down_ordered": (None, [I, P, SZ, SZ, P, P, P, P, I, I, I]),
+            "ref_moe_router_topk": (None, [P, P, P, I, I, I, F]),
+            "ref_quant_embedding": (None, [I, P, P, P, SZ, I, I]),
+            "ref_argmax": (None, [P, I, P]),
+            "ref_dequantize_q4k": (None, [P, P, I64]),
+            "ref_dequantize_q80": (None, [P, P, I64]),
+            "ref_dequantize_q50": (None, [P, P, I64]),
+            "ref_dequantize_q6k": (None, [P, P, I64]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _ref = L
+    return _ref
