@@ -1,0 +1,421 @@
+"""Benchmark: Qwen2-7B-shape Q4_K decode through the block-quantized linear path.
+
+One step = one decode token of every quantized linear of a Qwen2-7B-shape
+decoder (28 layers x {q, k, v, o, gate, up, down} + LM head) at batch 1 on
+synthetic random-init weights: RMSNorm fused into the q/k/v and gate/up
+GEMVs, SwiGLU fused into gate/up, residual adds fused into o/down, then the
+LM head and a greedy argmax.  Attention itself is outside the measured path
+(the attention output is stood in by the q projection, which has o_proj's
+input width), so the step reads exactly the 3.977 GB of quantized weights a
+real decode token reads.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (torchrun, one rank per GPU) the stack is tensor-parallel:
+q/k/v, gate/up and the LM head split by output rows, o and down by input
+blocks, one NCCL all-reduce after o and after down, and an all-gather of
+(value, index) for the vocabulary-split argmax.  Timing is CUDA events on the
+launching stream, max over ranks.  The reference arm (--impl reference) times
+the CPU restatement of the reference's arithmetic (the reference has no CPU
+path) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# Qwen2-7B architecture
+HIDDEN, FFN, VOCAB, LAYERS = 3584, 18944, 152064, 28
+N_Q, N_KV, HEAD = 28, 4, 128
+EPS = 1e-6
+QK = 12  # Q4_K
+BPE = 144 / 256
+METRIC = "decode tokens/s (batch 1 & 32) + quant-GEMV HBM GB/s vs peak, 1/2/4/8 B200"
+
+
+def weight_elems():
+    per_layer = HIDDEN * (N_Q * HEAD) + 2 * HIDDEN * (N_KV * HEAD) + (N_Q * HEAD) * HIDDEN + 3 * HIDDEN * FFN
+    return LAYERS * per_layer + VOCAB * HIDDEN
+
+
+def split_blocks(total, parts, granule):
+    """Partition `total` (a multiple of `granule`) into `parts` contiguous pieces of whole granules."""
+    nb = total // granule
+    cuts = [(r * nb) // parts for r in range(parts + 1)]
+    return [(cuts[r] * granule, (cuts[r + 1] - cuts[r]) * granule) for r in range(parts)]
+
+
+# --------------------------------------------------------------------------------------
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------
+class DecodeStack:
+    """The sharded Qwen2-7B-shape Q4_K linear stack of one rank."""
+
+    def __init__(self, Q, torch, rank, world, batch, seed=0):
+        self.Q, self.torch = Q, torch
+        self.rank, self.world, self.M = rank, world, batch
+        dev = "cuda"
+        rb = lambda k: Q.row_bytes(QK, k)
+        # K-split of o (input = q width) and down (input = FFN) at Q4_K block granularity;
+        # the producing column-parallel projections follow the same partition.
+        self.qo_off, self.qo_len = split_blocks(N_Q * HEAD, world, 256)[rank]
+        self.f_off, self.f_len = split_blocks(FFN, world, 256)[rank]
+        self.kv_off, self.kv_len = split_blocks(N_KV * HEAD, world, 32)[rank]
+        self.v_off, self.v_len = split_blocks(VOCAB, world, 32)[rank]
+        g = torch.Generator(device="cpu").manual_seed(seed)
+
+        def synth(rows, k, tag):
+            w = torch.empty((rows, rb(k)), dtype=torch.uint8, device=dev)
+            if rows:
+                Q.synth_quantized(QK, seed * 1000003 + tag * 7919 + rank, rows, k, 0.02, w.data_ptr())
+            return w
+
+        self.layers = []
+        for l in range(LAYERS):
+            L = {
+                "wq": synth(self.qo_len, HIDDEN, 10 * l + 1),
+                "wk": synth(self.kv_len, HIDDEN, 10 * l + 2),
+                "wv": synth(self.kv_len, HIDDEN, 10 * l + 3),
+                "wo": synth(HIDDEN, self.qo_len, 10 * l + 4),
+                "wg": synth(self.f_len, HIDDEN, 10 * l + 5),
+                "wu": synth(self.f_len, HIDDEN, 10 * l + 6),
+                "wd": synth(HIDDEN, self.f_len, 10 * l + 7),
+                "ln1": (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev),
+                "ln2": (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev),
+                "bq": (0.01 * torch.randn(self.qo_len, generator=g)).to(dev),
+                "bk": (0.01 * torch.randn(self.kv_len, generator=g)).to(dev),
+                "bv": (0.01 * torch.randn(self.kv_len, generator=g)).to(dev),
+            }
+            self.layers.append(L)
+        self.wlm = synth(self.v_len, HIDDEN, 999)
+        self.lnf = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev)
+        M = batch
+        self.h = torch.zeros((M, HIDDEN), device=dev)
+        self.h_in = torch.zeros((M, HIDDEN), device=dev)
+        self.q = torch.zeros((M, max(self.qo_len, 1)), device=dev)
+        self.k = torch.zeros((M, max(self.kv_len, 1)), device=dev)
+        self.v = torch.zeros((M, max(self.kv_len, 1)), device=dev)
+        self.act = torch.zeros((M, max(self.f_len, 1)), device=dev)
+        self.logits = torch.zeros((M, self.v_len), device=dev)
+        self.tok = torch.zeros((M,), dtype=torch.int32, device=dev)
+        self.best = torch.zeros((M, 2), device=dev)
+        self.gathered = torch.zeros((world, M, 2), device=dev)
+        self.token_ids = torch.zeros((M,), dtype=torch.int32, device=dev)
+        self.timed_events = []  # (start, end) pairs around the dominant kernel
+        torch.cuda.synchronize()
+
+    def weight_bytes(self):
+        n = sum(w.numel() for L in self.layers for key, w in L.items() if key.startswith("w"))
+        return n + self.wlm.numel()
+
+    def step(self, events=None):
+        """Enqueue one decode token on torch's current stream."""
+        Q, torch, M = self.Q, self.torch, self.M
+        Q.set_stream(torch.cuda.current_stream().cuda_stream)
+        rbh = Q.row_bytes(QK, HIDDEN)
+        self.h.copy_(self.h_in)
+        h = self.h.data_ptr()
+        for li, L in enumerate(self.layers):
+            Q.quant_gemv_ex(QK, L["wq"].data_ptr(), rbh, h, HIDDEN, self.q.data_ptr(), self.q.shape[1], self.qo_len,
+                            HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bq"].data_ptr())
+            if self.kv_len:
+                Q.quant_gemv_ex(QK, L["wk"].data_ptr(), rbh, h, HIDDEN, self.k.data_ptr(), self.k.shape[1],
+                                self.kv_len, HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bk"].data_ptr())
+                Q.quant_gemv_ex(QK, L["wv"].data_ptr(), rbh, h, HIDDEN, self.v.data_ptr(), self.v.shape[1],
+                                self.kv_len, HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bv"].data_ptr())
+            # o_proj (row-parallel): rank 0 accumulates onto h, others overwrite h with their partial
+            Q.quant_gemv_ex(QK, L["wo"].data_ptr(), Q.row_bytes(QK, self.qo_len), self.q.data_ptr(),
+                            self.q.shape[1], h, HIDDEN, HIDDEN, self.qo_len, M, accumulate=(self.rank == 0))
+            if self.world > 1:
+                torch.distributed.all_reduce(self.h)
+            sel = events is not None and li in events["layers"]
+            if sel:
+                events["pairs"][li][0].record()
+            Q.quant_swiglu_ex(QK, L["wg"].data_ptr(), L["wu"].data_ptr(), rbh, rbh, h, HIDDEN, self.act.data_ptr(),
+                              self.act.shape[1], self.f_len, HIDDEN, M, L["ln2"].data_ptr(), EPS)
+            if sel:
+                events["pairs"][li][1].record()
+            Q.quant_gemv_ex(QK, L["wd"].data_ptr(), Q.row_bytes(QK, self.f_len), self.act.data_ptr(),
+                            self.act.shape[1], h, HIDDEN, HIDDEN, self.f_len, M, accumulate=(self.rank == 0))
+            if self.world > 1:
+                torch.distributed.all_reduce(self.h)
+        Q.quant_gemv_ex(QK, self.wlm.data_ptr(), rbh, h, HIDDEN, self.logits.data_ptr(), self.v_len, self.v_len,
+                        HIDDEN, M, self.lnf.data_ptr(), EPS)
+        for m in range(M):
+            Q.argmax(self.logits[m].data_ptr(), self.v_len, self.tok[m:m + 1].data_ptr())
+        if self.world > 1:
+            idx = self.tok.long()
+            self.best[:, 0] = self.logits.gather(1, idx[:, None])[:, 0]
+            self.best[:, 1] = (idx + self.v_off).float()
+            torch.distributed.all_gather_into_tensor(self.gathered, self.best)
+            win = self.gathered[:, :, 0].argmax(0)  # first rank holding the max = lowest vocab index
+            self.token_ids.copy_(self.gathered[win, torch.arange(M, device=self.h.device), 1].int())
+        else:
+            self.token_ids.copy_(self.tok)
+
+    def launches_per_step(self):
+        per_layer = 1 + (2 if self.kv_len else 0) + 3
+        return LAYERS * per_layer * ((self.M + 3) // 4) + ((self.M + 3) // 4) + 2 * self.M
+
+
+# --------------------------------------------------------------------------------------
+def cpu_oracle_rate(sample_layers=2, reps=2):
+    """Times the CPU oracle (double-accumulating restatement, OpenMP over rows)
+    on a bounded sample of the step: `sample_layers` decoder layers' linears plus
+    the LM head at full Qwen2-7B shape; returns tokens/s scaled to the full
+    step by weight bytes."""
+    import oracle as O
+    rb = O.row_bytes(O.Q4_K, HIDDEN)
+    mats = []
+    for l in range(sample_layers):
+        for n, k in ((N_Q * HEAD, HIDDEN), (N_KV * HEAD, HIDDEN), (N_KV * HEAD, HIDDEN), (HIDDEN, N_Q * HEAD),
+                     (FFN, HIDDEN), (FFN, HIDDEN), (HIDDEN, FFN)):
+            mats.append((n, k, O.quantize(O.Q4_K, O.randn(100 + len(mats), n * k, 0.02).reshape(n, k))))
+    mats.append((VOCAB, HIDDEN, O.quantize(O.Q4_K, O.randn(99, VOCAB * HIDDEN, 0.02).reshape(VOCAB, HIDDEN))))
+    sample_elems = sum(n * k for n, k, _ in mats)
+    x = {k: np.random.default_rng(k).standard_normal((1, k)).astype(np.float32) for k in (HIDDEN, FFN)}
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for n, k, w in mats:
+            O.gemv(O.Q4_K, w, O.row_bytes(O.Q4_K, k), x[k], n, k, 1, order=1)
+        best = min(best, time.perf_counter() - t0)
+    full_s = best * weight_elems() / sample_elems
+    return {"value": 1.0 / full_s, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{sample_layers} of {LAYERS} layers' 7 linears + LM head at full shape, batch 1, "
+                      f"best of {reps}, scaled by weight bytes ({sample_elems / weight_elems():.3f} of a token)",
+            "seconds_per_sample": best}
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement of the reference's arithmetic (the
+    reference's only implementation of this path is CUDA; it has no CPU path)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    rates = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info = cpu_oracle_rate(sample_layers=1, reps=1)
+        if i >= args.warmup:
+            rates.append(info["value"])
+    v = float(np.mean(rates))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "qwen2-7b-q4k decode linear stack (28 x 7 linears + LM head), batch 1",
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+                             "sample": "each step: " + info["sample"]},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch32", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    import blog_b200 as Q
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                             timeout=datetime.timedelta(seconds=120))
+    Q.init(local)
+
+    def measure(batch):
+        stack = DecodeStack(Q, torch, rank, world, batch)
+        s = torch.cuda.Stream()
+        host_in = torch.randn((batch, HIDDEN), generator=torch.Generator().manual_seed(5)).pin_memory()
+        host_out = torch.zeros((batch,), dtype=torch.int32).pin_memory()
+        evl = [3, 10, 17, 24]
+        # event-record nodes inside the graph around the dominant kernel of 4 layers
+        events = {"layers": evl, "pairs": {l: (torch.cuda.Event(enable_timing=True, external=True),
+                                               torch.cuda.Event(enable_timing=True, external=True)) for l in evl}}
+        with torch.cuda.stream(s):
+            stack.h_in.copy_(host_in, non_blocking=True)
+            stack.step()  # eager warm-up: sets kernel attributes before capture
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                stack.step(events=events)
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        durs = []
+        with ClockSampler(local) as clk:
+            with torch.cuda.stream(s):
+                torch.cuda.synchronize()
+                t_start.record(s)
+                for _ in range(args.steps):
+                    graph.replay()
+                t_end.record(s)
+                torch.cuda.synchronize()
+            ms = t_start.elapsed_time(t_end) / args.steps
+            # dominant-kernel launch durations: the graph's own event nodes, read after each of
+            # a few further replays (an event holds only its latest record)
+            with torch.cuda.stream(s):
+                for _ in range(min(args.steps, 10)):
+                    graph.replay()
+                    torch.cuda.synchronize()
+                    durs += [events["pairs"][l][0].elapsed_time(events["pairs"][l][1]) for l in evl]
+        # e2e: host input -> device, step, token id -> host, every step
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            torch.cuda.synchronize()
+            e0.record(s)
+            for _ in range(args.steps):
+                stack.h_in.copy_(host_in, non_blocking=True)
+                graph.replay()
+                host_out.copy_(stack.token_ids, non_blocking=True)
+                s.synchronize()
+            e1.record(s)
+            torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        t = torch.tensor([ms, e2e_ms, float(np.mean(durs))], device="cuda")
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        res = {"ms": float(t[0]), "e2e_ms": float(t[1]), "kernel_ms": float(t[2]), "clocks": clk.summary(),
+               "launches": stack.launches_per_step(), "wbytes": stack.weight_bytes(),
+               "h2d": host_in.numel() * 4, "d2h": host_out.numel() * 4, "f_len": stack.f_len}
+        del graph
+        del stack
+        torch.cuda.empty_cache()
+        return res
+
+    r1 = measure(args.batch)
+    r32 = None if args.no_batch32 else measure(32)
+
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        toks = args.batch / (r1["ms"] / 1e3)
+        # dominant kernel: fused RMSNorm + gate/up SwiGLU GEMV (largest launch, 54% of weight bytes)
+        alg_bytes = 2 * r1["f_len"] * HIDDEN * BPE + args.batch * HIDDEN * 4 * 2 + args.batch * r1["f_len"] * 4
+        achieved = alg_bytes / (r1["kernel_ms"] / 1e3) / 1e9
+        total_bytes = weight_elems() * BPE
+        line = {
+            "metric": METRIC, "value": toks, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r1["ms"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "qwen2-7b-q4k decode linear stack (28 x 7 linears + LM head), batch 1",
+                       "weights": "random-init N(0,0.02) quantized to GGUF Q4_K on device",
+                       "global_batch": args.batch, "parallelism": f"tp{world}",
+                       "l2": f"each step streams {total_bytes / 1e9:.2f} GB of weights (> 126 MB L2)"},
+            "hbm_roofline_tokens_per_s": hbm * 1e9 / (total_bytes / world),
+            "step_weight_GBps": total_bytes / (r1["ms"] / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": None, "kernel": "qgemv_kernel<Q4_K,MT=1,NMAT=2> fused RMSNorm+gate/up SwiGLU",
+                         "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": r1["kernel_ms"],
+                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"},
+            "e2e": {"value": args.batch / (r1["e2e_ms"] / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": r1["h2d"] * world, "d2h_bytes_per_step": r1["d2h"] * world},
+            "gpu_launches": r1["launches"] * args.steps,
+            "clocks": r1["clocks"],
+        }
+        if r32 is not None:
+            line["batch32"] = {"value": 32 / (r32["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r32["ms"],
+                               "e2e_tokens_per_s": 32 / (r32["e2e_ms"] / 1e3)}
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_oracle_rate()
+            cb.pop("seconds_per_sample", None)
+            line["cpu_baseline"] = cb
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

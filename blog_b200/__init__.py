@@ -1,0 +1,170 @@
+"""blog_b200 -- B200-native block-quantized linear path of the local-llm engine.
+
+The product is the native library ``lib/libqlinear_b200.so`` (CUDA, sm_100a)
+with the C ABI declared in ``include/qlinear_b200.h``.  This module binds that
+ABI through ctypes for Python callers (tests, benchmarks).  It mirrors the
+reference's launch layer (AI/codes/local-llm/src/backend/cuda/ops/kernel.cuh):
+same function names without the ``launch_`` prefix, same argument order and
+meaning, device pointers passed as integers (e.g. ``tensor.data_ptr()``).
+
+There is no CPU fallback: if the library is missing the import of ``lib()``
+raises, and every call returns the library's status, raised as ``QLError``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "lib", "libqlinear_b200.so")
+HEADER = os.path.join(os.path.dirname(PKG), "include", "qlinear_b200.h")
+
+# GGML type codes (reference src/tensor/TensorCommon.h:15-33)
+F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 6, 8, 12, 14
+BLOCK = {Q4_0: (32, 18), Q5_0: (32, 22), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+QL_OK, QL_EINVAL, QL_ECUDA, QL_EDEVICE = 0, 1, 2, 3
+
+
+class QLError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"qlinear status {status}: {msg}")
+        self.status = status
+
+
+def row_bytes(t: int, k: int) -> int:
+    be, bb = BLOCK[t]
+    if k % be:
+        raise ValueError(f"in_dim {k} is not a multiple of {be}")
+    return k // be * bb
+
+
+P, I, I32, I64, U64, SZ, F = C.c_void_p, C.c_int, C.c_int32, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
+SIGNATURES = {
+    "ql_set_stream": (I, [P]),
+    "ql_get_stream": (P, []),
+    "ql_init": (I, [I]),
+    "ql_last_error": (C.c_char_p, []),
+    "ql_check_device": (I, []),
+    "ql_quant_gemv": (I, [I32, P, SZ, P, P, I, I, I]),
+    "ql_quant_gemv_add": (I, [I32, P, SZ, P, P, I, I]),
+    "ql_quant_matmul": (I, [I32, P, SZ, P, P, I, I, I]),
+    "ql_quant_swiglu": (I, [I32, P, P, SZ, SZ, P, P, I, I]),
+    "ql_quant_swiglu_indexed": (I, [I32, P, P, SZ, SZ, SZ, SZ, P, P, P, I, I, I]),
+    "ql_quant_down_f32_indexed_accum_ordered": (I, [I32, P, SZ, SZ, P, P, P, P, I, I, I]),
+    "ql_moe_router_topk": (I, [P, P, P, I, I, I, F]),
+    "ql_quant_embedding": (I, [I32, P, P, P, SZ, I, I]),
+    "ql_dequantize_to_f16": (I, [I32, P, P, I64]),
+    "ql_dequantize_q4k_to_f16": (I, [P, P, I64]),
+    "ql_dequantize_q80_to_f16": (I, [P, P, I64]),
+    "ql_dequantize_q50_to_f16": (I, [P, P, I64]),
+    "ql_dequantize_q6k_to_f16": (I, [P, P, I64]),
+    "ql_dequantize_q40_to_f16": (I, [P, P, I64]),
+    "ql_argmax": (I, [P, I, P]),
+    "ql_quant_gemv_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, P, I]),
+    "ql_quant_swiglu_ex": (I, [I32, P, P, SZ, SZ, P, I64, P, I64, I, I, I, P, F]),
+    "ql_rms_norm_f32": (I, [P, P, P, I, I, F]),
+    "ql_synth_quantized": (I, [I32, U64, I64, I, F, P]),
+    "ql_row_bytes": (SZ, [I32, I]),
+    "ql_last_launch_count": (I, []),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded native library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `python -m blog_b200.build` (there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != QL_OK:
+        raise QLError(status, lib().ql_last_error().decode(errors="replace"))
+
+
+def _call(name: str, *args) -> None:
+    _check(getattr(lib(), name)(*args))
+
+
+# ---- thin wrappers, names follow the reference's launch_* functions ----------
+def set_stream(stream_handle: int | None) -> None:
+    _call("ql_set_stream", stream_handle or None)
+
+
+def init(device: int = 0) -> None:
+    _call("ql_init", device)
+
+
+def check_device() -> None:
+    _call("ql_check_device")
+
+
+def quant_gemv(t, weight, rb, x, y, out_dim, in_dim, m):
+    _call("ql_quant_gemv", t, weight, rb, x, y, out_dim, in_dim, m)
+
+
+def quant_gemv_add(t, weight, rb, x, y, out_dim, in_dim):
+    _call("ql_quant_gemv_add", t, weight, rb, x, y, out_dim, in_dim)
+
+
+def quant_matmul(t, weight, rb, x, y, out_dim, in_dim, m):
+    _call("ql_quant_matmul", t, weight, rb, x, y, out_dim, in_dim, m)
+
+
+def quant_swiglu(t, gw, uw, grb, urb, x, act, ffn_dim, in_dim):
+    _call("ql_quant_swiglu", t, gw, uw, grb, urb, x, act, ffn_dim, in_dim)
+
+
+def quant_swiglu_indexed(t, gw, uw, geb, ueb, grb, urb, x, ids, act, k, ffn_dim, in_dim):
+    _call("ql_quant_swiglu_indexed", t, gw, uw, geb, ueb, grb, urb, x, ids, act, k, ffn_dim, in_dim)
+
+
+def quant_down_f32_indexed_accum_ordered(t, dw, deb, drb, act, ids, rw, out, k, hidden, ffn_dim):
+    _call("ql_quant_down_f32_indexed_accum_ordered", t, dw, deb, drb, act, ids, rw, out, k, hidden, ffn_dim)
+
+
+def moe_router_topk(logits, idx, w, tokens, n_experts, k, scale):
+    _call("ql_moe_router_topk", logits, idx, w, tokens, n_experts, k, scale)
+
+
+def quant_embedding(t, ids, out, table, rb, hidden, n):
+    _call("ql_quant_embedding", t, ids, out, table, rb, hidden, n)
+
+
+def dequantize_to_f16(t, src, out, n):
+    _call("ql_dequantize_to_f16", t, src, out, n)
+
+
+def argmax(logits, n, out_idx):
+    _call("ql_argmax", logits, n, out_idx)
+
+
+def quant_gemv_ex(t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma=None, eps=0.0, bias=None,
+                  accumulate=False):
+    _call("ql_quant_gemv_ex", t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma, eps, bias,
+          1 if accumulate else 0)
+
+
+def quant_swiglu_ex(t, gw, uw, grb, urb, x, x_stride, act, act_stride, ffn_dim, in_dim, m, gamma=None, eps=0.0):
+    _call("ql_quant_swiglu_ex", t, gw, uw, grb, urb, x, x_stride, act, act_stride, ffn_dim, in_dim, m, gamma, eps)
+
+
+def rms_norm_f32(x, y, gamma, rows, hidden, eps):
+    _call("ql_rms_norm_f32", x, y, gamma, rows, hidden, eps)
+
+
+def synth_quantized(t, seed, rows, in_dim, std, dst):
+    _call("ql_synth_quantized", t, seed, rows, in_dim, std, dst)
+
+
+def last_launch_count() -> int:
+    return int(lib().ql_last_launch_count())

@@ -1,0 +1,412 @@
+// ql_capi.cu -- the C ABI of libqlinear_b200.so (declared in include/qlinear_b200.h).
+//
+// Host-side mirror of the reference's launch layer (src/backend/cuda/ops/launch.cu):
+// dtype dispatch, grid sizing and the process-global current stream, plus what
+// the reference lacks: argument validation with status codes, a per-device
+// workspace allocated once (never inside a launch, so launches can be captured
+// into CUDA graphs), and a device error word for bounded waits that expired.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/qlinear_b200.h"
+#include "ql_common.cuh"
+#include "ql_gemv.cuh"
+
+namespace ql {
+cudaError_t gemv_launch(int fmt, int kind, const GemvArgs &a, int MT, int smem, cudaStream_t s);
+cudaError_t dequant_f16_launch(int t, const uint8_t *src, uint16_t *out, int64_t n, cudaStream_t s);
+cudaError_t embedding_launch(int t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n,
+                             cudaStream_t s);
+cudaError_t argmax_launch(const float *x, int n, int *out, float *pv, int *pi, int max_parts, cudaStream_t s);
+cudaError_t router_launch(const float *logits, int *idx, float *w, int tokens, int E, int k, float scale,
+                          cudaStream_t s);
+cudaError_t rmsnorm_launch(const float *x, float *y, const float *gamma, int rows, int H, float eps,
+                           cudaStream_t s);
+cudaError_t synth_launch(int t, uint64_t seed, int64_t rows, int K, float std, uint8_t *dst, cudaStream_t s);
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxGroups = 1 << 16;   // row groups per launch: out_dim <= 2,097,152
+constexpr int kArgmaxParts = 1024;
+
+struct Workspace {
+    bool ready = false;
+    int sms = 0;
+    int max_ctas = 0;
+    float *part = nullptr;       // [max_ctas][2][kGemvMaxTokens][2][32]
+    unsigned *counters = nullptr;
+    int *err = nullptr;
+    float *am_v = nullptr;
+    int *am_i = nullptr;
+};
+
+std::mutex g_mu;
+Workspace g_ws[kMaxDevices];
+cudaStream_t g_stream = nullptr;
+thread_local std::string t_err;
+thread_local int t_launches = 0;
+
+int fail(int code, const std::string &msg) {
+    t_err = msg;
+    return code;
+}
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(QL_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int init_device(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return fail(QL_EINVAL, "device index out of range");
+    std::lock_guard<std::mutex> lk(g_mu);
+    Workspace &w = g_ws[dev];
+    if (w.ready) return QL_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    w.sms = sms;
+    w.max_ctas = 4 * sms;
+    const size_t part_floats = (size_t)w.max_ctas * 2 * kGemvMaxTokens * 2 * kRowGroup;
+    if ((e = cudaMalloc(&w.part, part_floats * sizeof(float))) != cudaSuccess) return cuda_fail(e, "workspace");
+    if ((e = cudaMalloc(&w.counters, kMaxGroups * sizeof(unsigned))) != cudaSuccess) return cuda_fail(e, "workspace");
+    if ((e = cudaMalloc(&w.err, sizeof(int))) != cudaSuccess) return cuda_fail(e, "workspace");
+    if ((e = cudaMalloc(&w.am_v, kArgmaxParts * sizeof(float))) != cudaSuccess) return cuda_fail(e, "workspace");
+    if ((e = cudaMalloc(&w.am_i, kArgmaxParts * sizeof(int))) != cudaSuccess) return cuda_fail(e, "workspace");
+    if ((e = cudaMemset(w.counters, 0, kMaxGroups * sizeof(unsigned))) != cudaSuccess) return cuda_fail(e, "memset");
+    if ((e = cudaMemset(w.err, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "memset");
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "init sync");
+    w.ready = true;
+    cudaSetDevice(prev);
+    return QL_OK;
+}
+
+Workspace *workspace(int *status) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *status = cuda_fail(e, "cudaGetDevice");
+        return nullptr;
+    }
+    if (!g_ws[dev].ready) {
+        *status = init_device(dev);
+        if (*status != QL_OK) return nullptr;
+        cudaSetDevice(dev);
+    }
+    *status = QL_OK;
+    return &g_ws[dev];
+}
+
+bool quant_ok(int t) { return t == kQ4_0 || t == kQ5_0 || t == kQ8_0 || t == kQ4_K || t == kQ6_K; }
+
+// Validates a weight operand: dtype, block multiple, row size, alignment the
+// decoders rely on (Q4_K reads whole 16-byte lines; the others 2-byte words).
+int check_weight(int t, const void *w, size_t row_bytes, size_t expert_bytes, int in_dim, const char *what) {
+    if (!quant_ok(t)) return fail(QL_EINVAL, std::string(what) + ": unsupported quant_type " + std::to_string(t));
+    const int be = block_elems(t), bb = block_bytes(t);
+    if (in_dim <= 0 || in_dim % be != 0)
+        return fail(QL_EINVAL, std::string(what) + ": in_dim " + std::to_string(in_dim) +
+                                   " is not a positive multiple of the block size " + std::to_string(be));
+    if (row_bytes < (size_t)(in_dim / be) * bb)
+        return fail(QL_EINVAL, std::string(what) + ": row_bytes smaller than in_dim/block*block_bytes");
+    if (w == nullptr) return fail(QL_EINVAL, std::string(what) + ": null weight");
+    const size_t align = (t == kQ4_K) ? 16 : 2;
+    if (reinterpret_cast<uintptr_t>(w) % align || row_bytes % align || expert_bytes % align)
+        return fail(QL_EINVAL, std::string(what) + ": weight, row_bytes and expert_bytes must be multiples of " +
+                                   std::to_string(align) + " bytes for this quant_type");
+    return QL_OK;
+}
+
+// Plans and launches the streaming GEMV engine over M tokens (chunks of <= 4).
+int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
+    int st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    const int NMAT = (kind == 2 || kind == 3) ? 2 : 1;
+    const int BE = block_elems(fmt);
+    base.U = base.K / BE;
+    base.part = ws->part;
+    base.counters = ws->counters;
+    base.err = ws->err;
+    const int G = (base.rows + kRowGroup - 1) / kRowGroup;
+    if (G > kMaxGroups) return fail(QL_EINVAL, std::string(what) + ": out_dim too large");
+    if (G == 0 || M == 0) return QL_OK;
+    const int64_t T = (int64_t)G * base.U;
+    int done = 0;
+    while (done < M) {
+        // most tokens per launch (<= 4), then most stages (<= 4, >= 2), that fit 227 KB
+        int MT = M - done < kGemvMaxTokens ? M - done : kGemvMaxTokens;
+        GemvShape sh{};
+        bool fits = false;
+        for (; MT > 0 && !fits; MT -= fits ? 0 : 1)
+            for (int nst = kGemvStages; nst >= 2 && !fits; --nst) {
+                sh = gemv_shape(fmt, MT, NMAT, base.K, nst);
+                fits = sh.smem_bytes <= 227 * 1024;
+            }
+        if (!fits) return fail(QL_EINVAL, std::string(what) + ": in_dim too large for the shared-memory stage");
+        GemvArgs a = base;
+        a.M = MT;
+        a.nst = sh.nst;
+        a.x = base.x + (size_t)done * base.x_stride;
+        a.y = base.y + (size_t)done * base.y_stride;
+        int64_t C = T < ws->sms ? T : ws->sms;
+        if (C > ws->max_ctas) C = ws->max_ctas;
+        a.plan = Plan{T, G, base.U, (int)C};
+        cudaError_t e = gemv_launch(fmt, kind, a, MT, sh.smem_bytes, g_stream);
+        ++t_launches;
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        done += MT;
+    }
+    return QL_OK;
+}
+
+GemvArgs blank() {
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    return a;
+}
+
+}  // namespace
+}  // namespace ql
+
+using namespace ql;
+
+extern "C" {
+
+int ql_set_stream(void *stream) {
+    g_stream = static_cast<cudaStream_t>(stream);
+    return QL_OK;
+}
+void *ql_get_stream(void) { return g_stream; }
+int ql_init(int device) { return init_device(device); }
+const char *ql_last_error(void) { return t_err.c_str(); }
+int ql_last_launch_count(void) { return t_launches; }
+
+int ql_check_device(void) {
+    int st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    cudaError_t e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) return cuda_fail(e, "stream sync");
+    int h = 0;
+    if ((e = cudaMemcpy(&h, ws->err, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "read error word");
+    if (h != 0) {
+        cudaMemset(ws->err, 0, sizeof(int));
+        cudaMemset(ws->counters, 0, kMaxGroups * sizeof(unsigned));
+        cudaDeviceSynchronize();
+        return fail(QL_EDEVICE, "a kernel gave up a bounded wait (device error code " + std::to_string(h) + ")");
+    }
+    return QL_OK;
+}
+
+size_t ql_row_bytes(int32_t t, int in_dim) {
+    if (!quant_ok(t) || in_dim <= 0 || in_dim % block_elems(t)) return 0;
+    return (size_t)(in_dim / block_elems(t)) * block_bytes(t);
+}
+
+int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int64_t xs, float *y, int64_t ys,
+                     int out_dim, int in_dim, int m, const float *gamma, float eps, const float *bias,
+                     int accumulate) {
+    t_launches = 0;
+    if (out_dim < 0 || m < 0) return fail(QL_EINVAL, "ql_quant_gemv: negative size");
+    if (out_dim == 0 || m == 0) return QL_OK;
+    int st = check_weight(t, w, rb, 0, in_dim, "ql_quant_gemv");
+    if (st) return st;
+    if (!x || !y) return fail(QL_EINVAL, "ql_quant_gemv: null x or y");
+    GemvArgs a = blank();
+    a.w[0] = w;
+    a.row_bytes[0] = rb;
+    a.rows = out_dim;
+    a.K = in_dim;
+    a.x = x;
+    a.x_stride = xs;
+    a.y = y;
+    a.y_stride = ys;
+    a.gamma = gamma;
+    a.eps = eps;
+    a.bias = bias;
+    return run_gemv(t, accumulate ? 1 : 0, a, m, "ql_quant_gemv");
+}
+
+int ql_quant_gemv(int32_t t, const uint8_t *w, size_t rb, const float *x, float *y, int out_dim, int in_dim,
+                  int m) {
+    return ql_quant_gemv_ex(t, w, rb, x, in_dim, y, out_dim, out_dim, in_dim, m, nullptr, 0.f, nullptr, 0);
+}
+
+int ql_quant_gemv_add(int32_t t, const uint8_t *w, size_t rb, const float *x, float *y, int out_dim, int in_dim) {
+    return ql_quant_gemv_ex(t, w, rb, x, in_dim, y, out_dim, out_dim, in_dim, 1, nullptr, 0.f, nullptr, 1);
+}
+
+int ql_quant_matmul(int32_t t, const uint8_t *w, size_t rb, const float *x, float *y, int out_dim, int in_dim,
+                    int m) {
+    return ql_quant_gemv_ex(t, w, rb, x, in_dim, y, out_dim, out_dim, in_dim, m, nullptr, 0.f, nullptr, 0);
+}
+
+int ql_quant_swiglu_ex(int32_t t, const uint8_t *g, const uint8_t *u, size_t grb, size_t urb, const float *x,
+                       int64_t xs, float *act, int64_t as, int ffn_dim, int in_dim, int m, const float *gamma,
+                       float eps) {
+    t_launches = 0;
+    if (ffn_dim < 0 || m < 0) return fail(QL_EINVAL, "ql_quant_swiglu: negative size");
+    if (ffn_dim == 0 || m == 0) return QL_OK;
+    int st = check_weight(t, g, grb, 0, in_dim, "ql_quant_swiglu(gate)");
+    if (st) return st;
+    if ((st = check_weight(t, u, urb, 0, in_dim, "ql_quant_swiglu(up)"))) return st;
+    if (!x || !act) return fail(QL_EINVAL, "ql_quant_swiglu: null x or act");
+    GemvArgs a = blank();
+    a.w[0] = g;
+    a.w[1] = u;
+    a.row_bytes[0] = grb;
+    a.row_bytes[1] = urb;
+    a.rows = ffn_dim;
+    a.K = in_dim;
+    a.x = x;
+    a.x_stride = xs;
+    a.y = act;
+    a.y_stride = as;
+    a.gamma = gamma;
+    a.eps = eps;
+    return run_gemv(t, 2, a, m, "ql_quant_swiglu");
+}
+
+int ql_quant_swiglu(int32_t t, const uint8_t *g, const uint8_t *u, size_t grb, size_t urb, const float *x,
+                    float *act, int ffn_dim, int in_dim) {
+    return ql_quant_swiglu_ex(t, g, u, grb, urb, x, in_dim, act, ffn_dim, ffn_dim, in_dim, 1, nullptr, 0.f);
+}
+
+int ql_quant_swiglu_indexed(int32_t t, const uint8_t *g, const uint8_t *u, size_t geb, size_t ueb, size_t grb,
+                            size_t urb, const float *x, const int *ids, float *act, int k, int ffn_dim,
+                            int in_dim) {
+    t_launches = 0;
+    if (k < 0 || ffn_dim < 0) return fail(QL_EINVAL, "ql_quant_swiglu_indexed: negative size");
+    if (k == 0 || ffn_dim == 0) return QL_OK;
+    int st = check_weight(t, g, grb, geb, in_dim, "ql_quant_swiglu_indexed(gate)");
+    if (st) return st;
+    if ((st = check_weight(t, u, urb, ueb, in_dim, "ql_quant_swiglu_indexed(up)"))) return st;
+    if (!x || !ids || !act) return fail(QL_EINVAL, "ql_quant_swiglu_indexed: null pointer");
+    GemvArgs a = blank();
+    a.w[0] = g;
+    a.w[1] = u;
+    a.row_bytes[0] = grb;
+    a.row_bytes[1] = urb;
+    a.expert_bytes[0] = geb;
+    a.expert_bytes[1] = ueb;
+    a.rows = k * ffn_dim;
+    a.rows_per_route = ffn_dim;
+    a.K = in_dim;
+    a.x = x;
+    a.x_stride = in_dim;
+    a.ids = ids;
+    a.y = act;
+    a.y_stride = (int64_t)k * ffn_dim;
+    return run_gemv(t, 3, a, 1, "ql_quant_swiglu_indexed");
+}
+
+int ql_quant_down_f32_indexed_accum_ordered(int32_t t, const uint8_t *d, size_t deb, size_t drb, const float *act,
+                                            const int *ids, const float *rw, float *out, int k, int hidden,
+                                            int ffn_dim) {
+    t_launches = 0;
+    if (k < 0 || hidden < 0) return fail(QL_EINVAL, "ql_quant_down_f32_indexed_accum_ordered: negative size");
+    if (k == 0 || hidden == 0) return QL_OK;
+    int st = check_weight(t, d, drb, deb, ffn_dim, "ql_quant_down_f32_indexed_accum_ordered");
+    if (st) return st;
+    if (!act || !ids || !rw || !out) return fail(QL_EINVAL, "ql_quant_down_f32_indexed_accum_ordered: null pointer");
+    GemvArgs a = blank();
+    a.w[0] = d;
+    a.row_bytes[0] = drb;
+    a.expert_bytes[0] = deb;
+    a.rows = hidden;
+    a.K = k * ffn_dim;
+    a.units_per_route = ffn_dim / block_elems(t);
+    a.x = act;
+    a.x_stride = ffn_dim;
+    a.ids = ids;
+    a.route_w = rw;
+    a.y = out;
+    a.y_stride = hidden;
+    return run_gemv(t, 4, a, 1, "ql_quant_down_f32_indexed_accum_ordered");
+}
+
+int ql_moe_router_topk(const float *logits, int *idx, float *w, int tokens, int E, int k, float scale) {
+    t_launches = 0;
+    if (tokens < 0 || E <= 0 || E > 64 || k <= 0 || k > E)
+        return fail(QL_EINVAL, "ql_moe_router_topk: need 0 < k <= n_experts <= 64");
+    if (tokens == 0) return QL_OK;
+    if (!logits || !idx || !w) return fail(QL_EINVAL, "ql_moe_router_topk: null pointer");
+    int st;
+    if (!workspace(&st)) return st;
+    cudaError_t e = router_launch(logits, idx, w, tokens, E, k, scale, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_moe_router_topk");
+}
+
+int ql_quant_embedding(int32_t t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n) {
+    t_launches = 0;
+    if (n < 0) return fail(QL_EINVAL, "ql_quant_embedding: negative size");
+    if (n == 0) return QL_OK;
+    if (!quant_ok(t) || hidden <= 0 || hidden % block_elems(t))
+        return fail(QL_EINVAL, "ql_quant_embedding: bad quant_type or hidden_size");
+    if (!ids || !out || !table) return fail(QL_EINVAL, "ql_quant_embedding: null pointer");
+    int st;
+    if (!workspace(&st)) return st;
+    cudaError_t e = embedding_launch(t, ids, out, table, rb, hidden, n, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quant_embedding");
+}
+
+int ql_dequantize_to_f16(int32_t t, const uint8_t *src, uint16_t *out, int64_t n) {
+    t_launches = 0;
+    if (!quant_ok(t) || n < 0 || n % block_elems(t))
+        return fail(QL_EINVAL, "ql_dequantize_to_f16: bad quant_type or element count");
+    if (n == 0) return QL_OK;
+    if (!src || !out) return fail(QL_EINVAL, "ql_dequantize_to_f16: null pointer");
+    int st;
+    if (!workspace(&st)) return st;
+    cudaError_t e = dequant_f16_launch(t, src, out, n, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_dequantize_to_f16");
+}
+int ql_dequantize_q4k_to_f16(const uint8_t *s, uint16_t *o, int64_t n) { return ql_dequantize_to_f16(kQ4_K, s, o, n); }
+int ql_dequantize_q80_to_f16(const uint8_t *s, uint16_t *o, int64_t n) { return ql_dequantize_to_f16(kQ8_0, s, o, n); }
+int ql_dequantize_q50_to_f16(const uint8_t *s, uint16_t *o, int64_t n) { return ql_dequantize_to_f16(kQ5_0, s, o, n); }
+int ql_dequantize_q6k_to_f16(const uint8_t *s, uint16_t *o, int64_t n) { return ql_dequantize_to_f16(kQ6_K, s, o, n); }
+int ql_dequantize_q40_to_f16(const uint8_t *s, uint16_t *o, int64_t n) { return ql_dequantize_to_f16(kQ4_0, s, o, n); }
+
+int ql_argmax(const float *logits, int n, int *out_idx) {
+    t_launches = 0;
+    if (n <= 0 || !logits || !out_idx) return fail(QL_EINVAL, "ql_argmax: need n > 0 and non-null pointers");
+    int st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    cudaError_t e = argmax_launch(logits, n, out_idx, ws->am_v, ws->am_i, kArgmaxParts, g_stream);
+    t_launches += 2;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_argmax");
+}
+
+int ql_rms_norm_f32(const float *x, float *y, const float *gamma, int rows, int hidden, float eps) {
+    t_launches = 0;
+    if (rows < 0 || hidden <= 0 || !x || !y) return fail(QL_EINVAL, "ql_rms_norm_f32: bad arguments");
+    int st;
+    if (!workspace(&st)) return st;
+    cudaError_t e = rmsnorm_launch(x, y, gamma, rows, hidden, eps, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_rms_norm_f32");
+}
+
+int ql_synth_quantized(int32_t t, uint64_t seed, int64_t rows, int in_dim, float std, uint8_t *dst) {
+    t_launches = 0;
+    if ((t != kQ4_K && t != kQ8_0 && t != kQ4_0 && t != kQ5_0) || rows < 0 || in_dim <= 0 ||
+        in_dim % block_elems(t) || !dst)
+        return fail(QL_EINVAL, "ql_synth_quantized: bad arguments");
+    int st;
+    if (!workspace(&st)) return st;
+    cudaError_t e = synth_launch(t, seed, rows, in_dim, std, dst, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_synth_quantized");
+}
+
+}  // extern "C"

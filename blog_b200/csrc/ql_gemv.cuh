@@ -1,0 +1,148 @@
+// ql_gemv.cuh -- the streaming block-quantized GEMV engine (decode path, M <= 4).
+//
+// Replaces the reference's warp-per-row kernels quant_gemv_kernel,
+// quant_gemv_add_kernel, quant_matmul_kernel, quant_swiglu_kernel,
+// quant_swiglu_indexed_kernel and quant_down_f32_indexed_accum_ordered_kernel
+// (AI/codes/local-llm/src/backend/cuda/ops/kernel.cu:1191-1385,2252-2287).
+//
+// Design (B200, sm_100a):
+//  * One producer warp streams the raw GGUF bytes of 32 output rows x SEG
+//    blocks per stage into a shared-memory ring with 1-D TMA bulk copies
+//    (cp.async.bulk + mbarrier complete_tx, L2 evict-first).  Unaligned row
+//    starts (34/18/22-byte blocks) are handled by copying the 16-byte-aligned
+//    interior in bulk and the ragged head/tail bytes with plain loads, so no
+//    byte outside the requested range is ever read.
+//  * Consumer warps: lane = output row.  Warp w takes every W-th block of the
+//    stream.  The activation is staged once per CTA in shared memory,
+//    pre-multiplied by 2^(96-p), p being the bit position its weight nibble or
+//    byte occupies after one AND: the masked integer reinterpreted as a float
+//    is the exact denormal q * 2^(p-149), so one LOP3 and one FMA per weight
+//    give q * x * 2^-53 in fp32.  Scales and mins are applied once per 32-
+//    element sub-block: dot = D * 2^53 * S - M * X, X the block sum of the
+//    activation (precomputed).  Accumulation is fp32 throughout.
+//  * Row groups are split over CTAs in equal tile counts (stream-K); a group
+//    shared by several CTAs is finished by the last one to arrive, which sums
+//    the parts in K order, so results are deterministic.
+//  * Fused RMSNorm prologue (f32 gamma) and store / add / SwiGLU / bias
+//    epilogues.
+#pragma once
+
+#include "ql_common.cuh"
+
+namespace ql {
+
+enum SrcKind : int { kSrcPlain = 0, kSrcIndexedRows = 1, kSrcIndexedK = 2 };
+enum EpiKind : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2 };
+
+constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvThreads = 32 * (1 + kGemvConsumerWarps);
+constexpr int kGemvStages = 4;  // most stages (the host may pick fewer to fit shared memory)
+constexpr int kGemvMaxTokens = 4;
+
+// Blocks per stage for each format (about 0.5 KB of each row per stage).
+__host__ __device__ constexpr int gemv_seg(int t) {
+    return t == kQ4_K ? 4 : t == kQ6_K ? 2 : t == kQ8_0 ? 16 : t == kQ4_0 ? 32 : t == kQ5_0 ? 24 : 0;
+}
+// Shared-memory pitch of one row slot: data + 16 bytes of alignment slack +
+// 16 bytes of over-read slack, rounded so that pitch % 128 == 16 (lanes reading
+// the same offset of consecutive rows hit distinct bank groups).
+__host__ __device__ constexpr int gemv_pitch(int t) {
+    return ((gemv_seg(t) * block_bytes(t) + 32 + 127) / 128) * 128 + 16;
+}
+
+struct GemvArgs {
+    const uint8_t *w[2];      // weight buffers (raw GGUF blocks); w[1] only for SwiGLU pairs
+    size_t row_bytes[2];      // bytes per output row
+    size_t expert_bytes[2];   // bytes per expert (indexed kinds)
+    int rows;                 // output rows of the launch (virtual rows for indexed-rows)
+    int K;                    // reduction length in elements (virtual length for indexed-K)
+    int U;                    // blocks per row = K / block_elems
+    int units_per_route;      // indexed-K: blocks per route
+    int rows_per_route;       // indexed-rows: output rows per route
+    int M;                    // tokens in this launch (<= MT)
+    const float *x;           // activations [M][x_stride] (indexed-K: [k][F] route-major)
+    int64_t x_stride;
+    const float *gamma;       // optional fused RMSNorm weight (f32, length K); null = none
+    float eps;
+    const int *ids;           // expert id per route (indexed kinds)
+    const float *route_w;     // route weights (indexed-K)
+    const float *bias;        // optional per-row bias (kEpiStore / kEpiAdd)
+    float *y;                 // output [M][y_stride]
+    int64_t y_stride;
+    int nst;                  // stages in the shared-memory ring (2..kGemvStages)
+    Plan plan;
+    float *part;              // stream-K partial slots [C][2][MT][NMAT][32]
+    unsigned *counters;       // stream-K arrival counters [G], zero between launches
+    int *err;                 // device error word
+};
+
+// One stage of a CTA's stream: row group g, blocks [us, ue) of the group's
+// rows.  A stage never straddles a route boundary of an indexed-K source.
+struct Stage {
+    int g, us, ue;
+    bool last_in_group;
+};
+
+// Advances a CTA's stage cursor.  `t` is the next tile (g * U + u) to cover,
+// `t1` the end of the CTA's range.  Returns false when the range is exhausted.
+__host__ __device__ inline bool next_stage(int64_t &t, int64_t t1, int U, int seg, int upr, Stage &s) {
+    if (t >= t1) return false;
+    const int g = (int)(t / U);
+    const int u = (int)(t - (int64_t)g * U);
+    const int64_t gend = ((int64_t)g + 1) * U < t1 ? ((int64_t)g + 1) * U : t1;
+    const int uend = u + (int)(gend - t);
+    int ue = u + seg < uend ? u + seg : uend;
+    if (upr > 0) {
+        const int rb = (u / upr + 1) * upr;
+        if (rb < ue) ue = rb;
+    }
+    s.g = g;
+    s.us = u;
+    s.ue = ue;
+    s.last_in_group = (ue == uend);
+    t += ue - u;
+    return true;
+}
+
+// Address of block `u` of output row `v` of matrix `mat`, or nullptr when the
+// row's expert id is negative (the route is skipped).  `ids` may be a host or
+// device pointer; it is read only for indexed sources.
+template <int SRC, int FMT>
+__host__ __device__ inline const uint8_t *gemv_block_ptr(const GemvArgs &a, const int *ids, int mat, int v, int u) {
+    constexpr int BB = block_bytes(FMT);
+    if (SRC == kSrcPlain) return a.w[mat] + (size_t)v * a.row_bytes[mat] + (size_t)u * BB;
+    if (SRC == kSrcIndexedRows) {
+        const int r = v / a.rows_per_route, row = v - r * a.rows_per_route;
+        const int e = ids[r];
+        if (e < 0) return nullptr;
+        return a.w[mat] + (size_t)e * a.expert_bytes[mat] + (size_t)row * a.row_bytes[mat] + (size_t)u * BB;
+    }
+    const int r = u / a.units_per_route, lu = u - r * a.units_per_route;
+    const int e = ids[r];
+    if (e < 0) return nullptr;
+    return a.w[mat] + (size_t)e * a.expert_bytes[mat] + (size_t)v * a.row_bytes[mat] + (size_t)lu * BB;
+}
+
+// Host-side description of a launch (grid, shared memory) for one format.
+struct GemvShape {
+    int seg, pitch, stage_bytes, xs_floats, xsum_floats, red_floats, nst, smem_bytes;
+};
+__host__ inline GemvShape gemv_shape(int fmt, int MT, int NMAT, int K, int nst) {
+    GemvShape s;
+    s.seg = gemv_seg(fmt);
+    s.pitch = gemv_pitch(fmt);
+    s.stage_bytes = NMAT * kRowGroup * s.pitch;
+    s.xs_floats = MT * K;
+    s.xsum_floats = MT * (K / 32);
+    s.red_floats = kGemvConsumerWarps * MT * NMAT * kRowGroup;
+    s.nst = nst;
+    int off = 128;  // mbarriers, inv-rms slots, abort flag
+    off += ((s.xs_floats * 4 + 127) / 128) * 128;
+    off += ((s.xsum_floats * 4 + 127) / 128) * 128;
+    off += ((s.red_floats * 4 + 127) / 128) * 128;
+    off += nst * s.stage_bytes;
+    s.smem_bytes = off;
+    return s;
+}
+
+}  // namespace ql

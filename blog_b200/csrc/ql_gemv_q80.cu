@@ -1,0 +1,6 @@
+// ql_gemv_q80.cu -- GEMV engine instantiations for Q8_0.
+#include "ql_gemv_impl.cuh"
+
+namespace ql {
+template cudaError_t gemv_launch_fmt<kQ8_0>(int, const GemvArgs &, int, int, cudaStream_t);
+}  // namespace ql

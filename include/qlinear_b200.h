@@ -1,0 +1,139 @@
+/*
+ * qlinear_b200.h -- C ABI of libqlinear_b200.so, the B200 (sm_100a) block-quantized
+ * linear path of the local-llm engine (allenzhang61/blog, AI/codes/local-llm).
+ *
+ * Every entry point below is the C twin of one reference launch function in
+ * src/backend/cuda/ops/kernel.cuh (cited per function): same argument order and
+ * meaning, raw GGUF weight bytes as uploaded unchanged by CudaWeightPool
+ * (CudaWeightPool.cpp:148-175), fp32 activations, launches on the library's
+ * current stream (the reference's process-global stream, common.cpp:12-17).
+ * Differences from the reference, by design:
+ *   - each function returns a status instead of void; an unsupported dtype or
+ *     an invalid shape returns QL_EINVAL instead of silently doing nothing
+ *     (the reference's launchers fall through `default: break;`, launch.cu:57-58);
+ *   - Q4_0 is supported (the reference parses it but has no arithmetic for it);
+ *   - all pointers are device pointers unless stated otherwise.
+ * A C++ header-only shim with the reference's exact C++ signatures
+ * (DType enum, void return, throw on error) is in qlinear_b200_launch.hpp.
+ */
+#ifndef QLINEAR_B200_H
+#define QLINEAR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QL_API __attribute__((visibility("default")))
+#else
+#define QL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* GGML type codes, equal to the reference's DType (src/tensor/TensorCommon.h:15-33). */
+#define QL_F32 0
+#define QL_F16 1
+#define QL_Q4_0 2
+#define QL_Q5_0 6
+#define QL_Q8_0 8
+#define QL_Q4_K 12
+#define QL_Q6_K 14
+
+/* Status codes. */
+#define QL_OK 0
+#define QL_EINVAL 1   /* bad argument: dtype, shape, block multiple, null pointer */
+#define QL_ECUDA 2    /* CUDA runtime error (see ql_last_error) */
+#define QL_EDEVICE 3  /* a kernel gave up a bounded wait and recorded an error */
+
+/* ---- runtime -------------------------------------------------------------------- */
+/* set/get the stream every launch uses (reference set/get_current_cuda_stream,
+ * common.h:40-44).  NULL = the legacy default stream. */
+QL_API int ql_set_stream(void *stream);
+QL_API void *ql_get_stream(void);
+/* Allocate the per-device workspace (stream-K partials, arrival counters, argmax
+ * partials, error word) for `device`.  Called implicitly by the first launch on a
+ * device; call it explicitly before capturing launches into a CUDA graph. */
+QL_API int ql_init(int device);
+/* Human-readable description of the last error returned by this thread. */
+QL_API const char *ql_last_error(void);
+/* Synchronize the current stream and read (and clear) the device error word. */
+QL_API int ql_check_device(void);
+
+/* ---- quantized linear (reference kernel.cuh:34-43) ------------------------------- */
+/* y[m, o] = sum_k W[o, k] * x[m, k].  W: out_dim rows of row_bytes GGUF bytes.
+ * x: [m, in_dim] f32, y: [m, out_dim] f32, row-major.  kernel.cuh:34-35. */
+QL_API int ql_quant_gemv(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x, float *y,
+                  int out_dim, int in_dim, int m);
+/* y[o] += W[o, :] . x  (m = 1).  kernel.cuh:37-38. */
+QL_API int ql_quant_gemv_add(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x, float *y,
+                      int out_dim, int in_dim);
+/* Same contract as ql_quant_gemv, intended for m > 1 (prefill).  kernel.cuh:42-43. */
+QL_API int ql_quant_matmul(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x, float *y,
+                    int out_dim, int in_dim, int m);
+/* act[f] = SiLU(Wg[f] . x) * (Wu[f] . x).  kernel.cuh:65-67. */
+QL_API int ql_quant_swiglu(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,
+                    size_t gate_row_bytes, size_t up_row_bytes, const float *x, float *act, int ffn_dim,
+                    int in_dim);
+
+/* ---- MoE (reference kernel.cuh:72-76, 125-129, 335-336) -------------------------- */
+/* act[r, f] = SiLU(Wg[e_r][f] . x) * (Wu[e_r][f] . x), e_r = expert_ids[r] (device);
+ * e_r < 0 writes zeros.  Expert e's rows start at weight + e * expert_bytes. */
+QL_API int ql_quant_swiglu_indexed(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,
+                            size_t gate_expert_bytes, size_t up_expert_bytes, size_t gate_row_bytes,
+                            size_t up_row_bytes, const float *x, const int *expert_ids, float *act, int k,
+                            int ffn_dim, int in_dim);
+/* out[h] += sum_r route_weights[r] * (Wd[e_r][h] . act[r, :]) over routes with e_r >= 0,
+ * in a fixed (deterministic) order. */
+QL_API int ql_quant_down_f32_indexed_accum_ordered(int32_t quant_type, const uint8_t *down_weight,
+                                            size_t down_expert_bytes, size_t down_row_bytes, const float *act,
+                                            const int *expert_ids, const float *route_weights, float *out, int k,
+                                            int hidden_size, int ffn_dim);
+/* Per token: softmax over n_experts (<= 64) logits, top-k by logit (lowest id on
+ * ties, non-finite = -inf), top_w = p * routed_scaling. */
+QL_API int ql_moe_router_topk(const float *router_logits, int *top_idx, float *top_w, int tokens, int n_experts, int k,
+                       float routed_scaling);
+
+/* ---- embedding, dequant, argmax (reference kernel.cuh:141-142, 244-253, 347) ----- */
+QL_API int ql_quant_embedding(int32_t quant_type, const int *input, float *output, const uint8_t *table, size_t row_bytes,
+                       int hidden_size, int input_size);
+/* Whole-tensor dequant to IEEE f16 bits, num_elements a multiple of the block size. */
+QL_API int ql_dequantize_to_f16(int32_t quant_type, const uint8_t *src, uint16_t *out, int64_t num_elements);
+QL_API int ql_dequantize_q4k_to_f16(const uint8_t *src, uint16_t *out, int64_t num_elements);
+QL_API int ql_dequantize_q80_to_f16(const uint8_t *src, uint16_t *out, int64_t num_elements);
+QL_API int ql_dequantize_q50_to_f16(const uint8_t *src, uint16_t *out, int64_t num_elements);
+QL_API int ql_dequantize_q6k_to_f16(const uint8_t *src, uint16_t *out, int64_t num_elements);
+QL_API int ql_dequantize_q40_to_f16(const uint8_t *src, uint16_t *out, int64_t num_elements);
+/* out_idx[0] = argmax(logits[0..n)), lowest index on ties. */
+QL_API int ql_argmax(const float *logits, int n, int *out_idx);
+
+/* ---- fused forms (no reference counterpart; fusions the reference runs as
+ *      separate rms_norm / add kernels, kernel.cu:80-84,112-147) ------------------ */
+/* y[m*y_stride + o] (=|+=) W[o] . rmsnorm(x[m*x_stride + :]) (+ bias[o]).
+ * norm_gamma == NULL skips the norm; bias may be NULL; accumulate != 0 adds into y. */
+QL_API int ql_quant_gemv_ex(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x, int64_t x_stride,
+                     float *y, int64_t y_stride, int out_dim, int in_dim, int m, const float *norm_gamma, float eps,
+                     const float *bias, int accumulate);
+/* act[m*act_stride + f] = SiLU(Wg[f] . n(x_m)) * (Wu[f] . n(x_m)), n = optional RMSNorm. */
+QL_API int ql_quant_swiglu_ex(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,
+                       size_t gate_row_bytes, size_t up_row_bytes, const float *x, int64_t x_stride, float *act,
+                       int64_t act_stride, int ffn_dim, int in_dim, int m, const float *norm_gamma, float eps);
+/* y = x * rsqrt(mean(x^2) + eps) * gamma (gamma f32, may be NULL), rows x hidden. */
+QL_API int ql_rms_norm_f32(const float *x, float *y, const float *gamma, int rows, int hidden, float eps);
+
+/* ---- synthetic weights (benchmarks; no reference counterpart) -------------------- */
+/* dst[rows x row_bytes] = quantize(N(0, std) with seed), generated on the device. */
+QL_API int ql_synth_quantized(int32_t quant_type, uint64_t seed, int64_t rows, int in_dim, float std, uint8_t *dst);
+
+/* ---- introspection ------------------------------------------------------------- */
+/* Bytes per row of `in_dim` elements of `quant_type` (0 if not a block multiple). */
+QL_API size_t ql_row_bytes(int32_t quant_type, int in_dim);
+/* Number of kernel launches the last call on this thread issued. */
+QL_API int ql_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLINEAR_B200_H */
