@@ -5,17 +5,22 @@
 // the reference lacks: argument validation with status codes, a per-device
 // workspace allocated once (never inside a launch, so launches can be captured
 // into CUDA graphs), and a device error word for bounded waits that expired.
+#include <cudaTypedefs.h>
+
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 
 #include "../../include/qlinear_b200.h"
 #include "ql_common.cuh"
 #include "ql_gemv.cuh"
 
 namespace ql {
-cudaError_t gemv_launch(int fmt, int kind, const GemvArgs &a, int MT, int smem, cudaStream_t s);
+cudaError_t gemv_launch(int fmt, int kind, const GemvArgs &a, int MT, bool tma, int smem, cudaStream_t s);
 cudaError_t dequant_f16_launch(int t, const uint8_t *src, uint16_t *out, int64_t n, cudaStream_t s);
 cudaError_t embedding_launch(int t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n,
                              cudaStream_t s);
@@ -25,6 +30,14 @@ cudaError_t router_launch(const float *logits, int *idx, float *w, int tokens, i
 cudaError_t rmsnorm_launch(const float *x, float *y, const float *gamma, int rows, int H, float eps,
                            cudaStream_t s);
 cudaError_t synth_launch(int t, uint64_t seed, int64_t rows, int K, float std, uint8_t *dst, cudaStream_t s);
+
+bool gemv_pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("QL_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 namespace {
 
@@ -121,6 +134,86 @@ int check_weight(int t, const void *w, size_t row_bytes, size_t expert_bytes, in
     return QL_OK;
 }
 
+// ---- Q4_K tensor maps ----------------------------------------------------------
+// A Q4_K matrix is viewed as a 3-D uint8 tensor {144 B of a block, block index,
+// row} with strides {144, row_bytes}; the engine loads {144, 7, 32} boxes.  Maps
+// are encoded on the host (no device work, so this is safe during stream
+// capture) and cached by (base, blocks, rows, row_bytes).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+std::mutex g_map_mu;
+std::map<std::tuple<uintptr_t, int, uint64_t, size_t>, CUtensorMap> g_maps;
+
+bool q4k_tensor_map(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes) {
+    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), blocks, rows, row_bytes);
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+        *out = it->second;
+        return true;
+    }
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    CUtensorMap m;
+    const cuuint64_t dims[3] = {144, (cuuint64_t)blocks, rows};
+    const cuuint64_t strides[2] = {144, (cuuint64_t)row_bytes};
+    const cuuint32_t box[3] = {144, (cuuint32_t)kTmaSeg, (cuuint32_t)kRowGroup};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+    if (g_maps.size() > 4096) g_maps.clear();
+    g_maps.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+// Whether a Q4_K launch can stage through tensor maps, and the maps if so.
+// Indexed sources view the packed expert tensor as one tall matrix whose row
+// count is not known here, so a generous extent is declared; only rows of
+// valid experts are ever requested.
+bool prepare_tma(int fmt, int kind, GemvArgs &a) {
+    if (fmt != kQ4_K || a.U < kTmaSeg) return false;
+    const int NMAT = (kind == 2 || kind == 3) ? 2 : 1;
+    uint64_t rows = (uint64_t)a.rows;
+    if (kind <= 2) {
+        if (a.rows < kRowGroup) return false;
+    } else if (kind == 3) {
+        if (a.rows_per_route % kRowGroup) return false;
+        for (int m = 0; m < NMAT; ++m)
+            if (a.expert_bytes[m] != (size_t)a.rows_per_route * a.row_bytes[m]) return false;
+        rows = 1ull << 24;
+    } else {
+        if (a.rows % kRowGroup || a.units_per_route < kTmaSeg) return false;
+        if (a.expert_bytes[0] != (size_t)a.rows * a.row_bytes[0]) return false;
+        rows = 1ull << 24;
+    }
+    const int blocks = (kind == 4) ? a.units_per_route : a.U;
+    for (int m = 0; m < NMAT; ++m)
+        if (!q4k_tensor_map(&a.tmap[m], a.w[m], blocks, rows, a.row_bytes[m])) return false;
+    return true;
+}
+
+// The engine stages activations (and the fused-norm weight) with 16-byte loads.
+int check_act(const float *x, int64_t x_stride, const float *gamma, const char *what) {
+    if (reinterpret_cast<uintptr_t>(x) % 16 || x_stride % 4 || reinterpret_cast<uintptr_t>(gamma) % 16)
+        return fail(QL_EINVAL, std::string(what) + ": activations (and norm weight) must be 16-byte aligned with a "
+                                                   "row stride that is a multiple of 4 floats");
+    return QL_OK;
+}
+
 // Plans and launches the streaming GEMV engine over M tokens (chunks of <= 4).
 int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
     int st;
@@ -136,15 +229,17 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
     if (G > kMaxGroups) return fail(QL_EINVAL, std::string(what) + ": out_dim too large");
     if (G == 0 || M == 0) return QL_OK;
     const int64_t T = (int64_t)G * base.U;
+    const bool tma = prepare_tma(fmt, kind, base);
     int done = 0;
     while (done < M) {
         // most tokens per launch (<= 4), then most stages (<= 4, >= 2), that fit 227 KB
-        int MT = M - done < kGemvMaxTokens ? M - done : kGemvMaxTokens;
+        const int mt_cap = NMAT == 2 ? 2 : kGemvMaxTokens;  // two-matrix launches: at most 2 tokens
+        int MT = M - done < mt_cap ? M - done : mt_cap;
         GemvShape sh{};
         bool fits = false;
         for (; MT > 0 && !fits; MT -= fits ? 0 : 1)
             for (int nst = kGemvStages; nst >= 2 && !fits; --nst) {
-                sh = gemv_shape(fmt, MT, NMAT, base.K, nst);
+                sh = gemv_shape(fmt, MT, NMAT, base.K, nst, tma);
                 fits = sh.smem_bytes <= 227 * 1024;
             }
         if (!fits) return fail(QL_EINVAL, std::string(what) + ": in_dim too large for the shared-memory stage");
@@ -153,10 +248,12 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
         a.nst = sh.nst;
         a.x = base.x + (size_t)done * base.x_stride;
         a.y = base.y + (size_t)done * base.y_stride;
-        int64_t C = T < ws->sms ? T : ws->sms;
+        // Small reductions with at most one wave of row groups: one group per CTA
+        // (no stream-K fixups); otherwise equal tile ranges over all SMs.
+        int64_t C = (G <= ws->sms && base.U <= 32) ? G : (T < ws->sms ? T : ws->sms);
         if (C > ws->max_ctas) C = ws->max_ctas;
         a.plan = Plan{T, G, base.U, (int)C};
-        cudaError_t e = gemv_launch(fmt, kind, a, MT, sh.smem_bytes, g_stream);
+        cudaError_t e = gemv_launch(fmt, kind, a, MT, tma, sh.smem_bytes, g_stream);
         ++t_launches;
         if (e != cudaSuccess) return cuda_fail(e, what);
         done += MT;
@@ -218,6 +315,7 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     int st = check_weight(t, w, rb, 0, in_dim, "ql_quant_gemv");
     if (st) return st;
     if (!x || !y) return fail(QL_EINVAL, "ql_quant_gemv: null x or y");
+    if ((st = check_act(x, xs, gamma, "ql_quant_gemv"))) return st;
     GemvArgs a = blank();
     a.w[0] = w;
     a.row_bytes[0] = rb;
@@ -257,6 +355,7 @@ int ql_quant_swiglu_ex(int32_t t, const uint8_t *g, const uint8_t *u, size_t grb
     if (st) return st;
     if ((st = check_weight(t, u, urb, 0, in_dim, "ql_quant_swiglu(up)"))) return st;
     if (!x || !act) return fail(QL_EINVAL, "ql_quant_swiglu: null x or act");
+    if ((st = check_act(x, xs, gamma, "ql_quant_swiglu"))) return st;
     GemvArgs a = blank();
     a.w[0] = g;
     a.w[1] = u;
@@ -288,6 +387,7 @@ int ql_quant_swiglu_indexed(int32_t t, const uint8_t *g, const uint8_t *u, size_
     if (st) return st;
     if ((st = check_weight(t, u, urb, ueb, in_dim, "ql_quant_swiglu_indexed(up)"))) return st;
     if (!x || !ids || !act) return fail(QL_EINVAL, "ql_quant_swiglu_indexed: null pointer");
+    if ((st = check_act(x, in_dim, nullptr, "ql_quant_swiglu_indexed"))) return st;
     GemvArgs a = blank();
     a.w[0] = g;
     a.w[1] = u;
@@ -315,6 +415,7 @@ int ql_quant_down_f32_indexed_accum_ordered(int32_t t, const uint8_t *d, size_t 
     int st = check_weight(t, d, drb, deb, ffn_dim, "ql_quant_down_f32_indexed_accum_ordered");
     if (st) return st;
     if (!act || !ids || !rw || !out) return fail(QL_EINVAL, "ql_quant_down_f32_indexed_accum_ordered: null pointer");
+    if ((st = check_act(act, ffn_dim, nullptr, "ql_quant_down_f32_indexed_accum_ordered"))) return st;
     GemvArgs a = blank();
     a.w[0] = d;
     a.row_bytes[0] = drb;

@@ -110,6 +110,29 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// 3-D tiled tensor copy global -> shared through a tensor map (TMA), completion
+// counted on `bar` in bytes (the full box, including zero-filled out-of-range
+// elements).  The map must live in kernel-parameter (grid constant) memory.
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int c0, int c1, int c2, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (LDGSTS), L2-only, with an L2
+// eviction-priority policy.  Addresses must be 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "l"(policy)
+                 : "memory");
+}
+// Arrive on `bar` once every cp.async this thread has issued so far has landed
+// (the arrival is not pre-counted: the barrier's expected count includes it).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -126,6 +149,15 @@ __device__ __forceinline__ void ffma2(float2 &acc, float2 a, float2 b) {
     const unsigned long long y = *reinterpret_cast<unsigned long long *>(&b);
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(x), "l"(y));
     acc = *reinterpret_cast<float2 *>(&c);
+}
+
+// Packed fp32x2 add (sm_100).
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    unsigned long long c;
+    const unsigned long long x = *reinterpret_cast<unsigned long long *>(&a);
+    const unsigned long long y = *reinterpret_cast<unsigned long long *>(&b);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(c) : "l"(x), "l"(y));
+    return *reinterpret_cast<float2 *>(&c);
 }
 
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {

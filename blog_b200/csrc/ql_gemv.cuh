@@ -27,6 +27,8 @@
 //    epilogues.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (types only; the encoder is resolved at run time)
+
 #include "ql_common.cuh"
 
 namespace ql {
@@ -34,14 +36,21 @@ namespace ql {
 enum SrcKind : int { kSrcPlain = 0, kSrcIndexedRows = 1, kSrcIndexedK = 2 };
 enum EpiKind : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2 };
 
-constexpr int kGemvConsumerWarps = 8;
-constexpr int kGemvThreads = 32 * (1 + kGemvConsumerWarps);
+// 16 warps per CTA (4 per scheduler, 128 registers each): producers, one
+// row-group finisher, consumers.  TMA staging needs one producer warp; cp.async
+// staging uses 4 (bytes in flight scale with the number of issuing warps).
+constexpr int kGemvThreads = 512;
+__host__ __device__ constexpr int gemv_producer_warps(bool tma) { return tma ? 1 : 4; }
+__host__ __device__ constexpr int gemv_consumer_warps(bool tma) { return 16 - gemv_producer_warps(tma) - 1; }
+// Programmatic dependent launch on by default; QL_PDL=0 turns it off.
+bool gemv_pdl_enabled();
 constexpr int kGemvStages = 4;  // most stages (the host may pick fewer to fit shared memory)
 constexpr int kGemvMaxTokens = 4;
 
-// Blocks per stage for each format (about 0.5 KB of each row per stage).
+// Blocks per stage for each format (about 1 KB of each row per stage, so that
+// half the consumer warps get one block each).
 __host__ __device__ constexpr int gemv_seg(int t) {
-    return t == kQ4_K ? 4 : t == kQ6_K ? 2 : t == kQ8_0 ? 16 : t == kQ4_0 ? 32 : t == kQ5_0 ? 24 : 0;
+    return t == kQ4_K ? 8 : t == kQ6_K ? 4 : t == kQ8_0 ? 32 : t == kQ4_0 ? 64 : t == kQ5_0 ? 48 : 0;
 }
 // Shared-memory pitch of one row slot: data + 16 bytes of alignment slack +
 // 16 bytes of over-read slack, rounded so that pitch % 128 == 16 (lanes reading
@@ -49,6 +58,14 @@ __host__ __device__ constexpr int gemv_seg(int t) {
 __host__ __device__ constexpr int gemv_pitch(int t) {
     return ((gemv_seg(t) * block_bytes(t) + 32 + 127) / 128) * 128 + 16;
 }
+
+// Tensor-map (TMA) staging, used for Q4_K: one 3-D box {144 B, 7 blocks, 32 rows}
+// per matrix per stage.  The box lands as [32 rows][7 blocks][144 B], a row
+// pitch of 1008 B (= 112 mod 128), so lanes reading consecutive rows at the
+// same offset fall in distinct 16-byte bank groups.
+constexpr int kTmaSeg = 7;
+__host__ __device__ constexpr int stage_seg(int t, bool tma) { return tma ? kTmaSeg : gemv_seg(t); }
+__host__ __device__ constexpr int stage_pitch(int t, bool tma) { return tma ? kTmaSeg * 144 : gemv_pitch(t); }
 
 struct GemvArgs {
     const uint8_t *w[2];      // weight buffers (raw GGUF blocks); w[1] only for SwiGLU pairs
@@ -70,6 +87,7 @@ struct GemvArgs {
     float *y;                 // output [M][y_stride]
     int64_t y_stride;
     int nst;                  // stages in the shared-memory ring (2..kGemvStages)
+    CUtensorMap tmap[2];      // Q4_K tensor maps {144 B, blocks, rows} (TMA kernels only)
     Plan plan;
     float *part;              // stream-K partial slots [C][2][MT][NMAT][32]
     unsigned *counters;       // stream-K arrival counters [G], zero between launches
@@ -127,14 +145,14 @@ __host__ __device__ inline const uint8_t *gemv_block_ptr(const GemvArgs &a, cons
 struct GemvShape {
     int seg, pitch, stage_bytes, xs_floats, xsum_floats, red_floats, nst, smem_bytes;
 };
-__host__ inline GemvShape gemv_shape(int fmt, int MT, int NMAT, int K, int nst) {
+__host__ inline GemvShape gemv_shape(int fmt, int MT, int NMAT, int K, int nst, bool tma) {
     GemvShape s;
-    s.seg = gemv_seg(fmt);
-    s.pitch = gemv_pitch(fmt);
+    s.seg = stage_seg(fmt, tma);
+    s.pitch = stage_pitch(fmt, tma);
     s.stage_bytes = NMAT * kRowGroup * s.pitch;
     s.xs_floats = MT * K;
     s.xsum_floats = MT * (K / 32);
-    s.red_floats = kGemvConsumerWarps * MT * NMAT * kRowGroup;
+    s.red_floats = 2 * gemv_consumer_warps(tma) * MT * NMAT * kRowGroup;
     s.nst = nst;
     int off = 128;  // mbarriers, inv-rms slots, abort flag
     off += ((s.xs_floats * 4 + 127) / 128) * 128;

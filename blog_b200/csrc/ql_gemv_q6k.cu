@@ -2,5 +2,5 @@
 #include "ql_gemv_impl.cuh"
 
 namespace ql {
-template cudaError_t gemv_launch_fmt<kQ6_K>(int, const GemvArgs &, int, int, cudaStream_t);
+template cudaError_t gemv_launch_fmt<kQ6_K>(int, const GemvArgs &, int, bool, int, cudaStream_t);
 }  // namespace ql

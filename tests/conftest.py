@@ -20,3 +20,11 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def golden():
     return dict(np.load(os.path.join(ROOT, "tests", "golden", "golden.npz")))
+
+
+@pytest.fixture(autouse=True)
+def _release_device_buffers():
+    yield
+    mod = sys.modules.get("gpu_util")
+    if mod is not None:
+        mod.ALIVE.clear()

@@ -11,9 +11,17 @@ def rel_l2(got, ref) -> float:
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
 
 
+# Device buffers made by dev() stay referenced until the test ends: a temporary
+# whose data_ptr() is passed to a kernel must not return to torch's caching
+# allocator before the kernel has been enqueued (a later dev() would reuse it).
+ALIVE = []
+
+
 def dev(a):
     import torch
-    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda:0")
+    t = torch.from_numpy(np.ascontiguousarray(a)).to("cuda:0")
+    ALIVE.append(t)
+    return t
 
 
 def host(t):
