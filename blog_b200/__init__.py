@@ -60,6 +60,7 @@ SIGNATURES = {
     "ql_dequantize_q6k_to_f16": (I, [P, P, I64]),
     "ql_dequantize_q40_to_f16": (I, [P, P, I64]),
     "ql_argmax": (I, [P, I, P]),
+    "ql_argmax_noalloc": (I, [P, I, P]),
     "ql_quant_gemv_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, P, I]),
     "ql_quant_swiglu_ex": (I, [I32, P, P, SZ, SZ, P, I64, P, I64, I, I, I, P, F]),
     "ql_rms_norm_f32": (I, [P, P, P, I, I, F]),
@@ -146,6 +147,11 @@ def dequantize_to_f16(t, src, out, n):
 
 def argmax(logits, n, out_idx):
     _call("ql_argmax", logits, n, out_idx)
+
+
+def argmax_noalloc(logits, n, out_idx):
+    """ql_argmax without device allocation (fixed in-library scratch; see the header)."""
+    _call("ql_argmax_noalloc", logits, n, out_idx)
 
 
 def quant_gemv_ex(t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma=None, eps=0.0, bias=None,

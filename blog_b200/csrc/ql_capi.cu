@@ -268,6 +268,9 @@ GemvArgs blank() {
 }
 
 }  // namespace
+
+// Records `msg` as this thread's last error (for entry points in other files).
+int set_last_error(int code, const char *msg) { return fail(code, msg); }
 }  // namespace ql
 
 using namespace ql;

@@ -108,6 +108,16 @@ QL_API int ql_dequantize_q40_to_f16(const uint8_t *src, uint16_t *out, int64_t n
 /* out_idx[0] = argmax(logits[0..n)), lowest index on ties. */
 QL_API int ql_argmax(const float *logits, int n, int *out_idx);
 
+/* Same result as ql_argmax, without ever allocating device memory.  No
+ * counterpart in the reference.  For callers that cannot let a library call
+ * cudaMalloc: memory owned entirely by the caller's pool, a first argmax that
+ * happens during CUDA-graph capture, or an allocation ban after start-up.  The
+ * partials live in a fixed 8 KB array inside the library's device image: n is
+ * limited to 16,777,216 (larger n returns QL_EINVAL); calls that overlap on the
+ * GPU race on the shared array; the first call on a device performs a one-time
+ * set-up and should come before any stream capture. */
+QL_API int ql_argmax_noalloc(const float *logits, int n, int *out_idx);
+
 /* ---- fused forms (no reference counterpart; fusions the reference runs as
  *      separate rms_norm / add kernels, kernel.cu:80-84,112-147) ------------------ */
 /* y[m*y_stride + o] (=|+=) W[o] . rmsnorm(x[m*x_stride + :]) (+ bias[o]).
