@@ -2,9 +2,9 @@
 
 One step = one decode token of every quantized linear of a Qwen2-7B-shape
 decoder (28 layers x {q, k, v, o, gate, up, down} + LM head) at batch 1 on
-synthetic random-init weights: RMSNorm fused into the q/k/v and gate/up
-GEMVs, SwiGLU fused into gate/up, residual adds fused into o/down, then the
-LM head and a greedy argmax.  Attention itself is outside the measured path
+synthetic random-init weights: q/k/v in one launch with RMSNorm and bias
+fused, SwiGLU fused into gate/up (with RMSNorm), residual adds fused into
+o/down, then the LM head and a greedy argmax.  Attention itself is outside the measured path
 (the attention output is stood in by the q projection, which has o_proj's
 input width), so the step reads exactly the 3.977 GB of quantized weights a
 real decode token reads.
@@ -77,7 +77,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -152,9 +152,7 @@ class DecodeStack:
                 "wd": synth(HIDDEN, self.f_len, 10 * l + 7),
                 "ln1": (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev),
                 "ln2": (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev),
-                "bq": (0.01 * torch.randn(self.qo_len, generator=g)).to(dev),
-                "bk": (0.01 * torch.randn(self.kv_len, generator=g)).to(dev),
-                "bv": (0.01 * torch.randn(self.kv_len, generator=g)).to(dev),
+                "bqkv": (0.01 * torch.randn(self.qo_len + 2 * self.kv_len, generator=g)).to(dev),
             }
             self.layers.append(L)
         self.wlm = synth(self.v_len, HIDDEN, 999)
@@ -162,9 +160,8 @@ class DecodeStack:
         M = batch
         self.h = torch.zeros((M, HIDDEN), device=dev)
         self.h_in = torch.zeros((M, HIDDEN), device=dev)
-        self.q = torch.zeros((M, max(self.qo_len, 1)), device=dev)
-        self.k = torch.zeros((M, max(self.kv_len, 1)), device=dev)
-        self.v = torch.zeros((M, max(self.kv_len, 1)), device=dev)
+        self.qkv_w = self.qo_len + 2 * self.kv_len  # fused q|k|v output width
+        self.qkv = torch.zeros((M, self.qkv_w), device=dev)
         self.act = torch.zeros((M, max(self.f_len, 1)), device=dev)
         self.logits = torch.zeros((M, self.v_len), device=dev)
         self.tok = torch.zeros((M,), dtype=torch.int32, device=dev)
@@ -186,16 +183,14 @@ class DecodeStack:
         self.h.copy_(self.h_in)
         h = self.h.data_ptr()
         for li, L in enumerate(self.layers):
-            Q.quant_gemv_ex(QK, L["wq"].data_ptr(), rbh, h, HIDDEN, self.q.data_ptr(), self.q.shape[1], self.qo_len,
-                            HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bq"].data_ptr())
-            if self.kv_len:
-                Q.quant_gemv_ex(QK, L["wk"].data_ptr(), rbh, h, HIDDEN, self.k.data_ptr(), self.k.shape[1],
-                                self.kv_len, HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bk"].data_ptr())
-                Q.quant_gemv_ex(QK, L["wv"].data_ptr(), rbh, h, HIDDEN, self.v.data_ptr(), self.v.shape[1],
-                                self.kv_len, HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bv"].data_ptr())
-            # o_proj (row-parallel): rank 0 accumulates onto h, others overwrite h with their partial
-            Q.quant_gemv_ex(QK, L["wo"].data_ptr(), Q.row_bytes(QK, self.qo_len), self.q.data_ptr(),
-                            self.q.shape[1], h, HIDDEN, HIDDEN, self.qo_len, M, accumulate=(self.rank == 0))
+            # q, k, v in one launch (stacked sources), RMSNorm and bias fused
+            Q.quant_gemv_stacked_ex(QK, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
+                                    [self.qo_len, self.kv_len, self.kv_len], h, HIDDEN, self.qkv.data_ptr(),
+                                    self.qkv_w, HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr())
+            # o_proj (row-parallel) on the q columns (attention output stand-in): rank 0
+            # accumulates onto h, others overwrite h with their partial
+            Q.quant_gemv_ex(QK, L["wo"].data_ptr(), Q.row_bytes(QK, self.qo_len), self.qkv.data_ptr(),
+                            self.qkv_w, h, HIDDEN, HIDDEN, self.qo_len, M, accumulate=(self.rank == 0))
             if self.world > 1:
                 torch.distributed.all_reduce(self.h)
             sel = events is not None and li in events["layers"]
@@ -224,8 +219,10 @@ class DecodeStack:
             self.token_ids.copy_(self.tok)
 
     def launches_per_step(self):
-        per_layer = 1 + (2 if self.kv_len else 0) + 3
-        return LAYERS * per_layer * ((self.M + 3) // 4) + ((self.M + 3) // 4) + 2 * self.M
+        """Library kernel launches per step: per layer qkv, o, gate/up, down (each in
+        chunks of <= 4 tokens, gate/up <= 2), the LM head, and 2 argmax kernels per token."""
+        c4, c2 = (self.M + 3) // 4, (self.M + 1) // 2
+        return LAYERS * (3 * c4 + c2) + c4 + 2 * self.M
 
 
 # --------------------------------------------------------------------------------------
@@ -257,6 +254,74 @@ def cpu_oracle_rate(sample_layers=2, reps=2):
             "seconds_per_sample": best}
 
 
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gemv_q4k_swiglu_18944x3584.md")
+    try:
+        for line in open(p):
+            if "dram_bytes_per_launch:" in line:
+                return int(line.split("dram_bytes_per_launch:")[1].strip().strip("`").split()[0].strip("`."))
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
+def run_kernel_only(args):
+    """Times one kernel of the step at its bench shape (the ncu profiling target):
+    swiglu = fused RMSNorm + gate/up SwiGLU (18944 x 3584 x 2), down = down + residual
+    (3584 x 18944), qkv = stacked q/k/v (4608 x 3584), lmhead = RMSNorm + LM head."""
+    import torch
+    import blog_b200 as Q
+    torch.cuda.init()
+    Q.init(0)
+    Q.set_stream(torch.cuda.current_stream().cuda_stream)
+    rbh, rbf = Q.row_bytes(QK, HIDDEN), Q.row_bytes(QK, FFN)
+    nbuf = 2  # alternate two weight sets so consecutive launches do not hit in L2
+
+    def synth(rows, rb, k, seed):
+        w = torch.empty((rows, rb), dtype=torch.uint8, device="cuda")
+        Q.synth_quantized(QK, seed, rows, k, 0.02, w.data_ptr())
+        return w
+    gamma = torch.ones(HIDDEN, device="cuda")
+    x = torch.randn(1, FFN, device="cuda")
+    y = torch.zeros(1, VOCAB, device="cuda")
+    if args.kernel_only == "swiglu":
+        ws = [(synth(FFN, rbh, HIDDEN, 2 * i + 1), synth(FFN, rbh, HIDDEN, 2 * i + 2)) for i in range(nbuf)]
+        run = lambda i: Q.quant_swiglu_ex(QK, ws[i][0].data_ptr(), ws[i][1].data_ptr(), rbh, rbh, x.data_ptr(), HIDDEN,
+                                          y.data_ptr(), FFN, FFN, HIDDEN, 1, gamma.data_ptr(), EPS)
+        nbytes = 2 * FFN * rbh
+    elif args.kernel_only == "down":
+        ws = [synth(HIDDEN, rbf, FFN, i + 1) for i in range(nbuf)]
+        run = lambda i: Q.quant_gemv_ex(QK, ws[i].data_ptr(), rbf, x.data_ptr(), FFN, y.data_ptr(), HIDDEN, HIDDEN,
+                                        FFN, 1, accumulate=True)
+        nbytes = HIDDEN * rbf
+    elif args.kernel_only == "qkv":
+        rows = [N_Q * HEAD, N_KV * HEAD, N_KV * HEAD]
+        ws = [[synth(r, rbh, HIDDEN, 3 * i + j + 1) for j, r in enumerate(rows)] for i in range(nbuf)]
+        run = lambda i: Q.quant_gemv_stacked_ex(QK, [w.data_ptr() for w in ws[i]], [rbh] * 3, rows, x.data_ptr(),
+                                                HIDDEN, y.data_ptr(), sum(rows), HIDDEN, 1, gamma.data_ptr(), EPS)
+        nbytes = sum(rows) * rbh
+    else:
+        ws = [synth(VOCAB, rbh, HIDDEN, i + 1) for i in range(nbuf)]
+        run = lambda i: Q.quant_gemv_ex(QK, ws[i].data_ptr(), rbh, x.data_ptr(), HIDDEN, y.data_ptr(), VOCAB, VOCAB,
+                                        HIDDEN, 1, gamma.data_ptr(), EPS)
+        nbytes = VOCAB * rbh
+    for i in range(args.warmup):
+        run(i % nbuf)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        run(i % nbuf)
+    e1.record()
+    torch.cuda.synchronize()
+    Q.check_device()
+    us = e0.elapsed_time(e1) * 1000 / args.steps
+    print(json.dumps({"kernel_only": args.kernel_only, "avg_us": us, "weight_bytes": nbytes,
+                      "GBps": nbytes / us / 1e3, "launches": args.steps}), flush=True)
+    return 0
+
+
 def run_reference(args):
     """--impl reference: the CPU restatement of the reference's arithmetic (the
     reference's only implementation of this path is CUDA; it has no CPU path)."""
@@ -286,15 +351,19 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch32", action="store_true")
+    ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead"],
+                    help="time one kernel of the step at its bench shape (profiling target)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel_only:
+        return run_kernel_only(args)
     args.warmup = max(args.warmup, 3)
 
     import torch
@@ -395,7 +464,7 @@ def main():
             "hbm_roofline_tokens_per_s": hbm * 1e9 / (total_bytes / world),
             "step_weight_GBps": total_bytes / (r1["ms"] / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "traffic": None, "kernel": "qgemv_kernel<Q4_K,MT=1,NMAT=2> fused RMSNorm+gate/up SwiGLU",
+                         "traffic": profile_traffic(), "kernel": "qgemv_kernel<Q4_K,MT=1,NMAT=2> fused RMSNorm+gate/up SwiGLU",
                          "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": r1["kernel_ms"],
                          "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"},
             "e2e": {"value": args.batch / (r1["e2e_ms"] / 1e3), "unit": "tokens/s",

@@ -63,6 +63,7 @@ SIGNATURES = {
     "ql_argmax_noalloc": (I, [P, I, P]),
     "ql_quant_gemv_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, P, I]),
     "ql_quant_swiglu_ex": (I, [I32, P, P, SZ, SZ, P, I64, P, I64, I, I, I, P, F]),
+    "ql_quant_gemv_stacked_ex": (I, [I32, I, P, P, P, P, I64, P, I64, I, I, P, F, P]),
     "ql_rms_norm_f32": (I, [P, P, P, I, I, F]),
     "ql_synth_quantized": (I, [I32, U64, I64, I, F, P]),
     "ql_row_bytes": (SZ, [I32, I]),
@@ -158,6 +159,17 @@ def quant_gemv_ex(t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma=
                   accumulate=False):
     _call("ql_quant_gemv_ex", t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma, eps, bias,
           1 if accumulate else 0)
+
+
+def quant_gemv_stacked_ex(t, weights, row_bytes_list, rows, x, x_stride, y, y_stride, in_dim, m, gamma=None,
+                          eps=0.0, bias=None):
+    """Stacked projections (e.g. fused q/k/v): weights, row_bytes_list, rows are Python sequences (<= 3)."""
+    n = len(weights)
+    W = (C.c_void_p * n)(*weights)
+    RB = (C.c_size_t * n)(*row_bytes_list)
+    R = (C.c_int * n)(*rows)
+    _call("ql_quant_gemv_stacked_ex", t, n, C.cast(W, C.c_void_p), C.cast(RB, C.c_void_p), C.cast(R, C.c_void_p), x,
+          x_stride, y, y_stride, in_dim, m, gamma, eps, bias)
 
 
 def quant_swiglu_ex(t, gw, uw, grb, urb, x, x_stride, act, act_stride, ffn_dim, in_dim, m, gamma=None, eps=0.0):

@@ -188,7 +188,7 @@ bool prepare_tma(int fmt, int kind, GemvArgs &a) {
     if (fmt != kQ4_K || a.U < kTmaSeg) return false;
     const int NMAT = (kind == 2 || kind == 3) ? 2 : 1;
     uint64_t rows = (uint64_t)a.rows;
-    if (kind <= 2) {
+    if (kind <= 2 || kind == 5) {
         if (a.rows < kRowGroup) return false;
     } else if (kind == 3) {
         if (a.rows_per_route % kRowGroup) return false;
@@ -201,6 +201,17 @@ bool prepare_tma(int fmt, int kind, GemvArgs &a) {
         rows = 1ull << 24;
     }
     const int blocks = (kind == 4) ? a.units_per_route : a.U;
+    if (kind == 5) {  // stacked sources: one map per source, each with its own row count
+        const int starts[3] = {0, a.split[0], a.split[1]};
+        const int ends[3] = {a.split[0], a.split[1], a.rows};
+        for (int m = 0; m < kMaxStacked; ++m) {
+            if (ends[m] <= starts[m]) continue;
+            if (ends[m] - starts[m] < kRowGroup) return false;
+            if (!q4k_tensor_map(&a.tmap[m], a.w[m], blocks, (uint64_t)(ends[m] - starts[m]), a.row_bytes[m]))
+                return false;
+        }
+        return true;
+    }
     for (int m = 0; m < NMAT; ++m)
         if (!q4k_tensor_map(&a.tmap[m], a.w[m], blocks, rows, a.row_bytes[m])) return false;
     return true;
@@ -332,6 +343,46 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     a.eps = eps;
     a.bias = bias;
     return run_gemv(t, accumulate ? 1 : 0, a, m, "ql_quant_gemv");
+}
+
+int ql_quant_gemv_stacked_ex(int32_t t, int nsrc, const uint8_t *const *w, const size_t *rb, const int *rows,
+                             const float *x, int64_t xs, float *y, int64_t ys, int in_dim, int m, const float *gamma,
+                             float eps, const float *bias) {
+    t_launches = 0;
+    if (nsrc < 1 || nsrc > kMaxStacked || !w || !rb || !rows)
+        return fail(QL_EINVAL, "ql_quant_gemv_stacked_ex: need 1..3 sources");
+    if (m < 0) return fail(QL_EINVAL, "ql_quant_gemv_stacked_ex: negative size");
+    GemvArgs a = blank();
+    int total = 0;
+    for (int i = 0; i < nsrc; ++i) {
+        int st = check_weight(t, w[i], rb[i], 0, in_dim, "ql_quant_gemv_stacked_ex");
+        if (st) return st;
+        if (rows[i] < 0 || (i < nsrc - 1 && rows[i] % kRowGroup))
+            return fail(QL_EINVAL, "ql_quant_gemv_stacked_ex: every source but the last needs a multiple of 32 rows");
+        a.w[i] = w[i];
+        a.row_bytes[i] = rb[i];
+        total += rows[i];
+        if (i < 2) a.split[i] = total;
+    }
+    for (int i = nsrc; i < kMaxStacked; ++i) {
+        a.w[i] = w[nsrc - 1];
+        a.row_bytes[i] = rb[nsrc - 1];
+        if (i < 2 && i >= nsrc) a.split[i] = total;
+    }
+    if (total == 0 || m == 0) return QL_OK;
+    if (!x || !y) return fail(QL_EINVAL, "ql_quant_gemv_stacked_ex: null x or y");
+    int st = check_act(x, xs, gamma, "ql_quant_gemv_stacked_ex");
+    if (st) return st;
+    a.rows = total;
+    a.K = in_dim;
+    a.x = x;
+    a.x_stride = xs;
+    a.y = y;
+    a.y_stride = ys;
+    a.gamma = gamma;
+    a.eps = eps;
+    a.bias = bias;
+    return run_gemv(t, 5, a, m, "ql_quant_gemv_stacked_ex");
 }
 
 int ql_quant_gemv(int32_t t, const uint8_t *w, size_t rb, const float *x, float *y, int out_dim, int in_dim,

@@ -33,7 +33,11 @@
 
 namespace ql {
 
-enum SrcKind : int { kSrcPlain = 0, kSrcIndexedRows = 1, kSrcIndexedK = 2 };
+// kSrcStacked: up to 3 matrices sharing the activation, stacked by rows (fused
+// q/k/v): rows [0, split0) come from w[0], [split0, split1) from w[1], the rest
+// from w[2]; every split is a multiple of 32 so a row group has one source.
+enum SrcKind : int { kSrcPlain = 0, kSrcIndexedRows = 1, kSrcIndexedK = 2, kSrcStacked = 3 };
+constexpr int kMaxStacked = 3;
 enum EpiKind : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2 };
 
 // 16 warps per CTA (4 per scheduler, 128 registers each): producers, one
@@ -68,9 +72,10 @@ __host__ __device__ constexpr int stage_seg(int t, bool tma) { return tma ? kTma
 __host__ __device__ constexpr int stage_pitch(int t, bool tma) { return tma ? kTmaSeg * 144 : gemv_pitch(t); }
 
 struct GemvArgs {
-    const uint8_t *w[2];      // weight buffers (raw GGUF blocks); w[1] only for SwiGLU pairs
-    size_t row_bytes[2];      // bytes per output row
-    size_t expert_bytes[2];   // bytes per expert (indexed kinds)
+    const uint8_t *w[kMaxStacked];   // weight buffers (raw GGUF blocks): SwiGLU gate/up, or stacked sources
+    size_t row_bytes[kMaxStacked];   // bytes per output row
+    size_t expert_bytes[2];          // bytes per expert (indexed kinds)
+    int split[2];                    // stacked sources: first row of w[1] and of w[2]
     int rows;                 // output rows of the launch (virtual rows for indexed-rows)
     int K;                    // reduction length in elements (virtual length for indexed-K)
     int U;                    // blocks per row = K / block_elems
@@ -87,7 +92,7 @@ struct GemvArgs {
     float *y;                 // output [M][y_stride]
     int64_t y_stride;
     int nst;                  // stages in the shared-memory ring (2..kGemvStages)
-    CUtensorMap tmap[2];      // Q4_K tensor maps {144 B, blocks, rows} (TMA kernels only)
+    CUtensorMap tmap[kMaxStacked];   // Q4_K tensor maps {144 B, blocks, rows} (TMA kernels only)
     Plan plan;
     float *part;              // stream-K partial slots [C][2][MT][NMAT][32]
     unsigned *counters;       // stream-K arrival counters [G], zero between launches
@@ -125,10 +130,22 @@ __host__ __device__ inline bool next_stage(int64_t &t, int64_t t1, int U, int se
 // Address of block `u` of output row `v` of matrix `mat`, or nullptr when the
 // row's expert id is negative (the route is skipped).  `ids` may be a host or
 // device pointer; it is read only for indexed sources.
+// Stacked sources: which matrix holds virtual row v, and its local row.
+__host__ __device__ inline int stacked_source(const GemvArgs &a, int v, int *local) {
+    const int s = (v >= a.split[0]) + (v >= a.split[1]);
+    *local = v - (s == 0 ? 0 : a.split[s - 1]);
+    return s;
+}
+
 template <int SRC, int FMT>
 __host__ __device__ inline const uint8_t *gemv_block_ptr(const GemvArgs &a, const int *ids, int mat, int v, int u) {
     constexpr int BB = block_bytes(FMT);
     if (SRC == kSrcPlain) return a.w[mat] + (size_t)v * a.row_bytes[mat] + (size_t)u * BB;
+    if (SRC == kSrcStacked) {
+        int local;
+        const int s = stacked_source(a, v, &local);
+        return a.w[s] + (size_t)local * a.row_bytes[s] + (size_t)u * BB;
+    }
     if (SRC == kSrcIndexedRows) {
         const int r = v / a.rows_per_route, row = v - r * a.rows_per_route;
         const int e = ids[r];

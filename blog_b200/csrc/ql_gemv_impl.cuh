@@ -391,9 +391,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
                 if (!mbar_wait(&empty[slot], ph ^ 1u, a.err, kErrWaitEmpty)) *abort_flag = 1;
             }
             const bool aborted = *reinterpret_cast<volatile int *>(abort_flag) != 0;
-            int row0 = st.g * kRowGroup, blk0 = st.us;
+            int row0 = st.g * kRowGroup, blk0 = st.us, map = 0;
             bool live = !aborted;
-            if (SRC == kSrcIndexedRows) {  // a row group never straddles a route here
+            if (SRC == kSrcStacked) {
+                map = stacked_source(a, row0, &row0);
+            } else if (SRC == kSrcIndexedRows) {  // a row group never straddles a route here
                 const int r = row0 / a.rows_per_route, e = a.ids[r];
                 live = live && e >= 0;
                 row0 = e * a.rows_per_route + (row0 - r * a.rows_per_route);
@@ -408,7 +410,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
                 uint8_t *sbase = stages + slot * STAGE_BYTES;
 #pragma unroll
                 for (int mat = 0; mat < NMAT; ++mat)
-                    tma_load_3d(sbase + mat * BOX, &a.tmap[mat], 0, blk0, row0, &full[slot]);
+                    tma_load_3d(sbase + mat * BOX, &a.tmap[SRC == kSrcStacked ? map : mat], 0, blk0, row0,
+                                &full[slot]);
             }
             ++it;
         }
@@ -770,7 +773,7 @@ static cudaError_t launch_mt(const GemvArgs &a, int MT, bool tma, int smem, cuda
 }
 
 // kind: 0 plain store, 1 plain add, 2 plain SwiGLU pair, 3 indexed-rows SwiGLU
-// pair (MT = 1), 4 indexed-K add (MT = 1).  `tma` selects tensor-map staging
+// pair (MT = 1), 4 indexed-K add (MT = 1), 5 stacked sources store.  `tma` selects tensor-map staging
 // (Q4_K only; the caller has filled a.tmap).
 template <int FMT>
 cudaError_t gemv_launch_fmt(int kind, const GemvArgs &a, int MT, bool tma, int smem, cudaStream_t s) {
@@ -780,6 +783,7 @@ cudaError_t gemv_launch_fmt(int kind, const GemvArgs &a, int MT, bool tma, int s
     case 2: return launch_mt<FMT, 2, kSrcPlain, kEpiSwiglu>(a, MT, tma, smem, s);
     case 3: return MT == 1 ? launch_tma<FMT, 1, 2, kSrcIndexedRows, kEpiSwiglu>(a, tma, smem, s) : cudaErrorInvalidValue;
     case 4: return MT == 1 ? launch_tma<FMT, 1, 1, kSrcIndexedK, kEpiAdd>(a, tma, smem, s) : cudaErrorInvalidValue;
+    case 5: return launch_mt<FMT, 1, kSrcStacked, kEpiStore>(a, MT, tma, smem, s);
     default: return cudaErrorInvalidValue;
     }
 }

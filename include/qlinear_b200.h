@@ -125,6 +125,14 @@ QL_API int ql_argmax_noalloc(const float *logits, int n, int *out_idx);
 QL_API int ql_quant_gemv_ex(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x, int64_t x_stride,
                      float *y, int64_t y_stride, int out_dim, int in_dim, int m, const float *norm_gamma, float eps,
                      const float *bias, int accumulate);
+/* Fused projections sharing one activation (e.g. q, k and v): the outputs of
+ * nsrc (1..3) matrices, stacked by rows, y[m*y_stride + r] for r < sum(rows),
+ * with one optional RMSNorm and a stacked bias.  Every source but the last must
+ * have a multiple of 32 rows.  w, row_bytes and rows are host arrays of nsrc. */
+QL_API int ql_quant_gemv_stacked_ex(int32_t quant_type, int nsrc, const uint8_t *const *weights,
+                                    const size_t *row_bytes, const int *rows, const float *x, int64_t x_stride,
+                                    float *y, int64_t y_stride, int in_dim, int m, const float *norm_gamma, float eps,
+                                    const float *bias);
 /* act[m*act_stride + f] = SiLU(Wg[f] . n(x_m)) * (Wu[f] . n(x_m)), n = optional RMSNorm. */
 QL_API int ql_quant_swiglu_ex(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,
                        size_t gate_row_bytes, size_t up_row_bytes, const float *x, int64_t x_stride, float *act,

@@ -156,6 +156,26 @@ def test_gemv_ex_fused_rmsnorm_bias_accumulate():
     assert rel_l2(host(y), ref) < TOL
 
 
+@pytest.mark.parametrize("t,rows,k", [(O.Q4_K, (3584, 512, 512), 3584), (O.Q8_0, (896, 128, 128), 896),
+                                      (O.Q4_K, (64, 50), 2048), (O.Q5_0, (32, 32, 7), 1408)])
+def test_stacked_qkv_matches_separate(t, rows, k):
+    """Fused q/k/v (stacked sources) with RMSNorm and bias equals the separate projections."""
+    import torch
+    m, eps = 2, 1e-6
+    ws = [make_weights(t, n, k, seed=200 + i) for i, n in enumerate(rows)]
+    x = _x(210, m, k)
+    gamma = (1.0 + 0.1 * _x(211, 1, k)[0]).astype(np.float32)
+    total = sum(rows)
+    bias = _x(212, 1, total)[0]
+    y = torch.full((m, total), float("nan"), device="cuda:0")
+    rb = O.row_bytes(t, k)
+    Q.quant_gemv_stacked_ex(t, [dev(w).data_ptr() for w in ws], [rb] * len(ws), list(rows), dev(x).data_ptr(), k,
+                            y.data_ptr(), total, k, m, dev(gamma).data_ptr(), eps, dev(bias).data_ptr())
+    xn = O.rmsnorm(x, gamma, eps)
+    ref = np.concatenate([O.gemv(t, w, rb, xn, n, k, m, order=1) for w, n in zip(ws, rows)], axis=1) + bias[None, :]
+    assert rel_l2(host(y), ref) < TOL
+
+
 def test_lm_head_full_size_row_subset():
     """151936 x 4096 Q4_K (350 MB): every output row computed, 512 checked."""
     import torch
