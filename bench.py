@@ -266,17 +266,65 @@ def profile_traffic():
     return None
 
 
+def run_prefill_kernel(args):
+    """Times the tcgen05 prefill GEMM (activation prep + GEMM) on one Qwen2-7B
+    projection at --tokens rows: gate/up (18944 x 3584), down (3584 x 18944),
+    q/k/v (4608 x 3584) or o (3584 x 3584)."""
+    import torch
+    import blog_b200 as Q
+    torch.cuda.init()
+    Q.init(0)
+    Q.set_stream(torch.cuda.current_stream().cuda_stream)
+    n, k = {"prefill_gateup": (FFN, HIDDEN), "prefill_down": (HIDDEN, FFN), "prefill_qkv": ((N_Q + 2 * N_KV) * HEAD, HIDDEN),
+            "prefill_o": (HIDDEN, N_Q * HEAD)}[args.kernel_only]
+    m = args.tokens
+    rb = Q.row_bytes(QK, k)
+    nbuf = 2
+    ws = []
+    for i in range(nbuf):
+        w = torch.empty((n, rb), dtype=torch.uint8, device="cuda")
+        Q.synth_quantized(QK, i + 1, n, k, 0.02, w.data_ptr())
+        ws.append(w)
+    x = torch.randn(m, k, device="cuda")
+    y = torch.empty(m, n, device="cuda")
+    Q.reserve_prefill(m, k)
+    run = lambda i: Q.quant_matmul_ex(QK, ws[i].data_ptr(), rb, x.data_ptr(), k, y.data_ptr(), n, n, k, m, None, 0.0,
+                                      None, False, Q.PATH_TENSOR)
+    for i in range(args.warmup):
+        run(i % nbuf)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        run(i % nbuf)
+    e1.record()
+    torch.cuda.synchronize()
+    Q.check_device()
+    us = e0.elapsed_time(e1) * 1000 / args.steps
+    flops = 2.0 * m * n * k
+    print(json.dumps({"kernel_only": args.kernel_only, "tokens": m, "n": n, "k": k, "avg_us": us,
+                      "TFLOPs": flops / us / 1e6, "launches": 2 * args.steps}), flush=True)
+    return 0
+
+
 def run_kernel_only(args):
     """Times one kernel of the step at its bench shape (the ncu profiling target):
     swiglu = fused RMSNorm + gate/up SwiGLU (18944 x 3584 x 2), down = down + residual
     (3584 x 18944), qkv = stacked q/k/v (4608 x 3584), lmhead = RMSNorm + LM head."""
     import torch
     import blog_b200 as Q
+    if args.kernel_only.startswith("prefill_"):
+        return run_prefill_kernel(args)
     torch.cuda.init()
     Q.init(0)
     Q.set_stream(torch.cuda.current_stream().cuda_stream)
     rbh, rbf = Q.row_bytes(QK, HIDDEN), Q.row_bytes(QK, FFN)
-    nbuf = 2  # alternate two weight sets so consecutive launches do not hit in L2
+    rows_qkv = [N_Q * HEAD, N_KV * HEAD, N_KV * HEAD]
+    nbytes = {"swiglu": 2 * FFN * rbh, "down": HIDDEN * rbf, "qkv": sum(rows_qkv) * rbh}.get(args.kernel_only,
+                                                                                               VOCAB * rbh)
+    # rotate through enough distinct weight sets (>= 300 MB, over twice the 126 MB L2)
+    # that every launch streams its weights from HBM
+    nbuf = max(2, -(-300_000_000 // nbytes))
 
     def synth(rows, rb, k, seed):
         w = torch.empty((rows, rb), dtype=torch.uint8, device="cuda")
@@ -289,23 +337,18 @@ def run_kernel_only(args):
         ws = [(synth(FFN, rbh, HIDDEN, 2 * i + 1), synth(FFN, rbh, HIDDEN, 2 * i + 2)) for i in range(nbuf)]
         run = lambda i: Q.quant_swiglu_ex(QK, ws[i][0].data_ptr(), ws[i][1].data_ptr(), rbh, rbh, x.data_ptr(), HIDDEN,
                                           y.data_ptr(), FFN, FFN, HIDDEN, 1, gamma.data_ptr(), EPS)
-        nbytes = 2 * FFN * rbh
     elif args.kernel_only == "down":
         ws = [synth(HIDDEN, rbf, FFN, i + 1) for i in range(nbuf)]
         run = lambda i: Q.quant_gemv_ex(QK, ws[i].data_ptr(), rbf, x.data_ptr(), FFN, y.data_ptr(), HIDDEN, HIDDEN,
                                         FFN, 1, accumulate=True)
-        nbytes = HIDDEN * rbf
     elif args.kernel_only == "qkv":
-        rows = [N_Q * HEAD, N_KV * HEAD, N_KV * HEAD]
-        ws = [[synth(r, rbh, HIDDEN, 3 * i + j + 1) for j, r in enumerate(rows)] for i in range(nbuf)]
-        run = lambda i: Q.quant_gemv_stacked_ex(QK, [w.data_ptr() for w in ws[i]], [rbh] * 3, rows, x.data_ptr(),
-                                                HIDDEN, y.data_ptr(), sum(rows), HIDDEN, 1, gamma.data_ptr(), EPS)
-        nbytes = sum(rows) * rbh
+        ws = [[synth(r, rbh, HIDDEN, 3 * i + j + 1) for j, r in enumerate(rows_qkv)] for i in range(nbuf)]
+        run = lambda i: Q.quant_gemv_stacked_ex(QK, [w.data_ptr() for w in ws[i]], [rbh] * 3, rows_qkv, x.data_ptr(),
+                                                HIDDEN, y.data_ptr(), sum(rows_qkv), HIDDEN, 1, gamma.data_ptr(), EPS)
     else:
         ws = [synth(VOCAB, rbh, HIDDEN, i + 1) for i in range(nbuf)]
         run = lambda i: Q.quant_gemv_ex(QK, ws[i].data_ptr(), rbh, x.data_ptr(), HIDDEN, y.data_ptr(), VOCAB, VOCAB,
                                         HIDDEN, 1, gamma.data_ptr(), EPS)
-        nbytes = VOCAB * rbh
     for i in range(args.warmup):
         run(i % nbuf)
     torch.cuda.synchronize()
@@ -357,8 +400,10 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch32", action="store_true")
-    ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead"],
+    ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
+                                              "prefill_qkv", "prefill_o"],
                     help="time one kernel of the step at its bench shape (profiling target)")
+    ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -23,6 +23,7 @@ HEADER = os.path.join(os.path.dirname(PKG), "include", "qlinear_b200.h")
 F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 6, 8, 12, 14
 BLOCK = {Q4_0: (32, 18), Q5_0: (32, 22), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
 QL_OK, QL_EINVAL, QL_ECUDA, QL_EDEVICE = 0, 1, 2, 3
+PATH_AUTO, PATH_GEMV, PATH_TENSOR = 0, 1, 2
 
 
 class QLError(RuntimeError):
@@ -64,6 +65,8 @@ SIGNATURES = {
     "ql_quant_gemv_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, P, I]),
     "ql_quant_swiglu_ex": (I, [I32, P, P, SZ, SZ, P, I64, P, I64, I, I, I, P, F]),
     "ql_quant_gemv_stacked_ex": (I, [I32, I, P, P, P, P, I64, P, I64, I, I, P, F, P]),
+    "ql_quant_matmul_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, P, I, I]),
+    "ql_reserve_prefill": (I, [I, I]),
     "ql_rms_norm_f32": (I, [P, P, P, I, I, F]),
     "ql_synth_quantized": (I, [I32, U64, I64, I, F, P]),
     "ql_row_bytes": (SZ, [I32, I]),
@@ -120,6 +123,17 @@ def quant_gemv_add(t, weight, rb, x, y, out_dim, in_dim):
 
 def quant_matmul(t, weight, rb, x, y, out_dim, in_dim, m):
     _call("ql_quant_matmul", t, weight, rb, x, y, out_dim, in_dim, m)
+
+
+def quant_matmul_ex(t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma=None, eps=0.0, bias=None,
+                    accumulate=False, path=PATH_AUTO):
+    """Prefill GEMM; path PATH_TENSOR forces the tcgen05 kernel, PATH_GEMV the streaming engine."""
+    _call("ql_quant_matmul_ex", t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma, eps, bias,
+          1 if accumulate else 0, path)
+
+
+def reserve_prefill(max_tokens, max_in_dim):
+    _call("ql_reserve_prefill", max_tokens, max_in_dim)
 
 
 def quant_swiglu(t, gw, uw, grb, urb, x, act, ffn_dim, in_dim):

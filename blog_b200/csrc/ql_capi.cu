@@ -17,6 +17,7 @@
 
 #include "../../include/qlinear_b200.h"
 #include "ql_common.cuh"
+#include "ql_gemm.cuh"
 #include "ql_gemv.cuh"
 
 namespace ql {
@@ -54,7 +55,15 @@ struct Workspace {
     int *err = nullptr;
     float *am_v = nullptr;
     int *am_i = nullptr;
+    // tensor-core prefill scratch, grown on demand (ql_reserve_prefill)
+    __half *xh = nullptr;
+    size_t xh_cap = 0;
+    float *rinv = nullptr;
+    size_t rinv_cap = 0;
+    float *gpart = nullptr;
+    size_t gpart_cap = 0;
 };
+constexpr int kGemmCounterBase = 1 << 15;  // tensor-core GEMM tiles use counters[32768, 65536)
 
 std::mutex g_mu;
 Workspace g_ws[kMaxDevices];
@@ -153,10 +162,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 std::mutex g_map_mu;
-std::map<std::tuple<uintptr_t, int, uint64_t, size_t>, CUtensorMap> g_maps;
+std::map<std::tuple<uintptr_t, int, uint64_t, size_t, int>, CUtensorMap> g_maps;
 
-bool q4k_tensor_map(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes) {
-    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), blocks, rows, row_bytes);
+// box_rows = 32 with box_blocks = 7 (GEMV ring) or 256 with 1 (tensor-core GEMM).
+bool q4k_tensor_map(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes,
+                    int box_blocks = kTmaSeg, int box_rows = kRowGroup) {
+    const auto key =
+        std::make_tuple(reinterpret_cast<uintptr_t>(base), blocks, rows, row_bytes, box_blocks * 1024 + box_rows);
     std::lock_guard<std::mutex> lk(g_map_mu);
     auto it = g_maps.find(key);
     if (it != g_maps.end()) {
@@ -168,7 +180,7 @@ bool q4k_tensor_map(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t 
     CUtensorMap m;
     const cuuint64_t dims[3] = {144, (cuuint64_t)blocks, rows};
     const cuuint64_t strides[2] = {144, (cuuint64_t)row_bytes};
-    const cuuint32_t box[3] = {144, (cuuint32_t)kTmaSeg, (cuuint32_t)kRowGroup};
+    const cuuint32_t box[3] = {144, (cuuint32_t)box_blocks, (cuuint32_t)box_rows};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -272,6 +284,106 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
     return QL_OK;
 }
 
+// ---- tensor-core prefill GEMM ---------------------------------------------------
+// Grows the prefill scratch to hold `tokens` x `k` f16 activations, `tokens` row
+// scales and `part_floats` split-K partials.
+int ensure_prefill(Workspace *ws, size_t tokens, size_t k, size_t part_floats) {
+    cudaError_t e;
+    if (tokens * k > ws->xh_cap) {
+        if (ws->xh) cudaFree(ws->xh);
+        ws->xh = nullptr;
+        ws->xh_cap = 0;
+        if ((e = cudaMalloc(&ws->xh, tokens * k * sizeof(__half))) != cudaSuccess) return cuda_fail(e, "prefill scratch");
+        ws->xh_cap = tokens * k;
+    }
+    if (tokens > ws->rinv_cap) {
+        if (ws->rinv) cudaFree(ws->rinv);
+        ws->rinv = nullptr;
+        ws->rinv_cap = 0;
+        if ((e = cudaMalloc(&ws->rinv, tokens * sizeof(float))) != cudaSuccess) return cuda_fail(e, "prefill scratch");
+        ws->rinv_cap = tokens;
+    }
+    if (part_floats > ws->gpart_cap) {
+        if (ws->gpart) cudaFree(ws->gpart);
+        ws->gpart = nullptr;
+        ws->gpart_cap = 0;
+        if ((e = cudaMalloc(&ws->gpart, part_floats * sizeof(float))) != cudaSuccess)
+            return cuda_fail(e, "prefill scratch");
+        ws->gpart_cap = part_floats;
+    }
+    return QL_OK;
+}
+
+int tc_min_tokens() {
+    static const int v = [] {
+        const char *e = getenv("QL_TC_MIN_M");
+        return e ? atoi(e) : 8;
+    }();
+    return v;
+}
+
+// Whether the tensor-core GEMM can run this shape (Q4_K, K % 256, TMA-compatible strides).
+bool tc_eligible(int t, size_t rb, int K) { return t == kQ4_K && K % 256 == 0 && rb % 16 == 0; }
+
+// Splits of K per output tile so that small grids still cover the SMs.
+int choose_ksplit(int64_t tiles, int nsb, int sms) {
+    if (tiles >= sms) return 1;
+    int ks = (int)(sms / tiles);
+    if (ks > nsb) ks = nsb;
+    if (ks > 32) ks = 32;
+    return ks < 1 ? 1 : ks;
+}
+
+int run_gemm_tc(const uint8_t *w, size_t rb, const float *x, int64_t xs, float *y, int64_t ys, int N, int K, int M,
+                const float *gamma, float eps, const float *bias, int accumulate, const char *what) {
+    int st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    const int nsb = K / 256;
+    const int64_t mt = (M + kGemmBM - 1) / kGemmBM, nt = (N + kGemmBN - 1) / kGemmBN, tiles = mt * nt;
+    if (mt > 65535 || nt > 65535) return fail(QL_EINVAL, std::string(what) + ": shape too large for the tensor-core grid");
+    const int ks = choose_ksplit(tiles, nsb, ws->sms);
+    if (ks > 1 && tiles > (int64_t)(kMaxGroups - kGemmCounterBase))
+        return fail(QL_EINVAL, std::string(what) + ": too many tiles");
+    if ((st = ensure_prefill(ws, (size_t)M, (size_t)K, ks > 1 ? (size_t)tiles * ks * kGemmTileFloats : 0))) return st;
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return fail(QL_ECUDA, std::string(what) + ": cuTensorMapEncodeTiled unavailable");
+    GemmArgs a;
+    memset(&a, 0, sizeof(a));
+    if (!q4k_tensor_map(&a.tm_w, w, nsb, (uint64_t)N, rb, 1, kGemmBN))
+        return fail(QL_ECUDA, std::string(what) + ": weight tensor map");
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+        const cuuint64_t strides[1] = {(cuuint64_t)K * sizeof(__half)};
+        const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)kGemmBM};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult r = enc(&a.tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws->xh, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(QL_ECUDA, std::string(what) + ": activation tensor map");
+    }
+    a.rinv = ws->rinv;
+    a.bias = bias;
+    a.y = y;
+    a.accumulate = accumulate;
+    a.y_stride = ys;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.nsb = nsb;
+    a.ksplit = ks;
+    a.part = ws->gpart;
+    a.counters = ws->counters + kGemmCounterBase;
+    a.err = ws->err;
+    cudaError_t e = gemm_xprep_launch(x, xs, gamma, eps, ws->xh, ws->rinv, M, K, g_stream);
+    ++t_launches;
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    e = gemm_q4k_launch(a, g_stream);
+    ++t_launches;
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return QL_OK;
+}
+
 GemvArgs blank() {
     GemvArgs a;
     memset(&a, 0, sizeof(a));
@@ -330,6 +442,8 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     if (st) return st;
     if (!x || !y) return fail(QL_EINVAL, "ql_quant_gemv: null x or y");
     if ((st = check_act(x, xs, gamma, "ql_quant_gemv"))) return st;
+    if (m >= tc_min_tokens() && tc_eligible(t, rb, in_dim))
+        return run_gemm_tc(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate, "ql_quant_gemv");
     GemvArgs a = blank();
     a.w[0] = w;
     a.row_bytes[0] = rb;
@@ -343,6 +457,48 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     a.eps = eps;
     a.bias = bias;
     return run_gemv(t, accumulate ? 1 : 0, a, m, "ql_quant_gemv");
+}
+
+int ql_quant_matmul_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int64_t xs, float *y, int64_t ys,
+                       int out_dim, int in_dim, int m, const float *gamma, float eps, const float *bias, int accumulate,
+                       int path) {
+    t_launches = 0;
+    if (path < QL_PATH_AUTO || path > QL_PATH_TENSOR) return fail(QL_EINVAL, "ql_quant_matmul_ex: unknown path");
+    if (out_dim < 0 || m < 0) return fail(QL_EINVAL, "ql_quant_matmul_ex: negative size");
+    if (out_dim == 0 || m == 0) return QL_OK;
+    int st = check_weight(t, w, rb, 0, in_dim, "ql_quant_matmul_ex");
+    if (st) return st;
+    if (!x || !y) return fail(QL_EINVAL, "ql_quant_matmul_ex: null x or y");
+    if ((st = check_act(x, xs, gamma, "ql_quant_matmul_ex"))) return st;
+    const bool tc = tc_eligible(t, rb, in_dim);
+    if (path == QL_PATH_TENSOR && !tc)
+        return fail(QL_EINVAL, "ql_quant_matmul_ex: the tensor-core path needs Q4_K, in_dim % 256 == 0 and "
+                               "row_bytes % 16 == 0");
+    if (path == QL_PATH_TENSOR || (path == QL_PATH_AUTO && tc && m >= tc_min_tokens()))
+        return run_gemm_tc(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate,
+                           "ql_quant_matmul_ex");
+    GemvArgs a = blank();
+    a.w[0] = w;
+    a.row_bytes[0] = rb;
+    a.rows = out_dim;
+    a.K = in_dim;
+    a.x = x;
+    a.x_stride = xs;
+    a.y = y;
+    a.y_stride = ys;
+    a.gamma = gamma;
+    a.eps = eps;
+    a.bias = bias;
+    return run_gemv(t, accumulate ? 1 : 0, a, m, "ql_quant_matmul_ex");
+}
+
+int ql_reserve_prefill(int max_tokens, int max_in_dim) {
+    if (max_tokens < 0 || max_in_dim < 0) return fail(QL_EINVAL, "ql_reserve_prefill: negative size");
+    int st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    // split-K partials exist only for grids of fewer tiles than SMs: at most 2 * sms tile-splits
+    return ensure_prefill(ws, (size_t)max_tokens, (size_t)max_in_dim, (size_t)2 * ws->sms * kGemmTileFloats);
 }
 
 int ql_quant_gemv_stacked_ex(int32_t t, int nsrc, const uint8_t *const *w, const size_t *rb, const int *rows,

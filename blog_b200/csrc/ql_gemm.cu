@@ -1,0 +1,443 @@
+// ql_gemm.cu -- tcgen05 prefill GEMM over GGUF Q4_K weights (see ql_gemm.cuh).
+#include "ql_gemm.cuh"
+
+namespace ql {
+namespace {
+
+// ---------------------------------------------------------------------------
+// PTX wrappers: TMA 2-D load, TMEM allocation, tcgen05 MMA / commit / load.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, f16 inputs, f32 accumulate.
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// Arrive (once) on `bar` when every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns of TMEM -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row
+// atoms of 1024 B (stride byte offset), leading byte offset unused (1).
+__device__ __forceinline__ uint64_t sw128_desc(const void *p) {
+    const uint64_t a = smem_u32(p);
+    return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M x N.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kGemmBN >> 3) << 17) | ((uint32_t)(kGemmBM >> 4) << 24);
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// (1024 + n) from a nibble pair placed at bits 0-3 / 16-19 -> n * D - M, in f16.
+__device__ __forceinline__ uint32_t deq2(uint32_t nib, __half2 D, __half2 negM) {
+    const __half2 h = bits_h2(nib | 0x64006400u);
+    return h2_bits(__hfma2(__hsub2(h, __float2half2_rn(1024.f)), D, negM));
+}
+
+// ---------------------------------------------------------------------------
+// Activation preparation (one CTA per row).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gemm_xprep_kernel(const float *__restrict__ x, int64_t x_stride,
+                                                         const float *__restrict__ gamma, float eps,
+                                                         __half *__restrict__ xh, float *__restrict__ rinv, int K) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int m = blockIdx.x;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)m * x_stride);
+    const float4 *gr = reinterpret_cast<const float4 *>(gamma);
+    float mx = 0.f, ss = 0.f;
+    bool nan = false;
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        float4 v = xr[i];
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        if (gamma) {
+            const float4 g = gr[i];
+            v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        nan = nan || v.x != v.x || v.y != v.y || v.z != v.z || v.w != v.w;
+    }
+    if (nan) mx = __int_as_float(0x7f800000);
+    __shared__ float red[2][8];
+    for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        red[0][threadIdx.x >> 5] = mx;
+        red[1][threadIdx.x >> 5] = ss;
+    }
+    __syncthreads();
+    mx = red[0][0];
+    ss = red[1][0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+        mx = fmaxf(mx, red[0][w]);
+        ss += red[1][w];
+    }
+    // s = 2^k with max|x| * s in [2^13, 2^14); s = 1 for an all-zero or non-finite row.
+    int k = 0;
+    if (mx > 0.f && mx < __int_as_float(0x7f800000)) {
+        int ex;
+        frexpf(mx, &ex);  // mx = f * 2^ex, f in [0.5, 1)
+        k = 14 - ex;
+        k = k > 126 ? 126 : k;
+    }
+    const float s = __int_as_float((127 + k) << 23), si = __int_as_float((127 - k) << 23);
+    if (threadIdx.x == 0) rinv[m] = gamma ? si * rsqrtf(ss / (float)K + eps) : si;
+    uint4 *out = reinterpret_cast<uint4 *>(xh + (size_t)m * K);
+    for (int g = threadIdx.x; g < K / 8; g += blockDim.x) {
+        float4 a = xr[2 * g], b = xr[2 * g + 1];
+        if (gamma) {
+            const float4 ga = gr[2 * g], gb = gr[2 * g + 1];
+            a.x *= ga.x; a.y *= ga.y; a.z *= ga.z; a.w *= ga.w;
+            b.x *= gb.x; b.y *= gb.y; b.z *= gb.z; b.w *= gb.w;
+        }
+        uint4 o;  // positions 0..7 <- elements 0,2,1,3,4,6,5,7
+        o.x = h2_bits(__floats2half2_rn(a.x * s, a.z * s));
+        o.y = h2_bits(__floats2half2_rn(a.y * s, a.w * s));
+        o.z = h2_bits(__floats2half2_rn(b.x * s, b.z * s));
+        o.w = h2_bits(__floats2half2_rn(b.y * s, b.w * s));
+        out[g] = o;
+    }
+}
+
+// Epilogue store of 32 consecutive outputs of one row: y = acc * scale (+ bias) (+ y).
+__device__ __forceinline__ void store_row32(float *yp, const float *bias, const uint32_t (&v)[32], float scale,
+                                            int nv, int accumulate) {
+    if (nv >= 32 && (reinterpret_cast<uintptr_t>(yp) & 15) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            float4 o = make_float4(__uint_as_float(v[i]) * scale, __uint_as_float(v[i + 1]) * scale,
+                                   __uint_as_float(v[i + 2]) * scale, __uint_as_float(v[i + 3]) * scale);
+            if (bias) {
+                const float4 b = *reinterpret_cast<const float4 *>(bias + i);
+                o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
+            }
+            if (accumulate) {
+                const float4 p = *reinterpret_cast<const float4 *>(yp + i);
+                o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+            }
+            *reinterpret_cast<float4 *>(yp + i) = o;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < nv) {
+                float o = __uint_as_float(v[i]) * scale;
+                if (bias) o += bias[i];
+                if (accumulate) o += yp[i];
+                yp[i] = o;
+            }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// The GEMM.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_constant__ GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = sA + kGemmNA * kGemmABytes;
+    uint8_t *sR = sB + kGemmNB * kGemmBBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sR + kGemmNR * kGemmRBytes);
+    uint64_t *a_full = bars, *a_empty = a_full + kGemmNA;
+    uint64_t *b_full = a_empty + kGemmNA, *b_empty = b_full + kGemmNB;
+    uint64_t *r_full = b_empty + kGemmNB, *r_empty = r_full + kGemmNR;
+    uint64_t *acc_full = r_empty + kGemmNR;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *last_flag = const_cast<int *>(abort_flag) + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
+    const int s0 = (int)((int64_t)blockIdx.z * a.nsb / a.ksplit);
+    const int s1 = (int)((int64_t)(blockIdx.z + 1) * a.nsb / a.ksplit);
+    const int nsbl = s1 - s0, nch = 4 * nsbl;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kGemmNA; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < kGemmNB; ++i) { mbar_init(&b_full[i], 8); mbar_init(&b_empty[i], 1); }
+        for (int i = 0; i < kGemmNR; ++i) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], 8); }
+        mbar_init(acc_full, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kGemmBN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            int issued_r = 0, issued_a = 0;
+            for (int sl = 0; sl < nsbl && !*abort_flag; ++sl) {
+                const int rs = sl % kGemmNR;
+                if (sl >= kGemmNR && !mbar_wait(&r_empty[rs], (uint32_t)(sl / kGemmNR - 1) & 1u, a.err, kErrWaitEmpty)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&r_full[rs], kGemmRBytes);
+                tma_load_3d(sR + rs * kGemmRBytes, &a.tm_w, 0, s0 + sl, n0, &r_full[rs]);
+                issued_r = sl + 1;
+                for (int p = 0; p < 4; ++p) {
+                    const int c = 4 * sl + p, as = c % kGemmNA;
+                    if (c >= kGemmNA &&
+                        !mbar_wait(&a_empty[as], (uint32_t)(c / kGemmNA - 1) & 1u, a.err, kErrWaitEmpty)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&a_full[as], kGemmABytes);
+                    tma_load_2d(sA + as * kGemmABytes, &a.tm_x, (4 * (s0 + sl) + p) * kGemmBK, m0, &a_full[as]);
+                    issued_a = c + 1;
+                }
+            }
+            // Never leave with copies in flight: wait (bounded) for the last fill of every slot.
+            for (int j = issued_r > kGemmNR ? issued_r - kGemmNR : 0; j < issued_r; ++j)
+                mbar_wait(&r_full[j % kGemmNR], (uint32_t)(j / kGemmNR) & 1u, nullptr, 0);
+            for (int j = issued_a > kGemmNA ? issued_a - kGemmNA : 0; j < issued_a; ++j)
+                mbar_wait(&a_full[j % kGemmNA], (uint32_t)(j / kGemmNA) & 1u, nullptr, 0);
+        }
+    } else if (warp == 1) {
+        // ------------------------------- MMA issuer -------------------------------
+        if (lane == 0) {
+            for (int c = 0; c < nch; ++c) {
+                const int as = c % kGemmNA, bs = c % kGemmNB;
+                if (*abort_flag || !mbar_wait(&a_full[as], (uint32_t)(c / kGemmNA) & 1u, a.err, kErrWaitFull) ||
+                    !mbar_wait(&b_full[bs], (uint32_t)(c / kGemmNB) & 1u, a.err, kErrWaitFull)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk)
+                    mma_f16(tmem, sw128_desc(sA + as * kGemmABytes + 32 * kk), sw128_desc(sB + bs * kGemmBBytes + 32 * kk),
+                            kIdesc, (c | kk) != 0);
+                mma_commit(&a_empty[as]);
+                mma_commit(&b_empty[bs]);
+            }
+            mma_commit(acc_full);
+            // All MMAs complete before the CTA may free TMEM.
+            mbar_wait(acc_full, 0u, a.err, kErrWaitFull);
+        }
+        __syncwarp();
+    } else {
+        // ----------------------- dequantizers, then epilogue -----------------------
+        const int r = threadIdx.x - 64;  // weight row of the tile
+        for (int sl = 0; sl < nsbl; ++sl) {
+            const int rs = sl % kGemmNR;
+            // every wait's outcome is made warp-uniform: the warp-synchronous code below needs all lanes
+            if (!__all_sync(0xffffffffu,
+                            !*abort_flag && mbar_wait(&r_full[rs], (uint32_t)(sl / kGemmNR) & 1u, a.err, kErrWaitFull))) {
+                *abort_flag = 1;
+                break;
+            }
+            const uint8_t *blk = sR + rs * kGemmRBytes + r * 144;
+            const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+            const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+            // q4k_scale_min (reference kernel.cu:913-921), all eight sub-blocks as packed bytes
+            const uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
+            const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+            const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+            bool ok = true;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const int c = 4 * sl + p, bs = c % kGemmNB;
+                if (c >= kGemmNB &&
+                    !__all_sync(0xffffffffu, !*abort_flag && mbar_wait(&b_empty[bs], (uint32_t)(c / kGemmNB - 1) & 1u,
+                                                                       a.err, kErrWaitEmpty))) {
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                const uint32_t scw = p < 2 ? sc03 : sc47, mw = p < 2 ? m03 : m47;
+                const int sh0 = 16 * (p & 1), sh1 = sh0 + 8;
+                const __half2 D0 = __float2half2_rn(d * (float)((scw >> sh0) & 0xFFu));
+                const __half2 M0 = __hneg2(__float2half2_rn(dmin * (float)((mw >> sh0) & 0xFFu)));
+                const __half2 D1 = __float2half2_rn(d * (float)((scw >> sh1) & 0xFFu));
+                const __half2 M1 = __hneg2(__float2half2_rn(dmin * (float)((mw >> sh1) & 0xFFu)));
+                const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
+                const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
+                const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                uint8_t *brow = sB + bs * kGemmBBytes + r * 128;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t w0 = W[2 * j], w1 = W[2 * j + 1];
+                    uint4 lo, hi;  // sub-block 2p (low nibbles) and 2p+1 (high nibbles), elements 8j..8j+7
+                    lo.x = deq2(w0 & 0x000F000Fu, D0, M0);
+                    lo.y = deq2((w0 >> 8) & 0x000F000Fu, D0, M0);
+                    lo.z = deq2(w1 & 0x000F000Fu, D0, M0);
+                    lo.w = deq2((w1 >> 8) & 0x000F000Fu, D0, M0);
+                    hi.x = deq2((w0 >> 4) & 0x000F000Fu, D1, M1);
+                    hi.y = deq2((w0 >> 12) & 0x000F000Fu, D1, M1);
+                    hi.z = deq2((w1 >> 4) & 0x000F000Fu, D1, M1);
+                    hi.w = deq2((w1 >> 12) & 0x000F000Fu, D1, M1);
+                    *reinterpret_cast<uint4 *>(brow + ((j ^ (r & 7)) << 4)) = lo;
+                    *reinterpret_cast<uint4 *>(brow + (((4 + j) ^ (r & 7)) << 4)) = hi;
+                }
+                fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_full[bs]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[rs]);
+            if (!ok) break;
+        }
+
+        // -------------------------------- epilogue --------------------------------
+        // warp-uniform: tcgen05.ld is a warp-collective instruction
+        const bool ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait(acc_full, 0u, a.err, kErrWaitFull));
+        tc_fence_after();
+        const int q = warp & 3, hcol = (warp - 2) >> 2;  // TMEM lane quadrant, column half
+        const int row = 32 * q + lane, gm = m0 + row;
+        const float rs_m = (ok && gm < a.M) ? a.rinv[gm] : 0.f;
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        float *tp = a.part + ((size_t)tile * a.ksplit + blockIdx.z) * kGemmTileFloats + (size_t)row * kGemmBN;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+            if (!ok) break;
+            uint32_t v[32];
+            const int col = hcol * 128 + cc * 32;
+            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col, v);
+            if (a.ksplit == 1) {
+                if (gm < a.M) {
+                    float *yp = a.y + (size_t)gm * a.y_stride + n0 + col;
+                    const int nv = a.N - (n0 + col);
+                    store_row32(yp, a.bias ? a.bias + n0 + col : nullptr, v, rs_m, nv, a.accumulate);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    __stcg(reinterpret_cast<float4 *>(tp + col + i),
+                           make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
+                                       __uint_as_float(v[i + 3])));
+            }
+        }
+        if (a.ksplit > 1) {
+            // The last of the tile's K-split CTAs sums the partial tiles in split order.
+            // Every dequantizer thread takes both barriers, whatever its `ok`.
+            __threadfence();
+            named_bar_sync(1, 256);
+            if (threadIdx.x == 64) {
+                int last = 0;
+                if (ok) last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.ksplit - 1);
+                *last_flag = last;
+            }
+            named_bar_sync(1, 256);
+            if (ok && *last_flag) {
+                __threadfence();
+                const float *base = a.part + (size_t)tile * a.ksplit * kGemmTileFloats + (size_t)row * kGemmBN;
+                for (int cc = 0; cc < 4; ++cc) {
+                    const int col = hcol * 128 + cc * 32;
+                    float acc[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+                    for (int z = 0; z < a.ksplit; ++z) {
+                        const float4 *pz = reinterpret_cast<const float4 *>(base + (size_t)z * kGemmTileFloats + col);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 t = __ldcg(pz + i);
+                            acc[4 * i] += t.x; acc[4 * i + 1] += t.y; acc[4 * i + 2] += t.z; acc[4 * i + 3] += t.w;
+                        }
+                    }
+                    if (gm < a.M) {
+                        uint32_t v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[i]);
+                        store_row32(a.y + (size_t)gm * a.y_stride + n0 + col, a.bias ? a.bias + n0 + col : nullptr, v,
+                                    rs_m, a.N - (n0 + col), a.accumulate);
+                    }
+                }
+                if (threadIdx.x == 64) a.counters[tile] = 0u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kGemmBN);
+    }
+}
+
+}  // namespace
+
+cudaError_t gemm_xprep_launch(const float *x, int64_t x_stride, const float *gamma, float eps, __half *xh,
+                              float *rinv, int M, int K, cudaStream_t s) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = gemv_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemm_xprep_kernel, x, x_stride, gamma, eps, xh, rinv, K);
+}
+
+cudaError_t gemm_q4k_launch(const GemmArgs &a, cudaStream_t s) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((a.M + kGemmBM - 1) / kGemmBM, (a.N + kGemmBN - 1) / kGemmBN, a.ksplit);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = kGemmSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = gemv_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemm_q4k_kernel, a);
+}
+
+}  // namespace ql

@@ -70,22 +70,20 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *const (&blk)[NMAT], cons
                 const uint4 qa = *reinterpret_cast<const uint4 *>(blk[mat] + 16 + 32 * p);
                 const uint4 qb = *reinterpret_cast<const uint4 *>(blk[mat] + 32 + 32 * p);
                 const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+                // Two packed accumulators (fma.rn.f32x2): a = sub-block 2p, b = 2p+1;
+                // each lane of a pair sums every other element, as two scalar chains would.
+                float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const uint32_t w = wq[i], w2 = w >> 12;
-                    a0 = fmaf(dn(w & 0x0000000Fu), xl[i].x, a0);
-                    a1 = fmaf(dn(w & 0x00000F00u), xl[i].y, a1);
-                    a0 = fmaf(dn(w & 0x000F0000u), xl[i].z, a0);
-                    a1 = fmaf(dn(w2 & 0x0000F000u), xl[i].w, a1);
-                    b0 = fmaf(dn(w & 0x000000F0u), xh[i].x, b0);
-                    b1 = fmaf(dn(w & 0x0000F000u), xh[i].y, b1);
-                    b0 = fmaf(dn(w2 & 0x00000F00u), xh[i].z, b0);
-                    b1 = fmaf(dn(w2 & 0x000F0000u), xh[i].w, b1);
+                    ffma2(a, make_float2(dn(w & 0x0000000Fu), dn(w & 0x00000F00u)), make_float2(xl[i].x, xl[i].y));
+                    ffma2(a, make_float2(dn(w & 0x000F0000u), dn(w2 & 0x0000F000u)), make_float2(xl[i].z, xl[i].w));
+                    ffma2(b, make_float2(dn(w & 0x000000F0u), dn(w & 0x0000F000u)), make_float2(xh[i].x, xh[i].y));
+                    ffma2(b, make_float2(dn(w2 & 0x00000F00u), dn(w2 & 0x000F0000u)), make_float2(xh[i].z, xh[i].w));
                 }
                 float r = acc[mat][m];
-                r = fmaf(D0, a0 + a1, r);
-                r = fmaf(D1, b0 + b1, r);
+                r = fmaf(D0, a.x + a.y, r);
+                r = fmaf(D1, b.x + b.y, r);
                 r = fmaf(-M0, X0, r);
                 r = fmaf(-M1, X1, r);
                 acc[mat][m] = r;
@@ -169,20 +167,16 @@ __device__ __forceinline__ void unit_q40(const uint8_t *const (&blk)[NMAT], cons
         load_words_u16aligned<4>(blk[mat] + 2, wq);
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-            float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+            float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t w = wq[i], w2 = w >> 12;
-                a0 = fmaf(dn(w & 0x0000000Fu), xl[m][i].x, a0);
-                a1 = fmaf(dn(w & 0x00000F00u), xl[m][i].y, a1);
-                a0 = fmaf(dn(w & 0x000F0000u), xl[m][i].z, a0);
-                a1 = fmaf(dn(w2 & 0x0000F000u), xl[m][i].w, a1);
-                b0 = fmaf(dn(w & 0x000000F0u), xh[m][i].x, b0);
-                b1 = fmaf(dn(w & 0x0000F000u), xh[m][i].y, b1);
-                b0 = fmaf(dn(w2 & 0x00000F00u), xh[m][i].z, b0);
-                b1 = fmaf(dn(w2 & 0x000F0000u), xh[m][i].w, b1);
+                ffma2(a, make_float2(dn(w & 0x0000000Fu), dn(w & 0x00000F00u)), make_float2(xl[m][i].x, xl[m][i].y));
+                ffma2(a, make_float2(dn(w & 0x000F0000u), dn(w2 & 0x0000F000u)), make_float2(xl[m][i].z, xl[m][i].w));
+                ffma2(b, make_float2(dn(w & 0x000000F0u), dn(w & 0x0000F000u)), make_float2(xh[m][i].x, xh[m][i].y));
+                ffma2(b, make_float2(dn(w2 & 0x00000F00u), dn(w2 & 0x000F0000u)), make_float2(xh[m][i].z, xh[m][i].w));
             }
-            float r = fmaf(d * pow2f(53), (a0 + a1) + (b0 + b1), acc[mat][m]);
+            float r = fmaf(d * pow2f(53), (a.x + a.y) + (b.x + b.y), acc[mat][m]);
             acc[mat][m] = fmaf(-8.0f * d, X[m], r);
         }
     }

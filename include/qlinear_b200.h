@@ -72,6 +72,29 @@ QL_API int ql_quant_gemv_add(int32_t quant_type, const uint8_t *weight, size_t r
 /* Same contract as ql_quant_gemv, intended for m > 1 (prefill).  kernel.cuh:42-43. */
 QL_API int ql_quant_matmul(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x, float *y,
                     int out_dim, int in_dim, int m);
+/* Prefill GEMM with a selectable path and fused extras (no reference twin; the
+ * reference runs prefill as launch_quant_matmul, kernel.cuh:42-43, or as
+ * dequantize-to-f16 + cuBLAS, TensorTool.cpp:127-144):
+ *   y[m, o] (+)= scale_m * sum_k W[o, k] * g[k] * x[m, k] + bias[o]
+ * with x rows x_stride floats apart, y rows y_stride apart, optional fused RMSNorm
+ * (gamma != NULL: scale_m = 1/sqrt(mean_k x[m,k]^2 + eps), g = gamma; else 1),
+ * optional bias, accumulate != 0 adds into y.  path: QL_PATH_AUTO picks by shape;
+ * QL_PATH_GEMV forces the CUDA-core streaming engine (fp32 activations, exact
+ * decode); QL_PATH_TENSOR forces the tcgen05 tensor-core GEMM (Q4_K, in_dim a
+ * multiple of 256; activations and dequantized weights rounded to f16, fp32
+ * accumulation; QL_EINVAL when the shape or dtype does not qualify). */
+#define QL_PATH_AUTO 0
+#define QL_PATH_GEMV 1
+#define QL_PATH_TENSOR 2
+QL_API int ql_quant_matmul_ex(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x,
+                              int64_t x_stride, float *y, int64_t y_stride, int out_dim, int in_dim, int m,
+                              const float *gamma, float eps, const float *bias, int accumulate, int path);
+/* Reserve the tensor-core path's scratch (f16 activations, row scales, split-K
+ * partial tiles) on the current device for up to max_tokens x max_in_dim, so later
+ * prefill calls of at most that size allocate nothing (e.g. inside graph capture).
+ * Larger calls grow the scratch with cudaMalloc. */
+QL_API int ql_reserve_prefill(int max_tokens, int max_in_dim);
+
 /* act[f] = SiLU(Wg[f] . x) * (Wu[f] . x).  kernel.cuh:65-67. */
 QL_API int ql_quant_swiglu(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,
                     size_t gate_row_bytes, size_t up_row_bytes, const float *x, float *act, int ffn_dim,
