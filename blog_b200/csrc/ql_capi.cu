@@ -60,10 +60,7 @@ struct Workspace {
     size_t xh_cap = 0;
     float *rinv = nullptr;
     size_t rinv_cap = 0;
-    float *gpart = nullptr;
-    size_t gpart_cap = 0;
 };
-constexpr int kGemmCounterBase = 1 << 15;  // tensor-core GEMM tiles use counters[32768, 65536)
 
 std::mutex g_mu;
 Workspace g_ws[kMaxDevices];
@@ -237,6 +234,27 @@ int check_act(const float *x, int64_t x_stride, const float *gamma, const char *
     return QL_OK;
 }
 
+// Weight stages a GEMV CTA issues before its activations are staged (the rest
+// wait, so the activation loads are not queued behind the weight stream).
+int gemv_pre_x() {
+    static const int v = [] {
+        const char *e = getenv("QL_GEMV_PRE");
+        return e ? atoi(e) : 1;
+    }();
+    return v;
+}
+
+// Most ring stages a GEMV CTA keeps in flight (2..4).  More stages than needed
+// to cover memory latency only lengthen the memory queues every other load waits in.
+int gemv_max_stages() {
+    static const int v = [] {
+        const char *e = getenv("QL_GEMV_NST");
+        int n = e ? atoi(e) : kGemvStages;
+        return n < 2 ? 2 : (n > kGemvStages ? kGemvStages : n);
+    }();
+    return v;
+}
+
 // Plans and launches the streaming GEMV engine over M tokens (chunks of <= 4).
 int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
     int st;
@@ -261,7 +279,7 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
         GemvShape sh{};
         bool fits = false;
         for (; MT > 0 && !fits; MT -= fits ? 0 : 1)
-            for (int nst = kGemvStages; nst >= 2 && !fits; --nst) {
+            for (int nst = gemv_max_stages(); nst >= 2 && !fits; --nst) {
                 sh = gemv_shape(fmt, MT, NMAT, base.K, nst, tma);
                 fits = sh.smem_bytes <= 227 * 1024;
             }
@@ -269,6 +287,7 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
         GemvArgs a = base;
         a.M = MT;
         a.nst = sh.nst;
+        a.pre_x = gemv_pre_x();
         a.x = base.x + (size_t)done * base.x_stride;
         a.y = base.y + (size_t)done * base.y_stride;
         // Small reductions with at most one wave of row groups: one group per CTA
@@ -285,9 +304,8 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
 }
 
 // ---- tensor-core prefill GEMM ---------------------------------------------------
-// Grows the prefill scratch to hold `tokens` x `k` f16 activations, `tokens` row
-// scales and `part_floats` split-K partials.
-int ensure_prefill(Workspace *ws, size_t tokens, size_t k, size_t part_floats) {
+// Grows the prefill scratch to hold `tokens` x `k` f16 activations and `tokens` row scales.
+int ensure_prefill(Workspace *ws, size_t tokens, size_t k) {
     cudaError_t e;
     if (tokens * k > ws->xh_cap) {
         if (ws->xh) cudaFree(ws->xh);
@@ -303,14 +321,6 @@ int ensure_prefill(Workspace *ws, size_t tokens, size_t k, size_t part_floats) {
         if ((e = cudaMalloc(&ws->rinv, tokens * sizeof(float))) != cudaSuccess) return cuda_fail(e, "prefill scratch");
         ws->rinv_cap = tokens;
     }
-    if (part_floats > ws->gpart_cap) {
-        if (ws->gpart) cudaFree(ws->gpart);
-        ws->gpart = nullptr;
-        ws->gpart_cap = 0;
-        if ((e = cudaMalloc(&ws->gpart, part_floats * sizeof(float))) != cudaSuccess)
-            return cuda_fail(e, "prefill scratch");
-        ws->gpart_cap = part_floats;
-    }
     return QL_OK;
 }
 
@@ -322,39 +332,74 @@ int tc_min_tokens() {
     return v;
 }
 
-// Whether the tensor-core GEMM can run this shape (Q4_K, K % 256, TMA-compatible strides).
-bool tc_eligible(int t, size_t rb, int K) { return t == kQ4_K && K % 256 == 0 && rb % 16 == 0; }
+// One tensor-core GEMM launch pair: plain (1..3 stacked sources) or SwiGLU (gate, up).
+struct TcJob {
+    int epi = kGemmPlain;
+    int nsrc = 1;
+    const uint8_t *w[3] = {nullptr, nullptr, nullptr};
+    size_t rb[3] = {0, 0, 0};
+    int rows[3] = {0, 0, 0};
+    const float *x = nullptr;
+    int64_t xs = 0;
+    float *y = nullptr;
+    int64_t ys = 0;
+    int K = 0, M = 0;
+    const float *gamma = nullptr;
+    float eps = 0.f;
+    const float *bias = nullptr;
+    int accumulate = 0;
+};
 
-// Splits of K per output tile so that small grids still cover the SMs.
-int choose_ksplit(int64_t tiles, int nsb, int sms) {
-    if (tiles >= sms) return 1;
-    int ks = (int)(sms / tiles);
-    if (ks > nsb) ks = nsb;
-    if (ks > 32) ks = 32;
-    return ks < 1 ? 1 : ks;
+// Whether the tensor-core GEMM can run the job: Q4_K, K % 256, row strides that are
+// TMA-legal, and (stacked) sources that end on 256-row tile boundaries.
+bool tc_eligible(int t, const TcJob &j) {
+    if (t != kQ4_K || j.K % 256 != 0) return false;
+    for (int i = 0; i < j.nsrc; ++i) {
+        if (j.rb[i] % 16 != 0) return false;
+        if (j.epi == kGemmPlain && i < j.nsrc - 1 && j.rows[i] % kGemmBN != 0) return false;
+    }
+    return true;
 }
 
-int run_gemm_tc(const uint8_t *w, size_t rb, const float *x, int64_t xs, float *y, int64_t ys, int N, int K, int M,
-                const float *gamma, float eps, const float *bias, int accumulate, const char *what) {
+int run_gemm_tc(const TcJob &j, const char *what) {
     int st;
     Workspace *ws = workspace(&st);
     if (!ws) return st;
-    const int nsb = K / 256;
-    const int64_t mt = (M + kGemmBM - 1) / kGemmBM, nt = (N + kGemmBN - 1) / kGemmBN, tiles = mt * nt;
+    const bool swiglu = j.epi == kGemmSwiglu;
+    const int BNO = swiglu ? kGemmBN / 2 : kGemmBN;
+    int N = 0;
+    for (int i = 0; i < (swiglu ? 1 : j.nsrc); ++i) N += j.rows[i];
+    if (N == 0 || j.M == 0) return QL_OK;
+    const int nsb = j.K / 256;
+    const int64_t mt = (j.M + kGemmBM - 1) / kGemmBM, nt = (N + BNO - 1) / BNO, tiles = mt * nt;
     if (mt > 65535 || nt > 65535) return fail(QL_EINVAL, std::string(what) + ": shape too large for the tensor-core grid");
-    const int ks = choose_ksplit(tiles, nsb, ws->sms);
-    if (ks > 1 && tiles > (int64_t)(kMaxGroups - kGemmCounterBase))
-        return fail(QL_EINVAL, std::string(what) + ": too many tiles");
-    if ((st = ensure_prefill(ws, (size_t)M, (size_t)K, ks > 1 ? (size_t)tiles * ks * kGemmTileFloats : 0))) return st;
+    // K split over a cluster when the tiles alone would leave SMs idle
+    int ks = 1;
+    if (tiles < ws->sms) {
+        ks = (int)(ws->sms / tiles);
+        if (ks > kGemmMaxSplit) ks = kGemmMaxSplit;
+        if (ks > nsb) ks = nsb;
+        if (ks < 1) ks = 1;
+    }
+    if ((st = ensure_prefill(ws, (size_t)j.M, (size_t)j.K))) return st;
     auto enc = tensor_map_encoder();
     if (enc == nullptr) return fail(QL_ECUDA, std::string(what) + ": cuTensorMapEncodeTiled unavailable");
     GemmArgs a;
     memset(&a, 0, sizeof(a));
-    if (!q4k_tensor_map(&a.tm_w, w, nsb, (uint64_t)N, rb, 1, kGemmBN))
-        return fail(QL_ECUDA, std::string(what) + ": weight tensor map");
+    int end = 0;
+    for (int i = 0; i < 3; ++i) {
+        if (i < j.nsrc) {
+            if (!q4k_tensor_map(&a.tm_w[i], j.w[i], nsb, (uint64_t)j.rows[i], j.rb[i], 1, BNO))
+                return fail(QL_ECUDA, std::string(what) + ": weight tensor map");
+            end += j.rows[i];
+        } else {
+            a.tm_w[i] = a.tm_w[j.nsrc - 1];
+        }
+        a.src_end[i] = swiglu ? N : end;
+    }
     {
-        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-        const cuuint64_t strides[1] = {(cuuint64_t)K * sizeof(__half)};
+        const cuuint64_t dims[2] = {(cuuint64_t)j.K, (cuuint64_t)j.M};
+        const cuuint64_t strides[1] = {(cuuint64_t)j.K * sizeof(__half)};
         const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)kGemmBM};
         const cuuint32_t estr[2] = {1, 1};
         const CUresult r = enc(&a.tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws->xh, dims, strides, box, estr,
@@ -363,25 +408,44 @@ int run_gemm_tc(const uint8_t *w, size_t rb, const float *x, int64_t xs, float *
         if (r != CUDA_SUCCESS) return fail(QL_ECUDA, std::string(what) + ": activation tensor map");
     }
     a.rinv = ws->rinv;
-    a.bias = bias;
-    a.y = y;
-    a.accumulate = accumulate;
-    a.y_stride = ys;
-    a.M = M;
+    a.bias = swiglu ? nullptr : j.bias;
+    a.y = j.y;
+    a.y_stride = j.ys;
+    a.accumulate = swiglu ? 0 : j.accumulate;
+    a.vec = (reinterpret_cast<uintptr_t>(j.y) % 16 == 0) && (j.ys % 4 == 0) &&
+            (reinterpret_cast<uintptr_t>(a.bias) % 16 == 0);
+    a.M = j.M;
     a.N = N;
-    a.K = K;
+    a.K = j.K;
     a.nsb = nsb;
     a.ksplit = ks;
-    a.part = ws->gpart;
-    a.counters = ws->counters + kGemmCounterBase;
     a.err = ws->err;
-    cudaError_t e = gemm_xprep_launch(x, xs, gamma, eps, ws->xh, ws->rinv, M, K, g_stream);
+    cudaError_t e = gemm_xprep_launch(j.x, j.xs, j.gamma, j.eps, ws->xh, ws->rinv, j.M, j.K, g_stream);
     ++t_launches;
     if (e != cudaSuccess) return cuda_fail(e, what);
-    e = gemm_q4k_launch(a, g_stream);
+    e = gemm_q4k_launch(a, j.epi, g_stream);
     ++t_launches;
     if (e != cudaSuccess) return cuda_fail(e, what);
     return QL_OK;
+}
+
+TcJob plain_job(const uint8_t *w, size_t rb, const float *x, int64_t xs, float *y, int64_t ys, int N, int K, int M,
+                const float *gamma, float eps, const float *bias, int accumulate) {
+    TcJob j;
+    j.w[0] = w;
+    j.rb[0] = rb;
+    j.rows[0] = N;
+    j.x = x;
+    j.xs = xs;
+    j.y = y;
+    j.ys = ys;
+    j.K = K;
+    j.M = M;
+    j.gamma = gamma;
+    j.eps = eps;
+    j.bias = bias;
+    j.accumulate = accumulate;
+    return j;
 }
 
 GemvArgs blank() {
@@ -442,8 +506,10 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     if (st) return st;
     if (!x || !y) return fail(QL_EINVAL, "ql_quant_gemv: null x or y");
     if ((st = check_act(x, xs, gamma, "ql_quant_gemv"))) return st;
-    if (m >= tc_min_tokens() && tc_eligible(t, rb, in_dim))
-        return run_gemm_tc(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate, "ql_quant_gemv");
+    {
+        const TcJob j = plain_job(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate);
+        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_gemv");
+    }
     GemvArgs a = blank();
     a.w[0] = w;
     a.row_bytes[0] = rb;
@@ -470,13 +536,13 @@ int ql_quant_matmul_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, i
     if (st) return st;
     if (!x || !y) return fail(QL_EINVAL, "ql_quant_matmul_ex: null x or y");
     if ((st = check_act(x, xs, gamma, "ql_quant_matmul_ex"))) return st;
-    const bool tc = tc_eligible(t, rb, in_dim);
+    const TcJob j = plain_job(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate);
+    const bool tc = tc_eligible(t, j);
     if (path == QL_PATH_TENSOR && !tc)
         return fail(QL_EINVAL, "ql_quant_matmul_ex: the tensor-core path needs Q4_K, in_dim % 256 == 0 and "
                                "row_bytes % 16 == 0");
     if (path == QL_PATH_TENSOR || (path == QL_PATH_AUTO && tc && m >= tc_min_tokens()))
-        return run_gemm_tc(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate,
-                           "ql_quant_matmul_ex");
+        return run_gemm_tc(j, "ql_quant_matmul_ex");
     GemvArgs a = blank();
     a.w[0] = w;
     a.row_bytes[0] = rb;
@@ -497,8 +563,7 @@ int ql_reserve_prefill(int max_tokens, int max_in_dim) {
     int st;
     Workspace *ws = workspace(&st);
     if (!ws) return st;
-    // split-K partials exist only for grids of fewer tiles than SMs: at most 2 * sms tile-splits
-    return ensure_prefill(ws, (size_t)max_tokens, (size_t)max_in_dim, (size_t)2 * ws->sms * kGemmTileFloats);
+    return ensure_prefill(ws, (size_t)max_tokens, (size_t)max_in_dim);
 }
 
 int ql_quant_gemv_stacked_ex(int32_t t, int nsrc, const uint8_t *const *w, const size_t *rb, const int *rows,
@@ -529,6 +594,16 @@ int ql_quant_gemv_stacked_ex(int32_t t, int nsrc, const uint8_t *const *w, const
     if (!x || !y) return fail(QL_EINVAL, "ql_quant_gemv_stacked_ex: null x or y");
     int st = check_act(x, xs, gamma, "ql_quant_gemv_stacked_ex");
     if (st) return st;
+    if (m >= tc_min_tokens()) {
+        TcJob j = plain_job(w[0], rb[0], x, xs, y, ys, rows[0], in_dim, m, gamma, eps, bias, 0);
+        j.nsrc = nsrc;
+        for (int i = 1; i < nsrc; ++i) {
+            j.w[i] = w[i];
+            j.rb[i] = rb[i];
+            j.rows[i] = rows[i];
+        }
+        if (tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_gemv_stacked_ex");
+    }
     a.rows = total;
     a.K = in_dim;
     a.x = x;
@@ -566,6 +641,15 @@ int ql_quant_swiglu_ex(int32_t t, const uint8_t *g, const uint8_t *u, size_t grb
     if ((st = check_weight(t, u, urb, 0, in_dim, "ql_quant_swiglu(up)"))) return st;
     if (!x || !act) return fail(QL_EINVAL, "ql_quant_swiglu: null x or act");
     if ((st = check_act(x, xs, gamma, "ql_quant_swiglu"))) return st;
+    if (m >= tc_min_tokens()) {
+        TcJob j = plain_job(g, grb, x, xs, act, as, ffn_dim, in_dim, m, gamma, eps, nullptr, 0);
+        j.epi = kGemmSwiglu;
+        j.nsrc = 2;
+        j.w[1] = u;
+        j.rb[1] = urb;
+        j.rows[1] = ffn_dim;
+        if (tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_swiglu");
+    }
     GemvArgs a = blank();
     a.w[0] = g;
     a.w[1] = u;

@@ -140,45 +140,47 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const float *__restrict
     }
 }
 
-// Epilogue store of 32 consecutive outputs of one row: y = acc * scale (+ bias) (+ y).
-__device__ __forceinline__ void store_row32(float *yp, const float *bias, const uint32_t (&v)[32], float scale,
-                                            int nv, int accumulate) {
-    if (nv >= 32 && (reinterpret_cast<uintptr_t>(yp) & 15) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-            float4 o = make_float4(__uint_as_float(v[i]) * scale, __uint_as_float(v[i + 1]) * scale,
-                                   __uint_as_float(v[i + 2]) * scale, __uint_as_float(v[i + 3]) * scale);
-            if (bias) {
-                const float4 b = *reinterpret_cast<const float4 *>(bias + i);
-                o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
-            }
-            if (accumulate) {
-                const float4 p = *reinterpret_cast<const float4 *>(yp + i);
-                o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
-            }
-            *reinterpret_cast<float4 *>(yp + i) = o;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (i < nv) {
-                float o = __uint_as_float(v[i]) * scale;
-                if (bias) o += bias[i];
-                if (accumulate) o += yp[i];
-                yp[i] = o;
-            }
-    }
+// Distributed shared memory: this CTA's shared address `addr` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
 }
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
+    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
 // ---------------------------------------------------------------------------
-// The GEMM.
+// The GEMM.  EPI = kGemmPlain: 256 output columns per tile from one of up to
+// three stacked sources.  EPI = kGemmSwiglu: 128 output columns per tile, the
+// accumulator's columns 0-127 from the gate rows and 128-255 from the up rows.
 // ---------------------------------------------------------------------------
+template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_constant__ GemmArgs a) {
+    constexpr int BNO = EPI == kGemmSwiglu ? kGemmBN / 2 : kGemmBN;  // output columns per tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = sA + kGemmNA * kGemmABytes;
     uint8_t *sR = sB + kGemmNB * kGemmBBytes;
+    uint8_t *sRed = smem;  // epilogue fp32 tile [128][kGemmRedPitch], over the (then idle) rings
     uint64_t *bars = reinterpret_cast<uint64_t *>(sR + kGemmNR * kGemmRBytes);
     uint64_t *a_full = bars, *a_empty = a_full + kGemmNA;
     uint64_t *b_full = a_empty + kGemmNA, *b_empty = b_full + kGemmNB;
@@ -186,13 +188,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
     uint64_t *acc_full = r_empty + kGemmNR;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    int *last_flag = const_cast<int *>(abort_flag) + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
+    const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * BNO;
     const int s0 = (int)((int64_t)blockIdx.z * a.nsb / a.ksplit);
     const int s1 = (int)((int64_t)(blockIdx.z + 1) * a.nsb / a.ksplit);
     const int nsbl = s1 - s0, nch = 4 * nsbl;
+    const int rows_valid = a.M - m0 < kGemmBM ? a.M - m0 : kGemmBM;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kGemmNA; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
@@ -213,6 +215,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
+            // weight source of this tile (plain: stacked sources end on 256-row boundaries)
+            int src = 0, row0 = n0;
+            if (EPI == kGemmPlain) {
+                while (src < 2 && n0 >= a.src_end[src]) ++src;
+                row0 = n0 - (src > 0 ? a.src_end[src - 1] : 0);
+            }
             int issued_r = 0, issued_a = 0;
             for (int sl = 0; sl < nsbl && !*abort_flag; ++sl) {
                 const int rs = sl % kGemmNR;
@@ -221,7 +229,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                     break;
                 }
                 mbar_arrive_expect_tx(&r_full[rs], kGemmRBytes);
-                tma_load_3d(sR + rs * kGemmRBytes, &a.tm_w, 0, s0 + sl, n0, &r_full[rs]);
+                if (EPI == kGemmSwiglu) {
+                    tma_load_3d(sR + rs * kGemmRBytes, &a.tm_w[0], 0, s0 + sl, n0, &r_full[rs]);
+                    tma_load_3d(sR + rs * kGemmRBytes + BNO * 144, &a.tm_w[1], 0, s0 + sl, n0, &r_full[rs]);
+                } else {
+                    tma_load_3d(sR + rs * kGemmRBytes, &a.tm_w[src], 0, s0 + sl, row0, &r_full[rs]);
+                }
                 issued_r = sl + 1;
                 for (int p = 0; p < 4; ++p) {
                     const int c = 4 * sl + p, as = c % kGemmNA;
@@ -260,13 +273,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                 mma_commit(&b_empty[bs]);
             }
             mma_commit(acc_full);
-            // All MMAs complete before the CTA may free TMEM.
+            // All MMAs complete before the CTA may reuse the rings or free TMEM.
             mbar_wait(acc_full, 0u, a.err, kErrWaitFull);
         }
         __syncwarp();
     } else {
-        // ----------------------- dequantizers, then epilogue -----------------------
-        const int r = threadIdx.x - 64;  // weight row of the tile
+        // ------------------ dequantizers, then the TMEM -> smem drain ------------------
+        const int r = threadIdx.x - 64;  // row of the 256-row weight tile
         for (int sl = 0; sl < nsbl; ++sl) {
             const int rs = sl % kGemmNR;
             // every wait's outcome is made warp-uniform: the warp-synchronous code below needs all lanes
@@ -327,71 +340,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
             if (!ok) break;
         }
 
-        // -------------------------------- epilogue --------------------------------
-        // warp-uniform: tcgen05.ld is a warp-collective instruction
+        // Drain TMEM into the shared fp32 tile (row = accumulator lane).  The MMA
+        // thread's completed acc_full also means every ring slot is idle.
         const bool ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait(acc_full, 0u, a.err, kErrWaitFull));
         tc_fence_after();
         const int q = warp & 3, hcol = (warp - 2) >> 2;  // TMEM lane quadrant, column half
-        const int row = 32 * q + lane, gm = m0 + row;
-        const float rs_m = (ok && gm < a.M) ? a.rinv[gm] : 0.f;
-        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-        float *tp = a.part + ((size_t)tile * a.ksplit + blockIdx.z) * kGemmTileFloats + (size_t)row * kGemmBN;
+        const int row = 32 * q + lane;
+        if (ok) {
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-            if (!ok) break;
-            uint32_t v[32];
-            const int col = hcol * 128 + cc * 32;
-            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col, v);
-            if (a.ksplit == 1) {
-                if (gm < a.M) {
-                    float *yp = a.y + (size_t)gm * a.y_stride + n0 + col;
-                    const int nv = a.N - (n0 + col);
-                    store_row32(yp, a.bias ? a.bias + n0 + col : nullptr, v, rs_m, nv, a.accumulate);
+            for (int cc = 0; cc < 4; ++cc) {
+                uint32_t v[32];
+                const int col = hcol * 128 + cc * 32;
+                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col, v);
+                if (row < rows_valid) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(sRed + (size_t)row * kGemmRedPitch + col * 4);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dst[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    __stcg(reinterpret_cast<float4 *>(tp + col + i),
-                           make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
-                                       __uint_as_float(v[i + 3])));
-            }
-        }
-        if (a.ksplit > 1) {
-            // The last of the tile's K-split CTAs sums the partial tiles in split order.
-            // Every dequantizer thread takes both barriers, whatever its `ok`.
-            __threadfence();
-            named_bar_sync(1, 256);
-            if (threadIdx.x == 64) {
-                int last = 0;
-                if (ok) last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.ksplit - 1);
-                *last_flag = last;
-            }
-            named_bar_sync(1, 256);
-            if (ok && *last_flag) {
-                __threadfence();
-                const float *base = a.part + (size_t)tile * a.ksplit * kGemmTileFloats + (size_t)row * kGemmBN;
-                for (int cc = 0; cc < 4; ++cc) {
-                    const int col = hcol * 128 + cc * 32;
-                    float acc[32];
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-                    for (int z = 0; z < a.ksplit; ++z) {
-                        const float4 *pz = reinterpret_cast<const float4 *>(base + (size_t)z * kGemmTileFloats + col);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float4 t = __ldcg(pz + i);
-                            acc[4 * i] += t.x; acc[4 * i + 1] += t.y; acc[4 * i + 2] += t.z; acc[4 * i + 3] += t.w;
-                        }
-                    }
-                    if (gm < a.M) {
-                        uint32_t v[32];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[i]);
-                        store_row32(a.y + (size_t)gm * a.y_stride + n0 + col, a.bias ? a.bias + n0 + col : nullptr, v,
-                                    rs_m, a.N - (n0 + col), a.accumulate);
-                    }
-                }
-                if (threadIdx.x == 64) a.counters[tile] = 0u;
             }
         }
     }
@@ -402,6 +367,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
         tc_fence_after();
         tmem_dealloc(tmem, kGemmBN);
     }
+
+    // ---- epilogue: sum the cluster's partial tiles (fixed order), scale, store ----
+    const int ks = a.ksplit;
+    if (ks > 1) cluster_sync_all();
+    const int z = ks > 1 ? (int)cluster_rank() : 0;
+    const int r_lo = z * rows_valid / ks, r_hi = (z + 1) * rows_valid / ks;
+    constexpr int C4 = BNO / 4;  // float4 items per output row
+    const uint32_t red_base = smem_u32(sRed);
+    const bool good = !*abort_flag;
+    for (int it = threadIdx.x; good && it < (r_hi - r_lo) * C4; it += kGemmThreads) {
+        const int rr = r_lo + it / C4, c4 = it % C4;
+        const uint32_t off = red_base + (uint32_t)(rr * kGemmRedPitch + c4 * 16);
+        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+        for (int i = 0; i < ks; ++i) {  // cluster CTA order: a fixed summation order
+            const uint32_t pa = ks > 1 ? mapa_shared(off, (uint32_t)i) : off;
+            acc0 = f4_add(acc0, ld_cluster_v4(pa));
+            if (EPI == kGemmSwiglu) acc1 = f4_add(acc1, ld_cluster_v4(pa + BNO * 4));
+        }
+        const int gm = m0 + rr, gn = n0 + 4 * c4;
+        const float sc = a.rinv[gm];
+        float o[4] = {acc0.x * sc, acc0.y * sc, acc0.z * sc, acc0.w * sc};
+        if (EPI == kGemmSwiglu) {
+            const float u[4] = {acc1.x * sc, acc1.y * sc, acc1.z * sc, acc1.w * sc};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] = silu_mul(o[e], u[e]);
+        }
+        float *yp = a.y + (size_t)gm * a.y_stride + gn;
+        if (a.vec && gn + 4 <= a.N) {
+            float4 v4 = make_float4(o[0], o[1], o[2], o[3]);
+            if (EPI == kGemmPlain && a.bias) v4 = f4_add(v4, *reinterpret_cast<const float4 *>(a.bias + gn));
+            if (EPI == kGemmPlain && a.accumulate) v4 = f4_add(v4, *reinterpret_cast<const float4 *>(yp));
+            *reinterpret_cast<float4 *>(yp) = v4;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (gn + e < a.N) {
+                    float v = o[e];
+                    if (EPI == kGemmPlain && a.bias) v += a.bias[gn + e];
+                    if (EPI == kGemmPlain && a.accumulate) v += yp[e];
+                    yp[e] = v;
+                }
+        }
+    }
+    if (ks > 1) cluster_sync_all();  // peers may still be reading this CTA's tile
 }
 
 }  // namespace
@@ -420,24 +429,41 @@ cudaError_t gemm_xprep_launch(const float *x, int64_t x_stride, const float *gam
     return cudaLaunchKernelEx(&cfg, gemm_xprep_kernel, x, x_stride, gamma, eps, xh, rinv, K);
 }
 
-cudaError_t gemm_q4k_launch(const GemmArgs &a, cudaStream_t s) {
+template <int EPI>
+cudaError_t gemm_launch_t(const GemmArgs &a, cudaStream_t s) {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemm_q4k_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
+    constexpr int BNO = EPI == kGemmSwiglu ? kGemmBN / 2 : kGemmBN;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((a.M + kGemmBM - 1) / kGemmBM, (a.N + kGemmBN - 1) / kGemmBN, a.ksplit);
+    cfg.gridDim = dim3((a.M + kGemmBM - 1) / kGemmBM, (a.N + BNO - 1) / BNO, a.ksplit);
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = kGemmSmem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (gemv_pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (a.ksplit > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = (unsigned)a.ksplit;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = gemv_pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemm_q4k_kernel, a);
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, gemm_q4k_kernel<EPI>, a);
+}
+
+cudaError_t gemm_q4k_launch(const GemmArgs &a, int epi, cudaStream_t s) {
+    return epi == kGemmSwiglu ? gemm_launch_t<kGemmSwiglu>(a, s) : gemm_launch_t<kGemmPlain>(a, s);
 }
 
 }  // namespace ql

@@ -12,8 +12,10 @@
 //     permutation inside every 8-element group (the order in which the
 //     dequantizer below emits nibbles: positions 0..7 hold elements
 //     0,2,1,3,4,6,5,7).  1/s_m is kept per row.
-//  2. qgemm: one CTA per 128 x 256 output tile (and K split when the grid
-//     would underfill the GPU).  Warp roles, 320 threads:
+//  2. qgemm: one CTA per 128 x 256 accumulator tile; when the grid would
+//     underfill the GPU, the K range is split over a thread-block cluster of up
+//     to 8 CTAs whose partial tiles are summed through distributed shared memory
+//     in a fixed order (deterministic).  Warp roles, 320 threads:
 //       warp 0   -- one thread issues TMA: raw Q4_K super-blocks {144 B, 1, 256 rows}
 //                   and 128 x 64 f16 activation tiles (128-byte swizzle);
 //       warp 1   -- allocates 256 TMEM columns; one thread issues
@@ -47,26 +49,34 @@ constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;  // 32 KB
 constexpr int kGemmRBytes = kGemmBN * 144;          // 36 KB
 constexpr int kGemmSmem = kGemmNA * kGemmABytes + kGemmNB * kGemmBBytes + kGemmNR * kGemmRBytes + 256 + 1024;
 constexpr int kGemmTileFloats = kGemmBM * kGemmBN;
+constexpr int kGemmRedPitch = kGemmBN * 4 + 16;  // bytes per row of the epilogue's fp32 tile in shared memory
+constexpr int kGemmMaxSplit = 8;
+
+// Epilogues: plain (scale, optional bias, optional accumulate) over 256-column
+// tiles of one or several stacked weight sources, or SwiGLU over 128-column
+// tiles of a gate/up pair (the MMA's 256 columns are 128 gate + 128 up rows).
+enum GemmEpi : int { kGemmPlain = 1, kGemmSwiglu = 2 };
 
 struct GemmArgs {
-    CUtensorMap tm_x;     // f16 [M][K] activations (permuted), box {64, 128}, 128-byte swizzle
-    CUtensorMap tm_w;     // Q4_K viewed as uint8 {144, K/256, N}, box {144, 1, 256}
-    const float *rinv;    // [M] 1/s_m (times the row's RMSNorm factor when one is fused)
-    const float *bias;    // [N] or null
-    float *y;             // [M][y_stride]
-    int accumulate;       // y += result instead of y = result
+    CUtensorMap tm_x;      // f16 [M][K] activations (permuted), box {64, 128}, 128-byte swizzle
+    CUtensorMap tm_w[3];   // Q4_K sources viewed as uint8 {144, K/256, rows}; box {144, 1, 256} (plain)
+                           // or {144, 1, 128} (SwiGLU: tm_w[0] gate, tm_w[1] up)
+    int src_end[3];        // plain: cumulative row ends of the stacked sources (multiples of 256 but the last)
+    const float *rinv;     // [M] 1/s_m (times the row's RMSNorm factor when one is fused)
+    const float *bias;     // [N] or null (plain)
+    float *y;              // [M][y_stride]
     int64_t y_stride;
-    int M, N, K;
-    int nsb;              // K / 256
-    int ksplit;           // K ranges per output tile
-    float *part;          // [tiles][ksplit][128][256] partial tiles (ksplit > 1)
-    unsigned *counters;   // [tiles] arrival counters (ksplit > 1), left at zero
+    int accumulate;        // plain: y += result
+    int vec;               // y, y_stride and bias allow 16-byte stores
+    int M, N, K;           // N = output columns (plain: all sources' rows; SwiGLU: FFN rows)
+    int nsb;               // K / 256
+    int ksplit;            // K ranges per output tile = cluster size along z (<= 8)
     int *err;
 };
 
 bool gemv_pdl_enabled();  // QL_PDL=0 turns programmatic dependent launch off
 cudaError_t gemm_xprep_launch(const float *x, int64_t x_stride, const float *gamma, float eps, __half *xh,
                               float *rinv, int M, int K, cudaStream_t s);
-cudaError_t gemm_q4k_launch(const GemmArgs &a, cudaStream_t s);
+cudaError_t gemm_q4k_launch(const GemmArgs &a, int epi, cudaStream_t s);
 
 }  // namespace ql

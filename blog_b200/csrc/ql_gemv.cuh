@@ -71,6 +71,10 @@ constexpr int kTmaSeg = 7;
 __host__ __device__ constexpr int stage_seg(int t, bool tma) { return tma ? kTmaSeg : gemv_seg(t); }
 __host__ __device__ constexpr int stage_pitch(int t, bool tma) { return tma ? kTmaSeg * 144 : gemv_pitch(t); }
 
+// Shared-memory header of the GEMV kernel: mbarriers, abort flag, RMSNorm
+// factors [4] and per-warp partial sums of squares [14][4].
+constexpr int kGemvHeaderBytes = 512;
+
 struct GemvArgs {
     const uint8_t *w[kMaxStacked];   // weight buffers (raw GGUF blocks): SwiGLU gate/up, or stacked sources
     size_t row_bytes[kMaxStacked];   // bytes per output row
@@ -92,6 +96,7 @@ struct GemvArgs {
     float *y;                 // output [M][y_stride]
     int64_t y_stride;
     int nst;                  // stages in the shared-memory ring (2..kGemvStages)
+    int pre_x;                // stages the producer may issue before the activations are staged
     CUtensorMap tmap[kMaxStacked];   // Q4_K tensor maps {144 B, blocks, rows} (TMA kernels only)
     Plan plan;
     float *part;              // stream-K partial slots [C][2][MT][NMAT][32]
@@ -171,7 +176,7 @@ __host__ inline GemvShape gemv_shape(int fmt, int MT, int NMAT, int K, int nst, 
     s.xsum_floats = MT * (K / 32);
     s.red_floats = 2 * gemv_consumer_warps(tma) * MT * NMAT * kRowGroup;
     s.nst = nst;
-    int off = 128;  // mbarriers, inv-rms slots, abort flag
+    int off = kGemvHeaderBytes;  // mbarriers, abort flag, RMSNorm factors and partial sums
     off += ((s.xs_floats * 4 + 127) / 128) * 128;
     off += ((s.xsum_floats * 4 + 127) / 128) * 128;
     off += ((s.red_floats * 4 + 127) / 128) * 128;

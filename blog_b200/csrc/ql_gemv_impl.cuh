@@ -333,10 +333,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
     uint64_t *empty = full + kGemvStages;                        // [kGemvStages]
     uint64_t *red_full = empty + kGemvStages;                    // [2]
     uint64_t *red_empty = red_full + 2;                          // [2]
-    float *inv_rms = reinterpret_cast<float *>(red_empty + 2);   // [kGemvMaxTokens]
-    int *abort_flag = reinterpret_cast<int *>(inv_rms + kGemvMaxTokens);
+    uint64_t *x_ready = red_empty + 2;                           // [1] activations staged
+    int *abort_flag = reinterpret_cast<int *>(x_ready + 1);
+    float *inv_rms = reinterpret_cast<float *>(smem + 112);      // [kGemvMaxTokens]
+    float *ss_part = reinterpret_cast<float *>(smem + 128);      // [W][kGemvMaxTokens] sums of squares
     const int K = a.K, nblk = K / 32;
-    size_t off = 128;
+    size_t off = kGemvHeaderBytes;
     float *xs = reinterpret_cast<float *>(smem + off);
     off += ((size_t)MT * K * 4 + 127) / 128 * 128;
     float *xsum = reinterpret_cast<float *>(smem + off);
@@ -360,6 +362,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
             mbar_init(&red_full[b], W);
             mbar_init(&red_empty[b], 1);
         }
+        mbar_init(x_ready, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -381,6 +384,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
         while (next_stage(t, t1, U, SEG, upr, st)) {
             const int slot = it % NST;
             const uint32_t ph = (uint32_t)(it / NST) & 1u;
+            // After the first pre_x stages, let the activation loads go first.
+            if (it == a.pre_x && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                if (!mbar_wait(x_ready, 0u, a.err, kErrWaitFull)) *abort_flag = 1;
+            }
             if (it >= NST && !*reinterpret_cast<volatile int *>(abort_flag)) {
                 if (!mbar_wait(&empty[slot], ph ^ 1u, a.err, kErrWaitEmpty)) *abort_flag = 1;
             }
@@ -429,6 +436,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
         while (next_stage(t, t1, U, SEG, upr, st)) {
             const int slot = it % NST;
             const uint32_t ph = (uint32_t)(it / NST) & 1u;
+            // After the first pre_x stages, let the activation loads go first.
+            if (it == a.pre_x && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                if (!mbar_wait(x_ready, 0u, a.err, kErrWaitFull)) *abort_flag = 1;
+            }
             if (it >= NST && !*reinterpret_cast<volatile int *>(abort_flag)) {
                 if (!mbar_wait(&empty[slot], ph ^ 1u, a.err, kErrWaitEmpty)) *abort_flag = 1;
             }
@@ -550,13 +561,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
 #pragma unroll
                 for (int m = 0; m < MT; ++m) {
                     float *yp = a.y + (size_t)m * a.y_stride + v;
+                    const float nrm = a.gamma != nullptr ? inv_rms[m] : 1.0f;  // fused RMSNorm factor
                     if (EPI == kEpiSwiglu) {
-                        const float gv = val[0][m], uv = val[NMAT - 1][m];
+                        const float gv = val[0][m] * nrm, uv = val[NMAT - 1][m] * nrm;
                         float o = gv / (1.0f + expf(-gv)) * uv;
                         if (SRC == kSrcIndexedRows && a.ids[v / a.rows_per_route] < 0) o = 0.f;
                         *yp = o;
                     } else {
-                        float o = val[0][m];
+                        float o = val[0][m] * nrm;
                         if (a.bias != nullptr) o += a.bias[v];
                         if (EPI == kEpiAdd) *yp += o;
                         else *yp = o;
@@ -573,36 +585,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
     const int ctid = tid - 32 * CW0;
     asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
 
-    // Prologue: optional RMSNorm, then stage x * 2^(96-p) (float4 per thread,
-    // loads issued in batches) and the 32-element block sums (8-lane reduce).
-    constexpr int B = 8;
-    if (a.gamma != nullptr) {
-        for (int m = 0; m < MT; ++m) {
-            const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.x_stride);
-            float ss = 0.f;
-            for (int j0 = ctid; j0 < K / 4; j0 += B * nthr) {
-                float4 v[B];
+    // Prologue, one pass over x: stage x * g * 2^(96-p) (float4 per thread, loads
+    // issued in batches) and the 32-element block sums of x * g (8-lane reduce).
+    // With a fused RMSNorm the pass also sums x^2; the norm factor
+    // 1/sqrt(mean(x^2) + eps) is one scalar per token, so the finisher applies it
+    // to the finished dot products and nothing here waits for it.
+    constexpr int B = 12;  // float4 loads in flight per thread: K <= 21504 stages in one round trip
+    float ss[MT];
 #pragma unroll
-                for (int u = 0; u < B; ++u) {
-                    const int j = j0 + u * nthr;
-                    v[u] = j < K / 4 ? x4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int u = 0; u < B; ++u)
-                    ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) red[cw] = ss;
-            named_bar_sync(1, nthr);
-            if (cw == 0) {
-                float tsum = 0.f;
-                for (int w = lane; w < W; w += 32) tsum += red[w];
-                tsum = warp_sum(tsum);
-                if (lane == 0) inv_rms[m] = rsqrtf(tsum / (float)K + a.eps);
-            }
-            named_bar_sync(1, nthr);
-        }
-    }
+    for (int m = 0; m < MT; ++m) ss[m] = 0.f;
     {
         const int nch = MT * (K / 4);
         // The loop bound is warp-uniform (the shuffles below need every lane);
@@ -635,9 +626,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
                 const int m = ok ? j / (K / 4) : 0, k = ok ? 4 * (j - m * (K / 4)) : 0;
                 float4 xv = v[u];
                 if (ok && a.gamma != nullptr) {
+                    const float q = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, xv.w * xv.w)));
+#pragma unroll
+                    for (int mm = 0; mm < MT; ++mm)
+                        if (mm == m) ss[mm] += q;
                     const float4 g = *reinterpret_cast<const float4 *>(a.gamma + k);
-                    const float sc = inv_rms[m];
-                    xv.x = xv.x * sc * g.x; xv.y = xv.y * sc * g.y; xv.z = xv.z * sc * g.z; xv.w = xv.w * sc * g.w;
+                    xv.x *= g.x; xv.y *= g.y; xv.z *= g.z; xv.w *= g.w;
                 }
                 float bs = (xv.x + xv.y) + (xv.z + xv.w);
                 bs += __shfl_xor_sync(0xffffffffu, bs, 1);
@@ -655,7 +649,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
             }
         }
     }
+    if (a.gamma != nullptr) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float w = warp_sum(ss[m]);
+            if (lane == 0) ss_part[cw * kGemvMaxTokens + m] = w;
+        }
+    }
     named_bar_sync(1, nthr);
+    if (ctid == 0) mbar_arrive(x_ready);  // the producer may issue the rest of its stages
+    if (a.gamma != nullptr && cw == 0) {
+        for (int m = 0; m < MT; ++m) {
+            const float tsum = warp_sum(lane < W ? ss_part[lane * kGemvMaxTokens + m] : 0.f);
+            if (lane == 0) inv_rms[m] = rsqrtf(tsum / (float)K + a.eps);
+        }
+    }
 
     float acc[NMAT][MT];
 #pragma unroll

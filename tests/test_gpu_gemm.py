@@ -195,3 +195,48 @@ def test_tc_gemm_prefill_shape_against_torch():
         torch.backends.cuda.matmul.allow_tf32 = prev
     err = float(torch.linalg.norm((y - ref).double()) / torch.linalg.norm(ref.double()))
     assert err < EXACT_F16_OPERANDS, err
+
+
+def test_tc_swiglu_matches_oracle():
+    """Gate/up pair in one tensor-core launch (128 gate + 128 up rows per tile), fused RMSNorm."""
+    import torch
+    f, k, m, eps = 640, 1024, 40, 1e-6
+    g = make_weights(O.Q4_K, f, k, seed=101)
+    u = make_weights(O.Q4_K, f, k, seed=102)
+    x = _x(103, m, k)
+    gamma = (1.0 + 0.1 * _x(104, 1, k)[0]).astype(np.float32)
+    rb = O.row_bytes(O.Q4_K, k)
+    act = torch.full((m, f), float("nan"), device="cuda:0")
+    Q.quant_swiglu_ex(O.Q4_K, dev(g).data_ptr(), dev(u).data_ptr(), rb, rb, dev(x).data_ptr(), k, act.data_ptr(), f,
+                      f, k, m, dev(gamma).data_ptr(), eps)
+    got = host(act)
+    xn = O.rmsnorm(x, gamma, eps)
+    gv = O.gemv(O.Q4_K, g, rb, xn, f, k, m, order=1).astype(np.float64)
+    uv = O.gemv(O.Q4_K, u, rb, xn, f, k, m, order=1).astype(np.float64)
+    assert rel_l2(got, gv / (1.0 + np.exp(-gv)) * uv) < NORTH_STAR
+    x16 = act_f16_operand(x, gamma, eps)
+    g16 = x16 @ q4k_f16_operand(g, f, k).T
+    u16 = x16 @ q4k_f16_operand(u, f, k).T
+    assert rel_l2(got, g16 / (1.0 + np.exp(-g16)) * u16) < EXACT_F16_OPERANDS
+
+
+@pytest.mark.parametrize("rows,m", [((512, 256, 100), 24), ((3584, 512, 512), 64)])
+def test_tc_stacked_sources_match_concatenated(rows, m):
+    """Stacked q/k/v sources (each but the last a multiple of 256 rows) with bias and fused norm."""
+    import torch
+    k, eps = 1024, 1e-6
+    ws = [make_weights(O.Q4_K, r, k, seed=110 + i) for i, r in enumerate(rows)]
+    x = _x(115, m, k)
+    gamma = (1.0 + 0.1 * _x(116, 1, k)[0]).astype(np.float32)
+    n = sum(rows)
+    bias = _x(117, 1, n)[0]
+    rb = O.row_bytes(O.Q4_K, k)
+    y = torch.full((m, n), float("nan"), device="cuda:0")
+    Q.quant_gemv_stacked_ex(O.Q4_K, [dev(w).data_ptr() for w in ws], [rb] * 3, list(rows), dev(x).data_ptr(), k,
+                            y.data_ptr(), n, k, m, dev(gamma).data_ptr(), eps, dev(bias).data_ptr())
+    got = host(y)
+    wcat = np.concatenate(ws, axis=0)
+    ref = O.gemv(O.Q4_K, wcat, rb, O.rmsnorm(x, gamma, eps), n, k, m, order=1) + bias[None, :]
+    assert rel_l2(got, ref) < NORTH_STAR
+    ref16 = act_f16_operand(x, gamma, eps) @ q4k_f16_operand(wcat, n, k).T + bias[None, :]
+    assert rel_l2(got, ref16) < EXACT_F16_OPERANDS
