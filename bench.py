@@ -169,6 +169,15 @@ class DecodeStack:
         self.gathered = torch.zeros((world, M, 2), device=dev)
         self.token_ids = torch.zeros((M,), dtype=torch.int32, device=dev)
         self.timed_events = []  # (start, end) pairs around the dominant kernel
+        # Row-parallel partial sums: the library's one-shot peer-memory all-reduce
+        # for decode-sized vectors, NCCL for larger ones (QL_TP_NCCL=1 forces NCCL).
+        self.comm = None
+        if world > 1 and M * HIDDEN <= 4096 and os.environ.get("QL_TP_NCCL", "0") != "1":
+            def exchange(h):
+                out = [None] * world
+                torch.distributed.all_gather_object(out, h)
+                return out
+            self.comm = Q.Comm(rank, world, 4096, 2 * LAYERS, exchange)
         torch.cuda.synchronize()
 
     def weight_bytes(self):
@@ -182,6 +191,15 @@ class DecodeStack:
         rbh = Q.row_bytes(QK, HIDDEN)
         self.h.copy_(self.h_in)
         h = self.h.data_ptr()
+        slot = 0
+
+        def reduce_h():
+            nonlocal slot
+            if self.comm is not None:
+                self.comm.allreduce(h, M * HIDDEN, slot)
+                slot += 1
+            else:
+                torch.distributed.all_reduce(self.h)
         for li, L in enumerate(self.layers):
             # q, k, v in one launch (stacked sources), RMSNorm and bias fused
             Q.quant_gemv_stacked_ex(QK, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
@@ -192,7 +210,7 @@ class DecodeStack:
             Q.quant_gemv_ex(QK, L["wo"].data_ptr(), Q.row_bytes(QK, self.qo_len), self.qkv.data_ptr(),
                             self.qkv_w, h, HIDDEN, HIDDEN, self.qo_len, M, accumulate=(self.rank == 0))
             if self.world > 1:
-                torch.distributed.all_reduce(self.h)
+                reduce_h()
             sel = events is not None and li in events["layers"]
             if sel:
                 events["pairs"][li][0].record()
@@ -203,7 +221,7 @@ class DecodeStack:
             Q.quant_gemv_ex(QK, L["wd"].data_ptr(), Q.row_bytes(QK, self.f_len), self.act.data_ptr(),
                             self.act.shape[1], h, HIDDEN, HIDDEN, self.f_len, M, accumulate=(self.rank == 0))
             if self.world > 1:
-                torch.distributed.all_reduce(self.h)
+                reduce_h()
         Q.quant_gemv_ex(QK, self.wlm.data_ptr(), rbh, h, HIDDEN, self.logits.data_ptr(), self.v_len, self.v_len,
                         HIDDEN, M, self.lnf.data_ptr(), EPS)
         for m in range(M):
@@ -213,6 +231,8 @@ class DecodeStack:
             self.best[:, 0] = self.logits.gather(1, idx[:, None])[:, 0]
             self.best[:, 1] = (idx + self.v_off).float()
             torch.distributed.all_gather_into_tensor(self.gathered, self.best)
+            if self.comm is not None:
+                self.comm.step()
             win = self.gathered[:, :, 0].argmax(0)  # first rank holding the max = lowest vocab index
             self.token_ids.copy_(self.gathered[win, torch.arange(M, device=self.h.device), 1].int())
         else:
@@ -484,6 +504,11 @@ def main():
                "launches": stack.launches_per_step(), "wbytes": stack.weight_bytes(),
                "h2d": host_in.numel() * 4, "d2h": host_out.numel() * 4, "f_len": stack.f_len}
         del graph
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()  # no peer still reads this rank's exchange buffer
+        if stack.comm is not None:
+            stack.comm.close()
         del stack
         torch.cuda.empty_cache()
         return res

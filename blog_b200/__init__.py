@@ -67,6 +67,16 @@ SIGNATURES = {
     "ql_quant_gemv_stacked_ex": (I, [I32, I, P, P, P, P, I64, P, I64, I, I, P, F, P]),
     "ql_quant_matmul_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, P, I, I]),
     "ql_reserve_prefill": (I, [I, I]),
+    "ql_quant_gemv_argmax_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, I, P, P]),
+    "ql_gemv_chain_create": (I, [P, I, C.POINTER(C.c_void_p)]),
+    "ql_gemv_chain_run": (I, [P]),
+    "ql_gemv_chain_destroy": (I, [P]),
+    "ql_comm_bytes": (SZ, [I, I, I]),
+    "ql_comm_alloc": (I, [I, I, I, C.POINTER(C.c_void_p), C.c_char_p]),
+    "ql_comm_create": (I, [I, I, I, I, P, C.c_char_p, C.POINTER(C.c_void_p)]),
+    "ql_comm_destroy": (I, [P]),
+    "ql_allreduce_f32": (I, [P, P, I, I]),
+    "ql_comm_step": (I, [P]),
     "ql_rms_norm_f32": (I, [P, P, P, I, I, F]),
     "ql_synth_quantized": (I, [I32, U64, I64, I, F, P]),
     "ql_row_bytes": (SZ, [I32, I]),
@@ -130,6 +140,85 @@ def quant_matmul_ex(t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamm
     """Prefill GEMM; path PATH_TENSOR forces the tcgen05 kernel, PATH_GEMV the streaming engine."""
     _call("ql_quant_matmul_ex", t, w, rb, x, x_stride, y, y_stride, out_dim, in_dim, m, gamma, eps, bias,
           1 if accumulate else 0, path)
+
+
+IPC_HANDLE_BYTES = 64
+
+
+class Comm:
+    """Peer-memory all-reduce communicator of one rank (see include/qlinear_b200.h).
+
+    `exchange_handles(own_handle) -> list of handles in rank order` is supplied by the
+    caller (e.g. torch.distributed.all_gather_object); the library stays host-agnostic."""
+
+    def __init__(self, rank, world, max_floats, slots, exchange_handles):
+        ptr = C.c_void_p()
+        hbuf = C.create_string_buffer(IPC_HANDLE_BYTES)
+        _call("ql_comm_alloc", world, max_floats, slots, C.byref(ptr), hbuf)
+        handles = exchange_handles(bytes(hbuf.raw))
+        if len(handles) != world or any(len(h) != IPC_HANDLE_BYTES for h in handles):
+            raise ValueError("exchange_handles must return one 64-byte handle per rank")
+        comm = C.c_void_p()
+        _call("ql_comm_create", rank, world, max_floats, slots, ptr, b"".join(handles), C.byref(comm))
+        self.handle, self.max_floats, self.slots = comm, max_floats, slots
+
+    def allreduce(self, buf_ptr, n, slot):
+        _call("ql_allreduce_f32", self.handle, buf_ptr, n, slot)
+
+    def step(self):
+        _call("ql_comm_step", self.handle)
+
+    def close(self):
+        if self.handle:
+            _call("ql_comm_destroy", self.handle)
+            self.handle = None
+
+
+def quant_gemv_argmax_ex(t, w, rb, x, x_stride, logits, logits_stride, out_dim, in_dim, m, gamma=None, eps=0.0,
+                         index_offset=0, out_idx=None, out_key=None):
+    """Fused LM head + greedy argmax (see include/qlinear_b200.h)."""
+    _call("ql_quant_gemv_argmax_ex", t, w, rb, x, x_stride, logits, logits_stride, out_dim, in_dim, m, gamma, eps,
+          index_offset, out_idx, out_key)
+
+
+OP_STORE, OP_ADD, OP_SWIGLU = 0, 1, 2
+
+
+class ChainOp(C.Structure):
+    """ql_chain_op (include/qlinear_b200.h)."""
+    _fields_ = [("kind", C.c_int32), ("quant_type", C.c_int32), ("nsrc", C.c_int32),
+                ("w", C.c_void_p * 3), ("row_bytes", C.c_size_t * 3), ("rows", C.c_int32 * 3),
+                ("in_dim", C.c_int32), ("x", C.c_void_p), ("gamma", C.c_void_p), ("eps", C.c_float),
+                ("bias", C.c_void_p), ("y", C.c_void_p), ("argmax_idx", C.c_void_p), ("argmax_offset", C.c_int32)]
+
+
+def chain_op(kind, weights, row_bytes, rows, in_dim, x, y, gamma=None, eps=0.0, bias=None, argmax_idx=None,
+             argmax_offset=0, quant_type=Q4_K):
+    op = ChainOp()
+    op.kind, op.quant_type, op.nsrc, op.in_dim = kind, quant_type, len(weights), in_dim
+    for i, (w, rb, r) in enumerate(zip(weights, row_bytes, rows)):
+        op.w[i], op.row_bytes[i], op.rows[i] = w, rb, r
+    op.x, op.y, op.gamma, op.eps, op.bias = x, y, gamma, eps, bias
+    op.argmax_idx, op.argmax_offset = argmax_idx, argmax_offset
+    return op
+
+
+class GemvChain:
+    """A list of single-token GEMV ops run as one persistent launch (ql_gemv_chain_*)."""
+
+    def __init__(self, ops):
+        arr = (ChainOp * len(ops))(*ops)
+        h = C.c_void_p()
+        _call("ql_gemv_chain_create", C.cast(arr, C.c_void_p), len(ops), C.byref(h))
+        self.handle = h
+
+    def run(self):
+        _call("ql_gemv_chain_run", self.handle)
+
+    def close(self):
+        if self.handle:
+            _call("ql_gemv_chain_destroy", self.handle)
+            self.handle = None
 
 
 def reserve_prefill(max_tokens, max_in_dim):

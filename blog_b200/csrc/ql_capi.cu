@@ -45,6 +45,7 @@ namespace {
 constexpr int kMaxDevices = 64;
 constexpr int kMaxGroups = 1 << 16;   // row groups per launch: out_dim <= 2,097,152
 constexpr int kArgmaxParts = 1024;
+constexpr int kMaxArgmaxRows = 4096;  // tokens per fused LM-head argmax launch
 
 struct Workspace {
     bool ready = false;
@@ -55,6 +56,8 @@ struct Workspace {
     int *err = nullptr;
     float *am_v = nullptr;
     int *am_i = nullptr;
+    unsigned long long *amax = nullptr;  // [kMaxArgmaxRows] fused-argmax keys, zero between launches
+    unsigned *amax_done = nullptr;       // fused-argmax CTA arrival counter
     // tensor-core prefill scratch, grown on demand (ql_reserve_prefill)
     __half *xh = nullptr;
     size_t xh_cap = 0;
@@ -96,6 +99,12 @@ int init_device(int dev) {
     if ((e = cudaMalloc(&w.err, sizeof(int))) != cudaSuccess) return cuda_fail(e, "workspace");
     if ((e = cudaMalloc(&w.am_v, kArgmaxParts * sizeof(float))) != cudaSuccess) return cuda_fail(e, "workspace");
     if ((e = cudaMalloc(&w.am_i, kArgmaxParts * sizeof(int))) != cudaSuccess) return cuda_fail(e, "workspace");
+    if ((e = cudaMalloc(&w.amax, kMaxArgmaxRows * sizeof(unsigned long long))) != cudaSuccess)
+        return cuda_fail(e, "workspace");
+    if ((e = cudaMalloc(&w.amax_done, sizeof(unsigned))) != cudaSuccess) return cuda_fail(e, "workspace");
+    if ((e = cudaMemset(w.amax, 0, kMaxArgmaxRows * sizeof(unsigned long long))) != cudaSuccess)
+        return cuda_fail(e, "memset");
+    if ((e = cudaMemset(w.amax_done, 0, sizeof(unsigned))) != cudaSuccess) return cuda_fail(e, "memset");
     if ((e = cudaMemset(w.counters, 0, kMaxGroups * sizeof(unsigned))) != cudaSuccess) return cuda_fail(e, "memset");
     if ((e = cudaMemset(w.err, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "memset");
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "init sync");
@@ -289,7 +298,13 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
         a.nst = sh.nst;
         a.pre_x = gemv_pre_x();
         a.x = base.x + (size_t)done * base.x_stride;
-        a.y = base.y + (size_t)done * base.y_stride;
+        a.y = base.y ? base.y + (size_t)done * base.y_stride : nullptr;
+        if (a.amax.amax != nullptr) {
+            a.amax.amax = ws->amax + done;
+            a.amax.done = ws->amax_done;
+            if (a.amax.idx) a.amax.idx = base.amax.idx + done;
+            if (a.amax.key) a.amax.key = base.amax.key + done;
+        }
         // Small reductions with at most one wave of row groups: one group per CTA
         // (no stream-K fixups); otherwise equal tile ranges over all SMs.
         int64_t C = (G <= ws->sms && base.U <= 32) ? G : (T < ws->sms ? T : ws->sms);
@@ -348,6 +363,7 @@ struct TcJob {
     float eps = 0.f;
     const float *bias = nullptr;
     int accumulate = 0;
+    AmaxOut amax{};  // fused argmax (plain only; amax.amax non-null = on, filled by run_gemm_tc)
 };
 
 // Whether the tensor-core GEMM can run the job: Q4_K, K % 256, row strides that are
@@ -420,6 +436,11 @@ int run_gemm_tc(const TcJob &j, const char *what) {
     a.nsb = nsb;
     a.ksplit = ks;
     a.err = ws->err;
+    if (!swiglu && j.amax.amax != nullptr) {
+        a.amax = j.amax;
+        a.amax.amax = ws->amax;
+        a.amax.done = ws->amax_done;
+    }
     cudaError_t e = gemm_xprep_launch(j.x, j.xs, j.gamma, j.eps, ws->xh, ws->rinv, j.M, j.K, g_stream);
     ++t_launches;
     if (e != cudaSuccess) return cuda_fail(e, what);
@@ -458,6 +479,30 @@ GemvArgs blank() {
 
 // Records `msg` as this thread's last error (for entry points in other files).
 int set_last_error(int code, const char *msg) { return fail(code, msg); }
+
+// Q4_K tensor map with the GEMV ring's {144, 7, 32} box, for the chain kernel.
+bool q4k_tensor_map_public(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes) {
+    return q4k_tensor_map(out, base, blocks, rows, row_bytes);
+}
+
+// Stream-K scratch, error word and SM count of the current device, for the chain kernel.
+int chain_workspace(float **part, unsigned **counters, int **err, int *sms) {
+    int st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    *part = ws->part;
+    *counters = ws->counters;
+    *err = ws->err;
+    *sms = ws->sms;
+    return QL_OK;
+}
+
+// The current device's error word (initialising the workspace if needed), or null.
+int *device_error_word() {
+    int st;
+    Workspace *ws = workspace(&st);
+    return ws ? ws->err : nullptr;
+}
 }  // namespace ql
 
 using namespace ql;
@@ -485,6 +530,8 @@ int ql_check_device(void) {
     if (h != 0) {
         cudaMemset(ws->err, 0, sizeof(int));
         cudaMemset(ws->counters, 0, kMaxGroups * sizeof(unsigned));
+        cudaMemset(ws->amax, 0, kMaxArgmaxRows * sizeof(unsigned long long));
+        cudaMemset(ws->amax_done, 0, sizeof(unsigned));
         cudaDeviceSynchronize();
         return fail(QL_EDEVICE, "a kernel gave up a bounded wait (device error code " + std::to_string(h) + ")");
     }
@@ -523,6 +570,45 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     a.eps = eps;
     a.bias = bias;
     return run_gemv(t, accumulate ? 1 : 0, a, m, "ql_quant_gemv");
+}
+
+int ql_quant_gemv_argmax_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int64_t xs, float *logits,
+                            int64_t ls, int out_dim, int in_dim, int m, const float *gamma, float eps, int index_offset,
+                            int *out_idx, uint64_t *out_key) {
+    t_launches = 0;
+    if (out_dim <= 0 || m <= 0 || m > kMaxArgmaxRows)
+        return fail(QL_EINVAL, "ql_quant_gemv_argmax_ex: need out_dim > 0 and 0 < m <= 4096");
+    if (!out_idx && !out_key) return fail(QL_EINVAL, "ql_quant_gemv_argmax_ex: null out_idx and out_key");
+    int st = check_weight(t, w, rb, 0, in_dim, "ql_quant_gemv_argmax_ex");
+    if (st) return st;
+    if (!x) return fail(QL_EINVAL, "ql_quant_gemv_argmax_ex: null x");
+    if ((st = check_act(x, xs, gamma, "ql_quant_gemv_argmax_ex"))) return st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    AmaxOut am{};
+    am.amax = ws->amax;
+    am.done = ws->amax_done;
+    am.idx = out_idx;
+    am.key = reinterpret_cast<unsigned long long *>(out_key);
+    am.offset = index_offset;
+    {
+        TcJob j = plain_job(w, rb, x, xs, logits, ls, out_dim, in_dim, m, gamma, eps, nullptr, 0);
+        j.amax = am;
+        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_gemv_argmax_ex");
+    }
+    GemvArgs a = blank();
+    a.w[0] = w;
+    a.row_bytes[0] = rb;
+    a.rows = out_dim;
+    a.K = in_dim;
+    a.x = x;
+    a.x_stride = xs;
+    a.y = logits;
+    a.y_stride = ls;
+    a.gamma = gamma;
+    a.eps = eps;
+    a.amax = am;
+    return run_gemv(t, 0, a, m, "ql_quant_gemv_argmax_ex");
 }
 
 int ql_quant_matmul_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int64_t xs, float *y, int64_t ys,

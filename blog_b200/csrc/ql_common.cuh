@@ -160,6 +160,49 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return *reinterpret_cast<float2 *>(&c);
 }
 
+// Greedy-argmax key, order-preserving in one 64-bit word: a larger key is a larger
+// logit, then a lower index (reference argmax, kernel.cu:3531-3592: strict '>' in
+// ascending order keeps the lowest index; NaN never wins; nothing selected -> 0).
+// -0 and +0 compare equal; NaN and -inf get key 0 and never win.
+__device__ __forceinline__ unsigned long long amax_key(float v, uint32_t idx) {
+    if (!(v > -INFINITY)) return 0ull;
+    const uint32_t u = __float_as_uint(v == 0.f ? 0.f : v);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ int amax_index(unsigned long long k) { return k ? (int)(0xFFFFFFFFu - (uint32_t)k) : 0; }
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, k, o);
+        k = t > k ? t : k;
+    }
+    return k;
+}
+// Fused greedy argmax of a launch: CTAs atomically max keys into amax[m]; the last
+// CTA to finish (arrival counter) turns them into indices / keys and resets both.
+struct AmaxOut {
+    unsigned long long *amax;  // [M] running keys (zero between launches)
+    unsigned *done;            // CTA arrival counter (zero between launches)
+    int *idx;                  // [M] argmax index, or null
+    unsigned long long *key;   // [M] final key (for combining vocabulary shards), or null
+    int offset;                // added to every index (vocabulary shard offset)
+};
+__device__ __forceinline__ void amax_cta_done(const AmaxOut &o, int M) {
+    __threadfence();
+    const unsigned prev = atomicAdd(o.done, 1u);
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    if (prev == total - 1) {
+        __threadfence();
+        for (int m = 0; m < M; ++m) {
+            const unsigned long long k = atomicExch(&o.amax[m], 0ull);
+            if (o.idx) o.idx[m] = amax_index(k);
+            if (o.key) o.key[m] = k;
+        }
+        atomicExch(o.done, 0u);
+    }
+}
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)));
 }

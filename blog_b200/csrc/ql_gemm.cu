@@ -376,7 +376,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
     constexpr int C4 = BNO / 4;  // float4 items per output row
     const uint32_t red_base = smem_u32(sRed);
     const bool good = !*abort_flag;
-    for (int it = threadIdx.x; good && it < (r_hi - r_lo) * C4; it += kGemmThreads) {
+    static_assert(C4 % 32 == 0 && kGemmThreads % C4 == 0, "a warp's epilogue items must share one output row");
+    // the warp-collective argmax reduction below needs whole warps in every iteration
+    const int items = (r_hi - r_lo) * C4;
+    for (int it = threadIdx.x; good && it - (threadIdx.x & 31) < items; it += kGemmThreads) {
+        if (it >= items) {  // idle lanes of a partial warp still join the shuffles
+            if (EPI == kGemmPlain && a.amax.amax != nullptr) warp_max_u64(0ull);
+            continue;
+        }
         const int rr = r_lo + it / C4, c4 = it % C4;
         const uint32_t off = red_base + (uint32_t)(rr * kGemmRedPitch + c4 * 16);
         float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
@@ -398,7 +405,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
             float4 v4 = make_float4(o[0], o[1], o[2], o[3]);
             if (EPI == kGemmPlain && a.bias) v4 = f4_add(v4, *reinterpret_cast<const float4 *>(a.bias + gn));
             if (EPI == kGemmPlain && a.accumulate) v4 = f4_add(v4, *reinterpret_cast<const float4 *>(yp));
-            *reinterpret_cast<float4 *>(yp) = v4;
+            if (a.y) *reinterpret_cast<float4 *>(yp) = v4;
+            o[0] = v4.x; o[1] = v4.y; o[2] = v4.z; o[3] = v4.w;
         } else {
 #pragma unroll
             for (int e = 0; e < 4; ++e)
@@ -406,9 +414,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                     float v = o[e];
                     if (EPI == kGemmPlain && a.bias) v += a.bias[gn + e];
                     if (EPI == kGemmPlain && a.accumulate) v += yp[e];
-                    yp[e] = v;
+                    if (a.y) yp[e] = v;
+                    o[e] = v;
                 }
         }
+        if (EPI == kGemmPlain && a.amax.amax != nullptr) {
+            // a warp's items lie in one output row (C4 and the thread count are multiples of 32 items)
+            unsigned long long k = 0ull;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const unsigned long long ke = gn + e < a.N ? amax_key(o[e], (uint32_t)(gn + e + a.amax.offset)) : 0ull;
+                k = ke > k ? ke : k;
+            }
+            k = warp_max_u64(k);
+            if ((threadIdx.x & 31) == 0 && k != 0ull) atomicMax(&a.amax.amax[gm], k);
+        }
+    }
+    if (EPI == kGemmPlain && a.amax.amax != nullptr) {
+        __syncthreads();
+        if (threadIdx.x == 0) amax_cta_done(a.amax, a.M);
     }
     if (ks > 1) cluster_sync_all();  // peers may still be reading this CTA's tile
 }

@@ -72,6 +72,7 @@ struct GemmArgs {
     int nsb;               // K / 256
     int ksplit;            // K ranges per output tile = cluster size along z (<= 8)
     int *err;
+    AmaxOut amax;          // fused greedy argmax over the output columns (plain; amax.amax null = off)
 };
 
 bool gemv_pdl_enabled();  // QL_PDL=0 turns programmatic dependent launch off

@@ -102,6 +102,7 @@ struct GemvArgs {
     float *part;              // stream-K partial slots [C][2][MT][NMAT][32]
     unsigned *counters;       // stream-K arrival counters [G], zero between launches
     int *err;                 // device error word
+    AmaxOut amax;             // fused greedy argmax over the rows (kEpiStore; amax.amax null = off)
 };
 
 // One stage of a CTA's stream: row group g, blocks [us, ue) of the group's

@@ -571,11 +571,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
                         float o = val[0][m] * nrm;
                         if (a.bias != nullptr) o += a.bias[v];
                         if (EPI == kEpiAdd) *yp += o;
-                        else *yp = o;
+                        else if (a.y != nullptr) *yp = o;
+                        val[0][m] = o;
                     }
                 }
             }
+            if (EPI == kEpiStore && a.amax.amax != nullptr && finish) {  // fused greedy argmax
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    unsigned long long k = v < a.rows ? amax_key(val[0][m], (uint32_t)(v + a.amax.offset)) : 0ull;
+                    k = warp_max_u64(k);
+                    if (lane == 0 && k != 0ull) atomicMax(&a.amax.amax[m], k);
+                }
+            }
         }
+        if (EPI == kEpiStore && a.amax.amax != nullptr && lane == 0) amax_cta_done(a.amax, a.M);
         return;
     }
 

@@ -89,11 +89,79 @@ QL_API int ql_quant_matmul(int32_t quant_type, const uint8_t *weight, size_t row
 QL_API int ql_quant_matmul_ex(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x,
                               int64_t x_stride, float *y, int64_t y_stride, int out_dim, int in_dim, int m,
                               const float *gamma, float eps, const float *bias, int accumulate, int path);
+/* Greedy LM head (fused GEMV/GEMM + argmax, no separate argmax launch): for each token m,
+ * out_idx[m] = index_offset + argmax_o y[m, o] with y as ql_quant_matmul_ex (plain store,
+ * optional fused RMSNorm), lowest index on ties, NaN never wins (reference argmax,
+ * kernel.cu:3531-3592).  logits (nullable) also receives y.  out_key (nullable) receives
+ * an order-preserving 64-bit key per token (larger = better, ties to the lower index);
+ * the maximum key over vocabulary shards, each launched with its own index_offset,
+ * selects the same token as an argmax over the whole vocabulary.  m <= 4096. */
+QL_API int ql_quant_gemv_argmax_ex(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const float *x,
+                                   int64_t x_stride, float *logits, int64_t logits_stride, int out_dim, int in_dim,
+                                   int m, const float *gamma, float eps, int index_offset, int *out_idx,
+                                   uint64_t *out_key);
+/* ---- a chain of single-token GEMVs in one persistent launch ----------------------
+ * A decode step's projections (q/k/v, o + residual, gate/up SwiGLU, down + residual,
+ * ..., LM head + argmax) as one cooperative kernel: the weight stream runs across op
+ * boundaries and each op waits at a grid barrier for the previous op's output.  Q4_K,
+ * one token, in_dim a multiple of 256 and >= 1792, 16-byte aligned weights with
+ * row_bytes % 16 == 0 and >= 32 rows per source.  Op semantics equal the per-op entry
+ * points: STORE y = (RMSNorm?)(x) . W^T + bias over 1..3 stacked sources (all but the
+ * last a multiple of 32 rows), optionally with a greedy argmax (argmax_idx, device int,
+ * index + argmax_offset; y may then be NULL); ADD y += ...; SWIGLU y = SiLU(g) * u with
+ * w[0] = gate, w[1] = up.  Every op may read what any earlier op wrote.  The chain keeps
+ * the pointers: buffers must outlive it.  ql_gemv_chain_run enqueues one launch on the
+ * current stream (graph-capturable). */
+#define QL_OP_STORE 0
+#define QL_OP_ADD 1
+#define QL_OP_SWIGLU 2
+typedef struct ql_chain_op {
+    int32_t kind;
+    int32_t quant_type;
+    int32_t nsrc;
+    const uint8_t *w[3];
+    size_t row_bytes[3];
+    int32_t rows[3];
+    int32_t in_dim;
+    const float *x;
+    const float *gamma;
+    float eps;
+    const float *bias;
+    float *y;
+    int *argmax_idx;
+    int32_t argmax_offset;
+} ql_chain_op;
+QL_API int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain);
+QL_API int ql_gemv_chain_run(void *chain);
+QL_API int ql_gemv_chain_destroy(void *chain);
+
 /* Reserve the tensor-core path's scratch (f16 activations, row scales, split-K
  * partial tiles) on the current device for up to max_tokens x max_in_dim, so later
  * prefill calls of at most that size allocate nothing (e.g. inside graph capture).
  * Larger calls grow the scratch with cudaMalloc. */
 QL_API int ql_reserve_prefill(int max_tokens, int max_in_dim);
+
+/* ---- tensor-parallel exchange over NVLink peer memory ------------------------------
+ * One-shot all-reduce for the decode step's row-parallel projections (no reference
+ * twin: the reference engine is single-GPU).  Setup, once per rank:
+ *   ql_comm_alloc   allocates this rank's zeroed exchange buffer on the current device
+ *                   and returns its CUDA IPC handle (QL_IPC_HANDLE_BYTES bytes);
+ *   (exchange the handles between ranks by any host channel, in rank order)
+ *   ql_comm_create  maps every peer's buffer (handles: world x QL_IPC_HANDLE_BYTES).
+ * Per step: the same sequence of ql_allreduce_f32 calls on every rank, each naming
+ * its call site with a distinct slot < slots, then one ql_comm_step.  Everything is
+ * enqueued on the current stream and may be captured into a CUDA graph.  A peer that
+ * never arrives makes the call give up after ~5 s with an error in the device error
+ * word (ql_check_device returns QL_EDEVICE). */
+#define QL_IPC_HANDLE_BYTES 64
+QL_API size_t ql_comm_bytes(int world, int max_floats, int slots);
+QL_API int ql_comm_alloc(int world, int max_floats, int slots, void **exchange, uint8_t *handle);
+QL_API int ql_comm_create(int rank, int world, int max_floats, int slots, void *exchange, const uint8_t *handles,
+                          void **comm);
+QL_API int ql_comm_destroy(void *comm);
+/* buf[0..n) (device, n <= max_floats) := sum over ranks, bit-identical on every rank. */
+QL_API int ql_allreduce_f32(void *comm, float *buf, int n, int slot);
+QL_API int ql_comm_step(void *comm);
 
 /* act[f] = SiLU(Wg[f] . x) * (Wu[f] . x).  kernel.cuh:65-67. */
 QL_API int ql_quant_swiglu(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,

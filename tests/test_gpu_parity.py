@@ -322,3 +322,65 @@ def test_known_answers_through_capi(golden):
 
 def test_device_error_word_clean():
     Q.check_device()
+
+
+# ---- fused LM head + greedy argmax ---------------------------------------------------
+def _key_index(keys):
+    keys = np.asarray(keys, np.uint64)
+    return np.where(keys == 0, 0, (np.uint64(0xFFFFFFFF) - (keys & np.uint64(0xFFFFFFFF)))).astype(np.int64)
+
+
+@pytest.mark.parametrize("m", [1, 3, 16])  # GEMV engine (1, 3) and tensor-core path (16)
+def test_lm_head_argmax_matches_logits(m):
+    import torch
+    t, n, k, eps = O.Q4_K, 30000, 1024, 1e-6
+    w = make_weights(t, n, k, seed=201)
+    x = _x(202, m, k)
+    gamma = (1.0 + 0.1 * _x(203, 1, k)[0]).astype(np.float32)
+    rb = O.row_bytes(t, k)
+    logits = torch.empty((m, n), device="cuda:0")
+    idx = torch.full((m,), -1, dtype=torch.int32, device="cuda:0")
+    key = torch.zeros((m,), dtype=torch.int64, device="cuda:0")
+    for _ in range(2):  # the second launch checks that the keys were reset
+        Q.quant_gemv_argmax_ex(t, dev(w).data_ptr(), rb, dev(x).data_ptr(), k, logits.data_ptr(), n, n, k, m,
+                               dev(gamma).data_ptr(), eps, 0, idx.data_ptr(), key.data_ptr())
+        lg = host(logits)
+        want = np.argmax(lg, axis=1)  # first occurrence = lowest index on ties
+        assert np.array_equal(host(idx), want)
+        assert np.array_equal(_key_index(host(key).view(np.uint64)), want)
+
+
+def test_lm_head_argmax_vocabulary_shards_combine():
+    import torch
+    t, n, k, m = O.Q4_K, 20000, 512, 2
+    w = make_weights(t, n, k, seed=211)
+    x = _x(212, m, k)
+    rb = O.row_bytes(t, k)
+    full_idx = torch.empty((m,), dtype=torch.int32, device="cuda:0")
+    Q.quant_gemv_argmax_ex(t, dev(w).data_ptr(), rb, dev(x).data_ptr(), k, None, 0, n, k, m, None, 0.0, 0,
+                           full_idx.data_ptr(), None)
+    keys = []
+    for lo, hi in ((0, 9984), (9984, n)):  # two vocabulary shards, 32-row aligned
+        kk = torch.zeros((m,), dtype=torch.int64, device="cuda:0")
+        Q.quant_gemv_argmax_ex(t, dev(np.ascontiguousarray(w[lo:hi])).data_ptr(), rb, dev(x).data_ptr(), k, None, 0,
+                               hi - lo, k, m, None, 0.0, lo, None, kk.data_ptr())
+        keys.append(host(kk).view(np.uint64))
+    comb = np.maximum(keys[0], keys[1])
+    assert np.array_equal(_key_index(comb), host(full_idx))
+
+
+@pytest.mark.parametrize("m", [1, 16])
+def test_lm_head_argmax_nan_rows_select_zero(m):
+    import torch
+    t, n, k = O.Q4_K, 4096, 512
+    w = make_weights(t, n, k, seed=221)
+    x = _x(222, m, k)
+    x[0, :] = np.nan
+    rb = O.row_bytes(t, k)
+    idx = torch.full((m,), -1, dtype=torch.int32, device="cuda:0")
+    logits = torch.empty((m, n), device="cuda:0")
+    Q.quant_gemv_argmax_ex(t, dev(w).data_ptr(), rb, dev(x).data_ptr(), k, logits.data_ptr(), n, n, k, m, None, 0.0,
+                           0, idx.data_ptr(), None)
+    got = host(idx)
+    assert got[0] == 0
+    assert np.array_equal(got[1:], np.argmax(host(logits)[1:], axis=1))
