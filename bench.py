@@ -178,7 +178,28 @@ class DecodeStack:
                 torch.distributed.all_gather_object(out, h)
                 return out
             self.comm = Q.Comm(rank, world, 4096, 2 * LAYERS, exchange)
+        # Single GPU, one token: the whole stack as one persistent launch (QL_CHAIN=0: per-op launches)
+        self.chain = None
+        if world == 1 and M == 1 and os.environ.get("QL_CHAIN", "1") != "0":
+            self.chain = Q.GemvChain(self.chain_ops())
         torch.cuda.synchronize()
+
+    def chain_ops(self):
+        Q, rbh = self.Q, self.Q.row_bytes(QK, HIDDEN)
+        h, ops = self.h.data_ptr(), []
+        for L in self.layers:
+            ops.append(Q.chain_op(Q.OP_STORE, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
+                                  [self.qo_len, self.kv_len, self.kv_len], HIDDEN, h, self.qkv.data_ptr(),
+                                  L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr()))
+            ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [Q.row_bytes(QK, self.qo_len)], [HIDDEN],
+                                  self.qo_len, self.qkv.data_ptr(), h))
+            ops.append(Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rbh] * 2,
+                                  [self.f_len] * 2, HIDDEN, h, self.act.data_ptr(), L["ln2"].data_ptr(), EPS))
+            ops.append(Q.chain_op(Q.OP_ADD, [L["wd"].data_ptr()], [Q.row_bytes(QK, self.f_len)], [HIDDEN],
+                                  self.f_len, self.act.data_ptr(), h))
+        ops.append(Q.chain_op(Q.OP_STORE, [self.wlm.data_ptr()], [rbh], [self.v_len], HIDDEN, h,
+                              self.logits.data_ptr(), self.lnf.data_ptr(), EPS, argmax_idx=self.tok.data_ptr()))
+        return ops
 
     def weight_bytes(self):
         n = sum(w.numel() for L in self.layers for key, w in L.items() if key.startswith("w"))
@@ -190,6 +211,14 @@ class DecodeStack:
         Q.set_stream(torch.cuda.current_stream().cuda_stream)
         rbh = Q.row_bytes(QK, HIDDEN)
         self.h.copy_(self.h_in)
+        if self.chain is not None:
+            if events is not None:
+                events["pairs"]["chain"][0].record()
+            self.chain.run()
+            if events is not None:
+                events["pairs"]["chain"][1].record()
+            self.token_ids.copy_(self.tok)
+            return
         h = self.h.data_ptr()
         slot = 0
 
@@ -222,10 +251,9 @@ class DecodeStack:
                             self.act.shape[1], h, HIDDEN, HIDDEN, self.f_len, M, accumulate=(self.rank == 0))
             if self.world > 1:
                 reduce_h()
-        Q.quant_gemv_ex(QK, self.wlm.data_ptr(), rbh, h, HIDDEN, self.logits.data_ptr(), self.v_len, self.v_len,
-                        HIDDEN, M, self.lnf.data_ptr(), EPS)
-        for m in range(M):
-            Q.argmax(self.logits[m].data_ptr(), self.v_len, self.tok[m:m + 1].data_ptr())
+        # LM head with the greedy argmax fused into its epilogue
+        Q.quant_gemv_argmax_ex(QK, self.wlm.data_ptr(), rbh, h, HIDDEN, self.logits.data_ptr(), self.v_len,
+                               self.v_len, HIDDEN, M, self.lnf.data_ptr(), EPS, 0, self.tok.data_ptr(), None)
         if self.world > 1:
             idx = self.tok.long()
             self.best[:, 0] = self.logits.gather(1, idx[:, None])[:, 0]
@@ -239,10 +267,20 @@ class DecodeStack:
             self.token_ids.copy_(self.tok)
 
     def launches_per_step(self):
-        """Library kernel launches per step: per layer qkv, o, gate/up, down (each in
-        chunks of <= 4 tokens, gate/up <= 2), the LM head, and 2 argmax kernels per token."""
+        """Library kernel launches per step: one persistent chain launch, or per layer
+        qkv, o, gate/up, down plus the LM head with its fused argmax (one GEMV launch per
+        <= 4 tokens, gate/up <= 2; tensor-core path: activation prep + GEMM per op)."""
+        if self.chain is not None:
+            return 1
+        if self.M >= 8:
+            return 2 * (4 * LAYERS + 1)
         c4, c2 = (self.M + 3) // 4, (self.M + 1) // 2
-        return LAYERS * (3 * c4 + c2) + c4 + 2 * self.M
+        return LAYERS * (3 * c4 + c2) + c4
+
+    def chain_act_bytes(self):
+        """Activation bytes the chain reads and writes per step (x in, y out, per op)."""
+        per_layer = (HIDDEN + self.qkv_w) + (self.qo_len + HIDDEN) + (HIDDEN + self.f_len) + (self.f_len + HIDDEN)
+        return 4 * (LAYERS * per_layer + HIDDEN + self.v_len)
 
 
 # --------------------------------------------------------------------------------------
@@ -274,9 +312,9 @@ def cpu_oracle_rate(sample_layers=2, reps=2):
             "seconds_per_sample": best}
 
 
-def profile_traffic():
+def profile_traffic(name="gemv_q4k_swiglu_18944x3584.md"):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "gemv_q4k_swiglu_18944x3584.md")
+    p = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(p):
             if "dram_bytes_per_launch:" in line:
@@ -449,8 +487,9 @@ def main():
         s = torch.cuda.Stream()
         host_in = torch.randn((batch, HIDDEN), generator=torch.Generator().manual_seed(5)).pin_memory()
         host_out = torch.zeros((batch,), dtype=torch.int32).pin_memory()
-        evl = [3, 10, 17, 24]
-        # event-record nodes inside the graph around the dominant kernel of 4 layers
+        # event-record nodes inside the graph around the dominant kernel: the chain launch
+        # (the whole step) or the gate/up SwiGLU launch of 4 layers
+        evl = ["chain"] if stack.chain is not None else [3, 10, 17, 24]
         events = {"layers": evl, "pairs": {l: (torch.cuda.Event(enable_timing=True, external=True),
                                                torch.cuda.Event(enable_timing=True, external=True)) for l in evl}}
         with torch.cuda.stream(s):
@@ -501,6 +540,7 @@ def main():
         if world > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         res = {"ms": float(t[0]), "e2e_ms": float(t[1]), "kernel_ms": float(t[2]), "clocks": clk.summary(),
+               "chain": stack.chain is not None, "chain_act_bytes": stack.chain_act_bytes(),
                "launches": stack.launches_per_step(), "wbytes": stack.weight_bytes(),
                "h2d": host_in.numel() * 4, "d2h": host_out.numel() * 4, "f_len": stack.f_len}
         del graph
@@ -509,6 +549,8 @@ def main():
             torch.distributed.barrier()  # no peer still reads this rank's exchange buffer
         if stack.comm is not None:
             stack.comm.close()
+        if stack.chain is not None:
+            stack.chain.close()
         del stack
         torch.cuda.empty_cache()
         return res
@@ -519,10 +561,17 @@ def main():
     if rank == 0:
         hbm, peak_kind = peaks()
         toks = args.batch / (r1["ms"] / 1e3)
-        # dominant kernel: fused RMSNorm + gate/up SwiGLU GEMV (largest launch, 54% of weight bytes)
-        alg_bytes = 2 * r1["f_len"] * HIDDEN * BPE + args.batch * HIDDEN * 4 * 2 + args.batch * r1["f_len"] * 4
-        achieved = alg_bytes / (r1["kernel_ms"] / 1e3) / 1e9
         total_bytes = weight_elems() * BPE
+        if r1["chain"]:
+            # dominant kernel: the persistent chain launch = the whole step's weights and activations
+            alg_bytes = r1["wbytes"] + r1["chain_act_bytes"]
+            kname, traffic = "gemv_chain_kernel (28 layers x {qkv, o, gate/up, down} + LM head/argmax)", \
+                profile_traffic("gemv_chain_qwen2_7b_q4k_decode.md")
+        else:
+            # dominant kernel: fused RMSNorm + gate/up SwiGLU GEMV (largest launch, 54% of weight bytes)
+            alg_bytes = 2 * r1["f_len"] * HIDDEN * BPE + args.batch * HIDDEN * 4 * 2 + args.batch * r1["f_len"] * 4
+            kname, traffic = "qgemv_kernel<Q4_K,MT=1,NMAT=2> fused RMSNorm+gate/up SwiGLU", profile_traffic()
+        achieved = alg_bytes / (r1["kernel_ms"] / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": toks, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r1["ms"], "higher_is_better": True, "scaling": "strong",
@@ -534,7 +583,7 @@ def main():
             "hbm_roofline_tokens_per_s": hbm * 1e9 / (total_bytes / world),
             "step_weight_GBps": total_bytes / (r1["ms"] / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "traffic": profile_traffic(), "kernel": "qgemv_kernel<Q4_K,MT=1,NMAT=2> fused RMSNorm+gate/up SwiGLU",
+                         "traffic": traffic, "kernel": kname,
                          "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": r1["kernel_ms"],
                          "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"},
             "e2e": {"value": args.batch / (r1["e2e_ms"] / 1e3), "unit": "tokens/s",

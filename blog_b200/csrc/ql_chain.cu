@@ -18,6 +18,7 @@
 //     SwiGLU, fused RMSNorm, fused greedy argmax) as the per-op kernels.
 // Arrival counters and the launch epoch are monotonic, so a CUDA graph can
 // replay the launch without resets.  Every wait is bounded.
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -121,8 +122,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             const ChainOp &o = a.ops[p];
             for (int i = 0; i < (o.nmat == 2 ? 2 : 3); ++i) tensormap_acquire(&o.tmap[i]);
             const int seg = 2 * kTmaSeg / o.nmat;
-            int64_t t = plan_start(o.plan, cta);
-            const int64_t t1 = plan_start(o.plan, cta + 1);
+            int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
+            const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
             Stage st;
             while (next_stage(t, t1, o.U, seg, 0, st)) {
                 const int slot = it % kChainSlots;
@@ -163,7 +164,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
         for (int p = 0; p < a.nops; ++p) {
             const ChainOp &o = a.ops[p];
             const int NM = o.nmat, U = o.U;
-            const int64_t t0 = plan_start(o.plan, cta), t1 = plan_start(o.plan, cta + 1);
+            const int64_t t0 = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
+            const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
             for (int64_t gg = t0 / U; gg * U < t1; ++gg, ++gi) {
                 const int g = (int)gg;
                 const int bsel = gi & 1;
@@ -221,7 +223,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                         } else {
                             out = val[0] * nrm;
                             if (o.bias != nullptr) out += o.bias[v];
-                            if (o.kind == kOpAdd) *yp += out;
+                            if (o.kind == kOpAdd) __stcg(yp, __ldcg(yp) + out);  // residual written by other SMs
                             else if (o.y != nullptr) *yp = out;
                         }
                     }
@@ -274,11 +276,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             const int nch = K / 4;
             constexpr int B = 12;
             for (int j0 = ctid; j0 - lane < nch; j0 += B * nthr) {
-                float4 vv[B];
+                float4 vv[B], gg[B];
 #pragma unroll
                 for (int u = 0; u < B; ++u) {
                     const int j = j0 + u * nthr;
-                    vv[u] = j < nch ? reinterpret_cast<const float4 *>(o.x)[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    // L2 only: another SM wrote x during the previous op, after this SM may have cached it
+                    vv[u] = j < nch ? __ldcg(reinterpret_cast<const float4 *>(o.x) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    gg[u] = (j < nch && o.gamma != nullptr) ? reinterpret_cast<const float4 *>(o.gamma)[j]
+                                                            : make_float4(1.f, 1.f, 1.f, 1.f);
                 }
 #pragma unroll
                 for (int u = 0; u < B; ++u) {
@@ -288,7 +293,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                     float4 xv = vv[u];
                     if (ok && o.gamma != nullptr) {
                         ss += fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, xv.w * xv.w)));
-                        const float4 g = *reinterpret_cast<const float4 *>(o.gamma + k);
+                        const float4 g = gg[u];
                         xv.x *= g.x; xv.y *= g.y; xv.z *= g.z; xv.w *= g.w;
                     }
                     float bs = (xv.x + xv.y) + (xv.z + xv.w);
@@ -319,8 +324,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
 
         float acc[2][1] = {{0.f}, {0.f}};
         const int seg = 2 * kTmaSeg / NM;
-        int64_t t = plan_start(o.plan, cta);
-        const int64_t t1 = plan_start(o.plan, cta + 1);
+        int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
+        const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
         Stage st;
         while (next_stage(t, t1, U, seg, 0, st)) {
             const int slot = it % kChainSlots;
@@ -383,6 +388,15 @@ int chain_workspace(float **part, unsigned **counters, int **err, int *sms);
 }
 
 namespace {
+// Reductions of at most this many blocks run one row group per CTA (QL_CHAIN_ONEGROUP overrides, for tuning).
+int chain_max_units_one_group() {
+    static const int v = [] {
+        const char *e = getenv("QL_CHAIN_ONEGROUP");
+        return e ? atoi(e) : 80;  // includes the down projection (74 blocks): measured faster than stream-K there
+    }();
+    return v;
+}
+
 struct Chain {
     ChainOp *ops_dev = nullptr;
     unsigned long long *keys = nullptr;  // [nops] fused-argmax keys
@@ -448,7 +462,10 @@ int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain) {
         o.K = q.in_dim;
         o.U = blocks;
         const int G = (total + kRowGroup - 1) / kRowGroup;
-        o.plan = Plan{(int64_t)G * blocks, G, blocks, sms};
+        // like the per-op launcher: short reductions with at most one wave of row groups take one
+        // group per CTA (no stream-K fix-ups, whose latency would sit on the chain's critical path)
+        const int copt = (G <= sms && blocks <= chain_max_units_one_group()) ? G : sms;
+        o.plan = Plan{(int64_t)G * blocks, G, blocks, copt};
         o.x = q.x;
         o.gamma = q.gamma;
         o.eps = q.eps;

@@ -609,13 +609,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
         // The loop bound is warp-uniform (the shuffles below need every lane);
         // lanes past the end are masked by `ok`.
         for (int j0 = ctid; j0 - lane < nch; j0 += B * nthr) {
-            float4 v[B];
+            float4 v[B], gv[B];
 #pragma unroll
             for (int u = 0; u < B; ++u) {
                 const int j = j0 + u * nthr;
                 v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                gv[u] = make_float4(1.f, 1.f, 1.f, 1.f);
                 if (j < nch) {
                     const int m = j / (K / 4), k = 4 * (j - m * (K / 4));
+                    if (a.gamma != nullptr) gv[u] = *reinterpret_cast<const float4 *>(a.gamma + k);  // with x: one round trip
                     if (SRC == kSrcIndexedK) {
                         const int F = a.units_per_route * BE;
                         const int r = k / F;
@@ -640,7 +642,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
 #pragma unroll
                     for (int mm = 0; mm < MT; ++mm)
                         if (mm == m) ss[mm] += q;
-                    const float4 g = *reinterpret_cast<const float4 *>(a.gamma + k);
+                    const float4 g = gv[u];
                     xv.x *= g.x; xv.y *= g.y; xv.z *= g.z; xv.w *= g.w;
                 }
                 float bs = (xv.x + xv.y) + (xv.z + xv.w);
