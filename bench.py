@@ -172,16 +172,24 @@ class DecodeStack:
         # Row-parallel partial sums: the library's one-shot peer-memory all-reduce
         # for decode-sized vectors, NCCL for larger ones (QL_TP_NCCL=1 forces NCCL).
         self.comm = None
-        if world > 1 and M * HIDDEN <= 4096 and os.environ.get("QL_TP_NCCL", "0") != "1":
+        use_chain = M == 1 and os.environ.get("QL_CHAIN", "1") != "0"
+        if world > 1 and not use_chain and M * HIDDEN <= 4096 and os.environ.get("QL_TP_NCCL", "0") != "1":
             def exchange(h):
                 out = [None] * world
                 torch.distributed.all_gather_object(out, h)
                 return out
             self.comm = Q.Comm(rank, world, 4096, 2 * LAYERS, exchange)
-        # Single GPU, one token: the whole stack as one persistent launch (QL_CHAIN=0: per-op launches)
+        # One token: the whole stack as one persistent launch per step (QL_CHAIN=0: per-op launches);
+        # with world > 1 the row-parallel partial sums cross NVLink inside that launch
         self.chain = None
-        if world == 1 and M == 1 and os.environ.get("QL_CHAIN", "1") != "0":
-            self.chain = Q.GemvChain(self.chain_ops())
+        if use_chain:
+            exchange = None
+            if world > 1:
+                def exchange(hnd):
+                    out = [None] * world
+                    torch.distributed.all_gather_object(out, hnd)
+                    return out
+            self.chain = Q.GemvChain(self.chain_ops(), rank, world, exchange)
         torch.cuda.synchronize()
 
     def chain_ops(self):
@@ -192,13 +200,14 @@ class DecodeStack:
                                   [self.qo_len, self.kv_len, self.kv_len], HIDDEN, h, self.qkv.data_ptr(),
                                   L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr()))
             ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [Q.row_bytes(QK, self.qo_len)], [HIDDEN],
-                                  self.qo_len, self.qkv.data_ptr(), h))
+                                  self.qo_len, self.qkv.data_ptr(), h, reduce=self.world > 1))
             ops.append(Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rbh] * 2,
                                   [self.f_len] * 2, HIDDEN, h, self.act.data_ptr(), L["ln2"].data_ptr(), EPS))
             ops.append(Q.chain_op(Q.OP_ADD, [L["wd"].data_ptr()], [Q.row_bytes(QK, self.f_len)], [HIDDEN],
-                                  self.f_len, self.act.data_ptr(), h))
+                                  self.f_len, self.act.data_ptr(), h, reduce=self.world > 1))
         ops.append(Q.chain_op(Q.OP_STORE, [self.wlm.data_ptr()], [rbh], [self.v_len], HIDDEN, h,
-                              self.logits.data_ptr(), self.lnf.data_ptr(), EPS, argmax_idx=self.tok.data_ptr()))
+                              self.logits.data_ptr(), self.lnf.data_ptr(), EPS, argmax_idx=self.tok.data_ptr(),
+                              argmax_offset=self.v_off))
         return ops
 
     def weight_bytes(self):

@@ -69,6 +69,12 @@ SIGNATURES = {
     "ql_reserve_prefill": (I, [I, I]),
     "ql_quant_gemv_argmax_ex": (I, [I32, P, SZ, P, I64, P, I64, I, I, I, P, F, I, P, P]),
     "ql_gemv_chain_create": (I, [P, I, C.POINTER(C.c_void_p)]),
+    "ql_gemv_chain_exchange_bytes": (SZ, [P, I, I]),
+    "ql_gemv_chain_create_tp": (I, [P, I, I, I, P, C.POINTER(C.c_void_p)]),
+    "ql_ipc_alloc": (I, [SZ, C.POINTER(C.c_void_p), C.c_char_p]),
+    "ql_ipc_free": (I, [P]),
+    "ql_ipc_open": (I, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "ql_ipc_close": (I, [P]),
     "ql_gemv_chain_run": (I, [P]),
     "ql_gemv_chain_destroy": (I, [P]),
     "ql_comm_bytes": (SZ, [I, I, I]),
@@ -189,36 +195,68 @@ class ChainOp(C.Structure):
     _fields_ = [("kind", C.c_int32), ("quant_type", C.c_int32), ("nsrc", C.c_int32),
                 ("w", C.c_void_p * 3), ("row_bytes", C.c_size_t * 3), ("rows", C.c_int32 * 3),
                 ("in_dim", C.c_int32), ("x", C.c_void_p), ("gamma", C.c_void_p), ("eps", C.c_float),
-                ("bias", C.c_void_p), ("y", C.c_void_p), ("argmax_idx", C.c_void_p), ("argmax_offset", C.c_int32)]
+                ("bias", C.c_void_p), ("y", C.c_void_p), ("argmax_idx", C.c_void_p), ("argmax_offset", C.c_int32),
+                ("reduce", C.c_int32)]
 
 
 def chain_op(kind, weights, row_bytes, rows, in_dim, x, y, gamma=None, eps=0.0, bias=None, argmax_idx=None,
-             argmax_offset=0, quant_type=Q4_K):
+             argmax_offset=0, quant_type=Q4_K, reduce=False):
     op = ChainOp()
     op.kind, op.quant_type, op.nsrc, op.in_dim = kind, quant_type, len(weights), in_dim
     for i, (w, rb, r) in enumerate(zip(weights, row_bytes, rows)):
         op.w[i], op.row_bytes[i], op.rows[i] = w, rb, r
     op.x, op.y, op.gamma, op.eps, op.bias = x, y, gamma, eps, bias
-    op.argmax_idx, op.argmax_offset = argmax_idx, argmax_offset
+    op.argmax_idx, op.argmax_offset, op.reduce = argmax_idx, argmax_offset, 1 if reduce else 0
     return op
 
 
 class GemvChain:
-    """A list of single-token GEMV ops run as one persistent launch (ql_gemv_chain_*)."""
+    """A list of single-token GEMV ops run as one persistent launch (ql_gemv_chain_*).
 
-    def __init__(self, ops):
+    Tensor parallel: pass rank, world and `exchange_handles(own_handle) -> handles in rank
+    order` (any host channel, e.g. torch.distributed.all_gather_object); ops with reduce=True
+    then sum their partials over ranks inside the kernel through peer memory."""
+
+    def __init__(self, ops, rank=0, world=1, exchange_handles=None):
         arr = (ChainOp * len(ops))(*ops)
         h = C.c_void_p()
-        _call("ql_gemv_chain_create", C.cast(arr, C.c_void_p), len(ops), C.byref(h))
+        self.own, self.mapped = None, []
+        if world == 1:
+            _call("ql_gemv_chain_create", C.cast(arr, C.c_void_p), len(ops), C.byref(h))
+        else:
+            nbytes = lib().ql_gemv_chain_exchange_bytes(C.cast(arr, C.c_void_p), len(ops), world)
+            own = C.c_void_p()
+            hb = C.create_string_buffer(IPC_HANDLE_BYTES)
+            _call("ql_ipc_alloc", max(nbytes, 256), C.byref(own), hb)
+            self.own = own
+            handles = exchange_handles(bytes(hb.raw))
+            ptrs = (C.c_void_p * world)()
+            for r, hr in enumerate(handles):
+                if r == rank:
+                    ptrs[r] = own.value
+                else:
+                    m = C.c_void_p()
+                    _call("ql_ipc_open", hr, C.byref(m))
+                    self.mapped.append(m)
+                    ptrs[r] = m.value
+            _call("ql_gemv_chain_create_tp", C.cast(arr, C.c_void_p), len(ops), rank, world, C.cast(ptrs, C.c_void_p),
+                  C.byref(h))
         self.handle = h
 
     def run(self):
         _call("ql_gemv_chain_run", self.handle)
 
     def close(self):
+        """Release the chain; with world > 1 call it on every rank after a host barrier."""
         if self.handle:
             _call("ql_gemv_chain_destroy", self.handle)
             self.handle = None
+        for m in self.mapped:
+            _call("ql_ipc_close", m)
+        self.mapped = []
+        if self.own is not None:
+            _call("ql_ipc_free", self.own)
+            self.own = None
 
 
 def reserve_prefill(max_tokens, max_in_dim):

@@ -31,9 +31,11 @@ int set_last_error(int code, const char *msg);
 
 namespace {
 
-constexpr int kChainSlots = 2;                       // ring slots of two 32 x 7-block boxes each
-constexpr int kBox = kTmaSeg * 144 * kRowGroup;      // 32,256 B
+constexpr int kChainSlots = 2;                       // ring slots of two 32 x (<= 7)-block boxes each
+constexpr int kBox = kTmaSeg * 144 * kRowGroup;      // 32,256 B: the largest box
 constexpr int kSlotBytes = 2 * kBox;
+constexpr int kMaxWorld = 8;
+constexpr int kErrChainPeer = 6;                     // a peer's partial sums never arrived
 constexpr int kChainW = gemv_consumer_warps(true);   // 14 consumer warps
 constexpr int kChainRed = kChainW * 2 * kRowGroup;   // floats per reduction buffer (up to 2 matrices)
 constexpr int kErrChainBarrier = 5;
@@ -53,6 +55,9 @@ struct __align__(128) ChainOp {
     const float *bias;
     float *y;
     AmaxOut amax;
+    int bu;                // blocks per TMA box: min(7, U); a stage holds two boxes (one per matrix for SwiGLU)
+    int reduce;            // tensor parallel: y += (sum over ranks of this rank's W.x) through peer memory
+    long long xchg;        // first exchange cell of this op (reduce: [G][world][32]; argmax: [world][2])
 };
 
 struct ChainArgs {
@@ -64,12 +69,37 @@ struct ChainArgs {
     float *part;        // stream-K partial slots [C][2][2][32]
     unsigned *counters; // stream-K arrival counters (zero between ops)
     int *err;
+    unsigned long long *xchg[kMaxWorld];  // every rank's exchange cells (index = rank), mapped here
+    int rank, world;
 };
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+// Exchange cells: a 64-bit word (launch tag << 32 | payload), written and read whole
+// (aligned 64-bit accesses are single-copy atomic), so no fence orders payload and flag.
+__device__ __forceinline__ void st_cell(unsigned long long *p, unsigned tag, uint32_t payload) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(((unsigned long long)tag << 32) | payload)
+                 : "memory");
+}
+__device__ __forceinline__ bool ld_cell(const unsigned long long *p, unsigned tag, uint32_t *payload, int *err) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    if ((unsigned)(v >> 32) != tag) {
+        const uint64_t t0 = global_timer_ns();
+        do {
+            __nanosleep(64);
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+            if (global_timer_ns() - t0 > 5000000000ull) {
+                atomicExch(err, kErrChainPeer);
+                return false;
+            }
+        } while ((unsigned)(v >> 32) != tag);
+    }
+    *payload = (uint32_t)v;
+    return true;
 }
 __device__ __forceinline__ void tensormap_acquire(const void *map) {
     asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
@@ -112,7 +142,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    const unsigned target = (*epoch_s + 1u) * (unsigned)C;  // every op's counter after this launch
+    const unsigned tag = *epoch_s + 1u;                     // exchange-cell tag of this launch
+    const unsigned target = tag * (unsigned)C;             // every op's counter after this launch
 
     if (warp == 0) {
         // ---------------------------- producer (TMA) ----------------------------
@@ -121,7 +152,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
         for (int p = 0; p < a.nops; ++p) {
             const ChainOp &o = a.ops[p];
             for (int i = 0; i < (o.nmat == 2 ? 2 : 3); ++i) tensormap_acquire(&o.tmap[i]);
-            const int seg = 2 * kTmaSeg / o.nmat;
+            const int seg = 2 * o.bu / o.nmat;
+            const uint32_t kb = (uint32_t)o.bu * 144u * kRowGroup;
             int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
             const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
             Stage st;
@@ -135,19 +167,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                 uint8_t *sb = ring + (size_t)slot * kSlotBytes;
                 const int row0 = st.g * kRowGroup;
                 if (o.nmat == 2) {
-                    mbar_arrive_expect_tx(&full[slot], live ? 2u * kBox : 0u);
+                    mbar_arrive_expect_tx(&full[slot], live ? 2u * kb : 0u);
                     if (live) {
                         tma_load_3d(sb, &o.tmap[0], 0, st.us, row0, &full[slot]);
-                        tma_load_3d(sb + kBox, &o.tmap[1], 0, st.us, row0, &full[slot]);
+                        tma_load_3d(sb + kb, &o.tmap[1], 0, st.us, row0, &full[slot]);
                     }
                 } else {
                     const int src = (row0 >= o.split[0]) + (row0 >= o.split[1]);
                     const int lrow = row0 - (src == 0 ? 0 : o.split[src - 1]);
-                    const int nbox = st.ue - st.us > kTmaSeg ? 2 : 1;
-                    mbar_arrive_expect_tx(&full[slot], live ? (uint32_t)(nbox * kBox) : 0u);
+                    const int nbox = st.ue - st.us > o.bu ? 2 : 1;
+                    mbar_arrive_expect_tx(&full[slot], live ? (uint32_t)nbox * kb : 0u);
                     if (live) {
                         tma_load_3d(sb, &o.tmap[src], 0, st.us, lrow, &full[slot]);
-                        if (nbox == 2) tma_load_3d(sb + kBox, &o.tmap[src], 0, st.us + kTmaSeg, lrow, &full[slot]);
+                        if (nbox == 2) tma_load_3d(sb + kb, &o.tmap[src], 0, st.us + o.bu, lrow, &full[slot]);
                     }
                 }
                 ++it;
@@ -223,9 +255,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                         } else {
                             out = val[0] * nrm;
                             if (o.bias != nullptr) out += o.bias[v];
-                            if (o.kind == kOpAdd) __stcg(yp, __ldcg(yp) + out);  // residual written by other SMs
-                            else if (o.y != nullptr) *yp = out;
+                            if (o.kind == kOpAdd && !o.reduce) __stcg(yp, __ldcg(yp) + out);  // residual written by other SMs
+                            else if (o.kind != kOpAdd && o.y != nullptr) *yp = out;
                         }
+                    }
+                    if (o.reduce) {
+                        // tensor parallel: this rank's partial of the row group to every rank, then the
+                        // sum over ranks in rank order (bit-identical on every rank) onto the residual
+                        const size_t cell = (size_t)o.xchg + ((size_t)g * a.world + a.rank) * kRowGroup + lane;
+                        const uint32_t bits = __float_as_uint(v < o.rows ? out : 0.f);
+                        for (int d = 0; d < a.world; ++d) st_cell(a.xchg[d] + cell, tag, bits);
+                        float sum = 0.f;
+                        bool okp = true;
+                        for (int r = 0; r < a.world && okp; ++r) {
+                            uint32_t pb = 0;
+                            okp = ld_cell(a.xchg[a.rank] + (size_t)o.xchg + ((size_t)g * a.world + r) * kRowGroup + lane,
+                                          tag, &pb, a.err);
+                            sum += __uint_as_float(pb);
+                        }
+                        if (!__all_sync(0xffffffffu, okp)) *abort_flag = 1;
+                        else if (v < o.rows) __stcg(o.y + v, __ldcg(o.y + v) + sum);
                     }
                     if (o.kind == kOpStore && o.amax.amax != nullptr) {
                         unsigned long long k = v < o.rows ? amax_key(out, (uint32_t)(v + o.amax.offset)) : 0ull;
@@ -235,7 +284,36 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                 }
             }
             if (lane == 0) {
-                if (o.kind == kOpStore && o.amax.amax != nullptr) amax_cta_done(o.amax, 1);
+                if (o.kind == kOpStore && o.amax.amax != nullptr) {
+                    if (a.world == 1) {
+                        amax_cta_done(o.amax, 1);
+                    } else {
+                        // last CTA of this rank: local key -> every rank; the largest key over ranks wins
+                        __threadfence();
+                        const unsigned prev = atomicAdd(o.amax.done, 1u);
+                        if (prev == (unsigned)C - 1u) {
+                            __threadfence();
+                            const unsigned long long k = atomicExch(o.amax.amax, 0ull);
+                            atomicExch(o.amax.done, 0u);
+                            for (int d = 0; d < a.world; ++d) {
+                                st_cell(a.xchg[d] + o.xchg + 2 * a.rank, tag, (uint32_t)(k >> 32));
+                                st_cell(a.xchg[d] + o.xchg + 2 * a.rank + 1, tag, (uint32_t)k);
+                            }
+                            unsigned long long best = 0ull;
+                            for (int r = 0; r < a.world; ++r) {
+                                uint32_t hi = 0, lo = 0;
+                                if (!ld_cell(a.xchg[a.rank] + o.xchg + 2 * r, tag, &hi, a.err) ||
+                                    !ld_cell(a.xchg[a.rank] + o.xchg + 2 * r + 1, tag, &lo, a.err)) {
+                                    *abort_flag = 1;
+                                    break;
+                                }
+                                const unsigned long long kr = ((unsigned long long)hi << 32) | lo;
+                                best = kr > best ? kr : best;
+                            }
+                            if (o.amax.idx) o.amax.idx[0] = amax_index(best);
+                        }
+                    }
+                }
                 __threadfence();
                 const unsigned prev = atomicAdd(&a.done[p], 1u);  // this CTA's part of op p is written
                 if (p == a.nops - 1 && prev == target - 1u) atomicAdd(a.epoch, 1u);
@@ -323,7 +401,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
         }
 
         float acc[2][1] = {{0.f}, {0.f}};
-        const int seg = 2 * kTmaSeg / NM;
+        const int bu = o.bu, seg = 2 * bu / NM;
+        const int kb = bu * 144 * kRowGroup;
         int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
         const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
         Stage st;
@@ -337,18 +416,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             const int v = st.g * kRowGroup + lane;
             const bool aborted = *reinterpret_cast<volatile int *>(abort_flag) != 0;
             if (!aborted && v < o.rows) {
-                const uint8_t *sb = ring + (size_t)slot * kSlotBytes + (size_t)lane * (kTmaSeg * 144);
+                const uint8_t *sb = ring + (size_t)slot * kSlotBytes + (size_t)lane * (bu * 144);
                 const int first = ((cw - ucount) % W + W) % W;
                 for (int lu = first; lu < n; lu += W) {
                     const int k0 = (st.us + lu) * 256;
                     if (NM == 2) {
-                        const uint8_t *bp[2] = {sb + lu * 144, sb + kBox + lu * 144};
+                        const uint8_t *bp[2] = {sb + lu * 144, sb + kb + lu * 144};
                         float acc2[2][1] = {{acc[0][0]}, {acc[1][0]}};
                         unit_q4k<1, 2>(bp, xs, K, xsum, nblk, k0, acc2);
                         acc[0][0] = acc2[0][0];
                         acc[1][0] = acc2[1][0];
                     } else {
-                        const uint8_t *bp[1] = {sb + (lu / kTmaSeg) * kBox + (lu % kTmaSeg) * 144};
+                        const uint8_t *bp[1] = {sb + (lu / bu) * kb + (lu % bu) * 144};
                         float acc1[1][1] = {{acc[0][0]}};
                         unit_q4k<1, 1>(bp, xs, K, xsum, nblk, k0, acc1);
                         acc[0][0] = acc1[0][0];
@@ -383,7 +462,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
 using namespace ql;
 
 namespace ql {
-bool q4k_tensor_map_public(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes);
+bool q4k_tensor_map_public(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes,
+                           int box_blocks);
 int chain_workspace(float **part, unsigned **counters, int **err, int *sms);
 }
 
@@ -410,8 +490,21 @@ struct Chain {
 
 extern "C" {
 
-int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain) {
+// Exchange cells a tensor-parallel chain needs per rank (64-bit words).
+long long chain_cells(const ql_chain_op *ops, int nops, int world) {
+    long long n = 0;
+    for (int p = 0; p < nops; ++p) {
+        const ql_chain_op &q = ops[p];
+        if (q.kind == QL_OP_ADD && q.reduce) n += (long long)((q.rows[0] + kRowGroup - 1) / kRowGroup) * world * kRowGroup;
+        if (q.argmax_idx) n += 2LL * world;
+    }
+    return n;
+}
+
+int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *const *exchange, void **chain) {
     if (!ops || nops <= 0 || !chain) return set_last_error(QL_EINVAL, "ql_gemv_chain_create: need ops and nops > 0");
+    if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || (world > 1 && !exchange))
+        return set_last_error(QL_EINVAL, "ql_gemv_chain_create: bad rank/world or missing exchange buffers");
     float *part;
     unsigned *counters;
     int *err, sms;
@@ -432,7 +525,10 @@ int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain) {
         if (reinterpret_cast<uintptr_t>(q.x) % 16 || reinterpret_cast<uintptr_t>(q.gamma) % 16)
             return set_last_error(QL_EINVAL, (what + ": x and gamma must be 16-byte aligned").c_str());
         const int blocks = q.in_dim / 256;
-        if (blocks < kTmaSeg) return set_last_error(QL_EINVAL, (what + ": in_dim must be >= 1792").c_str());
+        o.bu = blocks < kTmaSeg ? blocks : kTmaSeg;
+        if (q.reduce && (q.kind != QL_OP_ADD || world < 2 || q.bias))
+            return set_last_error(QL_EINVAL, (what + ": reduce needs an ADD op without bias and world > 1").c_str());
+        o.reduce = q.reduce ? 1 : 0;
         int total = 0;
         for (int s = 0; s < nsrc; ++s) {
             if (!q.w[s] || reinterpret_cast<uintptr_t>(q.w[s]) % 16 || q.row_bytes[s] % 16 ||
@@ -440,7 +536,7 @@ int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain) {
                 return set_last_error(QL_EINVAL, (what + ": weights (16-byte aligned, >= 32 rows)").c_str());
             if (q.kind != QL_OP_SWIGLU && s < nsrc - 1 && q.rows[s] % kRowGroup)
                 return set_last_error(QL_EINVAL, (what + ": stacked sources but the last need multiples of 32 rows").c_str());
-            if (!q4k_tensor_map_public(&o.tmap[s], q.w[s], blocks, (uint64_t)q.rows[s], q.row_bytes[s]))
+            if (!q4k_tensor_map_public(&o.tmap[s], q.w[s], blocks, (uint64_t)q.rows[s], q.row_bytes[s], o.bu))
                 return set_last_error(QL_ECUDA, (what + ": tensor map").c_str());
             if (q.kind != QL_OP_SWIGLU) {
                 total += q.rows[s];
@@ -477,6 +573,15 @@ int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain) {
             o.amax.offset = q.argmax_offset;
         }
         if (q.in_dim > kmax) kmax = q.in_dim;
+    }
+    // exchange cells (tensor parallel): reduce ops [G][world][32], argmax ops [world][2]
+    {
+        long long cell = 0;
+        for (int p = 0; p < nops; ++p) {
+            h[p].xchg = cell;
+            if (h[p].reduce) cell += (long long)h[p].plan.G * world * kRowGroup;
+            if (ops[p].argmax_idx && world > 1) cell += 2LL * world;
+        }
     }
     Chain *c = new Chain();
     c->sms = sms;
@@ -523,8 +628,26 @@ int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain) {
     c->args.part = part;
     c->args.counters = counters;
     c->args.err = err;
+    c->args.rank = rank;
+    c->args.world = world;
+    for (int r = 0; r < world; ++r)
+        c->args.xchg[r] = world > 1 ? static_cast<unsigned long long *>(exchange[r]) : nullptr;
     *chain = c;
     return QL_OK;
+}
+
+int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain) {
+    return chain_create(ops, nops, 0, 1, nullptr, chain);
+}
+
+size_t ql_gemv_chain_exchange_bytes(const ql_chain_op *ops, int nops, int world) {
+    if (!ops || nops <= 0 || world < 1 || world > kMaxWorld) return 0;
+    return (size_t)chain_cells(ops, nops, world) * sizeof(unsigned long long);
+}
+
+int ql_gemv_chain_create_tp(const ql_chain_op *ops, int nops, int rank, int world, void *const *exchange,
+                            void **chain) {
+    return chain_create(ops, nops, rank, world, exchange, chain);
 }
 
 int ql_gemv_chain_run(void *chain) {

@@ -131,6 +131,42 @@ using namespace ql;
 
 extern "C" {
 
+int ql_ipc_alloc(size_t bytes, void **ptr, uint8_t *handle) {
+    if (!ptr || !handle || bytes == 0) return set_last_error(QL_EINVAL, "ql_ipc_alloc: need bytes > 0 and outputs");
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return set_last_error(QL_ECUDA, (std::string("ql_ipc_alloc: ") + cudaGetErrorString(e)).c_str());
+    }
+    memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return QL_OK;
+}
+
+int ql_ipc_free(void *ptr) {
+    if (ptr) cudaFree(ptr);
+    return QL_OK;
+}
+
+int ql_ipc_open(const uint8_t *handle, void **ptr) {
+    if (!handle || !ptr) return set_last_error(QL_EINVAL, "ql_ipc_open: null handle or output");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return set_last_error(QL_ECUDA, (std::string("ql_ipc_open: ") + cudaGetErrorString(e)).c_str());
+    return QL_OK;
+}
+
+int ql_ipc_close(void *ptr) {
+    if (ptr) cudaIpcCloseMemHandle(ptr);
+    return QL_OK;
+}
+
 size_t ql_comm_bytes(int world, int max_floats, int slots) {
     if (world < 1 || world > kMaxWorld || max_floats < 1 || slots < 1) return 0;
     return comm_bytes(world, max_floats, slots);

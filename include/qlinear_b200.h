@@ -130,8 +130,25 @@ typedef struct ql_chain_op {
     float *y;
     int *argmax_idx;
     int32_t argmax_offset;
+    int32_t reduce; /* tensor parallel ADD: y += sum over ranks of this op's partial (no bias) */
 } ql_chain_op;
 QL_API int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain);
+/* Tensor-parallel chain: ops with reduce != 0 (row-parallel ADD projections) sum their
+ * partials over ranks inside the kernel through peer memory (each rank's exchange buffer,
+ * ql_gemv_chain_exchange_bytes bytes, zeroed, mapped into every rank: exchange[r] for
+ * rank r, e.g. with ql_ipc_alloc / ql_ipc_open); an argmax op (vocabulary shard with
+ * argmax_offset) combines the ranks' keys the same way.  Every rank must create and run
+ * the same chain; a rank that never arrives makes the others give up after ~5 s with an
+ * error in the device error word. */
+QL_API size_t ql_gemv_chain_exchange_bytes(const ql_chain_op *ops, int nops, int world);
+QL_API int ql_gemv_chain_create_tp(const ql_chain_op *ops, int nops, int rank, int world, void *const *exchange,
+                                   void **chain);
+/* Device allocation shareable with other processes (zeroed), its CUDA IPC handle, and the
+ * peer side: map / unmap another process's allocation. */
+QL_API int ql_ipc_alloc(size_t bytes, void **ptr, uint8_t *handle);
+QL_API int ql_ipc_free(void *ptr);
+QL_API int ql_ipc_open(const uint8_t *handle, void **ptr);
+QL_API int ql_ipc_close(void *ptr);
 QL_API int ql_gemv_chain_run(void *chain);
 QL_API int ql_gemv_chain_destroy(void *chain);
 
