@@ -57,6 +57,7 @@ struct __align__(128) ChainOp {
     AmaxOut amax;
     int bu;                // blocks per TMA box: min(7, U); a stage holds two boxes (one per matrix for SwiGLU)
     int reduce;            // tensor parallel: y += (sum over ranks of this rank's W.x) through peer memory
+    int pre_y;             // ADD: y's last writer is at least two ops back, so y may be read early
     long long xchg;        // first exchange cell of this op (reduce: [G][world][32]; argmax: [world][2])
 };
 
@@ -201,6 +202,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             for (int64_t gg = t0 / U; gg * U < t1; ++gg, ++gi) {
                 const int g = (int)gg;
                 const int bsel = gi & 1;
+                // loads the epilogue needs, issued before waiting for the consumers: the bias, and the
+                // residual when its last writer finished before op p-1 started (o.pre_y)
+                const int vv = g * kRowGroup + lane;
+                if (o.pre_y && p >= 2 && lane == 0 && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                    // a CTA with no row group in op p-1 gets here without having waited for op p-2
+                    const unsigned *d2 = a.done + (p - 2);
+                    const uint64_t tw = global_timer_ns();
+                    while (ld_acquire_gpu(d2) < target) {
+                        if (global_timer_ns() - tw > 2000000000ull) {
+                            atomicExch(a.err, kErrChainBarrier);
+                            *abort_flag = 1;
+                            break;
+                        }
+                    }
+                }
+                __syncwarp();
+                const float bias_v = (o.bias != nullptr && vv < o.rows) ? o.bias[vv] : 0.f;
+                const float res_v = (o.kind == kOpAdd && o.pre_y && vv < o.rows) ? __ldcg(o.y + vv) : 0.f;
                 bool ok = !*reinterpret_cast<volatile int *>(abort_flag);
                 if (ok && !mbar_wait(&red_full[bsel], (uint32_t)(gi >> 1) & 1u, a.err, kErrWaitFull)) {
                     *abort_flag = 1;
@@ -254,8 +273,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                             *yp = out;
                         } else {
                             out = val[0] * nrm;
-                            if (o.bias != nullptr) out += o.bias[v];
-                            if (o.kind == kOpAdd && !o.reduce) __stcg(yp, __ldcg(yp) + out);  // residual written by other SMs
+                            if (o.bias != nullptr) out += bias_v;
+                            if (o.kind == kOpAdd && !o.reduce)  // residual written by other SMs: L2, not L1
+                                __stcg(yp, (o.pre_y ? res_v : __ldcg(yp)) + out);
                             else if (o.kind != kOpAdd && o.y != nullptr) *yp = out;
                         }
                     }
@@ -274,7 +294,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                             sum += __uint_as_float(pb);
                         }
                         if (!__all_sync(0xffffffffu, okp)) *abort_flag = 1;
-                        else if (v < o.rows) __stcg(o.y + v, __ldcg(o.y + v) + sum);
+                        else if (v < o.rows) __stcg(o.y + v, (o.pre_y ? res_v : __ldcg(o.y + v)) + sum);
                     }
                     if (o.kind == kOpStore && o.amax.amax != nullptr) {
                         unsigned long long k = v < o.rows ? amax_key(out, (uint32_t)(v + o.amax.offset)) : 0ull;
@@ -331,6 +351,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
     for (int p = 0; p < a.nops; ++p) {
         const ChainOp &o = a.ops[p];
         const int K = o.K, nblk = K / 32, U = o.U, NM = o.nmat;
+        // the RMSNorm weight does not depend on earlier ops: pull it into L2 while waiting
+        if (o.gamma != nullptr)
+            for (int i = ctid * 32; i < K; i += nthr * 32)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(o.gamma + i));
         // grid barrier: op p reads what op p-1 wrote
         if (p > 0) {
             if (ctid == 0 && !*reinterpret_cast<volatile int *>(abort_flag)) {
@@ -573,6 +597,14 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
             o.amax.offset = q.argmax_offset;
         }
         if (q.in_dim > kmax) kmax = q.in_dim;
+    }
+    // ADD ops may read their residual before op p-1 completes when no op since p-2 wrote it
+    for (int p = 0; p < nops; ++p) {
+        ChainOp &o = h[p];
+        o.pre_y = 0;
+        if (o.kind != kOpAdd) continue;
+        const bool prev_writes = p > 0 && h[p - 1].y && h[p - 1].y < o.y + o.rows && o.y < h[p - 1].y + h[p - 1].rows;
+        o.pre_y = prev_writes ? 0 : 1;
     }
     // exchange cells (tensor parallel): reduce ops [G][world][32], argmax ops [world][2]
     {

@@ -203,6 +203,15 @@ __device__ __forceinline__ void amax_cta_done(const AmaxOut &o, int M) {
     }
 }
 
+// Packed fp32x2 multiply (sm_100).
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    unsigned long long c;
+    const unsigned long long x = *reinterpret_cast<unsigned long long *>(&a);
+    const unsigned long long y = *reinterpret_cast<unsigned long long *>(&b);
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(c) : "l"(x), "l"(y));
+    return *reinterpret_cast<float2 *>(&c);
+}
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)));
 }

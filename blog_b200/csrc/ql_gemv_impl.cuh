@@ -27,14 +27,40 @@ __device__ __forceinline__ float dn(uint32_t bits) { return __uint_as_float(bits
 // Unit decoders: one GGUF block of one row (this lane) of each of NMAT matrices
 // (gate and up share the activation, which is loaded once), against MT tokens.
 // ----------------------------------------------------------------------------
+// Two bytes of a packed word -> the pair of floats (exact: byte | 2^23 bit pattern, minus 2^23).
+__device__ __forceinline__ float2 byte_pair_f(uint32_t w, int b0) {
+    const float2 t = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + b0)),
+                                 __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + b0 + 1)));
+    return fadd2(t, make_float2(-8388608.0f, -8388608.0f));
+}
+
 template <int MT, int NMAT>
 __device__ __forceinline__ void unit_q4k(const uint8_t *const (&blk)[NMAT], const float *xs, int K, const float *xsum,
                                          int nblk, int k0, float (&acc)[NMAT][MT]) {
-    uint4 h[NMAT];
+    // Per matrix, once per block: d, dmin and the eight 6-bit scales / mins (q4k_scale_min,
+    // reference kernel.cu:913-921) as packed bytes: sub-blocks 0-3 in sc03/m03, 4-7 in sc47/m47.
+    float2 d2[NMAT], dm2[NMAT];
+    uint32_t scw[NMAT][2], mw[NMAT][2];
 #pragma unroll
-    for (int mat = 0; mat < NMAT; ++mat) h[mat] = *reinterpret_cast<const uint4 *>(blk[mat]);
+    for (int mat = 0; mat < NMAT; ++mat) {
+        const uint4 h = *reinterpret_cast<const uint4 *>(blk[mat]);
+        const float d = half_bits_to_float(h.x) * pow2f(53), dmin = half_bits_to_float(h.x >> 16);
+        d2[mat] = make_float2(d, d);
+        dm2[mat] = make_float2(dmin, dmin);
+        scw[mat][0] = h.y & 0x3F3F3F3Fu;
+        mw[mat][0] = h.z & 0x3F3F3F3Fu;
+        scw[mat][1] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+        mw[mat][1] = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    }
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
+        // sub-blocks 2p, 2p+1: D = d*sc, M = dmin*m (packed multiplies, the same products as scalar ones)
+        float2 D[NMAT], Mn[NMAT];
+#pragma unroll
+        for (int mat = 0; mat < NMAT; ++mat) {
+            D[mat] = fmul2(d2[mat], byte_pair_f(scw[mat][p >> 1], 2 * (p & 1)));
+            Mn[mat] = fmul2(dm2[mat], byte_pair_f(mw[mat][p >> 1], 2 * (p & 1)));
+        }
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
             float4 xl[8], xh[8];
@@ -48,30 +74,11 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *const (&blk)[NMAT], cons
             const float X1 = xsum[(size_t)m * nblk + (k0 >> 5) + 2 * p + 1];
 #pragma unroll
             for (int mat = 0; mat < NMAT; ++mat) {
-                const float d = half_bits_to_float(h[mat].x) * pow2f(53);
-                const float dmin = half_bits_to_float(h[mat].x >> 16);
-                const uint32_t sA = h[mat].y, sB = h[mat].z, sC = h[mat].w;  // scale bytes 0-3, 4-7, 8-11
-                // q4k_scale_min (reference kernel.cu:913-921) for sub-blocks 2p and 2p+1
-                uint32_t sc0, m0, sc1, m1;
-                if (p < 2) {
-                    sc0 = (sA >> (16 * p)) & 63u;
-                    m0 = (sB >> (16 * p)) & 63u;
-                    sc1 = (sA >> (16 * p + 8)) & 63u;
-                    m1 = (sB >> (16 * p + 8)) & 63u;
-                } else {
-                    const int j0 = 2 * p - 4, j1 = 2 * p - 3;
-                    sc0 = ((sC >> (8 * j0)) & 0x0Fu) | (((sA >> (8 * j0 + 6)) & 3u) << 4);
-                    m0 = ((sC >> (8 * j0 + 4)) & 0x0Fu) | (((sB >> (8 * j0 + 6)) & 3u) << 4);
-                    sc1 = ((sC >> (8 * j1)) & 0x0Fu) | (((sA >> (8 * j1 + 6)) & 3u) << 4);
-                    m1 = ((sC >> (8 * j1 + 4)) & 0x0Fu) | (((sB >> (8 * j1 + 6)) & 3u) << 4);
-                }
-                const float D0 = d * (float)sc0, D1 = d * (float)sc1;
-                const float M0 = dmin * (float)m0, M1 = dmin * (float)m1;
+                // Two packed accumulators (fma.rn.f32x2): a = sub-block 2p, b = 2p+1;
+                // each lane of a pair sums every other element, as two scalar chains would.
                 const uint4 qa = *reinterpret_cast<const uint4 *>(blk[mat] + 16 + 32 * p);
                 const uint4 qb = *reinterpret_cast<const uint4 *>(blk[mat] + 32 + 32 * p);
                 const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                // Two packed accumulators (fma.rn.f32x2): a = sub-block 2p, b = 2p+1;
-                // each lane of a pair sums every other element, as two scalar chains would.
                 float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -82,10 +89,10 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *const (&blk)[NMAT], cons
                     ffma2(b, make_float2(dn(w2 & 0x00000F00u), dn(w2 & 0x000F0000u)), make_float2(xh[i].z, xh[i].w));
                 }
                 float r = acc[mat][m];
-                r = fmaf(D0, a.x + a.y, r);
-                r = fmaf(D1, b.x + b.y, r);
-                r = fmaf(-M0, X0, r);
-                r = fmaf(-M1, X1, r);
+                r = fmaf(D[mat].x, a.x + a.y, r);
+                r = fmaf(D[mat].y, b.x + b.y, r);
+                r = fmaf(-Mn[mat].x, X0, r);
+                r = fmaf(-Mn[mat].y, X1, r);
                 acc[mat][m] = r;
             }
         }
