@@ -374,6 +374,37 @@ def run_prefill_kernel(args):
     return 0
 
 
+def run_chain_kernel(args):
+    """Times the persistent chain launch (batch 1, one GPU) on a stack of --layers decoder
+    layers + LM head: the ncu target for the decode step (fewer layers keep the capture small)."""
+    global LAYERS
+    import torch
+    import blog_b200 as Q
+    LAYERS = args.layers
+    torch.cuda.init()
+    Q.init(0)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        Q.set_stream(s.cuda_stream)
+        st = DecodeStack(Q, torch, 0, 1, 1)
+        for _ in range(args.warmup):
+            st.step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            st.step()
+        e1.record(s)
+        torch.cuda.synchronize()
+    Q.check_device()
+    us = e0.elapsed_time(e1) * 1000 / args.steps
+    wb = st.weight_bytes()
+    print(json.dumps({"kernel_only": "chain", "layers": LAYERS, "avg_us": us, "weight_bytes": wb,
+                      "act_bytes": st.chain_act_bytes(), "GBps": wb / us / 1e3, "launches": args.steps}), flush=True)
+    st.chain.close()
+    return 0
+
+
 def run_kernel_only(args):
     """Times one kernel of the step at its bench shape (the ncu profiling target):
     swiglu = fused RMSNorm + gate/up SwiGLU (18944 x 3584 x 2), down = down + residual
@@ -382,6 +413,8 @@ def run_kernel_only(args):
     import blog_b200 as Q
     if args.kernel_only.startswith("prefill_"):
         return run_prefill_kernel(args)
+    if args.kernel_only == "chain":
+        return run_chain_kernel(args)
     torch.cuda.init()
     Q.init(0)
     Q.set_stream(torch.cuda.current_stream().cuda_stream)
@@ -467,10 +500,13 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch32", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
-                                              "prefill_qkv", "prefill_o"],
+                                              "prefill_qkv", "prefill_o", "chain"],
                     help="time one kernel of the step at its bench shape (profiling target)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers for --kernel-only chain")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -564,8 +600,79 @@ def main():
         torch.cuda.empty_cache()
         return res
 
+    def measure_prefill(T):
+        """Prefill of a T-token prompt through the stack's linears on the tcgen05 path: per layer
+        the stacked q/k/v GEMM (+RMSNorm, bias), o (+residual), gate/up SwiGLU (+RMSNorm), down
+        (+residual), then the LM head with the greedy argmax on the last token (GEMV).  Timed as a
+        CUDA graph with events; returns ms and the linear FLOPs."""
+        stack = DecodeStack(Q, torch, rank, world, 1)
+        qkv_w = stack.qkv_w
+        x = torch.randn((T, HIDDEN), generator=torch.Generator().manual_seed(7)).to("cuda")
+        h = torch.empty((T, HIDDEN), device="cuda")
+        qkv = torch.empty((T, qkv_w), device="cuda")
+        act = torch.empty((T, max(stack.f_len, 1)), device="cuda")
+        tok = torch.zeros((1,), dtype=torch.int32, device="cuda")
+        Q.reserve_prefill(T, max(HIDDEN, stack.f_len, stack.qo_len))
+        rbh = Q.row_bytes(QK, HIDDEN)
+        s = torch.cuda.Stream()
+
+        def run():
+            Q.set_stream(torch.cuda.current_stream().cuda_stream)
+            h.copy_(x)
+            for L in stack.layers:
+                Q.quant_gemv_stacked_ex(QK, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
+                                        [stack.qo_len, stack.kv_len, stack.kv_len], h.data_ptr(), HIDDEN,
+                                        qkv.data_ptr(), qkv_w, HIDDEN, T, L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr())
+                Q.quant_gemv_ex(QK, L["wo"].data_ptr(), Q.row_bytes(QK, stack.qo_len), qkv.data_ptr(), qkv_w,
+                                h.data_ptr(), HIDDEN, HIDDEN, stack.qo_len, T, accumulate=(rank == 0))
+                if world > 1:
+                    torch.distributed.all_reduce(h)
+                Q.quant_swiglu_ex(QK, L["wg"].data_ptr(), L["wu"].data_ptr(), rbh, rbh, h.data_ptr(), HIDDEN,
+                                  act.data_ptr(), act.shape[1], stack.f_len, HIDDEN, T, L["ln2"].data_ptr(), EPS)
+                Q.quant_gemv_ex(QK, L["wd"].data_ptr(), Q.row_bytes(QK, stack.f_len), act.data_ptr(), act.shape[1],
+                                h.data_ptr(), HIDDEN, HIDDEN, stack.f_len, T, accumulate=(rank == 0))
+                if world > 1:
+                    torch.distributed.all_reduce(h)
+            Q.quant_gemv_argmax_ex(QK, stack.wlm.data_ptr(), rbh, h[T - 1:].data_ptr(), HIDDEN, None, 0, stack.v_len,
+                                   HIDDEN, 1, stack.lnf.data_ptr(), EPS, stack.v_off, tok.data_ptr(), None)
+        with torch.cuda.stream(s):
+            run()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                run()
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+            if world > 1:
+                torch.distributed.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 3
+            e0.record(s)
+            for _ in range(reps):
+                g.replay()
+            e1.record(s)
+            torch.cuda.synchronize()
+        Q.check_device()
+        ms = e0.elapsed_time(e1) / reps
+        t = torch.tensor([ms], device="cuda")
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        per_layer = HIDDEN * (stack.qo_len + 2 * stack.kv_len) + stack.qo_len * HIDDEN + 3 * HIDDEN * stack.f_len
+        flops = 2.0 * T * per_layer * LAYERS * world + 2.0 * stack.v_len * HIDDEN * world
+        del g
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        if stack.chain is not None:
+            stack.chain.close()
+        del stack
+        torch.cuda.empty_cache()
+        return {"ms": float(t[0]), "flops": flops}
+
     r1 = measure(args.batch)
     r32 = None if args.no_batch32 else measure(32)
+    rp = None if args.no_prefill else measure_prefill(args.prefill_tokens)
 
     if rank == 0:
         hbm, peak_kind = peaks()
@@ -603,6 +710,16 @@ def main():
         if r32 is not None:
             line["batch32"] = {"value": 32 / (r32["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r32["ms"],
                                "e2e_tokens_per_s": 32 / (r32["e2e_ms"] / 1e3)}
+        if rp is not None:
+            tf = rp["flops"] / (rp["ms"] / 1e3) / 1e12
+            pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+                os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+            sus = float(pk.get("bf16_tflops_sustained", 1390.3)) * world
+            line["prefill"] = {"tokens": args.prefill_tokens, "value": args.prefill_tokens / (rp["ms"] / 1e3),
+                               "unit": "tokens/s", "ms": rp["ms"], "tflops": tf,
+                               "tensor_frac_of_sustained_bf16": tf / sus,
+                               "path": "tcgen05 f16 x f16 -> f32 GEMM, Q4_K dequantized into shared memory",
+                               "tensor_pipe_active": "see profiles/gemm_q4k_prefill_2048x18944x3584.md"}
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_oracle_rate()
             cb.pop("seconds_per_sample", None)
