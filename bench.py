@@ -465,6 +465,183 @@ def run_kernel_only(args):
     return 0
 
 
+# --------------------------------------------------------------------------------------
+# DeepSeek-V2-Lite-style MoE decode, expert parallel over the ranks.
+DS_H, DS_LAYERS, DS_E, DS_TOPK, DS_FE, DS_SHARED, DS_DENSE, DS_VOCAB = 2048, 27, 64, 6, 1408, 2816, 10944, 102400
+Q50 = 6  # Q5_0: the routed experts' down projection (K = 1408 is not a multiple of 256)
+
+
+class MoEStack:
+    """The linears of a DeepSeek-V2-Lite-shape decoder for one rank of an expert-parallel
+    group: MLA projections (q 3072x2048, kv_a 576x2048, kv_b 4096x512, o 2048x2048) stand in
+    for attention, layer 0 has a dense SwiGLU FFN (10944), layers 1..26 a softmax top-6 router
+    over 64 routed experts (gate/up Q4_K, down Q5_0) plus 2 shared experts (2816).  Rank r owns
+    experts [r*64/W, (r+1)*64/W); a route to another rank's expert is passed as id -1 (skipped),
+    the routed partial sums are combined by one all-reduce per layer, and the shared experts and
+    the LM head run on every rank (only rank 0 adds the shared output before the all-reduce)."""
+
+    def __init__(self, Q, torch, rank, world, T, layers=DS_LAYERS, seed=0):
+        self.Q, self.torch, self.rank, self.world, self.T, self.nl = Q, torch, rank, world, T, layers
+        self.e0, self.e1 = rank * DS_E // world, (rank + 1) * DS_E // world
+        ne = self.e1 - self.e0
+        rb = lambda t, k: Q.row_bytes(t, k)
+
+        def synth(t, rows, k, tag):
+            w = torch.empty((rows, rb(t, k)), dtype=torch.uint8, device="cuda")
+            Q.synth_quantized(t, seed * 1000003 + tag, rows, k, 0.02, w.data_ptr())
+            return w
+        def experts(t, rows, k, tag):  # this rank's experts, each seeded by its global id (same bytes at any W)
+            w = torch.empty((ne * rows, rb(t, k)), dtype=torch.uint8, device="cuda")
+            for i in range(ne):
+                Q.synth_quantized(t, seed * 1000003 + tag * 131 + (self.e0 + i) * 7, rows, k, 0.02,
+                                  w[i * rows:(i + 1) * rows].data_ptr())
+            return w
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        norm = lambda: (1.0 + 0.1 * torch.randn(DS_H, generator=g)).to("cuda")
+        self.layers = []
+        for l in range(layers):
+            L = {"wq": synth(QK, 3072, DS_H, 100 * l + 1), "wkva": synth(QK, 576, DS_H, 100 * l + 2),
+                 "wkvb": synth(QK, 4096, 512, 100 * l + 3), "wo": synth(QK, DS_H, DS_H, 100 * l + 4),
+                 "ln1": norm(), "ln2": norm()}
+            if l == 0:
+                L["wg"], L["wu"] = synth(QK, DS_DENSE, DS_H, 100 * l + 5), synth(QK, DS_DENSE, DS_H, 100 * l + 6)
+                L["wd"] = synth(Q50, DS_H, DS_DENSE, 100 * l + 7)
+            else:
+                L["wr"] = synth(QK, DS_E, DS_H, 100 * l + 8)
+                # this rank's experts only: [ne * 1408, 2048] gate/up, [ne * 2048, 1408] down, packed per expert
+                L["eg"] = experts(QK, DS_FE, DS_H, 100 * l + 9)
+                L["eu"] = experts(QK, DS_FE, DS_H, 100 * l + 10)
+                L["ed"] = experts(Q50, DS_H, DS_FE, 100 * l + 11)
+                L["sg"], L["su"] = synth(QK, DS_SHARED, DS_H, 100 * l + 12), synth(QK, DS_SHARED, DS_H, 100 * l + 13)
+                L["sd"] = synth(QK, DS_H, DS_SHARED, 100 * l + 14)
+            self.layers.append(L)
+        self.wlm = synth(QK, DS_VOCAB, DS_H, 999)
+        self.lnf = norm()
+        self.h_in = torch.randn((T, DS_H), generator=g).to("cuda")
+        self.h = torch.zeros((T, DS_H), device="cuda")
+        self.xn = torch.zeros((T, DS_H), device="cuda")
+        self.q = torch.zeros((T, 3072), device="cuda")
+        self.kva = torch.zeros((T, 576), device="cuda")
+        self.kvb = torch.zeros((T, 4096), device="cuda")
+        self.act = torch.zeros((T, max(DS_DENSE, DS_SHARED)), device="cuda")
+        self.eact = torch.zeros((T, DS_TOPK, DS_FE), device="cuda")
+        self.logits = torch.zeros((T, DS_E), device="cuda")
+        self.idx = torch.zeros((T, DS_TOPK), dtype=torch.int32, device="cuda")
+        self.ids = torch.zeros((T, DS_TOPK), dtype=torch.int32, device="cuda")
+        self.rw = torch.zeros((T, DS_TOPK), device="cuda")
+        self.moe = torch.zeros((T, DS_H), device="cuda")
+        self.tok = torch.zeros((T,), dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+
+    def weight_bytes(self):
+        return sum(w.numel() for L in self.layers for k, w in L.items() if k[0] in "wes") + self.wlm.numel()
+
+    def routed(self, L):
+        """Routed experts of one layer on this rank: ids outside the shard become -1."""
+        Q, torch, T = self.Q, self.torch, self.T
+        Q.moe_router_topk(self.logits.data_ptr(), self.idx.data_ptr(), self.rw.data_ptr(), T, DS_E, DS_TOPK, 1.0)
+        loc = self.idx - self.e0
+        self.ids.copy_(torch.where((self.idx >= self.e0) & (self.idx < self.e1), loc, torch.full_like(loc, -1)))
+        rbg, rbd = Q.row_bytes(QK, DS_H), Q.row_bytes(Q50, DS_FE)
+        for t in range(T):
+            Q.quant_swiglu_indexed(QK, L["eg"].data_ptr(), L["eu"].data_ptr(), DS_FE * rbg, DS_FE * rbg, rbg, rbg,
+                                   self.xn[t].data_ptr(), self.ids[t].data_ptr(), self.eact[t].data_ptr(), DS_TOPK,
+                                   DS_FE, DS_H)
+            Q.quant_down_f32_indexed_accum_ordered(Q50, L["ed"].data_ptr(), DS_H * rbd, rbd, self.eact[t].data_ptr(),
+                                                    self.ids[t].data_ptr(), self.rw[t].data_ptr(),
+                                                    self.moe[t].data_ptr(), DS_TOPK, DS_H, DS_FE)
+
+    def step(self):
+        Q, torch, T = self.Q, self.torch, self.T
+        Q.set_stream(torch.cuda.current_stream().cuda_stream)
+        rbh = Q.row_bytes(QK, DS_H)
+        self.h.copy_(self.h_in)
+        h = self.h.data_ptr()
+        for li, L in enumerate(self.layers):
+            # attention stand-in: the MLA projections (fused RMSNorm on q and kv_a)
+            Q.quant_gemv_ex(QK, L["wq"].data_ptr(), rbh, h, DS_H, self.q.data_ptr(), 3072, 3072, DS_H, T,
+                            L["ln1"].data_ptr(), EPS)
+            Q.quant_gemv_ex(QK, L["wkva"].data_ptr(), rbh, h, DS_H, self.kva.data_ptr(), 576, 576, DS_H, T,
+                            L["ln1"].data_ptr(), EPS)
+            Q.quant_gemv_ex(QK, L["wkvb"].data_ptr(), Q.row_bytes(QK, 512), self.kva.data_ptr(), 576,
+                            self.kvb.data_ptr(), 4096, 4096, 512, T)
+            Q.quant_gemv_ex(QK, L["wo"].data_ptr(), rbh, self.q.data_ptr(), 3072, h, DS_H, DS_H, DS_H, T,
+                            accumulate=True)
+            if li == 0:
+                Q.quant_swiglu_ex(QK, L["wg"].data_ptr(), L["wu"].data_ptr(), rbh, rbh, h, DS_H, self.act.data_ptr(),
+                                  self.act.shape[1], DS_DENSE, DS_H, T, L["ln2"].data_ptr(), EPS)
+                Q.quant_gemv_ex(Q50, L["wd"].data_ptr(), Q.row_bytes(Q50, DS_DENSE), self.act.data_ptr(),
+                                self.act.shape[1], h, DS_H, DS_H, DS_DENSE, T, accumulate=True)
+                continue
+            Q.rms_norm_f32(h, self.xn.data_ptr(), L["ln2"].data_ptr(), T, DS_H, EPS)
+            Q.quant_gemv_ex(QK, L["wr"].data_ptr(), rbh, self.xn.data_ptr(), DS_H, self.logits.data_ptr(), DS_E,
+                            DS_E, DS_H, T)
+            self.moe.zero_()
+            self.routed(L)
+            if self.rank == 0:  # shared experts, once over the group
+                Q.quant_swiglu_ex(QK, L["sg"].data_ptr(), L["su"].data_ptr(), rbh, rbh, self.xn.data_ptr(), DS_H,
+                                  self.act.data_ptr(), self.act.shape[1], DS_SHARED, DS_H, T)
+                Q.quant_gemv_ex(QK, L["sd"].data_ptr(), Q.row_bytes(QK, DS_SHARED), self.act.data_ptr(),
+                                self.act.shape[1], self.moe.data_ptr(), DS_H, DS_H, DS_SHARED, T, accumulate=True)
+            if self.world > 1:
+                torch.distributed.all_reduce(self.moe)
+            self.h.add_(self.moe)
+        Q.quant_gemv_argmax_ex(QK, self.wlm.data_ptr(), rbh, h, DS_H, None, 0, DS_VOCAB, DS_H, T,
+                               self.lnf.data_ptr(), EPS, 0, self.tok.data_ptr(), None)
+
+
+def run_moe(args):
+    """--moe: batch-64 decode steps of the MoE stack, expert parallel over the ranks (one JSON line)."""
+    import datetime
+    import torch
+    import blog_b200 as Q
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                             timeout=datetime.timedelta(seconds=120))
+    Q.init(local)
+    T = 64
+    st = MoEStack(Q, torch, rank, world, T)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        st.step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            st.step()
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+    Q.check_device()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t[0])
+    if rank == 0:
+        print(json.dumps({"metric": "moe decode tokens/s (DeepSeek-V2-Lite shapes, batch 64)", "value": T / (ms / 1e3),
+                          "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "ms_per_step": ms,
+                          "parallelism": f"ep{world}", "weight_bytes_per_rank": st.weight_bytes(),
+                          "routed_path": "per-token indexed gather (SwiGLU) and ordered scatter (down) launches",
+                          "data": "synthetic"}), flush=True)
+    del g
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
 def run_reference(args):
     """--impl reference: the CPU restatement of the reference's arithmetic (the
     reference's only implementation of this path is CUDA; it has no CPU path)."""
@@ -501,6 +678,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch32", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--moe", action="store_true", help="DeepSeek-V2-Lite-shape MoE decode, expert parallel")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
                                               "prefill_qkv", "prefill_o", "chain"],
@@ -512,6 +690,8 @@ def main():
         return run_reference(args)
     if args.kernel_only:
         return run_kernel_only(args)
+    if args.moe:
+        return run_moe(args)
     args.warmup = max(args.warmup, 3)
 
     import torch

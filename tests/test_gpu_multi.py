@@ -201,3 +201,68 @@ def test_tensor_parallel_chain_matches_single_gpu(world):
         p.join(timeout=60)
     for rank, ok, info in out:
         assert ok, (rank, info)
+
+
+def _ep_worker(rank, world, port, q):
+    import datetime
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import blog_b200 as Q
+    try:
+        import bench
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        Q.init(rank)
+        Q.set_stream(torch.cuda.current_stream().cuda_stream)
+        # two layers: the dense layer 0 and one MoE layer, batch 8
+        st = bench.MoEStack(Q, torch, rank, world, 8, layers=2)
+
+        def moe_layer(stk):
+            L = stk.layers[1]
+            stk.xn.copy_(torch.randn(stk.xn.shape, generator=torch.Generator().manual_seed(3)).to("cuda"))
+            Q.quant_gemv_ex(bench.QK, L["wr"].data_ptr(), Q.row_bytes(bench.QK, bench.DS_H), stk.xn.data_ptr(),
+                            bench.DS_H, stk.logits.data_ptr(), bench.DS_E, bench.DS_E, bench.DS_H, stk.T)
+            stk.moe.zero_()
+            stk.routed(L)
+            torch.cuda.synchronize()
+            return stk.moe.cpu().numpy().copy(), stk.idx.cpu().numpy().copy()
+        part, idx = moe_layer(st)
+        parts = [None] * world
+        dist.all_gather_object(parts, part)
+        ep = np.sum(np.stack(parts).astype(np.float64), axis=0)
+        ok, info = True, ""
+        if rank == 0:
+            del st
+            torch.cuda.empty_cache()
+            one = bench.MoEStack(Q, torch, 0, 1, 8, layers=2)
+            full, idx1 = moe_layer(one)
+            err = float(np.linalg.norm(ep - full) / np.linalg.norm(full))
+            ok = err < 1e-5 and np.array_equal(idx, idx1)
+            info = f"EP{world} vs 1 GPU: rel err {err:.2e}"
+        Q.check_device()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, ok, info))
+    except Exception:
+        import traceback
+        q.put((rank, False, traceback.format_exc()))
+
+
+def test_expert_parallel_moe_layer_matches_single_gpu():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=400) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, info in out:
+        assert ok, (rank, info)
