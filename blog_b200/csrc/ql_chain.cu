@@ -39,6 +39,7 @@ constexpr int kErrChainPeer = 6;                     // a peer's partial sums ne
 constexpr int kChainW = gemv_consumer_warps(true);   // 14 consumer warps
 constexpr int kChainRed = kChainW * 2 * kRowGroup;   // floats per reduction buffer (up to 2 matrices)
 constexpr int kErrChainBarrier = 5;
+constexpr int kChainPreX = 1;                        // stages of an op issued before its activations are staged
 
 enum ChainKind : int { kOpStore = 0, kOpAdd = 1, kOpSwiglu = 2 };
 
@@ -115,6 +116,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
     uint64_t *red_empty = red_full + 2;                     // [2]
     int *abort_flag = reinterpret_cast<int *>(red_empty + 2);
     unsigned *epoch_s = reinterpret_cast<unsigned *>(abort_flag + 1);
+    volatile unsigned *x_staged = reinterpret_cast<volatile unsigned *>(epoch_s + 1);  // ops whose x is staged
     float *inv_rms = reinterpret_cast<float *>(smem + 112);
     float *ss_part = reinterpret_cast<float *>(smem + 128);  // [W]
     size_t off = kGemvHeaderBytes;
@@ -139,6 +141,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             mbar_init(&red_empty[b], 1);
         }
         *abort_flag = 0;
+        *x_staged = 0u;
         *epoch_s = *reinterpret_cast<volatile unsigned *>(a.epoch);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -158,8 +161,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
             const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
             Stage st;
+            int sio = 0;  // stage index within the op
             while (next_stage(t, t1, o.U, seg, 0, st)) {
                 const int slot = it % kChainSlots;
+                // Past the op's first stage, let the activation loads go first: TMA data queued
+                // ahead of them on the SM's inbound path would add its transfer time to their latency.
+                if (sio++ == kChainPreX && *x_staged < (unsigned)(p + 1) &&
+                    !*reinterpret_cast<volatile int *>(abort_flag)) {
+                    const uint64_t tw = global_timer_ns();
+                    while (*x_staged < (unsigned)(p + 1)) {
+                        __nanosleep(64);
+                        if (global_timer_ns() - tw > 2000000000ull) {
+                            atomicExch(a.err, kErrWaitEmpty);
+                            *abort_flag = 1;
+                            break;
+                        }
+                    }
+                }
                 if (it >= kChainSlots && !*reinterpret_cast<volatile int *>(abort_flag)) {
                     if (!mbar_wait(&empty[slot], ((uint32_t)(it / kChainSlots) & 1u) ^ 1u, a.err, kErrWaitEmpty))
                         *abort_flag = 1;
@@ -419,6 +437,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             if (lane == 0) ss_part[cw] = wsum;
         }
         named_bar_sync(1, nthr);
+        if (ctid == 0) *x_staged = (unsigned)(p + 1);  // the producer may issue the op's remaining stages
         if (o.gamma != nullptr && cw == 0) {
             const float tsum = warp_sum(lane < W ? ss_part[lane] : 0.f);
             if (lane == 0) inv_rms[0] = rsqrtf(tsum / (float)K + o.eps);
