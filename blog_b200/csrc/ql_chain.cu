@@ -38,6 +38,7 @@ constexpr int kMaxWorld = 8;
 constexpr int kErrChainPeer = 6;                     // a peer's partial sums never arrived
 constexpr int kChainW = gemv_consumer_warps(true);   // 14 consumer warps
 constexpr int kChainRed = kChainW * 2 * kRowGroup;   // floats per reduction buffer (up to 2 matrices)
+constexpr int kChainThreads = (2 + kChainW) * 32;   // producer warp, finisher warp, consumers
 constexpr int kErrChainBarrier = 5;
 constexpr int kChainPreX = 1;                        // stages of an op issued before its activations are staged
 
@@ -107,7 +108,103 @@ __device__ __forceinline__ void tensormap_acquire(const void *map) {
     asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __grid_constant__ ChainArgs a) {
+// ----------------------------------------------------------------------------
+// Q4_K on the integer tensor cores (mma.sync m16n8k32, u8 weights x s8 activations, s32).
+//
+// Activations are staged per 256-element block b as fixed-point limbs: with 2^e_b > max|x'|
+// over the block, V = rint(x' * 2^(20 - e_b)) (|V| <= 2^20) = l0 * 2^14 + l1 * 2^7 + l2 with
+// l0 = V >> 14 (signed), l1 = (V >> 7) & 127, l2 = V & 127 -- three signed bytes, an exact
+// split of V (21 bits; the staging error is below 2^-21 of the block's largest |x'|).
+// Layout per block: [sub-block s 0..7][slot 0..3][32 bytes]; slot l < 3 holds limb l of the
+// sub-block's 32 elements, slot 3 zeros.  B columns 0, 2, 4 carry limbs 0, 1, 2 and the odd
+// columns zeros, so in the accumulator fragment thread (g, t) holds limb t of rows g, g+8.
+//
+// Weights go in raw: a 32-bit word of qs holds 4 low nibbles (sub-block 2q) and 4 high nibbles
+// (2q+1) of consecutive elements; word & 0x0F0F0F0F gives n, word & 0xF0F0F0F0 gives 16 n, both
+// valid u8 operands, so the decode is one AND per 4 elements.  Per (row, sub-block) the integer
+// sums are scaled by the 6-bit sub-block scale (IMAD, exact: |16 T| < 2^29 per block); the
+// block's d, the limb weight 2^(14 - 7t) and 2^(e_b - 24) apply once per block in fp32.  The
+// min term dmin * sum_s m_s * X_s (X_s = fp32 sum of x' over sub-block s) is split over the
+// four threads of a row (sub-blocks 2t, 2t+1).  The four threads' partial sums of a row are
+// added at the end of the row group.  Same block math as q4k_dequant / vec_dot_q4_K
+// (reference kernel.cu:913-921), with the activation rounding above in place of fp32 products.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// One Q4_K block (256 elements) of the 32 rows of a TMA box (row r at box[mat] + r * pitch),
+// against the staged limbs `xl` of that block (256 words), its sub-block sums `xs8` and its
+// scale `xe` = 2^(e_b - 24).  acc[mat][j]: this thread's partial sum of row g + 8j.
+template <int NM>
+__device__ __forceinline__ void unit_q4k_imma(const uint8_t *const (&box)[NM], int pitch, const uint32_t *xl,
+                                              const float *xs8, float xe, int lane, float (&acc)[NM][4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const int slot = (g < 6 && !(g & 1)) ? (g >> 1) : 3;
+    const float xw = xe * (t == 0 ? 16384.f : t == 1 ? 128.f : t == 2 ? 1.f : 0.f);
+    const float X0 = xs8[2 * t], X1 = xs8[2 * t + 1];
+    float dd[NM][4], mt[NM][4];
+    uint32_t s03[NM][4], s47[NM][4];
+#pragma unroll
+    for (int mat = 0; mat < NM; ++mat)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint4 h = *reinterpret_cast<const uint4 *>(box[mat] + (g + 8 * j) * pitch);
+            dd[mat][j] = half_bits_to_float(h.x) * xw;
+            s03[mat][j] = h.y & 0x3F3F3F3Fu;
+            s47[mat][j] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+            const uint32_t mw = t < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+            const float2 mf = byte_pair_f(mw, 2 * (t & 1));
+            mt[mat][j] = half_bits_to_float(h.x >> 16) * fmaf(mf.x, X0, mf.y * X1);
+        }
+    int te[NM][4], to[NM][4];
+#pragma unroll
+    for (int mat = 0; mat < NM; ++mat)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) te[mat][j] = to[mat][j] = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t *xq = xl + (8 * q + slot) * 8 + t;  // sub-block 2q; 2q+1 is 32 words on
+        const uint32_t b0e = xq[0], b1e = xq[4], b0o = xq[32], b1o = xq[36];
+#pragma unroll
+        for (int mat = 0; mat < NM; ++mat)
+#pragma unroll
+            for (int tile = 0; tile < 2; ++tile) {
+                const uint8_t *ra = box[mat] + (g + 16 * tile) * pitch + 16 + 32 * q + 4 * t;
+                const uint8_t *rb = ra + 8 * pitch;
+                const uint32_t wa0 = *reinterpret_cast<const uint32_t *>(ra);
+                const uint32_t wa1 = *reinterpret_cast<const uint32_t *>(ra + 16);
+                const uint32_t wb0 = *reinterpret_cast<const uint32_t *>(rb);
+                const uint32_t wb1 = *reinterpret_cast<const uint32_t *>(rb + 16);
+                const uint32_t sa = q < 2 ? s03[mat][2 * tile] : s47[mat][2 * tile];
+                const uint32_t sb = q < 2 ? s03[mat][2 * tile + 1] : s47[mat][2 * tile + 1];
+                const uint32_t sel = 0x4440u + 2u * (q & 1);
+                int c[4];
+                imma_u8s8(c, wa0 & 0x0F0F0F0Fu, wb0 & 0x0F0F0F0Fu, wa1 & 0x0F0F0F0Fu, wb1 & 0x0F0F0F0Fu, b0e, b1e);
+                te[mat][2 * tile] += (int)__byte_perm(sa, 0u, sel) * c[0];
+                te[mat][2 * tile + 1] += (int)__byte_perm(sb, 0u, sel) * c[2];
+                imma_u8s8(c, wa0 & 0xF0F0F0F0u, wb0 & 0xF0F0F0F0u, wa1 & 0xF0F0F0F0u, wb1 & 0xF0F0F0F0u, b0o, b1o);
+                to[mat][2 * tile] += (int)__byte_perm(sa, 0u, sel + 1u) * c[0];
+                to[mat][2 * tile + 1] += (int)__byte_perm(sb, 0u, sel + 1u) * c[2];
+            }
+    }
+#pragma unroll
+    for (int mat = 0; mat < NM; ++mat)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            acc[mat][j] += fmaf(dd[mat][j], (float)(16 * te[mat][j] + to[mat][j]), -mt[mat][j]);
+}
+
+// Packs byte 0 of each of four words.
+__device__ __forceinline__ uint32_t pack_b0(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __grid_constant__ ChainArgs a) {
     constexpr int EW = 1, CW0 = 2, W = kChainW;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);   // [kChainSlots]
@@ -120,10 +217,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
     float *inv_rms = reinterpret_cast<float *>(smem + 112);
     float *ss_part = reinterpret_cast<float *>(smem + 128);  // [W]
     size_t off = kGemvHeaderBytes;
-    float *xs = reinterpret_cast<float *>(smem + off);
+    uint32_t *xl = reinterpret_cast<uint32_t *>(smem + off);  // activation limbs, 1 KB per 256-element block
     off += ((size_t)a.kmax * 4 + 127) / 128 * 128;
-    float *xsum = reinterpret_cast<float *>(smem + off);
+    float *xsum = reinterpret_cast<float *>(smem + off);        // per 32-element sub-block
     off += ((size_t)(a.kmax / 32) * 4 + 127) / 128 * 128;
+    float *xe = reinterpret_cast<float *>(smem + off);          // per block: 2^(e_b - 24)
+    off += ((size_t)(a.kmax / 256) * 4 + 127) / 128 * 128;
     float *red = reinterpret_cast<float *>(smem + off);  // [2][W][2][32]
     off += ((size_t)2 * kChainRed * 4 + 127) / 128 * 128;
     off = (off + 1023) / 1024 * 1024;
@@ -368,7 +467,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
     int it = 0, gi = 0, ucount = 0;
     for (int p = 0; p < a.nops; ++p) {
         const ChainOp &o = a.ops[p];
-        const int K = o.K, nblk = K / 32, U = o.U, NM = o.nmat;
+        const int K = o.K, U = o.U, NM = o.nmat;
         // the RMSNorm weight does not depend on earlier ops: pull it into L2 while waiting
         if (o.gamma != nullptr)
             for (int i = ctid * 32; i < K; i += nthr * 32)
@@ -390,44 +489,67 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             }
             named_bar_sync(1, nthr);
         }
-        // prologue: stage x * g * 2^(96-p) and the block sums of x * g; sum x^2 for a fused RMSNorm
+        // prologue: x' = x * g staged as limbs per 256-element block (see unit_q4k_imma), with the
+        // sub-block sums of x' and the block scales; sum x^2 for a fused RMSNorm.  Warp cw stages
+        // blocks cw, cw + W, ...: lane l holds elements 4l..4l+3 and 128+4l..128+4l+3 of a block.
         float ss = 0.f;
         {
-            const int nch = K / 4;
-            constexpr int B = 12;
-            for (int j0 = ctid; j0 - lane < nch; j0 += B * nthr) {
-                float4 vv[B], gg[B];
+            const int nb = K / 256;
+            constexpr int B = 6;
+            for (int b0 = cw; b0 < nb; b0 += B * W) {
+                float4 vv[B][2], gg[B][2];
 #pragma unroll
                 for (int u = 0; u < B; ++u) {
-                    const int j = j0 + u * nthr;
-                    // L2 only: another SM wrote x during the previous op, after this SM may have cached it
-                    vv[u] = j < nch ? __ldcg(reinterpret_cast<const float4 *>(o.x) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    gg[u] = (j < nch && o.gamma != nullptr) ? reinterpret_cast<const float4 *>(o.gamma)[j]
-                                                            : make_float4(1.f, 1.f, 1.f, 1.f);
+                    const int b = b0 + u * W;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int j = b * 64 + 32 * h + lane;
+                        // L2 only: another SM wrote x during the previous op, after this SM may have cached it
+                        vv[u][h] = b < nb ? __ldcg(reinterpret_cast<const float4 *>(o.x) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        gg[u][h] = (b < nb && o.gamma != nullptr) ? reinterpret_cast<const float4 *>(o.gamma)[j]
+                                                                  : make_float4(1.f, 1.f, 1.f, 1.f);
+                    }
                 }
 #pragma unroll
                 for (int u = 0; u < B; ++u) {
-                    const int j = j0 + u * nthr;
-                    const bool ok = j < nch;
-                    const int k = ok ? 4 * j : 0;
-                    float4 xv = vv[u];
-                    if (ok && o.gamma != nullptr) {
-                        ss += fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, xv.w * xv.w)));
-                        const float4 g = gg[u];
-                        xv.x *= g.x; xv.y *= g.y; xv.z *= g.z; xv.w *= g.w;
+                    const int b = b0 + u * W;
+                    if (b >= nb) break;  // warp-uniform
+                    float4 xv[2];
+                    float amax = 0.f;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        xv[h] = vv[u][h];
+                        if (o.gamma != nullptr) {
+                            ss += fmaf(xv[h].x, xv[h].x, fmaf(xv[h].y, xv[h].y, fmaf(xv[h].z, xv[h].z, xv[h].w * xv[h].w)));
+                            const float4 gm = gg[u][h];
+                            xv[h].x *= gm.x; xv[h].y *= gm.y; xv[h].z *= gm.z; xv[h].w *= gm.w;
+                        }
+                        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(xv[h].x), fabsf(xv[h].y)), fmaxf(fabsf(xv[h].z), fabsf(xv[h].w))));
+                        float bs = (xv[h].x + xv[h].y) + (xv[h].z + xv[h].w);
+                        bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+                        bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+                        bs += __shfl_xor_sync(0xffffffffu, bs, 4);
+                        if ((lane & 7) == 0) xsum[b * 8 + 4 * h + (lane >> 3)] = bs;
                     }
-                    float bs = (xv.x + xv.y) + (xv.z + xv.w);
-                    bs += __shfl_xor_sync(0xffffffffu, bs, 1);
-                    bs += __shfl_xor_sync(0xffffffffu, bs, 2);
-                    bs += __shfl_xor_sync(0xffffffffu, bs, 4);
-                    if (ok) {
-                        float4 q;
-                        q.x = xv.x * pow2_dev(96 - weight_bitpos<kQ4_K>(k + 0));
-                        q.y = xv.y * pow2_dev(96 - weight_bitpos<kQ4_K>(k + 1));
-                        q.z = xv.z * pow2_dev(96 - weight_bitpos<kQ4_K>(k + 2));
-                        q.w = xv.w * pow2_dev(96 - weight_bitpos<kQ4_K>(k + 3));
-                        *reinterpret_cast<float4 *>(xs + k) = q;
-                        if ((k & 31) == 0) xsum[k >> 5] = bs;
+#pragma unroll
+                    for (int m = 16; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+                    // 2^e > amax with e = E - 126 (E: amax's biased exponent, at least 30 so that the
+                    // factors stay normal; smaller values are all but zero against 2^-96)
+                    int E = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
+                    const bool finite = E != 255;
+                    E = E < 30 ? 30 : E;
+                    const float f = __uint_as_float((uint32_t)(273 - E) << 23);  // 2^(20 - e)
+                    if (lane == 0) xe[b] = finite ? __uint_as_float((uint32_t)(E - 23) << 23) : __int_as_float(0x7fc00000);
+                    uint32_t *xb = xl + b * 256 + (lane & 7);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int V0 = __float2int_rn(xv[h].x * f), V1 = __float2int_rn(xv[h].y * f);
+                        const int V2 = __float2int_rn(xv[h].z * f), V3 = __float2int_rn(xv[h].w * f);
+                        uint32_t *xw = xb + (4 * h + (lane >> 3)) * 32;  // sub-block 4h + lane/8, slot 0
+                        xw[0] = pack_b0(V0 >> 14, V1 >> 14, V2 >> 14, V3 >> 14);
+                        xw[8] = pack_b0(V0 >> 7, V1 >> 7, V2 >> 7, V3 >> 7) & 0x7F7F7F7Fu;
+                        xw[16] = pack_b0(V0, V1, V2, V3) & 0x7F7F7F7Fu;
+                        xw[24] = 0u;
                     }
                 }
             }
@@ -443,9 +565,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
             if (lane == 0) inv_rms[0] = rsqrtf(tsum / (float)K + o.eps);
         }
 
-        float acc[2][1] = {{0.f}, {0.f}};
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // rows lane/4 + 8j, this thread's share
         const int bu = o.bu, seg = 2 * bu / NM;
-        const int kb = bu * 144 * kRowGroup;
+        const int kb = bu * 144 * kRowGroup, pitch = bu * 144;
         int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
         const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
         Stage st;
@@ -456,24 +578,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                 if (!mbar_wait(&full[slot], ph, a.err, kErrWaitFull)) *abort_flag = 1;
             }
             const int n = st.ue - st.us;
-            const int v = st.g * kRowGroup + lane;
-            const bool aborted = *reinterpret_cast<volatile int *>(abort_flag) != 0;
-            if (!aborted && v < o.rows) {
-                const uint8_t *sb = ring + (size_t)slot * kSlotBytes + (size_t)lane * (bu * 144);
+            // warp-uniform (the tensor-core decoder is warp-collective); rows past the op's end
+            // are zero-filled by the tensor map and never stored
+            const bool aborted = __any_sync(0xffffffffu, *reinterpret_cast<volatile int *>(abort_flag) != 0);
+            if (!aborted) {
+                const uint8_t *sb = ring + (size_t)slot * kSlotBytes;
                 const int first = ((cw - ucount) % W + W) % W;
                 for (int lu = first; lu < n; lu += W) {
-                    const int k0 = (st.us + lu) * 256;
+                    const int b = st.us + lu;
                     if (NM == 2) {
                         const uint8_t *bp[2] = {sb + lu * 144, sb + kb + lu * 144};
-                        float acc2[2][1] = {{acc[0][0]}, {acc[1][0]}};
-                        unit_q4k<1, 2>(bp, xs, K, xsum, nblk, k0, acc2);
-                        acc[0][0] = acc2[0][0];
-                        acc[1][0] = acc2[1][0];
+                        unit_q4k_imma<2>(bp, pitch, xl + b * 256, xsum + b * 8, xe[b], lane, acc);
                     } else {
                         const uint8_t *bp[1] = {sb + (lu / bu) * kb + (lu % bu) * 144};
-                        float acc1[1][1] = {{acc[0][0]}};
-                        unit_q4k<1, 1>(bp, xs, K, xsum, nblk, k0, acc1);
-                        acc[0][0] = acc1[0][0];
+                        float acc1[1][4] = {{acc[0][0], acc[0][1], acc[0][2], acc[0][3]}};
+                        unit_q4k_imma<1>(bp, pitch, xl + b * 256, xsum + b * 8, xe[b], lane, acc1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[0][j] = acc1[0][j];
                     }
                 }
             }
@@ -487,10 +608,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_chain_kernel(const __gri
                     if (!mbar_wait(&red_empty[bsel], ((uint32_t)(gi >> 1) & 1u) ^ 1u, a.err, kErrWaitEmpty))
                         *abort_flag = 1;
                 }
+                // the four threads of a row hold its limb / min-term shares: sum them, then
+                // thread t of group g stores row g + 8t
                 float *rb = red + bsel * kChainRed;
-                rb[(cw * 2 + 0) * kRowGroup + lane] = acc[0][0];
-                rb[(cw * 2 + 1) * kRowGroup + lane] = acc[1][0];
-                acc[0][0] = acc[1][0] = 0.f;
+#pragma unroll
+                for (int mat = 0; mat < 2; ++mat) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc[mat][j] += __shfl_xor_sync(0xffffffffu, acc[mat][j], 1);
+                        acc[mat][j] += __shfl_xor_sync(0xffffffffu, acc[mat][j], 2);
+                    }
+                    const int tq = lane & 3;
+                    const float mine = tq == 0 ? acc[mat][0] : tq == 1 ? acc[mat][1] : tq == 2 ? acc[mat][2] : acc[mat][3];
+                    rb[(cw * 2 + mat) * kRowGroup + (lane >> 2) + 8 * tq] = mine;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[mat][j] = 0.f;
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&red_full[bsel]);
                 ++gi;
@@ -663,6 +796,7 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
     size_t off = kGemvHeaderBytes;
     off += ((size_t)kmax * 4 + 127) / 128 * 128;
     off += ((size_t)(kmax / 32) * 4 + 127) / 128 * 128;
+    off += ((size_t)(kmax / 256) * 4 + 127) / 128 * 128;
     off += ((size_t)2 * kChainRed * 4 + 127) / 128 * 128;
     off = (off + 1023) / 1024 * 1024;
     off += (size_t)kChainSlots * kSlotBytes;
@@ -712,7 +846,7 @@ int ql_gemv_chain_run(void *chain) {
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(c->sms);
-    cfg.blockDim = dim3(kGemvThreads);
+    cfg.blockDim = dim3(kChainThreads);
     cfg.dynamicSmemBytes = c->smem;
     cfg.stream = static_cast<cudaStream_t>(ql_get_stream());
     cudaLaunchAttribute attr[1];

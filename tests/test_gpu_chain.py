@@ -1,9 +1,10 @@
 """The persistent GEMV chain (one cooperative launch for a decoder stack) against
 the same ops run one launch at a time through the per-op entry points.
 
-Both run the same decoders and epilogues; the chain splits every op over all SMs
-(stream-K), so fp32 partial sums may associate differently: results agree within
-1e-5 relative L2, and the fused argmax is exact on the chain's own logits."""
+The per-op launches compute exact fp32 products on the CUDA cores; the chain runs the
+Q4_K blocks on the integer tensor cores against activations staged as 21-bit fixed-point
+limbs per 256-element block, and splits every op over all SMs (stream-K).  Results agree
+within 1e-5 relative L2, and the fused argmax is exact on the chain's own logits."""
 import numpy as np
 import pytest
 
