@@ -201,6 +201,12 @@ class DecodeStack:
                                   L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr()))
             ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [Q.row_bytes(QK, self.qo_len)], [HIDDEN],
                                   self.qo_len, self.qkv.data_ptr(), h, reduce=self.world > 1))
+            if self.world == 1 and os.environ.get("QL_CHAIN_MLP", "1") != "0":
+                # gate/up SwiGLU and down + residual as one op, split over the FFN (no barrier between)
+                ops.append(Q.chain_op(Q.OP_MLP, [L["wg"].data_ptr(), L["wu"].data_ptr(), L["wd"].data_ptr()],
+                                      [rbh, rbh, Q.row_bytes(QK, self.f_len)], [self.f_len, self.f_len, HIDDEN],
+                                      HIDDEN, h, h, L["ln2"].data_ptr(), EPS))
+                continue
             ops.append(Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rbh] * 2,
                                   [self.f_len] * 2, HIDDEN, h, self.act.data_ptr(), L["ln2"].data_ptr(), EPS))
             ops.append(Q.chain_op(Q.OP_ADD, [L["wd"].data_ptr()], [Q.row_bytes(QK, self.f_len)], [HIDDEN],

@@ -187,7 +187,7 @@ def quant_gemv_argmax_ex(t, w, rb, x, x_stride, logits, logits_stride, out_dim, 
           index_offset, out_idx, out_key)
 
 
-OP_STORE, OP_ADD, OP_SWIGLU = 0, 1, 2
+OP_STORE, OP_ADD, OP_SWIGLU, OP_MLP = 0, 1, 2, 3
 
 
 class ChainOp(C.Structure):

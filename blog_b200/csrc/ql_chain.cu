@@ -42,7 +42,10 @@ constexpr int kChainThreads = (2 + kChainW) * 32;   // producer warp, finisher w
 constexpr int kErrChainBarrier = 5;
 constexpr int kChainPreX = 1;                        // stages of an op issued before its activations are staged
 
-enum ChainKind : int { kOpStore = 0, kOpAdd = 1, kOpSwiglu = 2 };
+enum ChainKind : int { kOpStore = 0, kOpAdd = 1, kOpSwiglu = 2, kOpMlp = 3 };
+constexpr int kMlpBoxRows = kBox / 144;              // 224 rows of one block column per down-projection box
+constexpr double kFix = 4294967296.0;                // fixed-point residual: 32 fractional bits in an int64
+constexpr int kMlpSmem = 2048 + 128;                 // MLP chunk activations (fp32, limbs), sums and scale
 
 struct __align__(128) ChainOp {
     CUtensorMap tmap[3];   // Q4_K sources {144, blocks, rows}, box {144, 7, 32}
@@ -61,6 +64,17 @@ struct __align__(128) ChainOp {
     int reduce;            // tensor parallel: y += (sum over ranks of this rank's W.x) through peer memory
     int pre_y;             // ADD: y's last writer is at least two ops back, so y may be read early
     long long xchg;        // first exchange cell of this op (reduce: [G][world][32]; argmax: [world][2])
+    // fused MLP (kOpMlp): tmap[0..1] gate/up, tmap[2] the down projection (box {144, 1, 224});
+    // split-K over 256-row chunks of the FFN, two CTAs per chunk (one per 128-row half)
+    long long *y_fixed;     // MLP: the residual in fixed point (int64 atomics); ADD: also store y there
+    const long long *x_fixed;  // the input in fixed point (the op right after an MLP reading its residual)
+    const long long *mat_src;  // the op right after an MLP: copies its fixed-point residual ...
+    float *mat_dst;            // ... back to fp32, a slice per CTA
+    int mat_rows;
+    int rows_d;             // MLP: rows of the down projection (= residual length)
+    int half_rows;          // MLP: down rows [0, half_rows) go to the even CTA of a pair, the rest to the odd one
+    int nunits;             // MLP: 2 x (FFN rows / 256)
+    long long cells;        // MLP: first pair-exchange cell ([nunits][128])
 };
 
 struct ChainArgs {
@@ -74,6 +88,7 @@ struct ChainArgs {
     int *err;
     unsigned long long *xchg[kMaxWorld];  // every rank's exchange cells (index = rank), mapped here
     int rank, world;
+    unsigned long long *mlp_cells;  // fused MLP pair exchange (tagged 64-bit cells)
 };
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
@@ -204,6 +219,46 @@ __device__ __forceinline__ uint32_t pack_b0(uint32_t a, uint32_t b, uint32_t c, 
     return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
 }
 
+// Stages one 256-element block for unit_q4k_imma from a warp: lane l holds x' elements
+// 4l..4l+3 (xv[0]) and 128+4l..128+4l+3 (xv[1]).  Writes the block's limbs (256 words at xl),
+// its eight sub-block sums (xsum) and its scale (*xe = 2^(e_b - 24), NaN when x' is not finite).
+__device__ __forceinline__ void stage_block_limbs(const float4 (&xv)[2], uint32_t *xl, float *xsum, float *xe,
+                                                  int lane) {
+    float amax = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(xv[h].x), fabsf(xv[h].y)), fmaxf(fabsf(xv[h].z), fabsf(xv[h].w))));
+        float bs = (xv[h].x + xv[h].y) + (xv[h].z + xv[h].w);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 4);
+        if ((lane & 7) == 0) xsum[4 * h + (lane >> 3)] = bs;
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    // 2^e > amax with e = E - 126 (E: amax's biased exponent, at least 30 so that the factors
+    // stay normal; smaller values are all but zero against 2^-96)
+    int E = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
+    const bool finite = E != 255;
+    E = E < 30 ? 30 : E;
+    const float f = __uint_as_float((uint32_t)(273 - E) << 23);  // 2^(20 - e)
+    if (lane == 0) *xe = finite ? __uint_as_float((uint32_t)(E - 23) << 23) : __int_as_float(0x7fc00000);
+    uint32_t *xb = xl + (lane & 7);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int V0 = __float2int_rn(xv[h].x * f), V1 = __float2int_rn(xv[h].y * f);
+        const int V2 = __float2int_rn(xv[h].z * f), V3 = __float2int_rn(xv[h].w * f);
+        uint32_t *xw = xb + (4 * h + (lane >> 3)) * 32;  // sub-block 4h + lane/8, slot 0
+        xw[0] = pack_b0(V0 >> 14, V1 >> 14, V2 >> 14, V3 >> 14);
+        xw[8] = pack_b0(V0 >> 7, V1 >> 7, V2 >> 7, V3 >> 7) & 0x7F7F7F7Fu;
+        xw[16] = pack_b0(V0, V1, V2, V3) & 0x7F7F7F7Fu;
+        xw[24] = 0u;
+    }
+}
+
+__device__ __forceinline__ long long to_fixed(float v) { return __float2ll_rn(v * (float)kFix); }
+__device__ __forceinline__ float from_fixed(long long v) { return __ll2float_rn(v) * (float)(1.0 / kFix); }
+
 __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __grid_constant__ ChainArgs a) {
     constexpr int EW = 1, CW0 = 2, W = kChainW;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -216,6 +271,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     volatile unsigned *x_staged = reinterpret_cast<volatile unsigned *>(epoch_s + 1);  // ops whose x is staged
     float *inv_rms = reinterpret_cast<float *>(smem + 112);
     float *ss_part = reinterpret_cast<float *>(smem + 128);  // [W]
+    uint64_t *a_ready = reinterpret_cast<uint64_t *>(smem + 192);  // MLP: the chunk's activations are staged
+    uint64_t *p2_done = reinterpret_cast<uint64_t *>(smem + 200);  // MLP: the consumers finished a unit
+    static_assert(128 + 4 * kChainW <= 192, "header layout");
     size_t off = kGemvHeaderBytes;
     uint32_t *xl = reinterpret_cast<uint32_t *>(smem + off);  // activation limbs, 1 KB per 256-element block
     off += ((size_t)a.kmax * 4 + 127) / 128 * 128;
@@ -225,6 +283,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     off += ((size_t)(a.kmax / 256) * 4 + 127) / 128 * 128;
     float *red = reinterpret_cast<float *>(smem + off);  // [2][W][2][32]
     off += ((size_t)2 * kChainRed * 4 + 127) / 128 * 128;
+    float *abuf = reinterpret_cast<float *>(smem + off);      // MLP: the chunk's 256 activations
+    uint32_t *xa = reinterpret_cast<uint32_t *>(smem + off + 1024);  // ... as limbs
+    float *xsa = reinterpret_cast<float *>(smem + off + 2048);        // ... sub-block sums, [8] then the scale
+    off += kMlpSmem;
     off = (off + 1023) / 1024 * 1024;
     uint8_t *ring = smem + off;
 
@@ -239,6 +301,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             mbar_init(&red_full[b], W);
             mbar_init(&red_empty[b], 1);
         }
+        mbar_init(a_ready, 1);
+        mbar_init(p2_done, W);
         *abort_flag = 0;
         *x_staged = 0u;
         *epoch_s = *reinterpret_cast<volatile unsigned *>(a.epoch);
@@ -252,9 +316,66 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
         // ---------------------------- producer (TMA) ----------------------------
         if (lane != 0) return;
         int it = 0;
+        // waits for a free ring slot (and, past an op's first stage, for its activations)
+        auto claim_slot = [&](int p, int sio) -> bool {
+            if (sio == kChainPreX && *x_staged < (unsigned)(p + 1) && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                const uint64_t tw = global_timer_ns();
+                while (*x_staged < (unsigned)(p + 1)) {
+                    __nanosleep(64);
+                    if (global_timer_ns() - tw > 2000000000ull) {
+                        atomicExch(a.err, kErrWaitEmpty);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+            }
+            const int slot = it % kChainSlots;
+            if (it >= kChainSlots && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                if (!mbar_wait(&empty[slot], ((uint32_t)(it / kChainSlots) & 1u) ^ 1u, a.err, kErrWaitEmpty))
+                    *abort_flag = 1;
+            }
+            return !*reinterpret_cast<volatile int *>(abort_flag);
+        };
         for (int p = 0; p < a.nops; ++p) {
             const ChainOp &o = a.ops[p];
-            for (int i = 0; i < (o.nmat == 2 ? 2 : 3); ++i) tensormap_acquire(&o.tmap[i]);
+            for (int i = 0; i < ((o.nmat == 2 && o.kind != kOpMlp) ? 2 : 3); ++i) tensormap_acquire(&o.tmap[i]);
+            if (o.kind == kOpMlp) {
+                // per unit: the half chunk's gate/up rows (4 row groups x all blocks), then the
+                // down projection's block column of the chunk over this half's rows
+                const uint32_t kb = (uint32_t)o.bu * 144u * kRowGroup;
+                const int Ce = C & ~1;
+                int sio = 0;
+                for (int u = cta; cta < Ce && u < o.nunits; u += Ce) {
+                    const int ci = u >> 1, hh = u & 1;
+                    for (int r = 0; r < 4; ++r)
+                        for (int us = 0; us < o.U; us += o.bu) {
+                            const bool live = claim_slot(p, sio++);
+                            const int slot = it % kChainSlots;
+                            uint8_t *sb = ring + (size_t)slot * kSlotBytes;
+                            const int row0 = 256 * ci + 128 * hh + 32 * r;
+                            mbar_arrive_expect_tx(&full[slot], live ? 2u * kb : 0u);
+                            if (live) {
+                                tma_load_3d(sb, &o.tmap[0], 0, us, row0, &full[slot]);
+                                tma_load_3d(sb + kb, &o.tmap[1], 0, us, row0, &full[slot]);
+                            }
+                            ++it;
+                        }
+                    const int r_beg = hh ? o.half_rows : 0, r_end = hh ? o.rows_d : o.half_rows;
+                    for (int r = r_beg; r < r_end; r += 2 * kMlpBoxRows) {
+                        const bool live = claim_slot(p, sio++);
+                        const int slot = it % kChainSlots;
+                        uint8_t *sb = ring + (size_t)slot * kSlotBytes;
+                        const int nbox = r + kMlpBoxRows < r_end ? 2 : 1;
+                        mbar_arrive_expect_tx(&full[slot], live ? (uint32_t)(nbox * kBox) : 0u);
+                        if (live) {
+                            tma_load_3d(sb, &o.tmap[2], 0, ci, r, &full[slot]);
+                            if (nbox == 2) tma_load_3d(sb + kBox, &o.tmap[2], 0, ci, r + kMlpBoxRows, &full[slot]);
+                        }
+                        ++it;
+                    }
+                }
+                continue;
+            }
             const int seg = 2 * o.bu / o.nmat;
             const uint32_t kb = (uint32_t)o.bu * 144u * kRowGroup;
             int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
@@ -311,8 +432,66 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     if (warp == EW) {
         // ------------------------------ finisher ------------------------------
         int gi = 0;
+        int mu = 0, p2_waited = 0;  // MLP units of this CTA so far; their p2_done phases consumed
+        auto wait_p2 = [&](int upto) {
+            for (; p2_waited < upto; ++p2_waited)
+                if (!*reinterpret_cast<volatile int *>(abort_flag) &&
+                    !mbar_wait(p2_done, (uint32_t)p2_waited & 1u, a.err, kErrWaitFull))
+                    *abort_flag = 1;
+        };
         for (int p = 0; p < a.nops; ++p) {
             const ChainOp &o = a.ops[p];
+            if (o.kind == kOpMlp) {
+                const int Ce = C & ~1;
+                for (int u = cta; cta < Ce && u < o.nunits; u += Ce, ++mu) {
+                    const int hh = u & 1;
+                    // phase 1: SwiGLU of the half chunk's four row groups -> smem and the pair's cells
+                    for (int r = 0; r < 4; ++r, ++gi) {
+                        const int bsel = gi & 1;
+                        if (!*reinterpret_cast<volatile int *>(abort_flag) &&
+                            !mbar_wait(&red_full[bsel], (uint32_t)(gi >> 1) & 1u, a.err, kErrWaitFull))
+                            *abort_flag = 1;
+                        const float nrm = o.gamma != nullptr ? inv_rms[0] : 1.0f;  // written before any group
+                        const float *rb = red + bsel * kChainRed;
+                        float gs = 0.f, us = 0.f;
+                        for (int w = 0; w < W; ++w) {
+                            gs += rb[(w * 2 + 0) * kRowGroup + lane];
+                            us += rb[(w * 2 + 1) * kRowGroup + lane];
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&red_empty[bsel]);
+                        const float gv = gs * nrm, uv = us * nrm;
+                        const float act = gv / (1.0f + expf(-gv)) * uv;
+                        abuf[128 * hh + 32 * r + lane] = act;
+                        st_cell(a.mlp_cells + o.cells + (size_t)u * 128 + 32 * r + lane, tag, __float_as_uint(act));
+                    }
+                    // the other half of the chunk from the pair CTA
+                    bool okc = true;
+                    for (int r = 0; r < 4 && okc; ++r) {
+                        uint32_t bits = 0;
+                        okc = ld_cell(a.mlp_cells + o.cells + (size_t)(u ^ 1) * 128 + 32 * r + lane, tag, &bits, a.err);
+                        abuf[128 * (hh ^ 1) + 32 * r + lane] = __uint_as_float(bits);
+                    }
+                    if (!__all_sync(0xffffffffu, okc)) *abort_flag = 1;
+                    // the previous unit's consumers are done with the staged activations
+                    wait_p2(mu);
+                    __syncwarp();
+                    float4 av[2];
+                    av[0] = reinterpret_cast<const float4 *>(abuf)[lane];
+                    av[1] = reinterpret_cast<const float4 *>(abuf)[32 + lane];
+                    stage_block_limbs(av, xa, xsa, xsa + 8, lane);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(a_ready);
+                }
+                wait_p2(mu);
+                if (lane == 0) {
+                    __threadfence();
+                    const unsigned prev = atomicAdd(&a.done[p], 1u);
+                    if (p == a.nops - 1 && prev == target - 1u) atomicAdd(a.epoch, 1u);
+                }
+                __syncwarp();
+                continue;
+            }
             const int NM = o.nmat, U = o.U;
             const int64_t t0 = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
             const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
@@ -391,8 +570,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                         } else {
                             out = val[0] * nrm;
                             if (o.bias != nullptr) out += bias_v;
-                            if (o.kind == kOpAdd && !o.reduce)  // residual written by other SMs: L2, not L1
-                                __stcg(yp, (o.pre_y ? res_v : __ldcg(yp)) + out);
+                            if (o.kind == kOpAdd && !o.reduce) {  // residual written by other SMs: L2, not L1
+                                const float yn = (o.pre_y ? res_v : __ldcg(yp)) + out;
+                                __stcg(yp, yn);
+                                if (o.y_fixed != nullptr) __stcg(o.y_fixed + v, to_fixed(yn));
+                            }
                             else if (o.kind != kOpAdd && o.y != nullptr) *yp = out;
                         }
                     }
@@ -464,7 +646,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     const int cw = warp - CW0;
     const int nthr = W * 32;
     const int ctid = tid - 32 * CW0;
-    int it = 0, gi = 0, ucount = 0;
+    int it = 0, gi = 0, ucount = 0, mu = 0;
     for (int p = 0; p < a.nops; ++p) {
         const ChainOp &o = a.ops[p];
         const int K = o.K, U = o.U, NM = o.nmat;
@@ -489,6 +671,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             }
             named_bar_sync(1, nthr);
         }
+        // the op right after a fused MLP: its fixed-point residual back to fp32, a slice per CTA
+        // (readers within this op use the fixed-point copy; later ops read the fp32 one)
+        if (o.mat_src != nullptr) {
+            const int n0 = (int)((int64_t)o.mat_rows * cta / C), n1 = (int)((int64_t)o.mat_rows * (cta + 1) / C);
+            for (int n = n0 + ctid; n < n1; n += nthr) __stcg(o.mat_dst + n, from_fixed(__ldcg(o.mat_src + n)));
+        }
         // prologue: x' = x * g staged as limbs per 256-element block (see unit_q4k_imma), with the
         // sub-block sums of x' and the block scales; sum x^2 for a fused RMSNorm.  Warp cw stages
         // blocks cw, cw + W, ...: lane l holds elements 4l..4l+3 and 128+4l..128+4l+3 of a block.
@@ -505,7 +693,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     for (int h = 0; h < 2; ++h) {
                         const int j = b * 64 + 32 * h + lane;
                         // L2 only: another SM wrote x during the previous op, after this SM may have cached it
-                        vv[u][h] = b < nb ? __ldcg(reinterpret_cast<const float4 *>(o.x) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (b >= nb) {
+                            vv[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        } else if (o.x_fixed != nullptr) {
+                            const longlong2 lo = __ldcg(reinterpret_cast<const longlong2 *>(o.x_fixed) + 2 * j);
+                            const longlong2 hi = __ldcg(reinterpret_cast<const longlong2 *>(o.x_fixed) + 2 * j + 1);
+                            vv[u][h] = make_float4(from_fixed(lo.x), from_fixed(lo.y), from_fixed(hi.x), from_fixed(hi.y));
+                        } else {
+                            vv[u][h] = __ldcg(reinterpret_cast<const float4 *>(o.x) + j);
+                        }
                         gg[u][h] = (b < nb && o.gamma != nullptr) ? reinterpret_cast<const float4 *>(o.gamma)[j]
                                                                   : make_float4(1.f, 1.f, 1.f, 1.f);
                     }
@@ -515,7 +711,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     const int b = b0 + u * W;
                     if (b >= nb) break;  // warp-uniform
                     float4 xv[2];
-                    float amax = 0.f;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         xv[h] = vv[u][h];
@@ -524,33 +719,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                             const float4 gm = gg[u][h];
                             xv[h].x *= gm.x; xv[h].y *= gm.y; xv[h].z *= gm.z; xv[h].w *= gm.w;
                         }
-                        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(xv[h].x), fabsf(xv[h].y)), fmaxf(fabsf(xv[h].z), fabsf(xv[h].w))));
-                        float bs = (xv[h].x + xv[h].y) + (xv[h].z + xv[h].w);
-                        bs += __shfl_xor_sync(0xffffffffu, bs, 1);
-                        bs += __shfl_xor_sync(0xffffffffu, bs, 2);
-                        bs += __shfl_xor_sync(0xffffffffu, bs, 4);
-                        if ((lane & 7) == 0) xsum[b * 8 + 4 * h + (lane >> 3)] = bs;
                     }
-#pragma unroll
-                    for (int m = 16; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-                    // 2^e > amax with e = E - 126 (E: amax's biased exponent, at least 30 so that the
-                    // factors stay normal; smaller values are all but zero against 2^-96)
-                    int E = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
-                    const bool finite = E != 255;
-                    E = E < 30 ? 30 : E;
-                    const float f = __uint_as_float((uint32_t)(273 - E) << 23);  // 2^(20 - e)
-                    if (lane == 0) xe[b] = finite ? __uint_as_float((uint32_t)(E - 23) << 23) : __int_as_float(0x7fc00000);
-                    uint32_t *xb = xl + b * 256 + (lane & 7);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int V0 = __float2int_rn(xv[h].x * f), V1 = __float2int_rn(xv[h].y * f);
-                        const int V2 = __float2int_rn(xv[h].z * f), V3 = __float2int_rn(xv[h].w * f);
-                        uint32_t *xw = xb + (4 * h + (lane >> 3)) * 32;  // sub-block 4h + lane/8, slot 0
-                        xw[0] = pack_b0(V0 >> 14, V1 >> 14, V2 >> 14, V3 >> 14);
-                        xw[8] = pack_b0(V0 >> 7, V1 >> 7, V2 >> 7, V3 >> 7) & 0x7F7F7F7Fu;
-                        xw[16] = pack_b0(V0, V1, V2, V3) & 0x7F7F7F7Fu;
-                        xw[24] = 0u;
-                    }
+                    stage_block_limbs(xv, xl + b * 256, xsum + b * 8, xe + b, lane);
                 }
             }
         }
@@ -566,6 +736,103 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
         }
 
         float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // rows lane/4 + 8j, this thread's share
+        // end of a row group: the four threads of a row hold its limb / min-term shares; sum
+        // them, then thread t of group g stores row g + 8t for the finisher
+        auto flush_group = [&]() {
+            const int bsel = gi & 1;
+            if (gi >= 2 && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                if (!mbar_wait(&red_empty[bsel], ((uint32_t)(gi >> 1) & 1u) ^ 1u, a.err, kErrWaitEmpty))
+                    *abort_flag = 1;
+            }
+            float *rb = red + bsel * kChainRed;
+#pragma unroll
+            for (int mat = 0; mat < 2; ++mat) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[mat][j] += __shfl_xor_sync(0xffffffffu, acc[mat][j], 1);
+                    acc[mat][j] += __shfl_xor_sync(0xffffffffu, acc[mat][j], 2);
+                }
+                const int tq = lane & 3;
+                const float mine = tq == 0 ? acc[mat][0] : tq == 1 ? acc[mat][1] : tq == 2 ? acc[mat][2] : acc[mat][3];
+                rb[(cw * 2 + mat) * kRowGroup + (lane >> 2) + 8 * tq] = mine;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[mat][j] = 0.f;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&red_full[bsel]);
+            ++gi;
+        };
+        if (o.kind == kOpMlp) {
+            const int bu = o.bu, kb = bu * 144 * kRowGroup, pitch = bu * 144;
+            const int Ce = C & ~1;
+            auto wait_full = [&](int slot) {
+                if (!*reinterpret_cast<volatile int *>(abort_flag) &&
+                    !mbar_wait(&full[slot], (uint32_t)(it / kChainSlots) & 1u, a.err, kErrWaitFull))
+                    *abort_flag = 1;
+                return !__any_sync(0xffffffffu, *reinterpret_cast<volatile int *>(abort_flag) != 0);
+            };
+            for (int u = cta; cta < Ce && u < o.nunits; u += Ce, ++mu) {
+                const int hh = u & 1;
+                // phase 1: gate/up of the half chunk (four row groups)
+                for (int r = 0; r < 4; ++r) {
+                    for (int us = 0; us < U; us += bu) {
+                        const int slot = it % kChainSlots;
+                        const int n = U - us < bu ? U - us : bu;
+                        if (wait_full(slot)) {
+                            const uint8_t *sb = ring + (size_t)slot * kSlotBytes;
+                            for (int lu = ((cw - ucount) % W + W) % W; lu < n; lu += W) {
+                                const int b = us + lu;
+                                const uint8_t *bp[2] = {sb + lu * 144, sb + kb + lu * 144};
+                                unit_q4k_imma<2>(bp, pitch, xl + b * 256, xsum + b * 8, xe[b], lane, acc);
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[slot]);
+                        ucount += n;
+                        ++it;
+                    }
+                    flush_group();
+                }
+                // phase 2: this half's rows of the down projection against the chunk's 256
+                // activations (staged by the finisher); per-row partials into the fixed-point residual
+                if (!*reinterpret_cast<volatile int *>(abort_flag) &&
+                    !mbar_wait(a_ready, (uint32_t)mu & 1u, a.err, kErrWaitFull))
+                    *abort_flag = 1;
+                const int r_beg = hh ? o.half_rows : 0, r_end = hh ? o.rows_d : o.half_rows;
+                for (int r = r_beg; r < r_end; r += 2 * kMlpBoxRows) {
+                    const int slot = it % kChainSlots;
+                    const int span = r_end - r < 2 * kMlpBoxRows ? r_end - r : 2 * kMlpBoxRows;
+                    const int n = (span + kRowGroup - 1) / kRowGroup;
+                    if (wait_full(slot)) {
+                        const uint8_t *sb = ring + (size_t)slot * kSlotBytes;
+                        for (int lu = ((cw - ucount) % W + W) % W; lu < n; lu += W) {
+                            const uint8_t *bp[1] = {sb + (lu / kTmaSeg) * kBox + (lu % kTmaSeg) * kRowGroup * 144};
+                            float pa[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+                            unit_q4k_imma<1>(bp, 144, xa, xsa, xsa[8], lane, pa);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                pa[0][j] += __shfl_xor_sync(0xffffffffu, pa[0][j], 1);
+                                pa[0][j] += __shfl_xor_sync(0xffffffffu, pa[0][j], 2);
+                            }
+                            const int tq = lane & 3;
+                            const float mine = tq == 0 ? pa[0][0] : tq == 1 ? pa[0][1] : tq == 2 ? pa[0][2] : pa[0][3];
+                            const int row = r + lu * kRowGroup + (lane >> 2) + 8 * tq;
+                            if (row < r_end)
+                                atomicAdd(reinterpret_cast<unsigned long long *>(o.y_fixed + row),
+                                          (unsigned long long)to_fixed(mine));
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[slot]);
+                    ucount += n;
+                    ++it;
+                }
+                __threadfence();  // the residual's atomics, before the finisher reports the op done
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p2_done);
+            }
+            continue;
+        }
         const int bu = o.bu, seg = 2 * bu / NM;
         const int kb = bu * 144 * kRowGroup, pitch = bu * 144;
         int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
@@ -602,32 +869,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             if (lane == 0) mbar_arrive(&empty[slot]);
             ucount += n;
             ++it;
-            if (st.last_in_group) {
-                const int bsel = gi & 1;
-                if (gi >= 2 && !*reinterpret_cast<volatile int *>(abort_flag)) {
-                    if (!mbar_wait(&red_empty[bsel], ((uint32_t)(gi >> 1) & 1u) ^ 1u, a.err, kErrWaitEmpty))
-                        *abort_flag = 1;
-                }
-                // the four threads of a row hold its limb / min-term shares: sum them, then
-                // thread t of group g stores row g + 8t
-                float *rb = red + bsel * kChainRed;
-#pragma unroll
-                for (int mat = 0; mat < 2; ++mat) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        acc[mat][j] += __shfl_xor_sync(0xffffffffu, acc[mat][j], 1);
-                        acc[mat][j] += __shfl_xor_sync(0xffffffffu, acc[mat][j], 2);
-                    }
-                    const int tq = lane & 3;
-                    const float mine = tq == 0 ? acc[mat][0] : tq == 1 ? acc[mat][1] : tq == 2 ? acc[mat][2] : acc[mat][3];
-                    rb[(cw * 2 + mat) * kRowGroup + (lane >> 2) + 8 * tq] = mine;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[mat][j] = 0.f;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&red_full[bsel]);
-                ++gi;
-            }
+            if (st.last_in_group) flush_group();
         }
     }
 }
@@ -639,7 +881,7 @@ using namespace ql;
 
 namespace ql {
 bool q4k_tensor_map_public(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes,
-                           int box_blocks);
+                           int box_blocks, int box_rows);
 int chain_workspace(float **part, unsigned **counters, int **err, int *sms);
 }
 
@@ -655,6 +897,7 @@ int chain_max_units_one_group() {
 
 struct Chain {
     ChainOp *ops_dev = nullptr;
+    void *mlp_mem = nullptr;             // fused MLP: fixed-point residuals, then pair-exchange cells
     unsigned long long *keys = nullptr;  // [nops] fused-argmax keys
     unsigned *done = nullptr;   // [nops] arrival counters, [nops] epoch, [nops+1 ..] argmax arrival counters
     unsigned *epoch = nullptr;
@@ -694,7 +937,44 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         memset(&o, 0, sizeof(o));
         const std::string what = "ql_gemv_chain_create: op " + std::to_string(p);
         if (q.quant_type != QL_Q4_K) return set_last_error(QL_EINVAL, (what + ": only Q4_K").c_str());
-        if (q.kind < QL_OP_STORE || q.kind > QL_OP_SWIGLU) return set_last_error(QL_EINVAL, (what + ": kind").c_str());
+        if (q.kind < QL_OP_STORE || q.kind > QL_OP_MLP) return set_last_error(QL_EINVAL, (what + ": kind").c_str());
+        if (q.kind == QL_OP_MLP) {
+            // y += down(SiLU(gate . x^) * (up . x^)), x^ = RMSNorm(x) when gamma is set
+            const int F = q.rows[0], blocks = q.in_dim > 0 ? q.in_dim / 256 : 0;
+            if (world != 1) return set_last_error(QL_EINVAL, (what + ": MLP ops run on one GPU (use SWIGLU + ADD)").c_str());
+            if (q.in_dim <= 0 || q.in_dim % 256 || !q.x || !q.y || q.bias || q.argmax_idx || q.reduce)
+                return set_last_error(QL_EINVAL, (what + ": MLP needs in_dim % 256 == 0, x and y, no bias/argmax").c_str());
+            if (F <= 0 || F % 256 || q.rows[1] != F || q.rows[2] < kRowGroup)
+                return set_last_error(QL_EINVAL, (what + ": MLP rows: gate = up = a multiple of 256, down >= 32").c_str());
+            if (reinterpret_cast<uintptr_t>(q.x) % 16 || reinterpret_cast<uintptr_t>(q.gamma) % 16)
+                return set_last_error(QL_EINVAL, (what + ": x and gamma must be 16-byte aligned").c_str());
+            for (int s = 0; s < 3; ++s) {
+                const int kb = s < 2 ? blocks : F / 256;
+                if (!q.w[s] || reinterpret_cast<uintptr_t>(q.w[s]) % 16 || q.row_bytes[s] % 16 ||
+                    q.row_bytes[s] < (size_t)kb * 144)
+                    return set_last_error(QL_EINVAL, (what + ": weights (16-byte aligned rows)").c_str());
+            }
+            o.bu = blocks < kTmaSeg ? blocks : kTmaSeg;
+            for (int s = 0; s < 2; ++s)
+                if (!q4k_tensor_map_public(&o.tmap[s], q.w[s], blocks, (uint64_t)F, q.row_bytes[s], o.bu, kRowGroup))
+                    return set_last_error(QL_ECUDA, (what + ": tensor map").c_str());
+            if (!q4k_tensor_map_public(&o.tmap[2], q.w[2], F / 256, (uint64_t)q.rows[2], q.row_bytes[2], 1, kMlpBoxRows))
+                return set_last_error(QL_ECUDA, (what + ": tensor map").c_str());
+            o.kind = kOpMlp;
+            o.nmat = 2;
+            o.rows = F;
+            o.K = q.in_dim;
+            o.U = blocks;
+            o.x = q.x;
+            o.gamma = q.gamma;
+            o.eps = q.eps;
+            o.y = q.y;
+            o.rows_d = q.rows[2];
+            o.half_rows = (q.rows[2] + 2 * kRowGroup - 1) / (2 * kRowGroup) * kRowGroup;
+            o.nunits = 2 * (F / 256);
+            if (q.in_dim > kmax) kmax = q.in_dim;
+            continue;
+        }
         const int nsrc = q.kind == QL_OP_SWIGLU ? 2 : q.nsrc;
         if (nsrc < 1 || nsrc > 3 || q.in_dim <= 0 || q.in_dim % 256 || !q.x || (!q.y && !q.argmax_idx))
             return set_last_error(QL_EINVAL, (what + ": sources, in_dim (a multiple of 256), x or y").c_str());
@@ -712,7 +992,7 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
                 return set_last_error(QL_EINVAL, (what + ": weights (16-byte aligned, >= 32 rows)").c_str());
             if (q.kind != QL_OP_SWIGLU && s < nsrc - 1 && q.rows[s] % kRowGroup)
                 return set_last_error(QL_EINVAL, (what + ": stacked sources but the last need multiples of 32 rows").c_str());
-            if (!q4k_tensor_map_public(&o.tmap[s], q.w[s], blocks, (uint64_t)q.rows[s], q.row_bytes[s], o.bu))
+            if (!q4k_tensor_map_public(&o.tmap[s], q.w[s], blocks, (uint64_t)q.rows[s], q.row_bytes[s], o.bu, kRowGroup))
                 return set_last_error(QL_ECUDA, (what + ": tensor map").c_str());
             if (q.kind != QL_OP_SWIGLU) {
                 total += q.rows[s];
@@ -750,12 +1030,44 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         }
         if (q.in_dim > kmax) kmax = q.in_dim;
     }
+    // fused MLP ops: the residual y in fixed point (int64, written by the last ADD into y before
+    // the MLP, accumulated by the MLP's atomics), read back by the next op, which also restores y
+    auto overlaps = [](const float *a0, int na, const float *b0, int nb) {
+        return a0 && b0 && a0 < b0 + nb && b0 < a0 + na;
+    };
+    std::vector<size_t> fixed_off(nops, 0), cell_off(nops, 0);
+    std::vector<int> seed(nops, -1);
+    size_t fixed_total = 0, cell_total = 0;
+    for (int p = 0; p < nops; ++p) {
+        ChainOp &o = h[p];
+        if (o.kind != kOpMlp) continue;
+        const std::string what = "ql_gemv_chain_create: MLP op " + std::to_string(p);
+        int q = p - 1;
+        while (q >= 0 && !(h[q].kind != kOpMlp && overlaps(h[q].y, h[q].rows, o.y, o.rows_d)) &&
+               !(h[q].kind == kOpMlp && overlaps(h[q].y, h[q].rows_d, o.y, o.rows_d)))
+            --q;
+        if (q < 0 || h[q].kind != kOpAdd || h[q].y != o.y || h[q].rows != o.rows_d || h[q].y_fixed)
+            return set_last_error(QL_EINVAL, (what + ": its residual y must be last written by an ADD op of the chain "
+                                                      "with the same y and rows").c_str());
+        if (p + 1 >= nops || h[p + 1].kind == kOpMlp ||
+            (h[p + 1].kind == kOpAdd && overlaps(h[p + 1].y, h[p + 1].rows, o.y, o.rows_d)))
+            return set_last_error(QL_EINVAL, (what + ": must be followed by a STORE or SWIGLU op, or an ADD into "
+                                                      "another buffer").c_str());
+        seed[p] = q;
+        fixed_off[p] = fixed_total;
+        fixed_total += (size_t)o.rows_d;
+        cell_off[p] = cell_total;
+        cell_total += (size_t)o.nunits * 128;
+    }
     // ADD ops may read their residual before op p-1 completes when no op since p-2 wrote it
     for (int p = 0; p < nops; ++p) {
         ChainOp &o = h[p];
         o.pre_y = 0;
         if (o.kind != kOpAdd) continue;
-        const bool prev_writes = p > 0 && h[p - 1].y && h[p - 1].y < o.y + o.rows && o.y < h[p - 1].y + h[p - 1].rows;
+        const bool prev_writes = p > 0 && (overlaps(h[p - 1].y, h[p - 1].rows, o.y, o.rows) ||
+                                           (h[p - 1].kind == kOpMlp && overlaps(h[p - 1].y, h[p - 1].rows_d, o.y, o.rows)) ||
+                                           (p >= 2 && h[p - 2].kind == kOpMlp &&
+                                            overlaps(h[p - 2].y, h[p - 2].rows_d, o.y, o.rows)));
         o.pre_y = prev_writes ? 0 : 1;
     }
     // exchange cells (tensor parallel): reduce ops [G][world][32], argmax ops [world][2]
@@ -769,7 +1081,30 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
     }
     Chain *c = new Chain();
     c->sms = sms;
-    cudaError_t e = cudaMalloc(&c->ops_dev, sizeof(ChainOp) * nops);
+    cudaError_t e = cudaSuccess;
+    if (fixed_total + cell_total) {
+        e = cudaMalloc(&c->mlp_mem, (fixed_total + cell_total) * 8);
+        if (e == cudaSuccess) e = cudaMemset(c->mlp_mem, 0, (fixed_total + cell_total) * 8);
+        if (e != cudaSuccess) {
+            delete c;
+            return set_last_error(QL_ECUDA, (std::string("ql_gemv_chain_create: ") + cudaGetErrorString(e)).c_str());
+        }
+        long long *fixed = static_cast<long long *>(c->mlp_mem);
+        for (int p = 0; p < nops; ++p) {
+            if (h[p].kind != kOpMlp) continue;
+            long long *yf = fixed + fixed_off[p];
+            h[p].y_fixed = yf;
+            h[p].cells = (long long)cell_off[p];
+            h[seed[p]].y_fixed = yf;
+            ChainOp &nx = h[p + 1];
+            nx.mat_src = yf;
+            nx.mat_dst = h[p].y;
+            nx.mat_rows = h[p].rows_d;
+            if (nx.x == h[p].y && nx.K <= h[p].rows_d) nx.x_fixed = yf;
+        }
+        c->args.mlp_cells = reinterpret_cast<unsigned long long *>(fixed + fixed_total);
+    }
+    e = cudaMalloc(&c->ops_dev, sizeof(ChainOp) * nops);
     // per-op argmax keys and arrival counter: one slot per op at the end of the counter block
     unsigned long long *keys = nullptr;
     if (e == cudaSuccess) e = cudaMalloc(&c->done, sizeof(unsigned) * (nops + 1) * 2);
@@ -790,6 +1125,7 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         if (c->ops_dev) cudaFree(c->ops_dev);
         if (c->done) cudaFree(c->done);
         if (keys) cudaFree(keys);
+        if (c->mlp_mem) cudaFree(c->mlp_mem);
         delete c;
         return set_last_error(QL_ECUDA, (std::string("ql_gemv_chain_create: ") + cudaGetErrorString(e)).c_str());
     }
@@ -798,6 +1134,7 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
     off += ((size_t)(kmax / 32) * 4 + 127) / 128 * 128;
     off += ((size_t)(kmax / 256) * 4 + 127) / 128 * 128;
     off += ((size_t)2 * kChainRed * 4 + 127) / 128 * 128;
+    off += kMlpSmem;
     off = (off + 1023) / 1024 * 1024;
     off += (size_t)kChainSlots * kSlotBytes;
     if (off > 227 * 1024) {
@@ -866,6 +1203,7 @@ int ql_gemv_chain_destroy(void *chain) {
     if (c->ops_dev) cudaFree(c->ops_dev);
     if (c->done) cudaFree(c->done);
     if (c->keys) cudaFree(c->keys);
+    if (c->mlp_mem) cudaFree(c->mlp_mem);
     delete c;
     return QL_OK;
 }

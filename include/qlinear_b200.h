@@ -115,6 +115,14 @@ QL_API int ql_quant_gemv_argmax_ex(int32_t quant_type, const uint8_t *weight, si
 #define QL_OP_STORE 0
 #define QL_OP_ADD 1
 #define QL_OP_SWIGLU 2
+/* MLP (one GPU): y += down . (SiLU(gate . x^) * (up . x^)), x^ = RMSNorm(x) with gamma, as SWIGLU
+ * then ADD in one op without the grid barrier between them: w[0] = gate, w[1] = up (rows[0] =
+ * rows[1] = FFN width, a multiple of 256), w[2] = down (rows[2] = len(y), in FFN blocks).  The
+ * down projection is split over the FFN (two SMs per 256-row chunk) and its partial sums are
+ * added in 64-bit fixed point (2^-32 resolution, |y| < 2^31; deterministic).  y must be last
+ * written by an ADD op of the chain (same y and rows), and the next op must not be an ADD into
+ * y or another MLP.  The SwiGLU activations are not stored. */
+#define QL_OP_MLP 3
 typedef struct ql_chain_op {
     int32_t kind;
     int32_t quant_type;

@@ -62,13 +62,17 @@ def _per_op(torch, layers, lm, lnf, rb, b):
     Q.quant_gemv_ex(O.Q4_K, lm.data_ptr(), rb(H), h, H, b["logits"].data_ptr(), V, V, H, 1, lnf.data_ptr(), EPS)
 
 
-def _chain_ops(layers, lm, lnf, rb, b, with_logits=True):
+def _chain_ops(layers, lm, lnf, rb, b, with_logits=True, mlp=False):
     h = b["h"].data_ptr()
     ops = []
     for L in layers:
         ops.append(Q.chain_op(Q.OP_STORE, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rb(H)] * 3,
                               [QW, KV, KV], H, h, b["qkv"].data_ptr(), L["ln1"].data_ptr(), EPS, L["b"].data_ptr()))
         ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [rb(QW)], [H], QW, b["qkv"].data_ptr(), h))
+        if mlp:  # gate/up SwiGLU and down + residual as one op (split over the FFN)
+            ops.append(Q.chain_op(Q.OP_MLP, [L["wg"].data_ptr(), L["wu"].data_ptr(), L["wd"].data_ptr()],
+                                  [rb(H), rb(H), rb(F)], [F, F, H], H, h, h, L["ln2"].data_ptr(), EPS))
+            continue
         ops.append(Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rb(H)] * 2, [F, F], H, h,
                               b["act"].data_ptr(), L["ln2"].data_ptr(), EPS))
         ops.append(Q.chain_op(Q.OP_ADD, [L["wd"].data_ptr()], [rb(F)], [H], F, b["act"].data_ptr(), h))
@@ -100,6 +104,42 @@ def test_chain_matches_per_op_launches():
         assert host(got["tok"])[0] == int(np.argmax(lg))
     finally:
         chain.close()
+
+
+def test_chain_fused_mlp_matches_per_op_launches():
+    import torch
+    layers, lm, lnf, rb = _stack(torch)
+    h0 = np.random.default_rng(8).standard_normal(H).astype(np.float32)
+    ref = _bufs(torch, h0)
+    _per_op(torch, layers, lm, lnf, rb, ref)
+    got = _bufs(torch, h0)
+    chain = Q.GemvChain(_chain_ops(layers, lm, lnf, rb, got, mlp=True))
+    try:
+        chain.run()
+        for k in ("qkv", "h", "logits"):
+            assert rel_l2(host(got[k]), host(ref[k])) < 1e-5, k
+        lg = host(got["logits"])
+        assert host(got["tok"])[0] == int(np.argmax(lg))
+        # the split-K partial sums add in fixed point: replays are bit-identical
+        for _ in range(3):
+            got["h"].copy_(dev(h0))
+            chain.run()
+        assert np.array_equal(host(got["logits"]).view(np.uint32), lg.view(np.uint32))
+    finally:
+        chain.close()
+
+
+def test_chain_fused_mlp_rejects_unseeded_residual():
+    import torch
+    layers, lm, lnf, rb = _stack(torch)
+    b = _bufs(torch, np.zeros(H, np.float32))
+    L = layers[0]
+    h = b["h"].data_ptr()
+    mlp = Q.chain_op(Q.OP_MLP, [L["wg"].data_ptr(), L["wu"].data_ptr(), L["wd"].data_ptr()], [rb(H), rb(H), rb(F)],
+                     [F, F, H], H, h, h, L["ln2"].data_ptr(), EPS)
+    lmop = Q.chain_op(Q.OP_STORE, [lm.data_ptr()], [rb(H)], [V], H, h, b["logits"].data_ptr(), lnf.data_ptr(), EPS)
+    with pytest.raises(Q.QLError):  # no ADD op of the chain wrote the residual first
+        Q.GemvChain([mlp, lmop])
 
 
 def test_chain_captured_in_graph():
