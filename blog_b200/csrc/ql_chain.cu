@@ -18,6 +18,7 @@
 //     SwiGLU, fused RMSNorm, fused greedy argmax) as the per-op kernels.
 // Arrival counters and the launch epoch are monotonic, so a CUDA graph can
 // replay the launch without resets.  Every wait is bounded.
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -31,7 +32,7 @@ int set_last_error(int code, const char *msg);
 
 namespace {
 
-constexpr int kChainSlots = 2;                       // ring slots of two 32 x (<= 7)-block boxes each
+constexpr int kChainSlots = 3;                       // most ring slots (two 32 x (<= 7)-block boxes each)
 constexpr int kBox = kTmaSeg * 144 * kRowGroup;      // 32,256 B: the largest box
 constexpr int kSlotBytes = 2 * kBox;
 constexpr int kMaxWorld = 8;
@@ -76,6 +77,11 @@ struct __align__(128) ChainOp {
     int nunits;             // MLP: 2 x (FFN rows / 256)
     long long cells;        // MLP: first pair-exchange cell ([nunits][128])
 };
+static_assert(sizeof(ChainOp) % 128 == 0, "descriptor copies stay 128-byte aligned");
+// Descriptor words copied to shared memory per op: everything after the tensor maps.  Reads of
+// the global copy after a grid barrier miss L1 (the barrier's acquire invalidates it).
+constexpr int kDescOff = offsetof(ChainOp, kind);
+constexpr int kDescWords = (int)(sizeof(ChainOp) - kDescOff) / 4;
 
 struct ChainArgs {
     const ChainOp *ops;
@@ -89,6 +95,7 @@ struct ChainArgs {
     unsigned long long *xchg[kMaxWorld];  // every rank's exchange cells (index = rank), mapped here
     int rank, world;
     unsigned long long *mlp_cells;  // fused MLP pair exchange (tagged 64-bit cells)
+    int nslots;                     // ring slots (2 or 3)
 };
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
@@ -283,6 +290,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     off += ((size_t)(a.kmax / 256) * 4 + 127) / 128 * 128;
     float *red = reinterpret_cast<float *>(smem + off);  // [2][W][2][32]
     off += ((size_t)2 * kChainRed * 4 + 127) / 128 * 128;
+    uint8_t *desc = smem + off;  // [2] copies of the current op's descriptor (all but the tensor maps)
+    off += 2 * sizeof(ChainOp);
     float *abuf = reinterpret_cast<float *>(smem + off);      // MLP: the chunk's 256 activations
     uint32_t *xa = reinterpret_cast<uint32_t *>(smem + off + 1024);  // ... as limbs
     float *xsa = reinterpret_cast<float *>(smem + off + 2048);        // ... sub-block sums, [8] then the scale
@@ -292,8 +301,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, cta = blockIdx.x;
+    const int NS = a.nslots;  // ring slots in use (3 when shared memory allows)
     if (tid == 0) {
-        for (int s = 0; s < kChainSlots; ++s) {
+        for (int s = 0; s < a.nslots; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], W);
         }
@@ -316,6 +326,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
         // ---------------------------- producer (TMA) ----------------------------
         if (lane != 0) return;
         int it = 0;
+        const uint64_t pol = l2_evict_first_policy();  // weights are read once per launch
         // waits for a free ring slot (and, past an op's first stage, for its activations)
         auto claim_slot = [&](int p, int sio) -> bool {
             if (sio == kChainPreX && *x_staged < (unsigned)(p + 1) && !*reinterpret_cast<volatile int *>(abort_flag)) {
@@ -329,61 +340,65 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     }
                 }
             }
-            const int slot = it % kChainSlots;
-            if (it >= kChainSlots && !*reinterpret_cast<volatile int *>(abort_flag)) {
-                if (!mbar_wait(&empty[slot], ((uint32_t)(it / kChainSlots) & 1u) ^ 1u, a.err, kErrWaitEmpty))
+            const int slot = it % NS;
+            if (it >= NS && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                if (!mbar_wait(&empty[slot], ((uint32_t)(it / NS) & 1u) ^ 1u, a.err, kErrWaitEmpty))
                     *abort_flag = 1;
             }
             return !*reinterpret_cast<volatile int *>(abort_flag);
         };
         for (int p = 0; p < a.nops; ++p) {
+            // the descriptor's scalars in registers: reloads after the waits below would miss L1
             const ChainOp &o = a.ops[p];
-            for (int i = 0; i < ((o.nmat == 2 && o.kind != kOpMlp) ? 2 : 3); ++i) tensormap_acquire(&o.tmap[i]);
-            if (o.kind == kOpMlp) {
+            const int kind = o.kind, nmat = o.nmat, bu = o.bu, U = o.U, split0 = o.split[0], split1 = o.split[1];
+            const int nunits = o.nunits, half_rows = o.half_rows, rows_d = o.rows_d;
+            const Plan plan = o.plan;
+            for (int i = 0; i < ((nmat == 2 && kind != kOpMlp) ? 2 : 3); ++i) tensormap_acquire(&o.tmap[i]);
+            if (kind == kOpMlp) {
                 // per unit: the half chunk's gate/up rows (4 row groups x all blocks), then the
                 // down projection's block column of the chunk over this half's rows
-                const uint32_t kb = (uint32_t)o.bu * 144u * kRowGroup;
+                const uint32_t kb = (uint32_t)bu * 144u * kRowGroup;
                 const int Ce = C & ~1;
                 int sio = 0;
-                for (int u = cta; cta < Ce && u < o.nunits; u += Ce) {
+                for (int u = cta; cta < Ce && u < nunits; u += Ce) {
                     const int ci = u >> 1, hh = u & 1;
                     for (int r = 0; r < 4; ++r)
-                        for (int us = 0; us < o.U; us += o.bu) {
+                        for (int us = 0; us < U; us += bu) {
                             const bool live = claim_slot(p, sio++);
-                            const int slot = it % kChainSlots;
+                            const int slot = it % NS;
                             uint8_t *sb = ring + (size_t)slot * kSlotBytes;
                             const int row0 = 256 * ci + 128 * hh + 32 * r;
                             mbar_arrive_expect_tx(&full[slot], live ? 2u * kb : 0u);
                             if (live) {
-                                tma_load_3d(sb, &o.tmap[0], 0, us, row0, &full[slot]);
-                                tma_load_3d(sb + kb, &o.tmap[1], 0, us, row0, &full[slot]);
+                                tma_load_3d_hint(sb, &o.tmap[0], 0, us, row0, &full[slot], pol);
+                                tma_load_3d_hint(sb + kb, &o.tmap[1], 0, us, row0, &full[slot], pol);
                             }
                             ++it;
                         }
-                    const int r_beg = hh ? o.half_rows : 0, r_end = hh ? o.rows_d : o.half_rows;
+                    const int r_beg = hh ? half_rows : 0, r_end = hh ? rows_d : half_rows;
                     for (int r = r_beg; r < r_end; r += 2 * kMlpBoxRows) {
                         const bool live = claim_slot(p, sio++);
-                        const int slot = it % kChainSlots;
+                        const int slot = it % NS;
                         uint8_t *sb = ring + (size_t)slot * kSlotBytes;
                         const int nbox = r + kMlpBoxRows < r_end ? 2 : 1;
                         mbar_arrive_expect_tx(&full[slot], live ? (uint32_t)(nbox * kBox) : 0u);
                         if (live) {
-                            tma_load_3d(sb, &o.tmap[2], 0, ci, r, &full[slot]);
-                            if (nbox == 2) tma_load_3d(sb + kBox, &o.tmap[2], 0, ci, r + kMlpBoxRows, &full[slot]);
+                            tma_load_3d_hint(sb, &o.tmap[2], 0, ci, r, &full[slot], pol);
+                            if (nbox == 2) tma_load_3d_hint(sb + kBox, &o.tmap[2], 0, ci, r + kMlpBoxRows, &full[slot], pol);
                         }
                         ++it;
                     }
                 }
                 continue;
             }
-            const int seg = 2 * o.bu / o.nmat;
-            const uint32_t kb = (uint32_t)o.bu * 144u * kRowGroup;
-            int64_t t = cta < o.plan.C ? plan_start(o.plan, cta) : 0;
-            const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
+            const int seg = 2 * bu / nmat;
+            const uint32_t kb = (uint32_t)bu * 144u * kRowGroup;
+            int64_t t = cta < plan.C ? plan_start(plan, cta) : 0;
+            const int64_t t1 = cta < plan.C ? plan_start(plan, cta + 1) : 0;
             Stage st;
             int sio = 0;  // stage index within the op
-            while (next_stage(t, t1, o.U, seg, 0, st)) {
-                const int slot = it % kChainSlots;
+            while (next_stage(t, t1, U, seg, 0, st)) {
+                const int slot = it % NS;
                 // Past the op's first stage, let the activation loads go first: TMA data queued
                 // ahead of them on the SM's inbound path would add its transfer time to their latency.
                 if (sio++ == kChainPreX && *x_staged < (unsigned)(p + 1) &&
@@ -398,34 +413,34 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                         }
                     }
                 }
-                if (it >= kChainSlots && !*reinterpret_cast<volatile int *>(abort_flag)) {
-                    if (!mbar_wait(&empty[slot], ((uint32_t)(it / kChainSlots) & 1u) ^ 1u, a.err, kErrWaitEmpty))
+                if (it >= NS && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                    if (!mbar_wait(&empty[slot], ((uint32_t)(it / NS) & 1u) ^ 1u, a.err, kErrWaitEmpty))
                         *abort_flag = 1;
                 }
                 const bool live = !*reinterpret_cast<volatile int *>(abort_flag);
                 uint8_t *sb = ring + (size_t)slot * kSlotBytes;
                 const int row0 = st.g * kRowGroup;
-                if (o.nmat == 2) {
+                if (nmat == 2) {
                     mbar_arrive_expect_tx(&full[slot], live ? 2u * kb : 0u);
                     if (live) {
-                        tma_load_3d(sb, &o.tmap[0], 0, st.us, row0, &full[slot]);
-                        tma_load_3d(sb + kb, &o.tmap[1], 0, st.us, row0, &full[slot]);
+                        tma_load_3d_hint(sb, &o.tmap[0], 0, st.us, row0, &full[slot], pol);
+                        tma_load_3d_hint(sb + kb, &o.tmap[1], 0, st.us, row0, &full[slot], pol);
                     }
                 } else {
-                    const int src = (row0 >= o.split[0]) + (row0 >= o.split[1]);
-                    const int lrow = row0 - (src == 0 ? 0 : o.split[src - 1]);
-                    const int nbox = st.ue - st.us > o.bu ? 2 : 1;
+                    const int src = (row0 >= split0) + (row0 >= split1);
+                    const int lrow = row0 - (src == 0 ? 0 : (src == 1 ? split0 : split1));
+                    const int nbox = st.ue - st.us > bu ? 2 : 1;
                     mbar_arrive_expect_tx(&full[slot], live ? (uint32_t)nbox * kb : 0u);
                     if (live) {
-                        tma_load_3d(sb, &o.tmap[src], 0, st.us, lrow, &full[slot]);
-                        if (nbox == 2) tma_load_3d(sb + kb, &o.tmap[src], 0, st.us + o.bu, lrow, &full[slot]);
+                        tma_load_3d_hint(sb, &o.tmap[src], 0, st.us, lrow, &full[slot], pol);
+                        if (nbox == 2) tma_load_3d_hint(sb + kb, &o.tmap[src], 0, st.us + bu, lrow, &full[slot], pol);
                     }
                 }
                 ++it;
             }
         }
-        for (int j = (it > kChainSlots ? it - kChainSlots : 0); j < it; ++j)
-            mbar_wait(&full[j % kChainSlots], (uint32_t)(j / kChainSlots) & 1u, nullptr, 0);
+        for (int j = (it > NS ? it - NS : 0); j < it; ++j)
+            mbar_wait(&full[j % NS], (uint32_t)(j / NS) & 1u, nullptr, 0);
         return;
     }
 
@@ -440,7 +455,28 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     *abort_flag = 1;
         };
         for (int p = 0; p < a.nops; ++p) {
-            const ChainOp &o = a.ops[p];
+            // the consumers copied op p's descriptor to shared memory before staging its activations
+            if (*x_staged < (unsigned)(p + 1) && !*reinterpret_cast<volatile int *>(abort_flag)) {
+                const uint64_t tw = global_timer_ns();
+                while (*x_staged < (unsigned)(p + 1)) {
+                    __nanosleep(32);
+                    if (global_timer_ns() - tw > 2000000000ull) {
+                        atomicExch(a.err, kErrWaitFull);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+            }
+            __threadfence_block();
+            __syncwarp();
+            const ChainOp &o = *reinterpret_cast<const ChainOp *>(desc + (p & 1) * sizeof(ChainOp));
+            // the op right after a fused MLP: the MLP's fixed-point residual back to fp32, a slice per
+            // CTA (the consumers of this op read the fixed-point copy; later ops read the fp32 one;
+            // the fence before this CTA's arrival on done[p] publishes it)
+            if (o.mat_src != nullptr) {
+                const int n0 = (int)((int64_t)o.mat_rows * cta / C), n1 = (int)((int64_t)o.mat_rows * (cta + 1) / C);
+                for (int n = n0 + lane; n < n1; n += 32) __stcg(o.mat_dst + n, from_fixed(__ldcg(o.mat_src + n)));
+            }
             if (o.kind == kOpMlp) {
                 const int Ce = C & ~1;
                 for (int u = cta; cta < Ce && u < o.nunits; u += Ce, ++mu) {
@@ -648,12 +684,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     const int ctid = tid - 32 * CW0;
     int it = 0, gi = 0, ucount = 0, mu = 0;
     for (int p = 0; p < a.nops; ++p) {
-        const ChainOp &o = a.ops[p];
-        const int K = o.K, U = o.U, NM = o.nmat;
-        // the RMSNorm weight does not depend on earlier ops: pull it into L2 while waiting
-        if (o.gamma != nullptr)
-            for (int i = ctid * 32; i < K; i += nthr * 32)
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(o.gamma + i));
+        {
+            // this op's descriptor into shared memory (loads issued before the barrier wait), and
+            // the RMSNorm weight, which does not depend on earlier ops, into L2
+            const ChainOp &og = a.ops[p];
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(reinterpret_cast<const uint8_t *>(&og) + kDescOff);
+            uint32_t *dst = reinterpret_cast<uint32_t *>(desc + (p & 1) * sizeof(ChainOp) + kDescOff);
+            for (int i = ctid; i < kDescWords; i += nthr) dst[i] = __ldg(src + i);
+            const float *gm = og.gamma;
+            const int Kg = og.K;
+            if (gm != nullptr)
+                for (int i = ctid * 32; i < Kg; i += nthr * 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(gm + i));
+        }
         // grid barrier: op p reads what op p-1 wrote
         if (p > 0) {
             if (ctid == 0 && !*reinterpret_cast<volatile int *>(abort_flag)) {
@@ -669,21 +711,17 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     }
                 }
             }
-            named_bar_sync(1, nthr);
         }
-        // the op right after a fused MLP: its fixed-point residual back to fp32, a slice per CTA
-        // (readers within this op use the fixed-point copy; later ops read the fp32 one)
-        if (o.mat_src != nullptr) {
-            const int n0 = (int)((int64_t)o.mat_rows * cta / C), n1 = (int)((int64_t)o.mat_rows * (cta + 1) / C);
-            for (int n = n0 + ctid; n < n1; n += nthr) __stcg(o.mat_dst + n, from_fixed(__ldcg(o.mat_src + n)));
-        }
+        named_bar_sync(1, nthr);
+        const ChainOp &o = *reinterpret_cast<const ChainOp *>(desc + (p & 1) * sizeof(ChainOp));
+        const int K = o.K, U = o.U, NM = o.nmat;
         // prologue: x' = x * g staged as limbs per 256-element block (see unit_q4k_imma), with the
         // sub-block sums of x' and the block scales; sum x^2 for a fused RMSNorm.  Warp cw stages
         // blocks cw, cw + W, ...: lane l holds elements 4l..4l+3 and 128+4l..128+4l+3 of a block.
         float ss = 0.f;
         {
             const int nb = K / 256;
-            constexpr int B = 6;
+            constexpr int B = 2;  // blocks per warp per pass (one pass for in_dim <= 7168)
             for (int b0 = cw; b0 < nb; b0 += B * W) {
                 float4 vv[B][2], gg[B][2];
 #pragma unroll
@@ -729,7 +767,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             if (lane == 0) ss_part[cw] = wsum;
         }
         named_bar_sync(1, nthr);
-        if (ctid == 0) *x_staged = (unsigned)(p + 1);  // the producer may issue the op's remaining stages
+        if (ctid == 0) {  // the producer may issue the op's remaining stages; the finisher may read the descriptor
+            __threadfence_block();
+            *x_staged = (unsigned)(p + 1);
+        }
         if (o.gamma != nullptr && cw == 0) {
             const float tsum = warp_sum(lane < W ? ss_part[lane] : 0.f);
             if (lane == 0) inv_rms[0] = rsqrtf(tsum / (float)K + o.eps);
@@ -767,7 +808,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             const int Ce = C & ~1;
             auto wait_full = [&](int slot) {
                 if (!*reinterpret_cast<volatile int *>(abort_flag) &&
-                    !mbar_wait(&full[slot], (uint32_t)(it / kChainSlots) & 1u, a.err, kErrWaitFull))
+                    !mbar_wait(&full[slot], (uint32_t)(it / NS) & 1u, a.err, kErrWaitFull))
                     *abort_flag = 1;
                 return !__any_sync(0xffffffffu, *reinterpret_cast<volatile int *>(abort_flag) != 0);
             };
@@ -776,7 +817,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                 // phase 1: gate/up of the half chunk (four row groups)
                 for (int r = 0; r < 4; ++r) {
                     for (int us = 0; us < U; us += bu) {
-                        const int slot = it % kChainSlots;
+                        const int slot = it % NS;
                         const int n = U - us < bu ? U - us : bu;
                         if (wait_full(slot)) {
                             const uint8_t *sb = ring + (size_t)slot * kSlotBytes;
@@ -800,7 +841,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     *abort_flag = 1;
                 const int r_beg = hh ? o.half_rows : 0, r_end = hh ? o.rows_d : o.half_rows;
                 for (int r = r_beg; r < r_end; r += 2 * kMlpBoxRows) {
-                    const int slot = it % kChainSlots;
+                    const int slot = it % NS;
                     const int span = r_end - r < 2 * kMlpBoxRows ? r_end - r : 2 * kMlpBoxRows;
                     const int n = (span + kRowGroup - 1) / kRowGroup;
                     if (wait_full(slot)) {
@@ -839,8 +880,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
         const int64_t t1 = cta < o.plan.C ? plan_start(o.plan, cta + 1) : 0;
         Stage st;
         while (next_stage(t, t1, U, seg, 0, st)) {
-            const int slot = it % kChainSlots;
-            const uint32_t ph = (uint32_t)(it / kChainSlots) & 1u;
+            const int slot = it % NS;
+            const uint32_t ph = (uint32_t)(it / NS) & 1u;
             if (!*reinterpret_cast<volatile int *>(abort_flag)) {
                 if (!mbar_wait(&full[slot], ph, a.err, kErrWaitFull)) *abort_flag = 1;
             }
@@ -1134,9 +1175,12 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
     off += ((size_t)(kmax / 32) * 4 + 127) / 128 * 128;
     off += ((size_t)(kmax / 256) * 4 + 127) / 128 * 128;
     off += ((size_t)2 * kChainRed * 4 + 127) / 128 * 128;
+    off += 2 * sizeof(ChainOp);
     off += kMlpSmem;
     off = (off + 1023) / 1024 * 1024;
-    off += (size_t)kChainSlots * kSlotBytes;
+    int nslots = kChainSlots;
+    while (nslots > 2 && off + (size_t)nslots * kSlotBytes > 227 * 1024) --nslots;
+    off += (size_t)nslots * kSlotBytes;
     if (off > 227 * 1024) {
         ql_gemv_chain_destroy(c);
         return set_last_error(QL_EINVAL, "ql_gemv_chain_create: in_dim too large for the shared-memory stage");
@@ -1152,6 +1196,7 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
     c->args.err = err;
     c->args.rank = rank;
     c->args.world = world;
+    c->args.nslots = nslots;
     for (int r = 0; r < world; ++r)
         c->args.xchg[r] = world > 1 ? static_cast<unsigned long long *>(exchange[r]) : nullptr;
     *chain = c;

@@ -77,16 +77,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
-// Test-and-sleep: the thread is suspended until the phase completes or ~0.1 ms pass
-// (the suspend-time hint), so waiting warps do not take issue slots from working ones.
+// Potentially blocking test: the hardware may suspend the thread until the phase completes
+// or a system-dependent time limit passes (measured marginally faster than a 0.1 ms hint).
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+        : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -120,6 +120,17 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int c0,
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
         "[%5];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// tma_load_3d with an L2 eviction-priority policy (e.g. evict-first for streamed weights, so
+// that they do not push the kernel's code, descriptors and activations out of L2).
+__device__ __forceinline__ void tma_load_3d_hint(void *dst, const void *tmap, int c0, int c1, int c2, uint64_t *bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
 
