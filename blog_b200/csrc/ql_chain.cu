@@ -64,6 +64,7 @@ struct __align__(128) ChainOp {
     int bu;                // blocks per TMA box: min(7, U); a stage holds two boxes (one per matrix for SwiGLU)
     int reduce;            // tensor parallel: y += (sum over ranks of this rank's W.x) through peer memory
     int pre_y;             // ADD: y's last writer is at least two ops back, so y may be read early
+    int pair;              // one matrix, many stages per CTA: consumers take the two boxes' blocks in pairs
     long long xchg;        // first exchange cell of this op (reduce: [G][world][32]; argmax: [world][2])
     // fused MLP (kOpMlp): tmap[0..1] gate/up, tmap[2] the down projection (box {144, 1, 224});
     // split-K over 256-row chunks of the FFN, two CTAs per chunk (one per 128-row half)
@@ -162,26 +163,30 @@ __device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1,
 // One Q4_K block (256 elements) of the 32 rows of a TMA box (row r at box[mat] + r * pitch),
 // against the staged limbs `xl` of that block (256 words), its sub-block sums `xs8` and its
 // scale `xe` = 2^(e_b - 24).  acc[mat][j]: this thread's partial sum of row g + 8j.
+// Matrix `mat` runs against activation block xl[mat]: the same block for gate/up, two blocks of one
+// row range when a single matrix's blocks are processed in pairs.
 template <int NM>
-__device__ __forceinline__ void unit_q4k_imma(const uint8_t *const (&box)[NM], int pitch, const uint32_t *xl,
-                                              const float *xs8, float xe, int lane, float (&acc)[NM][4]) {
+__device__ __forceinline__ void unit_q4k_imma(const uint8_t *const (&box)[NM], int pitch,
+                                              const uint32_t *const (&xl)[NM], const float *const (&xs8)[NM],
+                                              const float (&xe)[NM], int lane, float (&acc)[NM][4]) {
     const int g = lane >> 2, t = lane & 3;
     const int slot = (g < 6 && !(g & 1)) ? (g >> 1) : 3;
-    const float xw = xe * (t == 0 ? 16384.f : t == 1 ? 128.f : t == 2 ? 1.f : 0.f);
-    const float X0 = xs8[2 * t], X1 = xs8[2 * t + 1];
-    float dd[NM][4], mt[NM][4];
+    const float lw = t == 0 ? 16384.f : t == 1 ? 128.f : t == 2 ? 1.f : 0.f;
+    float dd[NM][4];
     uint32_t s03[NM][4], s47[NM][4];
 #pragma unroll
     for (int mat = 0; mat < NM; ++mat)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint4 h = *reinterpret_cast<const uint4 *>(box[mat] + (g + 8 * j) * pitch);
-            dd[mat][j] = half_bits_to_float(h.x) * xw;
+            const float X0 = xs8[mat][2 * t], X1 = xs8[mat][2 * t + 1];
+            dd[mat][j] = half_bits_to_float(h.x) * (xe[mat] * lw);
             s03[mat][j] = h.y & 0x3F3F3F3Fu;
             s47[mat][j] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
             const uint32_t mw = t < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
             const float2 mf = byte_pair_f(mw, 2 * (t & 1));
-            mt[mat][j] = half_bits_to_float(h.x >> 16) * fmaf(mf.x, X0, mf.y * X1);
+            // the min term goes into the accumulator right away (fewer live registers)
+            acc[mat][j] -= half_bits_to_float(h.x >> 16) * fmaf(mf.x, X0, mf.y * X1);
         }
     int te[NM][4], to[NM][4];
 #pragma unroll
@@ -190,10 +195,10 @@ __device__ __forceinline__ void unit_q4k_imma(const uint8_t *const (&box)[NM], i
         for (int j = 0; j < 4; ++j) te[mat][j] = to[mat][j] = 0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        const uint32_t *xq = xl + (8 * q + slot) * 8 + t;  // sub-block 2q; 2q+1 is 32 words on
-        const uint32_t b0e = xq[0], b1e = xq[4], b0o = xq[32], b1o = xq[36];
 #pragma unroll
-        for (int mat = 0; mat < NM; ++mat)
+        for (int mat = 0; mat < NM; ++mat) {
+            const uint32_t *xq = xl[mat] + (8 * q + slot) * 8 + t;  // sub-block 2q; 2q+1 is 32 words on
+            const uint32_t b0e = xq[0], b1e = xq[4], b0o = xq[32], b1o = xq[36];
 #pragma unroll
             for (int tile = 0; tile < 2; ++tile) {
                 const uint8_t *ra = box[mat] + (g + 16 * tile) * pitch + 16 + 32 * q + 4 * t;
@@ -213,12 +218,13 @@ __device__ __forceinline__ void unit_q4k_imma(const uint8_t *const (&box)[NM], i
                 to[mat][2 * tile] += (int)__byte_perm(sa, 0u, sel + 1u) * c[0];
                 to[mat][2 * tile + 1] += (int)__byte_perm(sb, 0u, sel + 1u) * c[2];
             }
+        }
     }
 #pragma unroll
     for (int mat = 0; mat < NM; ++mat)
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-            acc[mat][j] += fmaf(dd[mat][j], (float)(16 * te[mat][j] + to[mat][j]), -mt[mat][j]);
+            acc[mat][j] = fmaf(dd[mat][j], (float)(16 * te[mat][j] + to[mat][j]), acc[mat][j]);
 }
 
 // Packs byte 0 of each of four words.
@@ -824,7 +830,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                             for (int lu = ((cw - ucount) % W + W) % W; lu < n; lu += W) {
                                 const int b = us + lu;
                                 const uint8_t *bp[2] = {sb + lu * 144, sb + kb + lu * 144};
-                                unit_q4k_imma<2>(bp, pitch, xl + b * 256, xsum + b * 8, xe[b], lane, acc);
+                                const uint32_t *xp[2] = {xl + b * 256, xl + b * 256};
+                                const float *sp[2] = {xsum + b * 8, xsum + b * 8};
+                                const float ep[2] = {xe[b], xe[b]};
+                                unit_q4k_imma<2>(bp, pitch, xp, sp, ep, lane, acc);
                             }
                         }
                         __syncwarp();
@@ -849,7 +858,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                         for (int lu = ((cw - ucount) % W + W) % W; lu < n; lu += W) {
                             const uint8_t *bp[1] = {sb + (lu / kTmaSeg) * kBox + (lu % kTmaSeg) * kRowGroup * 144};
                             float pa[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-                            unit_q4k_imma<1>(bp, 144, xa, xsa, xsa[8], lane, pa);
+                            const uint32_t *xp[1] = {xa};
+                            const float *sp[1] = {xsa};
+                            const float ep[1] = {xsa[8]};
+                            unit_q4k_imma<1>(bp, 144, xp, sp, ep, lane, pa);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 pa[0][j] += __shfl_xor_sync(0xffffffffu, pa[0][j], 1);
@@ -886,21 +898,42 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                 if (!mbar_wait(&full[slot], ph, a.err, kErrWaitFull)) *abort_flag = 1;
             }
             const int n = st.ue - st.us;
+            // units: gate/up block pairs (NM = 2); for one matrix either single blocks, or (long ops,
+            // o.pair) the block pairs (j, j + bu) of the stage's two boxes -- same rows, two
+            // activation blocks, twice the independent work per warp
+            const bool pr = NM == 1 && o.pair;
+            const int nu = (pr && n > bu) ? bu : n;
             // warp-uniform (the tensor-core decoder is warp-collective); rows past the op's end
             // are zero-filled by the tensor map and never stored
             const bool aborted = __any_sync(0xffffffffu, *reinterpret_cast<volatile int *>(abort_flag) != 0);
             if (!aborted) {
                 const uint8_t *sb = ring + (size_t)slot * kSlotBytes;
                 const int first = ((cw - ucount) % W + W) % W;
-                for (int lu = first; lu < n; lu += W) {
+                for (int lu = first; lu < nu; lu += W) {
                     const int b = st.us + lu;
                     if (NM == 2) {
                         const uint8_t *bp[2] = {sb + lu * 144, sb + kb + lu * 144};
-                        unit_q4k_imma<2>(bp, pitch, xl + b * 256, xsum + b * 8, xe[b], lane, acc);
+                        const uint32_t *xp[2] = {xl + b * 256, xl + b * 256};
+                        const float *sp[2] = {xsum + b * 8, xsum + b * 8};
+                        const float ep[2] = {xe[b], xe[b]};
+                        unit_q4k_imma<2>(bp, pitch, xp, sp, ep, lane, acc);
+                    } else if (pr && lu + bu < n) {
+                        const int b2 = b + bu;  // same rows, the second box's block
+                        const uint8_t *bp[2] = {sb + lu * 144, sb + kb + lu * 144};
+                        const uint32_t *xp[2] = {xl + b * 256, xl + b2 * 256};
+                        const float *sp[2] = {xsum + b * 8, xsum + b2 * 8};
+                        const float ep[2] = {xe[b], xe[b2]};
+                        float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                        unit_q4k_imma<2>(bp, pitch, xp, sp, ep, lane, acc2);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[0][j] += acc2[0][j] + acc2[1][j];
                     } else {
                         const uint8_t *bp[1] = {sb + (lu / bu) * kb + (lu % bu) * 144};
+                        const uint32_t *xp[1] = {xl + b * 256};
+                        const float *sp[1] = {xsum + b * 8};
+                        const float ep[1] = {xe[b]};
                         float acc1[1][4] = {{acc[0][0], acc[0][1], acc[0][2], acc[0][3]}};
-                        unit_q4k_imma<1>(bp, pitch, xl + b * 256, xsum + b * 8, xe[b], lane, acc1);
+                        unit_q4k_imma<1>(bp, pitch, xp, sp, ep, lane, acc1);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) acc[0][j] = acc1[0][j];
                     }
@@ -908,7 +941,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            ucount += n;
+            ucount += nu;
             ++it;
             if (st.last_in_group) flush_group();
         }
@@ -932,6 +965,14 @@ int chain_max_units_one_group() {
     static const int v = [] {
         const char *e = getenv("QL_CHAIN_ONEGROUP");
         return e ? atoi(e) : 80;  // includes the down projection (74 blocks): measured faster than stream-K there
+    }();
+    return v;
+}
+
+bool chain_pair_enabled() {
+    static const bool v = [] {
+        const char *e = getenv("QL_CHAIN_PAIR");
+        return e ? atoi(e) != 0 : true;
     }();
     return v;
 }
@@ -1059,6 +1100,9 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         // group per CTA (no stream-K fix-ups, whose latency would sit on the chain's critical path)
         const int copt = (G <= sms && blocks <= chain_max_units_one_group()) ? G : sms;
         o.plan = Plan{(int64_t)G * blocks, G, blocks, copt};
+        // stream-K ops (several row groups per CTA, e.g. the LM head) are throughput-bound: pair the
+        // blocks; one-group-per-CTA ops are latency-bound and keep one block per warp
+        o.pair = (copt == sms && G > sms && chain_pair_enabled()) ? 1 : 0;
         o.x = q.x;
         o.gamma = q.gamma;
         o.eps = q.eps;
