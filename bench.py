@@ -867,8 +867,11 @@ def main():
         if r1["chain"]:
             # dominant kernel: the persistent chain launch = the whole step's weights and activations
             alg_bytes = r1["wbytes"] + r1["chain_act_bytes"]
-            kname, traffic = "gemv_chain_kernel (28 layers x {qkv, o, gate/up, down} + LM head/argmax)", \
-                profile_traffic("gemv_chain_qwen2_7b_q4k_decode.md")
+            if world == 1 and os.environ.get("QL_CHAIN_MLP", "1") != "0":
+                kname = "gemv_chain_kernel (28 layers x {qkv, o, fused MLP} + LM head/argmax)"
+                traffic = profile_traffic("gemv_chain_qwen2_7b_q4k_decode.md")
+            else:  # tensor parallel: SwiGLU + down as two ops per layer; the committed capture is one GPU's
+                kname, traffic = "gemv_chain_kernel (28 layers x {qkv, o, gate/up, down} + LM head/argmax)", None
         else:
             # dominant kernel: fused RMSNorm + gate/up SwiGLU GEMV (largest launch, 54% of weight bytes)
             alg_bytes = 2 * r1["f_len"] * HIDDEN * BPE + args.batch * HIDDEN * 4 * 2 + args.batch * r1["f_len"] * 4
