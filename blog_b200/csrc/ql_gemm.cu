@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
     if (threadIdx.x == 0) {
         for (int i = 0; i < kGemmNA; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < kGemmNB; ++i) { mbar_init(&b_full[i], 8); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < kGemmNR; ++i) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], 8); }
+        for (int i = 0; i < kGemmNR; ++i) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], kGemmDqWarps); }
         mbar_init(acc_full, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -209,8 +209,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Programmatic dependent launch: the weights do not depend on the previous kernel, so the
+    // producer starts the raw-weight ring before it waits; every thread that reads the previous
+    // kernel's output (activations, row scales, residual) waits first.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
@@ -222,12 +224,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                 row0 = n0 - (src > 0 ? a.src_end[src - 1] : 0);
             }
             int issued_r = 0, issued_a = 0;
-            for (int sl = 0; sl < nsbl && !*abort_flag; ++sl) {
+            auto load_raw = [&](int sl) {
                 const int rs = sl % kGemmNR;
-                if (sl >= kGemmNR && !mbar_wait(&r_empty[rs], (uint32_t)(sl / kGemmNR - 1) & 1u, a.err, kErrWaitEmpty)) {
-                    *abort_flag = 1;
-                    break;
-                }
                 mbar_arrive_expect_tx(&r_full[rs], kGemmRBytes);
                 if (EPI == kGemmSwiglu) {
                     tma_load_3d(sR + rs * kGemmRBytes, &a.tm_w[0], 0, s0 + sl, n0, &r_full[rs]);
@@ -236,6 +234,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                     tma_load_3d(sR + rs * kGemmRBytes, &a.tm_w[src], 0, s0 + sl, row0, &r_full[rs]);
                 }
                 issued_r = sl + 1;
+            };
+            const int early = nsbl < kGemmNR ? nsbl : kGemmNR;
+            for (int sl = 0; sl < early; ++sl) load_raw(sl);  // before the dependency wait
+            asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
+            for (int sl = 0; sl < nsbl && !*abort_flag; ++sl) {
+                const int rs = sl % kGemmNR;
+                if (sl >= kGemmNR) {
+                    if (!mbar_wait(&r_empty[rs], (uint32_t)(sl / kGemmNR - 1) & 1u, a.err, kErrWaitEmpty)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    load_raw(sl);
+                }
                 for (int p = 0; p < 4; ++p) {
                     const int c = 4 * sl + p, as = c % kGemmNA;
                     if (c >= kGemmNA &&
@@ -279,7 +290,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
         __syncwarp();
     } else {
         // ------------------ dequantizers, then the TMEM -> smem drain ------------------
-        const int r = threadIdx.x - 64;  // row of the 256-row weight tile
+        // row of the 256-row weight tile; with 16 dequantizer warps, two threads share a row and take
+        // alternate 64-element chunks, so that both ring slots fill at once (b_full still counts 8 warps)
+        const int r = (threadIdx.x - 64) & 255, pbeg = kGemmDqWarps == 16 ? ((threadIdx.x - 64) >> 8) : 0;
+        constexpr int pstep = kGemmDqWarps == 16 ? 2 : 1;
         for (int sl = 0; sl < nsbl; ++sl) {
             const int rs = sl % kGemmNR;
             // every wait's outcome is made warp-uniform: the warp-synchronous code below needs all lanes
@@ -297,7 +311,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
             const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
             bool ok = true;
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
+            for (int pp = 0; pp < 4 * 8 / kGemmDqWarps; ++pp) {
+                const int p = pbeg + pstep * pp;
                 const int c = 4 * sl + p, bs = c % kGemmNB;
                 if (c >= kGemmNB &&
                     !__all_sync(0xffffffffu, !*abort_flag && mbar_wait(&b_empty[bs], (uint32_t)(c / kGemmNB - 1) & 1u,
@@ -342,9 +357,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
 
         // Drain TMEM into the shared fp32 tile (row = accumulator lane).  The MMA
         // thread's completed acc_full also means every ring slot is idle.
-        const bool ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait(acc_full, 0u, a.err, kErrWaitFull));
+        const bool ok = warp < 10 && __all_sync(0xffffffffu, !*abort_flag && mbar_wait(acc_full, 0u, a.err, kErrWaitFull));
         tc_fence_after();
-        const int q = warp & 3, hcol = (warp - 2) >> 2;  // TMEM lane quadrant, column half
+        const int q = warp & 3, hcol = (warp - 2) >> 2;  // TMEM lane quadrant, column half (warps 2-9 drain)
         const int row = 32 * q + lane;
         if (ok) {
 #pragma unroll 1
@@ -369,6 +384,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
     }
 
     // ---- epilogue: sum the cluster's partial tiles (fixed order), scale, store ----
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // row scales, bias and residual of earlier kernels
     const int ks = a.ksplit;
     if (ks > 1) cluster_sync_all();
     const int z = ks > 1 ? (int)cluster_rank() : 0;

@@ -43,7 +43,8 @@ constexpr int kGemmBK = 64;    // K per pipeline chunk: one 128-byte swizzle row
 constexpr int kGemmNA = 4;     // activation chunk ring
 constexpr int kGemmNB = 2;     // dequantized weight chunk ring
 constexpr int kGemmNR = 2;     // raw super-block ring
-constexpr int kGemmThreads = 320;
+constexpr int kGemmDqWarps = 16;                         // dequantizer warps (8 or 16)
+constexpr int kGemmThreads = 64 + 32 * kGemmDqWarps;
 constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;  // 16 KB
 constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;  // 32 KB
 constexpr int kGemmRBytes = kGemmBN * 144;          // 36 KB
