@@ -127,6 +127,28 @@ __device__ __forceinline__ bool ld_cell(const unsigned long long *p, unsigned ta
     *payload = (uint32_t)v;
     return true;
 }
+// The same cells between CTAs of one GPU (the fused MLP's pair exchange): GPU scope, and a
+// tight bounded spin -- the partner finishes its phase 1 at about the same time.
+__device__ __forceinline__ void st_cell_gpu(unsigned long long *p, unsigned tag, uint32_t payload) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(((unsigned long long)tag << 32) | payload)
+                 : "memory");
+}
+__device__ __forceinline__ bool ld_cell_gpu(const unsigned long long *p, unsigned tag, uint32_t *payload, int *err) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    if ((unsigned)(v >> 32) != tag) {
+        const uint64_t t0 = global_timer_ns();
+        do {
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+            if (global_timer_ns() - t0 > 2000000000ull) {
+                atomicExch(err, kErrChainPeer);
+                return false;
+            }
+        } while ((unsigned)(v >> 32) != tag);
+    }
+    *payload = (uint32_t)v;
+    return true;
+}
 __device__ __forceinline__ void tensormap_acquire(const void *map) {
     asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
 }
@@ -488,6 +510,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                 for (int u = cta; cta < Ce && u < o.nunits; u += Ce, ++mu) {
                     const int hh = u & 1;
                     // phase 1: SwiGLU of the half chunk's four row groups -> smem and the pair's cells
+                    bool okc = true;
                     for (int r = 0; r < 4; ++r, ++gi) {
                         const int bsel = gi & 1;
                         if (!*reinterpret_cast<volatile int *>(abort_flag) &&
@@ -505,14 +528,20 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                         const float gv = gs * nrm, uv = us * nrm;
                         const float act = gv / (1.0f + expf(-gv)) * uv;
                         abuf[128 * hh + 32 * r + lane] = act;
-                        st_cell(a.mlp_cells + o.cells + (size_t)u * 128 + 32 * r + lane, tag, __float_as_uint(act));
+                        st_cell_gpu(a.mlp_cells + o.cells + (size_t)u * 128 + 32 * r + lane, tag, __float_as_uint(act));
+                        // the pair CTA's previous row group (it runs about in step): only its last group's
+                        // exchange latency remains after phase 1
+                        if (r > 0 && okc) {
+                            uint32_t bits = 0;
+                            okc = ld_cell_gpu(a.mlp_cells + o.cells + (size_t)(u ^ 1) * 128 + 32 * (r - 1) + lane, tag,
+                                              &bits, a.err);
+                            abuf[128 * (hh ^ 1) + 32 * (r - 1) + lane] = __uint_as_float(bits);
+                        }
                     }
-                    // the other half of the chunk from the pair CTA
-                    bool okc = true;
-                    for (int r = 0; r < 4 && okc; ++r) {
+                    if (okc) {
                         uint32_t bits = 0;
-                        okc = ld_cell(a.mlp_cells + o.cells + (size_t)(u ^ 1) * 128 + 32 * r + lane, tag, &bits, a.err);
-                        abuf[128 * (hh ^ 1) + 32 * r + lane] = __uint_as_float(bits);
+                        okc = ld_cell_gpu(a.mlp_cells + o.cells + (size_t)(u ^ 1) * 128 + 96 + lane, tag, &bits, a.err);
+                        abuf[128 * (hh ^ 1) + 96 + lane] = __uint_as_float(bits);
                     }
                     if (!__all_sync(0xffffffffu, okc)) *abort_flag = 1;
                     // the previous unit's consumers are done with the staged activations
