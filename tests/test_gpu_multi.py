@@ -77,7 +77,7 @@ def test_peer_allreduce_two_ranks():
         assert ok, (rank, info)
 
 
-def _tp_chain_worker(rank, world, port, q):
+def _tp_chain_worker(rank, world, port, q, mlp=False):
     import datetime
     import numpy as np
     import torch
@@ -135,6 +135,11 @@ def _tp_chain_worker(rank, world, port, q):
                                       1e-6, b.data_ptr()))
                 ops.append(Q.chain_op(Q.OP_ADD, [wo.data_ptr()], [rb(qhi - qlo)], [H], qhi - qlo, t["qkv"].data_ptr(),
                                       hp, reduce=red))
+                if mlp:  # gate/up + down as one op; with comm_world > 1 its partials are summed over ranks
+                    ops.append(Q.chain_op(Q.OP_MLP, [wg.data_ptr(), wu.data_ptr(), wd.data_ptr()],
+                                          [rb(H), rb(H), rb(fhi - flo)], [fhi - flo, fhi - flo, H], H, hp, hp,
+                                          g2.data_ptr(), 1e-6))
+                    continue
                 ops.append(Q.chain_op(Q.OP_SWIGLU, [wg.data_ptr(), wu.data_ptr()], [rb(H)] * 2, [fhi - flo] * 2, H, hp,
                                       t["act"].data_ptr(), g2.data_ptr(), 1e-6))
                 ops.append(Q.chain_op(Q.OP_ADD, [wd.data_ptr()], [rb(fhi - flo)], [H], fhi - flo, t["act"].data_ptr(),
@@ -160,11 +165,14 @@ def _tp_chain_worker(rank, world, port, q):
             torch.cuda.synchronize()
             res.append((t["h"].cpu().numpy().copy(), int(t["tok"].cpu()[0])))
         Q.check_device()
-        ok = all(np.array_equal(r[0].view(np.uint32), res[0][0].view(np.uint32)) and r[1] == res[0][1] for r in res)
+        ok_rep = all(np.array_equal(r[0].view(np.uint32), res[0][0].view(np.uint32)) and r[1] == res[0][1] for r in res)
         hs = [None] * world
         dist.all_gather_object(hs, (res[0][0], res[0][1]))
-        ok = ok and all(np.array_equal(x[0].view(np.uint32), hs[0][0].view(np.uint32)) and x[1] == hs[0][1] for x in hs)
-        info = "replicas agree" if ok else "replicas differ"
+        ok_rank = all(np.array_equal(x[0].view(np.uint32), hs[0][0].view(np.uint32)) and x[1] == hs[0][1] for x in hs)
+        ok = ok_rep and ok_rank
+        info = "replicas agree" if ok else (
+            f"replays differ: {[float(np.abs(r[0] - res[0][0]).max()) for r in res]}" if not ok_rep else
+            f"ranks differ: {[float(np.abs(x[0] - hs[0][0]).max()) for x in hs]}")
         if rank == 0 and ok:  # against the single-GPU chain with the whole matrices
             t1, ops1, keep1 = build(full, 0, QW, 0, KV, 0, F, 0, V, 1)
             c1 = Q.GemvChain(ops1)
@@ -185,7 +193,7 @@ def _tp_chain_worker(rank, world, port, q):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_tensor_parallel_chain_matches_single_gpu(world):
+def test_tensor_parallel_chain_matches_single_gpu(world, mlp=False):
     import torch
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -193,7 +201,7 @@ def test_tensor_parallel_chain_matches_single_gpu(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp_chain_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_tp_chain_worker, args=(r, world, port, q, mlp)) for r in range(world)]
     for p in procs:
         p.start()
     out = [q.get(timeout=300) for _ in procs]
