@@ -3,8 +3,8 @@
     python -m blog_b200.build          # or blog_b200.build.build()
 
 Objects go to blog_b200/_build/, the library to blog_b200/lib/.  The library
-links only the CUDA runtime (and NCCL for the tensor-parallel decode runner);
-it has no PyTorch dependency.
+links only the CUDA runtime (the tensor-parallel exchange runs over CUDA IPC
+peer memory inside the kernels); it has no PyTorch dependency.
 """
 from __future__ import annotations
 
@@ -60,7 +60,7 @@ def build(verbose: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
     if os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs):
         return LIB
-    cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lnccl"]
+    cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

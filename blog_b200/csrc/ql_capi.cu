@@ -32,13 +32,9 @@ cudaError_t rmsnorm_launch(const float *x, float *y, const float *gamma, int row
                            cudaStream_t s);
 cudaError_t synth_launch(int t, uint64_t seed, int64_t rows, int K, float std, uint8_t *dst, cudaStream_t s);
 
-bool gemv_pdl_enabled() {
-    static const bool on = [] {
-        const char *e = getenv("QL_PDL");
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
+// Programmatic dependent launch for the GEMV / GEMM kernels: a launch may start
+// streaming its weights while the previous kernel drains (always on).
+bool gemv_pdl_enabled() { return true; }
 
 namespace {
 
@@ -245,24 +241,11 @@ int check_act(const float *x, int64_t x_stride, const float *gamma, const char *
 
 // Weight stages a GEMV CTA issues before its activations are staged (the rest
 // wait, so the activation loads are not queued behind the weight stream).
-int gemv_pre_x() {
-    static const int v = [] {
-        const char *e = getenv("QL_GEMV_PRE");
-        return e ? atoi(e) : 1;
-    }();
-    return v;
-}
+int gemv_pre_x() { return 1; }
 
 // Most ring stages a GEMV CTA keeps in flight (2..4).  More stages than needed
 // to cover memory latency only lengthen the memory queues every other load waits in.
-int gemv_max_stages() {
-    static const int v = [] {
-        const char *e = getenv("QL_GEMV_NST");
-        int n = e ? atoi(e) : kGemvStages;
-        return n < 2 ? 2 : (n > kGemvStages ? kGemvStages : n);
-    }();
-    return v;
-}
+int gemv_max_stages() { return kGemvStages; }
 
 // Plans and launches the streaming GEMV engine over M tokens (chunks of <= 4).
 int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
@@ -339,13 +322,9 @@ int ensure_prefill(Workspace *ws, size_t tokens, size_t k) {
     return QL_OK;
 }
 
-int tc_min_tokens() {
-    static const int v = [] {
-        const char *e = getenv("QL_TC_MIN_M");
-        return e ? atoi(e) : 8;
-    }();
-    return v;
-}
+// Fewest tokens routed to the tensor-core GEMM by the automatic path selection;
+// below it the streaming GEMV engine (<= 4 tokens per weight pass) is faster.
+int tc_min_tokens() { return 8; }
 
 // One tensor-core GEMM launch pair: plain (1..3 stacked sources) or SwiGLU (gate, up).
 struct TcJob {
@@ -479,6 +458,8 @@ GemvArgs blank() {
 
 // Records `msg` as this thread's last error (for entry points in other files).
 int set_last_error(int code, const char *msg) { return fail(code, msg); }
+// Entry points defined in other files report their kernel launches here (ql_last_launch_count).
+void set_launch_count(int n) { t_launches = n; }
 
 // Q4_K tensor map with the GEMV ring's {144, 7, 32} box, for the chain kernel.
 bool q4k_tensor_map_public(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes,

@@ -989,22 +989,9 @@ int chain_workspace(float **part, unsigned **counters, int **err, int *sms);
 }
 
 namespace {
-// Reductions of at most this many blocks run one row group per CTA (QL_CHAIN_ONEGROUP overrides, for tuning).
-int chain_max_units_one_group() {
-    static const int v = [] {
-        const char *e = getenv("QL_CHAIN_ONEGROUP");
-        return e ? atoi(e) : 80;  // includes the down projection (74 blocks): measured faster than stream-K there
-    }();
-    return v;
-}
-
-bool chain_pair_enabled() {
-    static const bool v = [] {
-        const char *e = getenv("QL_CHAIN_PAIR");
-        return e ? atoi(e) != 0 : true;
-    }();
-    return v;
-}
+// Reductions of at most this many blocks run one row group per CTA.  80 includes the
+// down projection (74 blocks), measured faster than stream-K there.
+constexpr int kChainMaxUnitsOneGroup = 80;
 
 struct Chain {
     ChainOp *ops_dev = nullptr;
@@ -1127,11 +1114,11 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         const int G = (total + kRowGroup - 1) / kRowGroup;
         // like the per-op launcher: short reductions with at most one wave of row groups take one
         // group per CTA (no stream-K fix-ups, whose latency would sit on the chain's critical path)
-        const int copt = (G <= sms && blocks <= chain_max_units_one_group()) ? G : sms;
+        const int copt = (G <= sms && blocks <= kChainMaxUnitsOneGroup) ? G : sms;
         o.plan = Plan{(int64_t)G * blocks, G, blocks, copt};
         // stream-K ops (several row groups per CTA, e.g. the LM head) are throughput-bound: pair the
         // blocks; one-group-per-CTA ops are latency-bound and keep one block per warp
-        o.pair = (copt == sms && G > sms && chain_pair_enabled()) ? 1 : 0;
+        o.pair = (copt == sms && G > sms) ? 1 : 0;
         o.x = q.x;
         o.gamma = q.gamma;
         o.eps = q.eps;

@@ -76,7 +76,7 @@ struct GemmArgs {
     AmaxOut amax;          // fused greedy argmax over the output columns (plain; amax.amax null = off)
 };
 
-bool gemv_pdl_enabled();  // QL_PDL=0 turns programmatic dependent launch off
+bool gemv_pdl_enabled();  // programmatic dependent launch (always on)
 cudaError_t gemm_xprep_launch(const float *x, int64_t x_stride, const float *gamma, float eps, __half *xh,
                               float *rinv, int M, int K, cudaStream_t s);
 cudaError_t gemm_q4k_launch(const GemmArgs &a, int epi, cudaStream_t s);

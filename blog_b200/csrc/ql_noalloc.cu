@@ -4,9 +4,9 @@
 // Who needs it: ql_argmax keeps its block partials in the library workspace,
 // which the first call on a device allocates with cudaMalloc.  Some callers
 // cannot let a library allocate: a runtime whose device memory is all owned by
-// its own pool or budgeted up front, a caller that first reaches the argmax
-// while a CUDA graph is being captured (allocation is not a capturable
-// operation), or code running under a memory-allocation ban after start-up.
+// its own pool or budgeted up front (an inference server that sizes HBM for
+// weights and KV cache at start-up and treats any later cudaMalloc as a
+// fault), or code running under a memory-allocation ban after start-up.
 // This entry point keeps the same two-stage partials in a fixed 8 KB array in
 // the library's own device image instead, and never calls cudaMalloc, cudaFree
 // or an allocating library routine.
@@ -22,6 +22,10 @@
 //    resolves the array's device address with cudaGetSymbolAddress); make that
 //    first call before any stream capture.  Each device that loads the library
 //    holds the 8 KB until the process exits.
+//  * The resolved address is kept for the life of the process.  After
+//    cudaDeviceReset (or any teardown of the device's primary context) the
+//    library's device image is loaded again and the array may move: do not call
+//    this entry point on a device after resetting it.
 #include <mutex>
 
 #include "../../include/qlinear_b200.h"
@@ -30,6 +34,7 @@
 namespace ql {
 cudaError_t argmax_launch(const float *x, int n, int *out, float *pv, int *pi, int max_parts, cudaStream_t s);
 int set_last_error(int code, const char *msg);
+void set_launch_count(int n);
 
 namespace {
 constexpr int kNoAllocParts = 1024;
@@ -47,6 +52,7 @@ uint32_t *g_scratch_addr[kMaxDevices] = {};
 using namespace ql;
 
 extern "C" QL_API int ql_argmax_noalloc(const float *logits, int n, int *out_idx) {
+    set_launch_count(0);
     if (n <= 0 || !logits || !out_idx) return set_last_error(QL_EINVAL, "ql_argmax_noalloc: need n > 0 and non-null pointers");
     if (n > kNoAllocArgmaxMaxN)
         return set_last_error(QL_EINVAL, "ql_argmax_noalloc: n exceeds the no-allocation maximum of 16777216");
@@ -70,6 +76,7 @@ extern "C" QL_API int ql_argmax_noalloc(const float *logits, int n, int *out_idx
     float *pv = reinterpret_cast<float *>(scratch);
     int *pi = reinterpret_cast<int *>(scratch + kNoAllocParts);
     e = argmax_launch(logits, n, out_idx, pv, pi, kNoAllocParts, static_cast<cudaStream_t>(ql_get_stream()));
+    set_launch_count(2);
     if (e != cudaSuccess) return set_last_error(QL_ECUDA, cudaGetErrorString(e));
     return QL_OK;
 }

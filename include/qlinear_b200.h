@@ -226,12 +226,13 @@ QL_API int ql_argmax(const float *logits, int n, int *out_idx);
 
 /* Same result as ql_argmax, without ever allocating device memory.  No
  * counterpart in the reference.  For callers that cannot let a library call
- * cudaMalloc: memory owned entirely by the caller's pool, a first argmax that
- * happens during CUDA-graph capture, or an allocation ban after start-up.  The
- * partials live in a fixed 8 KB array inside the library's device image: n is
- * limited to 16,777,216 (larger n returns QL_EINVAL); calls that overlap on the
- * GPU race on the shared array; the first call on a device performs a one-time
- * set-up and should come before any stream capture. */
+ * cudaMalloc: a server whose HBM is owned by its own pool or budgeted once at
+ * start-up (weights, KV cache), or code under an allocation ban after start-up.
+ * The partials live in a fixed 8 KB array inside the library's device image: n
+ * is limited to 16,777,216 (larger n returns QL_EINVAL); calls that overlap on
+ * the GPU race on the shared array; the first call on a device performs a
+ * one-time set-up (resolving the array's address) and should come before any
+ * stream capture; do not use it on a device after cudaDeviceReset. */
 QL_API int ql_argmax_noalloc(const float *logits, int n, int *out_idx);
 
 /* ---- fused forms (no reference counterpart; fusions the reference runs as

@@ -9,7 +9,10 @@ import pytest
 import blog_b200 as Q
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = "/root/reference/AI/codes/local-llm/src"
+# the reference checkout (its local-llm directory): QL_REFERENCE_SRC, by default a
+# checkout of the reference repository next to this one
+REF = os.path.join(os.environ.get("QL_REFERENCE_SRC", os.path.join(os.path.dirname(ROOT), "reference", "AI", "codes",
+                                                                       "local-llm")), "src")
 
 
 @pytest.mark.skipif(not os.path.isdir(REF), reason="reference sources not present")

@@ -1,6 +1,6 @@
 """ql_argmax_noalloc: the argmax for callers that cannot let the library
-allocate device memory (a caller-owned memory pool, a first call during CUDA
-graph capture, an allocation ban after start-up).  It must return what
+allocate device memory (HBM owned by the caller's own pool or budgeted once at
+start-up, an allocation ban after start-up).  It must return what
 ql_argmax returns, call after call, through the C ABI.
 
 This file sorts last so that a run stopping at its first failure has run
@@ -32,6 +32,7 @@ def test_argmax_noalloc_matches_argmax_twice(n):
         a = torch.full((1,), -1, dtype=torch.int32, device="cuda")
         b = torch.full((1,), -2, dtype=torch.int32, device="cuda")
         assert L.ql_argmax_noalloc(x.data_ptr(), n, a.data_ptr()) == Q.QL_OK, L.ql_last_error()
+        assert L.ql_last_launch_count() == 2
         assert L.ql_argmax(x.data_ptr(), n, b.data_ptr()) == Q.QL_OK, L.ql_last_error()
         torch.cuda.synchronize()
         assert int(a.item()) == int(b.item())
