@@ -134,28 +134,41 @@ class DecodeStack:
         self.v_off, self.v_len = split_blocks(VOCAB, world, 32)[rank]
         g = torch.Generator(device="cpu").manual_seed(seed)
 
+        # Every rank's shard is a slice of the same full matrix (seeded by the matrix alone),
+        # so a one-GPU stack built with world = 1 holds exactly the matrices the ranks split.
         def synth(rows, k, tag):
             w = torch.empty((rows, rb(k)), dtype=torch.uint8, device=dev)
-            if rows:
-                Q.synth_quantized(QK, seed * 1000003 + tag * 7919 + rank, rows, k, 0.02, w.data_ptr())
+            Q.synth_quantized(QK, seed * 1000003 + tag * 7919, rows, k, 0.02, w.data_ptr())
             return w
 
+        def out_rows(rows, k, tag, lo, n):  # column parallel: this rank's output rows
+            return synth(rows, k, tag) if world == 1 else synth(rows, k, tag)[lo:lo + n].contiguous()
+
+        def in_blocks(rows, k, tag, lo, n):  # row parallel: this rank's input blocks of every row
+            return synth(rows, k, tag) if world == 1 else \
+                synth(rows, k, tag)[:, lo // 256 * 144:(lo + n) // 256 * 144].contiguous()
+
+        QWD, KVD = N_Q * HEAD, N_KV * HEAD
         self.layers = []
         for l in range(LAYERS):
+            ln1 = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev)
+            ln2 = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev)
+            b = 0.01 * torch.randn(QWD + 2 * KVD, generator=g)
+            bqkv = torch.cat([b[self.qo_off:self.qo_off + self.qo_len], b[QWD + self.kv_off:QWD + self.kv_off + self.kv_len],
+                              b[QWD + KVD + self.kv_off:QWD + KVD + self.kv_off + self.kv_len]]).to(dev)
             L = {
-                "wq": synth(self.qo_len, HIDDEN, 10 * l + 1),
-                "wk": synth(self.kv_len, HIDDEN, 10 * l + 2),
-                "wv": synth(self.kv_len, HIDDEN, 10 * l + 3),
-                "wo": synth(HIDDEN, self.qo_len, 10 * l + 4),
-                "wg": synth(self.f_len, HIDDEN, 10 * l + 5),
-                "wu": synth(self.f_len, HIDDEN, 10 * l + 6),
-                "wd": synth(HIDDEN, self.f_len, 10 * l + 7),
-                "ln1": (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev),
-                "ln2": (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev),
-                "bqkv": (0.01 * torch.randn(self.qo_len + 2 * self.kv_len, generator=g)).to(dev),
+                "wq": out_rows(QWD, HIDDEN, 10 * l + 1, self.qo_off, self.qo_len),
+                "wk": out_rows(KVD, HIDDEN, 10 * l + 2, self.kv_off, self.kv_len),
+                "wv": out_rows(KVD, HIDDEN, 10 * l + 3, self.kv_off, self.kv_len),
+                "wo": in_blocks(HIDDEN, QWD, 10 * l + 4, self.qo_off, self.qo_len),
+                "wg": out_rows(FFN, HIDDEN, 10 * l + 5, self.f_off, self.f_len),
+                "wu": out_rows(FFN, HIDDEN, 10 * l + 6, self.f_off, self.f_len),
+                "wd": in_blocks(HIDDEN, FFN, 10 * l + 7, self.f_off, self.f_len),
+                "ln1": ln1, "ln2": ln2, "bqkv": bqkv,
             }
             self.layers.append(L)
-        self.wlm = synth(self.v_len, HIDDEN, 999)
+        torch.cuda.empty_cache()
+        self.wlm = out_rows(VOCAB, HIDDEN, 999, self.v_off, self.v_len)
         self.lnf = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev)
         M = batch
         self.h = torch.zeros((M, HIDDEN), device=dev)
@@ -299,32 +312,85 @@ class DecodeStack:
 
 
 # --------------------------------------------------------------------------------------
-def cpu_oracle_rate(sample_layers=2, reps=2):
-    """Times the CPU oracle (double-accumulating restatement, OpenMP over rows)
-    on a bounded sample of the step: `sample_layers` decoder layers' linears plus
-    the LM head at full Qwen2-7B shape; returns tokens/s scaled to the full
-    step by weight bytes."""
-    import oracle as O
-    rb = O.row_bytes(O.Q4_K, HIDDEN)
-    mats = []
-    for l in range(sample_layers):
-        for n, k in ((N_Q * HEAD, HIDDEN), (N_KV * HEAD, HIDDEN), (N_KV * HEAD, HIDDEN), (HIDDEN, N_Q * HEAD),
-                     (FFN, HIDDEN), (FFN, HIDDEN), (HIDDEN, FFN)):
-            mats.append((n, k, O.quantize(O.Q4_K, O.randn(100 + len(mats), n * k, 0.02).reshape(n, k))))
-    mats.append((VOCAB, HIDDEN, O.quantize(O.Q4_K, O.randn(99, VOCAB * HIDDEN, 0.02).reshape(VOCAB, HIDDEN))))
-    sample_elems = sum(n * k for n, k, _ in mats)
-    x = {k: np.random.default_rng(k).standard_normal((1, k)).astype(np.float32) for k in (HIDDEN, FFN)}
-    best = float("inf")
-    for _ in range(reps):
+def bench_config(batch, world):
+    """The `config` object of every line this bench prints for the decode stack (both arms)."""
+    return {"workload": "qwen2-7b-q4k decode linear stack (28 x 7 linears + LM head), batch 1",
+            "weights": "random-init N(0,0.02) quantized to GGUF Q4_K",
+            "global_batch": batch, "parallelism": f"tp{world}",
+            "l2": f"each step streams {weight_elems() * BPE / 1e9:.2f} GB of weights (> 126 MB L2)"}
+
+
+class CpuReferenceStack:
+    """The Qwen2-7B-shape linear stack as host arrays for the CPU restatement of the
+    reference's arithmetic (oracle/, the reference has no CPU path): per layer q, k, v,
+    o, gate, up, down plus the LM head, every matrix its own memory.  Blocks are genuine
+    N(0, 0.02) Q4_K blocks: a pool quantized by the oracle, each matrix a seeded run of
+    it (values repeat across matrices, addresses do not, so nothing is cache-resident)."""
+
+    POOL_BLOCKS = 1 << 18
+
+    def __init__(self, layers=LAYERS, seed=0):
+        import oracle as O
+        self.O = O
+        pool = O.quantize(O.Q4_K, O.randn(seed + 11, self.POOL_BLOCKS * 256, 0.02).reshape(-1, 256))
+        rng = np.random.default_rng(seed)
+
+        def mat(rows, k):
+            nb = rows * (k // 256)
+            idx = (int(rng.integers(0, self.POOL_BLOCKS)) + np.arange(nb)) % self.POOL_BLOCKS
+            return np.take(pool, idx, axis=0).reshape(rows, (k // 256) * 144)
+        self.layers = []
+        for _ in range(layers):
+            self.layers.append({
+                "wq": mat(N_Q * HEAD, HIDDEN), "wk": mat(N_KV * HEAD, HIDDEN), "wv": mat(N_KV * HEAD, HIDDEN),
+                "wo": mat(HIDDEN, N_Q * HEAD), "wg": mat(FFN, HIDDEN), "wu": mat(FFN, HIDDEN), "wd": mat(HIDDEN, FFN),
+                "ln1": (1 + 0.1 * rng.standard_normal(HIDDEN)).astype(np.float32),
+                "ln2": (1 + 0.1 * rng.standard_normal(HIDDEN)).astype(np.float32),
+                "bqkv": (0.01 * rng.standard_normal((N_Q + 2 * N_KV) * HEAD)).astype(np.float32)})
+        self.lm = mat(VOCAB, HIDDEN)
+        self.lnf = (1 + 0.1 * rng.standard_normal(HIDDEN)).astype(np.float32)
+        self.h = rng.standard_normal(HIDDEN).astype(np.float32)
+
+    def elems(self, nl):
+        per_layer = HIDDEN * (N_Q * HEAD) + 2 * HIDDEN * (N_KV * HEAD) + (N_Q * HEAD) * HIDDEN + 3 * HIDDEN * FFN
+        return nl * per_layer + VOCAB * HIDDEN
+
+    def run(self, nl=None):
+        """The first `nl` layers (default all) and the LM head; returns the seconds taken.  Dot
+        products accumulate sequentially in double (oracle order 1), the faster of the oracle's
+        two CPU forms (the reference's lane-strided order runs ~1.6x slower on the host)."""
+        nl = len(self.layers) if nl is None else nl
         t0 = time.perf_counter()
-        for n, k, w in mats:
-            O.gemv(O.Q4_K, w, O.row_bytes(O.Q4_K, k), x[k], n, k, 1, order=1)
-        best = min(best, time.perf_counter() - t0)
-    full_s = best * weight_elems() / sample_elems
-    return {"value": 1.0 / full_s, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{sample_layers} of {LAYERS} layers' 7 linears + LM head at full shape, batch 1, "
-                      f"best of {reps}, scaled by weight bytes ({sample_elems / weight_elems():.3f} of a token)",
-            "seconds_per_sample": best}
+        self.O.linear_stack_token(self.layers[:nl], self.lm, self.lnf, self.h, order=1, with_logits=False)
+        return time.perf_counter() - t0
+
+
+def cpu_reference_steps(steps, warmup, budget_s=150.0):
+    """Times `warmup + steps` steps of the CPU restatement on all host cores.  A step is a
+    whole decode token (28 layers + LM head) unless that would take the run past
+    `budget_s`; then every step is the same prefix of the token (first n layers + LM head)
+    and the line says so.  Returns (tokens/s, seconds per step, info)."""
+    import oracle as O
+    O.set_threads(O.host_cores())
+    st = CpuReferenceStack()
+    full = st.elems(LAYERS)
+    t_tok = st.run()  # first warm-up step: a whole token
+    nl = LAYERS
+    if (steps + warmup) * t_tok > budget_s:
+        per_layer_s = t_tok * (st.elems(1) - st.elems(0)) / full
+        head_s = t_tok * st.elems(0) / full
+        nl = max(1, min(LAYERS, int((budget_s / (steps + warmup) - head_s) / per_layer_s)))
+    for _ in range(warmup - 1):
+        st.run(nl)
+    times = [st.run(nl) for _ in range(steps)]
+    sec = float(np.mean(times))
+    frac = st.elems(nl) / full
+    what = ("a whole token: 28 layers x 7 linears + LM head" if nl == LAYERS else
+            f"{nl} of 28 layers x 7 linears + LM head ({frac:.3f} of a token)")
+    info = {"cores": O.num_threads(), "kind": "port",
+            "sample": f"each step {what}, Qwen2-7B shapes, batch 1, Q4_K, OpenMP over rows; "
+                      f"mean of {steps} steps after {warmup} warm-up"}
+    return frac / sec, sec, info
 
 
 def profile_traffic(name="gemv_q4k_swiglu_18944x3584.md"):
@@ -649,25 +715,19 @@ def run_moe(args):
 
 
 def run_reference(args):
-    """--impl reference: the CPU restatement of the reference's arithmetic (the
-    reference's only implementation of this path is CUDA; it has no CPU path)."""
+    """--impl reference: the CPU restatement of the reference's arithmetic (the reference's
+    only implementation of this path is CUDA; it has no CPU path), whole decode tokens on
+    all host cores.  Under torchrun only rank 0 runs; the other ranks exit without work."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
-    rates = []
-    info = None
-    for i in range(args.warmup + args.steps):
-        info = cpu_oracle_rate(sample_layers=1, reps=1)
-        if i >= args.warmup:
-            rates.append(info["value"])
-    v = float(np.mean(rates))
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+    v, sec, info = cpu_reference_steps(args.steps, args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "qwen2-7b-q4k decode linear stack (28 x 7 linears + LM head), batch 1",
-                       "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
-                             "sample": "each step: " + info["sample"]},
+            "config": bench_config(args.batch, world),
+            "cpu_baseline": dict(info, value=v, unit="tokens/s"),
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -713,11 +773,37 @@ def main():
                                              timeout=datetime.timedelta(seconds=120))
     Q.init(local)
 
+    def tp_parity(stack, host_in):
+        """Tensor parallel only: one decode token through the sharded chain on every rank, then
+        on rank 0 the same token through a one-GPU chain over the unsplit matrices (the shards
+        are slices of them).  Returns the comparison (rank 0) or None."""
+        stack.h_in.copy_(host_in)
+        stack.step()
+        torch.cuda.synchronize()
+        h_tp, tok_tp = stack.h.double().cpu().numpy().ravel(), int(stack.token_ids.cpu()[0])
+        out = None
+        if rank == 0:
+            one = DecodeStack(Q, torch, 0, 1, 1)
+            one.h_in.copy_(host_in)
+            one.step()
+            torch.cuda.synchronize()
+            h1, tok1 = one.h.double().cpu().numpy().ravel(), int(one.token_ids.cpu()[0])
+            one.chain.close()
+            del one
+            torch.cuda.empty_cache()
+            err = float(np.linalg.norm(h_tp - h1) / np.linalg.norm(h1))
+            out = {"vs": "one-GPU chain over the unsplit matrices, same input", "h_rel_l2": err,
+                   "token_tp": tok_tp, "token_one_gpu": tok1, "ok": bool(err < 1e-4 and tok_tp == tok1)}
+        Q.check_device()
+        torch.distributed.barrier()
+        return out
+
     def measure(batch):
         stack = DecodeStack(Q, torch, rank, world, batch)
         s = torch.cuda.Stream()
         host_in = torch.randn((batch, HIDDEN), generator=torch.Generator().manual_seed(5)).pin_memory()
         host_out = torch.zeros((batch,), dtype=torch.int32).pin_memory()
+        parity = tp_parity(stack, host_in) if (world > 1 and stack.chain is not None) else None
         # event-record nodes inside the graph around the dominant kernel: the chain launch
         # (the whole step) or the gate/up SwiGLU launch of 4 layers
         evl = ["chain"] if stack.chain is not None else [3, 10, 17, 24]
@@ -773,7 +859,7 @@ def main():
         res = {"ms": float(t[0]), "e2e_ms": float(t[1]), "kernel_ms": float(t[2]), "clocks": clk.summary(),
                "chain": stack.chain is not None, "chain_act_bytes": stack.chain_act_bytes(),
                "launches": stack.launches_per_step(), "wbytes": stack.weight_bytes(),
-               "h2d": host_in.numel() * 4, "d2h": host_out.numel() * 4, "f_len": stack.f_len}
+               "h2d": host_in.numel() * 4, "d2h": host_out.numel() * 4, "f_len": stack.f_len, "parity": parity}
         del graph
         torch.cuda.synchronize()
         if world > 1:
@@ -881,10 +967,7 @@ def main():
             "metric": METRIC, "value": toks, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r1["ms"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "qwen2-7b-q4k decode linear stack (28 x 7 linears + LM head), batch 1",
-                       "weights": "random-init N(0,0.02) quantized to GGUF Q4_K on device",
-                       "global_batch": args.batch, "parallelism": f"tp{world}",
-                       "l2": f"each step streams {total_bytes / 1e9:.2f} GB of weights (> 126 MB L2)"},
+            "config": bench_config(args.batch, world),
             "hbm_roofline_tokens_per_s": hbm * 1e9 / (total_bytes / world),
             "step_weight_GBps": total_bytes / (r1["ms"] / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
@@ -896,6 +979,8 @@ def main():
             "gpu_launches": r1["launches"] * args.steps,
             "clocks": r1["clocks"],
         }
+        if r1["parity"] is not None:
+            line["tp_parity"] = r1["parity"]
         if r32 is not None:
             line["batch32"] = {"value": 32 / (r32["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r32["ms"],
                                "e2e_tokens_per_s": 32 / (r32["e2e_ms"] / 1e3)}
@@ -910,9 +995,8 @@ def main():
                                "path": "tcgen05 f16 x f16 -> f32 GEMM, Q4_K dequantized into shared memory",
                                "tensor_pipe_active": "see profiles/gemm_q4k_prefill_2048x18944x3584.md"}
         if world == 1 and not args.no_cpu_baseline:
-            cb = cpu_oracle_rate()
-            cb.pop("seconds_per_sample", None)
-            line["cpu_baseline"] = cb
+            v, _, info = cpu_reference_steps(2, 1, budget_s=30.0)
+            line["cpu_baseline"] = dict(info, value=v, unit="tokens/s")
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()

@@ -690,7 +690,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                                 st_cell(a.xchg[d] + o.xchg + 2 * a.rank + 1, tag, (uint32_t)k);
                             }
                             unsigned long long best = 0ull;
-                            for (int r = 0; r < a.world; ++r) {
+                            // after an abort (e.g. a peer that never arrived) no further peer waits
+                            for (int r = 0; r < a.world && !*reinterpret_cast<volatile int *>(abort_flag); ++r) {
                                 uint32_t hi = 0, lo = 0;
                                 if (!ld_cell(a.xchg[a.rank] + o.xchg + 2 * r, tag, &hi, a.err) ||
                                     !ld_cell(a.xchg[a.rank] + o.xchg + 2 * r + 1, tag, &lo, a.err)) {

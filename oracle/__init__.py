@@ -67,6 +67,7 @@ def lib():
             "orc_quantize_rows": (I, [I, P, I64, I, P]),
             "orc_randn": (None, [U64, U64, I64, F, P]),
             "orc_num_threads": (I, []),
+            "orc_set_num_threads": (None, [I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -188,6 +189,65 @@ def embedding(t, ids, table, rb, h):
 
 def num_threads() -> int:
     return int(lib().orc_num_threads())
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads of the oracle's loops (overrides OMP_NUM_THREADS)."""
+    lib().orc_set_num_threads(int(n))
+
+
+def host_cores() -> int:
+    """Cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------
+# One decode token of a Qwen2-style linear stack, restated on the CPU.
+#
+# The reference's decode step (DeepSeek/Qwen engines: LL/src/llm/module/*) is, per
+# layer, rms_norm (kernel.cu:112-147) -> q/k/v projections (+ bias) -> attention ->
+# o projection + residual add (kernel.cu:80-84) -> rms_norm -> gate/up SwiGLU
+# (quant_swiglu_kernel, kernel.cu:1288-1328) -> down projection + residual; then the
+# final rms_norm, the LM head and the greedy argmax (kernel.cu:3531-3592, strict '>'
+# as Sampler.cpp:24-50).  Attention is outside the quantized-linear path: its output
+# is stood in by the q projection (which has o_proj's input width).  Each layer is a
+# dict of quantized weights wq, wk, wv, wo, wg, wu, wd ([rows, row_bytes] uint8) and
+# float32 ln1, ln2, bqkv.
+# ----------------------------------------------------------------------------
+def linear_stack_token(layers, lm, lnf, h, t=Q4_K, eps=1e-6, order=1, with_logits=True):
+    """h (float32 [hidden]) -> (h after the stack, logits or None, greedy token)."""
+    h = np.array(h, np.float32, copy=True).reshape(1, -1)
+    H = h.shape[1]
+    for L in layers:
+        xn = rmsnorm(h, L["ln1"], eps)
+        parts = [gemv(t, L[n], L[n].shape[1], xn, L[n].shape[0], H, 1, order) for n in ("wq", "wk", "wv")]
+        qkv = np.concatenate(parts, axis=1) + np.asarray(L["bqkv"], np.float32)[None, :]
+        qw = L["wq"].shape[0]
+        h = gemv_add(t, L["wo"], L["wo"].shape[1], qkv[:, :qw], h[0], H, qw, order).reshape(1, -1)
+        xn = rmsnorm(h, L["ln2"], eps)
+        f = L["wg"].shape[0]
+        act = swiglu(t, L["wg"], L["wu"], L["wg"].shape[1], L["wu"].shape[1], xn, f, H, order)
+        h = gemv_add(t, L["wd"], L["wd"].shape[1], act, h[0], H, f, order).reshape(1, -1)
+    xn = rmsnorm(h, lnf, eps)
+    logits = gemv(t, lm, lm.shape[1], xn, lm.shape[0], H, 1, order)[0]
+    return h[0], (logits if with_logits else None), argmax(logits)
+
+
+def greedy_decode(layers, lm, lnf, table, first_token, steps, t=Q4_K, emb_type=Q4_K, eps=1e-6, order=1):
+    """Greedy loop: token -> quantized embedding row (quant_embedding_kernel, kernel.cu:2677-2693)
+    -> linear stack -> argmax -> next token.  Returns (tokens, per-step (best, runner-up) logit margins)."""
+    H = lm.shape[1] // BLOCK[t][1] * BLOCK[t][0]
+    tok, toks, margins = int(first_token), [], []
+    for _ in range(steps):
+        h = embedding(emb_type, np.array([tok], np.int32), table, table.shape[1], H)[0]
+        _, logits, tok = linear_stack_token(layers, lm, lnf, h, t, eps, order)
+        top2 = np.partition(logits, -2)[-2:]
+        toks.append(tok)
+        margins.append(float(top2[1] - top2[0]))
+    return toks, margins
 
 
 def f16_bits_to_f32(bits) -> np.ndarray:
