@@ -203,30 +203,38 @@ class DecodeStack:
                     torch.distributed.all_gather_object(out, hnd)
                     return out
             self.chain = Q.GemvChain(self.chain_ops(), rank, world, exchange)
+        elif world == 1 and 1 < M <= 32 and os.environ.get("QL_CHAIN", "1") != "0":
+            # batched decode: the whole stack for all M tokens as one persistent launch per step
+            self.chain = Q.GemvChain(self.chain_ops(batch=True), tokens=M)
         torch.cuda.synchronize()
 
-    def chain_ops(self):
+    def chain_ops(self, batch=False):
+        """The step's op list: one token (fused MLP on one GPU), or with batch=True the batched
+        chain's list over [M, *] activations (SwiGLU then down + residual)."""
         Q, rbh = self.Q, self.Q.row_bytes(QK, HIDDEN)
         h, ops = self.h.data_ptr(), []
+        st = (lambda xs, ys: {"x_stride": xs, "y_stride": ys}) if batch else (lambda xs, ys: {})
         for L in self.layers:
             ops.append(Q.chain_op(Q.OP_STORE, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
                                   [self.qo_len, self.kv_len, self.kv_len], HIDDEN, h, self.qkv.data_ptr(),
-                                  L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr()))
+                                  L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr(), **st(HIDDEN, self.qkv_w)))
             ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [Q.row_bytes(QK, self.qo_len)], [HIDDEN],
-                                  self.qo_len, self.qkv.data_ptr(), h, reduce=self.world > 1))
-            if self.world == 1 and os.environ.get("QL_CHAIN_MLP", "1") != "0":
+                                  self.qo_len, self.qkv.data_ptr(), h, reduce=self.world > 1, **st(self.qkv_w, HIDDEN)))
+            if self.world == 1 and not batch and os.environ.get("QL_CHAIN_MLP", "1") != "0":
                 # gate/up SwiGLU and down + residual as one op, split over the FFN (no barrier between)
                 ops.append(Q.chain_op(Q.OP_MLP, [L["wg"].data_ptr(), L["wu"].data_ptr(), L["wd"].data_ptr()],
                                       [rbh, rbh, Q.row_bytes(QK, self.f_len)], [self.f_len, self.f_len, HIDDEN],
                                       HIDDEN, h, h, L["ln2"].data_ptr(), EPS))
                 continue
             ops.append(Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rbh] * 2,
-                                  [self.f_len] * 2, HIDDEN, h, self.act.data_ptr(), L["ln2"].data_ptr(), EPS))
+                                  [self.f_len] * 2, HIDDEN, h, self.act.data_ptr(), L["ln2"].data_ptr(), EPS,
+                                  **st(HIDDEN, self.act.shape[1])))
             ops.append(Q.chain_op(Q.OP_ADD, [L["wd"].data_ptr()], [Q.row_bytes(QK, self.f_len)], [HIDDEN],
-                                  self.f_len, self.act.data_ptr(), h, reduce=self.world > 1))
+                                  self.f_len, self.act.data_ptr(), h, reduce=self.world > 1,
+                                  **st(self.act.shape[1], HIDDEN)))
         ops.append(Q.chain_op(Q.OP_STORE, [self.wlm.data_ptr()], [rbh], [self.v_len], HIDDEN, h,
                               self.logits.data_ptr(), self.lnf.data_ptr(), EPS, argmax_idx=self.tok.data_ptr(),
-                              argmax_offset=self.v_off))
+                              argmax_offset=self.v_off, **st(HIDDEN, self.v_len)))
         return ops
 
     def weight_bytes(self):
@@ -308,7 +316,7 @@ class DecodeStack:
     def chain_act_bytes(self):
         """Activation bytes the chain reads and writes per step (x in, y out, per op)."""
         per_layer = (HIDDEN + self.qkv_w) + (self.qo_len + HIDDEN) + (HIDDEN + self.f_len) + (self.f_len + HIDDEN)
-        return 4 * (LAYERS * per_layer + HIDDEN + self.v_len)
+        return 4 * self.M * (LAYERS * per_layer + HIDDEN + self.v_len)
 
 
 # --------------------------------------------------------------------------------------
@@ -1005,7 +1013,17 @@ def main():
             line["tp_parity"] = r1["parity"]
         if r32 is not None:
             line["batch32"] = {"value": 32 / (r32["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r32["ms"],
-                               "e2e_tokens_per_s": 32 / (r32["e2e_ms"] / 1e3)}
+                               "e2e_tokens_per_s": 32 / (r32["e2e_ms"] / 1e3),
+                               "hbm_roofline_tokens_per_s": 32 * hbm * 1e9 / (total_bytes / world),
+                               "launches_per_step": r32["launches"]}
+            if r32["chain"]:
+                ab = r32["wbytes"] + r32["chain_act_bytes"]
+                ach = ab / (r32["kernel_ms"] / 1e3) / 1e9
+                line["batch32"]["roofline"] = {
+                    "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                    "kernel": "bchain_kernel (batched chain: 28 layers x {qkv, o, gate/up, down} + LM head/argmax, "
+                              "32 tokens, mma.sync f16)",
+                    "algorithmic_bytes_per_launch": ab, "avg_launch_ms": r32["kernel_ms"]}
         if rp is not None:
             tf = rp["flops"] / (rp["ms"] / 1e3) / 1e12
             pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(

@@ -71,6 +71,7 @@ SIGNATURES = {
     "ql_gemv_chain_create": (I, [P, I, C.POINTER(C.c_void_p)]),
     "ql_gemv_chain_exchange_bytes": (SZ, [P, I, I]),
     "ql_gemv_chain_create_tp": (I, [P, I, I, I, P, C.POINTER(C.c_void_p)]),
+    "ql_gemv_chain_create_batch": (I, [P, I, I, C.POINTER(C.c_void_p)]),
     "ql_ipc_alloc": (I, [SZ, C.POINTER(C.c_void_p), C.c_char_p]),
     "ql_ipc_free": (I, [P]),
     "ql_ipc_open": (I, [C.c_char_p, C.POINTER(C.c_void_p)]),
@@ -196,17 +197,18 @@ class ChainOp(C.Structure):
                 ("w", C.c_void_p * 3), ("row_bytes", C.c_size_t * 3), ("rows", C.c_int32 * 3),
                 ("in_dim", C.c_int32), ("x", C.c_void_p), ("gamma", C.c_void_p), ("eps", C.c_float),
                 ("bias", C.c_void_p), ("y", C.c_void_p), ("argmax_idx", C.c_void_p), ("argmax_offset", C.c_int32),
-                ("reduce", C.c_int32)]
+                ("reduce", C.c_int32), ("x_stride", C.c_int64), ("y_stride", C.c_int64)]
 
 
 def chain_op(kind, weights, row_bytes, rows, in_dim, x, y, gamma=None, eps=0.0, bias=None, argmax_idx=None,
-             argmax_offset=0, quant_type=Q4_K, reduce=False):
+             argmax_offset=0, quant_type=Q4_K, reduce=False, x_stride=0, y_stride=0):
     op = ChainOp()
     op.kind, op.quant_type, op.nsrc, op.in_dim = kind, quant_type, len(weights), in_dim
     for i, (w, rb, r) in enumerate(zip(weights, row_bytes, rows)):
         op.w[i], op.row_bytes[i], op.rows[i] = w, rb, r
     op.x, op.y, op.gamma, op.eps, op.bias = x, y, gamma, eps, bias
     op.argmax_idx, op.argmax_offset, op.reduce = argmax_idx, argmax_offset, 1 if reduce else 0
+    op.x_stride, op.y_stride = x_stride, y_stride
     return op
 
 
@@ -217,11 +219,14 @@ class GemvChain:
     order` (any host channel, e.g. torch.distributed.all_gather_object); ops with reduce=True
     then sum their partials over ranks inside the kernel through peer memory."""
 
-    def __init__(self, ops, rank=0, world=1, exchange_handles=None):
+    def __init__(self, ops, rank=0, world=1, exchange_handles=None, tokens=None):
+        """tokens=None: the one-token chain; tokens=M (1..32): the batched chain over M tokens."""
         arr = (ChainOp * len(ops))(*ops)
         h = C.c_void_p()
         self.own, self.mapped = None, []
-        if world == 1:
+        if tokens is not None:
+            _call("ql_gemv_chain_create_batch", C.cast(arr, C.c_void_p), len(ops), tokens, C.byref(h))
+        elif world == 1:
             _call("ql_gemv_chain_create", C.cast(arr, C.c_void_p), len(ops), C.byref(h))
         else:
             nbytes = lib().ql_gemv_chain_exchange_bytes(C.cast(arr, C.c_void_p), len(ops), world)

@@ -462,6 +462,8 @@ int set_last_error(int code, const char *msg) { return fail(code, msg); }
 void set_launch_count(int n) { t_launches = n; }
 
 // Q4_K tensor map with the GEMV ring's {144, 7, 32} box, for the chain kernel.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder_public() { return tensor_map_encoder(); }
+
 bool q4k_tensor_map_public(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes,
                            int box_blocks, int box_rows) {
     return q4k_tensor_map(out, base, blocks, rows, row_bytes, box_blocks, box_rows);

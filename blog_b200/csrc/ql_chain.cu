@@ -987,6 +987,9 @@ namespace ql {
 bool q4k_tensor_map_public(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t rows, size_t row_bytes,
                            int box_blocks, int box_rows);
 int chain_workspace(float **part, unsigned **counters, int **err, int *sms);
+bool bchain_is(void *chain);
+int bchain_run(void *chain, cudaStream_t s);
+int bchain_destroy(void *chain);
 }
 
 namespace {
@@ -995,6 +998,7 @@ namespace {
 constexpr int kChainMaxUnitsOneGroup = 80;
 
 struct Chain {
+    int magic = 0x43484e31;  // the batched chain (ql_bchain.cu) starts with a different magic word
     ChainOp *ops_dev = nullptr;
     void *mlp_mem = nullptr;             // fused MLP: fixed-point residuals, then pair-exchange cells
     unsigned long long *keys = nullptr;  // [nops] fused-argmax keys
@@ -1281,6 +1285,7 @@ int ql_gemv_chain_create_tp(const ql_chain_op *ops, int nops, int rank, int worl
 int ql_gemv_chain_run(void *chain) {
     Chain *c = static_cast<Chain *>(chain);
     if (!c) return set_last_error(QL_EINVAL, "ql_gemv_chain_run: null chain");
+    if (bchain_is(chain)) return bchain_run(chain, static_cast<cudaStream_t>(ql_get_stream()));
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -1305,6 +1310,7 @@ int ql_gemv_chain_run(void *chain) {
 int ql_gemv_chain_destroy(void *chain) {
     Chain *c = static_cast<Chain *>(chain);
     if (!c) return QL_OK;
+    if (bchain_is(chain)) return bchain_destroy(chain);
     cudaDeviceSynchronize();
     if (c->ops_dev) cudaFree(c->ops_dev);
     if (c->done) cudaFree(c->done);

@@ -46,7 +46,7 @@ enum EpiKind : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2 };
 constexpr int kGemvThreads = 512;
 __host__ __device__ constexpr int gemv_producer_warps(bool tma) { return tma ? 1 : 4; }
 __host__ __device__ constexpr int gemv_consumer_warps(bool tma) { return 16 - gemv_producer_warps(tma) - 1; }
-// Programmatic dependent launch on by default; QL_PDL=0 turns it off.
+// Programmatic dependent launch (always on).
 bool gemv_pdl_enabled();
 constexpr int kGemvStages = 4;  // most stages (the host may pick fewer to fit shared memory)
 constexpr int kGemvMaxTokens = 4;

@@ -139,6 +139,10 @@ typedef struct ql_chain_op {
     int *argmax_idx;
     int32_t argmax_offset;
     int32_t reduce; /* tensor parallel ADD: y += sum over ranks of this op's partial (no bias) */
+    /* batched chains only (ql_gemv_chain_create_batch): floats between consecutive tokens' rows of
+     * x and of y; 0 = rows packed (in_dim, resp. the op's total output rows) */
+    int64_t x_stride;
+    int64_t y_stride;
 } ql_chain_op;
 QL_API int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain);
 /* Tensor-parallel chain: ops with reduce != 0 (row-parallel ADD projections) sum their
@@ -157,6 +161,15 @@ QL_API int ql_ipc_alloc(size_t bytes, void **ptr, uint8_t *handle);
 QL_API int ql_ipc_free(void *ptr);
 QL_API int ql_ipc_open(const uint8_t *handle, void **ptr);
 QL_API int ql_ipc_close(void *ptr);
+/* Batched chain (no reference twin; the reference runs batched decode as quant_matmul_kernel,
+ * kernel.cu:1253-1279, one warp per (token, row) on the CUDA cores): the same op list for
+ * `tokens` (1..32) tokens in one persistent launch on the tensor cores.  x and y are [tokens, *]
+ * row-major with the ops' x_stride / y_stride; RMSNorm, bias, residual add and SwiGLU apply per
+ * token; an argmax op writes one index per token (argmax_idx[0..tokens)).  Kinds STORE, ADD,
+ * SWIGLU (no MLP, no tensor-parallel reduce); Q4_K; stacked sources but the last a multiple of
+ * 128 rows; x rows 16-byte aligned.  Weights and x * gamma are rounded to f16 (|x * gamma| <
+ * 65504), accumulation is fp32.  ql_gemv_chain_run / ql_gemv_chain_destroy run and free it. */
+QL_API int ql_gemv_chain_create_batch(const ql_chain_op *ops, int nops, int tokens, void **chain);
 QL_API int ql_gemv_chain_run(void *chain);
 QL_API int ql_gemv_chain_destroy(void *chain);
 

@@ -236,6 +236,36 @@ def linear_stack_token(layers, lm, lnf, h, t=Q4_K, eps=1e-6, order=1, with_logit
     return h[0], (logits if with_logits else None), argmax(logits)
 
 
+def _dq(t, w, k, chunk=16384):
+    """Exact dequantized rows (float64), in row chunks to bound memory."""
+    rb = w.shape[1]
+    out = np.empty((w.shape[0], k), np.float64)
+    for r0 in range(0, w.shape[0], chunk):
+        out[r0:r0 + chunk] = dequant_rows(t, w[r0:r0 + chunk], k, rb)
+    return out
+
+
+def linear_stack_batch(layers, lm, lnf, h, t=Q4_K, eps=1e-6):
+    """linear_stack_token for a batch of tokens (h: [M, hidden]): the same steps with the exact
+    dequantized weights and float64 accumulation (numpy matmul).  Returns (h, logits [M, vocab])."""
+    h = np.array(h, np.float64, copy=True)
+    H = h.shape[1]
+
+    def norm(x, g):
+        return x / np.sqrt(np.mean(x * x, axis=1, keepdims=True) + eps) * np.asarray(g, np.float64)
+    for L in layers:
+        xn = norm(h, L["ln1"])
+        qkv = np.concatenate([xn @ _dq(t, L[n], H).T for n in ("wq", "wk", "wv")], axis=1) + L["bqkv"]
+        qw = L["wq"].shape[0]
+        h = h + qkv[:, :qw] @ _dq(t, L["wo"], qw).T
+        xn = norm(h, L["ln2"])
+        gv, uv = xn @ _dq(t, L["wg"], H).T, xn @ _dq(t, L["wu"], H).T
+        h = h + (gv / (1 + np.exp(-gv)) * uv) @ _dq(t, L["wd"], L["wg"].shape[0]).T
+    xn = norm(h, lnf)
+    logits = np.concatenate([xn @ _dq(t, lm[r0:r0 + 16384], H).T for r0 in range(0, lm.shape[0], 16384)], axis=1)
+    return h, logits
+
+
 def greedy_decode(layers, lm, lnf, table, first_token, steps, t=Q4_K, emb_type=Q4_K, eps=1e-6, order=1):
     """Greedy loop: token -> quantized embedding row (quant_embedding_kernel, kernel.cu:2677-2693)
     -> linear stack -> argmax -> next token.  Returns (tokens, per-step (best, runner-up) logit margins)."""

@@ -58,3 +58,13 @@ def test_greedy_decode_follows_embedding_rows():
         _, lg = _numpy_token(layers, lm, lnf, h)
         tok = int(np.argmax(lg))
         assert tok == want
+
+
+def test_linear_stack_batch_matches_per_token():
+    layers, lm, lnf, _ = _model()
+    hb = np.random.default_rng(6).standard_normal((3, H)).astype(np.float32)
+    h, lg = O.linear_stack_batch(layers, lm, lnf, hb)
+    for i in range(3):
+        h1, lg1 = _numpy_token(layers, lm, lnf, hb[i])
+        assert np.allclose(h[i], h1, rtol=1e-12, atol=1e-12)
+        assert np.allclose(lg[i], lg1, rtol=1e-12, atol=1e-12)
