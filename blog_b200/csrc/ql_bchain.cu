@@ -165,6 +165,10 @@ __device__ __forceinline__ uint32_t q4k_ab(const uint4 &h, int j) {
     return pack_h2(d * (float)sc, -dmin * (float)m);
 }
 __device__ __forceinline__ long long ss_to_fixed(float v) { return __float2ll_rn(v * (float)kSsFix); }
+// Stream-K split of an op's T units over min(C, T) CTAs (every participating CTA gets at least
+// one unit, so every CTA whose range touches a tile arrives on that tile's counter).
+__device__ __forceinline__ int op_ctas(int64_t T, int C) { return T < C ? (int)T : C; }
+__device__ __forceinline__ int64_t op_start(int64_t T, int Cp, int c) { return c >= Cp ? T : (int64_t)c * T / Cp; }
 
 __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_constant__ BArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -214,7 +218,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             const int U = o.U, nmat = o.nmat, split0 = o.split0, split1 = o.split1;
             const int64_t T = o.T;
             for (int i = 0; i < 3; ++i) tmap_acquire(&o.wmap[i]);
-            const int64_t u0 = (int64_t)cta * T / C, u1 = (int64_t)(cta + 1) * T / C;
+            const int Cp = op_ctas(T, C);
+            const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
             for (int64_t u = u0; u < u1; ++u, ++it) {
                 const int slot = it % kBWSlots;
                 if (it >= kBWSlots && !aborted() &&
@@ -265,7 +270,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             // the activations were written by generic-proxy stores; the tensor copies read them
             asm volatile("fence.proxy.async.global;" ::: "memory");
             tmap_acquire(&o.xmap);
-            const int64_t u0 = (int64_t)cta * T / C, u1 = (int64_t)(cta + 1) * T / C;
+            const int Cp = op_ctas(T, C);
+            const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
             for (int64_t u = u0; u < u1; ++u, ++it) {
                 const int slot = it % kBXSlots;
                 if (it >= kBXSlots && !aborted() &&
@@ -292,7 +298,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         const int kind = o.kind, U = o.U, rows = o.rows, K = o.K;
         const int64_t T = o.T;
         const float *gamma = o.gamma;
-        const int64_t u0 = (int64_t)cta * T / C, u1 = (int64_t)(cta + 1) * T / C;
+        const int Cp = op_ctas(T, C);
+            const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
         bool norm_ready = false;
         const bool track = o.amax.amax != nullptr || o.ss_out >= 0;
         // per-warp running results over the tiles this CTA finishes (greedy keys, sums of squares),
@@ -455,7 +462,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                 for (int i = 0; i < 16; ++i) __stcg(pp + (16 * th + i) * kBRows + r, v[i]);
                 __threadfence();
                 named_bar_sync(1, kBCw * 32);
-                const int cf = (int)(((ts + 1) * (int64_t)C - 1) / T), cl = (int)((te * (int64_t)C - 1) / T);
+                const int cf = (int)(((ts + 1) * (int64_t)Cp - 1) / T), cl = (int)((te * (int64_t)Cp - 1) / T);
                 if (ctid == 0) *bcast = (int)atomicAdd(&a.counters[tile], 1u) == cl - cf;
                 named_bar_sync(1, kBCw * 32);
                 finish = *bcast != 0;
@@ -464,7 +471,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = 0.f;
                     for (int c = cf; c <= cl; ++c) {
-                        const int sj = (tile == (int)((int64_t)c * T / C / U)) ? 0 : 1;
+                        const int sj = (tile == (int)(op_start(T, Cp, c) / U)) ? 0 : 1;
                         const float *qp = a.part + ((size_t)c * 2 + sj) * (kBMaxTok * kBRows);
 #pragma unroll
                         for (int i = 0; i < 16; ++i) v[i] += __ldcg(qp + (16 * th + i) * kBRows + r);
