@@ -455,8 +455,9 @@ def run_prefill_kernel(args):
 
 
 def run_chain_kernel(args):
-    """Times the persistent chain launch (batch 1, one GPU) on a stack of --layers decoder
-    layers + LM head: the ncu target for the decode step (fewer layers keep the capture small)."""
+    """Times the persistent chain launch (one GPU) on a stack of --layers decoder layers + LM
+    head: the ncu target for the decode step (fewer layers keep the capture small).  --kernel-only
+    chain is the one-token chain, bchain the batched chain over --batch tokens."""
     global LAYERS
     import torch
     import blog_b200 as Q
@@ -466,7 +467,7 @@ def run_chain_kernel(args):
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         Q.set_stream(s.cuda_stream)
-        st = DecodeStack(Q, torch, 0, 1, 1)
+        st = DecodeStack(Q, torch, 0, 1, args.batch if args.kernel_only == "bchain" else 1)
         for _ in range(args.warmup):
             st.step()
         torch.cuda.synchronize()
@@ -479,7 +480,7 @@ def run_chain_kernel(args):
     Q.check_device()
     us = e0.elapsed_time(e1) * 1000 / args.steps
     wb = st.weight_bytes()
-    print(json.dumps({"kernel_only": "chain", "layers": LAYERS, "avg_us": us, "weight_bytes": wb,
+    print(json.dumps({"kernel_only": args.kernel_only, "tokens": st.M, "layers": LAYERS, "avg_us": us, "weight_bytes": wb,
                       "act_bytes": st.chain_act_bytes(), "GBps": wb / us / 1e3, "launches": args.steps}), flush=True)
     st.chain.close()
     return 0
@@ -493,7 +494,7 @@ def run_kernel_only(args):
     import blog_b200 as Q
     if args.kernel_only.startswith("prefill_"):
         return run_prefill_kernel(args)
-    if args.kernel_only == "chain":
+    if args.kernel_only in ("chain", "bchain"):
         return run_chain_kernel(args)
     torch.cuda.init()
     Q.init(0)
@@ -755,7 +756,7 @@ def main():
     ap.add_argument("--moe", action="store_true", help="DeepSeek-V2-Lite-shape MoE decode, expert parallel")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
-                                              "prefill_qkv", "prefill_o", "chain"],
+                                              "prefill_qkv", "prefill_o", "chain", "bchain"],
                     help="time one kernel of the step at its bench shape (profiling target)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers for --kernel-only chain")
