@@ -74,7 +74,9 @@ constexpr int kBOffW = kBHdr;
 constexpr int kBOffX = kBOffW + kBWSlots * kBWBytes;     // 1024-byte aligned (128-byte swizzle)
 constexpr int kBOffRed = kBOffX + kBXSlots * kBXBytes;
 constexpr int kBOffMisc = kBOffRed + kBRedBytes;         // per-warp token reductions
-constexpr int kBSmem = kBOffMisc + 2 * kBCw * kBMaxTok * 8;
+constexpr int kBOffGamma = kBOffMisc + 2 * kBCw * kBMaxTok * 8;  // the op's RMSNorm weight
+constexpr int kBGammaMax = 4096;                         // inputs whose RMSNorm weight is staged
+constexpr int kBSmem = kBOffGamma + kBGammaMax * 4;
 static_assert(kBOffX % 1024 == 0, "activation ring must be 1024-byte aligned");
 static_assert(kBSmem <= 227 * 1024, "shared memory");
 constexpr int kErrBarrier = 5;
@@ -183,6 +185,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
     float *red = reinterpret_cast<float *>(smem + kBOffRed);          // [4 chunks][32 tokens][132]
     unsigned long long *wkey = reinterpret_cast<unsigned long long *>(smem + kBOffMisc);  // [8][32]
     float *wss = reinterpret_cast<float *>(smem + kBOffMisc + kBCw * kBMaxTok * 8);        // [8][32]
+    float *gsm = reinterpret_cast<float *>(smem + kBOffGamma);        // [K] RMSNorm weight of the op
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, cta = blockIdx.x;
@@ -301,6 +304,15 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         const int Cp = op_ctas(T, C);
             const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
         bool norm_ready = false;
+        // the RMSNorm weight (a weight: it does not depend on earlier ops) into shared memory once
+        // per op, so the k-steps read it at shared-memory latency
+        const bool gstaged = gamma != nullptr && K <= kBGammaMax;
+        if (gstaged && u0 < u1) {
+            for (int i = ctid; i < K / 4; i += kBCw * 32)
+                reinterpret_cast<float4 *>(gsm)[i] = __ldg(reinterpret_cast<const float4 *>(gamma) + i);
+        }
+        named_bar_sync(1, kBCw * 32);
+        const float *gk = gstaged ? gsm : gamma;
         const bool track = o.amax.amax != nullptr || o.ss_out >= 0;
         // per-warp running results over the tiles this CTA finishes (greedy keys, sums of squares),
         // each slot written by one lane only: deterministic
@@ -360,7 +372,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                         // B fragments: tokens 8n + g, inputs 16j + 4t .. +3 of sub-block sb (swizzled)
                         float4 gm = make_float4(1.f, 1.f, 1.f, 1.f);
                         if (gamma != nullptr)
-                            gm = __ldg(reinterpret_cast<const float4 *>(gamma + 256 * blk + 32 * sb + 16 * j + 4 * t));
+                            gm = *reinterpret_cast<const float4 *>(gk + 256 * blk + 32 * sb + 16 * j + 4 * t);
                         uint32_t bf[4][2];
 #pragma unroll
                         for (int n = 0; n < 4; ++n) {
