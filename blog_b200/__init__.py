@@ -86,6 +86,23 @@ SIGNATURES = {
     "ql_comm_step": (I, [P]),
     "ql_rms_norm_f32": (I, [P, P, P, I, I, F]),
     "ql_synth_quantized": (I, [I32, U64, I64, I, F, P]),
+    "ql_gguf_open": (I, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "ql_gguf_close": (I, [P]),
+    "ql_gguf_version": (I, [P]),
+    "ql_gguf_tensor_count": (I64, [P]),
+    "ql_gguf_find_tensor": (I64, [P, C.c_char_p]),
+    "ql_gguf_tensor_info": (I, [P, I64, C.POINTER(C.c_char_p), C.POINTER(C.c_int32), C.POINTER(C.c_int32), P,
+                                C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]),
+    "ql_gguf_metadata_type": (I, [P, C.c_char_p]),
+    "ql_gguf_metadata_int": (I, [P, C.c_char_p, C.POINTER(C.c_int64)]),
+    "ql_gguf_metadata_float": (I, [P, C.c_char_p, C.POINTER(C.c_double)]),
+    "ql_gguf_metadata_string": (I, [P, C.c_char_p, C.POINTER(C.c_char_p)]),
+    "ql_gguf_metadata_array_len": (I64, [P, C.c_char_p]),
+    "ql_gguf_metadata_array_int": (I, [P, C.c_char_p, I64, C.POINTER(C.c_int64)]),
+    "ql_gguf_metadata_array_float": (I, [P, C.c_char_p, I64, C.POINTER(C.c_double)]),
+    "ql_gguf_metadata_array_string": (I, [P, C.c_char_p, I64, C.POINTER(C.c_char_p)]),
+    "ql_gguf_validate": (I, [P]),
+    "ql_weight_upload": (I, [P, SZ, I64, I64, SZ, SZ, P]),
     "ql_row_bytes": (SZ, [I32, I]),
     "ql_last_launch_count": (I, []),
 }
@@ -328,6 +345,11 @@ def rms_norm_f32(x, y, gamma, rows, hidden, eps):
 
 def synth_quantized(t, seed, rows, in_dim, std, dst):
     _call("ql_synth_quantized", t, seed, rows, in_dim, std, dst)
+
+
+def weight_upload(host_ptr, row_bytes, row0, nrows, byte0, nbytes_per_row, dst):
+    """Host GGUF rows (a matrix or a tensor-parallel shard of it) to device memory (ql_weight_upload)."""
+    _call("ql_weight_upload", host_ptr, row_bytes, row0, nrows, byte0, nbytes_per_row, dst)
 
 
 def last_launch_count() -> int:

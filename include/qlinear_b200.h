@@ -270,6 +270,47 @@ QL_API int ql_quant_swiglu_ex(int32_t quant_type, const uint8_t *gate_weight, co
 /* y = x * rsqrt(mean(x^2) + eps) * gamma (gamma f32, may be NULL), rows x hidden. */
 QL_API int ql_rms_norm_f32(const float *x, float *y, const float *gamma, int rows, int hidden, float eps);
 
+/* ---- GGUF loader (reference GgufFile, src/format/gguf/GgufFile.cpp:152-250, and
+ *      MF::validate, src/format/MF.cpp:43-84) --------------------------------------
+ * ql_gguf_open maps a GGUF v2/v3 file read-only and parses its metadata and tensor table
+ * (QL_EINVAL with a message on any format error; every length is checked against the file).
+ * Tensor shapes are reported outermost-first (the file stores dims innermost-first); data
+ * points into the mapping (host memory, valid until ql_gguf_close); nbytes follows the ggml
+ * block traits.  The data section starts at the end of the tensor table rounded up to
+ * general.alignment (default 32).  ql_gguf_find_tensor returns the index or -1.
+ * ql_gguf_metadata_type returns the GGUF value type (0..12) or -1 when the key is absent;
+ * integer, bool and float values convert between the int and float getters.
+ * ql_gguf_validate applies MF::validate's container checks (tensors present, names non-empty
+ * and unique, shapes non-empty with positive dims, data present) and admits the types this
+ * library computes with: F32, F16, BF16, Q4_0, Q4_K, Q5_0, Q6_K, Q8_0 (the reference's
+ * validator leaves Q4_0 out although its parser reads it). */
+QL_API int ql_gguf_open(const char *path, void **file);
+QL_API int ql_gguf_close(void *file);
+QL_API int ql_gguf_version(void *file);
+QL_API int64_t ql_gguf_tensor_count(void *file);
+QL_API int64_t ql_gguf_find_tensor(void *file, const char *name);
+QL_API int ql_gguf_tensor_info(void *file, int64_t index, const char **name, int32_t *quant_type, int32_t *n_dims,
+                               int64_t *shape /* [8] */, const uint8_t **data, size_t *nbytes);
+QL_API int ql_gguf_metadata_type(void *file, const char *key);
+QL_API int ql_gguf_metadata_int(void *file, const char *key, int64_t *out);
+QL_API int ql_gguf_metadata_float(void *file, const char *key, double *out);
+QL_API int ql_gguf_metadata_string(void *file, const char *key, const char **out);
+QL_API int64_t ql_gguf_metadata_array_len(void *file, const char *key);
+QL_API int ql_gguf_metadata_array_int(void *file, const char *key, int64_t index, int64_t *out);
+QL_API int ql_gguf_metadata_array_float(void *file, const char *key, int64_t index, double *out);
+QL_API int ql_gguf_metadata_array_string(void *file, const char *key, int64_t index, const char **out);
+QL_API int ql_gguf_validate(void *file);
+/* Weight upload (reference CudaWeightPool::cached_weight, CudaWeightPool.cpp:119-175, which
+ * uploads the raw blocks unchanged): copies rows [row0, row0 + nrows) of a host matrix whose
+ * rows are row_bytes apart, bytes [byte0, byte0 + nbytes_per_row) of each row, to dst (device,
+ * rows packed nbytes_per_row apart), as one pitched copy on the current stream.  A whole matrix
+ * is byte0 = 0, nbytes_per_row = row_bytes; a column-parallel shard a row range; a row-parallel
+ * shard whole blocks of every row (byte0 and nbytes_per_row multiples of the block bytes).  The
+ * kernels read the raw GGUF layout, so no repack is needed.  Pinned host memory makes the copy
+ * asynchronous; pageable memory makes it synchronous. */
+QL_API int ql_weight_upload(const uint8_t *host, size_t row_bytes, int64_t row0, int64_t nrows, size_t byte0,
+                            size_t nbytes_per_row, uint8_t *dst);
+
 /* ---- synthetic weights (benchmarks; no reference counterpart) -------------------- */
 /* dst[rows x row_bytes] = quantize(N(0, std) with seed), generated on the device. */
 QL_API int ql_synth_quantized(int32_t quant_type, uint64_t seed, int64_t rows, int in_dim, float std, uint8_t *dst);
