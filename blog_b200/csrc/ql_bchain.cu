@@ -20,13 +20,14 @@
 //     4-slot ring as far ahead as the ring allows, across op boundaries (weights do not depend on
 //     activations).  Warp 1 waits for the op's grid barrier and then streams the unit's activations,
 //     fp32 [tokens][256], as a 128-byte-swizzled TMA box into a 2-slot ring.
-//   * Warps 2..9 (2 row sets of 64 rows x 4 k-chunks of 64 inputs) decode their weights in
-//     registers into f16 mma.sync A fragments: one 32-bit word of Q4_K nibbles gives four f16x2
+//   * Warps 2..5 (one per k-chunk of 64 inputs, all 128 rows each: 6 warps in all, so that a
+//     scheduler partition holds at most two and a thread may use 255 registers) decode their
+//     weights in registers into f16 mma.sync A fragments: one 32-bit word of Q4_K nibbles gives four f16x2
 //     operands through (w & 0x000F000F) | 0x6400 (= 1024 + n, exact), an exact f16 subtraction of
 //     1024 and one f16 FMA with the sub-block's (d*sc, -dmin*m) -- the reference's value formula
 //     d*sc*q - dmin*m (kernel.cu:913-921,1090-1119) rounded once to f16.  Activations are read from
 //     the swizzled tile, multiplied by the RMSNorm weight and converted to f16 B fragments in
-//     registers.  mma.sync.m16n8k16 accumulates in fp32 (64 rows x 32 tokens per warp).
+//     registers.  mma.sync.m16n8k16 accumulates in fp32 (128 rows x 32 tokens per warp).
 //     The k order inside a 16-element step is permuted identically on both operands (element
 //     4t + {0, 2, 1, 3} of a step goes to logical position 2t, 2t+1, 2t+8, 2t+9), which lets one
 //     AND extract two operands from bytes 0 and 2 (or 1 and 3) of a word.
@@ -61,7 +62,7 @@ namespace {
 
 constexpr int kBMaxTok = 32;
 constexpr int kBRows = 128;                        // output rows per tile
-constexpr int kBCw = 8;                            // consumer warps: 2 row sets x 4 k-chunks
+constexpr int kBCw = 4;                            // consumer warps: one per k-chunk, all 128 rows each
 constexpr int kBThreads = (2 + kBCw) * 32;         // weight producer, activation producer, consumers
 constexpr int kBWSlots = 4;
 constexpr int kBXSlots = 2;
@@ -76,7 +77,8 @@ constexpr int kBOffRed = kBOffX + kBXSlots * kBXBytes;
 constexpr int kBOffMisc = kBOffRed + kBRedBytes;         // per-warp token reductions
 constexpr int kBOffGamma = kBOffMisc + 2 * kBCw * kBMaxTok * 8;  // the op's RMSNorm weight
 constexpr int kBGammaMax = 4096;                         // inputs whose RMSNorm weight is staged
-constexpr int kBSmem = kBOffGamma + kBGammaMax * 4;
+constexpr int kBOffPslot = kBOffGamma + kBGammaMax * 4;  // stream-K part slots of the tile being finished
+constexpr int kBSmem = kBOffPslot + 256 * 4;
 static_assert(kBOffX % 1024 == 0, "activation ring must be 1024-byte aligned");
 static_assert(kBSmem <= 227 * 1024, "shared memory");
 constexpr int kErrBarrier = 5;
@@ -166,12 +168,15 @@ __device__ __forceinline__ uint32_t q4k_ab(const uint4 &h, int j) {
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
     return pack_h2(d * (float)sc, -dmin * (float)m);
 }
+// Token of column g of an 8-token MMA tile: 0, 4, 1, 5, 2, 6, 3, 7 (see the B-fragment loads).
+__device__ __forceinline__ int tperm(int g) { return (g >> 1) | ((g & 1) << 2); }
 __device__ __forceinline__ long long ss_to_fixed(float v) { return __float2ll_rn(v * (float)kSsFix); }
 // Stream-K split of an op's T units over min(C, T) CTAs (every participating CTA gets at least
 // one unit, so every CTA whose range touches a tile arrives on that tile's counter).
 __device__ __forceinline__ int op_ctas(int64_t T, int C) { return T < C ? (int)T : C; }
 __device__ __forceinline__ int64_t op_start(int64_t T, int Cp, int c) { return c >= Cp ? T : (int64_t)c * T / Cp; }
 
+template <int NT>  // 8-token MMA tiles per launch (tokens <= 8 * NT)
 __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_constant__ BArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *wfull = reinterpret_cast<uint64_t *>(smem);
@@ -183,13 +188,14 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
     int *bcast = reinterpret_cast<int *>(epoch_s + 1);
     float *inv_rms = reinterpret_cast<float *>(smem + 256);           // [32]
     float *red = reinterpret_cast<float *>(smem + kBOffRed);          // [4 chunks][32 tokens][132]
-    unsigned long long *wkey = reinterpret_cast<unsigned long long *>(smem + kBOffMisc);  // [8][32]
-    float *wss = reinterpret_cast<float *>(smem + kBOffMisc + kBCw * kBMaxTok * 8);        // [8][32]
+    unsigned long long *wkey = reinterpret_cast<unsigned long long *>(smem + kBOffMisc);  // [warp][32]
+    float *wss = reinterpret_cast<float *>(smem + kBOffMisc + kBCw * kBMaxTok * 8);        // [warp][32]
     float *gsm = reinterpret_cast<float *>(smem + kBOffGamma);        // [K] RMSNorm weight of the op
+    int *pslot = reinterpret_cast<int *>(smem + kBOffPslot);          // [parts of a shared tile]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, cta = blockIdx.x;
-    const int M = a.M, NT = a.NT;
+    const int M = a.M;
     if (tid == 0) {
         for (int s = 0; s < kBWSlots; ++s) {
             mbar_init(&wfull[s], 1);
@@ -207,8 +213,9 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
     const unsigned epoch = *epoch_s;
     const unsigned target = (epoch + 1u) * (unsigned)C;
     long long *ss_cur = a.ss + (size_t)(epoch & 1u) * a.nslots * kBMaxTok;
-    if (cta == 0 && tid < a.nslots * kBMaxTok)  // the other parity is next launch's: zero it now
-        a.ss[(size_t)((epoch + 1u) & 1u) * a.nslots * kBMaxTok + tid] = 0;
+    if (cta == 0)  // the other parity is next launch's: zero it now
+        for (int i = tid; i < a.nslots * kBMaxTok; i += blockDim.x)
+            a.ss[(size_t)((epoch + 1u) & 1u) * a.nslots * kBMaxTok + i] = 0;
     auto aborted = [&]() { return *reinterpret_cast<volatile int *>(abort_flag) != 0; };
 
     if (warp == 0) {
@@ -293,7 +300,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
 
     // -------------------------------- consumers --------------------------------
     const int cw = warp - 2, ctid = tid - 64;
-    const int rs = cw >> 2, kc = cw & 3;  // row set (64 rows), k-chunk (inputs 64kc .. 64kc+63 of a block)
+    const int kc = cw;  // k-chunk: inputs 64kc .. 64kc + 63 of every block
     const int g = lane >> 2, t = lane & 3;
     int itw = 0, itx = 0;
     for (int p = 0; p < a.nops; ++p) {
@@ -318,9 +325,9 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         // each slot written by one lane only: deterministic
         wkey[cw * kBMaxTok + lane] = 0ull;
         wss[cw * kBMaxTok + lane] = 0.f;
-        float acc[4][4][4];
+        float acc[8][4][4];  // rows 16m + g (+8), tokens of n-tile n
 #pragma unroll
-        for (int m = 0; m < 4; ++m)
+        for (int m = 0; m < 8; ++m)
 #pragma unroll
             for (int n = 0; n < 4; ++n)
 #pragma unroll
@@ -334,64 +341,66 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             if (!aborted() && !mbar_wait(&xfull[xsl], (uint32_t)(itx / kBXSlots) & 1u, a.err, kErrWaitFull))
                 *abort_flag = 1;
             if (!__any_sync(0xffffffffu, aborted())) {
-                const uint8_t *wb = smem + kBOffW + ws * kBWBytes + (rs * 64) * 144;
+                const uint8_t *wb = smem + kBOffW + ws * kBWBytes;
                 const uint8_t *xb = smem + kBOffX + xsl * kBXBytes;
-                // this thread's rows: 16m + g and 16m + g + 8 of the row set (m = 0..3); their words of
-                // qs for the chunk (bytes 32kc + 16j + 4t, j = 0, 1) and the two sub-blocks' (A, B)
-                uint32_t wd[4][2][2], ab[4][2][2];
-                {
-                    // lane (g, t) decodes the scales of rows 16t + g (+8), the four lanes of a quad
-                    // then share them
-                    uint32_t mine[2][2];
+                // This lane's rows are 16m + g and 16m + g + 8 (m = 0..7), its inputs 4t .. 4t + 3 of each
+                // 16-input step.  Lane (g, t) decodes the sub-block scales of rows 16m + g (+8) for
+                // m = t and t + 4; the four lanes of a quad then share them.  Few values stay live
+                // across the k-steps (the 128 accumulators take most registers): scales per
+                // sub-block, weight words per m-tile.
+                uint32_t mine[2][2][2];  // [m = t or t + 4][row g or g + 8][sub-block 2kc or 2kc + 1]
+#pragma unroll
+                for (int mm = 0; mm < 2; ++mm)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint4 hd = *reinterpret_cast<const uint4 *>(wb + (16 * t + g + 8 * h) * 144);
-                        mine[h][0] = q4k_ab(hd, 2 * kc);
-                        mine[h][1] = q4k_ab(hd, 2 * kc + 1);
+                        const uint4 hd = *reinterpret_cast<const uint4 *>(wb + (16 * (t + 4 * mm) + g + 8 * h) * 144);
+                        mine[mm][h][0] = q4k_ab(hd, 2 * kc);
+                        mine[mm][h][1] = q4k_ab(hd, 2 * kc + 1);
                     }
-#pragma unroll
-                    for (int m = 0; m < 4; ++m)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h)
-#pragma unroll
-                            for (int q = 0; q < 2; ++q) ab[m][h][q] = __shfl_sync(0xffffffffu, mine[h][q], (g << 2) | m);
-                }
-#pragma unroll
-                for (int m = 0; m < 4; ++m)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-#pragma unroll
-                        for (int j = 0; j < 2; ++j)
-                            wd[m][h][j] =
-                                *reinterpret_cast<const uint32_t *>(wb + (16 * m + g + 8 * h) * 144 + 16 + 32 * kc + 16 * j + 4 * t);
-#pragma unroll
+                const uint8_t *wq = wb + g * 144 + 16 + 32 * kc + 4 * t;  // this lane's word of row g, j = 0
+#pragma unroll 1
                 for (int sh = 0; sh < 2; ++sh) {  // sub-block 2kc (low nibbles), 2kc + 1 (high nibbles)
                     const int sb = 2 * kc + sh;
+                    uint32_t ab[8][2];
+#pragma unroll
+                    for (int m = 0; m < 8; ++m)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            ab[m][h] = __shfl_sync(0xffffffffu, sh ? mine[m >> 2][h][1] : mine[m >> 2][h][0],
+                                                   (g << 2) | (m & 3));
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {  // 16-input step
-                        // B fragments: tokens 8n + g, inputs 16j + 4t .. +3 of sub-block sb (swizzled)
-                        float4 gm = make_float4(1.f, 1.f, 1.f, 1.f);
-                        if (gamma != nullptr)
-                            gm = *reinterpret_cast<const float4 *>(gk + 256 * blk + 32 * sb + 16 * j + 4 * t);
+                        // B fragments: column g of n-tile n is token 8n + tperm(g) (tperm puts the two
+                        // rows a quarter-warp reads 4 apart, so their swizzled chunks never collide);
+                        // inputs 16j + 4t .. +3 of sub-block sb
+                        float2 g01 = make_float2(1.f, 1.f), g23 = make_float2(1.f, 1.f);
+                        if (gamma != nullptr) {
+                            const float4 gm = *reinterpret_cast<const float4 *>(gk + 256 * blk + 32 * sb + 16 * j + 4 * t);
+                            g01 = make_float2(gm.x, gm.z);
+                            g23 = make_float2(gm.y, gm.w);
+                        }
                         uint32_t bf[4][2];
 #pragma unroll
                         for (int n = 0; n < 4; ++n) {
                             if (n < NT) {
-                                const int tok = 8 * n + g;
+                                const int tok = 8 * n + tperm(g);
                                 const float4 v = *reinterpret_cast<const float4 *>(
                                     xb + ((size_t)sb * (NT * 8) + tok) * 128 + (((4 * j + t) ^ (tok & 7)) << 4));
-                                bf[n][0] = pack_h2(v.x * gm.x, v.z * gm.z);
-                                bf[n][1] = pack_h2(v.y * gm.y, v.w * gm.w);
+                                const float2 p0 = fmul2(make_float2(v.x, v.z), g01);
+                                const float2 p1 = fmul2(make_float2(v.y, v.w), g23);
+                                bf[n][0] = pack_h2(p0.x, p0.y);
+                                bf[n][1] = pack_h2(p1.x, p1.y);
                             } else {
                                 bf[n][0] = bf[n][1] = 0u;
                             }
                         }
 #pragma unroll
-                        for (int m = 0; m < 4; ++m) {
-                            const uint32_t a0 = ab[m][0][sh], a1 = ab[m][1][sh];
+                        for (int m = 0; m < 8; ++m) {
+                            const uint32_t a0 = ab[m][0], a1 = ab[m][1];
                             const uint32_t aa0 = __byte_perm(a0, 0, 0x1010), bb0 = __byte_perm(a0, 0, 0x3232);
                             const uint32_t aa1 = __byte_perm(a1, 0, 0x1010), bb1 = __byte_perm(a1, 0, 0x3232);
-                            const uint32_t w0 = wd[m][0][j] >> (4 * sh), w1 = wd[m][1][j] >> (4 * sh);
+                            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wq + (16 * m) * 144 + 16 * j) >> (4 * sh);
+                            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(wq + (16 * m + 8) * 144 + 16 * j) >> (4 * sh);
                             uint32_t af[4];
                             af[0] = dq2(w0, aa0, bb0);        // row g,     inputs 4t, 4t+2
                             af[1] = dq2(w1, aa1, bb1);        // row g + 8, inputs 4t, 4t+2
@@ -439,91 +448,95 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             // k-chunk partials -> red[kc][token][row]
             float *rw = red + (size_t)kc * kBMaxTok * kBRedPitch;
 #pragma unroll
-            for (int m = 0; m < 4; ++m)
+            for (int m = 0; m < 8; ++m)
 #pragma unroll
                 for (int n = 0; n < 4; ++n) {
                     if (n < NT) {
-                        const int r = rs * 64 + 16 * m + g, tk = 8 * n + 2 * t;
-                        rw[tk * kBRedPitch + r] = acc[m][n][0];
-                        rw[(tk + 1) * kBRedPitch + r] = acc[m][n][1];
-                        rw[tk * kBRedPitch + r + 8] = acc[m][n][2];
-                        rw[(tk + 1) * kBRedPitch + r + 8] = acc[m][n][3];
+                        const int r = 16 * m + g;
+                        const int tk0 = 8 * n + tperm(2 * t), tk1 = 8 * n + tperm(2 * t + 1);
+                        rw[tk0 * kBRedPitch + r] = acc[m][n][0];
+                        rw[tk1 * kBRedPitch + r] = acc[m][n][1];
+                        rw[tk0 * kBRedPitch + r + 8] = acc[m][n][2];
+                        rw[tk1 * kBRedPitch + r + 8] = acc[m][n][3];
                     }
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
                 }
             named_bar_sync(1, kBCw * 32);
-            // sums over the four k-chunks: thread = (row r, 16 tokens)
-            const int r = ctid & (kBRows - 1), th = ctid >> 7;
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int tk = 16 * th + i;
-                v[i] = red[(0 * kBMaxTok + tk) * kBRedPitch + r] + red[(1 * kBMaxTok + tk) * kBRedPitch + r] +
-                       red[(2 * kBMaxTok + tk) * kBRedPitch + r] + red[(3 * kBMaxTok + tk) * kBRedPitch + r];
-            }
+            // The tile's sums over the four k-chunks (from red), or, when the tile is shared with
+            // other CTAs, over the parts those CTAs parked (in CTA order): computed per (token, row)
+            // where needed, so that few values are live at once.
             const int64_t ts = (int64_t)tile * U, te = ts + U;
             // every decision that leads to a named barrier is uniform over the consumer threads
             // (never the abort flag, which another warp may set at any time)
+            const bool partial = ts < u0 || te > u1;
             bool finish = true;
-            if (ts < u0 || te > u1) {
+            int nparts = 0;
+            auto red_sum = [&](int tk, int row) {
+                return red[(0 * kBMaxTok + tk) * kBRedPitch + row] + red[(1 * kBMaxTok + tk) * kBRedPitch + row] +
+                       red[(2 * kBMaxTok + tk) * kBRedPitch + row] + red[(3 * kBMaxTok + tk) * kBRedPitch + row];
+            };
+            if (partial) {
                 // stream-K: park this part; the last CTA of the tile sums the parts in CTA order
                 const int si = (tile == (int)(u0 / U)) ? 0 : 1;
                 float *pp = a.part + ((size_t)cta * 2 + si) * (kBMaxTok * kBRows);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) __stcg(pp + (16 * th + i) * kBRows + r, v[i]);
+                const int r = ctid;  // thread = row, all tokens
+#pragma unroll 4
+                for (int tk = 0; tk < kBMaxTok; ++tk) __stcg(pp + tk * kBRows + r, red_sum(tk, r));
                 __threadfence();
                 named_bar_sync(1, kBCw * 32);
                 const int cf = (int)(((ts + 1) * (int64_t)Cp - 1) / T), cl = (int)((te * (int64_t)Cp - 1) / T);
+                nparts = cl - cf + 1;
                 if (ctid == 0) *bcast = (int)atomicAdd(&a.counters[tile], 1u) == cl - cf;
+                // slot of each part: (CTA, first or last tile of its range)
+                for (int i = ctid; i < nparts; i += kBCw * 32) {
+                    const int c = cf + i;
+                    pslot[i] = 2 * c + ((tile == (int)(op_start(T, Cp, c) / U)) ? 0 : 1);
+                }
                 named_bar_sync(1, kBCw * 32);
                 finish = *bcast != 0;
                 if (finish) {
                     __threadfence();
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) v[i] = 0.f;
-                    for (int c = cf; c <= cl; ++c) {
-                        const int sj = (tile == (int)(op_start(T, Cp, c) / U)) ? 0 : 1;
-                        const float *qp = a.part + ((size_t)c * 2 + sj) * (kBMaxTok * kBRows);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) v[i] += __ldcg(qp + (16 * th + i) * kBRows + r);
-                    }
                     if (ctid == 0) a.counters[tile] = 0u;
                 }
             }
+            auto tile_sum = [&](int tk, int row) {
+                if (!partial) return red_sum(tk, row);
+                float sacc = 0.f;
+                for (int i = 0; i < nparts; ++i)
+                    sacc += __ldcg(a.part + (size_t)pslot[i] * (kBMaxTok * kBRows) + tk * kBRows + row);
+                return sacc;
+            };
             if (finish) {
                 if (kind == kBSwiglu) {
-                    // rows r < 64 are gate rows, r + 64 the matching up rows: exchange through smem
-                    float *xu = red;  // reuse chunk 0 (all reads of red are done after the barrier)
-                    named_bar_sync(2, kBCw * 32);
-                    if (r >= 64)
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) xu[(16 * th + i) * kBRedPitch + r - 64] = v[i];
-                    named_bar_sync(2, kBCw * 32);
-                    if (r < 64) {
-                        const int row = tile * 64 + r;
-#pragma unroll
+                    // thread = (gate row r < 64, 16 tokens); its up row is r + 64
+                    const int r = ctid & 63, tq = ctid >> 6;
+                    const int row = tile * 64 + r;
+                    if (row < rows) {
+#pragma unroll 2
                         for (int i = 0; i < 16; ++i) {
-                            const int tk = 16 * th + i;
-                            if (tk < M && row < rows) {
+                            const int tk = 16 * tq + i;
+                            if (tk < M) {
                                 const float nrm = gamma != nullptr ? inv_rms[tk] : 1.f;
-                                const float gv = v[i] * nrm, uv = xu[tk * kBRedPitch + r] * nrm;
+                                const float gv = tile_sum(tk, r) * nrm, uv = tile_sum(tk, r + 64) * nrm;
                                 o.y[(size_t)tk * o.ys + row] = gv / (1.0f + expf(-gv)) * uv;
                             }
                         }
                     }
                 } else {
+                    // thread = (row r, all tokens); warp cw holds rows 32cw .. 32cw + 31
+                    const int r = ctid;
                     const int row = tile * kBRows + r;
                     const bool live = row < rows;
                     const float bias = (live && o.bias != nullptr) ? o.bias[row] : 0.f;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int tk = 16 * th + i;
+#pragma unroll 2
+                    for (int i = 0; i < kBMaxTok; ++i) {
+                        const int tk = i;
                         float out = 0.f;
                         unsigned long long key = 0ull;
                         if (live && tk < M) {
                             const float nrm = gamma != nullptr ? inv_rms[tk] : 1.f;
-                            out = v[i] * nrm;
+                            out = tile_sum(tk, r) * nrm;
                             float *yp = o.y != nullptr ? o.y + (size_t)tk * o.ys + row : nullptr;
                             if (kind == kBAdd) {
                                 out += __ldcg(yp);
@@ -555,11 +568,10 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         named_bar_sync(1, kBCw * 32);
         if (track) {
             if (ctid < M) {
-                // warps 4h .. 4h + 3 hold tokens 16h .. 16h + 15
-                const int h = ctid >> 4;
+                // every warp holds every token (for its 32 rows of each tile)
                 unsigned long long k = 0ull;
                 float s = 0.f;
-                for (int w = 4 * h; w < 4 * h + 4; ++w) {
+                for (int w = 0; w < kBCw; ++w) {
                     const unsigned long long kw = wkey[w * kBMaxTok + ctid];
                     k = kw > k ? kw : k;
                     s += wss[w * kBMaxTok + ctid];
@@ -578,6 +590,11 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             if (p == a.nops - 1 && prev == target - 1u) atomicAdd(a.epoch, 1u);
         }
     }
+}
+
+using BKernel = void (*)(const BArgs);
+BKernel bchain_kernel_for(int NT) {
+    return NT == 1 ? bchain_kernel<1> : NT == 2 ? bchain_kernel<2> : NT == 3 ? bchain_kernel<3> : bchain_kernel<4>;
 }
 
 struct BChain {
@@ -722,7 +739,7 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
             }
         e = cudaMemcpy(c->ops_dev, h.data(), sizeof(BOp) * nops, cudaMemcpyHostToDevice);
     }
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(bchain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBSmem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(bchain_kernel_for(NT), cudaFuncAttributeMaxDynamicSharedMemorySize, kBSmem);
     if (e != cudaSuccess) {
         if (c->ops_dev) cudaFree(c->ops_dev);
         if (c->done) cudaFree(c->done);
@@ -761,7 +778,7 @@ int bchain_run(void *chain, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, bchain_kernel, c->args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, bchain_kernel_for(c->args.NT), c->args);
     set_launch_count(1);
     if (e != cudaSuccess) return set_last_error(QL_ECUDA, cudaGetErrorString(e));
     return QL_OK;
