@@ -43,6 +43,33 @@ BPE = 144 / 256
 METRIC = "decode tokens/s (batch 1 & 32) + quant-GEMV HBM GB/s vs peak, 1/2/4/8 B200"
 
 
+class Model:
+    """Dimensions of a Qwen2-architecture decoder's quantized linears (attention itself excluded)."""
+
+    def __init__(self, name, hidden, n_q, n_kv, head, ffn, vocab, layers, qtype, tied=False):
+        self.name, self.hidden, self.ffn, self.vocab, self.layers = name, hidden, ffn, vocab, layers
+        self.q_dim, self.kv_dim, self.qtype, self.tied = n_q * head, n_kv * head, qtype, tied
+        self.block, self.block_bytes = {12: (256, 144), 8: (32, 34), 2: (32, 18)}[qtype]
+
+    def with_layers(self, layers):
+        m = Model(self.name, self.hidden, 1, 1, 1, self.ffn, self.vocab, layers, self.qtype, self.tied)
+        m.q_dim, m.kv_dim = self.q_dim, self.kv_dim
+        return m
+
+    def weight_elems(self):
+        per_layer = self.hidden * (self.q_dim + 2 * self.kv_dim) + self.q_dim * self.hidden + 3 * self.hidden * self.ffn
+        return self.layers * per_layer + self.vocab * self.hidden
+
+    def weight_bytes(self):
+        return self.weight_elems() // self.block * self.block_bytes
+
+
+# BASELINE configs[2], configs[0], configs[4]
+QWEN2_7B = Model("qwen2-7b-q4k", 3584, 28, 4, 128, 18944, 152064, 28, 12)
+QWEN2_05B = Model("qwen2-0.5b-q8_0", 896, 14, 2, 64, 4864, 151936, 24, 8, tied=True)
+QWEN2_72B = Model("qwen2-72b-q4_0", 8192, 64, 8, 128, 29568, 152064, 80, 2)
+
+
 def weight_elems():
     per_layer = HIDDEN * (N_Q * HEAD) + 2 * HIDDEN * (N_KV * HEAD) + (N_Q * HEAD) * HIDDEN + 3 * HIDDEN * FFN
     return LAYERS * per_layer + VOCAB * HIDDEN
@@ -119,26 +146,27 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------------------
 class DecodeStack:
-    """The sharded Qwen2-7B-shape Q4_K linear stack of one rank."""
+    """The sharded quantized linear stack of one rank (default: the Qwen2-7B-shape Q4_K model)."""
 
-    def __init__(self, Q, torch, rank, world, batch, seed=0):
+    def __init__(self, Q, torch, rank, world, batch, seed=0, model=None):
         self.Q, self.torch = Q, torch
+        md = self.md = model or QWEN2_7B
         self.rank, self.world, self.M = rank, world, batch
         dev = "cuda"
-        rb = lambda k: Q.row_bytes(QK, k)
-        # K-split of o (input = q width) and down (input = FFN) at Q4_K block granularity;
+        rb = lambda k: Q.row_bytes(md.qtype, k)
+        # K-split of o (input = q width) and down (input = the FFN width) at whole quant blocks;
         # the producing column-parallel projections follow the same partition.
-        self.qo_off, self.qo_len = split_blocks(N_Q * HEAD, world, 256)[rank]
-        self.f_off, self.f_len = split_blocks(FFN, world, 256)[rank]
-        self.kv_off, self.kv_len = split_blocks(N_KV * HEAD, world, 32)[rank]
-        self.v_off, self.v_len = split_blocks(VOCAB, world, 32)[rank]
+        self.qo_off, self.qo_len = split_blocks(md.q_dim, world, md.block)[rank]
+        self.f_off, self.f_len = split_blocks(md.ffn, world, md.block)[rank]
+        self.kv_off, self.kv_len = split_blocks(md.kv_dim, world, 32)[rank]
+        self.v_off, self.v_len = split_blocks(md.vocab, world, 32)[rank]
         g = torch.Generator(device="cpu").manual_seed(seed)
 
         # Every rank's shard is a slice of the same full matrix (seeded by the matrix alone),
         # so a one-GPU stack built with world = 1 holds exactly the matrices the ranks split.
         def synth(rows, k, tag):
             w = torch.empty((rows, rb(k)), dtype=torch.uint8, device=dev)
-            Q.synth_quantized(QK, seed * 1000003 + tag * 7919, rows, k, 0.02, w.data_ptr())
+            Q.synth_quantized(md.qtype, seed * 1000003 + tag * 7919, rows, k, 0.02, w.data_ptr())
             return w
 
         def out_rows(rows, k, tag, lo, n):  # column parallel: this rank's output rows
@@ -146,33 +174,33 @@ class DecodeStack:
 
         def in_blocks(rows, k, tag, lo, n):  # row parallel: this rank's input blocks of every row
             return synth(rows, k, tag) if world == 1 else \
-                synth(rows, k, tag)[:, lo // 256 * 144:(lo + n) // 256 * 144].contiguous()
+                synth(rows, k, tag)[:, lo // md.block * md.block_bytes:(lo + n) // md.block * md.block_bytes].contiguous()
 
-        QWD, KVD = N_Q * HEAD, N_KV * HEAD
+        QWD, KVD = md.q_dim, md.kv_dim
         self.layers = []
-        for l in range(LAYERS):
-            ln1 = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev)
-            ln2 = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev)
+        for l in range(md.layers):
+            ln1 = (1.0 + 0.1 * torch.randn(md.hidden, generator=g)).to(dev)
+            ln2 = (1.0 + 0.1 * torch.randn(md.hidden, generator=g)).to(dev)
             b = 0.01 * torch.randn(QWD + 2 * KVD, generator=g)
             bqkv = torch.cat([b[self.qo_off:self.qo_off + self.qo_len], b[QWD + self.kv_off:QWD + self.kv_off + self.kv_len],
                               b[QWD + KVD + self.kv_off:QWD + KVD + self.kv_off + self.kv_len]]).to(dev)
             L = {
-                "wq": out_rows(QWD, HIDDEN, 10 * l + 1, self.qo_off, self.qo_len),
-                "wk": out_rows(KVD, HIDDEN, 10 * l + 2, self.kv_off, self.kv_len),
-                "wv": out_rows(KVD, HIDDEN, 10 * l + 3, self.kv_off, self.kv_len),
-                "wo": in_blocks(HIDDEN, QWD, 10 * l + 4, self.qo_off, self.qo_len),
-                "wg": out_rows(FFN, HIDDEN, 10 * l + 5, self.f_off, self.f_len),
-                "wu": out_rows(FFN, HIDDEN, 10 * l + 6, self.f_off, self.f_len),
-                "wd": in_blocks(HIDDEN, FFN, 10 * l + 7, self.f_off, self.f_len),
+                "wq": out_rows(QWD, md.hidden, 10 * l + 1, self.qo_off, self.qo_len),
+                "wk": out_rows(KVD, md.hidden, 10 * l + 2, self.kv_off, self.kv_len),
+                "wv": out_rows(KVD, md.hidden, 10 * l + 3, self.kv_off, self.kv_len),
+                "wo": in_blocks(md.hidden, QWD, 10 * l + 4, self.qo_off, self.qo_len),
+                "wg": out_rows(md.ffn, md.hidden, 10 * l + 5, self.f_off, self.f_len),
+                "wu": out_rows(md.ffn, md.hidden, 10 * l + 6, self.f_off, self.f_len),
+                "wd": in_blocks(md.hidden, md.ffn, 10 * l + 7, self.f_off, self.f_len),
                 "ln1": ln1, "ln2": ln2, "bqkv": bqkv,
             }
             self.layers.append(L)
         torch.cuda.empty_cache()
-        self.wlm = out_rows(VOCAB, HIDDEN, 999, self.v_off, self.v_len)
-        self.lnf = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(dev)
+        self.wlm = out_rows(md.vocab, md.hidden, 999, self.v_off, self.v_len)
+        self.lnf = (1.0 + 0.1 * torch.randn(md.hidden, generator=g)).to(dev)
         M = batch
-        self.h = torch.zeros((M, HIDDEN), device=dev)
-        self.h_in = torch.zeros((M, HIDDEN), device=dev)
+        self.h = torch.zeros((M, md.hidden), device=dev)
+        self.h_in = torch.zeros((M, md.hidden), device=dev)
         self.qkv_w = self.qo_len + 2 * self.kv_len  # fused q|k|v output width
         self.qkv = torch.zeros((M, self.qkv_w), device=dev)
         self.act = torch.zeros((M, max(self.f_len, 1)), device=dev)
@@ -185,13 +213,13 @@ class DecodeStack:
         # Row-parallel partial sums: the library's one-shot peer-memory all-reduce
         # for decode-sized vectors, NCCL for larger ones (QL_TP_NCCL=1 forces NCCL).
         self.comm = None
-        use_chain = M == 1 and os.environ.get("QL_CHAIN", "1") != "0"
-        if world > 1 and not use_chain and M * HIDDEN <= 4096 and os.environ.get("QL_TP_NCCL", "0") != "1":
+        use_chain = M == 1 and md.qtype == 12 and os.environ.get("QL_CHAIN", "1") != "0"  # the chain is Q4_K
+        if world > 1 and not use_chain and M * md.hidden <= 4096 and os.environ.get("QL_TP_NCCL", "0") != "1":
             def exchange(h):
                 out = [None] * world
                 torch.distributed.all_gather_object(out, h)
                 return out
-            self.comm = Q.Comm(rank, world, 4096, 2 * LAYERS, exchange)
+            self.comm = Q.Comm(rank, world, 4096, 2 * md.layers, exchange)
         # One token: the whole stack as one persistent launch per step (QL_CHAIN=0: per-op launches);
         # with world > 1 the row-parallel partial sums cross NVLink inside that launch
         self.chain = None
@@ -203,7 +231,7 @@ class DecodeStack:
                     torch.distributed.all_gather_object(out, hnd)
                     return out
             self.chain = Q.GemvChain(self.chain_ops(), rank, world, exchange)
-        elif world == 1 and 1 < M <= 32 and os.environ.get("QL_CHAIN", "1") != "0":
+        elif world == 1 and 1 < M <= 32 and md.qtype == 12 and os.environ.get("QL_CHAIN", "1") != "0":
             # batched decode: the whole stack for all M tokens as one persistent launch per step
             self.chain = Q.GemvChain(self.chain_ops(batch=True), tokens=M)
         torch.cuda.synchronize()
@@ -211,41 +239,44 @@ class DecodeStack:
     def chain_ops(self, batch=False):
         """The step's op list: one token (fused MLP on one GPU), or with batch=True the batched
         chain's list over [M, *] activations (SwiGLU then down + residual)."""
-        Q, rbh = self.Q, self.Q.row_bytes(QK, HIDDEN)
+        md = self.md
+        Q, rbh = self.Q, self.Q.row_bytes(md.qtype, md.hidden)
         h, ops = self.h.data_ptr(), []
         st = (lambda xs, ys: {"x_stride": xs, "y_stride": ys}) if batch else (lambda xs, ys: {})
         for L in self.layers:
             ops.append(Q.chain_op(Q.OP_STORE, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
-                                  [self.qo_len, self.kv_len, self.kv_len], HIDDEN, h, self.qkv.data_ptr(),
-                                  L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr(), **st(HIDDEN, self.qkv_w)))
-            ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [Q.row_bytes(QK, self.qo_len)], [HIDDEN],
-                                  self.qo_len, self.qkv.data_ptr(), h, reduce=self.world > 1, **st(self.qkv_w, HIDDEN)))
+                                  [self.qo_len, self.kv_len, self.kv_len], md.hidden, h, self.qkv.data_ptr(),
+                                  L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr(), **st(md.hidden, self.qkv_w)))
+            ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [Q.row_bytes(md.qtype, self.qo_len)], [md.hidden],
+                                  self.qo_len, self.qkv.data_ptr(), h, reduce=self.world > 1, **st(self.qkv_w, md.hidden)))
             if self.world == 1 and not batch and os.environ.get("QL_CHAIN_MLP", "1") != "0":
-                # gate/up SwiGLU and down + residual as one op, split over the FFN (no barrier between)
+                # gate/up SwiGLU and down + residual as one op, split over the md.ffn (no barrier between)
                 ops.append(Q.chain_op(Q.OP_MLP, [L["wg"].data_ptr(), L["wu"].data_ptr(), L["wd"].data_ptr()],
-                                      [rbh, rbh, Q.row_bytes(QK, self.f_len)], [self.f_len, self.f_len, HIDDEN],
-                                      HIDDEN, h, h, L["ln2"].data_ptr(), EPS))
+                                      [rbh, rbh, Q.row_bytes(md.qtype, self.f_len)], [self.f_len, self.f_len, md.hidden],
+                                      md.hidden, h, h, L["ln2"].data_ptr(), EPS))
                 continue
             ops.append(Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rbh] * 2,
-                                  [self.f_len] * 2, HIDDEN, h, self.act.data_ptr(), L["ln2"].data_ptr(), EPS,
-                                  **st(HIDDEN, self.act.shape[1])))
-            ops.append(Q.chain_op(Q.OP_ADD, [L["wd"].data_ptr()], [Q.row_bytes(QK, self.f_len)], [HIDDEN],
+                                  [self.f_len] * 2, md.hidden, h, self.act.data_ptr(), L["ln2"].data_ptr(), EPS,
+                                  **st(md.hidden, self.act.shape[1])))
+            ops.append(Q.chain_op(Q.OP_ADD, [L["wd"].data_ptr()], [Q.row_bytes(md.qtype, self.f_len)], [md.hidden],
                                   self.f_len, self.act.data_ptr(), h, reduce=self.world > 1,
-                                  **st(self.act.shape[1], HIDDEN)))
-        ops.append(Q.chain_op(Q.OP_STORE, [self.wlm.data_ptr()], [rbh], [self.v_len], HIDDEN, h,
+                                  **st(self.act.shape[1], md.hidden)))
+        ops.append(Q.chain_op(Q.OP_STORE, [self.wlm.data_ptr()], [rbh], [self.v_len], md.hidden, h,
                               self.logits.data_ptr(), self.lnf.data_ptr(), EPS, argmax_idx=self.tok.data_ptr(),
-                              argmax_offset=self.v_off, **st(HIDDEN, self.v_len)))
+                              argmax_offset=self.v_off, **st(md.hidden, self.v_len)))
         return ops
 
     def weight_bytes(self):
+        md = self.md
         n = sum(w.numel() for L in self.layers for key, w in L.items() if key.startswith("w"))
         return n + self.wlm.numel()
 
     def step(self, events=None):
         """Enqueue one decode token on torch's current stream."""
+        md = self.md
         Q, torch, M = self.Q, self.torch, self.M
         Q.set_stream(torch.cuda.current_stream().cuda_stream)
-        rbh = Q.row_bytes(QK, HIDDEN)
+        rbh = Q.row_bytes(md.qtype, md.hidden)
         self.h.copy_(self.h_in)
         if self.chain is not None:
             if events is not None:
@@ -261,35 +292,35 @@ class DecodeStack:
         def reduce_h():
             nonlocal slot
             if self.comm is not None:
-                self.comm.allreduce(h, M * HIDDEN, slot)
+                self.comm.allreduce(h, M * md.hidden, slot)
                 slot += 1
             else:
                 torch.distributed.all_reduce(self.h)
         for li, L in enumerate(self.layers):
             # q, k, v in one launch (stacked sources), RMSNorm and bias fused
-            Q.quant_gemv_stacked_ex(QK, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
-                                    [self.qo_len, self.kv_len, self.kv_len], h, HIDDEN, self.qkv.data_ptr(),
-                                    self.qkv_w, HIDDEN, M, L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr())
+            Q.quant_gemv_stacked_ex(md.qtype, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
+                                    [self.qo_len, self.kv_len, self.kv_len], h, md.hidden, self.qkv.data_ptr(),
+                                    self.qkv_w, md.hidden, M, L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr())
             # o_proj (row-parallel) on the q columns (attention output stand-in): rank 0
             # accumulates onto h, others overwrite h with their partial
-            Q.quant_gemv_ex(QK, L["wo"].data_ptr(), Q.row_bytes(QK, self.qo_len), self.qkv.data_ptr(),
-                            self.qkv_w, h, HIDDEN, HIDDEN, self.qo_len, M, accumulate=(self.rank == 0))
+            Q.quant_gemv_ex(md.qtype, L["wo"].data_ptr(), Q.row_bytes(md.qtype, self.qo_len), self.qkv.data_ptr(),
+                            self.qkv_w, h, md.hidden, md.hidden, self.qo_len, M, accumulate=(self.rank == 0))
             if self.world > 1:
                 reduce_h()
             sel = events is not None and li in events["layers"]
             if sel:
                 events["pairs"][li][0].record()
-            Q.quant_swiglu_ex(QK, L["wg"].data_ptr(), L["wu"].data_ptr(), rbh, rbh, h, HIDDEN, self.act.data_ptr(),
-                              self.act.shape[1], self.f_len, HIDDEN, M, L["ln2"].data_ptr(), EPS)
+            Q.quant_swiglu_ex(md.qtype, L["wg"].data_ptr(), L["wu"].data_ptr(), rbh, rbh, h, md.hidden, self.act.data_ptr(),
+                              self.act.shape[1], self.f_len, md.hidden, M, L["ln2"].data_ptr(), EPS)
             if sel:
                 events["pairs"][li][1].record()
-            Q.quant_gemv_ex(QK, L["wd"].data_ptr(), Q.row_bytes(QK, self.f_len), self.act.data_ptr(),
-                            self.act.shape[1], h, HIDDEN, HIDDEN, self.f_len, M, accumulate=(self.rank == 0))
+            Q.quant_gemv_ex(md.qtype, L["wd"].data_ptr(), Q.row_bytes(md.qtype, self.f_len), self.act.data_ptr(),
+                            self.act.shape[1], h, md.hidden, md.hidden, self.f_len, M, accumulate=(self.rank == 0))
             if self.world > 1:
                 reduce_h()
         # LM head with the greedy argmax fused into its epilogue
-        Q.quant_gemv_argmax_ex(QK, self.wlm.data_ptr(), rbh, h, HIDDEN, self.logits.data_ptr(), self.v_len,
-                               self.v_len, HIDDEN, M, self.lnf.data_ptr(), EPS, 0, self.tok.data_ptr(), None)
+        Q.quant_gemv_argmax_ex(md.qtype, self.wlm.data_ptr(), rbh, h, md.hidden, self.logits.data_ptr(), self.v_len,
+                               self.v_len, md.hidden, M, self.lnf.data_ptr(), EPS, 0, self.tok.data_ptr(), None)
         if self.world > 1:
             idx = self.tok.long()
             self.best[:, 0] = self.logits.gather(1, idx[:, None])[:, 0]
@@ -306,17 +337,19 @@ class DecodeStack:
         """Library kernel launches per step: one persistent chain launch, or per layer
         qkv, o, gate/up, down plus the LM head with its fused argmax (one GEMV launch per
         <= 4 tokens, gate/up <= 2; tensor-core path: activation prep + GEMM per op)."""
+        md = self.md
         if self.chain is not None:
             return 1
         if self.M >= 8:
-            return 2 * (4 * LAYERS + 1)
+            return 2 * (4 * md.layers + 1)
         c4, c2 = (self.M + 3) // 4, (self.M + 1) // 2
-        return LAYERS * (3 * c4 + c2) + c4
+        return md.layers * (3 * c4 + c2) + c4
 
     def chain_act_bytes(self):
         """Activation bytes the chain reads and writes per step (x in, y out, per op)."""
-        per_layer = (HIDDEN + self.qkv_w) + (self.qo_len + HIDDEN) + (HIDDEN + self.f_len) + (self.f_len + HIDDEN)
-        return 4 * self.M * (LAYERS * per_layer + HIDDEN + self.v_len)
+        md = self.md
+        per_layer = (md.hidden + self.qkv_w) + (self.qo_len + md.hidden) + (md.hidden + self.f_len) + (self.f_len + md.hidden)
+        return 4 * self.M * (md.layers * per_layer + md.hidden + self.v_len)
 
 
 # --------------------------------------------------------------------------------------
@@ -458,16 +491,15 @@ def run_chain_kernel(args):
     """Times the persistent chain launch (one GPU) on a stack of --layers decoder layers + LM
     head: the ncu target for the decode step (fewer layers keep the capture small).  --kernel-only
     chain is the one-token chain, bchain the batched chain over --batch tokens."""
-    global LAYERS
     import torch
     import blog_b200 as Q
-    LAYERS = args.layers
     torch.cuda.init()
     Q.init(0)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         Q.set_stream(s.cuda_stream)
-        st = DecodeStack(Q, torch, 0, 1, args.batch if args.kernel_only == "bchain" else 1)
+        st = DecodeStack(Q, torch, 0, 1, args.batch if args.kernel_only == "bchain" else 1,
+                         model=QWEN2_7B.with_layers(args.layers))
         for _ in range(args.warmup):
             st.step()
         torch.cuda.synchronize()
@@ -480,7 +512,7 @@ def run_chain_kernel(args):
     Q.check_device()
     us = e0.elapsed_time(e1) * 1000 / args.steps
     wb = st.weight_bytes()
-    print(json.dumps({"kernel_only": args.kernel_only, "tokens": st.M, "layers": LAYERS, "avg_us": us, "weight_bytes": wb,
+    print(json.dumps({"kernel_only": args.kernel_only, "tokens": st.M, "layers": args.layers, "avg_us": us, "weight_bytes": wb,
                       "act_bytes": st.chain_act_bytes(), "GBps": wb / us / 1e3, "launches": args.steps}), flush=True)
     st.chain.close()
     return 0
@@ -753,6 +785,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch32", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-models", action="store_true", help="skip the Qwen2-0.5B Q8_0 and Qwen2-72B Q4_0 lines")
     ap.add_argument("--moe", action="store_true", help="DeepSeek-V2-Lite-shape MoE decode, expert parallel")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
@@ -807,12 +840,12 @@ def main():
         torch.distributed.barrier()
         return out
 
-    def measure(batch):
-        stack = DecodeStack(Q, torch, rank, world, batch)
+    def measure(batch, model=QWEN2_7B):
+        stack = DecodeStack(Q, torch, rank, world, batch, model=model)
         s = torch.cuda.Stream()
-        host_in = torch.randn((batch, HIDDEN), generator=torch.Generator().manual_seed(5)).pin_memory()
+        host_in = torch.randn((batch, model.hidden), generator=torch.Generator().manual_seed(5)).pin_memory()
         host_out = torch.zeros((batch,), dtype=torch.int32).pin_memory()
-        parity = tp_parity(stack, host_in) if (world > 1 and stack.chain is not None) else None
+        parity = tp_parity(stack, host_in) if (world > 1 and stack.chain is not None and model is QWEN2_7B) else None
         # event-record nodes inside the graph around the dominant kernel: the chain launch
         # (the whole step) or the gate/up SwiGLU launch of 4 layers
         evl = ["chain"] if stack.chain is not None else [3, 10, 17, 24]
@@ -975,6 +1008,13 @@ def main():
 
     r1 = measure(args.batch)
     r32 = None if args.no_batch32 else measure(32)
+    # the other BASELINE decoders, batch 1, on the per-op launches (the one-token chain is Q4_K):
+    # configs[0] Qwen2-0.5B Q8_0 on one GPU, configs[4] Qwen2-72B Q4_0 tensor parallel over the ranks
+    extra = {}
+    if not args.no_models:
+        if world == 1:
+            extra["qwen2_0.5b_q8_0"] = (QWEN2_05B, measure(1, QWEN2_05B))
+        extra["qwen2_72b_q4_0"] = (QWEN2_72B, measure(1, QWEN2_72B))
     rp = None if args.no_prefill else measure_prefill(args.prefill_tokens)
 
     if rank == 0:
@@ -1035,6 +1075,15 @@ def main():
                                "tensor_frac_of_sustained_bf16": tf / sus,
                                "path": "tcgen05 f16 x f16 -> f32 GEMM, Q4_K dequantized into shared memory",
                                "tensor_pipe_active": "see profiles/gemm_q4k_prefill_2048x18944x3584.md"}
+        for key, (md, r) in extra.items():
+            wb = md.weight_bytes()
+            line[key] = {"value": 1 / (r["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r["ms"],
+                         "e2e_tokens_per_s": 1 / (r["e2e_ms"] / 1e3), "weight_GB_per_token": wb / 1e9,
+                         "hbm_roofline_tokens_per_s": hbm * 1e9 / (wb / world),
+                         "roofline_frac": (wb / world) / (r["ms"] / 1e3) / 1e9 / hbm,
+                         "parallelism": f"tp{world}", "launches_per_step": r["launches"],
+                         "path": "per-op streaming GEMV launches in a CUDA graph"
+                                 + (", NCCL all-reduce after o and down" if world > 1 else "")}
         if world == 1 and not args.no_cpu_baseline:
             v, _, info = cpu_reference_steps(2, 1, budget_s=30.0)
             line["cpu_baseline"] = dict(info, value=v, unit="tokens/s")
