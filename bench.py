@@ -49,10 +49,11 @@ class Model:
     def __init__(self, name, hidden, n_q, n_kv, head, ffn, vocab, layers, qtype, tied=False):
         self.name, self.hidden, self.ffn, self.vocab, self.layers = name, hidden, ffn, vocab, layers
         self.q_dim, self.kv_dim, self.qtype, self.tied = n_q * head, n_kv * head, qtype, tied
+        self.head_dim, self.rope_theta = head, 1e6
         self.block, self.block_bytes = {12: (256, 144), 8: (32, 34), 2: (32, 18)}[qtype]
 
     def with_layers(self, layers):
-        m = Model(self.name, self.hidden, 1, 1, 1, self.ffn, self.vocab, layers, self.qtype, self.tied)
+        m = Model(self.name, self.hidden, 1, 1, self.head_dim, self.ffn, self.vocab, layers, self.qtype, self.tied)
         m.q_dim, m.kv_dim = self.q_dim, self.kv_dim
         return m
 
@@ -209,6 +210,8 @@ class DecodeStack:
         self.best = torch.zeros((M, 2), device=dev)
         self.gathered = torch.zeros((world, M, 2), device=dev)
         self.token_ids = torch.zeros((M,), dtype=torch.int32, device=dev)
+        # decode positions (after the 2048-token prompt), read by the fused RoPE on q and k
+        self.pos = torch.arange(2048, 2048 + M, dtype=torch.int32, device=dev)
         self.timed_events = []  # (start, end) pairs around the dominant kernel
         # Row-parallel partial sums: the library's one-shot peer-memory all-reduce
         # for decode-sized vectors, NCCL for larger ones (QL_TP_NCCL=1 forces NCCL).
@@ -243,10 +246,14 @@ class DecodeStack:
         Q, rbh = self.Q, self.Q.row_bytes(md.qtype, md.hidden)
         h, ops = self.h.data_ptr(), []
         st = (lambda xs, ys: {"x_stride": xs, "y_stride": ys}) if batch else (lambda xs, ys: {})
+        # RoPE on the q rows and (when this rank holds whole k heads) the k rows
+        rope_rows = self.qo_len + (self.kv_len if self.kv_len % md.head_dim == 0 else 0)
+        rope = dict(rope_pos=self.pos.data_ptr(), rope_theta=md.rope_theta, rope_rows=rope_rows,
+                    head_dim=md.head_dim)
         for L in self.layers:
             ops.append(Q.chain_op(Q.OP_STORE, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rbh] * 3,
                                   [self.qo_len, self.kv_len, self.kv_len], md.hidden, h, self.qkv.data_ptr(),
-                                  L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr(), **st(md.hidden, self.qkv_w)))
+                                  L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr(), **st(md.hidden, self.qkv_w), **rope))
             ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [Q.row_bytes(md.qtype, self.qo_len)], [md.hidden],
                                   self.qo_len, self.qkv.data_ptr(), h, reduce=self.world > 1, **st(self.qkv_w, md.hidden)))
             if self.world == 1 and not batch and os.environ.get("QL_CHAIN_MLP", "1") != "0":

@@ -214,11 +214,14 @@ class ChainOp(C.Structure):
                 ("w", C.c_void_p * 3), ("row_bytes", C.c_size_t * 3), ("rows", C.c_int32 * 3),
                 ("in_dim", C.c_int32), ("x", C.c_void_p), ("gamma", C.c_void_p), ("eps", C.c_float),
                 ("bias", C.c_void_p), ("y", C.c_void_p), ("argmax_idx", C.c_void_p), ("argmax_offset", C.c_int32),
-                ("reduce", C.c_int32), ("x_stride", C.c_int64), ("y_stride", C.c_int64)]
+                ("reduce", C.c_int32), ("x_stride", C.c_int64), ("y_stride", C.c_int64),
+                ("rope_pos", C.c_void_p), ("rope_theta", C.c_float), ("rope_rows", C.c_int32),
+                ("head_dim", C.c_int32)]
 
 
 def chain_op(kind, weights, row_bytes, rows, in_dim, x, y, gamma=None, eps=0.0, bias=None, argmax_idx=None,
-             argmax_offset=0, quant_type=Q4_K, reduce=False, x_stride=0, y_stride=0):
+             argmax_offset=0, quant_type=Q4_K, reduce=False, x_stride=0, y_stride=0, rope_pos=None, rope_theta=0.0,
+             rope_rows=0, head_dim=0):
     op = ChainOp()
     op.kind, op.quant_type, op.nsrc, op.in_dim = kind, quant_type, len(weights), in_dim
     for i, (w, rb, r) in enumerate(zip(weights, row_bytes, rows)):
@@ -226,6 +229,7 @@ def chain_op(kind, weights, row_bytes, rows, in_dim, x, y, gamma=None, eps=0.0, 
     op.x, op.y, op.gamma, op.eps, op.bias = x, y, gamma, eps, bias
     op.argmax_idx, op.argmax_offset, op.reduce = argmax_idx, argmax_offset, 1 if reduce else 0
     op.x_stride, op.y_stride = x_stride, y_stride
+    op.rope_pos, op.rope_theta, op.rope_rows, op.head_dim = rope_pos, rope_theta, rope_rows, head_dim
     return op
 
 

@@ -102,6 +102,10 @@ struct __align__(128) BOp {
     int ss_in;            // slot holding the sums of squares of this op's input rows; -1: sum x here
     int ss_out;           // slot this op's epilogue sums its output's squares into; -1: none
     AmaxOut amax;
+    const int *rope_pos;  // RoPE on rows [0, rope_rows): positions per token
+    float rope_theta;
+    int rope_rows, head_dim;
+    __device__ float bias_at(int row) const { return bias != nullptr ? bias[row] : 0.f; }
 };
 
 struct BArgs {
@@ -543,6 +547,17 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                                 __stcg(yp, out);
                             } else {
                                 out += bias;
+                                if (row < o.rope_rows) {
+                                    // RoPE: rows i and i + half of a head pair up (the reference's
+                                    // rotation, kernel.cu:186-260); both lie in this tile
+                                    const int hd = o.head_dim, half = hd >> 1, pi = row % hd;
+                                    const int i = pi % half, rp = r + (pi < half ? half : -half);
+                                    const float xp = tile_sum(tk, rp) * nrm + o.bias_at(tile * kBRows + rp);
+                                    const float inv_freq = 1.0f / powf(o.rope_theta, (float)(2 * i) / (float)hd);
+                                    const float ang = (float)__ldg(o.rope_pos + tk) * inv_freq;
+                                    const float c = cosf(ang), sn = sinf(ang);
+                                    out = pi < half ? out * c - xp * sn : out * c + xp * sn;
+                                }
                                 if (yp) *yp = out;
                             }
                             if (o.amax.amax != nullptr) key = amax_key(out, (uint32_t)(row + o.amax.offset));
@@ -697,6 +712,18 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
         o.ys = q.y_stride ? q.y_stride : total;
         if (q.y && o.ys < total) return set_last_error(QL_EINVAL, (what + ": y_stride below the output width").c_str());
         o.ss_in = o.ss_out = -1;
+        if (q.rope_rows > 0) {
+            const int hd = q.head_dim;
+            const int limit = nsrc == 3 ? o.split1 : total;  // sources 0 and 1 only (q, k)
+            if (q.kind != QL_OP_STORE || q.argmax_idx || !q.rope_pos || (hd != 32 && hd != 64 && hd != 128) ||
+                q.rope_rows % hd || q.rope_rows > limit || (nsrc >= 2 && q.rope_rows > o.split0 && o.split0 % hd))
+                return set_last_error(QL_EINVAL, (what + ": RoPE needs a STORE op without argmax, rope_pos, head_dim "
+                                                         "32, 64 or 128 and rope_rows whole heads of sources 0 and 1").c_str());
+            o.rope_pos = q.rope_pos;
+            o.rope_theta = q.rope_theta;
+            o.rope_rows = q.rope_rows;
+            o.head_dim = hd;
+        }
         if (q.argmax_idx) {
             if (q.kind != QL_OP_STORE) return set_last_error(QL_EINVAL, (what + ": argmax needs a store op").c_str());
             o.amax.idx = q.argmax_idx;

@@ -50,6 +50,7 @@ constexpr int kMlpSmem = 2048 + 128;                 // MLP chunk activations (f
 
 struct __align__(128) ChainOp {
     CUtensorMap tmap[3];   // Q4_K sources {144, blocks, rows}, box {144, 7, 32}
+    CUtensorMap tmap16[2]; // RoPE: sources 0 and 1 with 16-row boxes (a row group = two half boxes)
     int kind;              // ChainKind
     int nmat;              // 2 for SwiGLU (gate, up), else 1
     int split[2];          // stacked sources: first rows of sources 1 and 2
@@ -77,6 +78,13 @@ struct __align__(128) ChainOp {
     int half_rows;          // MLP: down rows [0, half_rows) go to the even CTA of a pair, the rest to the odd one
     int nunits;             // MLP: 2 x (FFN rows / 256)
     long long cells;        // MLP: first pair-exchange cell ([nunits][128])
+    // RoPE on output rows [0, rope_rows): row group g of that range holds rows 16q .. 16q + 15 and
+    // half + 16q .. half + 16q + 15 of head (32 g) / head_dim, q = ((32 g) % head_dim) / 32, so that
+    // lanes l and l ^ 16 of the finisher hold the two rows a rotation pairs
+    const int *rope_pos;
+    float rope_theta;
+    int rope_rows;
+    int rope_half;          // head_dim / 2
 };
 static_assert(sizeof(ChainOp) % 128 == 0, "descriptor copies stay 128-byte aligned");
 // Descriptor words copied to shared memory per op: everything after the tensor maps.  Reads of
@@ -379,9 +387,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             // the descriptor's scalars in registers: reloads after the waits below would miss L1
             const ChainOp &o = a.ops[p];
             const int kind = o.kind, nmat = o.nmat, bu = o.bu, U = o.U, split0 = o.split[0], split1 = o.split[1];
+            const int rope_rows = o.rope_rows, rope_half = o.rope_half;
             const int nunits = o.nunits, half_rows = o.half_rows, rows_d = o.rows_d;
             const Plan plan = o.plan;
             for (int i = 0; i < ((nmat == 2 && kind != kOpMlp) ? 2 : 3); ++i) tensormap_acquire(&o.tmap[i]);
+            if (rope_rows > 0) {
+                tensormap_acquire(&o.tmap16[0]);
+                tensormap_acquire(&o.tmap16[1]);
+            }
             if (kind == kOpMlp) {
                 // per unit: the half chunk's gate/up rows (4 row groups x all blocks), then the
                 // down projection's block column of the chunk over this half's rows
@@ -459,7 +472,17 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     const int lrow = row0 - (src == 0 ? 0 : (src == 1 ? split0 : split1));
                     const int nbox = st.ue - st.us > bu ? 2 : 1;
                     mbar_arrive_expect_tx(&full[slot], live ? (uint32_t)nbox * kb : 0u);
-                    if (live) {
+                    if (live && row0 < rope_rows) {
+                        // RoPE group: rows 16q.. and half + 16q.. of the head, as two 16-row half boxes
+                        // that land where one 32-row box would (rows are contiguous in the slot)
+                        const int hd = 2 * rope_half, hb = lrow / hd * hd, q16 = 16 * ((lrow % hd) / 32);
+                        const int ra = hb + q16, rbw = hb + rope_half + q16;
+                        const uint32_t hoff = 16u * (uint32_t)bu * 144u;
+                        for (int b2 = 0; b2 < nbox; ++b2) {
+                            tma_load_3d_hint(sb + b2 * kb, &o.tmap16[src], 0, st.us + b2 * bu, ra, &full[slot], pol);
+                            tma_load_3d_hint(sb + b2 * kb + hoff, &o.tmap16[src], 0, st.us + b2 * bu, rbw, &full[slot], pol);
+                        }
+                    } else if (live) {
                         tma_load_3d_hint(sb, &o.tmap[src], 0, st.us, lrow, &full[slot], pol);
                         if (nbox == 2) tma_load_3d_hint(sb + kb, &o.tmap[src], 0, st.us + bu, lrow, &full[slot], pol);
                     }
@@ -571,7 +594,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                 const int bsel = gi & 1;
                 // loads the epilogue needs, issued before waiting for the consumers: the bias, and the
                 // residual when its last writer finished before op p-1 started (o.pre_y)
-                const int vv = g * kRowGroup + lane;
+                // output row of this lane (RoPE groups hold two 16-row halves of a head)
+                int vv = g * kRowGroup + lane;
+                if (vv < o.rope_rows) {
+                    const int hd = 2 * o.rope_half, hb = vv / hd * hd, q16 = 16 * ((vv % hd) / 32);
+                    vv = hb + q16 + (lane & 15) + ((lane & 16) ? o.rope_half : 0);
+                }
                 if (o.pre_y && p >= 2 && lane == 0 && !*reinterpret_cast<volatile int *>(abort_flag)) {
                     // a CTA with no row group in op p-1 gets here without having waited for op p-2
                     const unsigned *d2 = a.done + (p - 2);
@@ -628,10 +656,23 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                         if (lane == 0) a.counters[g] = 0u;
                     }
                 }
-                const int v = g * kRowGroup + lane;
+                const int v = vv;
                 if (finish) {
                     const float nrm = o.gamma != nullptr ? inv_rms[0] : 1.0f;
                     float out = 0.f;
+                    // RoPE group (warp-uniform): rotate the pair x1 = row i, x2 = row i + half held by
+                    // lanes l and l ^ 16 (the reference's rotation, kernel.cu:186-260)
+                    const bool rope = g * kRowGroup < o.rope_rows;
+                    float rot = 0.f;
+                    if (rope) {
+                        const float x = val[0] * nrm + bias_v;
+                        const float xp = __shfl_xor_sync(0xffffffffu, x, 16);
+                        const int i = (v % (2 * o.rope_half)) % o.rope_half;
+                        const float inv_freq = 1.0f / powf(o.rope_theta, (float)(2 * i) / (float)(2 * o.rope_half));
+                        const float ang = (float)__ldg(o.rope_pos) * inv_freq;
+                        const float c = cosf(ang), sn = sinf(ang);
+                        rot = (lane & 16) ? x * c + xp * sn : x * c - xp * sn;
+                    }
                     if (v < o.rows) {
                         float *yp = o.y + v;
                         if (o.kind == kOpSwiglu) {
@@ -641,6 +682,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                         } else {
                             out = val[0] * nrm;
                             if (o.bias != nullptr) out += bias_v;
+                            if (rope) out = rot;
                             if (o.kind == kOpAdd && !o.reduce) {  // residual written by other SMs: L2, not L1
                                 const float yn = (o.pre_y ? res_v : __ldcg(yp)) + out;
                                 __stcg(yp, yn);
@@ -1110,6 +1152,22 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         for (int s = nsrc; s < 3; ++s) {
             o.tmap[s] = o.tmap[nsrc - 1];
             if (s < 2 && q.kind != QL_OP_SWIGLU) o.split[s] = total;
+        }
+        if (q.rope_rows > 0) {
+            const int hd = q.head_dim;
+            const int limit = nsrc == 3 ? o.split[1] : total;  // sources 0 and 1 only (q, k)
+            if (q.kind != QL_OP_STORE || q.argmax_idx || !q.rope_pos || hd <= 0 || hd % 32 || q.rope_rows % hd ||
+                q.rope_rows > limit || (nsrc >= 2 && q.rope_rows > o.split[0] && o.split[0] % hd))
+                return set_last_error(QL_EINVAL, (what + ": RoPE needs a STORE op without argmax, rope_pos, head_dim a "
+                                                         "multiple of 32 and rope_rows whole heads of sources 0 and 1").c_str());
+            for (int s = 0; s < (nsrc < 2 ? nsrc : 2); ++s)
+                if (!q4k_tensor_map_public(&o.tmap16[s], q.w[s], blocks, (uint64_t)q.rows[s], q.row_bytes[s], o.bu, 16))
+                    return set_last_error(QL_ECUDA, (what + ": tensor map").c_str());
+            if (nsrc < 2) o.tmap16[1] = o.tmap16[0];
+            o.rope_pos = q.rope_pos;
+            o.rope_theta = q.rope_theta;
+            o.rope_rows = q.rope_rows;
+            o.rope_half = hd / 2;
         }
         o.kind = q.kind == QL_OP_STORE ? kOpStore : q.kind == QL_OP_ADD ? kOpAdd : kOpSwiglu;
         o.nmat = q.kind == QL_OP_SWIGLU ? 2 : 1;

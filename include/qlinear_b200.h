@@ -143,6 +143,17 @@ typedef struct ql_chain_op {
      * x and of y; 0 = rows packed (in_dim, resp. the op's total output rows) */
     int64_t x_stride;
     int64_t y_stride;
+    /* RoPE fused into a STORE op (no reference twin as a fusion; the reference rotates q and k in
+     * its attention kernels, kernel.cu:186-260): output rows [0, rope_rows) -- whole heads of
+     * head_dim rows, e.g. the q and k rows of a stacked q/k/v -- are rotated after bias, pairing
+     * rows i and i + head_dim/2 of each head: (x1, x2) -> (x1 c - x2 s, x2 c + x1 s), angle =
+     * pos / rope_theta^(2i / head_dim).  rope_pos: device int32, the position (batched chains: one
+     * per token).  rope_rows = 0 disables it; head_dim a multiple of 32, at most 128 in batched
+     * chains; no argmax on a RoPE op. */
+    const int32_t *rope_pos;
+    float rope_theta;
+    int32_t rope_rows;
+    int32_t head_dim;
 } ql_chain_op;
 QL_API int ql_gemv_chain_create(const ql_chain_op *ops, int nops, void **chain);
 /* Tensor-parallel chain: ops with reduce != 0 (row-parallel ADD projections) sum their

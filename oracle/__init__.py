@@ -217,14 +217,37 @@ def host_cores() -> int:
 # dict of quantized weights wq, wk, wv, wo, wg, wu, wd ([rows, row_bytes] uint8) and
 # float32 ln1, ln2, bqkv.
 # ----------------------------------------------------------------------------
-def linear_stack_token(layers, lm, lnf, h, t=Q4_K, eps=1e-6, order=1, with_logits=True):
-    """h (float32 [hidden]) -> (h after the stack, logits or None, greedy token)."""
+def rope(x, pos, theta, head_dim, rows):
+    """Rotary embedding of rows [0, rows) of x[..., :] (whole heads of head_dim), restating the
+    reference's rotation (kernel.cu:186-260): for i < head_dim/2, inv_freq = 1 / powf(theta,
+    2i / head_dim) and angle = pos * inv_freq in fp32, then (x1, x2) -> (x1 c - x2 s, x2 c + x1 s)
+    for x1 = row i and x2 = row i + head_dim/2 of each head.  x: [tokens, n]; pos: one per token."""
+    x = np.array(x, np.float64, copy=True)
+    half = head_dim // 2
+    i = np.arange(half, dtype=np.float32)
+    inv = np.float32(1.0) / np.power(np.float32(theta), (np.float32(2) * i) / np.float32(head_dim))
+    for tk, p in enumerate(np.atleast_1d(pos)):
+        ang = (np.float32(p) * inv).astype(np.float64)
+        c, s = np.cos(ang), np.sin(ang)
+        for h0 in range(0, rows, head_dim):
+            x1, x2 = x[tk, h0:h0 + half].copy(), x[tk, h0 + half:h0 + head_dim].copy()
+            x[tk, h0:h0 + half] = x1 * c - x2 * s
+            x[tk, h0 + half:h0 + head_dim] = x2 * c + x1 * s
+    return x
+
+
+def linear_stack_token(layers, lm, lnf, h, t=Q4_K, eps=1e-6, order=1, with_logits=True, rope_args=None):
+    """h (float32 [hidden]) -> (h after the stack, logits or None, greedy token).  rope_args
+    (pos, theta, head_dim, rows): RoPE on the first `rows` q/k/v outputs, as the chain's fused
+    epilogue does."""
     h = np.array(h, np.float32, copy=True).reshape(1, -1)
     H = h.shape[1]
     for L in layers:
         xn = rmsnorm(h, L["ln1"], eps)
         parts = [gemv(t, L[n], L[n].shape[1], xn, L[n].shape[0], H, 1, order) for n in ("wq", "wk", "wv")]
         qkv = np.concatenate(parts, axis=1) + np.asarray(L["bqkv"], np.float32)[None, :]
+        if rope_args is not None:
+            qkv = rope(qkv, *rope_args).astype(np.float32)
         qw = L["wq"].shape[0]
         h = gemv_add(t, L["wo"], L["wo"].shape[1], qkv[:, :qw], h[0], H, qw, order).reshape(1, -1)
         xn = rmsnorm(h, L["ln2"], eps)
@@ -245,9 +268,10 @@ def _dq(t, w, k, chunk=16384):
     return out
 
 
-def linear_stack_batch(layers, lm, lnf, h, t=Q4_K, eps=1e-6):
+def linear_stack_batch(layers, lm, lnf, h, t=Q4_K, eps=1e-6, rope_args=None):
     """linear_stack_token for a batch of tokens (h: [M, hidden]): the same steps with the exact
-    dequantized weights and float64 accumulation (numpy matmul).  Returns (h, logits [M, vocab])."""
+    dequantized weights and float64 accumulation (numpy matmul).  Returns (h, logits [M, vocab]).
+    rope_args (positions [M], theta, head_dim, rows) as linear_stack_token."""
     h = np.array(h, np.float64, copy=True)
     H = h.shape[1]
 
@@ -256,6 +280,8 @@ def linear_stack_batch(layers, lm, lnf, h, t=Q4_K, eps=1e-6):
     for L in layers:
         xn = norm(h, L["ln1"])
         qkv = np.concatenate([xn @ _dq(t, L[n], H).T for n in ("wq", "wk", "wv")], axis=1) + L["bqkv"]
+        if rope_args is not None:
+            qkv = rope(qkv, *rope_args)
         qw = L["wq"].shape[0]
         h = h + qkv[:, :qw] @ _dq(t, L["wo"], qw).T
         xn = norm(h, L["ln2"])
@@ -266,14 +292,17 @@ def linear_stack_batch(layers, lm, lnf, h, t=Q4_K, eps=1e-6):
     return h, logits
 
 
-def greedy_decode(layers, lm, lnf, table, first_token, steps, t=Q4_K, emb_type=Q4_K, eps=1e-6, order=1):
+def greedy_decode(layers, lm, lnf, table, first_token, steps, t=Q4_K, emb_type=Q4_K, eps=1e-6, order=1,
+                  rope=None):
     """Greedy loop: token -> quantized embedding row (quant_embedding_kernel, kernel.cu:2677-2693)
-    -> linear stack -> argmax -> next token.  Returns (tokens, per-step (best, runner-up) logit margins)."""
+    -> linear stack -> argmax -> next token.  rope (theta, head_dim, rows): RoPE at position = step
+    index.  Returns (tokens, per-step (best, runner-up) logit margins)."""
     H = lm.shape[1] // BLOCK[t][1] * BLOCK[t][0]
     tok, toks, margins = int(first_token), [], []
-    for _ in range(steps):
+    for step in range(steps):
         h = embedding(emb_type, np.array([tok], np.int32), table, table.shape[1], H)[0]
-        _, logits, tok = linear_stack_token(layers, lm, lnf, h, t, eps, order)
+        ra = None if rope is None else (step, *rope)
+        _, logits, tok = linear_stack_token(layers, lm, lnf, h, t, eps, order, rope_args=ra)
         top2 = np.partition(logits, -2)[-2:]
         toks.append(tok)
         margins.append(float(top2[1] - top2[0]))

@@ -59,18 +59,27 @@ def _model(H, QW, KV, F, V, layers, seed):
             "dims": (H, QW, KV, F, V)}
 
 
-def _run(m, M, h0, replays=1):
+THETA = 1e6
+
+
+def _positions(M):
+    return (5 + 3 * np.arange(M)).astype(np.int32)
+
+
+def _run(m, M, h0, replays=1, head_dim=128):
+    """The stack as one batched chain, RoPE on q and k (rows of whole heads) at _positions(M)."""
     import torch
     H, QW, KV, F, V = m["dims"]
     rb = lambda k: Q.row_bytes(Q.Q4_K, k)
     b = {"h": dev(h0.copy()), "qkv": torch.zeros((M, QW + 2 * KV), device="cuda:0"),
          "act": torch.zeros((M, F), device="cuda:0"), "logits": torch.zeros((M, V), device="cuda:0"),
-         "tok": torch.full((M,), -1, dtype=torch.int32, device="cuda:0")}
+         "tok": torch.full((M,), -1, dtype=torch.int32, device="cuda:0"), "pos": dev(_positions(M))}
     hp, ops = b["h"].data_ptr(), []
     for L in m["dev"]:
         ops.append(Q.chain_op(Q.OP_STORE, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rb(H)] * 3,
                               [QW, KV, KV], H, hp, b["qkv"].data_ptr(), L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr(),
-                              x_stride=H, y_stride=QW + 2 * KV))
+                              x_stride=H, y_stride=QW + 2 * KV, rope_pos=b["pos"].data_ptr(), rope_theta=THETA,
+                              rope_rows=QW + KV, head_dim=head_dim))
         ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [rb(QW)], [H], QW, b["qkv"].data_ptr(), hp,
                               x_stride=QW + 2 * KV, y_stride=H))
         ops.append(Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rb(H)] * 2, [F, F], H, hp,
@@ -92,8 +101,10 @@ def _run(m, M, h0, replays=1):
     return outs
 
 
-def _check(m, M, h0, outs, bar=2.5e-3):
-    h_ref, lg_ref = O.linear_stack_batch(m["host"], m["lm_h"], m["lnf_h"], h0, eps=EPS)
+def _check(m, M, h0, outs, bar=2.5e-3, head_dim=128):
+    H, QW, KV, F, V = m["dims"]
+    h_ref, lg_ref = O.linear_stack_batch(m["host"], m["lm_h"], m["lnf_h"], h0, eps=EPS,
+                                         rope_args=(_positions(M), THETA, head_dim, QW + KV))
     h, lg, tok = outs[0]
     e_h, e_lg = rel_l2(h, h_ref), rel_l2(lg, lg_ref)
     print(f"batched chain M={M}: h rel_l2 {e_h:.2e}, logits rel_l2 {e_lg:.2e}")

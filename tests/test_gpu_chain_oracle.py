@@ -56,13 +56,19 @@ def model():
     Q.check_device()
 
 
-def _chain(m, b):
-    """The bench's one-GPU op list: qkv, o + residual, fused MLP per layer; LM head + argmax."""
+THETA, HEAD = 1e6, 128
+
+
+def _chain(m, b, rope=False):
+    """The bench's one-GPU op list: qkv (RoPE on q and k when rope), o + residual, fused MLP per
+    layer; LM head + argmax."""
     rb = lambda k: Q.row_bytes(Q.Q4_K, k)
     h, ops = b["h"].data_ptr(), []
+    rk = dict(rope_pos=b["pos"].data_ptr(), rope_theta=THETA, rope_rows=QW + KV, head_dim=HEAD) if rope else {}
     for L in m["dev"]:
         ops.append(Q.chain_op(Q.OP_STORE, [L["wq"].data_ptr(), L["wk"].data_ptr(), L["wv"].data_ptr()], [rb(H)] * 3,
-                              [QW, KV, KV], H, h, b["qkv"].data_ptr(), L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr()))
+                              [QW, KV, KV], H, h, b["qkv"].data_ptr(), L["ln1"].data_ptr(), EPS, L["bqkv"].data_ptr(),
+                              **rk))
         ops.append(Q.chain_op(Q.OP_ADD, [L["wo"].data_ptr()], [rb(QW)], [H], QW, b["qkv"].data_ptr(), h))
         ops.append(Q.chain_op(Q.OP_MLP, [L["wg"].data_ptr(), L["wu"].data_ptr(), L["wd"].data_ptr()],
                               [rb(H), rb(H), rb(F)], [F, F, H], H, h, h, L["ln2"].data_ptr(), EPS))
@@ -73,22 +79,39 @@ def _chain(m, b):
 
 def _bufs(torch):
     return {"h": torch.zeros(H, device="cuda:0"), "qkv": torch.zeros(QW + 2 * KV, device="cuda:0"),
-            "logits": torch.zeros(V, device="cuda:0"), "tok": torch.full((1,), -1, dtype=torch.int32, device="cuda:0")}
+            "logits": torch.zeros(V, device="cuda:0"), "tok": torch.full((1,), -1, dtype=torch.int32, device="cuda:0"),
+            "pos": torch.zeros(1, dtype=torch.int32, device="cuda:0")}
 
 
-def test_chain_matches_oracle_at_qwen2_7b_shapes(model):
+@pytest.mark.parametrize("rope", [False, True])
+def test_chain_matches_oracle_at_qwen2_7b_shapes(model, rope):
     import torch
     b = _bufs(torch)
+    b["pos"].fill_(37)
     h0 = np.random.default_rng(22).standard_normal(H).astype(np.float32)
-    chain = _chain(model, b)
+    chain = _chain(model, b, rope)
     try:
         b["h"].copy_(dev(h0))
         chain.run()
         h_dev, lg_dev, tok_dev = host(b["h"]), host(b["logits"]), int(host(b["tok"])[0])
+        qkv_dev = host(b["qkv"])
         Q.check_device()
     finally:
         chain.close()
-    h_ref, lg_ref, tok_ref = O.linear_stack_token(model["host"], model["lm_h"], model["lnf_h"], h0, eps=EPS)
+    ra = (37, THETA, HEAD, QW + KV) if rope else None
+    h_ref, lg_ref, tok_ref = O.linear_stack_token(model["host"], model["lm_h"], model["lnf_h"], h0, eps=EPS,
+                                                  rope_args=ra)
+    if rope:  # the last layer's q/k/v output, rotated, against the oracle's
+        L = model["host"][-1]
+        hl = O.linear_stack_token(model["host"][:-1], model["lm_h"], model["lnf_h"], h0, eps=EPS, rope_args=ra,
+                                  with_logits=False)[0]
+        xn = O.rmsnorm(hl.reshape(1, -1), L["ln1"], EPS)
+        qkv_ref = np.concatenate([O.gemv(Q.Q4_K, L[n], L[n].shape[1], xn, L[n].shape[0], H, 1, 1)
+                                  for n in ("wq", "wk", "wv")], axis=1) + L["bqkv"]
+        qkv_ref = O.rope(qkv_ref, 37, THETA, HEAD, QW + KV)[0]
+        e_qkv = rel_l2(qkv_dev, qkv_ref)
+        print(f"fused RoPE q/k/v at position 37: rel_l2 {e_qkv:.2e}")
+        assert e_qkv < 1e-4
     e_h, e_lg = rel_l2(h_dev, h_ref), rel_l2(lg_dev, lg_ref)
     print(f"chain vs oracle at Qwen2-7B shapes: h rel_l2 {e_h:.2e}, logits rel_l2 {e_lg:.2e}, tokens {tok_dev}/{tok_ref}")
     assert e_h < 1e-3 and e_lg < 1e-3
@@ -98,6 +121,8 @@ def test_chain_matches_oracle_at_qwen2_7b_shapes(model):
 
 
 def test_greedy_32_tokens_match_oracle(model):
+    """32 greedy steps, RoPE on q and k at position = step (the position is a device int, as in
+    the reference's graph-captured decode)."""
     import torch
     steps = 32
     b = _bufs(torch)
@@ -105,9 +130,10 @@ def test_greedy_32_tokens_match_oracle(model):
     hist = torch.zeros(steps, dtype=torch.int32, device="cuda:0")
     b["tok"].fill_(first)
     rbh = Q.row_bytes(Q.Q4_K, H)
-    chain = _chain(model, b)
+    chain = _chain(model, b, rope=True)
     try:
         for i in range(steps):  # token -> embedding -> stack -> argmax -> token, no host round trip
+            b["pos"].fill_(i)
             Q.quant_embedding(Q.Q4_K, b["tok"].data_ptr(), b["h"].data_ptr(), model["table"].data_ptr(), rbh, H, 1)
             chain.run()
             hist[i:i + 1].copy_(b["tok"])
@@ -116,7 +142,7 @@ def test_greedy_32_tokens_match_oracle(model):
     finally:
         chain.close()
     want, margins = O.greedy_decode(model["host"], model["lm_h"], model["lnf_h"], model["table_h"], first, steps,
-                                    eps=EPS)
+                                    eps=EPS, rope=(THETA, HEAD, QW + KV))
     print(f"greedy tokens: {got[:8]}..., distinct {len(set(got))}, smallest oracle margin {min(margins):.3e}")
     if got != want:
         i = next(j for j in range(steps) if got[j] != want[j])
