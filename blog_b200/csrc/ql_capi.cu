@@ -345,10 +345,10 @@ struct TcJob {
     AmaxOut amax{};  // fused argmax (plain only; amax.amax non-null = on, filled by run_gemm_tc)
 };
 
-// Whether the tensor-core GEMM can run the job: Q4_K, K % 256, row strides that are
+// Whether the tensor-core GEMM can run the job: Q4_K or Q4_0, K % 256, row strides that are
 // TMA-legal, and (stacked) sources that end on 256-row tile boundaries.
 bool tc_eligible(int t, const TcJob &j) {
-    if (t != kQ4_K || j.K % 256 != 0) return false;
+    if ((t != kQ4_K && t != kQ4_0) || j.K % 256 != 0) return false;
     for (int i = 0; i < j.nsrc; ++i) {
         if (j.rb[i] % 16 != 0) return false;
         if (j.epi == kGemmPlain && i < j.nsrc - 1 && j.rows[i] % kGemmBN != 0) return false;
@@ -356,7 +356,21 @@ bool tc_eligible(int t, const TcJob &j) {
     return true;
 }
 
-int run_gemm_tc(const TcJob &j, const char *what) {
+// A Q4_0 matrix as a 2-D byte tensor {row_bytes, rows} with boxes of 144 B (8 blocks = 256
+// inputs) x box_rows rows (row_bytes a multiple of 16: in_dim a multiple of 256).
+bool q40_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size_t row_bytes, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {144, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int run_gemm_tc(int t, const TcJob &j, const char *what) {
     int st;
     Workspace *ws = workspace(&st);
     if (!ws) return st;
@@ -384,8 +398,9 @@ int run_gemm_tc(const TcJob &j, const char *what) {
     int end = 0;
     for (int i = 0; i < 3; ++i) {
         if (i < j.nsrc) {
-            if (!q4k_tensor_map(&a.tm_w[i], j.w[i], nsb, (uint64_t)j.rows[i], j.rb[i], 1, BNO))
-                return fail(QL_ECUDA, std::string(what) + ": weight tensor map");
+            const bool okm = t == kQ4_0 ? q40_tensor_map(&a.tm_w[i], j.w[i], (uint64_t)j.rows[i], j.rb[i], BNO)
+                                        : q4k_tensor_map(&a.tm_w[i], j.w[i], nsb, (uint64_t)j.rows[i], j.rb[i], 1, BNO);
+            if (!okm) return fail(QL_ECUDA, std::string(what) + ": weight tensor map");
             end += j.rows[i];
         } else {
             a.tm_w[i] = a.tm_w[j.nsrc - 1];
@@ -413,6 +428,7 @@ int run_gemm_tc(const TcJob &j, const char *what) {
     a.N = N;
     a.K = j.K;
     a.nsb = nsb;
+    a.fmt = t;
     a.ksplit = ks;
     a.err = ws->err;
     if (!swiglu && j.amax.amax != nullptr) {
@@ -539,7 +555,7 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     if ((st = check_act(x, xs, gamma, "ql_quant_gemv"))) return st;
     {
         const TcJob j = plain_job(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate);
-        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_gemv");
+        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_gemv");
     }
     GemvArgs a = blank();
     a.w[0] = w;
@@ -578,7 +594,7 @@ int ql_quant_gemv_argmax_ex(int32_t t, const uint8_t *w, size_t rb, const float 
     {
         TcJob j = plain_job(w, rb, x, xs, logits, ls, out_dim, in_dim, m, gamma, eps, nullptr, 0);
         j.amax = am;
-        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_gemv_argmax_ex");
+        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_gemv_argmax_ex");
     }
     GemvArgs a = blank();
     a.w[0] = w;
@@ -609,10 +625,10 @@ int ql_quant_matmul_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, i
     const TcJob j = plain_job(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate);
     const bool tc = tc_eligible(t, j);
     if (path == QL_PATH_TENSOR && !tc)
-        return fail(QL_EINVAL, "ql_quant_matmul_ex: the tensor-core path needs Q4_K, in_dim % 256 == 0 and "
-                               "row_bytes % 16 == 0");
+        return fail(QL_EINVAL, "ql_quant_matmul_ex: the tensor-core path needs Q4_K or Q4_0, in_dim % 256 == 0 "
+                               "and row_bytes % 16 == 0");
     if (path == QL_PATH_TENSOR || (path == QL_PATH_AUTO && tc && m >= tc_min_tokens()))
-        return run_gemm_tc(j, "ql_quant_matmul_ex");
+        return run_gemm_tc(t, j, "ql_quant_matmul_ex");
     GemvArgs a = blank();
     a.w[0] = w;
     a.row_bytes[0] = rb;
@@ -672,7 +688,7 @@ int ql_quant_gemv_stacked_ex(int32_t t, int nsrc, const uint8_t *const *w, const
             j.rb[i] = rb[i];
             j.rows[i] = rows[i];
         }
-        if (tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_gemv_stacked_ex");
+        if (tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_gemv_stacked_ex");
     }
     a.rows = total;
     a.K = in_dim;
@@ -718,7 +734,7 @@ int ql_quant_swiglu_ex(int32_t t, const uint8_t *g, const uint8_t *u, size_t grb
         j.w[1] = u;
         j.rb[1] = urb;
         j.rows[1] = ffn_dim;
-        if (tc_eligible(t, j)) return run_gemm_tc(j, "ql_quant_swiglu");
+        if (tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_swiglu");
     }
     GemvArgs a = blank();
     a.w[0] = g;

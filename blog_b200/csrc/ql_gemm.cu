@@ -167,12 +167,52 @@ __device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
 }
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
+// Q4_0 chunk p (inputs 64p .. 64p + 63 of the 256-input step = blocks 2p, 2p + 1 of the row's
+// 8-block run at `row`, 18 B each: f16 d, then qs[16] with element i < 16 in the low nibble of
+// qs[i] and element i + 16 in the high nibble) -> 8 groups of 8 f16 in the order the activation
+// prep uses (0, 2, 1, 3, 4, 6, 5, 7), value d * (q - 8) rounded once.  A block at an even index
+// starts 4-byte aligned (qs then 2 bytes off), at an odd index 2 bytes off (qs aligned).
+__device__ __forceinline__ void dequant_q40_chunk(const uint8_t *row, int p, uint8_t *brow, int r) {
+#pragma unroll
+    for (int bb = 0; bb < 2; ++bb) {
+        const int b = 2 * p + bb;
+        const uint8_t *base = row + 18 * b;
+        uint32_t q[4], dbits;
+        if ((b & 1) == 0) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(base);
+            const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+            dbits = w0 & 0xFFFFu;
+            q[0] = __byte_perm(w0, w1, 0x5432);
+            q[1] = __byte_perm(w1, w2, 0x5432);
+            q[2] = __byte_perm(w2, w3, 0x5432);
+            q[3] = __byte_perm(w3, w4, 0x5432);
+        } else {
+            dbits = *reinterpret_cast<const uint16_t *>(base);
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(base + 2);
+            q[0] = w[0]; q[1] = w[1]; q[2] = w[2]; q[3] = w[3];
+        }
+        const float d = half_bits_to_float(dbits);
+        const __half2 D = __float2half2_rn(d), M = __float2half2_rn(-8.0f * d);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {  // elements 8jj .. 8jj + 7 of the block
+            const int sh = jj < 2 ? 0 : 4;  // low nibbles for elements < 16, high nibbles above
+            const uint32_t w0 = q[2 * (jj & 1)] >> sh, w1 = q[2 * (jj & 1) + 1] >> sh;
+            uint4 o;
+            o.x = deq2(w0 & 0x000F000Fu, D, M);
+            o.y = deq2((w0 >> 8) & 0x000F000Fu, D, M);
+            o.z = deq2(w1 & 0x000F000Fu, D, M);
+            o.w = deq2((w1 >> 8) & 0x000F000Fu, D, M);
+            *reinterpret_cast<uint4 *>(brow + (((4 * bb + jj) ^ (r & 7)) << 4)) = o;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // The GEMM.  EPI = kGemmPlain: 256 output columns per tile from one of up to
 // three stacked sources.  EPI = kGemmSwiglu: 128 output columns per tile, the
 // accumulator's columns 0-127 from the gate rows and 128-255 from the up rows.
 // ---------------------------------------------------------------------------
-template <int EPI>
+template <int EPI, int FMT>  // FMT: kQ4_K or kQ4_0 (both 144 B of each row per 256 inputs)
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_constant__ GemmArgs a) {
     constexpr int BNO = EPI == kGemmSwiglu ? kGemmBN / 2 : kGemmBN;  // output columns per tile
     extern __shared__ uint8_t smem_raw[];
@@ -227,7 +267,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
             auto load_raw = [&](int sl) {
                 const int rs = sl % kGemmNR;
                 mbar_arrive_expect_tx(&r_full[rs], kGemmRBytes);
-                if (EPI == kGemmSwiglu) {
+                if (FMT == kQ4_0) {  // 2-D byte view {row_bytes, rows}: 144 B = 8 blocks per step
+                    if (EPI == kGemmSwiglu) {
+                        tma_load_2d(sR + rs * kGemmRBytes, &a.tm_w[0], (s0 + sl) * 144, n0, &r_full[rs]);
+                        tma_load_2d(sR + rs * kGemmRBytes + BNO * 144, &a.tm_w[1], (s0 + sl) * 144, n0, &r_full[rs]);
+                    } else {
+                        tma_load_2d(sR + rs * kGemmRBytes, &a.tm_w[src], (s0 + sl) * 144, row0, &r_full[rs]);
+                    }
+                } else if (EPI == kGemmSwiglu) {
                     tma_load_3d(sR + rs * kGemmRBytes, &a.tm_w[0], 0, s0 + sl, n0, &r_full[rs]);
                     tma_load_3d(sR + rs * kGemmRBytes + BNO * 144, &a.tm_w[1], 0, s0 + sl, n0, &r_full[rs]);
                 } else {
@@ -303,7 +350,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                 break;
             }
             const uint8_t *blk = sR + rs * kGemmRBytes + r * 144;
-            const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+            const uint4 h = FMT == kQ4_K ? *reinterpret_cast<const uint4 *>(blk) : make_uint4(0u, 0u, 0u, 0u);
             const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
             // q4k_scale_min (reference kernel.cu:913-921), all eight sub-blocks as packed bytes
             const uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
@@ -321,6 +368,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                     ok = false;
                     break;
                 }
+                uint8_t *brow = sB + bs * kGemmBBytes + r * 128;
+                if (FMT == kQ4_0) {
+                    dequant_q40_chunk(blk, p, brow, r);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&b_full[bs]);
+                    continue;
+                }
                 const uint32_t scw = p < 2 ? sc03 : sc47, mw = p < 2 ? m03 : m47;
                 const int sh0 = 16 * (p & 1), sh1 = sh0 + 8;
                 const __half2 D0 = __float2half2_rn(d * (float)((scw >> sh0) & 0xFFu));
@@ -330,7 +385,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
                 const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
                 const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
                 const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                uint8_t *brow = sB + bs * kGemmBBytes + r * 128;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint32_t w0 = W[2 * j], w1 = W[2 * j + 1];
@@ -469,11 +523,12 @@ cudaError_t gemm_xprep_launch(const float *x, int64_t x_stride, const float *gam
     return cudaLaunchKernelEx(&cfg, gemm_xprep_kernel, x, x_stride, gamma, eps, xh, rinv, K);
 }
 
-template <int EPI>
+template <int EPI, int FMT>
 cudaError_t gemm_launch_t(const GemmArgs &a, cudaStream_t s) {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q4k_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+        cudaError_t e =
+            cudaFuncSetAttribute(gemm_q4k_kernel<EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
@@ -499,11 +554,13 @@ cudaError_t gemm_launch_t(const GemmArgs &a, cudaStream_t s) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, gemm_q4k_kernel<EPI>, a);
+    return cudaLaunchKernelEx(&cfg, gemm_q4k_kernel<EPI, FMT>, a);
 }
 
 cudaError_t gemm_q4k_launch(const GemmArgs &a, int epi, cudaStream_t s) {
-    return epi == kGemmSwiglu ? gemm_launch_t<kGemmSwiglu>(a, s) : gemm_launch_t<kGemmPlain>(a, s);
+    if (a.fmt == kQ4_0)
+        return epi == kGemmSwiglu ? gemm_launch_t<kGemmSwiglu, kQ4_0>(a, s) : gemm_launch_t<kGemmPlain, kQ4_0>(a, s);
+    return epi == kGemmSwiglu ? gemm_launch_t<kGemmSwiglu, kQ4_K>(a, s) : gemm_launch_t<kGemmPlain, kQ4_K>(a, s);
 }
 
 }  // namespace ql

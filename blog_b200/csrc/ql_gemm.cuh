@@ -74,6 +74,8 @@ struct GemmArgs {
     int ksplit;            // K ranges per output tile = cluster size along z (<= 8)
     int *err;
     AmaxOut amax;          // fused greedy argmax over the output columns (plain; amax.amax null = off)
+    int fmt;               // kQ4_K (tm_w 3-D views) or kQ4_0 (tm_w 2-D byte views {row_bytes, rows},
+                           // box {144, 256 or 128}: 8 blocks per 256 inputs)
 };
 
 bool gemv_pdl_enabled();  // programmatic dependent launch (always on)

@@ -80,7 +80,7 @@ QL_API int ql_quant_matmul(int32_t quant_type, const uint8_t *weight, size_t row
  * (gamma != NULL: scale_m = 1/sqrt(mean_k x[m,k]^2 + eps), g = gamma; else 1),
  * optional bias, accumulate != 0 adds into y.  path: QL_PATH_AUTO picks by shape;
  * QL_PATH_GEMV forces the CUDA-core streaming engine (fp32 activations, exact
- * decode); QL_PATH_TENSOR forces the tcgen05 tensor-core GEMM (Q4_K, in_dim a
+ * decode); QL_PATH_TENSOR forces the tcgen05 tensor-core GEMM (Q4_K or Q4_0, in_dim a
  * multiple of 256; activations and dequantized weights rounded to f16, fp32
  * accumulation; QL_EINVAL when the shape or dtype does not qualify). */
 #define QL_PATH_AUTO 0

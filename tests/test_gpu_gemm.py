@@ -1,4 +1,4 @@
-"""Parity of the tcgen05 prefill GEMM (Q4_K, called through the C ABI).
+"""Parity of the tcgen05 prefill GEMM (Q4_K and Q4_0, called through the C ABI).
 
 The tensor-core path rounds each activation row (after an exact power-of-two
 scale) and each dequantized weight to f16 and accumulates in fp32 on the tensor
@@ -57,6 +57,19 @@ def q4k_f16_operand(w, n, k):
     return out.reshape(n, k)
 
 
+def q40_f16_operand(w, n, k):
+    """Q4_0 weights as the tensor-core dequantizer rounds them: f16(d * (q - 8)), one rounding."""
+    b = w.reshape(n, k // 32, 18)
+    d = b[..., 0:2].copy().view(np.float16)[..., 0].astype(np.float64)
+    qs = b[..., 2:18].astype(np.int64)
+    q = np.concatenate([qs & 0xF, qs >> 4], axis=-1)  # elements 0..15 low nibbles, 16..31 high
+    return (d[..., None] * (q - 8)).astype(np.float16).astype(np.float64).reshape(n, k)
+
+
+def f16_operand(t, w, n, k):
+    return q40_f16_operand(w, n, k) if t == O.Q4_0 else q4k_f16_operand(w, n, k)
+
+
 def act_f16_operand(x, gamma=None, eps=0.0):
     """Activations as the tensor-core path sees them: f16(x * g * 2^k) * 2^-k (* RMSNorm factor)."""
     xg = x.astype(np.float64) * (gamma.astype(np.float64)[None, :] if gamma is not None else 1.0)
@@ -75,10 +88,10 @@ def act_f16_operand(x, gamma=None, eps=0.0):
     return out
 
 
-def run_tc(w, rb, x, n, k, m, gamma=None, eps=0.0, bias=None, y0=None, path=Q.PATH_TENSOR):
+def run_tc(w, rb, x, n, k, m, gamma=None, eps=0.0, bias=None, y0=None, path=Q.PATH_TENSOR, t=O.Q4_K):
     import torch
     y = dev(y0.copy()) if y0 is not None else torch.full((m, n), float("nan"), device="cuda:0")
-    Q.quant_matmul_ex(O.Q4_K, dev(w).data_ptr(), rb, dev(x).data_ptr(), k, y.data_ptr(), n, n, k, m,
+    Q.quant_matmul_ex(t, dev(w).data_ptr(), rb, dev(x).data_ptr(), k, y.data_ptr(), n, n, k, m,
                       dev(gamma).data_ptr() if gamma is not None else None, eps,
                       dev(bias).data_ptr() if bias is not None else None, y0 is not None, path)
     return host(y)
@@ -88,18 +101,46 @@ def run_tc(w, rb, x, n, k, m, gamma=None, eps=0.0, bias=None, y0=None, path=Q.PA
 SHAPES = [(256, 256, 128), (300, 512, 77), (512, 4096, 64), (1024, 2048, 256), (4096, 4096, 128), (100, 768, 8)]
 
 
+@pytest.mark.parametrize("t", [O.Q4_K, O.Q4_0])
 @pytest.mark.parametrize("n,k,m", SHAPES)
-def test_tc_gemm_matches_oracle_and_f16_operands(n, k, m):
-    w = make_weights(O.Q4_K, n, k, seed=n + 3 * k)
+def test_tc_gemm_matches_oracle_and_f16_operands(n, k, m, t):
+    w = make_weights(t, n, k, seed=n + 3 * k)
     x = _x(n + k + m, m, k)
-    rb = O.row_bytes(O.Q4_K, k)
-    got = run_tc(w, rb, x, n, k, m)
+    rb = O.row_bytes(t, k)
+    got = run_tc(w, rb, x, n, k, m, t=t)
     assert np.isfinite(got).all()
-    ref = O.gemv(O.Q4_K, w, rb, x, n, k, m, order=1)
+    ref = O.gemv(t, w, rb, x, n, k, m, order=1)
     err = rel_l2(got, ref)
     assert err < NORTH_STAR, err
-    ref16 = act_f16_operand(x) @ q4k_f16_operand(w, n, k).T
+    ref16 = act_f16_operand(x) @ f16_operand(t, w, n, k).T
     assert rel_l2(got, ref16) < EXACT_F16_OPERANDS
+
+
+def test_tc_gemm_q40_sweep_shape_and_swiglu():
+    """Q4_0 at a BASELINE sweep shape (N 11008, K 4096, M 512) and as a SwiGLU pair with a fused
+    RMSNorm, against the oracle."""
+    import torch
+    n, k, m = 11008, 4096, 512
+    w = make_weights(O.Q4_0, n, k, seed=91)
+    x = _x(92, m, k)
+    rb = O.row_bytes(O.Q4_0, k)
+    got = run_tc(w, rb, x, n, k, m, t=O.Q4_0)
+    err = rel_l2(got, O.gemv(O.Q4_0, w, rb, x, n, k, m, order=1))
+    print(f"Q4_0 tensor-core GEMM 11008x4096 M=512: rel_l2 {err:.2e}")
+    assert err < NORTH_STAR
+    f, k2, m2 = 1024, 2048, 64
+    g, u = make_weights(O.Q4_0, f, k2, seed=93), make_weights(O.Q4_0, f, k2, seed=94)
+    x2 = _x(95, m2, k2)
+    gamma = (1.0 + 0.1 * _x(96, 1, k2)[0]).astype(np.float32)
+    act = torch.empty((m2, f), device="cuda:0")
+    rb2 = O.row_bytes(O.Q4_0, k2)
+    Q.quant_swiglu_ex(O.Q4_0, dev(g).data_ptr(), dev(u).data_ptr(), rb2, rb2, dev(x2).data_ptr(), k2,
+                      act.data_ptr(), f, f, k2, m2, dev(gamma).data_ptr(), 1e-6)
+    xn = O.rmsnorm(x2, gamma, 1e-6)
+    gv = O.gemv(O.Q4_0, g, rb2, xn, f, k2, m2, order=1).astype(np.float64)
+    uv = O.gemv(O.Q4_0, u, rb2, xn, f, k2, m2, order=1).astype(np.float64)
+    assert rel_l2(host(act), gv / (1 + np.exp(-gv)) * uv) < NORTH_STAR
+    assert Q.last_launch_count() == 2  # xprep + the tensor-core GEMM
 
 
 def test_tc_gemm_fused_rmsnorm_bias_accumulate():
