@@ -413,7 +413,7 @@ class CpuReferenceStack:
         return time.perf_counter() - t0
 
 
-def cpu_reference_steps(steps, warmup, budget_s=150.0):
+def cpu_reference_steps(steps, warmup, budget_s=150.0, keep_stack=False):
     """Times `warmup + steps` steps of the CPU restatement on all host cores.  A step is a
     whole decode token (28 layers + LM head) unless that would take the run past
     `budget_s`; then every step is the same prefix of the token (first n layers + LM head)
@@ -438,7 +438,7 @@ def cpu_reference_steps(steps, warmup, budget_s=150.0):
     info = {"cores": O.num_threads(), "kind": "port",
             "sample": f"each step {what}, Qwen2-7B shapes, batch 1, Q4_K, OpenMP over rows; "
                       f"mean of {steps} steps after {warmup} warm-up"}
-    return frac / sec, sec, info
+    return (frac / sec, sec, info, st) if keep_stack else (frac / sec, sec, info)
 
 
 def profile_traffic(name="gemv_q4k_swiglu_18944x3584.md"):
@@ -492,6 +492,60 @@ def run_prefill_kernel(args):
     print(json.dumps({"kernel_only": args.kernel_only, "tokens": m, "n": n, "k": k, "avg_us": us,
                       "TFLOPs": flops / us / 1e6, "launches": 2 * args.steps}), flush=True)
     return 0
+
+
+def run_sweep(Q, torch, reps=10):
+    """the isolated quantized linear through the public entry point
+    (ql_quant_matmul: streaming GEMV engine below 8 tokens, tcgen05 GEMM above for Q4_K / Q4_0),
+    weights (N, K) in {(4096, 4096), (11008, 4096), (4096, 11008), (151936, 4096)} as Q8_0, Q4_0 and
+    Q4_K, fp32 activations N(0, 1) (the ABI's input type), M in {1, 8, 64, 512, 2048}.  Every call
+    reads weights from HBM: each timing loop rotates over >= 300 MB of distinct weight copies.
+    M <= 64 is charged N*row_bytes + M*K*4 + M*N*4 bytes (HBM roofline), M >= 512 2*M*N*K flops."""
+    hbm, _ = peaks()
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tf_peak = float(pk.get("bf16_tflops", 1590.0))
+    Q.reserve_prefill(2048, 11008)
+    out = []
+    names = {8: "Q8_0", 2: "Q4_0", 12: "Q4_K"}
+    for n, k in ((4096, 4096), (11008, 4096), (4096, 11008), (151936, 4096)):
+        x = torch.randn(2048, k, device="cuda")
+        y = torch.empty(2048, n, device="cuda")
+        for t in (8, 2, 12):
+            rb = Q.row_bytes(t, k)
+            wb = n * rb
+            nbuf = max(1, -(-300_000_000 // wb))
+            ws = []
+            for i in range(nbuf):
+                w = torch.empty((n, rb), dtype=torch.uint8, device="cuda")
+                Q.synth_quantized(t, 1000 * n + 7 * k + 31 * t + i, n, k, 0.02, w.data_ptr())
+                ws.append(w)
+            for m in (1, 8, 64, 512, 2048):
+                run = lambda i: Q.quant_matmul(t, ws[i % nbuf].data_ptr(), rb, x.data_ptr(), y.data_ptr(), n, k, m)
+                for i in range(3):
+                    run(i)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(reps):
+                    run(i)
+                e1.record()
+                torch.cuda.synchronize()
+                sec = e0.elapsed_time(e1) / 1e3 / reps
+                ent = {"N": n, "K": k, "type": names[t], "M": m, "us": sec * 1e6, "launches": Q.last_launch_count()}
+                if m <= 64:
+                    gbs = (wb + m * k * 4 + m * n * 4) / sec / 1e9
+                    ent.update({"GBps": gbs, "frac_hbm": gbs / hbm})
+                else:
+                    tfl = 2.0 * m * n * k / sec / 1e12
+                    ent.update({"TFLOPs": tfl, "frac_bf16_burst": tfl / tf_peak})
+                out.append(ent)
+            del ws
+            torch.cuda.empty_cache()
+        del x, y
+        torch.cuda.empty_cache()
+    Q.check_device()
+    return out
 
 
 def run_chain_kernel(args):
@@ -762,6 +816,74 @@ def run_moe(args):
     return 0
 
 
+def reference_cuda_rate(st, steps, warmup):
+    """The reference's own CUDA kernels (kernel.cu / launch.cu, compiled unchanged for sm_100a into
+    oracle/_ref) on this GPU, for the same decode step's linears: per layer q, k, v
+    (launch_quant_gemv), o + residual (launch_quant_gemv_add), gate/up (launch_quant_swiglu), down +
+    residual (launch_quant_gemv_add); then the LM head (launch_quant_gemv) and launch_argmax, as
+    the reference engine runs them (one launch each; RMSNorm launches left out), captured in a CUDA
+    graph as the reference's decode graph does.  Weights are the CPU stack's host arrays copied
+    to the device.  Returns a dict, or None when there is no GPU or no reference build."""
+    import oracle as O
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return None
+    except Exception:
+        return None
+    R = O.ref_lib()
+    if R is None:
+        return None
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    L = [{k: d(v) for k, v in lay.items() if k.startswith("w")} for lay in st.layers]
+    lm = d(st.lm)
+    h = torch.randn(HIDDEN, device="cuda")
+    qkv = torch.zeros(3 * N_Q * HEAD, device="cuda")
+    act = torch.zeros(FFN, device="cuda")
+    logits = torch.zeros(VOCAB, device="cuda")
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    qw, kv = N_Q * HEAD, N_KV * HEAD
+    rbh, rbq, rbf = O.row_bytes(O.Q4_K, HIDDEN), O.row_bytes(O.Q4_K, qw), O.row_bytes(O.Q4_K, FFN)
+
+    def step():
+        R.ref_set_stream(s.cuda_stream)
+        for Lw in L:
+            R.ref_quant_gemv(O.Q4_K, Lw["wq"].data_ptr(), rbh, h.data_ptr(), qkv.data_ptr(), qw, HIDDEN, 1)
+            R.ref_quant_gemv(O.Q4_K, Lw["wk"].data_ptr(), rbh, h.data_ptr(), qkv.data_ptr() + 4 * qw, kv, HIDDEN, 1)
+            R.ref_quant_gemv(O.Q4_K, Lw["wv"].data_ptr(), rbh, h.data_ptr(), qkv.data_ptr() + 4 * (qw + kv), kv,
+                             HIDDEN, 1)
+            R.ref_quant_gemv_add(O.Q4_K, Lw["wo"].data_ptr(), rbq, qkv.data_ptr(), h.data_ptr(), HIDDEN, qw)
+            R.ref_quant_swiglu(O.Q4_K, Lw["wg"].data_ptr(), Lw["wu"].data_ptr(), rbh, rbh, h.data_ptr(),
+                               act.data_ptr(), FFN, HIDDEN)
+            R.ref_quant_gemv_add(O.Q4_K, Lw["wd"].data_ptr(), rbf, act.data_ptr(), h.data_ptr(), HIDDEN, FFN)
+        R.ref_quant_gemv(O.Q4_K, lm.data_ptr(), rbh, h.data_ptr(), logits.data_ptr(), VOCAB, HIDDEN, 1)
+        R.ref_argmax(logits.data_ptr(), VOCAB, tok.data_ptr())
+    with torch.cuda.stream(s):
+        step()  # eager first: the reference's argmax allocates its partial buffers on first use
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+        for _ in range(max(warmup, 1)):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+    err = R.ref_last_error()
+    ms = e0.elapsed_time(e1) / steps
+    del g
+    wb = weight_elems() * BPE
+    return {"value": 1e3 / ms, "unit": "tokens/s", "ms_per_step": ms, "launches_per_step": 6 * LAYERS + 2,
+            "step_weight_GBps": wb / (ms / 1e3) / 1e9, "cuda_error": int(err),
+            "what": "the reference's own CUDA kernels (kernel.cu, launch.cu) built for sm_100a, same decode step's "
+                    "linears on this B200, CUDA graph, batch 1"}
+
+
 def run_reference(args):
     """--impl reference: the CPU restatement of the reference's arithmetic (the reference's
     only implementation of this path is CUDA; it has no CPU path), whole decode tokens on
@@ -770,13 +892,19 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
-    v, sec, info = cpu_reference_steps(args.steps, args.warmup)
+    v, sec, info, st = cpu_reference_steps(args.steps, args.warmup, keep_stack=True)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": bench_config(args.batch, world),
             "cpu_baseline": dict(info, value=v, unit="tokens/s"),
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    try:
+        rc = reference_cuda_rate(st, args.steps, args.warmup)
+    except Exception as e:  # the CPU line stands on its own
+        rc = {"unavailable": f"{type(e).__name__}: {e}"}
+    if rc is not None:
+        line["reference_cuda_kernels_on_this_gpu"] = rc
     print(json.dumps(line), flush=True)
     return 0
 
@@ -793,6 +921,7 @@ def main():
     ap.add_argument("--no-batch32", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-models", action="store_true", help="skip the Qwen2-0.5B Q8_0 and Qwen2-72B Q4_0 lines")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the isolated quantized-linear sweep (configs[1])")
     ap.add_argument("--moe", action="store_true", help="DeepSeek-V2-Lite-shape MoE decode, expert parallel")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
@@ -1023,6 +1152,7 @@ def main():
             extra["qwen2_0.5b_q8_0"] = (QWEN2_05B, measure(1, QWEN2_05B))
         extra["qwen2_72b_q4_0"] = (QWEN2_72B, measure(1, QWEN2_72B))
     rp = None if args.no_prefill else measure_prefill(args.prefill_tokens)
+    sweep = run_sweep(Q, torch) if (world == 1 and not args.no_sweep) else None
 
     if rank == 0:
         hbm, peak_kind = peaks()
@@ -1082,6 +1212,10 @@ def main():
                                "tensor_frac_of_sustained_bf16": tf / sus,
                                "path": "tcgen05 f16 x f16 -> f32 GEMM, Q4_K dequantized into shared memory",
                                "tensor_pipe_active": "see profiles/gemm_q4k_prefill_2048x18944x3584.md"}
+        if sweep is not None:
+            line["sweep"] = {"config": "BASELINE configs[1]: 4 shapes x {Q8_0, Q4_0, Q4_K} x M in {1,8,64,512,2048}, "
+                                       "public ql_quant_matmul, weights rotated over >= 300 MB",
+                             "entries": sweep}
         for key, (md, r) in extra.items():
             wb = md.weight_bytes()
             line[key] = {"value": 1 / (r["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r["ms"],
