@@ -169,3 +169,20 @@ class GgufFile:
         st = lib().ql_gguf_validate(self.h)
         if st != 0:
             raise QLError(st, lib().ql_last_error().decode(errors="replace"))
+
+
+def upload_tensor(f: GgufFile, name: str, torch, device="cuda", rows=None, byte_range=None):
+    """A tensor's raw bytes on the device through ql_weight_upload: the whole matrix, a row range
+    (column-parallel shard) or a byte range of every row (row-parallel shard, whole blocks).
+    Returns a uint8 tensor [rows, bytes per row] (1-D tensors: [1, nbytes])."""
+    _, t, shape, buf = f.tensor(name)
+    nrows = int(np.prod(shape[:-1])) if len(shape) > 1 else 1
+    rb = len(buf) // nrows
+    r0, r1 = rows if rows is not None else (0, nrows)
+    b0, b1 = byte_range if byte_range is not None else (0, rb)
+    dst = torch.empty((r1 - r0, b1 - b0), dtype=torch.uint8, device=device)
+    host = np.ascontiguousarray(buf)  # the mapped file (pageable): the copy is synchronous
+    from . import weight_upload
+    weight_upload(host.ctypes.data, rb, r0, r1 - r0, b0, b1 - b0, dst.data_ptr())
+    torch.cuda.synchronize()
+    return dst
