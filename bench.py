@@ -984,7 +984,8 @@ def main():
         parity = tp_parity(stack, host_in) if (world > 1 and stack.chain is not None and model is QWEN2_7B) else None
         # event-record nodes inside the graph around the dominant kernel: the chain launch
         # (the whole step) or the gate/up SwiGLU launch of 4 layers
-        evl = ["chain"] if stack.chain is not None else [3, 10, 17, 24]
+        nl = model.layers
+        evl = ["chain"] if stack.chain is not None else sorted({nl // 8, 3 * nl // 8, 5 * nl // 8, 7 * nl // 8})
         events = {"layers": evl, "pairs": {l: (torch.cuda.Event(enable_timing=True, external=True),
                                                torch.cuda.Event(enable_timing=True, external=True)) for l in evl}}
         with torch.cuda.stream(s):

@@ -20,14 +20,14 @@
 //     4-slot ring as far ahead as the ring allows, across op boundaries (weights do not depend on
 //     activations).  Warp 1 waits for the op's grid barrier and then streams the unit's activations,
 //     fp32 [tokens][256], as a 128-byte-swizzled TMA box into a 2-slot ring.
-//   * Warps 2..5 (one per k-chunk of 64 inputs, all 128 rows each: 6 warps in all, so that a
-//     scheduler partition holds at most two and a thread may use 255 registers) decode their
-//     weights in registers into f16 mma.sync A fragments: one 32-bit word of Q4_K nibbles gives four f16x2
+//   * Warps 2..9 (2 row sets of 64 rows x 4 k-chunks of 64 inputs; two consumer warps per
+//     scheduler partition hide each other's latency) decode their weights in registers into f16
+//     mma.sync A fragments: one 32-bit word of Q4_K nibbles gives four f16x2
 //     operands through (w & 0x000F000F) | 0x6400 (= 1024 + n, exact), an exact f16 subtraction of
 //     1024 and one f16 FMA with the sub-block's (d*sc, -dmin*m) -- the reference's value formula
 //     d*sc*q - dmin*m (kernel.cu:913-921,1090-1119) rounded once to f16.  Activations are read from
 //     the swizzled tile, multiplied by the RMSNorm weight and converted to f16 B fragments in
-//     registers.  mma.sync.m16n8k16 accumulates in fp32 (128 rows x 32 tokens per warp).
+//     registers.  mma.sync.m16n8k16 accumulates in fp32 (64 rows x 32 tokens per warp).
 //     The k order inside a 16-element step is permuted identically on both operands (element
 //     4t + {0, 2, 1, 3} of a step goes to logical position 2t, 2t+1, 2t+8, 2t+9), which lets one
 //     AND extract two operands from bytes 0 and 2 (or 1 and 3) of a word.
@@ -62,7 +62,7 @@ namespace {
 
 constexpr int kBMaxTok = 32;
 constexpr int kBRows = 128;                        // output rows per tile
-constexpr int kBCw = 4;                            // consumer warps: one per k-chunk, all 128 rows each
+constexpr int kBCw = 8;                            // consumer warps: 2 row sets (64 rows) x 4 k-chunks
 constexpr int kBThreads = (2 + kBCw) * 32;         // weight producer, activation producer, consumers
 constexpr int kBWSlots = 4;
 constexpr int kBXSlots = 2;
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
 
     // -------------------------------- consumers --------------------------------
     const int cw = warp - 2, ctid = tid - 64;
-    const int kc = cw;  // k-chunk: inputs 64kc .. 64kc + 63 of every block
+    const int rs = cw >> 2, kc = cw & 3;  // row set (rows 64rs ..), k-chunk (inputs 64kc .. 64kc + 63)
     const int g = lane >> 2, t = lane & 3;
     int itw = 0, itx = 0;
     for (int p = 0; p < a.nops; ++p) {
@@ -329,9 +329,9 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         // each slot written by one lane only: deterministic
         wkey[cw * kBMaxTok + lane] = 0ull;
         wss[cw * kBMaxTok + lane] = 0.f;
-        float acc[8][4][4];  // rows 16m + g (+8), tokens of n-tile n
+        float acc[4][4][4];  // rows 64rs + 16m + g (+8), tokens of n-tile n
 #pragma unroll
-        for (int m = 0; m < 8; ++m)
+        for (int m = 0; m < 4; ++m)
 #pragma unroll
             for (int n = 0; n < 4; ++n)
 #pragma unroll
@@ -345,33 +345,29 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             if (!aborted() && !mbar_wait(&xfull[xsl], (uint32_t)(itx / kBXSlots) & 1u, a.err, kErrWaitFull))
                 *abort_flag = 1;
             if (!__any_sync(0xffffffffu, aborted())) {
-                const uint8_t *wb = smem + kBOffW + ws * kBWBytes;
+                const uint8_t *wb = smem + kBOffW + ws * kBWBytes + rs * 64 * 144;
                 const uint8_t *xb = smem + kBOffX + xsl * kBXBytes;
-                // This lane's rows are 16m + g and 16m + g + 8 (m = 0..7), its inputs 4t .. 4t + 3 of each
-                // 16-input step.  Lane (g, t) decodes the sub-block scales of rows 16m + g (+8) for
-                // m = t and t + 4; the four lanes of a quad then share them.  Few values stay live
-                // across the k-steps (the 128 accumulators take most registers): scales per
-                // sub-block, weight words per m-tile.
-                uint32_t mine[2][2][2];  // [m = t or t + 4][row g or g + 8][sub-block 2kc or 2kc + 1]
+                // This lane's rows are 16m + g and 16m + g + 8 of the row set (m = 0..3), its inputs
+                // 4t .. 4t + 3 of each 16-input step.  Lane (g, t) decodes the sub-block scales of rows
+                // 16t + g (+8); the four lanes of a quad then share them.  Few values stay live across
+                // the k-steps: scales per sub-block, weight words per m-tile.
+                uint32_t mine[2][2];  // [row 16t + g or 16t + g + 8][sub-block 2kc or 2kc + 1]
 #pragma unroll
-                for (int mm = 0; mm < 2; ++mm)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint4 hd = *reinterpret_cast<const uint4 *>(wb + (16 * (t + 4 * mm) + g + 8 * h) * 144);
-                        mine[mm][h][0] = q4k_ab(hd, 2 * kc);
-                        mine[mm][h][1] = q4k_ab(hd, 2 * kc + 1);
-                    }
+                for (int h = 0; h < 2; ++h) {
+                    const uint4 hd = *reinterpret_cast<const uint4 *>(wb + (16 * t + g + 8 * h) * 144);
+                    mine[h][0] = q4k_ab(hd, 2 * kc);
+                    mine[h][1] = q4k_ab(hd, 2 * kc + 1);
+                }
                 const uint8_t *wq = wb + g * 144 + 16 + 32 * kc + 4 * t;  // this lane's word of row g, j = 0
 #pragma unroll 1
                 for (int sh = 0; sh < 2; ++sh) {  // sub-block 2kc (low nibbles), 2kc + 1 (high nibbles)
                     const int sb = 2 * kc + sh;
-                    uint32_t ab[8][2];
+                    uint32_t ab[4][2];
 #pragma unroll
-                    for (int m = 0; m < 8; ++m)
+                    for (int m = 0; m < 4; ++m)
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
-                            ab[m][h] = __shfl_sync(0xffffffffu, sh ? mine[m >> 2][h][1] : mine[m >> 2][h][0],
-                                                   (g << 2) | (m & 3));
+                            ab[m][h] = __shfl_sync(0xffffffffu, sh ? mine[h][1] : mine[h][0], (g << 2) | m);
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {  // 16-input step
                         // B fragments: column g of n-tile n is token 8n + tperm(g) (tperm puts the two
@@ -399,7 +395,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                             }
                         }
 #pragma unroll
-                        for (int m = 0; m < 8; ++m) {
+                        for (int m = 0; m < 4; ++m) {
                             const uint32_t a0 = ab[m][0], a1 = ab[m][1];
                             const uint32_t aa0 = __byte_perm(a0, 0, 0x1010), bb0 = __byte_perm(a0, 0, 0x3232);
                             const uint32_t aa1 = __byte_perm(a1, 0, 0x1010), bb1 = __byte_perm(a1, 0, 0x3232);
@@ -452,11 +448,11 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             // k-chunk partials -> red[kc][token][row]
             float *rw = red + (size_t)kc * kBMaxTok * kBRedPitch;
 #pragma unroll
-            for (int m = 0; m < 8; ++m)
+            for (int m = 0; m < 4; ++m)
 #pragma unroll
                 for (int n = 0; n < 4; ++n) {
                     if (n < NT) {
-                        const int r = 16 * m + g;
+                        const int r = 64 * rs + 16 * m + g;
                         const int tk0 = 8 * n + tperm(2 * t), tk1 = 8 * n + tperm(2 * t + 1);
                         rw[tk0 * kBRedPitch + r] = acc[m][n][0];
                         rw[tk1 * kBRedPitch + r] = acc[m][n][1];
@@ -484,9 +480,9 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                 // stream-K: park this part; the last CTA of the tile sums the parts in CTA order
                 const int si = (tile == (int)(u0 / U)) ? 0 : 1;
                 float *pp = a.part + ((size_t)cta * 2 + si) * (kBMaxTok * kBRows);
-                const int r = ctid;  // thread = row, all tokens
+                const int r = ctid & (kBRows - 1), th = ctid >> 7;  // thread = (row, 16 tokens)
 #pragma unroll 4
-                for (int tk = 0; tk < kBMaxTok; ++tk) __stcg(pp + tk * kBRows + r, red_sum(tk, r));
+                for (int i = 0; i < 16; ++i) __stcg(pp + (16 * th + i) * kBRows + r, red_sum(16 * th + i, r));
                 __threadfence();
                 named_bar_sync(1, kBCw * 32);
                 const int cf = (int)(((ts + 1) * (int64_t)Cp - 1) / T), cl = (int)((te * (int64_t)Cp - 1) / T);
@@ -513,13 +509,13 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             };
             if (finish) {
                 if (kind == kBSwiglu) {
-                    // thread = (gate row r < 64, 16 tokens); its up row is r + 64
+                    // thread = (gate row r < 64, 8 tokens); its up row is r + 64
                     const int r = ctid & 63, tq = ctid >> 6;
                     const int row = tile * 64 + r;
                     if (row < rows) {
 #pragma unroll 2
-                        for (int i = 0; i < 16; ++i) {
-                            const int tk = 16 * tq + i;
+                        for (int i = 0; i < 8; ++i) {
+                            const int tk = 8 * tq + i;
                             if (tk < M) {
                                 const float nrm = gamma != nullptr ? inv_rms[tk] : 1.f;
                                 const float gv = tile_sum(tk, r) * nrm, uv = tile_sum(tk, r + 64) * nrm;
@@ -528,14 +524,14 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                         }
                     }
                 } else {
-                    // thread = (row r, all tokens); warp cw holds rows 32cw .. 32cw + 31
-                    const int r = ctid;
+                    // thread = (row r, 16 tokens); warp cw holds rows 32(cw & 3) .., tokens 16(cw >> 2) ..
+                    const int r = ctid & (kBRows - 1), th = ctid >> 7;
                     const int row = tile * kBRows + r;
                     const bool live = row < rows;
                     const float bias = (live && o.bias != nullptr) ? o.bias[row] : 0.f;
 #pragma unroll 2
-                    for (int i = 0; i < kBMaxTok; ++i) {
-                        const int tk = i;
+                    for (int i = 0; i < 16; ++i) {
+                        const int tk = 16 * th + i;
                         float out = 0.f;
                         unsigned long long key = 0ull;
                         if (live && tk < M) {
@@ -583,10 +579,11 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         named_bar_sync(1, kBCw * 32);
         if (track) {
             if (ctid < M) {
-                // every warp holds every token (for its 32 rows of each tile)
+                // warps 4h .. 4h + 3 hold tokens 16h .. 16h + 15
+                const int h = ctid >> 4;
                 unsigned long long k = 0ull;
                 float s = 0.f;
-                for (int w = 0; w < kBCw; ++w) {
+                for (int w = 4 * h; w < 4 * h + 4; ++w) {
                     const unsigned long long kw = wkey[w * kBMaxTok + ctid];
                     k = kw > k ? kw : k;
                     s += wss[w * kBMaxTok + ctid];

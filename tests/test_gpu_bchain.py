@@ -135,19 +135,22 @@ def test_batched_chain_qwen2_7b_shapes():
     _check(m, M, h0, _run(m, M, h0, replays=2))
 
 
-@pytest.mark.parametrize("op", ["qkv", "o", "swiglu", "down", "lmhead"])
+@pytest.mark.parametrize("op", ["qkv", "o", "gate", "up", "swiglu", "down", "lmhead"])
 def test_batched_chain_each_linear(op):
-    """One linear of each kind as a one-op batched chain (32 tokens) against the oracle."""
+    """One linear of each kind as a one-op batched chain (32 tokens) against the oracle.  The
+    SwiGLU op's output is SiLU(gate) * up, the product of two linear outputs (each checked here on
+    its own as a STORE op at 1e-3), so its bar is 1.5e-3."""
     import torch
     H, QW, KV, F, V, M = 3584, 3584, 512, 18944, 152064, 32
     m = _model(H, QW, KV, F, V, 1, seed=45)
     L, Lh = m["dev"][0], m["host"][0]
     rb = lambda k: Q.row_bytes(Q.Q4_K, k)
     rng = np.random.default_rng(46)
-    k_in = {"qkv": H, "o": QW, "swiglu": H, "down": F, "lmhead": H}[op]
+    k_in = {"qkv": H, "o": QW, "gate": H, "up": H, "swiglu": H, "down": F, "lmhead": H}[op]
     x = rng.standard_normal((M, k_in)).astype(np.float32)
     xd = dev(x)
-    xn = O.rmsnorm(x, Lh["ln1"] if op == "qkv" else Lh["ln2"] if op == "swiglu" else m["lnf_h"], EPS)
+    xn = O.rmsnorm(x, Lh["ln1"] if op == "qkv" else Lh["ln2"] if op in ("swiglu", "gate", "up") else m["lnf_h"],
+                   EPS)
     W = lambda w, k: O._dq(Q.Q4_K, w, k)
     if op == "qkv":
         y = torch.zeros((M, QW + 2 * KV), device="cuda:0")
@@ -160,6 +163,12 @@ def test_batched_chain_each_linear(op):
         w = "wo" if op == "o" else "wd"
         opd = Q.chain_op(Q.OP_ADD, [L[w].data_ptr()], [rb(k_in)], [H], k_in, xd.data_ptr(), y.data_ptr())
         ref = base + x.astype(np.float64) @ W(Lh[w], k_in).T
+    elif op in ("gate", "up"):
+        w = "wg" if op == "gate" else "wu"
+        y = torch.zeros((M, F), device="cuda:0")
+        opd = Q.chain_op(Q.OP_STORE, [L[w].data_ptr()], [rb(H)], [F], H, xd.data_ptr(), y.data_ptr(),
+                         L["ln2"].data_ptr(), EPS)
+        ref = xn @ W(Lh[w], H).T
     elif op == "swiglu":
         y = torch.zeros((M, F), device="cuda:0")
         opd = Q.chain_op(Q.OP_SWIGLU, [L["wg"].data_ptr(), L["wu"].data_ptr()], [rb(H)] * 2, [F, F], H,
@@ -181,7 +190,7 @@ def test_batched_chain_each_linear(op):
         chain.close()
     err = rel_l2(got, ref) if op not in ("o", "down") else rel_l2(got - base, ref - base)
     print(f"batched chain, one {op} linear, 32 tokens: rel_l2 {err:.2e}")
-    assert err < 1e-3
+    assert err < (1.5e-3 if op == "swiglu" else 1e-3)
     if op == "lmhead":
         assert np.array_equal(host(tok), np.argmax(got, axis=1).astype(np.int32))
 
