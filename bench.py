@@ -505,6 +505,7 @@ def run_sweep(Q, torch, reps=10):
     pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
         os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
     tf_peak = float(pk.get("bf16_tflops", 1590.0))
+    Q.set_stream(torch.cuda.current_stream().cuda_stream)  # timed on this stream
     Q.reserve_prefill(2048, 11008)
     out = []
     names = {8: "Q8_0", 2: "Q4_0", 12: "Q4_K"}

@@ -18,6 +18,7 @@
 //     SwiGLU, fused RMSNorm, fused greedy argmax) as the per-op kernels.
 // Arrival counters and the launch epoch are monotonic, so a CUDA graph can
 // replay the launch without resets.  Every wait is bounded.
+#include <cmath>
 #include <cstddef>
 #include <cstdlib>
 #include <cstring>
@@ -82,7 +83,7 @@ struct __align__(128) ChainOp {
     // half + 16q .. half + 16q + 15 of head (32 g) / head_dim, q = ((32 g) % head_dim) / 32, so that
     // lanes l and l ^ 16 of the finisher hold the two rows a rotation pairs
     const int *rope_pos;
-    float rope_theta;
+    const float *rope_inv;  // [head_dim / 2] inverse frequencies 1 / theta^(2i / head_dim)
     int rope_rows;
     int rope_half;          // head_dim / 2
 };
@@ -596,9 +597,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                 // residual when its last writer finished before op p-1 started (o.pre_y)
                 // output row of this lane (RoPE groups hold two 16-row halves of a head)
                 int vv = g * kRowGroup + lane;
+                float rope_c = 1.f, rope_s = 0.f;
                 if (vv < o.rope_rows) {
                     const int hd = 2 * o.rope_half, hb = vv / hd * hd, q16 = 16 * ((vv % hd) / 32);
                     vv = hb + q16 + (lane & 15) + ((lane & 16) ? o.rope_half : 0);
+                    // the rotation angle depends only on the position: computed while the consumers work
+                    const float ang = (float)__ldg(o.rope_pos) * __ldg(o.rope_inv + (q16 + (lane & 15)));
+                    sincosf(ang, &rope_s, &rope_c);
                 }
                 if (o.pre_y && p >= 2 && lane == 0 && !*reinterpret_cast<volatile int *>(abort_flag)) {
                     // a CTA with no row group in op p-1 gets here without having waited for op p-2
@@ -667,11 +672,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                     if (rope) {
                         const float x = val[0] * nrm + bias_v;
                         const float xp = __shfl_xor_sync(0xffffffffu, x, 16);
-                        const int i = (v % (2 * o.rope_half)) % o.rope_half;
-                        const float inv_freq = 1.0f / powf(o.rope_theta, (float)(2 * i) / (float)(2 * o.rope_half));
-                        const float ang = (float)__ldg(o.rope_pos) * inv_freq;
-                        const float c = cosf(ang), sn = sinf(ang);
-                        rot = (lane & 16) ? x * c + xp * sn : x * c - xp * sn;
+                        rot = (lane & 16) ? x * rope_c + xp * rope_s : x * rope_c - xp * rope_s;
                     }
                     if (v < o.rows) {
                         float *yp = o.y + v;
@@ -1039,10 +1040,19 @@ namespace {
 // down projection (74 blocks), measured faster than stream-K there.
 constexpr int kChainMaxUnitsOneGroup = 80;
 
+// The reference's RoPE inverse frequencies 1 / powf(theta, 2i / head_dim), i < head_dim / 2
+// (kernel.cu:186-260), computed once on the host.
+std::vector<float> rope_inverse_frequencies(float theta, int head_dim) {
+    std::vector<float> t(head_dim / 2);
+    for (int i = 0; i < head_dim / 2; ++i) t[i] = 1.0f / powf(theta, (float)(2 * i) / (float)head_dim);
+    return t;
+}
+
 struct Chain {
     int magic = 0x43484e31;  // the batched chain (ql_bchain.cu) starts with a different magic word
     ChainOp *ops_dev = nullptr;
     void *mlp_mem = nullptr;             // fused MLP: fixed-point residuals, then pair-exchange cells
+    float *rope_mem = nullptr;           // RoPE inverse-frequency tables
     unsigned long long *keys = nullptr;  // [nops] fused-argmax keys
     unsigned *done = nullptr;   // [nops] arrival counters, [nops] epoch, [nops+1 ..] argmax arrival counters
     unsigned *epoch = nullptr;
@@ -1075,6 +1085,7 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
     int st = chain_workspace(&part, &counters, &err, &sms);
     if (st) return st;
     std::vector<ChainOp> h(nops);
+    std::vector<std::pair<int, std::vector<float>>> rope_tables;  // (op, inverse frequencies)
     int kmax = 0;
     for (int p = 0; p < nops; ++p) {
         const ql_chain_op &q = ops[p];
@@ -1165,9 +1176,9 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
                     return set_last_error(QL_ECUDA, (what + ": tensor map").c_str());
             if (nsrc < 2) o.tmap16[1] = o.tmap16[0];
             o.rope_pos = q.rope_pos;
-            o.rope_theta = q.rope_theta;
             o.rope_rows = q.rope_rows;
             o.rope_half = hd / 2;
+            rope_tables.push_back({p, rope_inverse_frequencies(q.rope_theta, hd)});
         }
         o.kind = q.kind == QL_OP_STORE ? kOpStore : q.kind == QL_OP_ADD ? kOpAdd : kOpSwiglu;
         o.nmat = q.kind == QL_OP_SWIGLU ? 2 : 1;
@@ -1268,6 +1279,24 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         }
         c->args.mlp_cells = reinterpret_cast<unsigned long long *>(fixed + fixed_total);
     }
+    if (!rope_tables.empty()) {
+        size_t nf = 0;
+        for (auto &rt : rope_tables) nf += rt.second.size();
+        e = cudaMalloc(&c->rope_mem, nf * sizeof(float));
+        size_t at = 0;
+        for (auto &rt : rope_tables) {
+            if (e == cudaSuccess)
+                e = cudaMemcpy(c->rope_mem + at, rt.second.data(), rt.second.size() * sizeof(float), cudaMemcpyHostToDevice);
+            h[rt.first].rope_inv = c->rope_mem + at;
+            at += rt.second.size();
+        }
+        if (e != cudaSuccess) {
+            if (c->mlp_mem) cudaFree(c->mlp_mem);
+            if (c->rope_mem) cudaFree(c->rope_mem);
+            delete c;
+            return set_last_error(QL_ECUDA, (std::string("ql_gemv_chain_create: ") + cudaGetErrorString(e)).c_str());
+        }
+    }
     e = cudaMalloc(&c->ops_dev, sizeof(ChainOp) * nops);
     // per-op argmax keys and arrival counter: one slot per op at the end of the counter block
     unsigned long long *keys = nullptr;
@@ -1290,6 +1319,7 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
         if (c->done) cudaFree(c->done);
         if (keys) cudaFree(keys);
         if (c->mlp_mem) cudaFree(c->mlp_mem);
+        if (c->rope_mem) cudaFree(c->rope_mem);
         delete c;
         return set_last_error(QL_ECUDA, (std::string("ql_gemv_chain_create: ") + cudaGetErrorString(e)).c_str());
     }
@@ -1374,6 +1404,7 @@ int ql_gemv_chain_destroy(void *chain) {
     if (c->done) cudaFree(c->done);
     if (c->keys) cudaFree(c->keys);
     if (c->mlp_mem) cudaFree(c->mlp_mem);
+    if (c->rope_mem) cudaFree(c->rope_mem);
     delete c;
     return QL_OK;
 }
