@@ -1,12 +1,12 @@
 // ql_bchain.cu -- batched decode: a decode step's Q4_K projections for up to 32 tokens in one
-// persistent launch on the tensor cores.
+// persistent launch on the 5th-generation tensor cores (tcgen05).
 //
 // The reference runs batched decode and prefill as one warp per (token, output row) on the
 // CUDA cores (quant_matmul_kernel, AI/codes/local-llm/src/backend/cuda/ops/kernel.cu:1253-1279,
 // via launch_quant_matmul, launch.cu:101-119), or as dequantize-to-f16 plus cuBLAS
 // (TensorTool.cpp:127-144).  At 8..32 tokens the step is still bound by the weight stream (each
 // weight is used by every token once), so the design goal is to decode every weight exactly once
-// per step, with few instructions, straight into tensor-core operands:
+// per step, with as few instructions as possible, straight into a tensor-core operand:
 //
 //   * One cooperative launch of one CTA per SM runs the whole op list (same semantics as
 //     ql_gemv_chain: stacked q/k/v with RMSNorm and bias, o + residual, gate/up SwiGLU, down +
@@ -16,26 +16,29 @@
 //     inputs).  Units are split over the CTAs in equal contiguous ranges (stream-K); a tile shared
 //     by several CTAs is finished by the last to arrive, which sums the parts in CTA order
 //     (deterministic).
+//   * The weights are the MMA's M side (128 rows), the tokens its N side (32 columns):
+//     tcgen05.mma.kind::f16, M 128, N 32, K 16, fp32 accumulators in TMEM (two 32-column
+//     buffers, so a tile's drain overlaps the next tile's MMAs).
 //   * Warp 0 streams the raw Q4_K bytes of every unit (TMA box {144 B, 1 block, 128 rows}) into a
-//     4-slot ring as far ahead as the ring allows, across op boundaries (weights do not depend on
-//     activations).  Warp 1 waits for the op's grid barrier and then streams the unit's activations,
-//     fp32 [tokens][256], as a 128-byte-swizzled TMA box into a 2-slot ring.
-//   * Warps 2..9 (2 row sets of 64 rows x 4 k-chunks of 64 inputs; two consumer warps per
-//     scheduler partition hide each other's latency) decode their weights in registers into f16
-//     mma.sync A fragments: one 32-bit word of Q4_K nibbles gives four f16x2
-//     operands through (w & 0x000F000F) | 0x6400 (= 1024 + n, exact), an exact f16 subtraction of
-//     1024 and one f16 FMA with the sub-block's (d*sc, -dmin*m) -- the reference's value formula
-//     d*sc*q - dmin*m (kernel.cu:913-921,1090-1119) rounded once to f16.  Activations are read from
-//     the swizzled tile, multiplied by the RMSNorm weight and converted to f16 B fragments in
-//     registers.  mma.sync.m16n8k16 accumulates in fp32 (64 rows x 32 tokens per warp).
-//     The k order inside a 16-element step is permuted identically on both operands (element
-//     4t + {0, 2, 1, 3} of a step goes to logical position 2t, 2t+1, 2t+8, 2t+9), which lets one
-//     AND extract two operands from bytes 0 and 2 (or 1 and 3) of a word.
-//   * At the end of a tile the four k-chunk partials meet in shared memory and the epilogue runs
-//     (RMSNorm factor, bias, residual add, SwiGLU, greedy-argmax keys).  The RMSNorm factor of an op
-//     needs the sum of squares of its whole input row per token: the op that produced that input
-//     (an ADD or STORE of the chain) accumulates it in its epilogue in 64-bit fixed point (exact,
-//     order-free, so deterministic); an input written outside the chain is summed by each CTA.
+//     4-slot ring, across op boundaries (weights do not depend on activations).  Warp 1 waits for
+//     the op's grid barrier and streams the unit's activations: f16, [32 tokens][256 inputs], four
+//     TMA boxes {64, 32} with 128-byte swizzle, i.e. already the MMA's canonical K-major B layout.
+//     Warp 2 owns TMEM and one of its threads issues the MMAs.
+//   * Warps 3..10 (thread = weight row x half block) dequantize their 128 weights per unit into
+//     the canonical K-major 128-byte-swizzled A layout: a 32-bit word of nibbles gives f16 pairs
+//     through (w & 0x000F000F) | 0x6400 (= 1024 + n, exact), an exact f16 subtraction of 1024 and
+//     one f16 FMA with the sub-block's (d*sc, -dmin*m) -- the reference's value formula
+//     d*sc*q - dmin*m (kernel.cu:913-921,1090-1119) rounded once to f16.  Elements are emitted in
+//     the order 0, 2, 1, 3, 4, 6, 5, 7 inside every group of 8 (two nibbles per AND); the
+//     activations are stored in the same order.  At a tile end the same warps drain the
+//     accumulator (tcgen05.ld) and run the epilogue.
+//   * Activations: each op's input, times its RMSNorm weight, rounded to f16, lives in one of two
+//     global buffers [32][K].  It is written by the epilogue of the op that produced the input (the
+//     previous op: rows of its output are the next op's inputs), or, for an op whose input comes
+//     from outside the chain, by all CTAs at the op's start followed by a second grid barrier.
+//     The RMSNorm factor is one scalar per token applied in the epilogue: the op that produced the
+//     input accumulates its sum of squares in 64-bit fixed point (exact, order-free, so
+//     deterministic); an input written outside the chain is summed by each CTA.
 //
 // Numerics: weights and activations (x * gamma) rounded to f16, fp32 accumulation; |x * gamma|
 // must stay below 65504.  Every wait is bounded (about 2 s): on expiry the kernel records an error
@@ -43,6 +46,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -60,39 +64,44 @@ int chain_workspace(float **part, unsigned **counters, int **err, int *sms);
 
 namespace {
 
-constexpr int kBMaxTok = 32;
-constexpr int kBRows = 128;                        // output rows per tile
-constexpr int kBCw = 8;                            // consumer warps: 2 row sets (64 rows) x 4 k-chunks
-constexpr int kBThreads = (2 + kBCw) * 32;         // weight producer, activation producer, consumers
-constexpr int kBWSlots = 4;
-constexpr int kBXSlots = 2;
+constexpr int kBMaxTok = 32;                       // MMA N
+constexpr int kBRows = 128;                        // output rows per tile = MMA M
+constexpr int kBCw = 8;                            // dequantizer / epilogue warps
+constexpr int kBThreads = (3 + kBCw) * 32;         // weight TMA, activation TMA, MMA, consumers
+constexpr int kBWSlots = 4;                        // raw weight ring
+constexpr int kBXSlots = 3;                        // activation ring
+constexpr int kBASlots = 2;                        // dequantized 64-input chunks per half block
 constexpr int kBWBytes = kBRows * 144;             // 18,432 B: one block column of a tile
-constexpr int kBXBytes = kBMaxTok * 256 * 4;       // 32 KB: one block of up to 32 tokens, fp32
-constexpr int kBRedPitch = kBRows + 4;             // floats per (k-chunk, token) row of the reduction tile
-constexpr int kBRedBytes = 4 * kBMaxTok * kBRedPitch * 4;
+constexpr int kBXBox = kBMaxTok * 64 * 2;          // 4 KB: 32 tokens x 64 inputs, f16
+constexpr int kBXBytes = 4 * kBXBox;               // one block of activations
+constexpr int kBABytes = kBRows * 128;             // 16 KB: 128 rows x 64 inputs, f16
+constexpr int kBRedPitch = kBRows + 4;             // floats per token row of the drained tile
+constexpr int kBRedBytes = kBMaxTok * kBRedPitch * 4;
 constexpr int kBHdr = 1024;
 constexpr int kBOffW = kBHdr;
-constexpr int kBOffX = kBOffW + kBWSlots * kBWBytes;     // 1024-byte aligned (128-byte swizzle)
-constexpr int kBOffRed = kBOffX + kBXSlots * kBXBytes;
-constexpr int kBOffMisc = kBOffRed + kBRedBytes;         // per-warp token reductions
-constexpr int kBOffGamma = kBOffMisc + 2 * kBCw * kBMaxTok * 8;  // the op's RMSNorm weight
-constexpr int kBGammaMax = 4096;                         // inputs whose RMSNorm weight is staged
-constexpr int kBOffPslot = kBOffGamma + kBGammaMax * 4;  // stream-K part slots of the tile being finished
+constexpr int kBOffX = kBOffW + kBWSlots * kBWBytes;
+constexpr int kBOffA = kBOffX + kBXSlots * kBXBytes;
+constexpr int kBOffRed = kBOffA + 2 * kBASlots * kBABytes;
+constexpr int kBOffMisc = kBOffRed + kBRedBytes;   // per-warp token reductions
+constexpr int kBOffPslot = kBOffMisc + 2 * kBCw * kBMaxTok * 8;  // stream-K part slots of the tile being finished
 constexpr int kBSmem = kBOffPslot + 256 * 4;
-static_assert(kBOffX % 1024 == 0, "activation ring must be 1024-byte aligned");
+constexpr uint32_t kBTmemCols = 64;                // two 32-column accumulators
+static_assert(kBOffX % 1024 == 0 && kBOffA % 1024 == 0, "swizzled rings must be 1024-byte aligned");
 static_assert(kBSmem <= 227 * 1024, "shared memory");
 constexpr int kErrBarrier = 5;
 constexpr double kSsFix = 16777216.0;  // 2^24: fixed-point sums of squares
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M 128, N 32.
+constexpr uint32_t kBIdesc = (1u << 4) | ((uint32_t)(kBMaxTok >> 3) << 17) | ((uint32_t)(kBRows >> 4) << 24);
 
 enum BKind : int { kBStore = 0, kBAdd = 1, kBSwiglu = 2 };
 
 struct __align__(128) BOp {
     CUtensorMap wmap[3];  // Q4_K sources {144, blocks, rows}, box {144, 1, 128} (SwiGLU: 64 rows each)
-    CUtensorMap xmap;     // activations {32, tokens, K/32} fp32, box {32, 8*NT, 8}, 128-byte swizzle
+    CUtensorMap xmap;     // f16 input xh_in {K, 32}, box {64, 32}, 128-byte swizzle
     int kind, nmat, rows, K, U, tiles;
     int split0, split1;   // stacked sources: first rows of sources 1 and 2 (multiples of 128)
     int64_t T;            // units = tiles * U
-    const float *x;
+    const float *x;       // fp32 input [M][xs]
     int64_t xs;
     const float *gamma;
     float eps;
@@ -103,16 +112,22 @@ struct __align__(128) BOp {
     int ss_out;           // slot this op's epilogue sums its output's squares into; -1: none
     AmaxOut amax;
     const int *rope_pos;  // RoPE on rows [0, rope_rows): positions per token
-    float rope_theta;
+    const float *rope_inv;  // [head_dim / 2] inverse frequencies 1 / theta^(2i / head_dim)
     int rope_rows, head_dim;
+    __half *xh_in;        // this op's f16 input [32][K] (x * gamma, permuted inside groups of 8)
+    int convert;          // 1: this op writes xh_in from x itself (its input comes from outside)
+    int k_out;            // > 0: rows [0, k_out) of the output, times g_out, are the next op's input
+    __half *xh_out;       // ... written here [32][k_out]
+    const float *g_out;   // the next op's RMSNorm weight (or null)
     __device__ float bias_at(int row) const { return bias != nullptr ? bias[row] : 0.f; }
 };
 
 struct BArgs {
     const BOp *ops;
     int nops;
-    int M, NT;
+    int M;
     unsigned *done;       // [nops] arrival counters (monotonic)
+    unsigned *cdone;      // [nops] input-conversion arrival counters (monotonic)
     unsigned *epoch;      // completed launches
     float *part;          // [C][2][32][128] stream-K partial tiles
     unsigned *counters;   // per-tile arrival counters (zero between ops)
@@ -126,76 +141,106 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+// Bounded wait until *p >= target (a grid barrier); false (and the error word set) on expiry.
+__device__ __forceinline__ bool wait_counter(const unsigned *p, unsigned target, int *err) {
+    if (ld_acquire(p) >= target) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire(p) < target) {
+        if (global_timer_ns() - t0 > 2000000000ull) {
+            atomicExch(err, kErrBarrier);
+            return false;
+        }
+    }
+    return true;
+}
 __device__ __forceinline__ void tmap_acquire(const void *map) {
     asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
 }
-__device__ __forceinline__ void tma_load_3d_plain(void *dst, const void *tmap, int c0, int c1, int c2, uint64_t *bar) {
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int c0, int c1, uint64_t *bar) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 }
-// Two Q4_K nibbles (bits 0-3 and 16-19 of w) -> f16x2 of n * A + B with (A, B) = ab (f16 lo, hi).
-__device__ __forceinline__ uint32_t dq2(uint32_t w, uint32_t aa, uint32_t bb) {
-    uint32_t v, n, r;
-    asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(v) : "r"(w));  // (w & m) | c
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(n) : "r"(v), "r"(0x64006400u));     // n, exact
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(n), "r"(aa), "r"(bb));
-    return r;
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-__device__ __forceinline__ void hmma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, f16 inputs, f32 accumulate.
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
 }
-// (d*sc, -dmin*m) of sub-block j of a Q4_K block header h (bytes 0..15) as f16 (lo: A, hi: B).
-__device__ __forceinline__ uint32_t q4k_ab(const uint4 &h, int j) {
-    const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;  // scales bytes 0-3, 4-7, 8-11
-    uint32_t sc, m;
-    if (j < 4) {
-        sc = (s03 >> (8 * j)) & 63u;
-        m = (s47 >> (8 * j)) & 63u;
-    } else {
-        const int i = j - 4;
-        const uint32_t b8 = (s811 >> (8 * i)) & 0xFFu;
-        sc = (b8 & 0x0Fu) | (((s03 >> (8 * i)) >> 6 & 3u) << 4);
-        m = (b8 >> 4) | (((s47 >> (8 * i)) >> 6 & 3u) << 4);
-    }
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    return pack_h2(d * (float)sc, -dmin * (float)m);
+// Arrive (once) on `bar` when every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
 }
-// Token of column g of an 8-token MMA tile: 0, 4, 1, 5, 2, 6, 3, 7 (see the B-fragment loads).
-__device__ __forceinline__ int tperm(int g) { return (g >> 1) | ((g & 1) << 2); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 32 lanes x 16 consecutive 32-bit columns of TMEM -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row atoms of 1024 B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t a) {
+    return ((uint64_t)(a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+// (1024 + n) from a nibble pair placed at bits 0-3 / 16-19 -> n * D - M, in f16.
+__device__ __forceinline__ uint32_t deq2(uint32_t nib, __half2 D, __half2 negM) {
+    const __half2 h = bits_h2(nib | 0x64006400u);
+    return h2_bits(__hfma2(__hsub2(h, __float2half2_rn(1024.f)), D, negM));
+}
+// Position of input k inside its group of 8 in the f16 activation layout (elements 0, 2, 1, 3,
+// 4, 6, 5, 7 at positions 0..7: the order in which the dequantizer emits nibbles).
+__device__ __forceinline__ int xh_pos(int k) { return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1); }
 __device__ __forceinline__ long long ss_to_fixed(float v) { return __float2ll_rn(v * (float)kSsFix); }
 // Stream-K split of an op's T units over min(C, T) CTAs (every participating CTA gets at least
 // one unit, so every CTA whose range touches a tile arrives on that tile's counter).
 __device__ __forceinline__ int op_ctas(int64_t T, int C) { return T < C ? (int)T : C; }
 __device__ __forceinline__ int64_t op_start(int64_t T, int Cp, int c) { return c >= Cp ? T : (int64_t)c * T / Cp; }
 
-template <int NT>  // 8-token MMA tiles per launch (tokens <= 8 * NT)
 __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_constant__ BArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *wfull = reinterpret_cast<uint64_t *>(smem);
     uint64_t *wempty = wfull + kBWSlots;
     uint64_t *xfull = wempty + kBWSlots;
     uint64_t *xempty = xfull + kBXSlots;
-    int *abort_flag = reinterpret_cast<int *>(xempty + kBXSlots);
+    uint64_t *afull = xempty + kBXSlots;       // [half][slot]
+    uint64_t *aempty = afull + 2 * kBASlots;
+    uint64_t *accfull = aempty + 2 * kBASlots;  // [2] accumulator buffers
+    uint64_t *accempty = accfull + 2;
+    uint64_t *mma_done = accempty + 2;
+    uint64_t *tmem_free = mma_done + 1;
+    int *abort_flag = reinterpret_cast<int *>(tmem_free + 1);
     unsigned *epoch_s = reinterpret_cast<unsigned *>(abort_flag + 1);
     int *bcast = reinterpret_cast<int *>(epoch_s + 1);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bcast + 1);
     float *inv_rms = reinterpret_cast<float *>(smem + 256);           // [32]
-    float *red = reinterpret_cast<float *>(smem + kBOffRed);          // [4 chunks][32 tokens][132]
+    float *red = reinterpret_cast<float *>(smem + kBOffRed);          // [32 tokens][132]
     unsigned long long *wkey = reinterpret_cast<unsigned long long *>(smem + kBOffMisc);  // [warp][32]
     float *wss = reinterpret_cast<float *>(smem + kBOffMisc + kBCw * kBMaxTok * 8);        // [warp][32]
-    float *gsm = reinterpret_cast<float *>(smem + kBOffGamma);        // [K] RMSNorm weight of the op
     int *pslot = reinterpret_cast<int *>(smem + kBOffPslot);          // [parts of a shared tile]
+    const uint32_t sX = smem_u32(smem + kBOffX), sA = smem_u32(smem + kBOffA);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, cta = blockIdx.x;
@@ -207,13 +252,27 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         }
         for (int s = 0; s < kBXSlots; ++s) {
             mbar_init(&xfull[s], 1);
-            mbar_init(&xempty[s], kBCw);
+            mbar_init(&xempty[s], 1);
         }
+        for (int s = 0; s < 2 * kBASlots; ++s) {
+            mbar_init(&afull[s], kBCw / 2);
+            mbar_init(&aempty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accfull[b], 1);
+            mbar_init(&accempty[b], 1);
+        }
+        mbar_init(mma_done, 1);
+        mbar_init(tmem_free, kBCw);
         *abort_flag = 0;
         *epoch_s = *reinterpret_cast<volatile unsigned *>(a.epoch);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (warp == 2) tmem_alloc(tmem_slot, kBTmemCols);
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
     const unsigned epoch = *epoch_s;
     const unsigned target = (epoch + 1u) * (unsigned)C;
     long long *ss_cur = a.ss + (size_t)(epoch & 1u) * a.nslots * kBMaxTok;
@@ -263,23 +322,15 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         // -------------------------- activation producer --------------------------
         if (lane != 0) return;
         int it = 0;
-        const uint32_t xbytes = (uint32_t)(NT * 8 * 256 * 4);
         for (int p = 0; p < a.nops; ++p) {
             const BOp &o = a.ops[p];
             const int U = o.U;
             const int64_t T = o.T;
-            if (p > 0 && !aborted()) {  // grid barrier: op p reads what earlier ops wrote
-                const unsigned *d = a.done + (p - 1);
-                if (ld_acquire(d) < target) {
-                    const uint64_t t0 = global_timer_ns();
-                    while (ld_acquire(d) < target) {
-                        if (global_timer_ns() - t0 > 2000000000ull) {
-                            atomicExch(a.err, kErrBarrier);
-                            *abort_flag = 1;
-                            break;
-                        }
-                    }
-                }
+            // grid barrier: the op's f16 input is complete (written by the previous op's epilogues,
+            // or by every CTA's conversion step)
+            if (!aborted()) {
+                const unsigned *d = o.convert ? a.cdone + p : (p > 0 ? a.done + (p - 1) : nullptr);
+                if (d != nullptr && !wait_counter(d, target, a.err)) *abort_flag = 1;
             }
             // the activations were written by generic-proxy stores; the tensor copies read them
             asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -292,136 +343,202 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                     !mbar_wait(&xempty[slot], ((uint32_t)(it / kBXSlots) & 1u) ^ 1u, a.err, kErrWaitEmpty))
                     *abort_flag = 1;
                 const bool live = !aborted();
-                mbar_arrive_expect_tx(&xfull[slot], live ? xbytes : 0u);
-                if (live)
-                    tma_load_3d_plain(smem + kBOffX + slot * kBXBytes, &o.xmap, 0, 0, (int)(u % U) * 8, &xfull[slot]);
+                mbar_arrive_expect_tx(&xfull[slot], live ? (uint32_t)kBXBytes : 0u);
+                if (live) {
+                    const int blk = (int)(u % U);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_2d(smem + kBOffX + slot * kBXBytes + c * kBXBox, &o.xmap, 256 * blk + 64 * c, 0,
+                                    &xfull[slot]);
+                }
             }
         }
         for (int j = (it > kBXSlots ? it - kBXSlots : 0); j < it; ++j)
             mbar_wait(&xfull[j % kBXSlots], (uint32_t)(j / kBXSlots) & 1u, nullptr, 0);
         return;
     }
+    if (warp == 2) {
+        // ------------------------------- MMA issuer -------------------------------
+        if (lane == 0) {
+            int uc = 0, tc = 0;  // units and tiles of this CTA, over all ops
+            for (int p = 0; p < a.nops; ++p) {
+                const BOp &o = a.ops[p];
+                const int U = o.U;
+                const int64_t T = o.T;
+                const int Cp = op_ctas(T, C);
+                const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
+                for (int64_t u = u0; u < u1; ++u, ++uc) {
+                    const int blk = (int)(u % U);
+                    const bool first = (u == u0) || blk == 0, last = (blk == U - 1) || (u + 1 == u1);
+                    const int b = tc & 1;
+                    if (first && tc >= 2 && !aborted() &&
+                        !mbar_wait(&accempty[b], (uint32_t)((tc >> 1) - 1) & 1u, a.err, kErrWaitEmpty))
+                        *abort_flag = 1;
+                    const int xs = uc % kBXSlots;
+                    if (!aborted() && !mbar_wait(&xfull[xs], (uint32_t)(uc / kBXSlots) & 1u, a.err, kErrWaitFull))
+                        *abort_flag = 1;
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        const int hf = c >> 1, j = 2 * uc + (c & 1), slot = hf * kBASlots + j % kBASlots;
+                        if (!aborted() &&
+                            !mbar_wait(&afull[slot], (uint32_t)(j / kBASlots) & 1u, a.err, kErrWaitFull))
+                            *abort_flag = 1;
+                        tc_fence_after();
+                        if (!aborted()) {
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+                                mma_f16(tmem + 32u * (uint32_t)b, sw128_desc(sA + slot * kBABytes + 32 * kk),
+                                        sw128_desc(sX + xs * kBXBytes + c * kBXBox + 32 * kk), kBIdesc,
+                                        (first && c == 0 && kk == 0) ? 0u : 1u);
+                        }
+                        mma_commit(&aempty[slot]);
+                    }
+                    mma_commit(&xempty[xs]);
+                    if (last) {
+                        mma_commit(&accfull[b]);
+                        ++tc;
+                    }
+                }
+            }
+            // every MMA has completed before TMEM is freed
+            mma_commit(mma_done);
+            mbar_wait(mma_done, 0u, a.err, kErrWaitFull);
+        }
+        __syncwarp();
+        // the consumers have read the last accumulator
+        mbar_wait(tmem_free, 0u, a.err, kErrWaitFull);
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kBTmemCols);
+        return;
+    }
 
     // -------------------------------- consumers --------------------------------
-    const int cw = warp - 2, ctid = tid - 64;
-    const int rs = cw >> 2, kc = cw & 3;  // row set (rows 64rs ..), k-chunk (inputs 64kc .. 64kc + 63)
-    const int g = lane >> 2, t = lane & 3;
-    int itw = 0, itx = 0;
+    const int cw = warp - 3, ctid = tid - 96;
+    const int r = ctid & (kBRows - 1), hf = ctid >> 7;  // weight row, half block (sub-blocks 4hf .. 4hf + 3)
+    const int q = warp & 3, dh = cw >> 2;              // TMEM lane quadrant, token half of the drain
+    int itw = 0, uc = 0, tc = 0;
     for (int p = 0; p < a.nops; ++p) {
         const BOp &o = a.ops[p];
         const int kind = o.kind, U = o.U, rows = o.rows, K = o.K;
         const int64_t T = o.T;
         const float *gamma = o.gamma;
         const int Cp = op_ctas(T, C);
-            const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
-        bool norm_ready = false;
-        // the RMSNorm weight (a weight: it does not depend on earlier ops) into shared memory once
-        // per op, so the k-steps read it at shared-memory latency
-        const bool gstaged = gamma != nullptr && K <= kBGammaMax;
-        if (gstaged && u0 < u1) {
-            for (int i = ctid; i < K / 4; i += kBCw * 32)
-                reinterpret_cast<float4 *>(gsm)[i] = __ldg(reinterpret_cast<const float4 *>(gamma) + i);
+        const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
+        if (o.convert) {
+            // this op's input comes from outside the chain (or from an op other than the previous
+            // one): every CTA converts a share of it to f16 x gamma, then a second grid barrier
+            if (p > 0) {
+                if (ctid == 0 && !aborted() && !wait_counter(a.done + (p - 1), target, a.err)) *abort_flag = 1;
+                named_bar_sync(1, kBCw * 32);
+            }
+            const int g8 = K / 8, ng = M * g8;
+            for (int i = cta * kBCw * 32 + ctid; i < ng; i += C * kBCw * 32) {
+                const int t = i / g8, k = 8 * (i - t * g8);
+                const float4 *xp = reinterpret_cast<const float4 *>(o.x + (size_t)t * o.xs + k);
+                float4 v0 = xp[0], v1 = xp[1];
+                if (gamma != nullptr) {
+                    const float4 g0 = reinterpret_cast<const float4 *>(gamma + k)[0];
+                    const float4 g1 = reinterpret_cast<const float4 *>(gamma + k)[1];
+                    v0.x *= g0.x; v0.y *= g0.y; v0.z *= g0.z; v0.w *= g0.w;
+                    v1.x *= g1.x; v1.y *= g1.y; v1.z *= g1.z; v1.w *= g1.w;
+                }
+                uint4 hv;  // positions 0..7 <- elements 0, 2, 1, 3, 4, 6, 5, 7
+                hv.x = h2_bits(__floats2half2_rn(v0.x, v0.z));
+                hv.y = h2_bits(__floats2half2_rn(v0.y, v0.w));
+                hv.z = h2_bits(__floats2half2_rn(v1.x, v1.z));
+                hv.w = h2_bits(__floats2half2_rn(v1.y, v1.w));
+                *reinterpret_cast<uint4 *>(o.xh_in + (size_t)t * K + k) = hv;
+            }
+            __threadfence();
+            named_bar_sync(1, kBCw * 32);
+            if (ctid == 0) atomicAdd(a.cdone + p, 1u);
         }
-        named_bar_sync(1, kBCw * 32);
-        const float *gk = gstaged ? gsm : gamma;
+        bool norm_ready = false;
         const bool track = o.amax.amax != nullptr || o.ss_out >= 0;
         // per-warp running results over the tiles this CTA finishes (greedy keys, sums of squares),
         // each slot written by one lane only: deterministic
         wkey[cw * kBMaxTok + lane] = 0ull;
         wss[cw * kBMaxTok + lane] = 0.f;
-        float acc[4][4][4];  // rows 64rs + 16m + g (+8), tokens of n-tile n
-#pragma unroll
-        for (int m = 0; m < 4; ++m)
-#pragma unroll
-            for (int n = 0; n < 4; ++n)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
 
-        for (int64_t u = u0; u < u1; ++u, ++itw, ++itx) {
+        for (int64_t u = u0; u < u1; ++u, ++itw, ++uc) {
             const int tile = (int)(u / U), blk = (int)(u % U);
-            const int ws = itw % kBWSlots, xsl = itx % kBXSlots;
-            if (!aborted() && !mbar_wait(&wfull[ws], (uint32_t)(itw / kBWSlots) & 1u, a.err, kErrWaitFull))
+            const int ws = itw % kBWSlots;
+            if (!__all_sync(0xffffffffu, !aborted() && mbar_wait(&wfull[ws], (uint32_t)(itw / kBWSlots) & 1u,
+                                                                  a.err, kErrWaitFull)))
                 *abort_flag = 1;
-            if (!aborted() && !mbar_wait(&xfull[xsl], (uint32_t)(itx / kBXSlots) & 1u, a.err, kErrWaitFull))
-                *abort_flag = 1;
-            if (!__any_sync(0xffffffffu, aborted())) {
-                const uint8_t *wb = smem + kBOffW + ws * kBWBytes + rs * 64 * 144;
-                const uint8_t *xb = smem + kBOffX + xsl * kBXBytes;
-                // This lane's rows are 16m + g and 16m + g + 8 of the row set (m = 0..3), its inputs
-                // 4t .. 4t + 3 of each 16-input step.  Lane (g, t) decodes the sub-block scales of rows
-                // 16t + g (+8); the four lanes of a quad then share them.  Few values stay live across
-                // the k-steps: scales per sub-block, weight words per m-tile.
-                uint32_t mine[2][2];  // [row 16t + g or 16t + g + 8][sub-block 2kc or 2kc + 1]
+            {
+                // ---- dequantize this thread's row, inputs 128 hf .. 128 hf + 127 of the block ----
+                const uint8_t *wrow = smem + kBOffW + ws * kBWBytes + r * 144;
+                const uint4 hd = *reinterpret_cast<const uint4 *>(wrow);
+                const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
+                // q4k_scale_min (reference kernel.cu:913-921): sub-blocks 0-3 or 4-7 as packed bytes
+                const uint32_t scw = hf == 0 ? (hd.y & 0x3F3F3F3Fu) : ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u));
+                const uint32_t mw = hf == 0 ? (hd.z & 0x3F3F3F3Fu)
+                                            : (((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u));
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint4 hd = *reinterpret_cast<const uint4 *>(wb + (16 * t + g + 8 * h) * 144);
-                    mine[h][0] = q4k_ab(hd, 2 * kc);
-                    mine[h][1] = q4k_ab(hd, 2 * kc + 1);
-                }
-                const uint8_t *wq = wb + g * 144 + 16 + 32 * kc + 4 * t;  // this lane's word of row g, j = 0
-#pragma unroll 1
-                for (int sh = 0; sh < 2; ++sh) {  // sub-block 2kc (low nibbles), 2kc + 1 (high nibbles)
-                    const int sb = 2 * kc + sh;
-                    uint32_t ab[4][2];
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int pch = 2 * hf + cc;  // 64-input chunk of the block: sub-blocks 2 pch, 2 pch + 1
+                    const int j = 2 * uc + cc, slot = hf * kBASlots + j % kBASlots;
+                    const int sh0 = 16 * cc, sh1 = sh0 + 8;
+                    const __half2 D0 = __float2half2_rn(d * (float)((scw >> sh0) & 0xFFu));
+                    const __half2 M0 = __hneg2(__float2half2_rn(dmin * (float)((mw >> sh0) & 0xFFu)));
+                    const __half2 D1 = __float2half2_rn(d * (float)((scw >> sh1) & 0xFFu));
+                    const __half2 M1 = __hneg2(__float2half2_rn(dmin * (float)((mw >> sh1) & 0xFFu)));
+                    const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + 16 + 32 * pch);
+                    const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + 32 + 32 * pch);
+                    const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                    uint4 lo[4], hi[4];
 #pragma unroll
-                    for (int m = 0; m < 4; ++m)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            ab[m][h] = __shfl_sync(0xffffffffu, sh ? mine[h][1] : mine[h][0], (g << 2) | m);
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {  // 16-input step
-                        // B fragments: column g of n-tile n is token 8n + tperm(g) (tperm puts the two
-                        // rows a quarter-warp reads 4 apart, so their swizzled chunks never collide);
-                        // inputs 16j + 4t .. +3 of sub-block sb
-                        float2 g01 = make_float2(1.f, 1.f), g23 = make_float2(1.f, 1.f);
-                        if (gamma != nullptr) {
-                            const float4 gm = *reinterpret_cast<const float4 *>(gk + 256 * blk + 32 * sb + 16 * j + 4 * t);
-                            g01 = make_float2(gm.x, gm.z);
-                            g23 = make_float2(gm.y, gm.w);
-                        }
-                        uint32_t bf[4][2];
-#pragma unroll
-                        for (int n = 0; n < 4; ++n) {
-                            if (n < NT) {
-                                const int tok = 8 * n + tperm(g);
-                                const float4 v = *reinterpret_cast<const float4 *>(
-                                    xb + ((size_t)sb * (NT * 8) + tok) * 128 + (((4 * j + t) ^ (tok & 7)) << 4));
-                                const float2 p0 = fmul2(make_float2(v.x, v.z), g01);
-                                const float2 p1 = fmul2(make_float2(v.y, v.w), g23);
-                                bf[n][0] = pack_h2(p0.x, p0.y);
-                                bf[n][1] = pack_h2(p1.x, p1.y);
-                            } else {
-                                bf[n][0] = bf[n][1] = 0u;
-                            }
-                        }
-#pragma unroll
-                        for (int m = 0; m < 4; ++m) {
-                            const uint32_t a0 = ab[m][0], a1 = ab[m][1];
-                            const uint32_t aa0 = __byte_perm(a0, 0, 0x1010), bb0 = __byte_perm(a0, 0, 0x3232);
-                            const uint32_t aa1 = __byte_perm(a1, 0, 0x1010), bb1 = __byte_perm(a1, 0, 0x3232);
-                            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wq + (16 * m) * 144 + 16 * j) >> (4 * sh);
-                            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(wq + (16 * m + 8) * 144 + 16 * j) >> (4 * sh);
-                            uint32_t af[4];
-                            af[0] = dq2(w0, aa0, bb0);        // row g,     inputs 4t, 4t+2
-                            af[1] = dq2(w1, aa1, bb1);        // row g + 8, inputs 4t, 4t+2
-                            af[2] = dq2(w0 >> 8, aa0, bb0);   // row g,     inputs 4t+1, 4t+3
-                            af[3] = dq2(w1 >> 8, aa1, bb1);   // row g + 8, inputs 4t+1, 4t+3
-#pragma unroll
-                            for (int n = 0; n < 4; ++n)
-                                if (n < NT) hmma(acc[m][n], af, bf[n][0], bf[n][1]);
-                        }
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const uint32_t w0 = W[2 * jj], w1 = W[2 * jj + 1];
+                        // sub-block 2 pch (low nibbles) and 2 pch + 1 (high nibbles), elements 8 jj .. 8 jj + 7
+                        lo[jj].x = deq2(w0 & 0x000F000Fu, D0, M0);
+                        lo[jj].y = deq2((w0 >> 8) & 0x000F000Fu, D0, M0);
+                        lo[jj].z = deq2(w1 & 0x000F000Fu, D0, M0);
+                        lo[jj].w = deq2((w1 >> 8) & 0x000F000Fu, D0, M0);
+                        hi[jj].x = deq2((w0 >> 4) & 0x000F000Fu, D1, M1);
+                        hi[jj].y = deq2((w0 >> 12) & 0x000F000Fu, D1, M1);
+                        hi[jj].z = deq2((w1 >> 4) & 0x000F000Fu, D1, M1);
+                        hi[jj].w = deq2((w1 >> 12) & 0x000F000Fu, D1, M1);
                     }
+                    // the slot is free once the MMAs that read it two chunks ago have completed
+                    if (j >= kBASlots &&
+                        !__all_sync(0xffffffffu, !aborted() && mbar_wait(&aempty[slot], (uint32_t)(j / kBASlots - 1) & 1u,
+                                                                          a.err, kErrWaitEmpty)))
+                        *abort_flag = 1;
+                    uint8_t *arow = smem + kBOffA + slot * kBABytes + r * 128;
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = lo[jj];
+                        *reinterpret_cast<uint4 *>(arow + (((4 + jj) ^ (r & 7)) << 4)) = hi[jj];
+                    }
+                    fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's async proxy
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&afull[slot]);
                 }
             }
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&wempty[ws]);
-                mbar_arrive(&xempty[xsl]);
-            }
+            if (lane == 0) mbar_arrive(&wempty[ws]);
             const bool tile_end = (blk == U - 1) || (u + 1 == u1);
             if (!tile_end) continue;
 
             // ---------------- end of this CTA's part of a tile ----------------
+            {
+                const int b = tc & 1;
+                if (!__all_sync(0xffffffffu, !aborted() && mbar_wait(&accfull[b], (uint32_t)(tc >> 1) & 1u, a.err,
+                                                                      kErrWaitFull)))
+                    *abort_flag = 1;
+                tc_fence_after();
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 32u * (uint32_t)b + 16u * (uint32_t)dh, v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) red[(16 * dh + i) * kBRedPitch + 32 * q + lane] = __uint_as_float(v[i]);
+                tc_fence_before();
+                named_bar_sync(1, kBCw * 32);
+                if (ctid == 0) mbar_arrive(&accempty[b]);
+                ++tc;
+            }
             if (!norm_ready && gamma != nullptr) {
                 // RMSNorm factors of the op's input rows (the op's activations are complete: this
                 // CTA consumed at least one of their tiles)
@@ -435,8 +552,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                         const float *xr = o.x + (size_t)tok * o.xs;
                         float s = 0.f;
                         for (int k = 4 * lane; k < K; k += 128) {
-                            const float4 v = __ldcg(reinterpret_cast<const float4 *>(xr + k));
-                            s = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, s))));
+                            const float4 xv = __ldcg(reinterpret_cast<const float4 *>(xr + k));
+                            s = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, fmaf(xv.w, xv.w, s))));
                         }
 #pragma unroll
                         for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
@@ -444,45 +561,24 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                     }
                 }
                 norm_ready = true;
+                named_bar_sync(1, kBCw * 32);
             }
-            // k-chunk partials -> red[kc][token][row]
-            float *rw = red + (size_t)kc * kBMaxTok * kBRedPitch;
-#pragma unroll
-            for (int m = 0; m < 4; ++m)
-#pragma unroll
-                for (int n = 0; n < 4; ++n) {
-                    if (n < NT) {
-                        const int r = 64 * rs + 16 * m + g;
-                        const int tk0 = 8 * n + tperm(2 * t), tk1 = 8 * n + tperm(2 * t + 1);
-                        rw[tk0 * kBRedPitch + r] = acc[m][n][0];
-                        rw[tk1 * kBRedPitch + r] = acc[m][n][1];
-                        rw[tk0 * kBRedPitch + r + 8] = acc[m][n][2];
-                        rw[tk1 * kBRedPitch + r + 8] = acc[m][n][3];
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
-                }
-            named_bar_sync(1, kBCw * 32);
-            // The tile's sums over the four k-chunks (from red), or, when the tile is shared with
-            // other CTAs, over the parts those CTAs parked (in CTA order): computed per (token, row)
-            // where needed, so that few values are live at once.
+            // The tile's sums (from red), or, when the tile is shared with other CTAs, over the parts
+            // those CTAs parked (in CTA order): computed per (token, row) where needed.
             const int64_t ts = (int64_t)tile * U, te = ts + U;
             // every decision that leads to a named barrier is uniform over the consumer threads
             // (never the abort flag, which another warp may set at any time)
             const bool partial = ts < u0 || te > u1;
             bool finish = true;
             int nparts = 0;
-            auto red_sum = [&](int tk, int row) {
-                return red[(0 * kBMaxTok + tk) * kBRedPitch + row] + red[(1 * kBMaxTok + tk) * kBRedPitch + row] +
-                       red[(2 * kBMaxTok + tk) * kBRedPitch + row] + red[(3 * kBMaxTok + tk) * kBRedPitch + row];
-            };
             if (partial) {
                 // stream-K: park this part; the last CTA of the tile sums the parts in CTA order
                 const int si = (tile == (int)(u0 / U)) ? 0 : 1;
                 float *pp = a.part + ((size_t)cta * 2 + si) * (kBMaxTok * kBRows);
-                const int r = ctid & (kBRows - 1), th = ctid >> 7;  // thread = (row, 16 tokens)
+                const int th = ctid >> 7;  // thread = (row r, 16 tokens)
 #pragma unroll 4
-                for (int i = 0; i < 16; ++i) __stcg(pp + (16 * th + i) * kBRows + r, red_sum(16 * th + i, r));
+                for (int i = 0; i < 16; ++i)
+                    __stcg(pp + (16 * th + i) * kBRows + r, red[(16 * th + i) * kBRedPitch + r]);
                 __threadfence();
                 named_bar_sync(1, kBCw * 32);
                 const int cf = (int)(((ts + 1) * (int64_t)Cp - 1) / T), cl = (int)((te * (int64_t)Cp - 1) / T);
@@ -501,31 +597,40 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                 }
             }
             auto tile_sum = [&](int tk, int row) {
-                if (!partial) return red_sum(tk, row);
+                if (!partial) return red[tk * kBRedPitch + row];
                 float sacc = 0.f;
                 for (int i = 0; i < nparts; ++i)
                     sacc += __ldcg(a.part + (size_t)pslot[i] * (kBMaxTok * kBRows) + tk * kBRows + row);
                 return sacc;
             };
+            // the next op's f16 input: rows < k_out of this output, times its RMSNorm weight
+            auto put_next = [&](int tk, int row, float v) {
+                if (row < o.k_out) {
+                    const float g = o.g_out != nullptr ? __ldg(o.g_out + row) : 1.f;
+                    o.xh_out[(size_t)tk * o.k_out + xh_pos(row)] = __float2half_rn(v * g);
+                }
+            };
             if (finish) {
                 if (kind == kBSwiglu) {
-                    // thread = (gate row r < 64, 8 tokens); its up row is r + 64
-                    const int r = ctid & 63, tq = ctid >> 6;
-                    const int row = tile * 64 + r;
+                    // thread = (gate row rr < 64, 8 tokens); its up row is rr + 64
+                    const int rr = ctid & 63, tq = ctid >> 6;
+                    const int row = tile * 64 + rr;
                     if (row < rows) {
 #pragma unroll 2
                         for (int i = 0; i < 8; ++i) {
                             const int tk = 8 * tq + i;
                             if (tk < M) {
                                 const float nrm = gamma != nullptr ? inv_rms[tk] : 1.f;
-                                const float gv = tile_sum(tk, r) * nrm, uv = tile_sum(tk, r + 64) * nrm;
-                                o.y[(size_t)tk * o.ys + row] = gv / (1.0f + expf(-gv)) * uv;
+                                const float gv = tile_sum(tk, rr) * nrm, uv = tile_sum(tk, rr + 64) * nrm;
+                                const float out = gv / (1.0f + expf(-gv)) * uv;
+                                if (o.y != nullptr) o.y[(size_t)tk * o.ys + row] = out;
+                                put_next(tk, row, out);
                             }
                         }
                     }
                 } else {
                     // thread = (row r, 16 tokens); warp cw holds rows 32(cw & 3) .., tokens 16(cw >> 2) ..
-                    const int r = ctid & (kBRows - 1), th = ctid >> 7;
+                    const int th = ctid >> 7;
                     const int row = tile * kBRows + r;
                     const bool live = row < rows;
                     const float bias = (live && o.bias != nullptr) ? o.bias[row] : 0.f;
@@ -547,15 +652,16 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                                     // RoPE: rows i and i + half of a head pair up (the reference's
                                     // rotation, kernel.cu:186-260); both lie in this tile
                                     const int hd = o.head_dim, half = hd >> 1, pi = row % hd;
-                                    const int i = pi % half, rp = r + (pi < half ? half : -half);
+                                    const int i2 = pi % half, rp = r + (pi < half ? half : -half);
                                     const float xp = tile_sum(tk, rp) * nrm + o.bias_at(tile * kBRows + rp);
-                                    const float inv_freq = 1.0f / powf(o.rope_theta, (float)(2 * i) / (float)hd);
-                                    const float ang = (float)__ldg(o.rope_pos + tk) * inv_freq;
-                                    const float c = cosf(ang), sn = sinf(ang);
+                                    const float ang = (float)__ldg(o.rope_pos + tk) * __ldg(o.rope_inv + i2);
+                                    float sn, c;
+                                    sincosf(ang, &sn, &c);
                                     out = pi < half ? out * c - xp * sn : out * c + xp * sn;
                                 }
                                 if (yp) *yp = out;
                             }
+                            put_next(tk, row, out);
                             if (o.amax.amax != nullptr) key = amax_key(out, (uint32_t)(row + o.amax.offset));
                         }
                         if (track) {  // warp-uniform: fold this tile into the warp's running slots
@@ -602,34 +708,46 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             if (p == a.nops - 1 && prev == target - 1u) atomicAdd(a.epoch, 1u);
         }
     }
-}
-
-using BKernel = void (*)(const BArgs);
-BKernel bchain_kernel_for(int NT) {
-    return NT == 1 ? bchain_kernel<1> : NT == 2 ? bchain_kernel<2> : NT == 3 ? bchain_kernel<3> : bchain_kernel<4>;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tmem_free);
 }
 
 struct BChain {
     int magic = 0x42434821;  // "BCH!": told apart from the one-token chain by ql_gemv_chain_run
     BOp *ops_dev = nullptr;
-    unsigned *done = nullptr;          // [nops] counters, [1] epoch, [nops] argmax counters
+    unsigned *done = nullptr;          // [nops] counters, [1] epoch, [nops] argmax counters, [nops] conversions
     unsigned long long *keys = nullptr;  // [nops][32]
     long long *ss = nullptr;
     float *part = nullptr;
+    __half *xh = nullptr;              // [2][32][kmax] f16 op inputs (by op parity)
+    float *rope = nullptr;             // RoPE inverse-frequency tables
     BArgs args{};
     int sms = 0;
 };
 
-bool f32_act_map(CUtensorMap *out, const float *x, int M, int64_t xs, int K, int NT) {
+// f16 activations [32][K] viewed as {K, 32}; box {64, 32} with 128-byte swizzle.
+bool f16_act_map(CUtensorMap *out, const __half *xh, int K) {
     auto enc = tensor_map_encoder_public();
     if (enc == nullptr) return false;
-    const cuuint64_t dims[3] = {32, (cuuint64_t)M, (cuuint64_t)(K / 32)};
-    const cuuint64_t strides[2] = {(cuuint64_t)xs * 4, 128};
-    const cuuint32_t box[3] = {32, (cuuint32_t)(NT * 8), 8};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    return enc(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(x), dims, strides, box, estr,
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)kBMaxTok};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)kBMaxTok};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(xh), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+void bchain_free(BChain *c) {
+    if (c->ops_dev) cudaFree(c->ops_dev);
+    if (c->done) cudaFree(c->done);
+    if (c->keys) cudaFree(c->keys);
+    if (c->ss) cudaFree(c->ss);
+    if (c->part) cudaFree(c->part);
+    if (c->xh) cudaFree(c->xh);
+    if (c->rope) cudaFree(c->rope);
+    delete c;
 }
 
 }  // namespace
@@ -644,12 +762,11 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
     int *err, sms;
     int st = chain_workspace(&wpart, &counters, &err, &sms);
     if (st) return st;
-    const int NT = (tokens + 7) / 8;
     std::vector<BOp> h(nops);
     // rows each op writes (for the producer/consumer analysis of the RMSNorm sums)
     std::vector<int> out_w(nops, 0);
-    std::vector<int64_t> out_s(nops, 0);
-    int nslots = 0;
+    std::vector<std::pair<int, std::vector<float>>> rope_tables;  // (op, inverse frequencies)
+    int nslots = 0, kmax = 0;
     for (int p = 0; p < nops; ++p) {
         const ql_chain_op &q = ops[p];
         BOp &o = h[p];
@@ -690,8 +807,6 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
         }
         if (nsrc == 1 && q.kind != QL_OP_SWIGLU) o.split0 = o.split1 = total;
         for (int s = nsrc; s < 3; ++s) o.wmap[s] = o.wmap[nsrc - 1];
-        if (!f32_act_map(&o.xmap, q.x, tokens, xs, q.in_dim, NT))
-            return set_last_error(QL_ECUDA, (what + ": activation tensor map").c_str());
         o.kind = q.kind == QL_OP_STORE ? kBStore : q.kind == QL_OP_ADD ? kBAdd : kBSwiglu;
         o.nmat = q.kind == QL_OP_SWIGLU ? 2 : 1;
         o.rows = total;
@@ -717,9 +832,12 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
                 return set_last_error(QL_EINVAL, (what + ": RoPE needs a STORE op without argmax, rope_pos, head_dim "
                                                          "32, 64 or 128 and rope_rows whole heads of sources 0 and 1").c_str());
             o.rope_pos = q.rope_pos;
-            o.rope_theta = q.rope_theta;
             o.rope_rows = q.rope_rows;
             o.head_dim = hd;
+            // the reference's inverse frequencies 1 / powf(theta, 2i / head_dim) (kernel.cu:186-260)
+            std::vector<float> inv(hd / 2);
+            for (int i = 0; i < hd / 2; ++i) inv[i] = 1.0f / powf(q.rope_theta, (float)(2 * i) / (float)hd);
+            rope_tables.push_back({p, inv});
         }
         if (q.argmax_idx) {
             if (q.kind != QL_OP_STORE) return set_last_error(QL_EINVAL, (what + ": argmax needs a store op").c_str());
@@ -727,7 +845,7 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
             o.amax.offset = q.argmax_offset;
         }
         out_w[p] = q.y ? total : 0;
-        out_s[p] = o.ys;
+        kmax = q.in_dim > kmax ? q.in_dim : kmax;
     }
     // RMSNorm inputs produced inside the chain: the last earlier op that wrote them sums their
     // squares in its epilogue (same buffer, same row stride, covering all in_dim columns)
@@ -747,38 +865,67 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
     }
     BChain *c = new BChain();
     c->sms = sms;
+    const size_t xh_elems = (size_t)kBMaxTok * kmax;
+    size_t nrope = 0;
+    for (auto &rt : rope_tables) nrope += rt.second.size();
     cudaError_t e = cudaMalloc(&c->ops_dev, sizeof(BOp) * nops);
-    if (e == cudaSuccess) e = cudaMalloc(&c->done, sizeof(unsigned) * (2 * nops + 1));
+    if (e == cudaSuccess) e = cudaMalloc(&c->done, sizeof(unsigned) * (3 * nops + 1));
     if (e == cudaSuccess) e = cudaMalloc(&c->keys, sizeof(unsigned long long) * nops * kBMaxTok);
     if (e == cudaSuccess) e = cudaMalloc(&c->ss, sizeof(long long) * 2 * (nslots > 0 ? nslots : 1) * kBMaxTok);
     if (e == cudaSuccess) e = cudaMalloc(&c->part, sizeof(float) * (size_t)sms * 2 * kBMaxTok * kBRows);
-    if (e == cudaSuccess) e = cudaMemset(c->done, 0, sizeof(unsigned) * (2 * nops + 1));
+    if (e == cudaSuccess) e = cudaMalloc(&c->xh, sizeof(__half) * 2 * xh_elems);
+    if (e == cudaSuccess && nrope) e = cudaMalloc(&c->rope, sizeof(float) * nrope);
+    if (e == cudaSuccess) e = cudaMemset(c->done, 0, sizeof(unsigned) * (3 * nops + 1));
     if (e == cudaSuccess) e = cudaMemset(c->keys, 0, sizeof(unsigned long long) * nops * kBMaxTok);
     if (e == cudaSuccess) e = cudaMemset(c->ss, 0, sizeof(long long) * 2 * (nslots > 0 ? nslots : 1) * kBMaxTok);
-    if (e == cudaSuccess) {
-        for (int p = 0; p < nops; ++p)
-            if (h[p].amax.idx) {
-                h[p].amax.amax = c->keys + (size_t)p * kBMaxTok;
-                h[p].amax.done = c->done + nops + 1 + p;
-            }
-        e = cudaMemcpy(c->ops_dev, h.data(), sizeof(BOp) * nops, cudaMemcpyHostToDevice);
+    // token rows >= tokens stay zero: the MMA always runs 32 columns
+    if (e == cudaSuccess) e = cudaMemset(c->xh, 0, sizeof(__half) * 2 * xh_elems);
+    size_t at = 0;
+    for (auto &rt : rope_tables) {
+        if (e == cudaSuccess)
+            e = cudaMemcpy(c->rope + at, rt.second.data(), rt.second.size() * sizeof(float), cudaMemcpyHostToDevice);
+        h[rt.first].rope_inv = c->rope + at;
+        at += rt.second.size();
     }
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(bchain_kernel_for(NT), cudaFuncAttributeMaxDynamicSharedMemorySize, kBSmem);
     if (e != cudaSuccess) {
-        if (c->ops_dev) cudaFree(c->ops_dev);
-        if (c->done) cudaFree(c->done);
-        if (c->keys) cudaFree(c->keys);
-        if (c->ss) cudaFree(c->ss);
-        if (c->part) cudaFree(c->part);
-        delete c;
+        bchain_free(c);
+        return set_last_error(QL_ECUDA, (std::string("ql_gemv_chain_create_batch: ") + cudaGetErrorString(e)).c_str());
+    }
+    // f16 inputs: op p reads buffer p & 1.  Its input is written by op p - 1's epilogue when op p
+    // reads op p - 1's output (same buffer and row stride, all in_dim columns written); otherwise op
+    // p converts it at its start.
+    for (int p = 0; p < nops; ++p) {
+        BOp &o = h[p];
+        o.xh_in = c->xh + (size_t)(p & 1) * xh_elems;
+        const bool chained = p > 0 && h[p - 1].y == o.x && h[p - 1].ys == o.xs && out_w[p - 1] >= o.K;
+        o.convert = chained ? 0 : 1;
+        if (chained) {
+            h[p - 1].k_out = o.K;
+            h[p - 1].xh_out = o.xh_in;
+            h[p - 1].g_out = o.gamma;
+        }
+        if (!f16_act_map(&o.xmap, o.xh_in, o.K)) {
+            bchain_free(c);
+            return set_last_error(QL_ECUDA, "ql_gemv_chain_create_batch: activation tensor map");
+        }
+    }
+    for (int p = 0; p < nops; ++p)
+        if (h[p].amax.idx) {
+            h[p].amax.amax = c->keys + (size_t)p * kBMaxTok;
+            h[p].amax.done = c->done + nops + 1 + p;
+        }
+    e = cudaMemcpy(c->ops_dev, h.data(), sizeof(BOp) * nops, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(bchain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBSmem);
+    if (e != cudaSuccess) {
+        bchain_free(c);
         return set_last_error(QL_ECUDA, (std::string("ql_gemv_chain_create_batch: ") + cudaGetErrorString(e)).c_str());
     }
     c->args.ops = c->ops_dev;
     c->args.nops = nops;
     c->args.M = tokens;
-    c->args.NT = NT;
     c->args.done = c->done;
     c->args.epoch = c->done + nops;
+    c->args.cdone = c->done + 2 * nops + 1;
     c->args.part = c->part;
     c->args.counters = counters;
     c->args.err = err;
@@ -802,7 +949,7 @@ int bchain_run(void *chain, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, bchain_kernel_for(c->args.NT), c->args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, bchain_kernel, c->args);
     set_launch_count(1);
     if (e != cudaSuccess) return set_last_error(QL_ECUDA, cudaGetErrorString(e));
     return QL_OK;
@@ -811,12 +958,7 @@ int bchain_run(void *chain, cudaStream_t s) {
 int bchain_destroy(void *chain) {
     BChain *c = static_cast<BChain *>(chain);
     cudaDeviceSynchronize();
-    cudaFree(c->ops_dev);
-    cudaFree(c->done);
-    cudaFree(c->keys);
-    cudaFree(c->ss);
-    cudaFree(c->part);
-    delete c;
+    bchain_free(c);
     return QL_OK;
 }
 
