@@ -14,18 +14,19 @@
 //     (monotonic arrival counters, so a CUDA graph can replay the launch without resets).
 //   * Work unit = a tile of 128 output rows (SwiGLU: 64 gate + 64 up rows) x one Q4_K block (256
 //     inputs).  Units are split over the CTAs in equal contiguous ranges (stream-K); a tile shared
-//     by several CTAs is finished by the last to arrive, which sums the parts in CTA order
-//     (deterministic).
+//     by several CTAs is summed in a 64-bit fixed-point accumulator (integer reductions: exact, so
+//     deterministic) and finished by the last CTA to arrive.
 //   * The weights are the MMA's M side (128 rows), the tokens its N side (32 columns):
 //     tcgen05.mma.kind::f16, M 128, N 32, K 16, fp32 accumulators in TMEM (two 32-column
 //     buffers, so a tile's drain overlaps the next tile's MMAs).
 //   * Warp 0 streams the raw Q4_K bytes of every unit (TMA box {144 B, 1 block, 128 rows}) into a
-//     4-slot ring, across op boundaries (weights do not depend on activations).  Warp 1 waits for
+//     6-slot ring, across op boundaries (weights do not depend on activations).  Warp 1 waits for
 //     the op's grid barrier and streams the unit's activations: f16, [32 tokens][256 inputs], four
 //     TMA boxes {64, 32} with 128-byte swizzle, i.e. already the MMA's canonical K-major B layout.
 //     Warp 2 owns TMEM and one of its threads issues the MMAs.
-//   * Warps 3..10 (thread = weight row x half block) dequantize their 128 weights per unit into
-//     the canonical K-major 128-byte-swizzled A layout: a 32-bit word of nibbles gives f16 pairs
+//   * Warps 3..10 (thread = weight row x half block) dequantize their 128 weights per unit straight
+//     into tensor memory (tcgen05.st: the MMA reads A from TMEM, lane = weight row, so the weights
+//     never pass through shared memory; a 3-unit TMEM ring): a 32-bit word of nibbles gives f16 pairs
 //     through (w & 0x000F000F) | 0x6400 (= 1024 + n, exact), an exact f16 subtraction of 1024 and
 //     one f16 FMA with the sub-block's (d*sc, -dmin*m) -- the reference's value formula
 //     d*sc*q - dmin*m (kernel.cu:913-921,1090-1119) rounded once to f16.  Elements are emitted in
@@ -68,25 +69,24 @@ constexpr int kBMaxTok = 32;                       // MMA N
 constexpr int kBRows = 128;                        // output rows per tile = MMA M
 constexpr int kBCw = 8;                            // dequantizer / epilogue warps
 constexpr int kBThreads = (3 + kBCw) * 32;         // weight TMA, activation TMA, MMA, consumers
-constexpr int kBWSlots = 4;                        // raw weight ring
-constexpr int kBXSlots = 3;                        // activation ring
-constexpr int kBASlots = 2;                        // dequantized 64-input chunks per half block
+constexpr int kBWSlots = 6;                        // raw weight ring
+constexpr int kBXSlots = 4;                        // activation ring
+constexpr int kBASlots = 3;                        // dequantized units in TMEM (128 columns each)
 constexpr int kBWBytes = kBRows * 144;             // 18,432 B: one block column of a tile
 constexpr int kBXBox = kBMaxTok * 64 * 2;          // 4 KB: 32 tokens x 64 inputs, f16
 constexpr int kBXBytes = 4 * kBXBox;               // one block of activations
-constexpr int kBABytes = kBRows * 128;             // 16 KB: 128 rows x 64 inputs, f16
 constexpr int kBRedPitch = kBRows + 4;             // floats per token row of the drained tile
 constexpr int kBRedBytes = kBMaxTok * kBRedPitch * 4;
 constexpr int kBHdr = 1024;
 constexpr int kBOffW = kBHdr;
 constexpr int kBOffX = kBOffW + kBWSlots * kBWBytes;
-constexpr int kBOffA = kBOffX + kBXSlots * kBXBytes;
-constexpr int kBOffRed = kBOffA + 2 * kBASlots * kBABytes;
+constexpr int kBOffRed = kBOffX + kBXSlots * kBXBytes;
 constexpr int kBOffMisc = kBOffRed + kBRedBytes;   // per-warp token reductions
-constexpr int kBOffPslot = kBOffMisc + 2 * kBCw * kBMaxTok * 8;  // stream-K part slots of the tile being finished
-constexpr int kBSmem = kBOffPslot + 256 * 4;
-constexpr uint32_t kBTmemCols = 64;                // two 32-column accumulators
-static_assert(kBOffX % 1024 == 0 && kBOffA % 1024 == 0, "swizzled rings must be 1024-byte aligned");
+constexpr int kBSmem = kBOffMisc + 2 * kBCw * kBMaxTok * 8;
+constexpr uint32_t kBTmemCols = 512;               // two 32-column accumulators, then the A ring
+constexpr uint32_t kBTmemA = 64;                   // first column of the A ring
+static_assert(kBTmemA + 128 * kBASlots <= kBTmemCols, "tensor memory");
+static_assert(kBOffX % 1024 == 0, "swizzled ring must be 1024-byte aligned");
 static_assert(kBSmem <= 227 * 1024, "shared memory");
 constexpr int kErrBarrier = 5;
 constexpr double kSsFix = 16777216.0;  // 2^24: fixed-point sums of squares
@@ -129,7 +129,7 @@ struct BArgs {
     unsigned *done;       // [nops] arrival counters (monotonic)
     unsigned *cdone;      // [nops] input-conversion arrival counters (monotonic)
     unsigned *epoch;      // completed launches
-    float *part;          // [C][2][32][128] stream-K partial tiles
+    long long *fixacc;    // [tiles][32][128] stream-K tile accumulators in fixed point (zero between ops)
     unsigned *counters;   // per-tile arrival counters (zero between ops)
     int *err;
     long long *ss;        // [2][nslots][32] fixed-point sums of squares, by launch parity
@@ -173,21 +173,32 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, f16 inputs, f32 accumulate.
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, f16 inputs, f32 accumulate.
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc)
         : "memory");
 }
+// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes <- 32 registers per thread.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Arrive (once) on `bar` when every tcgen05 operation this thread issued so far has completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // 32 lanes x 16 consecutive 32-bit columns of TMEM -> 16 registers per thread.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
@@ -214,6 +225,53 @@ __device__ __forceinline__ uint32_t deq2(uint32_t nib, __half2 D, __half2 negM) 
 // 4, 6, 5, 7 at positions 0..7: the order in which the dequantizer emits nibbles).
 __device__ __forceinline__ int xh_pos(int k) { return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1); }
 __device__ __forceinline__ long long ss_to_fixed(float v) { return __float2ll_rn(v * (float)kSsFix); }
+// Stream-K partial sums in fixed point: 32 fractional bits in an int64 (|v| < 2^31).
+__device__ __forceinline__ long long to_fixed32(float v) { return __float2ll_rn(v * 4294967296.0f); }
+__device__ __forceinline__ float from_fixed32(long long v) { return (float)((double)v * (1.0 / 4294967296.0)); }
+// Warp reductions of 8 values per lane over the 32 lanes, in a fixed order (deterministic): three
+// exchange-half steps (lane bits 4, 3, 2), then two butterfly steps (bits 1, 0).  Lane l ends with
+// the result for value index reduce8_index(l).
+__device__ __forceinline__ int reduce8_index(int lane) {
+    return 4 * ((lane >> 4) & 1) + 2 * ((lane >> 3) & 1) + ((lane >> 2) & 1);
+}
+__device__ __forceinline__ float reduce8_sum(const float (&v)[8], int lane) {
+    float w[4], x[2];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const bool hi = lane & 16;
+        w[k] = (hi ? v[k + 4] : v[k]) + __shfl_xor_sync(0xffffffffu, hi ? v[k] : v[k + 4], 16);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const bool hi = lane & 8;
+        x[k] = (hi ? w[k + 2] : w[k]) + __shfl_xor_sync(0xffffffffu, hi ? w[k] : w[k + 2], 8);
+    }
+    const bool hi = lane & 4;
+    float y = (hi ? x[1] : x[0]) + __shfl_xor_sync(0xffffffffu, hi ? x[0] : x[1], 4);
+    y += __shfl_xor_sync(0xffffffffu, y, 2);
+    y += __shfl_xor_sync(0xffffffffu, y, 1);
+    return y;
+}
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
+__device__ __forceinline__ unsigned long long reduce8_max(const unsigned long long (&v)[8], int lane) {
+    unsigned long long w[4], x[2];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const bool hi = lane & 16;
+        w[k] = umax64(hi ? v[k + 4] : v[k], __shfl_xor_sync(0xffffffffu, hi ? v[k] : v[k + 4], 16));
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const bool hi = lane & 8;
+        x[k] = umax64(hi ? w[k + 2] : w[k], __shfl_xor_sync(0xffffffffu, hi ? w[k] : w[k + 2], 8));
+    }
+    const bool hi = lane & 4;
+    unsigned long long y = umax64(hi ? x[1] : x[0], __shfl_xor_sync(0xffffffffu, hi ? x[0] : x[1], 4));
+    y = umax64(y, __shfl_xor_sync(0xffffffffu, y, 2));
+    y = umax64(y, __shfl_xor_sync(0xffffffffu, y, 1));
+    return y;
+}
+
 // Stream-K split of an op's T units over min(C, T) CTAs (every participating CTA gets at least
 // one unit, so every CTA whose range touches a tile arrives on that tile's counter).
 __device__ __forceinline__ int op_ctas(int64_t T, int C) { return T < C ? (int)T : C; }
@@ -225,9 +283,9 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
     uint64_t *wempty = wfull + kBWSlots;
     uint64_t *xfull = wempty + kBWSlots;
     uint64_t *xempty = xfull + kBXSlots;
-    uint64_t *afull = xempty + kBXSlots;       // [half][slot]
-    uint64_t *aempty = afull + 2 * kBASlots;
-    uint64_t *accfull = aempty + 2 * kBASlots;  // [2] accumulator buffers
+    uint64_t *afull = xempty + kBXSlots;       // [slot] of the TMEM A ring
+    uint64_t *aempty = afull + kBASlots;
+    uint64_t *accfull = aempty + kBASlots;     // [2] accumulator buffers
     uint64_t *accempty = accfull + 2;
     uint64_t *mma_done = accempty + 2;
     uint64_t *tmem_free = mma_done + 1;
@@ -235,12 +293,11 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
     unsigned *epoch_s = reinterpret_cast<unsigned *>(abort_flag + 1);
     int *bcast = reinterpret_cast<int *>(epoch_s + 1);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bcast + 1);
-    float *inv_rms = reinterpret_cast<float *>(smem + 256);           // [32]
+    float *inv_rms = reinterpret_cast<float *>(smem + 384);           // [32]
     float *red = reinterpret_cast<float *>(smem + kBOffRed);          // [32 tokens][132]
     unsigned long long *wkey = reinterpret_cast<unsigned long long *>(smem + kBOffMisc);  // [warp][32]
     float *wss = reinterpret_cast<float *>(smem + kBOffMisc + kBCw * kBMaxTok * 8);        // [warp][32]
-    int *pslot = reinterpret_cast<int *>(smem + kBOffPslot);          // [parts of a shared tile]
-    const uint32_t sX = smem_u32(smem + kBOffX), sA = smem_u32(smem + kBOffA);
+    const uint32_t sX = smem_u32(smem + kBOffX);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = gridDim.x, cta = blockIdx.x;
@@ -254,8 +311,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             mbar_init(&xfull[s], 1);
             mbar_init(&xempty[s], 1);
         }
-        for (int s = 0; s < 2 * kBASlots; ++s) {
-            mbar_init(&afull[s], kBCw / 2);
+        for (int s = 0; s < kBASlots; ++s) {
+            mbar_init(&afull[s], kBCw);
             mbar_init(&aempty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -293,13 +350,13 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             for (int i = 0; i < 3; ++i) tmap_acquire(&o.wmap[i]);
             const int Cp = op_ctas(T, C);
             const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
-            for (int64_t u = u0; u < u1; ++u, ++it) {
+            int tile = (int)(u0 / U), blk = (int)(u0 % U);  // (tile, block) of unit u, stepped below
+            for (int64_t u = u0; u < u1; ++u, ++it, blk = blk + 1 == U ? 0 : blk + 1, tile += blk == 0) {
                 const int slot = it % kBWSlots;
                 if (it >= kBWSlots && !aborted() &&
                     !mbar_wait(&wempty[slot], ((uint32_t)(it / kBWSlots) & 1u) ^ 1u, a.err, kErrWaitEmpty))
                     *abort_flag = 1;
                 const bool live = !aborted();
-                const int tile = (int)(u / U), blk = (int)(u % U);
                 uint8_t *dst = smem + kBOffW + slot * kBWBytes;
                 mbar_arrive_expect_tx(&wfull[slot], live ? (uint32_t)kBWBytes : 0u);
                 if (!live) continue;
@@ -337,7 +394,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             tmap_acquire(&o.xmap);
             const int Cp = op_ctas(T, C);
             const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
-            for (int64_t u = u0; u < u1; ++u, ++it) {
+            int blk = (int)(u0 % U);
+            for (int64_t u = u0; u < u1; ++u, ++it, blk = blk + 1 == U ? 0 : blk + 1) {
                 const int slot = it % kBXSlots;
                 if (it >= kBXSlots && !aborted() &&
                     !mbar_wait(&xempty[slot], ((uint32_t)(it / kBXSlots) & 1u) ^ 1u, a.err, kErrWaitEmpty))
@@ -345,7 +403,6 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                 const bool live = !aborted();
                 mbar_arrive_expect_tx(&xfull[slot], live ? (uint32_t)kBXBytes : 0u);
                 if (live) {
-                    const int blk = (int)(u % U);
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
                         tma_load_2d(smem + kBOffX + slot * kBXBytes + c * kBXBox, &o.xmap, 256 * blk + 64 * c, 0,
@@ -367,32 +424,29 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                 const int64_t T = o.T;
                 const int Cp = op_ctas(T, C);
                 const int64_t u0 = op_start(T, Cp, cta), u1 = op_start(T, Cp, cta + 1);
-                for (int64_t u = u0; u < u1; ++u, ++uc) {
-                    const int blk = (int)(u % U);
+                int blk = (int)(u0 % U);
+                for (int64_t u = u0; u < u1; ++u, ++uc, blk = blk + 1 == U ? 0 : blk + 1) {
                     const bool first = (u == u0) || blk == 0, last = (blk == U - 1) || (u + 1 == u1);
                     const int b = tc & 1;
                     if (first && tc >= 2 && !aborted() &&
                         !mbar_wait(&accempty[b], (uint32_t)((tc >> 1) - 1) & 1u, a.err, kErrWaitEmpty))
                         *abort_flag = 1;
-                    const int xs = uc % kBXSlots;
+                    const int xs = uc % kBXSlots, as = uc % kBASlots;
                     if (!aborted() && !mbar_wait(&xfull[xs], (uint32_t)(uc / kBXSlots) & 1u, a.err, kErrWaitFull))
                         *abort_flag = 1;
-#pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
-                        const int hf = c >> 1, j = 2 * uc + (c & 1), slot = hf * kBASlots + j % kBASlots;
-                        if (!aborted() &&
-                            !mbar_wait(&afull[slot], (uint32_t)(j / kBASlots) & 1u, a.err, kErrWaitFull))
-                            *abort_flag = 1;
-                        tc_fence_after();
-                        if (!aborted()) {
+                    if (!aborted() && !mbar_wait(&afull[as], (uint32_t)(uc / kBASlots) & 1u, a.err, kErrWaitFull))
+                        *abort_flag = 1;
+                    tc_fence_after();
+                    if (!aborted()) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
 #pragma unroll
                             for (int kk = 0; kk < 4; ++kk)
-                                mma_f16(tmem + 32u * (uint32_t)b, sw128_desc(sA + slot * kBABytes + 32 * kk),
-                                        sw128_desc(sX + xs * kBXBytes + c * kBXBox + 32 * kk), kBIdesc,
-                                        (first && c == 0 && kk == 0) ? 0u : 1u);
-                        }
-                        mma_commit(&aempty[slot]);
+                                mma_f16_ta(tmem + 32u * (uint32_t)b, tmem + kBTmemA + 128u * (uint32_t)as + 32u * c + 8u * kk,
+                                           sw128_desc(sX + xs * kBXBytes + c * kBXBox + 32 * kk), kBIdesc,
+                                           (first && c == 0 && kk == 0) ? 0u : 1u);
                     }
+                    mma_commit(&aempty[as]);
                     mma_commit(&xempty[xs]);
                     if (last) {
                         mma_commit(&accfull[b]);
@@ -415,8 +469,9 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
 
     // -------------------------------- consumers --------------------------------
     const int cw = warp - 3, ctid = tid - 96;
-    const int r = ctid & (kBRows - 1), hf = ctid >> 7;  // weight row, half block (sub-blocks 4hf .. 4hf + 3)
+    // weight row = TMEM lane (a warp reaches lanes 32 (warp % 4) ..), half block (sub-blocks 4hf .. 4hf + 3)
     const int q = warp & 3, dh = cw >> 2;              // TMEM lane quadrant, token half of the drain
+    const int r = 32 * q + lane, hf = cw >> 2;
     int itw = 0, uc = 0, tc = 0;
     for (int p = 0; p < a.nops; ++p) {
         const BOp &o = a.ops[p];
@@ -461,8 +516,8 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
         wkey[cw * kBMaxTok + lane] = 0ull;
         wss[cw * kBMaxTok + lane] = 0.f;
 
-        for (int64_t u = u0; u < u1; ++u, ++itw, ++uc) {
-            const int tile = (int)(u / U), blk = (int)(u % U);
+        int tile = (int)(u0 / U), blk = (int)(u0 % U);  // (tile, block) of unit u, stepped below
+        for (int64_t u = u0; u < u1; ++u, ++itw, ++uc, blk = blk + 1 == U ? 0 : blk + 1, tile += blk == 0) {
             const int ws = itw % kBWSlots;
             if (!__all_sync(0xffffffffu, !aborted() && mbar_wait(&wfull[ws], (uint32_t)(itw / kBWSlots) & 1u,
                                                                   a.err, kErrWaitFull)))
@@ -476,10 +531,16 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                 const uint32_t scw = hf == 0 ? (hd.y & 0x3F3F3F3Fu) : ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u));
                 const uint32_t mw = hf == 0 ? (hd.z & 0x3F3F3F3Fu)
                                             : (((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u));
+                const int as = uc % kBASlots;
+                // the ring slot is free once the MMAs that read it three units ago have completed
+                if (uc >= kBASlots &&
+                    !__all_sync(0xffffffffu, !aborted() && mbar_wait(&aempty[as], (uint32_t)(uc / kBASlots - 1) & 1u,
+                                                                      a.err, kErrWaitEmpty)))
+                    *abort_flag = 1;
+                tc_fence_after();
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
                     const int pch = 2 * hf + cc;  // 64-input chunk of the block: sub-blocks 2 pch, 2 pch + 1
-                    const int j = 2 * uc + cc, slot = hf * kBASlots + j % kBASlots;
                     const int sh0 = 16 * cc, sh1 = sh0 + 8;
                     const __half2 D0 = __float2half2_rn(d * (float)((scw >> sh0) & 0xFFu));
                     const __half2 M0 = __hneg2(__float2half2_rn(dmin * (float)((mw >> sh0) & 0xFFu)));
@@ -488,35 +549,27 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                     const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + 16 + 32 * pch);
                     const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + 32 + 32 * pch);
                     const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                    uint4 lo[4], hi[4];
+                    // columns 4 jj .. 4 jj + 3: elements 8 jj .. 8 jj + 7 of sub-block 2 pch (low nibbles);
+                    // columns 16 + 4 jj ..: sub-block 2 pch + 1 (high nibbles); two f16 per column
+                    uint32_t v[32];
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj) {
                         const uint32_t w0 = W[2 * jj], w1 = W[2 * jj + 1];
-                        // sub-block 2 pch (low nibbles) and 2 pch + 1 (high nibbles), elements 8 jj .. 8 jj + 7
-                        lo[jj].x = deq2(w0 & 0x000F000Fu, D0, M0);
-                        lo[jj].y = deq2((w0 >> 8) & 0x000F000Fu, D0, M0);
-                        lo[jj].z = deq2(w1 & 0x000F000Fu, D0, M0);
-                        lo[jj].w = deq2((w1 >> 8) & 0x000F000Fu, D0, M0);
-                        hi[jj].x = deq2((w0 >> 4) & 0x000F000Fu, D1, M1);
-                        hi[jj].y = deq2((w0 >> 12) & 0x000F000Fu, D1, M1);
-                        hi[jj].z = deq2((w1 >> 4) & 0x000F000Fu, D1, M1);
-                        hi[jj].w = deq2((w1 >> 12) & 0x000F000Fu, D1, M1);
+                        v[4 * jj + 0] = deq2(w0 & 0x000F000Fu, D0, M0);
+                        v[4 * jj + 1] = deq2((w0 >> 8) & 0x000F000Fu, D0, M0);
+                        v[4 * jj + 2] = deq2(w1 & 0x000F000Fu, D0, M0);
+                        v[4 * jj + 3] = deq2((w1 >> 8) & 0x000F000Fu, D0, M0);
+                        v[16 + 4 * jj + 0] = deq2((w0 >> 4) & 0x000F000Fu, D1, M1);
+                        v[16 + 4 * jj + 1] = deq2((w0 >> 12) & 0x000F000Fu, D1, M1);
+                        v[16 + 4 * jj + 2] = deq2((w1 >> 4) & 0x000F000Fu, D1, M1);
+                        v[16 + 4 * jj + 3] = deq2((w1 >> 12) & 0x000F000Fu, D1, M1);
                     }
-                    // the slot is free once the MMAs that read it two chunks ago have completed
-                    if (j >= kBASlots &&
-                        !__all_sync(0xffffffffu, !aborted() && mbar_wait(&aempty[slot], (uint32_t)(j / kBASlots - 1) & 1u,
-                                                                          a.err, kErrWaitEmpty)))
-                        *abort_flag = 1;
-                    uint8_t *arow = smem + kBOffA + slot * kBABytes + r * 128;
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        *reinterpret_cast<uint4 *>(arow + ((jj ^ (r & 7)) << 4)) = lo[jj];
-                        *reinterpret_cast<uint4 *>(arow + (((4 + jj) ^ (r & 7)) << 4)) = hi[jj];
-                    }
-                    fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's async proxy
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&afull[slot]);
+                    tmem_st32(tmem + ((uint32_t)(32 * q) << 16) + kBTmemA + 128u * (uint32_t)as + 32u * (uint32_t)pch, v);
                 }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&afull[as]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&wempty[ws]);
@@ -570,39 +623,37 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
             // (never the abort flag, which another warp may set at any time)
             const bool partial = ts < u0 || te > u1;
             bool finish = true;
-            int nparts = 0;
             if (partial) {
-                // stream-K: park this part; the last CTA of the tile sums the parts in CTA order
-                const int si = (tile == (int)(u0 / U)) ? 0 : 1;
-                float *pp = a.part + ((size_t)cta * 2 + si) * (kBMaxTok * kBRows);
+                // stream-K: every CTA of the tile adds its part into the tile's fixed-point
+                // accumulator (64-bit integer reductions: exact, so the sum does not depend on the
+                // order of arrival); the last to arrive reads the total back and clears it
+                long long *fa = a.fixacc + (size_t)tile * (kBMaxTok * kBRows);
                 const int th = ctid >> 7;  // thread = (row r, 16 tokens)
 #pragma unroll 4
                 for (int i = 0; i < 16; ++i)
-                    __stcg(pp + (16 * th + i) * kBRows + r, red[(16 * th + i) * kBRedPitch + r]);
+                    atomicAdd(reinterpret_cast<unsigned long long *>(fa + (16 * th + i) * kBRows + r),
+                              (unsigned long long)to_fixed32(red[(16 * th + i) * kBRedPitch + r]));
                 __threadfence();
                 named_bar_sync(1, kBCw * 32);
                 const int cf = (int)(((ts + 1) * (int64_t)Cp - 1) / T), cl = (int)((te * (int64_t)Cp - 1) / T);
-                nparts = cl - cf + 1;
                 if (ctid == 0) *bcast = (int)atomicAdd(&a.counters[tile], 1u) == cl - cf;
-                // slot of each part: (CTA, first or last tile of its range)
-                for (int i = ctid; i < nparts; i += kBCw * 32) {
-                    const int c = cf + i;
-                    pslot[i] = 2 * c + ((tile == (int)(op_start(T, Cp, c) / U)) ? 0 : 1);
-                }
                 named_bar_sync(1, kBCw * 32);
                 finish = *bcast != 0;
                 if (finish) {
                     __threadfence();
+                    long long v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = __ldcg(fa + (16 * th + i) * kBRows + r);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        red[(16 * th + i) * kBRedPitch + r] = from_fixed32(v[i]);
+                        __stcg(fa + (16 * th + i) * kBRows + r, 0ll);
+                    }
                     if (ctid == 0) a.counters[tile] = 0u;
+                    named_bar_sync(1, kBCw * 32);
                 }
             }
-            auto tile_sum = [&](int tk, int row) {
-                if (!partial) return red[tk * kBRedPitch + row];
-                float sacc = 0.f;
-                for (int i = 0; i < nparts; ++i)
-                    sacc += __ldcg(a.part + (size_t)pslot[i] * (kBMaxTok * kBRows) + tk * kBRows + row);
-                return sacc;
-            };
+            auto tile_sum = [&](int tk, int row) { return red[tk * kBRedPitch + row]; };
             // the next op's f16 input: rows < k_out of this output, times its RMSNorm weight
             auto put_next = [&](int tk, int row, float v) {
                 if (row < o.k_out) {
@@ -629,49 +680,55 @@ __global__ void __launch_bounds__(kBThreads, 1) bchain_kernel(const __grid_const
                         }
                     }
                 } else {
-                    // thread = (row r, 16 tokens); warp cw holds rows 32(cw & 3) .., tokens 16(cw >> 2) ..
+                    // thread = (row r, 16 tokens); warp cw holds rows 32 (warp % 4) .., tokens 16 (cw >> 2) ..
                     const int th = ctid >> 7;
                     const int row = tile * kBRows + r;
                     const bool live = row < rows;
                     const float bias = (live && o.bias != nullptr) ? o.bias[row] : 0.f;
-#pragma unroll 2
-                    for (int i = 0; i < 16; ++i) {
-                        const int tk = 16 * th + i;
-                        float out = 0.f;
-                        unsigned long long key = 0ull;
-                        if (live && tk < M) {
-                            const float nrm = gamma != nullptr ? inv_rms[tk] : 1.f;
-                            out = tile_sum(tk, r) * nrm;
-                            float *yp = o.y != nullptr ? o.y + (size_t)tk * o.ys + row : nullptr;
-                            if (kind == kBAdd) {
-                                out += __ldcg(yp);
-                                __stcg(yp, out);
-                            } else {
-                                out += bias;
-                                if (row < o.rope_rows) {
-                                    // RoPE: rows i and i + half of a head pair up (the reference's
-                                    // rotation, kernel.cu:186-260); both lie in this tile
-                                    const int hd = o.head_dim, half = hd >> 1, pi = row % hd;
-                                    const int i2 = pi % half, rp = r + (pi < half ? half : -half);
-                                    const float xp = tile_sum(tk, rp) * nrm + o.bias_at(tile * kBRows + rp);
-                                    const float ang = (float)__ldg(o.rope_pos + tk) * __ldg(o.rope_inv + i2);
-                                    float sn, c;
-                                    sincosf(ang, &sn, &c);
-                                    out = pi < half ? out * c - xp * sn : out * c + xp * sn;
-                                }
-                                if (yp) *yp = out;
-                            }
-                            put_next(tk, row, out);
-                            if (o.amax.amax != nullptr) key = amax_key(out, (uint32_t)(row + o.amax.offset));
-                        }
-                        if (track) {  // warp-uniform: fold this tile into the warp's running slots
-                            key = warp_max_u64(key);
-                            float sq = out * out;
+#pragma unroll 1
+                    for (int i0 = 0; i0 < 16; i0 += 8) {
+                        float sqv[8];
+                        unsigned long long keyv[8];
 #pragma unroll
-                            for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-                            if (lane == i) {
+                        for (int k = 0; k < 8; ++k) {
+                            const int tk = 16 * th + i0 + k;
+                            float out = 0.f;
+                            unsigned long long key = 0ull;
+                            if (live && tk < M) {
+                                const float nrm = gamma != nullptr ? inv_rms[tk] : 1.f;
+                                out = tile_sum(tk, r) * nrm;
+                                float *yp = o.y != nullptr ? o.y + (size_t)tk * o.ys + row : nullptr;
+                                if (kind == kBAdd) {
+                                    out += __ldcg(yp);
+                                    __stcg(yp, out);
+                                } else {
+                                    out += bias;
+                                    if (row < o.rope_rows) {
+                                        // RoPE: rows i and i + half of a head pair up (the reference's
+                                        // rotation, kernel.cu:186-260); both lie in this tile
+                                        const int hd = o.head_dim, half = hd >> 1, pi = row % hd;
+                                        const int i2 = pi % half, rp = r + (pi < half ? half : -half);
+                                        const float xp = tile_sum(tk, rp) * nrm + o.bias_at(tile * kBRows + rp);
+                                        const float ang = (float)__ldg(o.rope_pos + tk) * __ldg(o.rope_inv + i2);
+                                        float sn, c;
+                                        sincosf(ang, &sn, &c);
+                                        out = pi < half ? out * c - xp * sn : out * c + xp * sn;
+                                    }
+                                    if (yp) *yp = out;
+                                }
+                                put_next(tk, row, out);
+                                if (o.amax.amax != nullptr) key = amax_key(out, (uint32_t)(row + o.amax.offset));
+                            }
+                            sqv[k] = out * out;
+                            keyv[k] = key;
+                        }
+                        if (track) {  // warp-uniform: fold these 8 tokens into the warp's running slots
+                            const float sq = reduce8_sum(sqv, lane);
+                            const unsigned long long kmax = reduce8_max(keyv, lane);
+                            if ((lane & 3) == 0) {  // lanes 4j hold token 16 th + i0 + reduce8_index(lane)
+                                const int tk = 16 * th + i0 + reduce8_index(lane);
                                 const unsigned long long kw = wkey[cw * kBMaxTok + tk];
-                                wkey[cw * kBMaxTok + tk] = key > kw ? key : kw;
+                                wkey[cw * kBMaxTok + tk] = kmax > kw ? kmax : kw;
                                 wss[cw * kBMaxTok + tk] += sq;
                             }
                         }
@@ -719,7 +776,7 @@ struct BChain {
     unsigned *done = nullptr;          // [nops] counters, [1] epoch, [nops] argmax counters, [nops] conversions
     unsigned long long *keys = nullptr;  // [nops][32]
     long long *ss = nullptr;
-    float *part = nullptr;
+    long long *fixacc = nullptr;
     __half *xh = nullptr;              // [2][32][kmax] f16 op inputs (by op parity)
     float *rope = nullptr;             // RoPE inverse-frequency tables
     BArgs args{};
@@ -744,7 +801,7 @@ void bchain_free(BChain *c) {
     if (c->done) cudaFree(c->done);
     if (c->keys) cudaFree(c->keys);
     if (c->ss) cudaFree(c->ss);
-    if (c->part) cudaFree(c->part);
+    if (c->fixacc) cudaFree(c->fixacc);
     if (c->xh) cudaFree(c->xh);
     if (c->rope) cudaFree(c->rope);
     delete c;
@@ -766,7 +823,7 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
     // rows each op writes (for the producer/consumer analysis of the RMSNorm sums)
     std::vector<int> out_w(nops, 0);
     std::vector<std::pair<int, std::vector<float>>> rope_tables;  // (op, inverse frequencies)
-    int nslots = 0, kmax = 0;
+    int nslots = 0, kmax = 0, tmax = 0;
     for (int p = 0; p < nops; ++p) {
         const ql_chain_op &q = ops[p];
         BOp &o = h[p];
@@ -846,6 +903,7 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
         }
         out_w[p] = q.y ? total : 0;
         kmax = q.in_dim > kmax ? q.in_dim : kmax;
+        tmax = o.tiles > tmax ? o.tiles : tmax;
     }
     // RMSNorm inputs produced inside the chain: the last earlier op that wrote them sums their
     // squares in its epilogue (same buffer, same row stride, covering all in_dim columns)
@@ -872,7 +930,8 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
     if (e == cudaSuccess) e = cudaMalloc(&c->done, sizeof(unsigned) * (3 * nops + 1));
     if (e == cudaSuccess) e = cudaMalloc(&c->keys, sizeof(unsigned long long) * nops * kBMaxTok);
     if (e == cudaSuccess) e = cudaMalloc(&c->ss, sizeof(long long) * 2 * (nslots > 0 ? nslots : 1) * kBMaxTok);
-    if (e == cudaSuccess) e = cudaMalloc(&c->part, sizeof(float) * (size_t)sms * 2 * kBMaxTok * kBRows);
+    if (e == cudaSuccess) e = cudaMalloc(&c->fixacc, sizeof(long long) * (size_t)tmax * kBMaxTok * kBRows);
+    if (e == cudaSuccess) e = cudaMemset(c->fixacc, 0, sizeof(long long) * (size_t)tmax * kBMaxTok * kBRows);
     if (e == cudaSuccess) e = cudaMalloc(&c->xh, sizeof(__half) * 2 * xh_elems);
     if (e == cudaSuccess && nrope) e = cudaMalloc(&c->rope, sizeof(float) * nrope);
     if (e == cudaSuccess) e = cudaMemset(c->done, 0, sizeof(unsigned) * (3 * nops + 1));
@@ -926,7 +985,7 @@ int bchain_create(const ql_chain_op *ops, int nops, int tokens, void **chain) {
     c->args.done = c->done;
     c->args.epoch = c->done + nops;
     c->args.cdone = c->done + 2 * nops + 1;
-    c->args.part = c->part;
+    c->args.fixacc = c->fixacc;
     c->args.counters = counters;
     c->args.err = err;
     c->args.ss = c->ss;
