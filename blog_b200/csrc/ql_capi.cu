@@ -382,9 +382,14 @@ int run_gemm_tc(int t, const TcJob &j, const char *what) {
     const int nsb = j.K / 256;
     const int64_t mt = (j.M + kGemmBM - 1) / kGemmBM, nt = (N + BNO - 1) / BNO, tiles = mt * nt;
     if (mt > 65535 || nt > 65535) return fail(QL_EINVAL, std::string(what) + ": shape too large for the tensor-core grid");
+    // Prefill-sized token counts run the weights-as-M kernel (weights dequantized into tensor memory
+    // once per 128 or 256 tokens); small batches and the fused argmax keep the tokens-as-M kernel.
+    const bool ta = j.M >= 128 && j.amax.amax == nullptr;
+    const int ntok = ta ? gemm_ta_tokens(j.M) : 0;
+    const int box_rows = ta ? (swiglu ? 64 : 128) : BNO;
     // K split over a cluster when the tiles alone would leave SMs idle
     int ks = 1;
-    if (tiles < ws->sms) {
+    if (!ta && tiles < ws->sms) {
         ks = (int)(ws->sms / tiles);
         if (ks > kGemmMaxSplit) ks = kGemmMaxSplit;
         if (ks > nsb) ks = nsb;
@@ -398,8 +403,8 @@ int run_gemm_tc(int t, const TcJob &j, const char *what) {
     int end = 0;
     for (int i = 0; i < 3; ++i) {
         if (i < j.nsrc) {
-            const bool okm = t == kQ4_0 ? q40_tensor_map(&a.tm_w[i], j.w[i], (uint64_t)j.rows[i], j.rb[i], BNO)
-                                        : q4k_tensor_map(&a.tm_w[i], j.w[i], nsb, (uint64_t)j.rows[i], j.rb[i], 1, BNO);
+            const bool okm = t == kQ4_0 ? q40_tensor_map(&a.tm_w[i], j.w[i], (uint64_t)j.rows[i], j.rb[i], box_rows)
+                                        : q4k_tensor_map(&a.tm_w[i], j.w[i], nsb, (uint64_t)j.rows[i], j.rb[i], 1, box_rows);
             if (!okm) return fail(QL_ECUDA, std::string(what) + ": weight tensor map");
             end += j.rows[i];
         } else {
@@ -410,7 +415,7 @@ int run_gemm_tc(int t, const TcJob &j, const char *what) {
     {
         const cuuint64_t dims[2] = {(cuuint64_t)j.K, (cuuint64_t)j.M};
         const cuuint64_t strides[1] = {(cuuint64_t)j.K * sizeof(__half)};
-        const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)kGemmBM};
+        const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)(ta ? ntok : kGemmBM)};
         const cuuint32_t estr[2] = {1, 1};
         const CUresult r = enc(&a.tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws->xh, dims, strides, box, estr,
                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -439,7 +444,7 @@ int run_gemm_tc(int t, const TcJob &j, const char *what) {
     cudaError_t e = gemm_xprep_launch(j.x, j.xs, j.gamma, j.eps, ws->xh, ws->rinv, j.M, j.K, g_stream);
     ++t_launches;
     if (e != cudaSuccess) return cuda_fail(e, what);
-    e = gemm_q4k_launch(a, j.epi, g_stream);
+    e = ta ? gemm_ta_launch(a, j.epi, ntok, g_stream) : gemm_q4k_launch(a, j.epi, g_stream);
     ++t_launches;
     if (e != cudaSuccess) return cuda_fail(e, what);
     return QL_OK;

@@ -507,6 +507,325 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
     if (ks > 1) cluster_sync_all();  // peers may still be reading this CTA's tile
 }
 
+
+// ---------------------------------------------------------------------------
+// Prefill GEMM with the weights as the MMA's M side (gemm_ta): one CTA per 128 weight rows
+// (SwiGLU: 64 gate + 64 up) x NTOK tokens.  The dequantizers write the weights straight into
+// tensor memory (tcgen05.st; the MMA reads A from TMEM), so each weight is dequantized once per
+// NTOK tokens and never passes through shared memory; the activations (xprep's f16 rows) are the
+// B operand, loaded by TMA in the canonical K-major 128-byte-swizzled layout.  Warp 0: TMA; warp 1:
+// TMEM owner and MMA issuer (M 128, N NTOK, K 16; fp32 accumulator in TMEM columns [0, NTOK));
+// warps 2-9: thread = weight row (TMEM lane) x half block, then the epilogue (TMEM -> registers ->
+// global, one token column per register).
+// ---------------------------------------------------------------------------
+constexpr int kTaThreads = 320;
+constexpr int kTaNR = 4;         // raw weight ring: 128 rows x one 256-input block column
+constexpr int kTaNX = 4;         // activation ring: NTOK tokens x 64 inputs
+constexpr int kTaNA = 2;         // dequantized blocks in TMEM (128 columns each)
+constexpr uint32_t kTaTmemA = 256;
+constexpr int kTaRBytes = 128 * 144;
+__host__ __device__ constexpr int ta_smem(int ntok) {
+    return 1024 + kTaNX * ntok * 128 + kTaNR * kTaRBytes + 2 * 64 * 33 * 4 + 256;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// Q4_K: the 64 f16 values of chunk p (sub-blocks 2p, 2p+1) of a row's block, as 32 TMEM columns
+// (column 4jj + i: elements of sub-block 2p, group jj; 16 + 4jj + i: sub-block 2p + 1).
+__device__ __forceinline__ void q4k_chunk_cols(const uint8_t *blk, const uint4 &hd, int p, uint32_t (&v)[32]) {
+    const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
+    const uint32_t scw = p < 2 ? (hd.y & 0x3F3F3F3Fu) : ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u));
+    const uint32_t mw = p < 2 ? (hd.z & 0x3F3F3F3Fu) : (((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u));
+    const int sh0 = 16 * (p & 1), sh1 = sh0 + 8;
+    const __half2 D0 = __float2half2_rn(d * (float)((scw >> sh0) & 0xFFu));
+    const __half2 M0 = __hneg2(__float2half2_rn(dmin * (float)((mw >> sh0) & 0xFFu)));
+    const __half2 D1 = __float2half2_rn(d * (float)((scw >> sh1) & 0xFFu));
+    const __half2 M1 = __hneg2(__float2half2_rn(dmin * (float)((mw >> sh1) & 0xFFu)));
+    const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
+    const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+        const uint32_t w0 = W[2 * jj], w1 = W[2 * jj + 1];
+        v[4 * jj + 0] = deq2(w0 & 0x000F000Fu, D0, M0);
+        v[4 * jj + 1] = deq2((w0 >> 8) & 0x000F000Fu, D0, M0);
+        v[4 * jj + 2] = deq2(w1 & 0x000F000Fu, D0, M0);
+        v[4 * jj + 3] = deq2((w1 >> 8) & 0x000F000Fu, D0, M0);
+        v[16 + 4 * jj + 0] = deq2((w0 >> 4) & 0x000F000Fu, D1, M1);
+        v[16 + 4 * jj + 1] = deq2((w0 >> 12) & 0x000F000Fu, D1, M1);
+        v[16 + 4 * jj + 2] = deq2((w1 >> 4) & 0x000F000Fu, D1, M1);
+        v[16 + 4 * jj + 3] = deq2((w1 >> 12) & 0x000F000Fu, D1, M1);
+    }
+}
+// Q4_0: chunk p (blocks 2p, 2p + 1 of the row's 8-block run) as 32 TMEM columns in the same
+// element order (columns 16 bb + 4 jj + i: block 2p + bb, elements 8 jj ..).
+__device__ __forceinline__ void q40_chunk_cols(const uint8_t *row, int p, uint32_t (&v)[32]) {
+#pragma unroll
+    for (int bb = 0; bb < 2; ++bb) {
+        const int b = 2 * p + bb;
+        const uint8_t *base = row + 18 * b;
+        uint32_t q[4], dbits;
+        if ((b & 1) == 0) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(base);
+            const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+            dbits = w0 & 0xFFFFu;
+            q[0] = __byte_perm(w0, w1, 0x5432);
+            q[1] = __byte_perm(w1, w2, 0x5432);
+            q[2] = __byte_perm(w2, w3, 0x5432);
+            q[3] = __byte_perm(w3, w4, 0x5432);
+        } else {
+            dbits = *reinterpret_cast<const uint16_t *>(base);
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(base + 2);
+            q[0] = w[0]; q[1] = w[1]; q[2] = w[2]; q[3] = w[3];
+        }
+        const float d = half_bits_to_float(dbits);
+        const __half2 D = __float2half2_rn(d), M = __float2half2_rn(-8.0f * d);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int sh = jj < 2 ? 0 : 4;
+            const uint32_t w0 = q[2 * (jj & 1)] >> sh, w1 = q[2 * (jj & 1) + 1] >> sh;
+            v[16 * bb + 4 * jj + 0] = deq2(w0 & 0x000F000Fu, D, M);
+            v[16 * bb + 4 * jj + 1] = deq2((w0 >> 8) & 0x000F000Fu, D, M);
+            v[16 * bb + 4 * jj + 2] = deq2(w1 & 0x000F000Fu, D, M);
+            v[16 * bb + 4 * jj + 3] = deq2((w1 >> 8) & 0x000F000Fu, D, M);
+        }
+    }
+}
+
+template <int EPI, int FMT, int NTOK>
+__global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_constant__ GemmArgs a) {
+    constexpr int RO = EPI == kGemmSwiglu ? 64 : 128;  // output columns (weight rows) per tile
+    constexpr int XB = NTOK * 128;                     // bytes of one activation chunk slot
+    constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(NTOK >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sX = smem;
+    uint8_t *sR = sX + kTaNX * XB;
+    float *sU = reinterpret_cast<float *>(sR + kTaNR * kTaRBytes);  // SwiGLU: [2 token halves][64 rows][33]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sU + 2 * 64 * 33);
+    uint64_t *rfull = bars, *rempty = rfull + kTaNR, *xfull = rempty + kTaNR, *xempty = xfull + kTaNX;
+    uint64_t *afull = xempty + kTaNX, *aempty = afull + kTaNA, *accfull = aempty + kTaNA;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accfull + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * NTOK, n0 = blockIdx.y * RO;
+    const int nsb = a.nsb;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kTaNR; ++i) { mbar_init(&rfull[i], 1); mbar_init(&rempty[i], 8); }
+        for (int i = 0; i < kTaNX; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xempty[i], 1); }
+        for (int i = 0; i < kTaNA; ++i) { mbar_init(&afull[i], 8); mbar_init(&aempty[i], 1); }
+        mbar_init(accfull, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane != 0) return;
+        int src = 0, row0 = n0;
+        if (EPI == kGemmPlain) {
+            while (src < 2 && n0 >= a.src_end[src]) ++src;
+            row0 = n0 - (src > 0 ? a.src_end[src - 1] : 0);
+        }
+        auto load_raw = [&](int b) {
+            const int rs = b % kTaNR;
+            uint8_t *dst = sR + rs * kTaRBytes;
+            mbar_arrive_expect_tx(&rfull[rs], kTaRBytes);
+            if (FMT == kQ4_0) {
+                if (EPI == kGemmSwiglu) {
+                    tma_load_2d(dst, &a.tm_w[0], b * 144, n0, &rfull[rs]);
+                    tma_load_2d(dst + 64 * 144, &a.tm_w[1], b * 144, n0, &rfull[rs]);
+                } else {
+                    tma_load_2d(dst, &a.tm_w[src], b * 144, row0, &rfull[rs]);
+                }
+            } else if (EPI == kGemmSwiglu) {
+                tma_load_3d(dst, &a.tm_w[0], 0, b, n0, &rfull[rs]);
+                tma_load_3d(dst + 64 * 144, &a.tm_w[1], 0, b, n0, &rfull[rs]);
+            } else {
+                tma_load_3d(dst, &a.tm_w[src], 0, b, row0, &rfull[rs]);
+            }
+        };
+        const int early = nsb < kTaNR ? nsb : kTaNR;
+        for (int b = 0; b < early; ++b) load_raw(b);  // weights do not depend on the previous kernel
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // activations: xprep's output
+        int issued_r = early, issued_x = 0;
+        for (int b = 0; b < nsb && !*abort_flag; ++b) {
+            if (b >= kTaNR) {
+                if (!mbar_wait(&rempty[b % kTaNR], (uint32_t)(b / kTaNR - 1) & 1u, a.err, kErrWaitEmpty)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                load_raw(b);
+                issued_r = b + 1;
+            }
+            for (int c = 0; c < 4; ++c) {
+                const int qx = 4 * b + c, xs = qx % kTaNX;
+                if (qx >= kTaNX &&
+                    !mbar_wait(&xempty[xs], (uint32_t)(qx / kTaNX - 1) & 1u, a.err, kErrWaitEmpty)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&xfull[xs], XB);
+                tma_load_2d(sX + xs * XB, &a.tm_x, 256 * b + 64 * c, m0, &xfull[xs]);
+                issued_x = qx + 1;
+            }
+        }
+        // never leave with copies in flight
+        for (int j = issued_r > kTaNR ? issued_r - kTaNR : 0; j < issued_r; ++j)
+            mbar_wait(&rfull[j % kTaNR], (uint32_t)(j / kTaNR) & 1u, nullptr, 0);
+        for (int j = issued_x > kTaNX ? issued_x - kTaNX : 0; j < issued_x; ++j)
+            mbar_wait(&xfull[j % kTaNX], (uint32_t)(j / kTaNX) & 1u, nullptr, 0);
+        return;
+    }
+    if (warp == 1) {
+        // ------------------------------- MMA issuer -------------------------------
+        if (lane == 0) {
+            for (int b = 0; b < nsb; ++b) {
+                const int as = b % kTaNA;
+                if (*abort_flag || !mbar_wait(&afull[as], (uint32_t)(b / kTaNA) & 1u, a.err, kErrWaitFull)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                bool ok = true;
+                for (int c = 0; c < 4; ++c) {
+                    const int qx = 4 * b + c, xs = qx % kTaNX;
+                    if (!mbar_wait(&xfull[xs], (uint32_t)(qx / kTaNX) & 1u, a.err, kErrWaitFull)) {
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16_ta(tmem, tmem + kTaTmemA + 128u * (uint32_t)as + 32u * (uint32_t)c + 8u * (uint32_t)kk,
+                                   sw128_desc(sX + xs * XB + 32 * kk), IDESC, (b | c | kk) != 0);
+                    mma_commit(&xempty[xs]);
+                }
+                mma_commit(&aempty[as]);
+                if (!ok) break;
+            }
+            mma_commit(accfull);
+            // every MMA has completed before TMEM may be freed
+            mbar_wait(accfull, 0u, a.err, kErrWaitFull);
+        }
+        __syncwarp();
+    } else {
+        // ------------------- dequantizers, then the epilogue -------------------
+        const int q = warp & 3, hf = (warp - 2) >> 2;
+        const int r = 32 * q + lane;  // weight row of the tile = TMEM lane
+        bool ok = true;
+        for (int b = 0; b < nsb; ++b) {
+            const int rs = b % kTaNR, as = b % kTaNA;
+            if (!__all_sync(0xffffffffu,
+                            !*abort_flag && mbar_wait(&rfull[rs], (uint32_t)(b / kTaNR) & 1u, a.err, kErrWaitFull))) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+            }
+            if (b >= kTaNA &&
+                !__all_sync(0xffffffffu, !*abort_flag && mbar_wait(&aempty[as], (uint32_t)(b / kTaNA - 1) & 1u, a.err,
+                                                                    kErrWaitEmpty))) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint8_t *rowp = sR + rs * kTaRBytes + r * 144;
+            const uint4 hd = FMT == kQ4_K ? *reinterpret_cast<const uint4 *>(rowp) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                const int pch = 2 * hf + cc;
+                uint32_t v[32];
+                if (FMT == kQ4_0) q40_chunk_cols(rowp, pch, v);
+                else q4k_chunk_cols(rowp, hd, pch, v);
+                tmem_st32(tmem + ((uint32_t)(32 * q) << 16) + kTaTmemA + 128u * (uint32_t)as + 32u * (uint32_t)pch, v);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&afull[as]);
+                mbar_arrive(&rempty[rs]);
+            }
+        }
+        ok = __all_sync(0xffffffffu, ok && !*abort_flag && mbar_wait(accfull, 0u, a.err, kErrWaitFull));
+        tc_fence_after();
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // row scales, bias and residual of earlier kernels
+        // token columns [hf * NTOK / 2, (hf + 1) * NTOK / 2) of the accumulator, 32 at a time
+        for (int cb = 0; cb < NTOK / 64; ++cb) {
+            const int col0 = hf * (NTOK / 2) + 32 * cb;
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col0, v);
+            if (EPI == kGemmSwiglu) {
+                // up rows (TMEM lanes 64..127) hand their values to the gate rows (lanes 0..63)
+                float *su = sU + hf * (64 * 33);
+                if (q >= 2)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) su[(r - 64) * 33 + i] = __uint_as_float(v[i]);
+                named_bar_sync(1, 256);
+                if (q < 2 && ok) {
+                    const int n = n0 + r;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int t = m0 + col0 + i;
+                        if (t < a.M && n < a.N) {
+                            const float sc = a.rinv[t];
+                            a.y[(size_t)t * a.y_stride + n] = silu_mul(__uint_as_float(v[i]) * sc, su[r * 33 + i] * sc);
+                        }
+                    }
+                }
+                named_bar_sync(1, 256);
+            } else if (ok) {
+                const int n = n0 + r;
+                if (n < a.N) {
+                    const float bv = a.bias != nullptr ? a.bias[n] : 0.f;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int t = m0 + col0 + i;
+                        if (t < a.M) {
+                            float *yp = a.y + (size_t)t * a.y_stride + n;
+                            float o = __uint_as_float(v[i]) * a.rinv[t] + bv;
+                            if (a.accumulate) o += *yp;
+                            *yp = o;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // warps 1..9 meet before TMEM is freed (warp 0 has returned)
+    tc_fence_before();
+    named_bar_sync(2, kTaThreads - 32);
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
 }  // namespace
 
 cudaError_t gemm_xprep_launch(const float *x, int64_t x_stride, const float *gamma, float eps, __half *xh,
@@ -555,6 +874,47 @@ cudaError_t gemm_launch_t(const GemmArgs &a, cudaStream_t s) {
     cfg.attrs = attr;
     cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, gemm_q4k_kernel<EPI, FMT>, a);
+}
+
+
+template <int EPI, int FMT, int NTOK>
+cudaError_t gemm_ta_launch_t(const GemmArgs &a, cudaStream_t s) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_ta_kernel<EPI, FMT, NTOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             ta_smem(NTOK));
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    constexpr int RO = EPI == kGemmSwiglu ? 64 : 128;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((a.M + NTOK - 1) / NTOK, (a.N + RO - 1) / RO, 1);
+    cfg.blockDim = dim3(kTaThreads);
+    cfg.dynamicSmemBytes = ta_smem(NTOK);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = gemv_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemm_ta_kernel<EPI, FMT, NTOK>, a);
+}
+
+int gemm_ta_tokens(int M) { return M >= 256 ? 256 : 128; }
+
+cudaError_t gemm_ta_launch(const GemmArgs &a, int epi, int ntok, cudaStream_t s) {
+    if (ntok == 256) {
+        if (a.fmt == kQ4_0)
+            return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ4_0, 256>(a, s)
+                                      : gemm_ta_launch_t<kGemmPlain, kQ4_0, 256>(a, s);
+        return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ4_K, 256>(a, s)
+                                  : gemm_ta_launch_t<kGemmPlain, kQ4_K, 256>(a, s);
+    }
+    if (a.fmt == kQ4_0)
+        return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ4_0, 128>(a, s)
+                                  : gemm_ta_launch_t<kGemmPlain, kQ4_0, 128>(a, s);
+    return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ4_K, 128>(a, s)
+                              : gemm_ta_launch_t<kGemmPlain, kQ4_K, 128>(a, s);
 }
 
 cudaError_t gemm_q4k_launch(const GemmArgs &a, int epi, cudaStream_t s) {

@@ -82,5 +82,10 @@ bool gemv_pdl_enabled();  // programmatic dependent launch (always on)
 cudaError_t gemm_xprep_launch(const float *x, int64_t x_stride, const float *gamma, float eps, __half *xh,
                               float *rinv, int M, int K, cudaStream_t s);
 cudaError_t gemm_q4k_launch(const GemmArgs &a, int epi, cudaStream_t s);
+// Prefill GEMM with the weights as the MMA's M side (A in tensor memory): tiles of 128 weight rows
+// (SwiGLU: 64 + 64) x ntok tokens (128 or 256); tm_w boxes of 128 (SwiGLU: 64) rows, tm_x boxes
+// {64, ntok}; no K split, no fused argmax.
+int gemm_ta_tokens(int M);
+cudaError_t gemm_ta_launch(const GemmArgs &a, int epi, int ntok, cudaStream_t s);
 
 }  // namespace ql

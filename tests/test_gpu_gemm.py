@@ -238,10 +238,13 @@ def test_tc_gemm_prefill_shape_against_torch():
     assert err < EXACT_F16_OPERANDS, err
 
 
-def test_tc_swiglu_matches_oracle():
-    """Gate/up pair in one tensor-core launch (128 gate + 128 up rows per tile), fused RMSNorm."""
+@pytest.mark.parametrize("m", [40, 300])
+def test_tc_swiglu_matches_oracle(m):
+    """Gate/up pair in one tensor-core launch, fused RMSNorm: below 128 tokens the tokens-as-M kernel
+    (128 gate + 128 up rows per tile), from 128 tokens the weights-as-M kernel (64 + 64 rows per
+    tile, A in tensor memory, a ragged last token tile at 300)."""
     import torch
-    f, k, m, eps = 640, 1024, 40, 1e-6
+    f, k, eps = 640, 1024, 1e-6
     g = make_weights(O.Q4_K, f, k, seed=101)
     u = make_weights(O.Q4_K, f, k, seed=102)
     x = _x(103, m, k)
@@ -261,7 +264,7 @@ def test_tc_swiglu_matches_oracle():
     assert rel_l2(got, g16 / (1.0 + np.exp(-g16)) * u16) < EXACT_F16_OPERANDS
 
 
-@pytest.mark.parametrize("rows,m", [((512, 256, 100), 24), ((3584, 512, 512), 64)])
+@pytest.mark.parametrize("rows,m", [((512, 256, 100), 24), ((3584, 512, 512), 64), ((3584, 512, 512), 300)])
 def test_tc_stacked_sources_match_concatenated(rows, m):
     """Stacked q/k/v sources (each but the last a multiple of 256 rows) with bias and fused norm."""
     import torch
