@@ -463,7 +463,7 @@ def run_prefill_kernel(args):
     Q.init(0)
     Q.set_stream(torch.cuda.current_stream().cuda_stream)
     n, k = {"prefill_gateup": (FFN, HIDDEN), "prefill_down": (HIDDEN, FFN), "prefill_qkv": ((N_Q + 2 * N_KV) * HEAD, HIDDEN),
-            "prefill_o": (HIDDEN, N_Q * HEAD)}[args.kernel_only]
+            "prefill_o": (HIDDEN, N_Q * HEAD), "prefill_swiglu": (FFN, HIDDEN)}[args.kernel_only]
     m = args.tokens
     rb = Q.row_bytes(QK, k)
     nbuf = 2
@@ -475,8 +475,13 @@ def run_prefill_kernel(args):
     x = torch.randn(m, k, device="cuda")
     y = torch.empty(m, n, device="cuda")
     Q.reserve_prefill(m, k)
-    run = lambda i: Q.quant_matmul_ex(QK, ws[i].data_ptr(), rb, x.data_ptr(), k, y.data_ptr(), n, n, k, m, None, 0.0,
-                                      None, False, Q.PATH_TENSOR)
+    if args.kernel_only == "prefill_swiglu":  # gate and up: both weight sets, one SwiGLU launch pair
+        gamma = torch.ones(k, device="cuda")
+        run = lambda i: Q.quant_swiglu_ex(QK, ws[0].data_ptr(), ws[1].data_ptr(), rb, rb, x.data_ptr(), k, y.data_ptr(),
+                                          n, n, k, m, gamma.data_ptr(), EPS)
+    else:
+        run = lambda i: Q.quant_matmul_ex(QK, ws[i].data_ptr(), rb, x.data_ptr(), k, y.data_ptr(), n, n, k, m, None,
+                                          0.0, None, False, Q.PATH_TENSOR)
     for i in range(args.warmup):
         run(i % nbuf)
     torch.cuda.synchronize()
@@ -488,7 +493,7 @@ def run_prefill_kernel(args):
     torch.cuda.synchronize()
     Q.check_device()
     us = e0.elapsed_time(e1) * 1000 / args.steps
-    flops = 2.0 * m * n * k
+    flops = 2.0 * m * n * k * (2 if args.kernel_only == "prefill_swiglu" else 1)
     print(json.dumps({"kernel_only": args.kernel_only, "tokens": m, "n": n, "k": k, "avg_us": us,
                       "TFLOPs": flops / us / 1e6, "launches": 2 * args.steps}), flush=True)
     return 0
@@ -926,7 +931,7 @@ def main():
     ap.add_argument("--moe", action="store_true", help="DeepSeek-V2-Lite-shape MoE decode, expert parallel")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
-                                              "prefill_qkv", "prefill_o", "chain", "bchain"],
+                                              "prefill_qkv", "prefill_o", "prefill_swiglu", "chain", "bchain"],
                     help="time one kernel of the step at its bench shape (profiling target)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers for --kernel-only chain")
@@ -1221,7 +1226,8 @@ def main():
             line["prefill"] = {"tokens": args.prefill_tokens, "value": args.prefill_tokens / (rp["ms"] / 1e3),
                                "unit": "tokens/s", "ms": rp["ms"], "tflops": tf,
                                "tensor_frac_of_sustained_bf16": tf / sus,
-                               "path": "tcgen05 f16 x f16 -> f32 GEMM, Q4_K dequantized into shared memory",
+                               "path": "tcgen05 f16 x f16 -> f32 GEMM, Q4_K weights dequantized into tensor memory "
+                                       "(MMA M side), 256-token tiles",
                                "tensor_pipe_active": "see profiles/gemm_q4k_prefill_2048x18944x3584.md"}
         if sweep is not None:
             line["sweep"] = {"config": "BASELINE configs[1]: 4 shapes x {Q8_0, Q4_0, Q4_K} x M in {1,8,64,512,2048}, "
