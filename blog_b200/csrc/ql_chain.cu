@@ -66,6 +66,8 @@ struct __align__(128) ChainOp {
     int bu;                // blocks per TMA box: min(7, U); a stage holds two boxes (one per matrix for SwiGLU)
     int reduce;            // tensor parallel: y += (sum over ranks of this rank's W.x) through peer memory
     int pre_y;             // ADD: y's last writer is at least two ops back, so y may be read early
+    const long long *res_fixed;  // ADD two ops after a fused MLP on the same y: read the residual early
+                                 // from the MLP's fixed-point copy (final when the MLP completes)
     int pair;              // one matrix, many stages per CTA: consumers take the two boxes' blocks in pairs
     long long xchg;        // first exchange cell of this op (reduce: [G][world][32]; argmax: [world][2])
     // fused MLP (kOpMlp): tmap[0..1] gate/up, tmap[2] the down projection (box {144, 1, 224});
@@ -619,7 +621,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
                 }
                 __syncwarp();
                 const float bias_v = (o.bias != nullptr && vv < o.rows) ? o.bias[vv] : 0.f;
-                const float res_v = (o.kind == kOpAdd && o.pre_y && vv < o.rows) ? __ldcg(o.y + vv) : 0.f;
+                const float res_v = (o.kind == kOpAdd && o.pre_y && vv < o.rows)
+                                        ? (o.res_fixed != nullptr ? from_fixed(__ldcg(o.res_fixed + vv)) : __ldcg(o.y + vv))
+                                        : 0.f;
                 bool ok = !*reinterpret_cast<volatile int *>(abort_flag);
                 if (ok && !mbar_wait(&red_full[bsel], (uint32_t)(gi >> 1) & 1u, a.err, kErrWaitFull)) {
                     *abort_flag = 1;
@@ -1276,6 +1280,17 @@ int chain_create(const ql_chain_op *ops, int nops, int rank, int world, void *co
             nx.mat_dst = h[p].y;
             nx.mat_rows = h[p].rows_d;
             if (nx.x == h[p].y && nx.K <= h[p].rows_d) nx.x_fixed = yf;
+        }
+        // an ADD two ops after an MLP on the same residual (o_proj after q/k/v) reads that residual from
+        // the MLP's fixed-point copy before its partial sums are ready: op p-1 only restores the fp32
+        // copy, with the same values
+        for (int p = 2; p < nops; ++p) {
+            ChainOp &o = h[p];
+            const ChainOp &m = h[p - 2], &mid = h[p - 1];
+            if (o.kind != kOpAdd || o.reduce || m.kind != kOpMlp || m.y != o.y || m.rows_d != o.rows) continue;
+            if (mid.kind == kOpMlp || overlaps(mid.y, mid.rows, o.y, o.rows)) continue;
+            o.res_fixed = m.y_fixed;
+            o.pre_y = 1;
         }
         c->args.mlp_cells = reinterpret_cast<unsigned long long *>(fixed + fixed_total);
     }
