@@ -194,13 +194,46 @@ bool q4k_tensor_map(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t 
     return true;
 }
 
-// Whether a Q4_K launch can stage through tensor maps, and the maps if so.
+// A 32-element-block matrix (Q4_0 / Q5_0 / Q8_0) as a 2-D tensor {row_bytes / 8, rows} of 8-byte
+// elements with boxes {pitch / 8, 32 rows} (the GEMV engine's TMA stage); rows must start on 16 bytes.
+bool small_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size_t row_bytes, int fmt) {
+    if (reinterpret_cast<uintptr_t>(base) % 16 || row_bytes % 16) return false;
+    const int bw = tma_pitch(fmt) / 8;
+    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), -fmt, rows, row_bytes, bw);
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+        *out = it->second;
+        return true;
+    }
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)bw, (cuuint32_t)kRowGroup};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+    if (g_maps.size() > 4096) g_maps.clear();
+    g_maps.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+// Whether a launch can stage through tensor maps (Q4_K; Q4_0 / Q5_0 / Q8_0 with rows that start on
+// 16 bytes), and the maps if so.
 // Indexed sources view the packed expert tensor as one tall matrix whose row
 // count is not known here, so a generous extent is declared; only rows of
 // valid experts are ever requested.
 bool prepare_tma(int fmt, int kind, GemvArgs &a) {
-    if (fmt != kQ4_K || a.U < kTmaSeg) return false;
+    if (!tma_format(fmt) || a.U < tma_seg(fmt)) return false;
     const int NMAT = (kind == 2 || kind == 3) ? 2 : 1;
+    auto make_map = [&](CUtensorMap *out, const uint8_t *base, int blocks, uint64_t nrows, size_t rb) {
+        return fmt == kQ4_K ? q4k_tensor_map(out, base, blocks, nrows, rb) : small_tensor_map(out, base, nrows, rb, fmt);
+    };
     uint64_t rows = (uint64_t)a.rows;
     if (kind <= 2 || kind == 5) {
         if (a.rows < kRowGroup) return false;
@@ -210,7 +243,7 @@ bool prepare_tma(int fmt, int kind, GemvArgs &a) {
             if (a.expert_bytes[m] != (size_t)a.rows_per_route * a.row_bytes[m]) return false;
         rows = 1ull << 24;
     } else {
-        if (a.rows % kRowGroup || a.units_per_route < kTmaSeg) return false;
+        if (a.rows % kRowGroup || a.units_per_route < tma_seg(fmt)) return false;
         if (a.expert_bytes[0] != (size_t)a.rows * a.row_bytes[0]) return false;
         rows = 1ull << 24;
     }
@@ -221,13 +254,12 @@ bool prepare_tma(int fmt, int kind, GemvArgs &a) {
         for (int m = 0; m < kMaxStacked; ++m) {
             if (ends[m] <= starts[m]) continue;
             if (ends[m] - starts[m] < kRowGroup) return false;
-            if (!q4k_tensor_map(&a.tmap[m], a.w[m], blocks, (uint64_t)(ends[m] - starts[m]), a.row_bytes[m]))
-                return false;
+            if (!make_map(&a.tmap[m], a.w[m], blocks, (uint64_t)(ends[m] - starts[m]), a.row_bytes[m])) return false;
         }
         return true;
     }
     for (int m = 0; m < NMAT; ++m)
-        if (!q4k_tensor_map(&a.tmap[m], a.w[m], blocks, rows, a.row_bytes[m])) return false;
+        if (!make_map(&a.tmap[m], a.w[m], blocks, rows, a.row_bytes[m])) return false;
     return true;
 }
 

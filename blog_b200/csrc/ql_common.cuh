@@ -123,6 +123,15 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int c0,
         : "memory");
 }
 
+// 2-D tiled tensor copy global -> shared (TMA), completion counted on `bar` in bytes.
+__device__ __forceinline__ void tma_box2d(void *dst, const void *tmap, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // tma_load_3d with an L2 eviction-priority policy (e.g. evict-first for streamed weights, so
 // that they do not push the kernel's code, descriptors and activations out of L2).
 __device__ __forceinline__ void tma_load_3d_hint(void *dst, const void *tmap, int c0, int c1, int c2, uint64_t *bar,

@@ -63,13 +63,24 @@ __host__ __device__ constexpr int gemv_pitch(int t) {
     return ((gemv_seg(t) * block_bytes(t) + 32 + 127) / 128) * 128 + 16;
 }
 
-// Tensor-map (TMA) staging, used for Q4_K: one 3-D box {144 B, 7 blocks, 32 rows}
-// per matrix per stage.  The box lands as [32 rows][7 blocks][144 B], a row
-// pitch of 1008 B (= 112 mod 128), so lanes reading consecutive rows at the
-// same offset fall in distinct 16-byte bank groups.
+// Tensor-map (TMA) staging.  Q4_K: one 3-D box {144 B, 7 blocks, 32 rows} per matrix per
+// stage, landing as [32 rows][7 blocks][144 B], a row pitch of 1008 B (= 112 mod 128), so lanes
+// reading consecutive rows at the same offset fall in distinct 16-byte bank groups.  The
+// 32-element formats (rows a multiple of 16 bytes long): a 2-D view {row_bytes / 8, rows} of
+// 8-byte elements, one box {pitch / 8, 32 rows} per stage starting at the 16-byte boundary at or
+// before the stage's first block (blocks are 18/22/34 bytes, so a stage may start mid-chunk);
+// the pitch covers the stage's blocks plus that 0..15-byte lead and is 16 mod 128.
 constexpr int kTmaSeg = 7;
-__host__ __device__ constexpr int stage_seg(int t, bool tma) { return tma ? kTmaSeg : gemv_seg(t); }
-__host__ __device__ constexpr int stage_pitch(int t, bool tma) { return tma ? kTmaSeg * 144 : gemv_pitch(t); }
+__host__ __device__ constexpr int tma_seg(int t) {
+    return t == kQ4_K ? kTmaSeg : t == kQ4_0 ? 56 : t == kQ8_0 ? 32 : t == kQ5_0 ? 48 : 0;
+}
+__host__ __device__ constexpr int tma_pitch(int t) {
+    return t == kQ4_K ? kTmaSeg * 144 : ((tma_seg(t) * block_bytes(t) + 15 - 16 + 127) / 128) * 128 + 16;
+}
+__host__ __device__ constexpr bool tma_format(int t) { return tma_seg(t) > 0; }
+__host__ __device__ constexpr int stage_seg(int t, bool tma) { return tma ? tma_seg(t) : gemv_seg(t); }
+__host__ __device__ constexpr int stage_pitch(int t, bool tma) { return tma ? tma_pitch(t) : gemv_pitch(t); }
+static_assert(tma_pitch(kQ4_0) == 1040 && tma_pitch(kQ8_0) == 1168 && tma_pitch(kQ5_0) == 1168, "TMA pitches");
 
 // Shared-memory header of the GEMV kernel: mbarriers, abort flag, RMSNorm
 // factors [4] and per-warp partial sums of squares [14][4].
@@ -97,7 +108,8 @@ struct GemvArgs {
     int64_t y_stride;
     int nst;                  // stages in the shared-memory ring (2..kGemvStages)
     int pre_x;                // stages the producer may issue before the activations are staged
-    CUtensorMap tmap[kMaxStacked];   // Q4_K tensor maps {144 B, blocks, rows} (TMA kernels only)
+    CUtensorMap tmap[kMaxStacked];   // tensor maps (TMA kernels only): Q4_K {144 B, blocks, rows},
+                                     // 32-element formats {row_bytes / 8, rows} of 8-byte elements
     Plan plan;
     float *part;              // stream-K partial slots [C][2][MT][NMAT][32]
     unsigned *counters;       // stream-K arrival counters [G], zero between launches

@@ -381,13 +381,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
 
     if (TMA && warp < NPW) {
         // ---------------------------- producer (TMA) ----------------------------
-        // One thread issues one 3-D box per matrix per stage.
+        // One thread issues one box per matrix per stage (Q4_K: 3-D; 32-element formats: 2-D from the
+        // 16-byte boundary at or before the stage's first block).
         if (lane != 0) return;
         if (SRC != kSrcPlain) asm volatile("griddepcontrol.wait;" ::: "memory");  // expert ids
         int64_t t = t0;
         Stage st;
         int it = 0;
-        constexpr uint32_t BOX = kRowGroup * SEG * 144;
+        constexpr uint32_t BOX = kRowGroup * PITCH;
         while (next_stage(t, t1, U, SEG, upr, st)) {
             const int slot = it % NST;
             const uint32_t ph = (uint32_t)(it / NST) & 1u;
@@ -417,9 +418,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
             if (live) {
                 uint8_t *sbase = stages + slot * STAGE_BYTES;
 #pragma unroll
-                for (int mat = 0; mat < NMAT; ++mat)
-                    tma_load_3d(sbase + mat * BOX, &a.tmap[SRC == kSrcStacked ? map : mat], 0, blk0, row0,
-                                &full[slot]);
+                for (int mat = 0; mat < NMAT; ++mat) {
+                    if (FMT == kQ4_K)
+                        tma_load_3d(sbase + mat * BOX, &a.tmap[SRC == kSrcStacked ? map : mat], 0, blk0, row0,
+                                    &full[slot]);
+                    else  // x in 8-byte elements: the 16-byte chunk holding the stage's first byte
+                        tma_box2d(sbase + mat * BOX, &a.tmap[SRC == kSrcStacked ? map : mat], ((blk0 * BB) >> 4) << 1,
+                                  row0, &full[slot]);
+                }
             }
             ++it;
         }
@@ -779,7 +785,7 @@ static cudaError_t launch_typed(const GemvArgs &a, int smem, cudaStream_t stream
 
 template <int FMT, int MT, int NMAT, int SRC, int EPI>
 static cudaError_t launch_tma(const GemvArgs &a, bool tma, int smem, cudaStream_t s) {
-    if (FMT == kQ4_K && tma) return launch_typed<FMT, MT, NMAT, SRC, EPI, true>(a, smem, s);
+    if (tma_format(FMT) && tma) return launch_typed<FMT, MT, NMAT, SRC, EPI, true>(a, smem, s);
     return launch_typed<FMT, MT, NMAT, SRC, EPI, false>(a, smem, s);
 }
 
@@ -795,7 +801,7 @@ static cudaError_t launch_mt(const GemvArgs &a, int MT, bool tma, int smem, cuda
 
 // kind: 0 plain store, 1 plain add, 2 plain SwiGLU pair, 3 indexed-rows SwiGLU
 // pair (MT = 1), 4 indexed-K add (MT = 1), 5 stacked sources store.  `tma` selects tensor-map staging
-// (Q4_K only; the caller has filled a.tmap).
+// (Q4_K, Q4_0, Q5_0, Q8_0; the caller has filled a.tmap).
 template <int FMT>
 cudaError_t gemv_launch_fmt(int kind, const GemvArgs &a, int MT, bool tma, int smem, cudaStream_t s) {
     switch (kind) {

@@ -62,6 +62,10 @@ SHAPES = [
     (O.Q8_0, 896, 896, 1), (O.Q8_0, 4864, 896, 1), (O.Q8_0, 37, 4864, 2), (O.Q8_0, 2, 32, 3), (O.Q8_0, 4096, 4096, 4),
     (O.Q4_0, 4096, 4096, 1), (O.Q4_0, 1024, 29568, 1), (O.Q4_0, 33, 8192, 2), (O.Q4_0, 11008, 4096, 1),
     (O.Q5_0, 2048, 1408, 1), (O.Q5_0, 64, 10944, 2), (O.Q5_0, 70, 96, 1),
+    # rows a multiple of 16 bytes: tensor-map staging of the 32-element formats (stages that start
+    # mid 16-byte chunk, ragged last row group, 72B-shape q projection)
+    (O.Q5_0, 256, 4096, 1), (O.Q5_0, 100, 2048, 3), (O.Q8_0, 4096, 4096, 1), (O.Q4_0, 8192, 8192, 1),
+    (O.Q4_0, 4640, 4096, 2),
     (O.Q6_K, 64, 2048, 1), (O.Q6_K, 300, 512, 2),
 ]
 
@@ -120,7 +124,7 @@ def test_gemv_add(t, n, k):
 
 
 @pytest.mark.parametrize("t,f,k,m", [(O.Q4_K, 2816, 2048, 1), (O.Q4_K, 18944, 3584, 1), (O.Q8_0, 4864, 896, 2),
-                                     (O.Q4_0, 1000, 1024, 3)])
+                                     (O.Q4_0, 1000, 1024, 3), (O.Q4_0, 2048, 4096, 1), (O.Q8_0, 1024, 4096, 2)])
 def test_swiglu(t, f, k, m):
     import torch
     g = make_weights(t, f, k, seed=21)
@@ -157,7 +161,8 @@ def test_gemv_ex_fused_rmsnorm_bias_accumulate():
 
 
 @pytest.mark.parametrize("t,rows,k", [(O.Q4_K, (3584, 512, 512), 3584), (O.Q8_0, (896, 128, 128), 896),
-                                      (O.Q4_K, (64, 50), 2048), (O.Q5_0, (32, 32, 7), 1408)])
+                                      (O.Q4_K, (64, 50), 2048), (O.Q5_0, (32, 32, 7), 1408),
+                                      (O.Q4_0, (1024, 128, 128), 4096)])
 def test_stacked_qkv_matches_separate(t, rows, k):
     """Fused q/k/v (stacked sources) with RMSNorm and bias equals the separate projections."""
     import torch
