@@ -196,10 +196,12 @@ bool q4k_tensor_map(CUtensorMap *out, const uint8_t *base, int blocks, uint64_t 
 
 // A 32-element-block matrix (Q4_0 / Q5_0 / Q8_0) as a 2-D tensor {row_bytes / 8, rows} of 8-byte
 // elements with boxes {pitch / 8, 32 rows} (the GEMV engine's TMA stage); rows must start on 16 bytes.
-bool small_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size_t row_bytes, int fmt) {
-    if (reinterpret_cast<uintptr_t>(base) % 16 || row_bytes % 16) return false;
+// pair: rows a multiple of 8 bytes long, an even row count: each pair of rows is one 16-byte-aligned
+// super-row {2 row_bytes / 8, rows / 2} read in boxes of 16 super-rows.
+bool small_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size_t row_bytes, int fmt, bool pair) {
+    if (reinterpret_cast<uintptr_t>(base) % 16 || row_bytes % (pair ? 8 : 16) || (pair && rows % 2)) return false;
     const int bw = tma_pitch(fmt) / 8;
-    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), -fmt, rows, row_bytes, bw);
+    const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), -fmt, rows, row_bytes, bw + (pair ? 1 << 20 : 0));
     std::lock_guard<std::mutex> lk(g_map_mu);
     auto it = g_maps.find(key);
     if (it != g_maps.end()) {
@@ -209,9 +211,10 @@ bool small_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size
     auto enc = tensor_map_encoder();
     if (enc == nullptr) return false;
     CUtensorMap m;
-    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)bw, (cuuint32_t)kRowGroup};
+    const uint64_t f = pair ? 2 : 1;
+    const cuuint64_t dims[2] = {(cuuint64_t)(f * row_bytes / 8), rows / f};
+    const cuuint64_t strides[1] = {(cuuint64_t)(f * row_bytes)};
+    const cuuint32_t box[2] = {(cuuint32_t)bw, (cuuint32_t)(kRowGroup / f)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t *>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -229,10 +232,19 @@ bool small_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size
 // count is not known here, so a generous extent is declared; only rows of
 // valid experts are ever requested.
 bool prepare_tma(int fmt, int kind, GemvArgs &a) {
-    if (!tma_format(fmt) || a.U < tma_seg(fmt)) return false;
+    if (!tma_format(fmt)) return false;
     const int NMAT = (kind == 2 || kind == 3) ? 2 : 1;
+    // 32-element formats: rows that all start on 16 bytes, or all on 8 bytes (row pairs)
+    bool all16 = true;
+    for (int m = 0; m < (kind == 5 ? kMaxStacked : NMAT); ++m)
+        if (a.w[m] != nullptr && a.row_bytes[m] % 16) all16 = false;
+    a.tma_pair = (fmt != kQ4_K && !all16) ? 1 : 0;
+    // a stage box no wider than the (super-)row: rows shorter than one stage only as row pairs
+    if (a.U < tma_seg(fmt) && !(a.tma_pair && 2 * (size_t)a.U * block_bytes(fmt) >= (size_t)tma_pitch(fmt)))
+        return false;
     auto make_map = [&](CUtensorMap *out, const uint8_t *base, int blocks, uint64_t nrows, size_t rb) {
-        return fmt == kQ4_K ? q4k_tensor_map(out, base, blocks, nrows, rb) : small_tensor_map(out, base, nrows, rb, fmt);
+        return fmt == kQ4_K ? q4k_tensor_map(out, base, blocks, nrows, rb)
+                            : small_tensor_map(out, base, nrows, rb, fmt, a.tma_pair != 0);
     };
     uint64_t rows = (uint64_t)a.rows;
     if (kind <= 2 || kind == 5) {
@@ -295,6 +307,7 @@ int run_gemv(int fmt, int kind, GemvArgs base, int M, const char *what) {
     if (G == 0 || M == 0) return QL_OK;
     const int64_t T = (int64_t)G * base.U;
     const bool tma = prepare_tma(fmt, kind, base);
+    if (!tma) base.tma_pair = 0;
     int done = 0;
     while (done < M) {
         // most tokens per launch (<= 4), then most stages (<= 4, >= 2), that fit 227 KB

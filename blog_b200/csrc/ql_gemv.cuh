@@ -108,6 +108,9 @@ struct GemvArgs {
     int64_t y_stride;
     int nst;                  // stages in the shared-memory ring (2..kGemvStages)
     int pre_x;                // stages the producer may issue before the activations are staged
+    int tma_pair;             // 32-element formats with rows a multiple of 8 (not 16) bytes long: the tensor
+                              // maps view row pairs as 16-byte-aligned super-rows; a stage is two 16-row boxes
+                              // (even rows, then odd rows of the group)
     CUtensorMap tmap[kMaxStacked];   // tensor maps (TMA kernels only): Q4_K {144 B, blocks, rows},
                                      // 32-element formats {row_bytes / 8, rows} of 8-byte elements
     Plan plan;

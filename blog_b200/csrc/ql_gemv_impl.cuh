@@ -422,9 +422,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
                     if (FMT == kQ4_K)
                         tma_load_3d(sbase + mat * BOX, &a.tmap[SRC == kSrcStacked ? map : mat], 0, blk0, row0,
                                     &full[slot]);
-                    else  // x in 8-byte elements: the 16-byte chunk holding the stage's first byte
+                    else if (!a.tma_pair)  // x in 8-byte elements: the 16-byte chunk holding the stage's first byte
                         tma_box2d(sbase + mat * BOX, &a.tmap[SRC == kSrcStacked ? map : mat], ((blk0 * BB) >> 4) << 1,
                                   row0, &full[slot]);
+                    else {  // super-rows of two rows: even rows from the stage's offset, odd rows one row later
+                        const int src = SRC == kSrcStacked ? map : mat;
+                        const int rb = (int)a.row_bytes[src];
+                        tma_box2d(sbase + mat * BOX, &a.tmap[src], ((blk0 * BB) >> 4) << 1, row0 >> 1, &full[slot]);
+                        tma_box2d(sbase + mat * BOX + (BOX >> 1), &a.tmap[src], ((rb + blk0 * BB) >> 4) << 1, row0 >> 1,
+                                  &full[slot]);
+                    }
                 }
             }
             ++it;
@@ -716,7 +723,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(const __grid_con
             for (int mat = 0; mat < NMAT; ++mat) {
                 const uint8_t *rs = gemv_block_ptr<SRC, FMT>(a, a.ids, mat, v, st.us);
                 live = live && (rs != nullptr);
-                rowp[mat] = stages + slot * STAGE_BYTES + (mat * kRowGroup + lane) * PITCH +
+                // row slot of this lane: paired tensor-map stages hold the even rows, then the odd rows
+                const int rsl = (TMA && FMT != kQ4_K && a.tma_pair) ? ((lane & 1) << 4) | (lane >> 1) : lane;
+                rowp[mat] = stages + slot * STAGE_BYTES + (mat * kRowGroup + rsl) * PITCH +
                             (reinterpret_cast<uintptr_t>(rs) & 15);
             }
             if (live) {

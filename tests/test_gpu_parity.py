@@ -66,6 +66,9 @@ SHAPES = [
     # mid 16-byte chunk, ragged last row group, 72B-shape q projection)
     (O.Q5_0, 256, 4096, 1), (O.Q5_0, 100, 2048, 3), (O.Q8_0, 4096, 4096, 1), (O.Q4_0, 8192, 8192, 1),
     (O.Q4_0, 4640, 4096, 2),
+    # rows a multiple of 8 (not 16) bytes: row pairs staged as one super-row (72B down projection,
+    # 0.5B's K = 896 projections and LM head rows)
+    (O.Q4_0, 8192, 29568, 1), (O.Q8_0, 4864, 896, 3), (O.Q8_0, 151936, 896, 1), (O.Q8_0, 64, 1792, 2),
     (O.Q6_K, 64, 2048, 1), (O.Q6_K, 300, 512, 2),
 ]
 
