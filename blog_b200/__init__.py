@@ -53,6 +53,8 @@ SIGNATURES = {
     "ql_quant_swiglu_indexed": (I, [I32, P, P, SZ, SZ, SZ, SZ, P, P, P, I, I, I]),
     "ql_quant_down_f32_indexed_accum_ordered": (I, [I32, P, SZ, SZ, P, P, P, P, I, I, I]),
     "ql_moe_router_topk": (I, [P, P, P, I, I, I, F]),
+    "ql_moe_swiglu_grouped": (I, [I32, P, P, SZ, SZ, SZ, SZ, P, I64, P, I, I, P, I, I, I, I]),
+    "ql_moe_down_grouped_accum_ordered": (I, [I32, P, SZ, SZ, P, P, I, I, P, P, I64, I, I, I, I]),
     "ql_quant_embedding": (I, [I32, P, P, P, SZ, I, I]),
     "ql_dequantize_to_f16": (I, [I32, P, P, I64]),
     "ql_dequantize_q4k_to_f16": (I, [P, P, I64]),
@@ -303,6 +305,18 @@ def quant_down_f32_indexed_accum_ordered(t, dw, deb, drb, act, ids, rw, out, k, 
 
 def moe_router_topk(logits, idx, w, tokens, n_experts, k, scale):
     _call("ql_moe_router_topk", logits, idx, w, tokens, n_experts, k, scale)
+
+
+def moe_swiglu_grouped(t, gw, uw, geb, ueb, grb, urb, x, x_stride, ids, expert_begin, n_experts, act, tokens, k,
+                       ffn_dim, in_dim):
+    _call("ql_moe_swiglu_grouped", t, gw, uw, geb, ueb, grb, urb, x, x_stride, ids, expert_begin, n_experts, act,
+          tokens, k, ffn_dim, in_dim)
+
+
+def moe_down_grouped_accum_ordered(t, dw, deb, drb, act, ids, expert_begin, n_experts, rw, out, out_stride, tokens,
+                                   k, hidden, ffn_dim):
+    _call("ql_moe_down_grouped_accum_ordered", t, dw, deb, drb, act, ids, expert_begin, n_experts, rw, out,
+          out_stride, tokens, k, hidden, ffn_dim)
 
 
 def quant_embedding(t, ids, out, table, rb, hidden, n):

@@ -19,6 +19,7 @@
 #include "ql_common.cuh"
 #include "ql_gemm.cuh"
 #include "ql_gemv.cuh"
+#include "ql_moe.cuh"
 
 namespace ql {
 cudaError_t gemv_launch(int fmt, int kind, const GemvArgs &a, int MT, bool tma, int smem, cudaStream_t s);
@@ -59,6 +60,13 @@ struct Workspace {
     size_t xh_cap = 0;
     float *rinv = nullptr;
     size_t rinv_cap = 0;
+    // grouped routed experts: per-(token, route) down rows and local expert ids, grown on demand
+    float *moe_y = nullptr;
+    size_t moe_y_cap = 0;
+    int *moe_ids = nullptr;
+    size_t moe_ids_cap = 0;
+    float *moe_bsum = nullptr;
+    size_t moe_bsum_cap = 0;
 };
 
 std::mutex g_mu;
@@ -367,9 +375,10 @@ int ensure_prefill(Workspace *ws, size_t tokens, size_t k) {
     return QL_OK;
 }
 
-// Fewest tokens routed to the tensor-core GEMM by the automatic path selection;
-// below it the streaming GEMV engine (<= 4 tokens per weight pass) is faster.
-int tc_min_tokens() { return 8; }
+// Fewest tokens routed to the tensor-core GEMM by the automatic path selection; below it the
+// streaming GEMV engine (<= 4 tokens per weight pass) is faster.  Q8_0 runs only the weights-as-M
+// kernel (tiles of 128 tokens, no split-K), which pays off from 32 tokens.
+int tc_min_tokens(int t) { return t == kQ8_0 ? 32 : 8; }
 
 // One tensor-core GEMM launch pair: plain (1..3 stacked sources) or SwiGLU (gate, up).
 struct TcJob {
@@ -390,10 +399,12 @@ struct TcJob {
     AmaxOut amax{};  // fused argmax (plain only; amax.amax non-null = on, filled by run_gemm_tc)
 };
 
-// Whether the tensor-core GEMM can run the job: Q4_K or Q4_0, K % 256, row strides that are
-// TMA-legal, and (stacked) sources that end on 256-row tile boundaries.
+// Whether the tensor-core GEMM can run the job: Q4_K, Q4_0 or Q8_0 (not with the fused argmax,
+// which only the tokens-as-M kernel has), K % 256, row strides that are TMA-legal, and (stacked)
+// sources that end on 256-row tile boundaries.
 bool tc_eligible(int t, const TcJob &j) {
-    if ((t != kQ4_K && t != kQ4_0) || j.K % 256 != 0) return false;
+    if ((t != kQ4_K && t != kQ4_0 && t != kQ8_0) || j.K % 256 != 0) return false;
+    if (t == kQ8_0 && j.amax.amax != nullptr) return false;
     for (int i = 0; i < j.nsrc; ++i) {
         if (j.rb[i] % 16 != 0) return false;
         if (j.epi == kGemmPlain && i < j.nsrc - 1 && j.rows[i] % kGemmBN != 0) return false;
@@ -415,6 +426,20 @@ bool q40_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size_t
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A Q8_0 matrix as a 2-D tensor of 2-byte elements {row_bytes / 2, rows} with boxes of 136
+// elements (272 B = 8 blocks = 256 inputs) x box_rows rows (row_bytes = 272 * in_dim / 256).
+bool q80_tensor_map(CUtensorMap *out, const uint8_t *base, uint64_t rows, size_t row_bytes, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 2), rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {136, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int run_gemm_tc(int t, const TcJob &j, const char *what) {
     int st;
     Workspace *ws = workspace(&st);
@@ -429,8 +454,8 @@ int run_gemm_tc(int t, const TcJob &j, const char *what) {
     if (mt > 65535 || nt > 65535) return fail(QL_EINVAL, std::string(what) + ": shape too large for the tensor-core grid");
     // Prefill-sized token counts run the weights-as-M kernel (weights dequantized into tensor memory
     // once per 128 or 256 tokens); small batches and the fused argmax keep the tokens-as-M kernel.
-    const bool ta = j.M >= 128 && j.amax.amax == nullptr;
-    const int ntok = ta ? gemm_ta_tokens(j.M) : 0;
+    const bool ta = (j.M >= 128 || t == kQ8_0) && j.amax.amax == nullptr;
+    const int ntok = ta ? gemm_ta_tokens(j.M, (N + (swiglu ? 63 : 127)) / (swiglu ? 64 : 128), ws->sms) : 0;
     const int box_rows = ta ? (swiglu ? 64 : 128) : BNO;
     // K split over a cluster when the tiles alone would leave SMs idle
     int ks = 1;
@@ -448,8 +473,10 @@ int run_gemm_tc(int t, const TcJob &j, const char *what) {
     int end = 0;
     for (int i = 0; i < 3; ++i) {
         if (i < j.nsrc) {
-            const bool okm = t == kQ4_0 ? q40_tensor_map(&a.tm_w[i], j.w[i], (uint64_t)j.rows[i], j.rb[i], box_rows)
-                                        : q4k_tensor_map(&a.tm_w[i], j.w[i], nsb, (uint64_t)j.rows[i], j.rb[i], 1, box_rows);
+            const bool okm =
+                t == kQ8_0   ? q80_tensor_map(&a.tm_w[i], j.w[i], (uint64_t)j.rows[i], j.rb[i], box_rows)
+                : t == kQ4_0 ? q40_tensor_map(&a.tm_w[i], j.w[i], (uint64_t)j.rows[i], j.rb[i], box_rows)
+                             : q4k_tensor_map(&a.tm_w[i], j.w[i], nsb, (uint64_t)j.rows[i], j.rb[i], 1, box_rows);
             if (!okm) return fail(QL_ECUDA, std::string(what) + ": weight tensor map");
             end += j.rows[i];
         } else {
@@ -605,7 +632,7 @@ int ql_quant_gemv_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, int
     if ((st = check_act(x, xs, gamma, "ql_quant_gemv"))) return st;
     {
         const TcJob j = plain_job(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate);
-        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_gemv");
+        if (m >= tc_min_tokens(t) && tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_gemv");
     }
     GemvArgs a = blank();
     a.w[0] = w;
@@ -644,7 +671,7 @@ int ql_quant_gemv_argmax_ex(int32_t t, const uint8_t *w, size_t rb, const float 
     {
         TcJob j = plain_job(w, rb, x, xs, logits, ls, out_dim, in_dim, m, gamma, eps, nullptr, 0);
         j.amax = am;
-        if (m >= tc_min_tokens() && tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_gemv_argmax_ex");
+        if (m >= tc_min_tokens(t) && tc_eligible(t, j)) return run_gemm_tc(t, j, "ql_quant_gemv_argmax_ex");
     }
     GemvArgs a = blank();
     a.w[0] = w;
@@ -675,9 +702,9 @@ int ql_quant_matmul_ex(int32_t t, const uint8_t *w, size_t rb, const float *x, i
     const TcJob j = plain_job(w, rb, x, xs, y, ys, out_dim, in_dim, m, gamma, eps, bias, accumulate);
     const bool tc = tc_eligible(t, j);
     if (path == QL_PATH_TENSOR && !tc)
-        return fail(QL_EINVAL, "ql_quant_matmul_ex: the tensor-core path needs Q4_K or Q4_0, in_dim % 256 == 0 "
+        return fail(QL_EINVAL, "ql_quant_matmul_ex: the tensor-core path needs Q4_K, Q4_0 or Q8_0, in_dim % 256 == 0 "
                                "and row_bytes % 16 == 0");
-    if (path == QL_PATH_TENSOR || (path == QL_PATH_AUTO && tc && m >= tc_min_tokens()))
+    if (path == QL_PATH_TENSOR || (path == QL_PATH_AUTO && tc && m >= tc_min_tokens(t)))
         return run_gemm_tc(t, j, "ql_quant_matmul_ex");
     GemvArgs a = blank();
     a.w[0] = w;
@@ -730,7 +757,7 @@ int ql_quant_gemv_stacked_ex(int32_t t, int nsrc, const uint8_t *const *w, const
     if (!x || !y) return fail(QL_EINVAL, "ql_quant_gemv_stacked_ex: null x or y");
     int st = check_act(x, xs, gamma, "ql_quant_gemv_stacked_ex");
     if (st) return st;
-    if (m >= tc_min_tokens()) {
+    if (m >= tc_min_tokens(t)) {
         TcJob j = plain_job(w[0], rb[0], x, xs, y, ys, rows[0], in_dim, m, gamma, eps, bias, 0);
         j.nsrc = nsrc;
         for (int i = 1; i < nsrc; ++i) {
@@ -777,7 +804,7 @@ int ql_quant_swiglu_ex(int32_t t, const uint8_t *g, const uint8_t *u, size_t grb
     if ((st = check_weight(t, u, urb, 0, in_dim, "ql_quant_swiglu(up)"))) return st;
     if (!x || !act) return fail(QL_EINVAL, "ql_quant_swiglu: null x or act");
     if ((st = check_act(x, xs, gamma, "ql_quant_swiglu"))) return st;
-    if (m >= tc_min_tokens()) {
+    if (m >= tc_min_tokens(t)) {
         TcJob j = plain_job(g, grb, x, xs, act, as, ffn_dim, in_dim, m, gamma, eps, nullptr, 0);
         j.epi = kGemmSwiglu;
         j.nsrc = 2;
@@ -873,6 +900,185 @@ int ql_moe_router_topk(const float *logits, int *idx, float *w, int tokens, int 
     cudaError_t e = router_launch(logits, idx, w, tokens, E, k, scale, g_stream);
     ++t_launches;
     return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_moe_router_topk");
+}
+
+// ---- grouped routed experts ------------------------------------------------------
+namespace {
+// Grows a scratch buffer to hold n elements of elem bytes.
+int grow(void **buf, size_t *cap, size_t n, size_t elem, const char *what) {
+    if (n <= *cap) return QL_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(buf, n * elem);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    *cap = n;
+    return QL_OK;
+}
+// Whether the grouped kernel can stage a matrix: 16 rows in a warp's slab, and a 16-byte-aligned
+// base (the bulk copy starts at the 16-byte boundary at or before a row range).
+bool moe_stageable(const uint8_t *w, size_t rb) {
+    return reinterpret_cast<uintptr_t>(w) % 16 == 0 && moe_slab_bytes(rb) <= moe_max_slab_bytes();
+}
+int moe_check(int t, int tokens, int k, int e_begin, int n_experts, const char *what) {
+    if (tokens < 0 || k <= 0 || n_experts <= 0 || e_begin < 0)
+        return fail(QL_EINVAL, std::string(what) + ": need tokens >= 0, k > 0, n_experts > 0, expert_begin >= 0");
+    if (t != kQ4_0 && t != kQ5_0 && t != kQ8_0 && t != kQ4_K)
+        return fail(QL_EINVAL, std::string(what) + ": quant_type must be Q4_0, Q5_0, Q8_0 or Q4_K");
+    if ((int64_t)tokens * k > (1 << 30)) return fail(QL_EINVAL, std::string(what) + ": too many routes");
+    return QL_OK;
+}
+}  // namespace
+
+int ql_moe_swiglu_grouped(int32_t t, const uint8_t *g, const uint8_t *u, size_t geb, size_t ueb, size_t grb,
+                          size_t urb, const float *x, int64_t xs, const int *ids, int e_begin, int n_experts,
+                          float *act, int tokens, int k, int ffn_dim, int in_dim) {
+    const char *what = "ql_moe_swiglu_grouped";
+    t_launches = 0;
+    int st = moe_check(t, tokens, k, e_begin, n_experts, what);
+    if (st) return st;
+    if (ffn_dim < 0) return fail(QL_EINVAL, std::string(what) + ": negative ffn_dim");
+    if (tokens == 0 || ffn_dim == 0) return QL_OK;
+    if ((st = check_weight(t, g, grb, geb, in_dim, "ql_moe_swiglu_grouped(gate)"))) return st;
+    if ((st = check_weight(t, u, urb, ueb, in_dim, "ql_moe_swiglu_grouped(up)"))) return st;
+    if (!x || !ids || !act) return fail(QL_EINVAL, std::string(what) + ": null pointer");
+    if ((st = check_act(x, xs, nullptr, what))) return st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    const int npairs = tokens * k;
+    if (!moe_stageable(g, grb) || !moe_stageable(u, urb)) {
+        // rows too long for the grouped kernel's slabs: the per-token indexed launches
+        if ((st = grow(reinterpret_cast<void **>(&ws->moe_ids), &ws->moe_ids_cap, (size_t)npairs, sizeof(int), what))) return st;
+        cudaError_t e = moe_local_ids_launch(ids, e_begin, n_experts, ws->moe_ids, npairs, g_stream);
+        ++t_launches;
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        for (int tok = 0; tok < tokens; ++tok) {
+            GemvArgs a = blank();
+            a.w[0] = g;
+            a.w[1] = u;
+            a.row_bytes[0] = grb;
+            a.row_bytes[1] = urb;
+            a.expert_bytes[0] = geb;
+            a.expert_bytes[1] = ueb;
+            a.rows = k * ffn_dim;
+            a.rows_per_route = ffn_dim;
+            a.K = in_dim;
+            a.x = x + (size_t)tok * xs;
+            a.x_stride = in_dim;
+            a.ids = ws->moe_ids + (size_t)tok * k;
+            a.y = act + (size_t)tok * k * ffn_dim;
+            a.y_stride = (int64_t)k * ffn_dim;
+            if ((st = run_gemv(t, 3, a, 1, what))) return st;  // counts its launches
+        }
+        return QL_OK;
+    }
+    if ((st = ensure_prefill(ws, (size_t)tokens, 2 * (size_t)in_dim))) return st;  // two f16 limbs per input
+    if ((st = grow(reinterpret_cast<void **>(&ws->moe_bsum), &ws->moe_bsum_cap, (size_t)tokens * (in_dim / 32),
+                   sizeof(float), what)))
+        return st;
+    cudaError_t e = moe_xprep_launch(x, xs, reinterpret_cast<uint4 *>(ws->xh), ws->rinv, ws->moe_bsum, tokens, in_dim,
+                                     g_stream);
+    ++t_launches;
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    MoeArgs a{};
+    a.w[0] = g;
+    a.w[1] = u;
+    a.eb[0] = geb;
+    a.eb[1] = ueb;
+    a.rb[0] = grb;
+    a.rb[1] = urb;
+    a.slab_bytes = moe_slab_bytes(grb > urb ? grb : urb);
+    a.rows = ffn_dim;
+    a.K = in_dim;
+    a.xq = reinterpret_cast<const uint4 *>(ws->xh);
+    a.rinv = ws->rinv;
+    a.bsum = ws->moe_bsum;
+    a.ids = ids;
+    a.e_begin = e_begin;
+    a.n_experts = n_experts;
+    a.npairs = npairs;
+    a.k = k;
+    a.y = act;
+    a.y_stride = ffn_dim;
+    a.err = ws->err;
+    e = moe_grouped_launch(a, t, true, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, what);
+}
+
+int ql_moe_down_grouped_accum_ordered(int32_t t, const uint8_t *d, size_t deb, size_t drb, const float *act,
+                                      const int *ids, int e_begin, int n_experts, const float *rw, float *out,
+                                      int64_t out_stride, int tokens, int k, int hidden, int ffn_dim) {
+    const char *what = "ql_moe_down_grouped_accum_ordered";
+    t_launches = 0;
+    int st = moe_check(t, tokens, k, e_begin, n_experts, what);
+    if (st) return st;
+    if (hidden < 0) return fail(QL_EINVAL, std::string(what) + ": negative hidden");
+    if (tokens == 0 || hidden == 0) return QL_OK;
+    if ((st = check_weight(t, d, drb, deb, ffn_dim, what))) return st;
+    if (!act || !ids || !rw || !out) return fail(QL_EINVAL, std::string(what) + ": null pointer");
+    if ((st = check_act(act, ffn_dim, nullptr, what))) return st;
+    if (out_stride < hidden) return fail(QL_EINVAL, std::string(what) + ": out_stride < hidden");
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    const int npairs = tokens * k;
+    if (!moe_stageable(d, drb)) {
+        if ((st = grow(reinterpret_cast<void **>(&ws->moe_ids), &ws->moe_ids_cap, (size_t)npairs, sizeof(int), what))) return st;
+        cudaError_t e = moe_local_ids_launch(ids, e_begin, n_experts, ws->moe_ids, npairs, g_stream);
+        ++t_launches;
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        for (int tok = 0; tok < tokens; ++tok) {
+            GemvArgs a = blank();
+            a.w[0] = d;
+            a.row_bytes[0] = drb;
+            a.expert_bytes[0] = deb;
+            a.rows = hidden;
+            a.K = k * ffn_dim;
+            a.units_per_route = ffn_dim / block_elems(t);
+            a.x = act + (size_t)tok * k * ffn_dim;
+            a.x_stride = ffn_dim;
+            a.ids = ws->moe_ids + (size_t)tok * k;
+            a.route_w = rw + (size_t)tok * k;
+            a.y = out + (size_t)tok * out_stride;
+            a.y_stride = hidden;
+            if ((st = run_gemv(t, 4, a, 1, what))) return st;  // counts its launches
+        }
+        return QL_OK;
+    }
+    if ((st = ensure_prefill(ws, (size_t)npairs, 2 * (size_t)ffn_dim))) return st;
+    if ((st = grow(reinterpret_cast<void **>(&ws->moe_y), &ws->moe_y_cap, (size_t)npairs * hidden, sizeof(float), what)))
+        return st;
+    if ((st = grow(reinterpret_cast<void **>(&ws->moe_bsum), &ws->moe_bsum_cap, (size_t)npairs * (ffn_dim / 32),
+                   sizeof(float), what)))
+        return st;
+    cudaError_t e = moe_xprep_launch(act, ffn_dim, reinterpret_cast<uint4 *>(ws->xh), ws->rinv, ws->moe_bsum, npairs,
+                                     ffn_dim, g_stream);
+    ++t_launches;
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    MoeArgs a{};
+    a.w[0] = a.w[1] = d;
+    a.eb[0] = a.eb[1] = deb;
+    a.rb[0] = a.rb[1] = drb;
+    a.slab_bytes = moe_slab_bytes(drb);
+    a.rows = hidden;
+    a.K = ffn_dim;
+    a.xq = reinterpret_cast<const uint4 *>(ws->xh);
+    a.rinv = ws->rinv;
+    a.bsum = ws->moe_bsum;
+    a.ids = ids;
+    a.e_begin = e_begin;
+    a.n_experts = n_experts;
+    a.npairs = npairs;
+    a.k = k;
+    a.y = ws->moe_y;
+    a.y_stride = hidden;
+    a.err = ws->err;
+    e = moe_grouped_launch(a, t, false, g_stream);
+    ++t_launches;
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    e = moe_combine_launch(ws->moe_y, ids, e_begin, n_experts, rw, out, out_stride, tokens, k, hidden, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, what);
 }
 
 int ql_quant_embedding(int32_t t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n) {

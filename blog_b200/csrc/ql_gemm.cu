@@ -519,14 +519,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4k_kernel(const __grid_
 // global, one token column per register).
 // ---------------------------------------------------------------------------
 constexpr int kTaThreads = 320;
-constexpr int kTaNR = 4;         // raw weight ring: 128 rows x one 256-input block column
+constexpr int kTaNR = 4;         // raw weight ring slots (barrier arrays; Q8_0 uses 2 of them)
 constexpr int kTaNX = 4;         // activation ring: NTOK tokens x 64 inputs
 constexpr int kTaNA = 2;         // dequantized blocks in TMEM (128 columns each)
 constexpr uint32_t kTaTmemA = 256;
-constexpr int kTaRBytes = 128 * 144;
-__host__ __device__ constexpr int ta_smem(int ntok) {
-    return 1024 + kTaNX * ntok * 128 + kTaNR * kTaRBytes + 2 * 64 * 33 * 4 + 256;
+// Bytes of one weight row per 256 inputs: Q4_K one super-block, Q4_0 8 x 18, Q8_0 8 x 34.
+__host__ __device__ constexpr int ta_row_bytes(int fmt) { return fmt == kQ8_0 ? 272 : 144; }
+// Raw weight ring depth: 4 stages of 128 x 144 B, or 2 of 128 x 272 B (Q8_0), within 227 KB.
+__host__ __device__ constexpr int ta_ring(int fmt) { return fmt == kQ8_0 ? 2 : kTaNR; }
+__host__ __device__ constexpr int ta_smem(int ntok, int fmt) {
+    return 1024 + kTaNX * ntok * 128 + ta_ring(fmt) * 128 * ta_row_bytes(fmt) + 2 * 64 * 33 * 4 + 256;
 }
+static_assert(ta_smem(256, kQ8_0) <= 232448 && ta_smem(256, kQ4_K) <= 232448, "gemm_ta shared memory");
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
@@ -609,16 +613,55 @@ __device__ __forceinline__ void q40_chunk_cols(const uint8_t *row, int p, uint32
     }
 }
 
+// Q8_0: chunk p (blocks 2p, 2p + 1 of the row's 8-block run, 34 B each) as 32 TMEM columns in the
+// same element order (column 16 bb + 4 jj + i: block 2p + bb, elements 8 jj + {0, 2}, {1, 3}, {4, 6},
+// {5, 7}).  Each quant is biased to an unsigned byte (q + 128) for the f16 magic-number conversion;
+// d * (u - 128) is one f16 fma, so every weight is f16(d * q), rounded once.
+__device__ __forceinline__ void q80_chunk_cols(const uint8_t *row, int p, uint32_t (&v)[32]) {
+#pragma unroll
+    for (int bb = 0; bb < 2; ++bb) {
+        const uint8_t *base = row + 34 * (2 * p + bb);
+        uint32_t q[8], dbits;
+        if (bb == 0) {  // the block starts on 4 bytes (row pitch 272 B, 68 B per chunk)
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(base);
+            uint32_t w9[9];
+#pragma unroll
+            for (int i = 0; i < 9; ++i) w9[i] = w[i];
+            dbits = w9[0] & 0xFFFFu;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = __byte_perm(w9[i], w9[i + 1], 0x5432);
+        } else {  // 2 bytes past a 4-byte boundary: its quants start on 4 bytes
+            dbits = *reinterpret_cast<const uint16_t *>(base);
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(base + 2);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = w[i];
+        }
+        const float d = half_bits_to_float(dbits);
+        const __half2 D = __float2half2_rn(d), M = __float2half2_rn(-128.0f * d);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const uint32_t w0 = q[2 * jj] ^ 0x80808080u, w1 = q[2 * jj + 1] ^ 0x80808080u;
+            v[16 * bb + 4 * jj + 0] = deq2(w0 & 0x00FF00FFu, D, M);
+            v[16 * bb + 4 * jj + 1] = deq2((w0 >> 8) & 0x00FF00FFu, D, M);
+            v[16 * bb + 4 * jj + 2] = deq2(w1 & 0x00FF00FFu, D, M);
+            v[16 * bb + 4 * jj + 3] = deq2((w1 >> 8) & 0x00FF00FFu, D, M);
+        }
+    }
+}
+
 template <int EPI, int FMT, int NTOK>
 __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_constant__ GemmArgs a) {
     constexpr int RO = EPI == kGemmSwiglu ? 64 : 128;  // output columns (weight rows) per tile
+    constexpr int WRB = ta_row_bytes(FMT);              // bytes of one weight row per stage
+    constexpr int NR = ta_ring(FMT);                    // raw weight ring depth
+    constexpr int RBYTES = 128 * WRB;                   // one raw weight stage
     constexpr int XB = NTOK * 128;                     // bytes of one activation chunk slot
     constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(NTOK >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sX = smem;
     uint8_t *sR = sX + kTaNX * XB;
-    float *sU = reinterpret_cast<float *>(sR + kTaNR * kTaRBytes);  // SwiGLU: [2 token halves][64 rows][33]
+    float *sU = reinterpret_cast<float *>(sR + NR * RBYTES);  // SwiGLU: [2 token halves][64 rows][33]
     uint64_t *bars = reinterpret_cast<uint64_t *>(sU + 2 * 64 * 33);
     uint64_t *rfull = bars, *rempty = rfull + kTaNR, *xfull = rempty + kTaNR, *xempty = xfull + kTaNX;
     uint64_t *afull = xempty + kTaNX, *aempty = afull + kTaNA, *accfull = aempty + kTaNA;
@@ -629,7 +672,7 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
     const int m0 = blockIdx.x * NTOK, n0 = blockIdx.y * RO;
     const int nsb = a.nsb;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kTaNR; ++i) { mbar_init(&rfull[i], 1); mbar_init(&rempty[i], 8); }
+        for (int i = 0; i < NR; ++i) { mbar_init(&rfull[i], 1); mbar_init(&rempty[i], 8); }
         for (int i = 0; i < kTaNX; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xempty[i], 1); }
         for (int i = 0; i < kTaNA; ++i) { mbar_init(&afull[i], 8); mbar_init(&aempty[i], 1); }
         mbar_init(accfull, 1);
@@ -652,10 +695,17 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
             row0 = n0 - (src > 0 ? a.src_end[src - 1] : 0);
         }
         auto load_raw = [&](int b) {
-            const int rs = b % kTaNR;
-            uint8_t *dst = sR + rs * kTaRBytes;
-            mbar_arrive_expect_tx(&rfull[rs], kTaRBytes);
-            if (FMT == kQ4_0) {
+            const int rs = b % NR;
+            uint8_t *dst = sR + rs * RBYTES;
+            mbar_arrive_expect_tx(&rfull[rs], RBYTES);
+            if (FMT == kQ8_0) {  // 2-D view of 2-byte elements: 136 of them = 8 blocks = 256 inputs
+                if (EPI == kGemmSwiglu) {
+                    tma_load_2d(dst, &a.tm_w[0], b * 136, n0, &rfull[rs]);
+                    tma_load_2d(dst + 64 * WRB, &a.tm_w[1], b * 136, n0, &rfull[rs]);
+                } else {
+                    tma_load_2d(dst, &a.tm_w[src], b * 136, row0, &rfull[rs]);
+                }
+            } else if (FMT == kQ4_0) {
                 if (EPI == kGemmSwiglu) {
                     tma_load_2d(dst, &a.tm_w[0], b * 144, n0, &rfull[rs]);
                     tma_load_2d(dst + 64 * 144, &a.tm_w[1], b * 144, n0, &rfull[rs]);
@@ -669,13 +719,13 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
                 tma_load_3d(dst, &a.tm_w[src], 0, b, row0, &rfull[rs]);
             }
         };
-        const int early = nsb < kTaNR ? nsb : kTaNR;
+        const int early = nsb < NR ? nsb : NR;
         for (int b = 0; b < early; ++b) load_raw(b);  // weights do not depend on the previous kernel
         asm volatile("griddepcontrol.wait;" ::: "memory");  // activations: xprep's output
         int issued_r = early, issued_x = 0;
         for (int b = 0; b < nsb && !*abort_flag; ++b) {
-            if (b >= kTaNR) {
-                if (!mbar_wait(&rempty[b % kTaNR], (uint32_t)(b / kTaNR - 1) & 1u, a.err, kErrWaitEmpty)) {
+            if (b >= NR) {
+                if (!mbar_wait(&rempty[b % NR], (uint32_t)(b / NR - 1) & 1u, a.err, kErrWaitEmpty)) {
                     *abort_flag = 1;
                     break;
                 }
@@ -695,8 +745,8 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
             }
         }
         // never leave with copies in flight
-        for (int j = issued_r > kTaNR ? issued_r - kTaNR : 0; j < issued_r; ++j)
-            mbar_wait(&rfull[j % kTaNR], (uint32_t)(j / kTaNR) & 1u, nullptr, 0);
+        for (int j = issued_r > NR ? issued_r - NR : 0; j < issued_r; ++j)
+            mbar_wait(&rfull[j % NR], (uint32_t)(j / NR) & 1u, nullptr, 0);
         for (int j = issued_x > kTaNX ? issued_x - kTaNX : 0; j < issued_x; ++j)
             mbar_wait(&xfull[j % kTaNX], (uint32_t)(j / kTaNX) & 1u, nullptr, 0);
         return;
@@ -740,9 +790,9 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
         const int r = 32 * q + lane;  // weight row of the tile = TMEM lane
         bool ok = true;
         for (int b = 0; b < nsb; ++b) {
-            const int rs = b % kTaNR, as = b % kTaNA;
+            const int rs = b % NR, as = b % kTaNA;
             if (!__all_sync(0xffffffffu,
-                            !*abort_flag && mbar_wait(&rfull[rs], (uint32_t)(b / kTaNR) & 1u, a.err, kErrWaitFull))) {
+                            !*abort_flag && mbar_wait(&rfull[rs], (uint32_t)(b / NR) & 1u, a.err, kErrWaitFull))) {
                 *abort_flag = 1;
                 ok = false;
                 break;
@@ -755,13 +805,14 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
                 break;
             }
             tc_fence_after();
-            const uint8_t *rowp = sR + rs * kTaRBytes + r * 144;
+            const uint8_t *rowp = sR + rs * RBYTES + r * WRB;
             const uint4 hd = FMT == kQ4_K ? *reinterpret_cast<const uint4 *>(rowp) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int pch = 2 * hf + cc;
                 uint32_t v[32];
-                if (FMT == kQ4_0) q40_chunk_cols(rowp, pch, v);
+                if (FMT == kQ8_0) q80_chunk_cols(rowp, pch, v);
+                else if (FMT == kQ4_0) q40_chunk_cols(rowp, pch, v);
                 else q4k_chunk_cols(rowp, hd, pch, v);
                 tmem_st32(tmem + ((uint32_t)(32 * q) << 16) + kTaTmemA + 128u * (uint32_t)as + 32u * (uint32_t)pch, v);
             }
@@ -882,7 +933,7 @@ cudaError_t gemm_ta_launch_t(const GemmArgs &a, cudaStream_t s) {
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(gemm_ta_kernel<EPI, FMT, NTOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             ta_smem(NTOK));
+                                             ta_smem(NTOK, FMT));
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
@@ -890,7 +941,7 @@ cudaError_t gemm_ta_launch_t(const GemmArgs &a, cudaStream_t s) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((a.M + NTOK - 1) / NTOK, (a.N + RO - 1) / RO, 1);
     cfg.blockDim = dim3(kTaThreads);
-    cfg.dynamicSmemBytes = ta_smem(NTOK);
+    cfg.dynamicSmemBytes = ta_smem(NTOK, FMT);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -900,16 +951,26 @@ cudaError_t gemm_ta_launch_t(const GemmArgs &a, cudaStream_t s) {
     return cudaLaunchKernelEx(&cfg, gemm_ta_kernel<EPI, FMT, NTOK>, a);
 }
 
-int gemm_ta_tokens(int M) { return M >= 256 ? 256 : 128; }
+// 256-token tiles dequantize each weight half as often as 128-token tiles, but only when they still
+// give every SM a tile; otherwise the smaller tiles fill more SMs.
+int gemm_ta_tokens(int M, int row_tiles, int sms) {
+    return (M >= 256 && (int64_t)((M + 255) / 256) * row_tiles >= sms) ? 256 : 128;
+}
 
 cudaError_t gemm_ta_launch(const GemmArgs &a, int epi, int ntok, cudaStream_t s) {
     if (ntok == 256) {
+        if (a.fmt == kQ8_0)
+            return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ8_0, 256>(a, s)
+                                      : gemm_ta_launch_t<kGemmPlain, kQ8_0, 256>(a, s);
         if (a.fmt == kQ4_0)
             return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ4_0, 256>(a, s)
                                       : gemm_ta_launch_t<kGemmPlain, kQ4_0, 256>(a, s);
         return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ4_K, 256>(a, s)
                                   : gemm_ta_launch_t<kGemmPlain, kQ4_K, 256>(a, s);
     }
+    if (a.fmt == kQ8_0)
+        return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ8_0, 128>(a, s)
+                                  : gemm_ta_launch_t<kGemmPlain, kQ8_0, 128>(a, s);
     if (a.fmt == kQ4_0)
         return epi == kGemmSwiglu ? gemm_ta_launch_t<kGemmSwiglu, kQ4_0, 128>(a, s)
                                   : gemm_ta_launch_t<kGemmPlain, kQ4_0, 128>(a, s);

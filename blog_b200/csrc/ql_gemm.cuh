@@ -85,7 +85,7 @@ cudaError_t gemm_q4k_launch(const GemmArgs &a, int epi, cudaStream_t s);
 // Prefill GEMM with the weights as the MMA's M side (A in tensor memory): tiles of 128 weight rows
 // (SwiGLU: 64 + 64) x ntok tokens (128 or 256); tm_w boxes of 128 (SwiGLU: 64) rows, tm_x boxes
 // {64, ntok}; no K split, no fused argmax.
-int gemm_ta_tokens(int M);
+int gemm_ta_tokens(int M, int row_tiles, int sms);
 cudaError_t gemm_ta_launch(const GemmArgs &a, int epi, int ntok, cudaStream_t s);
 
 }  // namespace ql

@@ -80,8 +80,8 @@ QL_API int ql_quant_matmul(int32_t quant_type, const uint8_t *weight, size_t row
  * (gamma != NULL: scale_m = 1/sqrt(mean_k x[m,k]^2 + eps), g = gamma; else 1),
  * optional bias, accumulate != 0 adds into y.  path: QL_PATH_AUTO picks by shape;
  * QL_PATH_GEMV forces the CUDA-core streaming engine (fp32 activations, exact
- * decode); QL_PATH_TENSOR forces the tcgen05 tensor-core GEMM (Q4_K or Q4_0, in_dim a
- * multiple of 256; activations and dequantized weights rounded to f16, fp32
+ * decode); QL_PATH_TENSOR forces the tcgen05 tensor-core GEMM (Q4_K, Q4_0 or Q8_0, in_dim
+ * a multiple of 256; activations and dequantized weights rounded to f16, fp32
  * accumulation; QL_EINVAL when the shape or dtype does not qualify). */
 #define QL_PATH_AUTO 0
 #define QL_PATH_GEMV 1
@@ -234,6 +234,32 @@ QL_API int ql_quant_down_f32_indexed_accum_ordered(int32_t quant_type, const uin
  * ties, non-finite = -inf), top_w = p * routed_scaling. */
 QL_API int ql_moe_router_topk(const float *router_logits, int *top_idx, float *top_w, int tokens, int n_experts, int k,
                        float routed_scaling);
+
+/* Grouped routed experts for a batch of tokens (no reference twin: the reference runs
+ * ql_quant_swiglu_indexed and ql_quant_down_f32_indexed_accum_ordered once per token,
+ * RoutedExperts.cpp:80-118).  Every expert's rows are read once per call for all the tokens
+ * routed to it.  Route (t, r) has expert id expert_ids[t * k + r]; it belongs to this call when
+ * e = id - expert_begin is in [0, n_experts) (expert e's rows start expert_bytes * e past the
+ * weight pointer: one expert-parallel shard of experts), and is skipped otherwise.
+ *   act[t * k + r][f] = SiLU(Wg[e][f] . x_t) * (Wu[e][f] . x_t), 0 for a skipped route,
+ * x_t = x + t * x_stride, act rows ffn_dim floats apart.  Numerics as QL_PATH_TENSOR: each
+ * activation row (times a power of two) and each dequantized weight rounded to f16, fp32
+ * accumulation on the tensor cores.  Q4_0, Q5_0, Q8_0, Q4_K; rows up to ~3.5 KB run grouped
+ * (16 rows per warp in shared memory), longer rows run the per-token indexed launches. */
+QL_API int ql_moe_swiglu_grouped(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,
+                                 size_t gate_expert_bytes, size_t up_expert_bytes, size_t gate_row_bytes,
+                                 size_t up_row_bytes, const float *x, int64_t x_stride, const int *expert_ids,
+                                 int expert_begin, int n_experts, float *act, int tokens, int k, int ffn_dim,
+                                 int in_dim);
+/* out[t][h] += total_t,h with total = fmaf(Wd[e][h] . act[t * k + r], route_weights[t * k + r],
+ * total) over t's routes r = 0..k-1 that belong to this call, in route order (the reference
+ * combine, kernel.cu:2252-2287); out rows out_stride floats apart.  Same numerics and limits
+ * as ql_moe_swiglu_grouped. */
+QL_API int ql_moe_down_grouped_accum_ordered(int32_t quant_type, const uint8_t *down_weight, size_t down_expert_bytes,
+                                             size_t down_row_bytes, const float *act, const int *expert_ids,
+                                             int expert_begin, int n_experts, const float *route_weights,
+                                             float *out, int64_t out_stride, int tokens, int k, int hidden,
+                                             int ffn_dim);
 
 /* ---- embedding, dequant, argmax (reference kernel.cuh:141-142, 244-253, 347) ----- */
 QL_API int ql_quant_embedding(int32_t quant_type, const int *input, float *output, const uint8_t *table, size_t row_bytes,

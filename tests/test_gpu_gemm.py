@@ -1,4 +1,4 @@
-"""Parity of the tcgen05 prefill GEMM (Q4_K and Q4_0, called through the C ABI).
+"""Parity of the tcgen05 prefill GEMM (Q4_K, Q4_0 and Q8_0, called through the C ABI).
 
 The tensor-core path rounds each activation row (after an exact power-of-two
 scale) and each dequantized weight to f16 and accumulates in fp32 on the tensor
@@ -66,7 +66,17 @@ def q40_f16_operand(w, n, k):
     return (d[..., None] * (q - 8)).astype(np.float16).astype(np.float64).reshape(n, k)
 
 
+def q80_f16_operand(w, n, k):
+    """Q8_0 weights as the tensor-core dequantizer rounds them: f16(d * q), one rounding."""
+    b = w.reshape(n, k // 32, 34)
+    d = b[..., 0:2].copy().view(np.float16)[..., 0].astype(np.float64)
+    q = b[..., 2:34].copy().view(np.int8).astype(np.float64)
+    return (d[..., None] * q).astype(np.float16).astype(np.float64).reshape(n, k)
+
+
 def f16_operand(t, w, n, k):
+    if t == O.Q8_0:
+        return q80_f16_operand(w, n, k)
     return q40_f16_operand(w, n, k) if t == O.Q4_0 else q4k_f16_operand(w, n, k)
 
 
@@ -101,7 +111,7 @@ def run_tc(w, rb, x, n, k, m, gamma=None, eps=0.0, bias=None, y0=None, path=Q.PA
 SHAPES = [(256, 256, 128), (300, 512, 77), (512, 4096, 64), (1024, 2048, 256), (4096, 4096, 128), (100, 768, 8)]
 
 
-@pytest.mark.parametrize("t", [O.Q4_K, O.Q4_0])
+@pytest.mark.parametrize("t", [O.Q4_K, O.Q4_0, O.Q8_0])
 @pytest.mark.parametrize("n,k,m", SHAPES)
 def test_tc_gemm_matches_oracle_and_f16_operands(n, k, m, t):
     w = make_weights(t, n, k, seed=n + 3 * k)
@@ -141,6 +151,51 @@ def test_tc_gemm_q40_sweep_shape_and_swiglu():
     uv = O.gemv(O.Q4_0, u, rb2, xn, f, k2, m2, order=1).astype(np.float64)
     assert rel_l2(host(act), gv / (1 + np.exp(-gv)) * uv) < NORTH_STAR
     assert Q.last_launch_count() == 2  # xprep + the tensor-core GEMM
+
+
+@pytest.mark.parametrize("n,k,m", [(4096, 4096, 512), (11008, 4096, 512), (4096, 11008, 2048)])
+def test_tc_gemm_q80_sweep_shapes(n, k, m):
+    """Q8_0 on the tensor cores at the BASELINE sweep shapes (M 512 and 2048, routed by QL_PATH_AUTO),
+    against the oracle and against the exact f16 operands."""
+    w = make_weights(O.Q8_0, n, k, seed=n + k + 7)
+    x = _x(m + 5, m, k)
+    rb = O.row_bytes(O.Q8_0, k)
+    got = run_tc(w, rb, x, n, k, m, t=O.Q8_0, path=Q.PATH_AUTO)
+    assert Q.last_launch_count() == 2  # xprep + the tensor-core GEMM
+    mo = 256  # the oracle on one full 256-token tile (it takes ~1 s per GMAC on the host)
+    err = rel_l2(got[:mo], O.gemv(O.Q8_0, w, rb, x[:mo], n, k, mo, order=1))
+    print(f"Q8_0 tensor-core GEMM {n}x{k} M={m}: rel_l2 {err:.2e} (first {mo} tokens vs the oracle)")
+    assert err < NORTH_STAR
+    # every token against the exact f16 operands (float64 host product); fp32 accumulation error grows
+    # with K (random walk over the K products), hence twice the bar at K = 11008
+    ref16 = act_f16_operand(x) @ q80_f16_operand(w, n, k).T
+    assert rel_l2(got, ref16) < EXACT_F16_OPERANDS * (2 if k > 8192 else 1)
+
+
+def test_tc_gemm_q80_swiglu_stacked_bias_accumulate():
+    """Q8_0 SwiGLU pair with a fused RMSNorm, a stacked q/k/v-style job with bias, and an accumulating
+    plain GEMM, all on the tensor cores, against the oracle."""
+    import torch
+    f, k, m = 1280, 2048, 96
+    g, u = make_weights(O.Q8_0, f, k, seed=201), make_weights(O.Q8_0, f, k, seed=202)
+    x = _x(203, m, k)
+    gamma = (1.0 + 0.1 * _x(204, 1, k)[0]).astype(np.float32)
+    rb = O.row_bytes(O.Q8_0, k)
+    act = torch.empty((m, f), device="cuda:0")
+    Q.quant_swiglu_ex(O.Q8_0, dev(g).data_ptr(), dev(u).data_ptr(), rb, rb, dev(x).data_ptr(), k,
+                      act.data_ptr(), f, f, k, m, dev(gamma).data_ptr(), 1e-6)
+    assert Q.last_launch_count() == 2
+    xn = O.rmsnorm(x, gamma, 1e-6)
+    gv = O.gemv(O.Q8_0, g, rb, xn, f, k, m, order=1).astype(np.float64)
+    uv = O.gemv(O.Q8_0, u, rb, xn, f, k, m, order=1).astype(np.float64)
+    assert rel_l2(host(act), gv / (1 + np.exp(-gv)) * uv) < NORTH_STAR
+    n = 640
+    w = make_weights(O.Q8_0, n, k, seed=205)
+    bias = _x(206, 1, n)[0]
+    y0 = _x(207, m, n)
+    got = run_tc(w, rb, x, n, k, m, gamma=gamma, eps=1e-6, bias=bias, y0=y0, t=O.Q8_0)
+    ref = y0 + O.gemv(O.Q8_0, w, rb, xn, n, k, m, order=1) + bias[None, :]
+    assert rel_l2(got, ref) < NORTH_STAR
 
 
 def test_tc_gemm_fused_rmsnorm_bias_accumulate():
@@ -201,14 +256,16 @@ def test_auto_path_routes_by_token_count():
         assert np.array_equal(host(y).view(np.uint32), run_tc(w, rb, x, n, k, m, path=forced).view(np.uint32))
 
 
-def test_tensor_path_rejects_ineligible_shapes():
+@pytest.mark.parametrize("t,k", [(O.Q5_0, 512), (O.Q8_0, 480)])
+def test_tensor_path_rejects_ineligible_shapes(t, k):
+    """No tensor-core kernel for Q5_0, and none for in_dim not a multiple of 256."""
     import torch
-    w = make_weights(O.Q8_0, 64, 512, seed=81)
-    x = dev(_x(82, 16, 512))
+    w = make_weights(t, 64, k, seed=81)
+    x = dev(_x(82, 16, k))
     y = torch.empty((16, 64), device="cuda:0")
     with pytest.raises(Q.QLError) as e:
-        Q.quant_matmul_ex(O.Q8_0, dev(w).data_ptr(), O.row_bytes(O.Q8_0, 512), x.data_ptr(), 512, y.data_ptr(), 64,
-                          64, 512, 16, None, 0.0, None, False, Q.PATH_TENSOR)
+        Q.quant_matmul_ex(t, dev(w).data_ptr(), O.row_bytes(t, k), x.data_ptr(), k, y.data_ptr(), 64,
+                          64, k, 16, None, 0.0, None, False, Q.PATH_TENSOR)
     assert e.value.status == Q.QL_EINVAL
 
 
