@@ -826,10 +826,22 @@ def run_moe(args):
             if world > 1:
                 torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms[grouped] = float(t[0])
+        # one layer's routed output both ways from the same router input (no collective inside)
+        layer = st.layers[1]
+        routed_out = {}
+        for grouped in (True, False):
+            st.grouped = grouped
+            st.moe.zero_()
+            st.routed(layer)
+            routed_out[grouped] = st.moe.clone().double()
+        torch.cuda.synchronize()
     Q.check_device()
     hg, hp = out[True][0].double(), out[False][0].double()
-    parity = {"hidden_rel_l2_vs_per_token": float((hg - hp).norm() / hp.norm()),
-              "tokens_equal_per_token": int((out[True][1] == out[False][1]).sum()), "tokens": T}
+    rg, rp = routed_out[True], routed_out[False]
+    parity = {"routed_layer_rel_l2_vs_per_token": float((rg - rp).norm() / rp.norm()),
+              "hidden_rel_l2_vs_per_token_after_all_layers": float((hg - hp).norm() / hp.norm()),
+              "tokens_equal_per_token": int((out[True][1] == out[False][1]).sum()), "tokens": T,
+              "note": "after all layers, routes whose top-k scores nearly tie can flip between the two paths"}
     hbm, _ = peaks()
     wb = st.weight_bytes()
     if rank == 0:
@@ -838,7 +850,8 @@ def run_moe(args):
                           "value": T / (ms[True] / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                           "ms_per_step": ms[True], "parallelism": f"ep{world}", "weight_bytes_per_rank": wb,
                           "routed_path": "grouped: per layer one SwiGLU and one down + ordered-combine call over "
-                                         "all (token, route) pairs, each expert's rows read once (mma.sync f16)",
+                                         "all (token, route) pairs, each expert's rows read once (mma.sync: exact "
+                                         "integer quants x two-limb f16 activations, fp32 block scales)",
                           "per_token_path": {"tokens_per_s": T / (ms[False] / 1e3), "ms_per_step": ms[False],
                                              "routed_path": "the reference's per-token loop: indexed SwiGLU and "
                                                             "ordered down launches per token"},
@@ -846,8 +859,8 @@ def run_moe(args):
                                        "frac": gbs / hbm,
                                        "bytes": "all of the rank's weights once per step (64 tokens x 6 routes "
                                                 "reach nearly every expert of every layer)"},
-                          "parity": parity, "dtype": "f16 tensor-core operands, fp32 accumulation (routed); "
-                                                     "fp32 activations elsewhere",
+                          "parity": parity, "dtype": "f32 (routed: fp32-class, 1e-7 of the oracle); attention "
+                                                     "stand-ins and shared experts on the f16 tensor-core GEMM",
                           "data": "synthetic"}), flush=True)
     g = None
     graphs.clear()

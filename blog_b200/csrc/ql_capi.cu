@@ -67,6 +67,10 @@ struct Workspace {
     size_t moe_ids_cap = 0;
     float *moe_bsum = nullptr;
     size_t moe_bsum_cap = 0;
+    int *moe_off = nullptr;  // expert buckets of the (token, route) pairs
+    size_t moe_off_cap = 0;
+    int *moe_list = nullptr;
+    size_t moe_list_cap = 0;
 };
 
 std::mutex g_mu;
@@ -915,10 +919,25 @@ int grow(void **buf, size_t *cap, size_t n, size_t elem, const char *what) {
     *cap = n;
     return QL_OK;
 }
-// Whether the grouped kernel can stage a matrix: 16 rows in a warp's slab, and a 16-byte-aligned
-// base (the bulk copy starts at the 16-byte boundary at or before a row range).
+// Whether the grouped kernel can stage a matrix: 64 rows in shared memory, and a 16-byte-aligned
+// base (each row's bulk copy starts at the 16-byte boundary at or before the row).
 bool moe_stageable(const uint8_t *w, size_t rb) {
-    return reinterpret_cast<uintptr_t>(w) % 16 == 0 && moe_slab_bytes(rb) <= moe_max_slab_bytes();
+    return reinterpret_cast<uintptr_t>(w) % 16 == 0 && moe_row_pitch(rb) <= moe_max_row_pitch();
+}
+// Buckets the call's (token, route) pairs by expert (one launch) into the workspace.
+int moe_buckets(Workspace *ws, const int *ids, int npairs, int e_begin, int n_experts, MoeArgs &a, const char *what) {
+    int st;
+    if ((st = grow(reinterpret_cast<void **>(&ws->moe_off), &ws->moe_off_cap, (size_t)n_experts + 2, sizeof(int),
+                   what)))
+        return st;
+    if ((st = grow(reinterpret_cast<void **>(&ws->moe_list), &ws->moe_list_cap, (size_t)npairs, sizeof(int), what)))
+        return st;
+    cudaError_t e = moe_bucket_launch(ids, npairs, e_begin, n_experts, ws->moe_off, ws->moe_list, g_stream);
+    ++t_launches;
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    a.bucket_off = ws->moe_off;
+    a.bucket = ws->moe_list;
+    return QL_OK;
 }
 int moe_check(int t, int tokens, int k, int e_begin, int n_experts, const char *what) {
     if (tokens < 0 || k <= 0 || n_experts <= 0 || e_begin < 0)
@@ -946,7 +965,7 @@ int ql_moe_swiglu_grouped(int32_t t, const uint8_t *g, const uint8_t *u, size_t 
     Workspace *ws = workspace(&st);
     if (!ws) return st;
     const int npairs = tokens * k;
-    if (!moe_stageable(g, grb) || !moe_stageable(u, urb)) {
+    if (!moe_stageable(g, grb) || !moe_stageable(u, urb) || n_experts > moe_max_experts()) {
         // rows too long for the grouped kernel's slabs: the per-token indexed launches
         if ((st = grow(reinterpret_cast<void **>(&ws->moe_ids), &ws->moe_ids_cap, (size_t)npairs, sizeof(int), what))) return st;
         cudaError_t e = moe_local_ids_launch(ids, e_begin, n_experts, ws->moe_ids, npairs, g_stream);
@@ -987,7 +1006,7 @@ int ql_moe_swiglu_grouped(int32_t t, const uint8_t *g, const uint8_t *u, size_t 
     a.eb[1] = ueb;
     a.rb[0] = grb;
     a.rb[1] = urb;
-    a.slab_bytes = moe_slab_bytes(grb > urb ? grb : urb);
+    a.row_pitch = moe_row_pitch(grb > urb ? grb : urb);
     a.rows = ffn_dim;
     a.K = in_dim;
     a.xq = reinterpret_cast<const uint4 *>(ws->xh);
@@ -1001,6 +1020,7 @@ int ql_moe_swiglu_grouped(int32_t t, const uint8_t *g, const uint8_t *u, size_t 
     a.y = act;
     a.y_stride = ffn_dim;
     a.err = ws->err;
+    if ((st = moe_buckets(ws, ids, npairs, e_begin, n_experts, a, what))) return st;
     e = moe_grouped_launch(a, t, true, g_stream);
     ++t_launches;
     return e == cudaSuccess ? QL_OK : cuda_fail(e, what);
@@ -1022,7 +1042,7 @@ int ql_moe_down_grouped_accum_ordered(int32_t t, const uint8_t *d, size_t deb, s
     Workspace *ws = workspace(&st);
     if (!ws) return st;
     const int npairs = tokens * k;
-    if (!moe_stageable(d, drb)) {
+    if (!moe_stageable(d, drb) || n_experts > moe_max_experts()) {
         if ((st = grow(reinterpret_cast<void **>(&ws->moe_ids), &ws->moe_ids_cap, (size_t)npairs, sizeof(int), what))) return st;
         cudaError_t e = moe_local_ids_launch(ids, e_begin, n_experts, ws->moe_ids, npairs, g_stream);
         ++t_launches;
@@ -1059,7 +1079,7 @@ int ql_moe_down_grouped_accum_ordered(int32_t t, const uint8_t *d, size_t deb, s
     a.w[0] = a.w[1] = d;
     a.eb[0] = a.eb[1] = deb;
     a.rb[0] = a.rb[1] = drb;
-    a.slab_bytes = moe_slab_bytes(drb);
+    a.row_pitch = moe_row_pitch(drb);
     a.rows = hidden;
     a.K = ffn_dim;
     a.xq = reinterpret_cast<const uint4 *>(ws->xh);
@@ -1073,6 +1093,7 @@ int ql_moe_down_grouped_accum_ordered(int32_t t, const uint8_t *d, size_t deb, s
     a.y = ws->moe_y;
     a.y_stride = hidden;
     a.err = ws->err;
+    if ((st = moe_buckets(ws, ids, npairs, e_begin, n_experts, a, what))) return st;
     e = moe_grouped_launch(a, t, false, g_stream);
     ++t_launches;
     if (e != cudaSuccess) return cuda_fail(e, what);

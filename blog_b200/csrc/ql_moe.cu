@@ -5,11 +5,11 @@
 // launch (RoutedExperts.cpp:80-118; kernel.cu:1339-1385, 2252-2287), so an expert chosen by n
 // tokens is read n times.  Here each expert's rows are read once per layer for all the tokens
 // routed to it:
-//   1. xprep (the tensor-core GEMM's activation prep): token rows -> f16, power-of-two row scale;
-//   2. moe_grouped_kernel<SwiGLU>: CTA = (expert, 32 gate + 32 up rows); it finds the (token,
-//      route) pairs of its expert by scanning the routing table, multiplies its weight rows with
-//      those tokens on the tensor cores, and writes act[(t, r), f] = SiLU(g) * u in fp32;
-//   3. xprep over the act rows;
+//   1. moe_xprep: token rows -> two f16 limbs with a power-of-two row scale, 32-element block sums;
+//   2. moe_bucket_kernel: the (token, route) pairs grouped by expert, in routing-table order;
+//      moe_grouped_kernel<SwiGLU>: CTA = (expert, 32 gate + 32 up rows); it multiplies its weight
+//      rows with its expert's tokens on the tensor cores, and writes act[(t, r), f] = SiLU(g) * u;
+//   3. moe_xprep over the act rows, and the buckets again;
 //   4. moe_grouped_kernel<down>: CTA = (expert, 64 rows of the hidden size); writes each pair's
 //      down projection (fp32) to a scratch row;
 //   5. moe_combine_kernel: out[t, h] += sum over t's routes in route order (fmaf(y, w, total)),
@@ -23,8 +23,9 @@
 // shared memory (no dequantized tile): mma.sync m16n8k16 with the k order of the activation
 // layout (elements 0, 2, 1, 3 | 4, 6, 5, 7 of each group of 8), so lane (g, c) of a 16-element
 // step needs quants 4c..4c+3 of rows g and g + 8: one 32-bit word of nibbles per row, masked
-// into f16 pairs with the magic-number conversion.  Tokens are the MMA's n = 8 columns, up to
-// 32 per pass over the staged rows (decode at batch 64: ~6 tokens per expert, one n-tile).
+// into exact integer f16 pairs with the magic-number conversion.  Tokens are the MMA's n = 8
+// columns, up to 32 per pass over the staged rows (decode at batch 64: ~6 tokens per expert,
+// one n-tile).
 #include "ql_common.cuh"
 #include "ql_gemm.cuh"
 #include "ql_moe.cuh"
@@ -32,8 +33,8 @@
 namespace ql {
 namespace {
 
-constexpr int kMoeThreads = 128;  // 4 warps x 16 weight rows
-constexpr int kMoePass = 32;      // tokens per pass (4 MMA n-tiles)
+constexpr int kMoeThreads = 256;  // 4 slabs of 16 weight rows x 2 warps (one per half of K)
+constexpr int kMoePass = 16;      // tokens per pass (2 MMA n-tiles)
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
@@ -187,90 +188,277 @@ __global__ void __launch_bounds__(256) moe_xprep_kernel(const float *__restrict_
     }
 }
 
-__device__ __forceinline__ bool route_is(const int *ids, int i, int e_begin, int e) { return ids[i] - e_begin == e; }
+// One pass over the warp's 16 staged rows for NT token tiles: per 32-element block, the exact
+// integer quants times both activation limbs on the tensor cores (4 MMAs per tile), then the
+// block's fp32 scale (and Q4_K's min times the block sum) into the accumulators.  The activation
+// words and block sums of block kb + PF load while block kb computes (they come from L2, and an
+// SM holds only 12 of these warps).
+template <int FMT, int NT>
+__device__ __forceinline__ void pass_blocks(const uint8_t *row0, const uint8_t *row1, int kb_lo, int nkb, int c,
+                                            const uint4 *const (&xr)[2], const float *const (&bsr)[2][2],
+                                            float (&acc)[2][4]) {
+    constexpr int PF = NT == 1 ? 4 : 2;
+    uint4 b[PF][NT][2];
+    float bs[PF][NT][2];
+    auto load = [&](int p, int kb) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            b[p][j][0] = xr[j][8 * kb];      // step 0 of the block: 4 words per 16 elements
+            b[p][j][1] = xr[j][8 * kb + 4];  // step 1
+            if (FMT == kQ4_K) {
+                bs[p][j][0] = bsr[j][0][kb];
+                bs[p][j][1] = bsr[j][1][kb];
+            }
+        }
+    };
+#pragma unroll
+    for (int p = 0; p < PF; ++p)
+        if (kb_lo + p < nkb) load(p, kb_lo + p);
+    for (int kb0 = kb_lo; kb0 < nkb; kb0 += PF) {
+#pragma unroll
+        for (int p = 0; p < PF; ++p) {
+            const int kb = kb0 + p;
+            if (kb < nkb) {
+                uint32_t A0[4], A1[4];
+                BlockScale bsc;
+                decode_block<FMT>(row0, row1, kb, c, A0, A1, bsc);
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    float t[4] = {0.f, 0.f, 0.f, 0.f};  // this block's integer-weight dot products
+                    mma16816(t, A0, b[p][j][0].x, b[p][j][0].y);
+                    mma16816(t, A0, b[p][j][0].z, b[p][j][0].w);
+                    mma16816(t, A1, b[p][j][1].x, b[p][j][1].y);
+                    mma16816(t, A1, b[p][j][1].z, b[p][j][1].w);
+                    acc[j][0] = fmaf(bsc.d[0], t[0], acc[j][0]);
+                    acc[j][1] = fmaf(bsc.d[0], t[1], acc[j][1]);
+                    acc[j][2] = fmaf(bsc.d[1], t[2], acc[j][2]);
+                    acc[j][3] = fmaf(bsc.d[1], t[3], acc[j][3]);
+                    if (FMT == kQ4_K) {
+                        acc[j][0] = fmaf(-bsc.m[0], bs[p][j][0], acc[j][0]);
+                        acc[j][1] = fmaf(-bsc.m[0], bs[p][j][1], acc[j][1]);
+                        acc[j][2] = fmaf(-bsc.m[1], bs[p][j][0], acc[j][2]);
+                        acc[j][3] = fmaf(-bsc.m[1], bs[p][j][1], acc[j][3]);
+                    }
+                }
+                if (kb + PF < nkb) load(p, kb + PF);
+            }
+        }
+    }
+}
+
+// Q4_K pass: per super-block, each row's header (d, dmin, 12 scale bytes) is loaded once as 4
+// words and each 32-bit word of quants once per sub-block pair (low nibbles: sub-block 2p, high:
+// 2p + 1); the unrolled sub-block index makes the scale/min extraction constant shifts.  Rows are
+// 16-byte multiples (144 B per 256 inputs), so every load is aligned.
+template <int NT>
+__device__ __forceinline__ void pass_q4k(const uint8_t *row0, const uint8_t *row1, int kb_lo, int nkb, int c,
+                                         const uint4 *const (&xr)[2], const float *const (&bsr)[2][2],
+                                         float (&acc)[2][4]) {
+    constexpr int PF = NT == 1 ? 4 : 2;  // divides 8 and the start (a multiple of 8): slot = sub-block % PF
+    uint4 b[PF][NT][2];
+    float bs[PF][NT][2];
+    auto load = [&](int p, int kb) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            b[p][j][0] = xr[j][8 * kb];
+            b[p][j][1] = xr[j][8 * kb + 4];
+            bs[p][j][0] = bsr[j][0][kb];
+            bs[p][j][1] = bsr[j][1][kb];
+        }
+    };
+#pragma unroll
+    for (int p = 0; p < PF; ++p)
+        if (kb_lo + p < nkb) load(p, kb_lo + p);
+    const __half2 B = __float2half2_rn(1024.f);
+    for (int sb = kb_lo / 8; sb < nkb / 8; ++sb) {
+        uint4 hd[2];  // rows g, g + 8: {d | dmin << 16, scales 0-3, 4-7, 8-11}
+        hd[0] = *reinterpret_cast<const uint4 *>(row0 + 144 * sb);
+        hd[1] = *reinterpret_cast<const uint4 *>(row1 + 144 * sb);
+        float dsup[2], msup[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            dsup[h] = half_bits_to_float(hd[h].x);
+            msup[h] = half_bits_to_float(hd[h].x >> 16);
+        }
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            uint32_t w[2][2];  // rows x (bytes 4c.., bytes 16 + 4c..) of sub-blocks 2pr, 2pr + 1
+            w[0][0] = *reinterpret_cast<const uint32_t *>(row0 + 144 * sb + 16 + 32 * pr + 4 * c);
+            w[0][1] = *reinterpret_cast<const uint32_t *>(row0 + 144 * sb + 32 + 32 * pr + 4 * c);
+            w[1][0] = *reinterpret_cast<const uint32_t *>(row1 + 144 * sb + 16 + 32 * pr + 4 * c);
+            w[1][1] = *reinterpret_cast<const uint32_t *>(row1 + 144 * sb + 32 + 32 * pr + 4 * c);
+#pragma unroll
+            for (int hb = 0; hb < 2; ++hb) {
+                const int j = 2 * pr + hb, kb = 8 * sb + j, slot = j % PF;
+                uint32_t A0[4], A1[4];
+                float dsc[2], msc[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t scv, mnv;  // q4k_scale_min (reference kernel.cu:913-921)
+                    if (j < 4) {
+                        scv = (hd[h].y >> (8 * j)) & 63u;
+                        mnv = (hd[h].z >> (8 * j)) & 63u;
+                    } else {
+                        const int sj = 8 * (j - 4);
+                        scv = ((hd[h].w >> sj) & 0xFu) | (((hd[h].y >> (sj + 6)) & 3u) << 4);
+                        mnv = ((hd[h].w >> (sj + 4)) & 0xFu) | (((hd[h].z >> (sj + 6)) & 3u) << 4);
+                    }
+                    dsc[h] = dsup[h] * (float)scv;  // exact: 11-bit x 6-bit
+                    msc[h] = msup[h] * (float)mnv;
+                    const uint32_t w0 = w[h][0] >> (4 * hb), w1 = w[h][1] >> (4 * hb);
+                    A0[h] = int_pair(w0 & 0x000F000Fu, B);
+                    A0[2 + h] = int_pair((w0 >> 8) & 0x000F000Fu, B);
+                    A1[h] = int_pair(w1 & 0x000F000Fu, B);
+                    A1[2 + h] = int_pair((w1 >> 8) & 0x000F000Fu, B);
+                }
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    float r[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(r, A0, b[slot][t][0].x, b[slot][t][0].y);
+                    mma16816(r, A0, b[slot][t][0].z, b[slot][t][0].w);
+                    mma16816(r, A1, b[slot][t][1].x, b[slot][t][1].y);
+                    mma16816(r, A1, b[slot][t][1].z, b[slot][t][1].w);
+                    acc[t][0] = fmaf(dsc[0], r[0], fmaf(-msc[0], bs[slot][t][0], acc[t][0]));
+                    acc[t][1] = fmaf(dsc[0], r[1], fmaf(-msc[0], bs[slot][t][1], acc[t][1]));
+                    acc[t][2] = fmaf(dsc[1], r[2], fmaf(-msc[1], bs[slot][t][0], acc[t][2]));
+                    acc[t][3] = fmaf(dsc[1], r[3], fmaf(-msc[1], bs[slot][t][1], acc[t][3]));
+                }
+                if (kb + PF < nkb) load(slot, kb + PF);
+            }
+        }
+    }
+}
+
+// Stable bucketing of the (token, route) pairs by expert, one CTA of 1024 threads: bucket e in
+// [0, n) holds the pairs of this call's expert e, bucket n the pairs routed elsewhere, each in
+// routing-table order; off[b] .. off[b + 1] is bucket b's range of `list`.  Chunks of 1024
+// pairs: a pair's place = its bucket's running base + the same-bucket pairs of earlier warps in
+// the chunk + those of earlier lanes in its warp (__match_any_sync).
+constexpr int kBucketMax = 257;  // n_experts <= 256, plus the skipped bucket
+__global__ void __launch_bounds__(1024) moe_bucket_kernel(const int *__restrict__ ids, int npairs, int e_begin,
+                                                          int n, int *__restrict__ off, int *__restrict__ list) {
+    __shared__ int base[kBucketMax + 1];
+    __shared__ unsigned short wcnt[32][kBucketMax];  // per warp of a chunk: pairs per bucket
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nb = n + 1;
+    auto bucket_of = [&](int i) {
+        const int le = ids[i] - e_begin;
+        return (le >= 0 && le < n) ? le : n;
+    };
+    for (int b = tid; b <= nb; b += blockDim.x) base[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < npairs; i += blockDim.x) atomicAdd(&base[bucket_of(i) + 1], 1);  // counts
+    __syncthreads();
+    if (tid == 0) {  // exclusive offsets
+        for (int b = 1; b <= nb; ++b) base[b] += base[b - 1];
+        for (int b = 0; b <= nb; ++b) off[b] = base[b];
+    }
+    __syncthreads();
+    for (int c0 = 0; c0 < npairs; c0 += blockDim.x) {
+        const int i = c0 + tid;
+        const bool valid = i < npairs;
+        const int b = valid ? bucket_of(i) : nb;  // nb: not a pair
+        for (int x = tid; x < 32 * nb; x += blockDim.x) wcnt[x / nb][x % nb] = 0;
+        __syncthreads();
+        const unsigned peers = __match_any_sync(0xffffffffu, b);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        if (valid && rank == 0) wcnt[warp][b] = (unsigned short)__popc(peers);
+        __syncthreads();
+        if (valid) {
+            int before = 0;
+            for (int w = 0; w < warp; ++w) before += wcnt[w][b];
+            list[base[b] + before + rank] = i;
+        }
+        __syncthreads();
+        for (int bb = tid; bb < nb; bb += blockDim.x) {
+            int total = 0;
+            for (int w = 0; w < 32; ++w) total += wcnt[w][bb];
+            base[bb] += total;
+        }
+        __syncthreads();
+    }
+}
 
 template <int FMT, bool SWIGLU>
-__global__ void __launch_bounds__(kMoeThreads) moe_grouped_kernel(const __grid_constant__ MoeArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];  // [4 warps][slab] raw weight rows
+__global__ void __launch_bounds__(kMoeThreads, 2) moe_grouped_kernel(const __grid_constant__ MoeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];  // [4 slabs][16 rows][row_pitch] raw weight rows
+    __shared__ float red[4][32][8];                  // second K half's partial sums, per slab and lane
     __shared__ float su[32][kMoePass + 1];           // SwiGLU: up rows handed to the gate warps
-    __shared__ int plist[4][kMoePass];               // per warp: the pass's (token, route) pairs
+    __shared__ int plist[8][kMoePass];               // per warp: the pass's (token, route) pairs
     __shared__ uint64_t bar[4];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slab_i = warp & 3, khalf = warp >> 2;  // warps w and w + 4 share slab w, one K half each
     const int g = lane >> 2, c = lane & 3;
     const int e = blockIdx.y;
     constexpr int RT = SWIGLU ? 32 : 64;  // output rows per CTA
     const int row_base = blockIdx.x * RT;
 
+    const int lbeg = a.bucket_off[e], lend = a.bucket_off[e + 1];  // this expert's pairs in a.bucket
     if (SWIGLU && e == a.n_experts) {
-        // zero act[(t, r), row_base ..] for routes that go to no expert of this call
-        for (int i = warp; i < a.npairs; i += 4) {
-            const int le = a.ids[i] - a.e_begin;
-            if ((le < 0 || le >= a.n_experts) && row_base + lane < a.rows)
-                a.y[(size_t)i * a.y_stride + row_base + lane] = 0.f;
-        }
+        // zero act[(t, r), row_base ..] for the routes that go to no expert of this call
+        for (int l = lbeg + warp; l < lend; l += 8)
+            if (row_base + lane < a.rows) a.y[(size_t)a.bucket[l] * a.y_stride + row_base + lane] = 0.f;
         return;
     }
-    // skip experts no route chose (every warp reaches the same answer; nothing is in flight yet)
-    {
-        bool any = false;
-        for (int i0 = 0; i0 < a.npairs && !any; i0 += 32) {
-            const int i = i0 + lane;
-            any = __any_sync(0xffffffffu, i < a.npairs && route_is(a.ids, i, a.e_begin, e));
-        }
-        if (!any) return;
-    }
-    // ---- stage this warp's 16 rows (one contiguous byte range) ----
-    const int mat = SWIGLU ? (warp >> 1) : 0;
-    const int wrow0 = row_base + 16 * (SWIGLU ? (warp & 1) : warp);
+    if (lbeg == lend) return;  // no route chose this expert (nothing is in flight yet)
+    // ---- slab s: 16 rows, one bulk copy per row into a slot of a.row_pitch bytes (warp s issues) ----
+    // (pitch = 16 mod 32: rows g = 0..7 of a quad's 4-byte loads fall in 32 distinct banks)
+    const int mat = SWIGLU ? (slab_i >> 1) : 0;
+    const int wrow0 = row_base + 16 * (SWIGLU ? (slab_i & 1) : slab_i);
     int nr = min(16, a.rows - wrow0);
     const size_t rb = a.rb[mat];
-    uint8_t *slab = smem + (size_t)warp * a.slab_bytes;
-    int shift = 0;
-    if (nr > 0) {
-        const uint8_t *src = a.w[mat] + (size_t)e * a.eb[mat] + (size_t)wrow0 * rb;
-        const size_t bytes = (size_t)nr * rb;
-        const uintptr_t lo = reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15);
-        const uintptr_t end = reinterpret_cast<uintptr_t>(src) + bytes, hi = end & ~uintptr_t(15);
-        shift = (int)(reinterpret_cast<uintptr_t>(src) - lo);
-        if (lane == 0) {
-            mbar_init(&bar[warp], 1);
-            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-            mbar_arrive_expect_tx(&bar[warp], (uint32_t)(hi - lo));
-            if (hi > lo)
-                bulk_g2s(slab, reinterpret_cast<const void *>(lo), (uint32_t)(hi - lo), &bar[warp],
-                         l2_evict_first_policy());
+    const int P = a.row_pitch;
+    uint8_t *slab = smem + (size_t)slab_i * 16 * P;
+    const uint8_t *wbase = a.w[mat] + (size_t)e * a.eb[mat] + (size_t)wrow0 * rb;
+    uintptr_t lo = 0, hi = 0, end = 0;
+    if (khalf == 0 && nr > 0) {
+        // lane r < nr copies row r: [floor16(start), floor16(end)) by the TMA engine, the < 16 bytes
+        // after that by plain loads
+        if (lane < nr) {
+            const uintptr_t st = reinterpret_cast<uintptr_t>(wbase + (size_t)lane * rb);
+            lo = st & ~uintptr_t(15);
+            end = st + rb;
+            hi = end & ~uintptr_t(15);
         }
-        if (lane < (int)(end - hi)) slab[(hi - lo) + lane] = reinterpret_cast<const uint8_t *>(hi)[lane];
-        __syncwarp();
-        if (!mbar_wait(&bar[warp], 0u, a.err, kErrWaitFull)) {
-            mbar_wait(&bar[warp], 0u, nullptr, 0);  // never leave with the copy in flight
-            nr = 0;                                 // rows not staged: nothing is computed or stored
+        const uint32_t tx = __reduce_add_sync(0xffffffffu, (uint32_t)(hi - lo));
+        if (lane == 0) {
+            mbar_init(&bar[slab_i], 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            mbar_arrive_expect_tx(&bar[slab_i], tx);
         }
     }
-    const uint8_t *row0 = slab + shift + (size_t)g * rb, *row1 = row0 + 8 * rb;
+    __syncthreads();  // barriers initialised before the other K half waits on them
+    if (khalf == 0 && lane < nr) {
+        uint8_t *dst = slab + (size_t)lane * P;
+        if (hi > lo)
+            bulk_g2s(dst, reinterpret_cast<const void *>(lo), (uint32_t)(hi - lo), &bar[slab_i],
+                     l2_evict_first_policy());
+        for (uintptr_t q = hi; q < end; ++q) dst[q - lo] = *reinterpret_cast<const uint8_t *>(q);
+    }
+    __syncthreads();  // the tails' plain stores, for both K halves
+    if (nr > 0 && !mbar_wait(&bar[slab_i], 0u, a.err, kErrWaitFull)) {
+        mbar_wait(&bar[slab_i], 0u, nullptr, 0);  // never leave with the copies in flight
+        nr = 0;                                   // rows not staged: nothing is computed or stored
+    }
+    const int sh0 = (int)(reinterpret_cast<uintptr_t>(wbase + (size_t)g * rb) & 15);
+    const int sh1 = (int)(reinterpret_cast<uintptr_t>(wbase + (size_t)(g + 8) * rb) & 15);
+    const uint8_t *row0 = slab + (size_t)g * P + sh0, *row1 = slab + (size_t)(g + 8) * P + sh1;
     const int nkb = a.K / 32;
+    // K halves (Q4_K on super-block boundaries)
+    const int unit = FMT == kQ4_K ? 8 : 1;
+    const int kmid = ((nkb / unit) / 2) * unit;
+    const int kb_lo = khalf ? kmid : 0, kb_hi = khalf ? nkb : kmid;
 
-    // ---- passes of up to 32 (token, route) pairs of expert e, in routing-table order ----
-    int pos = 0;
-    for (;;) {
-        int cnt = 0;
-        while (cnt < kMoePass && pos < a.npairs) {
-            const int i = pos + lane;
-            const bool m = i < a.npairs && route_is(a.ids, i, a.e_begin, e);
-            const unsigned bal = __ballot_sync(0xffffffffu, m);
-            const int nm = __popc(bal), take = min(nm, kMoePass - cnt);
-            const int rank = __popc(bal & ((1u << lane) - 1u));
-            if (m && rank < take) plist[warp][cnt + rank] = i;
-            pos += take < nm ? (int)__fns(bal, 0, take + 1) : 32;
-            cnt += take;
-        }
+    // ---- passes of up to 16 (token, route) pairs of expert e, in routing-table order ----
+    for (int l0 = lbeg; l0 < lend; l0 += kMoePass) {
+        const int cnt = min(kMoePass, lend - l0);
+        if (lane < cnt) plist[warp][lane] = a.bucket[l0 + lane];
         __syncwarp();
-        if (cnt == 0) break;
         const int nt = (cnt + 7) >> 3;
-        const uint4 *xr[4];     // B operand rows: token slot 8j + g
-        const float *bsr[4][2];  // block sums of the accumulator's token slots 8j + 2c, 8j + 2c + 1
+        const uint4 *xr[2];     // B operand rows: token slot 8j + g
+        const float *bsr[2][2];  // block sums of the accumulator's token slots 8j + 2c, 8j + 2c + 1
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 2; ++j) {
             const int p = plist[warp][min(8 * j + g, cnt - 1)];
             xr[j] = a.xq + (size_t)(SWIGLU ? p / a.k : p) * (a.K / 4) + c;
 #pragma unroll
@@ -279,49 +467,37 @@ __global__ void __launch_bounds__(kMoeThreads) moe_grouped_kernel(const __grid_c
                 bsr[j][q] = a.bsum + (size_t)(SWIGLU ? p2 / a.k : p2) * (a.K / 32);
             }
         }
-        float acc[4][4];
+        float acc[2][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-        if (nr > 0) {
-#pragma unroll 2
-            for (int kb = 0; kb < nkb; ++kb) {
-                uint4 b[4][2];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (j < nt) {
-                        b[j][0] = xr[j][8 * kb];      // step 0 of the block: 4 words per 16 elements
-                        b[j][1] = xr[j][8 * kb + 4];  // step 1
-                    }
-                uint32_t A0[4], A1[4];
-                BlockScale bsc;
-                decode_block<FMT>(row0, row1, kb, c, A0, A1, bsc);
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (j < nt) {
-                        float t[4] = {0.f, 0.f, 0.f, 0.f};  // this block's integer-weight dot products
-                        mma16816(t, A0, b[j][0].x, b[j][0].y);
-                        mma16816(t, A0, b[j][0].z, b[j][0].w);
-                        mma16816(t, A1, b[j][1].x, b[j][1].y);
-                        mma16816(t, A1, b[j][1].z, b[j][1].w);
-                        acc[j][0] = fmaf(bsc.d[0], t[0], acc[j][0]);
-                        acc[j][1] = fmaf(bsc.d[0], t[1], acc[j][1]);
-                        acc[j][2] = fmaf(bsc.d[1], t[2], acc[j][2]);
-                        acc[j][3] = fmaf(bsc.d[1], t[3], acc[j][3]);
-                        if (FMT == kQ4_K) {
-                            const float s0 = bsr[j][0][kb], s1 = bsr[j][1][kb];
-                            acc[j][0] = fmaf(-bsc.m[0], s0, acc[j][0]);
-                            acc[j][1] = fmaf(-bsc.m[0], s1, acc[j][1]);
-                            acc[j][2] = fmaf(-bsc.m[1], s0, acc[j][2]);
-                            acc[j][3] = fmaf(-bsc.m[1], s1, acc[j][3]);
-                        }
-                    }
+        for (int j = 0; j < 2; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        if (nr > 0 && kb_lo < kb_hi) {
+            if (FMT == kQ4_K) {
+                if (nt == 1) pass_q4k<1>(row0, row1, kb_lo, kb_hi, c, xr, bsr, acc);
+                else pass_q4k<2>(row0, row1, kb_lo, kb_hi, c, xr, bsr, acc);
+            } else {
+                if (nt == 1) pass_blocks<FMT, 1>(row0, row1, kb_lo, kb_hi, c, xr, bsr, acc);
+                else pass_blocks<FMT, 2>(row0, row1, kb_lo, kb_hi, c, xr, bsr, acc);
             }
         }
-        // ---- epilogue: acc[j] = rows (g, g + 8) x token slots (8j + 2c, 8j + 2c + 1) ----
-        if (SWIGLU) {
-            if (warp >= 2) {
+        // ---- the second K half's partial sums join the first's (fixed order: deterministic) ----
+        if (khalf) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) red[slab_i][lane][4 * j + q] = acc[j][q];
+        }
+        __syncthreads();
+        if (!khalf) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[j][q] += red[slab_i][lane][4 * j + q];
+        }
+        // ---- epilogue (first-half warps): acc[j] = rows (g, g + 8) x token slots (8j + 2c, 8j + 2c + 1) ----
+        if (SWIGLU) {
+            if (warp == 2 || warp == 3) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
                     su[16 * (warp & 1) + g][8 * j + 2 * c] = acc[j][0];
                     su[16 * (warp & 1) + g][8 * j + 2 * c + 1] = acc[j][1];
                     su[16 * (warp & 1) + g + 8][8 * j + 2 * c] = acc[j][2];
@@ -331,7 +507,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_grouped_kernel(const __grid_c
             __syncthreads();
             if (warp < 2) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
+                for (int j = 0; j < 2; ++j)
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const int slot = 8 * j + 2 * c + (q & 1), rr = g + 8 * (q >> 1);
@@ -343,10 +519,9 @@ __global__ void __launch_bounds__(kMoeThreads) moe_grouped_kernel(const __grid_c
                         }
                     }
             }
-            __syncthreads();
-        } else {
+        } else if (!khalf) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < 2; ++j)
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const int slot = 8 * j + 2 * c + (q & 1), rr = g + 8 * (q >> 1);
@@ -356,7 +531,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_grouped_kernel(const __grid_c
                     }
                 }
         }
-        __syncwarp();
+        __syncthreads();  // red, su and plist are rewritten by the next pass
     }
 }
 
@@ -387,7 +562,7 @@ __global__ void moe_local_ids_kernel(const int *__restrict__ ids, int e_begin, i
 
 template <int FMT, bool SWIGLU>
 cudaError_t grouped_launch_t(const MoeArgs &a, cudaStream_t s) {
-    const size_t smem = 4 * a.slab_bytes;
+    const size_t smem = (size_t)4 * 16 * a.row_pitch;  // 4 slabs of 16 rows
     cudaError_t e = cudaFuncSetAttribute(moe_grouped_kernel<FMT, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
@@ -404,13 +579,26 @@ cudaError_t moe_xprep_launch(const float *x, int64_t x_stride, uint4 *xq, float 
     return cudaGetLastError();
 }
 
+cudaError_t moe_bucket_launch(const int *ids, int npairs, int e_begin, int n_experts, int *off, int *list,
+                              cudaStream_t s) {
+    moe_bucket_kernel<<<1, 1024, 0, s>>>(ids, npairs, e_begin, n_experts, off, list);
+    return cudaGetLastError();
+}
+int moe_max_experts() { return kBucketMax - 1; }
+
 cudaError_t moe_local_ids_launch(const int *ids, int e_begin, int n_experts, int *out, int n, cudaStream_t s) {
     moe_local_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, e_begin, n_experts, out, n);
     return cudaGetLastError();
 }
 
-size_t moe_slab_bytes(size_t row_bytes) { return 16 * row_bytes + 16; }
-size_t moe_max_slab_bytes() { return (232448 - 8192) / 4; }  // dynamic shared memory of 4 slabs
+// Shared-memory slot of one staged row: the row plus up to 15 bytes of alignment shift, rounded
+// to 16 bytes and made = 16 mod 32 (bank spread of the 8 rows a quad of lanes reads at once).
+int moe_row_pitch(size_t row_bytes) {
+    int p = (int)((row_bytes + 15 + 15) & ~size_t(15));
+    if (p % 32 == 0) p += 16;
+    return p;
+}
+int moe_max_row_pitch() { return (232448 - 8192) / 64; }  // 4 warps x 16 rows of dynamic shared memory
 
 cudaError_t moe_grouped_launch(const MoeArgs &a, int fmt, bool swiglu, cudaStream_t s) {
     switch (fmt) {

@@ -244,8 +244,9 @@ QL_API int ql_moe_router_topk(const float *router_logits, int *top_idx, float *t
  *   act[t * k + r][f] = SiLU(Wg[e][f] . x_t) * (Wu[e][f] . x_t), 0 for a skipped route,
  * x_t = x + t * x_stride, act rows ffn_dim floats apart.  Numerics as QL_PATH_TENSOR: each
  * activation row (times a power of two) and each dequantized weight rounded to f16, fp32
- * accumulation on the tensor cores.  Q4_0, Q5_0, Q8_0, Q4_K; rows up to ~3.5 KB run grouped
- * (16 rows per warp in shared memory), longer rows run the per-token indexed launches. */
+ * accumulation on the tensor cores.  Q4_0, Q5_0, Q8_0, Q4_K; rows up to ~3.5 KB and up to 256
+ * experts per call run grouped (16 rows per warp in shared memory), others run the per-token
+ * indexed launches. */
 QL_API int ql_moe_swiglu_grouped(int32_t quant_type, const uint8_t *gate_weight, const uint8_t *up_weight,
                                  size_t gate_expert_bytes, size_t up_expert_bytes, size_t gate_row_bytes,
                                  size_t up_row_bytes, const float *x, int64_t x_stride, const int *expert_ids,

@@ -91,7 +91,7 @@ def test_grouped_deepseek_shapes(e_begin, n):
     x = _x(304, T, H)
     ids = _routes(305, T, k, E)
     act = grouped_swiglu(tg, g, u, F * rbg, rbg, x, ids, e_begin, n, F, H)
-    assert Q.last_launch_count() == 2  # activation prep + one grouped launch
+    assert Q.last_launch_count() == 3  # activation prep + expert buckets + one grouped launch
     ref = oracle_swiglu(tg, g, u, F * rbg, rbg, x, ids, e_begin, n, F, H)
     skipped = _local(ids, e_begin, n) < 0
     assert np.all(act[skipped] == 0.0)
@@ -102,7 +102,7 @@ def test_grouped_deepseek_shapes(e_begin, n):
     out0 = _x(307, T, H)
     a2 = ref.reshape(T * k, F).astype(np.float32)
     got = grouped_down(td, d, H * rbd, rbd, a2, ids, e_begin, n, rw, out0, H, F)
-    assert Q.last_launch_count() == 3  # activation prep + grouped launch + ordered combine
+    assert Q.last_launch_count() == 4  # activation prep + expert buckets + grouped launch + ordered combine
     want = oracle_down(td, d, H * rbd, rbd, a2, ids, e_begin, n, rw, out0, H, F)
     err = rel_l2(got - out0, want - out0)
     print(f"grouped down + ordered combine (experts {e_begin}..{e_begin + n - 1}): rel_l2 {err:.2e}")
