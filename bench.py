@@ -586,6 +586,59 @@ def run_chain_kernel(args):
     return 0
 
 
+def run_moe_kernel(args):
+    """--kernel-only moe_swiglu / moe_down: one MoE layer's grouped routed experts at DeepSeek-V2-Lite
+    shapes (64 experts, gate/up Q4_K 1408 x 2048, down Q5_0 2048 x 1408, 64 tokens x top-6 routes
+    drawn without repeats per token), the ncu target of the grouped kernel.  One expert set (333 MB of
+    weights, over twice the L2) per layer call."""
+    import torch
+    import blog_b200 as Q
+    torch.cuda.init()
+    Q.init(0)
+    Q.set_stream(torch.cuda.current_stream().cuda_stream)
+    T, k = 64, DS_TOPK
+    rbg, rbd = Q.row_bytes(QK, DS_H), Q.row_bytes(Q50, DS_FE)
+
+    def synth(t, rows, rb, kk, seed):
+        w = torch.empty((rows, rb), dtype=torch.uint8, device="cuda")
+        Q.synth_quantized(t, seed, rows, kk, 0.02, w.data_ptr())
+        return w
+    eg, eu = synth(QK, DS_E * DS_FE, rbg, DS_H, 1), synth(QK, DS_E * DS_FE, rbg, DS_H, 2)
+    ed = synth(Q50, DS_E * DS_H, rbd, DS_FE, 3)
+    gen = torch.Generator().manual_seed(0)
+    ids = torch.stack([torch.randperm(DS_E, generator=gen)[:k] for _ in range(T)]).to(torch.int32).cuda()
+    rw = torch.rand(T, k, generator=gen).cuda()
+    x = torch.randn(T, DS_H, device="cuda")
+    act = torch.randn(T * k, DS_FE, device="cuda")
+    out = torch.zeros(T, DS_H, device="cuda")
+    if args.kernel_only == "moe_swiglu":
+        nbytes = 2 * eg.numel()
+        run = lambda: Q.moe_swiglu_grouped(QK, eg.data_ptr(), eu.data_ptr(), DS_FE * rbg, DS_FE * rbg, rbg, rbg,
+                                           x.data_ptr(), DS_H, ids.data_ptr(), 0, DS_E, act.data_ptr(), T, k,
+                                           DS_FE, DS_H)
+    else:
+        nbytes = ed.numel()
+        run = lambda: Q.moe_down_grouped_accum_ordered(Q50, ed.data_ptr(), DS_H * rbd, rbd, act.data_ptr(),
+                                                       ids.data_ptr(), 0, DS_E, rw.data_ptr(), out.data_ptr(), DS_H,
+                                                       T, k, DS_H, DS_FE)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    Q.check_device()
+    us = e0.elapsed_time(e1) / args.steps * 1e3
+    hbm, _ = peaks()
+    print(json.dumps({"kernel_only": args.kernel_only, "avg_us": us, "weight_bytes": nbytes,
+                      "GBps": nbytes / us / 1e3, "frac_hbm": nbytes / us / 1e3 / hbm,
+                      "launches": Q.last_launch_count()}), flush=True)
+    return 0
+
+
 def run_kernel_only(args):
     """Times one kernel of the step at its bench shape (the ncu profiling target):
     swiglu = fused RMSNorm + gate/up SwiGLU (18944 x 3584 x 2), down = down + residual
@@ -594,6 +647,8 @@ def run_kernel_only(args):
     import blog_b200 as Q
     if args.kernel_only.startswith("prefill_"):
         return run_prefill_kernel(args)
+    if args.kernel_only.startswith("moe_"):
+        return run_moe_kernel(args)
     if args.kernel_only in ("chain", "bchain"):
         return run_chain_kernel(args)
     torch.cuda.init()
@@ -784,19 +839,12 @@ class MoEStack:
                                self.lnf.data_ptr(), EPS, 0, self.tok.data_ptr(), None)
 
 
-def run_moe(args):
-    """--moe: batch-64 decode steps of the MoE stack, expert parallel over the ranks (one JSON line)."""
-    import datetime
-    import torch
-    import blog_b200 as Q
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                             timeout=datetime.timedelta(seconds=120))
-    Q.init(local)
+def moe_measure(Q, torch, rank, world, steps, warmup):
+    """Batch-64 decode steps of the MoE stack (DeepSeek-V2-Lite shapes), expert parallel over the
+    ranks: the grouped routed path and the reference's per-token loop, each captured in a CUDA graph
+    and timed on the device (max over ranks), plus one layer's routed output both ways from the same
+    router input.  Every rank calls it (the steps hold one all-reduce per MoE layer).  Returns the
+    fields of a JSON object (rank 0) or None."""
     T = 64
     st = MoEStack(Q, torch, rank, world, T)
     s = torch.cuda.Stream()
@@ -811,18 +859,18 @@ def run_moe(args):
             with torch.cuda.graph(g, stream=s):
                 st.step()
             graphs[grouped] = g
-            for _ in range(max(args.warmup, 3)):
+            for _ in range(max(warmup, 3)):
                 g.replay()
             torch.cuda.synchronize()
             if world > 1:
                 torch.distributed.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(s)
-            for _ in range(args.steps):
+            for _ in range(steps):
                 g.replay()
             e1.record(s)
             torch.cuda.synchronize()
-            t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+            t = torch.tensor([e0.elapsed_time(e1) / steps], device="cuda")
             if world > 1:
                 torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms[grouped] = float(t[0])
@@ -844,30 +892,50 @@ def run_moe(args):
               "note": "after all layers, routes whose top-k scores nearly tie can flip between the two paths"}
     hbm, _ = peaks()
     wb = st.weight_bytes()
+    res = None
     if rank == 0:
         gbs = wb / (ms[True] / 1e3) / 1e9
-        print(json.dumps({"metric": "moe decode tokens/s (DeepSeek-V2-Lite shapes, batch 64)",
-                          "value": T / (ms[True] / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-                          "ms_per_step": ms[True], "parallelism": f"ep{world}", "weight_bytes_per_rank": wb,
-                          "routed_path": "grouped: per layer one SwiGLU and one down + ordered-combine call over "
-                                         "all (token, route) pairs, each expert's rows read once (mma.sync: exact "
-                                         "integer quants x two-limb f16 activations, fp32 block scales)",
-                          "per_token_path": {"tokens_per_s": T / (ms[False] / 1e3), "ms_per_step": ms[False],
-                                             "routed_path": "the reference's per-token loop: indexed SwiGLU and "
-                                                            "ordered down launches per token"},
-                          "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                                       "frac": gbs / hbm,
-                                       "bytes": "all of the rank's weights once per step (64 tokens x 6 routes "
-                                                "reach nearly every expert of every layer)"},
-                          "parity": parity, "dtype": "f32 (routed: fp32-class, 1e-7 of the oracle); attention "
-                                                     "stand-ins and shared experts on the f16 tensor-core GEMM",
-                          "data": "synthetic"}), flush=True)
-    g = None
+        res = {"value": T / (ms[True] / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+               "ms_per_step": ms[True], "parallelism": f"ep{world}", "weight_bytes_per_rank": wb,
+               "routed_path": "grouped: per layer one SwiGLU and one down + ordered-combine call over all (token, "
+                              "route) pairs, each expert's rows read once (mma.sync: exact integer quants x "
+                              "two-limb f16 activations, fp32 block scales)",
+               "per_token_path": {"tokens_per_s": T / (ms[False] / 1e3), "ms_per_step": ms[False],
+                                  "routed_path": "the reference's per-token loop: indexed SwiGLU and ordered "
+                                                 "down launches per token"},
+               "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                            "bytes": "all of the rank's weights once per step (64 tokens x 6 routes reach nearly "
+                                     "every expert of every layer)"},
+               "parity": parity, "dtype": "f32 (routed: fp32-class, 1e-7 of the oracle); attention stand-ins and "
+                                          "shared experts on the f16 tensor-core GEMM",
+               "data": "synthetic"}
     graphs.clear()
-    del g
+    g = None
+    del st
     torch.cuda.synchronize()
+    torch.cuda.empty_cache()
     if world > 1:
         torch.distributed.barrier()
+    return res
+
+
+def run_moe(args):
+    """--moe: the MoE stack alone (one JSON line)."""
+    import datetime
+    import torch
+    import blog_b200 as Q
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                             timeout=datetime.timedelta(seconds=120))
+    Q.init(local)
+    res = moe_measure(Q, torch, rank, world, args.steps, args.warmup)
+    if rank == 0:
+        print(json.dumps({"metric": "moe decode tokens/s (DeepSeek-V2-Lite shapes, batch 64)", **res}), flush=True)
+    if world > 1:
         torch.distributed.destroy_process_group()
     return 0
 
@@ -978,10 +1046,11 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-models", action="store_true", help="skip the Qwen2-0.5B Q8_0 and Qwen2-72B Q4_0 lines")
     ap.add_argument("--no-sweep", action="store_true", help="skip the isolated quantized-linear sweep (configs[1])")
-    ap.add_argument("--moe", action="store_true", help="DeepSeek-V2-Lite-shape MoE decode, expert parallel")
+    ap.add_argument("--moe", action="store_true", help="only the DeepSeek-V2-Lite-shape MoE decode line")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE object of the main line")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
-                                              "prefill_qkv", "prefill_o", "prefill_swiglu", "chain", "bchain"],
+                                              "prefill_qkv", "prefill_o", "prefill_swiglu", "chain", "bchain", "moe_swiglu", "moe_down"],
                     help="time one kernel of the step at its bench shape (profiling target)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers for --kernel-only chain")
@@ -1214,6 +1283,8 @@ def main():
         extra["qwen2_72b_q4_0"] = (QWEN2_72B, measure(1, QWEN2_72B))
     rp = None if args.no_prefill else measure_prefill(args.prefill_tokens)
     sweep = run_sweep(Q, torch) if (world == 1 and not args.no_sweep) else None
+    # DeepSeek-V2-Lite-shape MoE decode at batch 64, expert parallel over the ranks
+    rmoe = None if args.no_moe else moe_measure(Q, torch, rank, world, min(args.steps, 20), args.warmup)
 
     if rank == 0:
         hbm, peak_kind = peaks()
@@ -1292,6 +1363,8 @@ def main():
                          "parallelism": f"tp{world}", "launches_per_step": r["launches"],
                          "path": "per-op streaming GEMV launches in a CUDA graph"
                                  + (", NCCL all-reduce after o and down" if world > 1 else "")}
+        if rmoe is not None:
+            line["moe_deepseek_v2_lite"] = rmoe
         if world == 1 and not args.no_cpu_baseline:
             v, _, info = cpu_reference_steps(2, 1, budget_s=30.0)
             line["cpu_baseline"] = dict(info, value=v, unit="tokens/s")
