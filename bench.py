@@ -639,6 +639,60 @@ def run_moe_kernel(args):
     return 0
 
 
+def run_attn_kernel(args):
+    """--kernel-only attn: decode attention of one token at position --tokens - 1 over each of 28
+    layers' KV caches in turn (Qwen2-7B: 28 query heads, 4 KV heads, head_dim 128, f32 caches of
+    --tokens positions; 28 caches exceed the L2), through ql_full_attention_attend, and the
+    reference's own kernel (oracle/_ref) on the same caches when it is built.  Bytes per call =
+    the K and V rows of the window."""
+    import torch
+    import blog_b200 as Q
+    torch.cuda.init()
+    Q.init(0)
+    Q.set_stream(torch.cuda.current_stream().cuda_stream)
+    nh, kvh, hd, ms, nl = N_Q, N_KV, HEAD, args.tokens, LAYERS
+    pos = ms - 1
+    caches = [(torch.randn(ms, kvh * hd, device="cuda") * 0.5, torch.randn(ms, kvh * hd, device="cuda"))
+              for _ in range(nl)]
+    q = torch.randn(nh * hd, device="cuda")
+    gate = torch.randn(nh * hd, device="cuda")
+    out = torch.empty(nh * hd, device="cuda")
+    p = torch.full((1,), pos, dtype=torch.int32, device="cuda")
+    nbytes = 2 * (pos + 1) * kvh * hd * 4
+
+    def timed(fn):
+        for i in range(max(args.warmup, 3)):
+            fn(i % nl)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            fn(i % nl)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps * 1e3
+    us = timed(lambda i: Q.full_attention_attend(q.data_ptr(), gate.data_ptr(), caches[i][0].data_ptr(),
+                                                 caches[i][1].data_ptr(), False, out.data_ptr(), nh, kvh, hd, ms,
+                                                 p.data_ptr()))
+    Q.check_device()
+    hbm, _ = peaks()
+    res = {"kernel_only": "attn", "positions": pos + 1, "avg_us": us, "kv_bytes": nbytes,
+           "GBps": nbytes / us / 1e3, "frac_hbm": nbytes / us / 1e3 / hbm, "launches": Q.last_launch_count()}
+    try:
+        import oracle as O
+        R = O.ref_lib()
+    except Exception:
+        R = None
+    if R is not None:
+        R.ref_set_stream(torch.cuda.current_stream().cuda_stream)
+        rus = timed(lambda i: R.ref_full_attention_attend(q.data_ptr(), gate.data_ptr(), caches[i][0].data_ptr(),
+                                                          caches[i][1].data_ptr(), 0, out.data_ptr(), nh, kvh, hd, ms,
+                                                          p.data_ptr()))
+        res["reference_kernel_us"] = rus
+    print(json.dumps(res), flush=True)
+    return 0
+
+
 def run_kernel_only(args):
     """Times one kernel of the step at its bench shape (the ncu profiling target):
     swiglu = fused RMSNorm + gate/up SwiGLU (18944 x 3584 x 2), down = down + residual
@@ -649,6 +703,8 @@ def run_kernel_only(args):
         return run_prefill_kernel(args)
     if args.kernel_only.startswith("moe_"):
         return run_moe_kernel(args)
+    if args.kernel_only == "attn":
+        return run_attn_kernel(args)
     if args.kernel_only in ("chain", "bchain"):
         return run_chain_kernel(args)
     torch.cuda.init()
@@ -1050,7 +1106,7 @@ def main():
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE object of the main line")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
-                                              "prefill_qkv", "prefill_o", "prefill_swiglu", "chain", "bchain", "moe_swiglu", "moe_down"],
+                                              "prefill_qkv", "prefill_o", "prefill_swiglu", "chain", "bchain", "moe_swiglu", "moe_down", "attn"],
                     help="time one kernel of the step at its bench shape (profiling target)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers for --kernel-only chain")

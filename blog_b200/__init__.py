@@ -53,6 +53,8 @@ SIGNATURES = {
     "ql_quant_swiglu_indexed": (I, [I32, P, P, SZ, SZ, SZ, SZ, P, P, P, I, I, I]),
     "ql_quant_down_f32_indexed_accum_ordered": (I, [I32, P, SZ, SZ, P, P, P, P, I, I, I]),
     "ql_moe_router_topk": (I, [P, P, P, I, I, I, F]),
+    "ql_full_attention_attend": (I, [P, P, P, P, I, P, I, I, I, I, P]),
+    "ql_full_attention_attend_batch": (I, [P, P, P, P, I, P, I, I, I, I, I, I]),
     "ql_moe_swiglu_grouped": (I, [I32, P, P, SZ, SZ, SZ, SZ, P, I64, P, I, I, P, I, I, I, I]),
     "ql_moe_down_grouped_accum_ordered": (I, [I32, P, SZ, SZ, P, P, I, I, P, P, I64, I, I, I, I]),
     "ql_quant_embedding": (I, [I32, P, P, P, SZ, I, I]),
@@ -305,6 +307,17 @@ def quant_down_f32_indexed_accum_ordered(t, dw, deb, drb, act, ids, rw, out, k, 
 
 def moe_router_topk(logits, idx, w, tokens, n_experts, k, scale):
     _call("ql_moe_router_topk", logits, idx, w, tokens, n_experts, k, scale)
+
+
+def full_attention_attend(q, gate, kc, vc, kv_bf16, attn, n_heads, kv_heads, head_dim, max_seq_len, pos_dev):
+    _call("ql_full_attention_attend", q, gate, kc, vc, int(kv_bf16), attn, n_heads, kv_heads, head_dim, max_seq_len,
+          pos_dev)
+
+
+def full_attention_attend_batch(q, gate, kc, vc, kv_bf16, attn, tokens, n_heads, kv_heads, head_dim, max_seq_len,
+                                start_pos):
+    _call("ql_full_attention_attend_batch", q, gate, kc, vc, int(kv_bf16), attn, tokens, n_heads, kv_heads, head_dim,
+          max_seq_len, start_pos)
 
 
 def moe_swiglu_grouped(t, gw, uw, geb, ueb, grb, urb, x, x_stride, ids, expert_begin, n_experts, act, tokens, k,

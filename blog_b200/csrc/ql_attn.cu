@@ -1,0 +1,382 @@
+// Causal decode attention with an output gate over a KV cache (the reference's
+// full_attention_attend{,_batch}, kernel.cu:355-490 / launch.cu:676-709):
+//   out_h = softmax_j((q_h . k_j) / sqrt(head_dim)) . v_j * sigmoid(gate_h),  j = 0..pos,
+// cache layout [max_seq_len][kv_heads][head_dim], f32 or bf16.
+//
+// The reference runs one CTA per query head over all keys, so the 7 query heads of a GQA group
+// (Qwen2-7B: 28 / 4) each read the group's keys and values, and one CTA per head leaves most SMs
+// idle.  Here a CTA takes one KV head and one split of the keys (flash-decoding): it loads each
+// 64-key tile of K and V into shared memory once for all the group's query heads, keeps a running
+// max / sum / weighted value per head, and writes them as a partial; a second launch merges the
+// splits (max-rescaled sums) and applies the gate.  The split count follows the cache length (so
+// the grid is fixed for a CUDA graph) and each CTA sizes its range from the device-side position.
+#include <cuda_bf16.h>
+
+#include <type_traits>
+
+#include "ql_attn.cuh"
+#include "ql_common.cuh"
+
+namespace ql {
+namespace {
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnTile = 64;        // keys per shared-memory tile
+constexpr int kAttnMaxGroup = 16;    // query heads per KV head on the head_dim-specialised kernels
+constexpr int kAttnMaxSplits = 512;  // key splits per (token, KV head)
+
+template <typename KvT>
+__device__ __forceinline__ float kv_f32(KvT v);
+template <>
+__device__ __forceinline__ float kv_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float kv_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Key range of one split: equal ranges rounded to whole tiles.
+__device__ __forceinline__ void split_range(const AttnArgs &a, int split, int tok, int &j0, int &j1) {
+    const int pos = (a.pos_dev != nullptr ? *a.pos_dev : a.start_pos) + tok;
+    const int n_keys = min(pos + 1, a.max_seq_len);
+    const int per = ((n_keys + a.splits - 1) / a.splits + kAttnTile - 1) / kAttnTile * kAttnTile;
+    j0 = min(split * per, n_keys);
+    j1 = min(j0 + per, n_keys);
+}
+
+// Online softmax over one tile's scores p[G][kAttnTile] (a warp per head): p <- exp(s - m_new),
+// running max m, running sum l, and the rescale factor of the earlier terms in corr.
+__device__ __forceinline__ void tile_softmax(float *p_s, float *m_s, float *l_s, float *c_s, int G, int nt, int warp,
+                                             int lane) {
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+        float *pg = p_s + g * kAttnTile;
+        float tmax = -INFINITY;
+        for (int jj = lane; jj < kAttnTile; jj += 32) tmax = fmaxf(tmax, pg[jj]);
+        for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+        const float m_old = m_s[g], m_new = fmaxf(m_old, tmax);
+        float tsum = 0.f;
+        for (int jj = lane; jj < kAttnTile; jj += 32) {
+            const float pv = jj < nt ? expf(pg[jj] - m_new) : 0.f;
+            pg[jj] = pv;
+            tsum += pv;
+        }
+        for (int o = 16; o > 0; o >>= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, o);
+        if (lane == 0) {
+            const float corr = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+            c_s[g] = corr;
+            l_s[g] = l_s[g] * corr + tsum;
+            m_s[g] = m_new;
+        }
+    }
+}
+
+// Any head_dim (<= 256).  Shared memory: q[G][hd] | acc[G][hd] | K[kAttnTile][hd + 1] |
+// V[kAttnTile][hd] | p[G][kAttnTile] | m, l, corr[G].
+template <typename KvT>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const int hd = a.head_dim, G = a.n_heads / a.kv_heads;
+    float *q_s = sm, *acc_s = q_s + G * hd, *k_s = acc_s + G * hd, *v_s = k_s + kAttnTile * (hd + 1);
+    float *p_s = v_s + kAttnTile * hd, *m_s = p_s + G * kAttnTile, *l_s = m_s + G, *c_s = l_s + G;
+    const int split = blockIdx.x, kh = blockIdx.y, tok = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int j0, j1;
+    split_range(a, split, tok, j0, j1);
+    const float scale = rsqrtf((float)hd);
+    const KvT *kc = static_cast<const KvT *>(a.key_cache), *vc = static_cast<const KvT *>(a.value_cache);
+
+    const size_t q_base = ((size_t)tok * a.n_heads + (size_t)kh * G) * hd;  // the group's heads are adjacent
+    for (int i = tid; i < G * hd; i += kAttnThreads) {
+        q_s[i] = a.q[q_base + i];
+        acc_s[i] = 0.f;
+    }
+    if (tid < G) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
+    }
+    __syncthreads();
+    for (int t0 = j0; t0 < j1; t0 += kAttnTile) {
+        const int nt = min(kAttnTile, j1 - t0);
+        // K and V rows of this tile (each key's head_dim values are contiguous)
+        for (int i = tid; i < nt * hd; i += kAttnThreads) {
+            const int jj = i / hd, d = i - jj * hd;
+            const size_t src = ((size_t)(t0 + jj) * a.kv_heads + kh) * hd + d;
+            k_s[jj * (hd + 1) + d] = kv_f32<KvT>(kc[src]);
+            v_s[jj * hd + d] = kv_f32<KvT>(vc[src]);
+        }
+        __syncthreads();
+        // scores: lane = key (padded K rows: 32 keys in 32 banks), q broadcast
+        for (int i = tid; i < G * kAttnTile; i += kAttnThreads) {
+            const int g = i / kAttnTile, jj = i - g * kAttnTile;
+            float s = -INFINITY;
+            if (jj < nt) {
+                const float *qg = q_s + g * hd, *kr = k_s + jj * (hd + 1);
+                float dot = 0.f;
+                for (int d = 0; d < hd; ++d) dot = fmaf(qg[d], kr[d], dot);
+                s = dot * scale;
+            }
+            p_s[i] = s;
+        }
+        __syncthreads();
+        tile_softmax(p_s, m_s, l_s, c_s, G, nt, warp, lane);
+        __syncthreads();
+        // weighted values: thread = (head, dim), consecutive dims in a warp
+        for (int i = tid; i < G * hd; i += kAttnThreads) {
+            const int g = i / hd, d = i - g * hd;
+            const float *pg = p_s + g * kAttnTile;
+            float acc = acc_s[i] * c_s[g];
+            for (int jj = 0; jj < nt; ++jj) acc = fmaf(pg[jj], v_s[jj * hd + d], acc);
+            acc_s[i] = acc;
+        }
+        __syncthreads();
+    }
+    // partial of this split: per head (m, l, acc[hd])
+    const size_t pbase = (((size_t)tok * a.n_heads + (size_t)kh * G) * a.splits + split);
+    for (int i = tid; i < G * hd; i += kAttnThreads) {
+        const int g = i / hd, d = i - g * hd;
+        a.part_acc[(pbase + (size_t)g * a.splits) * hd + d] = acc_s[i];
+    }
+    if (tid < G) {
+        a.part_ml[(pbase + (size_t)tid * a.splits) * 2] = m_s[tid];
+        a.part_ml[(pbase + (size_t)tid * a.splits) * 2 + 1] = l_s[tid];
+    }
+}
+
+// The same for a head_dim known at compile time (64, 128, 256) and groups of <= 16 heads: float4
+// tiles (K rows padded by 4 floats, so the 8 lanes of each 16-byte load phase hit distinct banks),
+// scores with lane = key (4 threads per key: heads g0, g0 + 4, ...), weighted values with thread =
+// (head, 4 dims) accumulating in registers.  Shared memory: q[G][HD] | K[kAttnTile][HD + 4] |
+// V[kAttnTile][HD] | p[G][kAttnTile] | m, l, corr[G].
+template <typename KvT, int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_hd_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    constexpr int Q4 = HD / 4, KP = HD + 4;
+    constexpr int MAXV = (kAttnMaxGroup * Q4 + kAttnThreads - 1) / kAttnThreads;  // float4 accumulators
+    const int G = a.n_heads / a.kv_heads;
+    float *q_s = sm, *k_s = q_s + G * HD, *v_s = k_s + kAttnTile * KP, *p_s = v_s + kAttnTile * HD;
+    float *m_s = p_s + G * kAttnTile, *l_s = m_s + G, *c_s = l_s + G;
+    const int split = blockIdx.x, kh = blockIdx.y, tok = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int j0, j1;
+    split_range(a, split, tok, j0, j1);
+    const float scale = rsqrtf((float)HD);
+    const size_t q_base = ((size_t)tok * a.n_heads + (size_t)kh * G) * HD;
+    for (int i = tid; i < G * Q4; i += kAttnThreads)
+        reinterpret_cast<float4 *>(q_s)[i] = reinterpret_cast<const float4 *>(a.q + q_base)[i];
+    if (tid < G) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
+    }
+    float4 acc[MAXV];
+#pragma unroll
+    for (int u = 0; u < MAXV; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    // Tile loads: NL 4-element pieces of K and of V per thread, all issued before any is stored; the
+    // next tile's pieces are loaded while the current tile computes (registers: 2 x NL pieces).
+    constexpr int NL = kAttnTile * Q4 / kAttnThreads;
+    using Piece = typename std::conditional<sizeof(KvT) == 4, float4, uint2>::type;
+    Piece kp[NL], vp[NL];
+    auto issue = [&](int t0) {
+        const int nt = min(kAttnTile, j1 - t0);
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+            const int i = tid + u * kAttnThreads, jj = i / Q4, c4 = i - jj * Q4;
+            if (jj < nt) {
+                const size_t src = ((size_t)(t0 + jj) * a.kv_heads + kh) * HD + 4 * c4;
+                kp[u] = *reinterpret_cast<const Piece *>(static_cast<const KvT *>(a.key_cache) + src);
+                vp[u] = *reinterpret_cast<const Piece *>(static_cast<const KvT *>(a.value_cache) + src);
+            }
+        }
+    };
+    auto widen = [](const Piece &p) -> float4 {
+        if constexpr (sizeof(KvT) == 4) {
+            return p;
+        } else {  // bf16: the top 16 bits of an f32
+            return make_float4(__uint_as_float(p.x << 16), __uint_as_float(p.x & 0xFFFF0000u),
+                               __uint_as_float(p.y << 16), __uint_as_float(p.y & 0xFFFF0000u));
+        }
+    };
+    if (j0 < j1) issue(j0);
+    for (int t0 = j0; t0 < j1; t0 += kAttnTile) {
+        const int nt = min(kAttnTile, j1 - t0);
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+            const int i = tid + u * kAttnThreads, jj = i / Q4, c4 = i - jj * Q4;
+            if (jj < nt) {
+                *reinterpret_cast<float4 *>(k_s + jj * KP + 4 * c4) = widen(kp[u]);
+                *reinterpret_cast<float4 *>(v_s + jj * HD + 4 * c4) = widen(vp[u]);
+            }
+        }
+        __syncthreads();
+        if (t0 + kAttnTile < j1) issue(t0 + kAttnTile);  // in flight while this tile computes
+        {
+            const int jj = tid & (kAttnTile - 1);
+            const float4 *kr = reinterpret_cast<const float4 *>(k_s + jj * KP);
+            for (int g = tid / kAttnTile; g < G; g += kAttnThreads / kAttnTile) {
+                const float4 *qg = reinterpret_cast<const float4 *>(q_s + g * HD);
+                float d0 = 0.f, d1 = 0.f;
+#pragma unroll 8
+                for (int c4 = 0; c4 < Q4; ++c4) {
+                    const float4 kk = kr[c4], qq = qg[c4];
+                    d0 = fmaf(qq.x, kk.x, d0);
+                    d1 = fmaf(qq.y, kk.y, d1);
+                    d0 = fmaf(qq.z, kk.z, d0);
+                    d1 = fmaf(qq.w, kk.w, d1);
+                }
+                p_s[g * kAttnTile + jj] = jj < nt ? (d0 + d1) * scale : -INFINITY;
+            }
+        }
+        __syncthreads();
+        tile_softmax(p_s, m_s, l_s, c_s, G, nt, warp, lane);
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < MAXV; ++u) {
+            const int i = tid + u * kAttnThreads;
+            if (i < G * Q4) {
+                const int g = i / Q4, c4 = i - g * Q4;
+                const float *pg = p_s + g * kAttnTile;
+                const float cr = c_s[g];
+                float4 r = make_float4(acc[u].x * cr, acc[u].y * cr, acc[u].z * cr, acc[u].w * cr);
+                for (int jj = 0; jj < nt; ++jj) {
+                    const float pv = pg[jj];
+                    const float4 vv = *reinterpret_cast<const float4 *>(v_s + jj * HD + 4 * c4);
+                    r.x = fmaf(pv, vv.x, r.x);
+                    r.y = fmaf(pv, vv.y, r.y);
+                    r.z = fmaf(pv, vv.z, r.z);
+                    r.w = fmaf(pv, vv.w, r.w);
+                }
+                acc[u] = r;
+            }
+        }
+        __syncthreads();
+    }
+    const size_t pbase = (((size_t)tok * a.n_heads + (size_t)kh * G) * a.splits + split);
+#pragma unroll
+    for (int u = 0; u < MAXV; ++u) {
+        const int i = tid + u * kAttnThreads;
+        if (i < G * Q4) {
+            const int g = i / Q4, c4 = i - g * Q4;
+            *reinterpret_cast<float4 *>(a.part_acc + (pbase + (size_t)g * a.splits) * HD + 4 * c4) = acc[u];
+        }
+    }
+    if (tid < G) {
+        a.part_ml[(pbase + (size_t)tid * a.splits) * 2] = m_s[tid];
+        a.part_ml[(pbase + (size_t)tid * a.splits) * 2 + 1] = l_s[tid];
+    }
+}
+
+// out[tok][h] = (sum_s w_s acc_s) / (sum_s w_s l_s) * sigmoid(gate), w_s = exp(m_s - max_s m_s) for
+// the splits that saw keys; the weights are computed once per head into shared memory.
+__global__ void attn_combine_kernel(const __grid_constant__ AttnArgs a) {
+    __shared__ float w_s[kAttnMaxSplits];
+    __shared__ float inv_l;
+    const int h = blockIdx.x, tok = blockIdx.y, hd = a.head_dim;
+    const size_t pbase = ((size_t)tok * a.n_heads + h) * a.splits;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        float m = -INFINITY;
+        for (int s = lane; s < a.splits; s += 32)
+            if (a.part_ml[(pbase + s) * 2 + 1] > 0.f) m = fmaxf(m, a.part_ml[(pbase + s) * 2]);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.f;
+        for (int s = lane; s < a.splits; s += 32) {
+            const float ls = a.part_ml[(pbase + s) * 2 + 1];
+            const float w = ls > 0.f ? expf(a.part_ml[(pbase + s) * 2] - m) : 0.f;
+            w_s[s] = w;
+            l += w * ls;
+        }
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) inv_l = 1.0f / l;
+    }
+    __syncthreads();
+    const size_t o = ((size_t)tok * a.n_heads + h) * hd;
+    if (hd % 4 == 0 && hd <= 4 * kAttnThreads) {
+        // thread = (4 dims, split group): float4 loads over the splits of its group, groups summed
+        // through shared memory in a fixed order
+        __shared__ float4 red[kAttnThreads];
+        const int q4 = hd / 4, ng = kAttnThreads / q4;
+        const int c4 = threadIdx.x % q4, grp = threadIdx.x / q4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (grp < ng)
+            for (int s = grp; s < a.splits; s += ng) {
+                const float4 v = *reinterpret_cast<const float4 *>(a.part_acc + (pbase + s) * hd + 4 * c4);
+                const float w = w_s[s];
+                acc.x = fmaf(v.x, w, acc.x);
+                acc.y = fmaf(v.y, w, acc.y);
+                acc.z = fmaf(v.z, w, acc.z);
+                acc.w = fmaf(v.w, w, acc.w);
+            }
+        red[threadIdx.x] = acc;
+        __syncthreads();
+        if (threadIdx.x < q4) {
+            float4 t = red[threadIdx.x];
+            for (int g2 = 1; g2 < ng; ++g2) {
+                const float4 u = red[g2 * q4 + threadIdx.x];
+                t.x += u.x;
+                t.y += u.y;
+                t.z += u.z;
+                t.w += u.w;
+            }
+            const float r[4] = {t.x, t.y, t.z, t.w};
+            for (int e = 0; e < 4; ++e) {
+                const float g = a.gate[o + 4 * threadIdx.x + e];
+                a.attn[o + 4 * threadIdx.x + e] = r[e] * inv_l * (1.0f / (1.0f + expf(-g)));
+            }
+        }
+        return;
+    }
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float acc = 0.f;
+        for (int s = 0; s < a.splits; ++s) acc = fmaf(a.part_acc[(pbase + s) * hd + d], w_s[s], acc);
+        const float g = a.gate[o + d];
+        a.attn[o + d] = acc * inv_l * (1.0f / (1.0f + expf(-g)));
+    }
+}
+
+template <typename KvT, int HD>
+cudaError_t attn_hd_launch(const AttnArgs &a, cudaStream_t s) {
+    const int G = a.n_heads / a.kv_heads;
+    const size_t smem = sizeof(float) * ((size_t)G * HD + (size_t)kAttnTile * (HD + 4) + (size_t)kAttnTile * HD +
+                                         (size_t)G * kAttnTile + 3 * (size_t)G);
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_split_hd_kernel<KvT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attn_split_hd_kernel<KvT, HD><<<dim3(a.splits, a.kv_heads, a.tokens), kAttnThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <typename KvT>
+cudaError_t attn_launch_t(const AttnArgs &a, cudaStream_t s) {
+    cudaError_t e;
+    const bool vec = reinterpret_cast<uintptr_t>(a.key_cache) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(a.value_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(a.q) % 16 == 0 &&
+                     a.n_heads / a.kv_heads <= kAttnMaxGroup;
+    if (vec && a.head_dim == 128) {
+        e = attn_hd_launch<KvT, 128>(a, s);
+    } else if (vec && a.head_dim == 64) {
+        e = attn_hd_launch<KvT, 64>(a, s);
+    } else if (vec && a.head_dim == 256) {
+        e = attn_hd_launch<KvT, 256>(a, s);
+    } else {
+        const size_t smem = attn_smem_bytes(a.n_heads / a.kv_heads, a.head_dim);
+        e = cudaFuncSetAttribute(attn_split_kernel<KvT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attn_split_kernel<KvT><<<dim3(a.splits, a.kv_heads, a.tokens), kAttnThreads, smem, s>>>(a);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return e;
+    attn_combine_kernel<<<dim3(a.n_heads, a.tokens), kAttnThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+}  // namespace
+
+// Shared memory of the general kernel (the larger of the two layouts).
+size_t attn_smem_bytes(int group, int head_dim) {
+    return sizeof(float) * ((size_t)2 * group * head_dim + (size_t)kAttnTile * (head_dim + 4) +
+                            (size_t)kAttnTile * head_dim + (size_t)group * kAttnTile + 3 * (size_t)group);
+}
+int attn_tile() { return kAttnTile; }
+int attn_max_splits() { return kAttnMaxSplits; }
+
+cudaError_t attn_launch(const AttnArgs &a, bool kv_bf16, cudaStream_t s) {
+    return kv_bf16 ? attn_launch_t<__nv_bfloat16>(a, s) : attn_launch_t<float>(a, s);
+}
+
+}  // namespace ql

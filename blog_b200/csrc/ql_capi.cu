@@ -20,6 +20,7 @@
 #include "ql_gemm.cuh"
 #include "ql_gemv.cuh"
 #include "ql_moe.cuh"
+#include "ql_attn.cuh"
 
 namespace ql {
 cudaError_t gemv_launch(int fmt, int kind, const GemvArgs &a, int MT, bool tma, int smem, cudaStream_t s);
@@ -71,6 +72,8 @@ struct Workspace {
     size_t moe_off_cap = 0;
     int *moe_list = nullptr;
     size_t moe_list_cap = 0;
+    float *attn_part = nullptr;  // decode attention: per-split partials
+    size_t attn_part_cap = 0;
 };
 
 std::mutex g_mu;
@@ -1100,6 +1103,74 @@ int ql_moe_down_grouped_accum_ordered(int32_t t, const uint8_t *d, size_t deb, s
     e = moe_combine_launch(ws->moe_y, ids, e_begin, n_experts, rw, out, out_stride, tokens, k, hidden, g_stream);
     ++t_launches;
     return e == cudaSuccess ? QL_OK : cuda_fail(e, what);
+}
+
+// ---- causal gated decode attention --------------------------------------------
+namespace {
+int attention(const float *q, const float *gate, const void *kc, const void *vc, int kv_bf16, float *attn, int tokens,
+              int n_heads, int kv_heads, int head_dim, int max_seq_len, const int *pos_dev, int start_pos,
+              const char *what) {
+    t_launches = 0;
+    if (tokens < 0 || n_heads <= 0 || kv_heads <= 0 || n_heads % kv_heads || head_dim <= 0 || head_dim > 256 ||
+        max_seq_len <= 0 || start_pos < 0)
+        return fail(QL_EINVAL, std::string(what) + ": need n_heads a multiple of kv_heads > 0, 0 < head_dim <= 256, "
+                                                   "max_seq_len > 0, start_pos >= 0");
+    if (tokens == 0) return QL_OK;
+    if (!q || !gate || !kc || !vc || !attn) return fail(QL_EINVAL, std::string(what) + ": null pointer");
+    const int group = n_heads / kv_heads;
+    if (attn_smem_bytes(group, head_dim) > 232448)
+        return fail(QL_EINVAL, std::string(what) + ": n_heads / kv_heads x head_dim too large for shared memory");
+    int st;
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    // splits: enough CTAs for about two per SM over the cache length (the grid does not depend on the
+    // position, so a captured launch replays for any position)
+    const int keys = pos_dev != nullptr ? max_seq_len : std::min(max_seq_len, start_pos + tokens);
+    const int by_len = (keys + attn_tile() - 1) / attn_tile();
+    const int by_sms = std::max(1, 2 * ws->sms / (kv_heads * tokens));
+    const int splits = std::max(1, std::min(std::min(by_len, by_sms), attn_max_splits()));
+    const size_t per = (size_t)tokens * n_heads * splits;
+    const size_t acc_off = (per * 2 + 3) & ~size_t(3);  // the accumulators start on 16 bytes (float4 stores)
+    if ((st = grow(reinterpret_cast<void **>(&ws->attn_part), &ws->attn_part_cap, acc_off + per * head_dim,
+                   sizeof(float), what)))
+        return st;
+    AttnArgs a{};
+    a.q = q;
+    a.gate = gate;
+    a.key_cache = kc;
+    a.value_cache = vc;
+    a.attn = attn;
+    a.pos_dev = pos_dev;
+    a.start_pos = start_pos;
+    a.tokens = tokens;
+    a.n_heads = n_heads;
+    a.kv_heads = kv_heads;
+    a.head_dim = head_dim;
+    a.max_seq_len = max_seq_len;
+    a.splits = splits;
+    a.part_ml = ws->attn_part;
+    a.part_acc = ws->attn_part + acc_off;
+    cudaError_t e = attn_launch(a, kv_bf16 != 0, g_stream);
+    t_launches += 2;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, what);
+}
+}  // namespace
+
+int ql_full_attention_attend(const float *q, const float *gate, const void *key_cache, const void *value_cache,
+                             int kv_bf16, float *attn, int n_heads, int kv_heads, int head_dim, int max_seq_len,
+                             const int *pos_dev) {
+    if (!pos_dev) return fail(QL_EINVAL, "ql_full_attention_attend: null pos_dev");
+    return attention(q, gate, key_cache, value_cache, kv_bf16, attn, 1, n_heads, kv_heads, head_dim, max_seq_len,
+                     pos_dev, 0, "ql_full_attention_attend");
+}
+
+int ql_full_attention_attend_batch(const float *q, const float *gate, const void *key_cache, const void *value_cache,
+                                   int kv_bf16, float *attn, int tokens, int n_heads, int kv_heads, int head_dim,
+                                   int max_seq_len, int start_pos) {
+    if (start_pos + (int64_t)tokens > max_seq_len)
+        return fail(QL_EINVAL, "ql_full_attention_attend_batch: start_pos + tokens > max_seq_len");
+    return attention(q, gate, key_cache, value_cache, kv_bf16, attn, tokens, n_heads, kv_heads, head_dim, max_seq_len,
+                     nullptr, start_pos, "ql_full_attention_attend_batch");
 }
 
 int ql_quant_embedding(int32_t t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n) {

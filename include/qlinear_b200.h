@@ -262,6 +262,23 @@ QL_API int ql_moe_down_grouped_accum_ordered(int32_t quant_type, const uint8_t *
                                              float *out, int64_t out_stride, int tokens, int k, int hidden,
                                              int ffn_dim);
 
+/* ---- decode attention around the projections (reference kernel.cuh:185-194) ------- */
+/* Causal attention with an output gate for the token at position *pos_dev (device int, so a
+ * captured launch replays at every step): for query head h (kv head h / (n_heads / kv_heads)),
+ *   attn_h = softmax_j((q_h . k_j) / sqrt(head_dim)) . v_j * sigmoid(gate_h),  j = 0..pos,
+ * q, gate, attn [n_heads * head_dim]; key_cache / value_cache [max_seq_len][kv_heads][head_dim],
+ * bf16 when kv_bf16 != 0, else f32 (launch_full_attention_attend, launch.cu:676-692).  Keys are
+ * split over CTAs per KV head (each K/V tile read once for the head's whole query group) and the
+ * splits merged by a second launch.  head_dim <= 256. */
+QL_API int ql_full_attention_attend(const float *q, const float *gate, const void *key_cache,
+                                    const void *value_cache, int kv_bf16, float *attn, int n_heads, int kv_heads,
+                                    int head_dim, int max_seq_len, const int *pos_dev);
+/* The same for `tokens` queries at positions start_pos .. start_pos + tokens - 1, rows
+ * n_heads * head_dim apart (launch_full_attention_attend_batch, launch.cu:694-709). */
+QL_API int ql_full_attention_attend_batch(const float *q, const float *gate, const void *key_cache,
+                                          const void *value_cache, int kv_bf16, float *attn, int tokens, int n_heads,
+                                          int kv_heads, int head_dim, int max_seq_len, int start_pos);
+
 /* ---- embedding, dequant, argmax (reference kernel.cuh:141-142, 244-253, 347) ----- */
 QL_API int ql_quant_embedding(int32_t quant_type, const int *input, float *output, const uint8_t *table, size_t row_bytes,
                        int hidden_size, int input_size);

@@ -61,6 +61,7 @@ def lib():
             "orc_swiglu_indexed": (I, [I, P, P, SZ, SZ, SZ, SZ, P, P, P, I, I, I, I]),
             "orc_down_indexed_ordered": (I, [I, P, SZ, SZ, P, P, P, P, I, I, I, I]),
             "orc_router_topk": (I, [P, P, P, I, I, I, F]),
+            "orc_attention_attend": (I, [P, P, P, P, I, P, I, I, I, I, I]),
             "orc_argmax": (I, [P, I]),
             "orc_rmsnorm": (None, [P, P, P, I, I, F]),
             "orc_embedding": (I, [I, P, P, P, SZ, I, I]),
@@ -154,6 +155,18 @@ def down_indexed_ordered(t, d, deb, drb, act, ids, rw, out, k, h, f, order=0):
     ids, rw = _c(ids, np.int32), _c(rw, np.float32)
     out = np.array(out, np.float32, copy=True)
     _ok(lib().orc_down_indexed_ordered(t, _p(d), deb, drb, _p(act), _p(ids), _p(rw), _p(out), k, h, f, order))
+    return out
+
+
+def attention_attend(q, gate, kc, vc, kv_bf16, tokens, n_heads, kv_heads, head_dim, start_pos):
+    """Causal gated decode attention for `tokens` queries at positions start_pos.. (restates
+    full_attn_attend_head, kernel.cu:355-430); kc / vc: [seq][kv_heads][head_dim] float32, or uint16
+    bf16 bits when kv_bf16."""
+    q, gate = _c(q, np.float32), _c(gate, np.float32)
+    kc, vc = _c(kc, np.uint16 if kv_bf16 else np.float32), _c(vc, np.uint16 if kv_bf16 else np.float32)
+    out = np.empty((tokens, n_heads * head_dim), np.float32)
+    _ok(lib().orc_attention_attend(_p(q), _p(gate), _p(kc), _p(vc), int(kv_bf16), _p(out), tokens, n_heads,
+                                   kv_heads, head_dim, start_pos))
     return out
 
 
@@ -343,6 +356,8 @@ def ref_lib():
             "ref_dequantize_q80": (None, [P, P, I64]),
             "ref_dequantize_q50": (None, [P, P, I64]),
             "ref_dequantize_q6k": (None, [P, P, I64]),
+            "ref_full_attention_attend": (None, [P, P, P, P, I, P, I, I, I, I, P]),
+            "ref_full_attention_attend_batch": (None, [P, P, P, P, I, P, I, I, I, I, I, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

@@ -355,6 +355,56 @@ int orc_router_topk(const float *logits, int *top_idx, float *top_w, int T, int 
 
 /* argmax, lowest index on ties (argmax_partial/final_kernel, kernel.cu:3531-3592;
  * host Sampler strict '>' rule, Sampler.cpp:24-50).  NaN never wins. */
+/* Causal decode attention with an output gate (full_attn_attend_head, kernel.cu:355-430, one
+ * head per block): for query head h of token t at position pos, kv head kh = h / (n_heads /
+ * kv_heads), scores s_j = (q_h . k_j) / sqrt(head_dim) over keys j = 0..pos, p = softmax(s),
+ * out_h = (sum_j p_j v_j) * sigmoid(gate_h).  The cache is [max_seq][kv_heads][head_dim], f32 or
+ * bf16 (kv_bf16: 16-bit values, the top half of an f32).  The reference keeps an online softmax
+ * in f32 with __expf; this restatement evaluates the softmax directly in double. */
+static inline double kv_at(const void *cache, int bf16, size_t i) {
+    if (bf16) {
+        const uint32_t b = (uint32_t)((const uint16_t *)cache)[i] << 16;
+        float f;
+        memcpy(&f, &b, 4);
+        return (double)f;
+    }
+    return (double)((const float *)cache)[i];
+}
+int orc_attention_attend(const float *q, const float *gate, const void *kc, const void *vc, int kv_bf16, float *out,
+                         int tokens, int n_heads, int kv_heads, int head_dim, int start_pos) {
+    if (n_heads <= 0 || kv_heads <= 0 || n_heads % kv_heads || head_dim <= 0 || start_pos < 0) return 1;
+    const int group = n_heads / kv_heads;
+    const double scale = 1.0 / sqrt((double)head_dim);
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int t = 0; t < tokens; ++t)
+        for (int h = 0; h < n_heads; ++h) {
+            const int n_keys = start_pos + t + 1, kh = h / group;
+            const float *qh = q + ((size_t)t * n_heads + h) * head_dim;
+            double *s = (double *)malloc(sizeof(double) * (size_t)n_keys);
+            double mx = -INFINITY, den = 0.0;
+            for (int j = 0; j < n_keys; ++j) {
+                double dot = 0.0;
+                for (int d = 0; d < head_dim; ++d)
+                    dot += (double)qh[d] * kv_at(kc, kv_bf16, ((size_t)j * kv_heads + kh) * head_dim + d);
+                s[j] = dot * scale;
+                if (s[j] > mx) mx = s[j];
+            }
+            for (int j = 0; j < n_keys; ++j) {
+                s[j] = exp(s[j] - mx);
+                den += s[j];
+            }
+            for (int d = 0; d < head_dim; ++d) {
+                double acc = 0.0;
+                for (int j = 0; j < n_keys; ++j)
+                    acc += s[j] * kv_at(vc, kv_bf16, ((size_t)j * kv_heads + kh) * head_dim + d);
+                const size_t o = ((size_t)t * n_heads + h) * head_dim + d;
+                out[o] = (float)(acc / den / (1.0 + exp(-(double)gate[o])));
+            }
+            free(s);
+        }
+    return 0;
+}
+
 int orc_argmax(const float *v, int n) {
     int bi = 0;
     float bv = -INFINITY;

@@ -65,4 +65,19 @@ void ref_dequantize_q80(const uint8_t *src, uint16_t *out, int64_t n) { launch_d
 void ref_dequantize_q50(const uint8_t *src, uint16_t *out, int64_t n) { launch_dequantize_q50_to_f16(src, out, n); }
 void ref_dequantize_q6k(const uint8_t *src, uint16_t *out, int64_t n) { launch_dequantize_q6k_to_f16(src, out, n); }
 
+// kernel.cuh:186-189
+void ref_full_attention_attend(const float *q, const float *gate, const void *k, const void *v, int kv_bf16,
+                               float *attn, int n_heads, int kv_heads, int head_dim, int max_seq_len,
+                               const int *pos_dev) {
+    launch_full_attention_attend(q, gate, k, v, kv_bf16 != 0, attn, n_heads, kv_heads, head_dim, max_seq_len,
+                                 pos_dev);
+}
+// kernel.cuh:191-194
+void ref_full_attention_attend_batch(const float *q, const float *gate, const void *k, const void *v, int kv_bf16,
+                                     float *attn, int tokens, int n_heads, int kv_heads, int head_dim,
+                                     int max_seq_len, int start_pos) {
+    launch_full_attention_attend_batch(q, gate, k, v, kv_bf16 != 0, attn, tokens, n_heads, kv_heads, head_dim,
+                                       max_seq_len, start_pos);
+}
+
 }  // extern "C"
