@@ -197,7 +197,7 @@ template <int FMT, int NT>
 __device__ __forceinline__ void pass_blocks(const uint8_t *row0, const uint8_t *row1, int kb_lo, int nkb, int c,
                                             const uint4 *const (&xr)[2], const float *const (&bsr)[2][2],
                                             float (&acc)[2][4]) {
-    constexpr int PF = NT == 1 ? 4 : 2;
+    constexpr int PF = NT == 1 ? 6 : 3;
     uint4 b[PF][NT][2];
     float bs[PF][NT][2];
     auto load = [&](int p, int kb) {
