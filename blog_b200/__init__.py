@@ -54,6 +54,9 @@ SIGNATURES = {
     "ql_quant_down_f32_indexed_accum_ordered": (I, [I32, P, SZ, SZ, P, P, P, P, I, I, I]),
     "ql_moe_router_topk": (I, [P, P, P, I, I, I, F]),
     "ql_full_attention_attend": (I, [P, P, P, P, I, P, I, I, I, I, P]),
+    "ql_q8_1_row_bytes": (SZ, [I]),
+    "ql_quantize_q8_1": (I, [P, P, I, I, I]),
+    "ql_quant_gemv_q8_1": (I, [I32, P, SZ, P, P, I, I]),
     "ql_full_attention_attend_batch": (I, [P, P, P, P, I, P, I, I, I, I, I, I]),
     "ql_moe_swiglu_grouped": (I, [I32, P, P, SZ, SZ, SZ, SZ, P, I64, P, I, I, P, I, I, I, I]),
     "ql_moe_down_grouped_accum_ordered": (I, [I32, P, SZ, SZ, P, P, I, I, P, P, I64, I, I, I, I]),
@@ -307,6 +310,18 @@ def quant_down_f32_indexed_accum_ordered(t, dw, deb, drb, act, ids, rw, out, k, 
 
 def moe_router_topk(logits, idx, w, tokens, n_experts, k, scale):
     _call("ql_moe_router_topk", logits, idx, w, tokens, n_experts, k, scale)
+
+
+def q8_1_row_bytes(in_dim):
+    return lib().ql_q8_1_row_bytes(in_dim)
+
+
+def quantize_q8_1(x, xq, in_dim, m, store_raw_sum=False):
+    _call("ql_quantize_q8_1", x, xq, in_dim, m, int(store_raw_sum))
+
+
+def quant_gemv_q8_1(t, w, rb, xq, y, out_dim, in_dim):
+    _call("ql_quant_gemv_q8_1", t, w, rb, xq, y, out_dim, in_dim)
 
 
 def full_attention_attend(q, gate, kc, vc, kv_bf16, attn, n_heads, kv_heads, head_dim, max_seq_len, pos_dev):

@@ -21,6 +21,7 @@
 #include "ql_gemv.cuh"
 #include "ql_moe.cuh"
 #include "ql_attn.cuh"
+#include "ql_q81.cuh"
 
 namespace ql {
 cudaError_t gemv_launch(int fmt, int kind, const GemvArgs &a, int MT, bool tma, int smem, cudaStream_t s);
@@ -1171,6 +1172,41 @@ int ql_full_attention_attend_batch(const float *q, const float *gate, const void
         return fail(QL_EINVAL, "ql_full_attention_attend_batch: start_pos + tokens > max_seq_len");
     return attention(q, gate, key_cache, value_cache, kv_bf16, attn, tokens, n_heads, kv_heads, head_dim, max_seq_len,
                      nullptr, start_pos, "ql_full_attention_attend_batch");
+}
+
+// ---- opt-in Q8_1 activation path ----------------------------------------------------
+size_t ql_q8_1_row_bytes(int in_dim) { return in_dim > 0 ? q81_row_bytes(in_dim) : 0; }
+
+int ql_quantize_q8_1(const float *x, uint8_t *x_q8_1, int in_dim, int m, int store_raw_sum) {
+    t_launches = 0;
+    if (in_dim <= 0 || m < 0) return fail(QL_EINVAL, "ql_quantize_q8_1: need in_dim > 0 and m >= 0");
+    if (m == 0) return QL_OK;
+    if (!x || !x_q8_1) return fail(QL_EINVAL, "ql_quantize_q8_1: null pointer");
+    if (reinterpret_cast<uintptr_t>(x_q8_1) % 4)
+        return fail(QL_EINVAL, "ql_quantize_q8_1: x_q8_1 must be 4-byte aligned");
+    int st;
+    if (!workspace(&st)) return st;
+    cudaError_t e = quantize_q81_launch(x, x_q8_1, in_dim, m, store_raw_sum != 0, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quantize_q8_1");
+}
+
+int ql_quant_gemv_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_q8_1, float *y, int out_dim,
+                       int in_dim) {
+    t_launches = 0;
+    if (t != kQ4_K && t != kQ6_K && t != kQ5_0 && t != kQ8_0)
+        return fail(QL_EINVAL, "ql_quant_gemv_q8_1: quant_type must be Q4_K, Q6_K, Q5_0 or Q8_0");
+    if (out_dim < 0) return fail(QL_EINVAL, "ql_quant_gemv_q8_1: negative out_dim");
+    if (out_dim == 0) return QL_OK;
+    int st = check_weight(t, w, rb, 0, in_dim, "ql_quant_gemv_q8_1");
+    if (st) return st;
+    if (!x_q8_1 || !y) return fail(QL_EINVAL, "ql_quant_gemv_q8_1: null pointer");
+    if (reinterpret_cast<uintptr_t>(x_q8_1) % 4)
+        return fail(QL_EINVAL, "ql_quant_gemv_q8_1: x_q8_1 must be 4-byte aligned");
+    if (!workspace(&st)) return st;
+    cudaError_t e = gemv_q81_launch(t, w, rb, x_q8_1, y, out_dim, in_dim, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quant_gemv_q8_1");
 }
 
 int ql_quant_embedding(int32_t t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n) {

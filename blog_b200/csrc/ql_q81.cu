@@ -1,0 +1,165 @@
+// Opt-in int8 activation path (Q8_1), the reference's llama.cpp-style alternative to fp32
+// activations (kernel.cu:1679-1865, launch.cu:191-240; the engine keeps it off by default because
+// it changes numerics, TensorTool.cpp:159-161).
+//
+// Q8_1 block (36 bytes per 32 activations): f16 d = max|x| / 127, f16 sum (sum of x, or d * sum of q),
+// 32 x int8 q = round(x / d) clamped to +-127.  The quantizer reproduces the reference's bytes
+// exactly: the same per-block arithmetic (IEEE divide, round-half-even conversion) and the same
+// warp tree for the sum (lane l adds lane l + 16, then + 8, + 4, + 2, + 1), eight blocks per CTA.
+//
+// The GEMV takes one Q8_1 activation row: a warp per weight row, lane = one 32-element block at a
+// time (32 adjacent blocks per warp pass: coalesced row reads), the block's integer dot product
+// with 8 dp4a, then the block's scale terms in fp32:
+//   Q4_K: acc += (d_w sc d_x) qdot - dmin_w m sum_x      (the min folded through the block sum)
+//   Q6_K: acc += (d_w d_x) (s0 qdot_lo16 + s1 qdot_hi16)  (two 16-element scale groups)
+//   Q5_0 / Q8_0: acc += (d_w d_x) qdot
+// and a warp reduction.  The reference sums blocks in order on one lane (Q4_K / Q6_K) or per
+// element in floats (Q5_0 / Q8_0); the results agree to float rounding (~1e-7 relative).
+#include "ql_common.cuh"
+#include "ql_q81.cuh"
+
+namespace ql {
+namespace {
+
+constexpr int kQ81Warps = 8;
+
+__global__ void __launch_bounds__(32 * kQ81Warps) quantize_q81_kernel(const float *__restrict__ x,
+                                                                     uint8_t *__restrict__ xq, int in_dim, int m,
+                                                                     int bpr, int store_raw_sum) {
+    const int lane = threadIdx.x & 31;
+    const long long blk = (long long)blockIdx.x * kQ81Warps + (threadIdx.x >> 5);
+    if (blk >= (long long)m * bpr) return;
+    const int row = (int)(blk / bpr), qb = (int)(blk - (long long)row * bpr);
+    const int k = qb * 32 + lane;
+    const float v = k < in_dim ? x[(size_t)row * in_dim + k] : 0.0f;
+    float amax = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_down_sync(0xffffffffu, amax, o));
+    amax = __shfl_sync(0xffffffffu, amax, 0);
+    const float d = amax > 0.0f ? amax / 127.0f : 0.0f;
+    const float id = d > 0.0f ? 1.0f / d : 0.0f;
+    float raw = v;  // lane 0 ends with the tree sum ((v0 + v16) + (v8 + v24)) + ...
+    for (int o = 16; o > 0; o >>= 1) raw += __shfl_down_sync(0xffffffffu, raw, o);
+    int q = __float2int_rn(v * id);
+    q = max(-127, min(127, q));
+    int qs = q;
+    for (int o = 16; o > 0; o >>= 1) qs += __shfl_down_sync(0xffffffffu, qs, o);
+    uint8_t *dst = xq + (size_t)blk * 36;
+    if (lane == 0) {
+        *reinterpret_cast<uint16_t *>(dst) = __half_as_ushort(__float2half(d));
+        const float s = store_raw_sum ? raw : d * (float)qs;
+        *reinterpret_cast<uint16_t *>(dst + 2) = __half_as_ushort(__float2half(s));
+    }
+    reinterpret_cast<int8_t *>(dst + 4)[lane] = (int8_t)q;
+}
+
+__device__ __forceinline__ uint32_t ld_u16_pair(const uint8_t *p) {  // 4 bytes at a 2-byte-aligned address
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(p);
+    return (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+}
+// Spread bits 0..3 of h to bit 4 of bytes 0..3.
+__device__ __forceinline__ uint32_t bits_to_byte4(uint32_t h) { return ((h * 0x00204081u) & 0x01010101u) << 4; }
+
+template <int FMT>
+__global__ void __launch_bounds__(32 * kQ81Warps) gemv_q81_kernel(const uint8_t *__restrict__ w, size_t rb,
+                                                                 const uint8_t *__restrict__ xq, float *__restrict__ y,
+                                                                 int out_dim, int bpr) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kQ81Warps + (threadIdx.x >> 5);
+    if (row >= out_dim) return;
+    const uint8_t *rp = w + (size_t)row * rb;
+    float acc = 0.f;
+    for (int b = lane; b < bpr; b += 32) {
+        const uint8_t *xb = xq + (size_t)b * 36;
+        const uint32_t dh = *reinterpret_cast<const uint32_t *>(xb);
+        const float dx = half_bits_to_float(dh), sx = half_bits_to_float(dh >> 16);
+        const int *qx = reinterpret_cast<const int *>(xb + 4);
+        if (FMT == kQ4_K) {
+            const int sb = b >> 3, j = b & 7;
+            const uint8_t *base = rp + 144 * sb;
+            const uint4 q0 = *reinterpret_cast<const uint4 *>(base + 16 + 32 * (j >> 1));
+            const uint4 q1 = *reinterpret_cast<const uint4 *>(base + 32 + 32 * (j >> 1));
+            const uint32_t W[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            const int sh = 4 * (j & 1);
+            int dot = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dot = __dp4a((int)((W[i] >> sh) & 0x0F0F0F0Fu), qx[i], dot);
+            const uint8_t *s = base + 4;  // q4k_scale_min (reference kernel.cu:913-921)
+            uint32_t sc, mn;
+            if (j < 4) {
+                sc = s[j] & 63u;
+                mn = s[j + 4] & 63u;
+            } else {
+                sc = (s[j + 4] & 0xFu) | ((uint32_t)(s[j - 4] >> 6) << 4);
+                mn = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+            }
+            const uint32_t dd = *reinterpret_cast<const uint32_t *>(base);
+            acc = fmaf(half_bits_to_float(dd) * (float)sc * dx, (float)dot, acc);
+            acc -= half_bits_to_float(dd >> 16) * (float)mn * sx;
+        } else if (FMT == kQ6_K) {
+            const int sb = b >> 3, sub = b & 7, hf = sub >> 2, grp = sub & 3;
+            const uint8_t *base = rp + 210 * sb;
+            const uint8_t *ql = base + 64 * hf + ((grp & 1) ? 32 : 0), *qh = base + 128 + 32 * hf;
+            const int8_t *scl = reinterpret_cast<const int8_t *>(base + 192) + 8 * hf + 2 * grp;
+            const int lsh = (grp >> 1) ? 4 : 0, hsh = 2 * grp;
+            int dot0 = 0, dot1 = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {  // elements 4i .. 4i + 3: 6-bit values minus 32 as signed bytes
+                const uint32_t l = ld_u16_pair(ql + 4 * i), h = ld_u16_pair(qh + 4 * i);
+                const uint32_t v6 = ((l >> lsh) & 0x0F0F0F0Fu) | (((h >> hsh) & 0x03030303u) << 4);
+                const int q = (int)__vsub4(v6, 0x20202020u);
+                if (i < 4) dot0 = __dp4a(q, qx[i], dot0);
+                else dot1 = __dp4a(q, qx[i], dot1);
+            }
+            const float dwx = half_bits_to_float(*reinterpret_cast<const uint16_t *>(base + 208)) * dx;
+            acc = fmaf(dwx, (float)scl[0] * (float)dot0 + (float)scl[1] * (float)dot1, acc);
+        } else if (FMT == kQ5_0) {
+            const uint8_t *base = rp + 22 * b;
+            const uint32_t qh = ld_u16_pair(base + 2);
+            int dot = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t l = ld_u16_pair(base + 6 + 4 * i);
+                const int lo = (int)__vsub4((l & 0x0F0F0F0Fu) | bits_to_byte4((qh >> (4 * i)) & 0xFu), 0x10101010u);
+                const int hi =
+                    (int)__vsub4(((l >> 4) & 0x0F0F0F0Fu) | bits_to_byte4((qh >> (16 + 4 * i)) & 0xFu), 0x10101010u);
+                dot = __dp4a(lo, qx[i], dot);
+                dot = __dp4a(hi, qx[4 + i], dot);
+            }
+            acc = fmaf(half_bits_to_float(*reinterpret_cast<const uint16_t *>(base)) * dx, (float)dot, acc);
+        } else {  // Q8_0
+            const uint8_t *base = rp + 34 * b;
+            int dot = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dot = __dp4a((int)ld_u16_pair(base + 2 + 4 * i), qx[i], dot);
+            acc = fmaf(half_bits_to_float(*reinterpret_cast<const uint16_t *>(base)) * dx, (float)dot, acc);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) y[row] = acc;
+}
+}  // namespace
+
+size_t q81_row_bytes(int in_dim) { return (size_t)((in_dim + 31) / 32) * 36; }
+
+cudaError_t quantize_q81_launch(const float *x, uint8_t *xq, int in_dim, int m, bool store_raw_sum, cudaStream_t s) {
+    const int bpr = (in_dim + 31) / 32;
+    const long long blocks = ((long long)m * bpr + kQ81Warps - 1) / kQ81Warps;
+    quantize_q81_kernel<<<(unsigned)blocks, 32 * kQ81Warps, 0, s>>>(x, xq, in_dim, m, bpr, store_raw_sum ? 1 : 0);
+    return cudaGetLastError();
+}
+
+cudaError_t gemv_q81_launch(int fmt, const uint8_t *w, size_t rb, const uint8_t *xq, float *y, int out_dim, int in_dim,
+                            cudaStream_t s) {
+    const int bpr = (in_dim + 31) / 32;
+    const unsigned grid = (unsigned)((out_dim + kQ81Warps - 1) / kQ81Warps);
+    switch (fmt) {
+    case kQ4_K: gemv_q81_kernel<kQ4_K><<<grid, 32 * kQ81Warps, 0, s>>>(w, rb, xq, y, out_dim, bpr); break;
+    case kQ6_K: gemv_q81_kernel<kQ6_K><<<grid, 32 * kQ81Warps, 0, s>>>(w, rb, xq, y, out_dim, bpr); break;
+    case kQ5_0: gemv_q81_kernel<kQ5_0><<<grid, 32 * kQ81Warps, 0, s>>>(w, rb, xq, y, out_dim, bpr); break;
+    case kQ8_0: gemv_q81_kernel<kQ8_0><<<grid, 32 * kQ81Warps, 0, s>>>(w, rb, xq, y, out_dim, bpr); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace ql

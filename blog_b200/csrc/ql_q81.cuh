@@ -1,0 +1,14 @@
+// Opt-in int8 activation path (ql_q81.cu): Q8_1 activation quantizer and Q8_1 GEMV.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace ql {
+
+size_t q81_row_bytes(int in_dim);
+cudaError_t quantize_q81_launch(const float *x, uint8_t *xq, int in_dim, int m, bool store_raw_sum, cudaStream_t s);
+cudaError_t gemv_q81_launch(int fmt, const uint8_t *w, size_t rb, const uint8_t *xq, float *y, int out_dim, int in_dim,
+                            cudaStream_t s);
+
+}  // namespace ql

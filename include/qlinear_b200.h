@@ -279,6 +279,19 @@ QL_API int ql_full_attention_attend_batch(const float *q, const float *gate, con
                                           const void *value_cache, int kv_bf16, float *attn, int tokens, int n_heads,
                                           int kv_heads, int head_dim, int max_seq_len, int start_pos);
 
+/* ---- opt-in int8 activation path, Q8_1 (reference kernel.cuh:47-52) -------------------
+ * Changes numerics (activations rounded to int8 per 32), as in the reference, which keeps it off
+ * by default (TensorTool.cpp:159-161).  Bytes of one Q8_1 row of in_dim activations (36 per 32). */
+QL_API size_t ql_q8_1_row_bytes(int in_dim);
+/* x [m][in_dim] (rows in_dim apart) -> x_q8_1 [m][ql_q8_1_row_bytes(in_dim)]: per 32 activations
+ * f16 d = max|x| / 127, f16 sum (sum of x when store_raw_sum, else d * sum q), 32 int8 q; the same
+ * bytes as launch_quantize_q8_1 (launch.cu:201-207). */
+QL_API int ql_quantize_q8_1(const float *x, uint8_t *x_q8_1, int in_dim, int m, int store_raw_sum);
+/* y[out_dim] = W . x for one Q8_1 activation row: integer dot products per 32-element block with
+ * the block scales in fp32 (launch_quant_gemv_q8_1, launch.cu:222-245); Q4_K, Q6_K, Q5_0, Q8_0. */
+QL_API int ql_quant_gemv_q8_1(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const uint8_t *x_q8_1,
+                              float *y, int out_dim, int in_dim);
+
 /* ---- embedding, dequant, argmax (reference kernel.cuh:141-142, 244-253, 347) ----- */
 QL_API int ql_quant_embedding(int32_t quant_type, const int *input, float *output, const uint8_t *table, size_t row_bytes,
                        int hidden_size, int input_size);

@@ -62,6 +62,8 @@ def lib():
             "orc_down_indexed_ordered": (I, [I, P, SZ, SZ, P, P, P, P, I, I, I, I]),
             "orc_router_topk": (I, [P, P, P, I, I, I, F]),
             "orc_attention_attend": (I, [P, P, P, P, I, P, I, I, I, I, I]),
+            "orc_quantize_q8_1": (I, [P, P, I, I, I]),
+            "orc_gemv_q8_1": (I, [I, P, C.c_size_t, P, P, I, I]),
             "orc_argmax": (I, [P, I]),
             "orc_rmsnorm": (None, [P, P, P, I, I, F]),
             "orc_embedding": (I, [I, P, P, P, SZ, I, I]),
@@ -168,6 +170,27 @@ def attention_attend(q, gate, kc, vc, kv_bf16, tokens, n_heads, kv_heads, head_d
     _ok(lib().orc_attention_attend(_p(q), _p(gate), _p(kc), _p(vc), int(kv_bf16), _p(out), tokens, n_heads,
                                    kv_heads, head_dim, start_pos))
     return out
+
+
+def q8_1_row_bytes(k: int) -> int:
+    return (k + 31) // 32 * 36
+
+
+def quantize_q8_1(x, store_raw_sum=False):
+    """Q8_1 blocks of each row of x [m, k] (restates quantize_q8_1_kernel, kernel.cu:1679-1720)."""
+    x = _c(np.atleast_2d(x), np.float32)
+    m, k = x.shape
+    out = np.empty((m, q8_1_row_bytes(k)), np.uint8)
+    _ok(lib().orc_quantize_q8_1(_p(x), _p(out), k, m, int(store_raw_sum)))
+    return out
+
+
+def gemv_q8_1(t, w, rb, xq, n, k):
+    """y[n] against one Q8_1 activation row (restates quant_gemv_q8_1_kernel, kernel.cu:1767-1865)."""
+    w, xq = _c(w, np.uint8), _c(xq, np.uint8)
+    y = np.empty(n, np.float32)
+    _ok(lib().orc_gemv_q8_1(t, _p(w), rb, _p(xq), _p(y), n, k))
+    return y
 
 
 def router_topk(logits, k, scale):
@@ -358,6 +381,8 @@ def ref_lib():
             "ref_dequantize_q6k": (None, [P, P, I64]),
             "ref_full_attention_attend": (None, [P, P, P, P, I, P, I, I, I, I, P]),
             "ref_full_attention_attend_batch": (None, [P, P, P, P, I, P, I, I, I, I, I, I]),
+            "ref_quantize_q8_1": (None, [P, P, I, I, I]),
+            "ref_quant_gemv_q8_1": (None, [I, P, SZ, P, P, I, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

@@ -405,6 +405,96 @@ int orc_attention_attend(const float *q, const float *gate, const void *kc, cons
     return 0;
 }
 
+/* Q8_1 activation blocks (quantize_q8_1_kernel, kernel.cu:1679-1720): per 32 activations (zeros
+ * past in_dim), d = max|x| / 127, q = round-half-even(x * (1 / d)) clamped to +-127, f16 d, f16 sum
+ * (the warp-tree sum of x when store_raw_sum, else d * sum q), 32 x int8.  The tree adds lane
+ * l + 16, then + 8, + 4, + 2, + 1 into lane l; lane 0 holds the block sum. */
+int orc_quantize_q8_1(const float *x, uint8_t *out, int in_dim, int m, int store_raw_sum) {
+    if (in_dim <= 0 || m < 0) return 1;
+    const int bpr = (in_dim + 31) / 32;
+    for (int r = 0; r < m; ++r)
+        for (int b = 0; b < bpr; ++b) {
+            float v[32], t[32];
+            float amax = 0.0f;
+            for (int l = 0; l < 32; ++l) {
+                const int k = b * 32 + l;
+                v[l] = k < in_dim ? x[(size_t)r * in_dim + k] : 0.0f;
+                t[l] = v[l];
+                amax = fmaxf(amax, fabsf(v[l]));
+            }
+            const float d = amax > 0.0f ? amax / 127.0f : 0.0f;
+            const float id = d > 0.0f ? 1.0f / d : 0.0f;
+            for (int o = 16; o > 0; o >>= 1)
+                for (int l = 0; l < o; ++l) t[l] = t[l] + t[l + o];
+            uint8_t *dst = out + ((size_t)r * bpr + b) * 36;
+            int qsum = 0;
+            for (int l = 0; l < 32; ++l) {
+                const float p = v[l] * id;
+                int q = (int)lrintf(p);
+                q = q < -127 ? -127 : q > 127 ? 127 : q;
+                qsum += q;
+                dst[4 + l] = (uint8_t)(int8_t)q;
+            }
+            put_h(dst, orc_f32_to_f16(d));
+            put_h(dst + 2, orc_f32_to_f16(store_raw_sum ? t[0] : d * (float)qsum));
+        }
+    return 0;
+}
+
+/* GEMV against one Q8_1 activation row (quant_gemv_q8_1_kernel, kernel.cu:1767-1865), per block b
+ * in order: Q4_K acc = fmaf(d sc dx, qdot, acc) - dmin m sum_x; Q6_K acc = fmaf(d dx, s0 qdot_lo +
+ * s1 qdot_hi, acc); Q5_0 / Q8_0 acc += w_k * (dx q_k) per element (the reference's float form). */
+int orc_gemv_q8_1(int t, const uint8_t *w, size_t rb, const uint8_t *xq, float *y, int N, int K) {
+    if (t != 12 && t != 14 && t != 6 && t != 8) return 1;
+    const int bpr = (K + 31) / 32;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        const uint8_t *row = w + (size_t)n * rb;
+        float acc = 0.0f;
+        for (int b = 0; b < bpr; ++b) {
+            const uint8_t *xb = xq + (size_t)b * 36;
+            const float dx = h2f(xb), sx = h2f(xb + 2);
+            const int8_t *qx = (const int8_t *)(xb + 4);
+            if (t == 12) {
+                const uint8_t *base = row + (size_t)(b >> 3) * 144;
+                const int j = b & 7;
+                int dot = 0;
+                for (int l = 0; l < 32; ++l) {
+                    const uint8_t pk = base[16 + (j >> 1) * 32 + l];
+                    dot += ((j & 1) ? (pk >> 4) : (pk & 15)) * qx[l];
+                }
+                uint8_t sc, mn;
+                q4k_scale_min(j, base + 4, &sc, &mn);
+                acc = fmaf(h2f(base) * (float)sc * dx, (float)dot, acc);
+                acc -= h2f(base + 2) * (float)mn * sx;
+            } else if (t == 14) {
+                const uint8_t *base = row + (size_t)(b >> 3) * 210;
+                const int sub = b & 7, hf = sub >> 2, grp = sub & 3;
+                const uint8_t *ql = base + 64 * hf, *qh = base + 128 + 32 * hf;
+                const int8_t *sc = (const int8_t *)(base + 192) + 8 * hf;
+                int d0 = 0, d1 = 0;
+                for (int l = 0; l < 32; ++l) {
+                    const int lo = (grp & 1) ? ql[l + 32] : ql[l];
+                    const int q = (((grp >> 1) ? (lo >> 4) : (lo & 15)) | (((qh[l] >> (2 * grp)) & 3) << 4)) - 32;
+                    if (l < 16) d0 += q * qx[l];
+                    else d1 += q * qx[l];
+                }
+                acc = fmaf(h2f(base + 208) * dx, (float)sc[2 * grp] * (float)d0 + (float)sc[2 * grp + 1] * (float)d1,
+                           acc);
+            } else {
+                for (int l = 0; l < 32; ++l) {
+                    const int k = b * 32 + l;
+                    if (k >= K) break;
+                    const float wv = t == 6 ? q50_at(row, k) : q80_at(row, k);
+                    acc = fmaf(wv, dx * (float)qx[l], acc);
+                }
+            }
+        }
+        y[n] = acc;
+    }
+    return 0;
+}
+
 int orc_argmax(const float *v, int n) {
     int bi = 0;
     float bv = -INFINITY;

@@ -80,4 +80,13 @@ void ref_full_attention_attend_batch(const float *q, const float *gate, const vo
                                        max_seq_len, start_pos);
 }
 
+// kernel.cuh:48-49
+void ref_quantize_q8_1(const float *x, uint8_t *xq, int in_dim, int m, int store_raw_sum) {
+    launch_quantize_q8_1(x, xq, in_dim, m, store_raw_sum != 0);
+}
+// kernel.cuh:50-52
+void ref_quant_gemv_q8_1(int t, const uint8_t *w, size_t rb, const uint8_t *xq, float *y, int out_dim, int in_dim) {
+    launch_quant_gemv_q8_1(static_cast<DType>(t), w, rb, xq, y, out_dim, in_dim);
+}
+
 }  // extern "C"

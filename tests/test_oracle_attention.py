@@ -38,3 +38,38 @@ def test_oracle_attention_matches_numpy():
     got = O.attention_attend(q, gate, kb, vb, True, tokens, nh, kvh, hd, start)
     want = _numpy(q, gate, kf, vf, tokens, nh, kvh, hd, start)
     assert np.max(np.abs(got - want)) < 1e-6
+
+
+def _q8_1_numpy(x, raw):
+    """Q8_1 blocks restated in numpy float32 (quantize_q8_1_kernel, kernel.cu:1679-1720)."""
+    m, k = x.shape
+    bpr = (k + 31) // 32
+    out = np.zeros((m, bpr * 36), np.uint8)
+    for r in range(m):
+        for b in range(bpr):
+            v = np.zeros(32, np.float32)
+            seg = x[r, b * 32:min(k, b * 32 + 32)]
+            v[:len(seg)] = seg
+            amax = np.float32(np.max(np.abs(v)))
+            d = np.float32(amax / np.float32(127.0)) if amax > 0 else np.float32(0)
+            idv = np.float32(np.float32(1.0) / d) if d > 0 else np.float32(0)
+            t = v.copy()
+            o = 16
+            while o:
+                t[:o] = t[:o] + t[o:2 * o]
+                o //= 2
+            q = np.clip(np.rint(v * idv), -127, 127).astype(np.int32)  # rint: round half to even
+            s = t[0] if raw else np.float32(d * np.float32(q.sum()))
+            blk = out[r, b * 36:(b + 1) * 36]
+            blk[0:2] = np.array([d], np.float16).view(np.uint8)
+            blk[2:4] = np.array([s], np.float16).view(np.uint8)
+            blk[4:36] = q.astype(np.int8).view(np.uint8)
+    return out
+
+
+def test_oracle_quantize_q8_1_matches_numpy():
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((3, 200)) * 3).astype(np.float32)
+    x[1, 32:64] = 0.0
+    for raw in (False, True):
+        assert np.array_equal(O.quantize_q8_1(x, raw), _q8_1_numpy(x, raw))
