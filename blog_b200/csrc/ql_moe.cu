@@ -274,12 +274,15 @@ __device__ __forceinline__ void pass_q4k(const uint8_t *row0, const uint8_t *row
         uint4 hd[2];  // rows g, g + 8: {d | dmin << 16, scales 0-3, 4-7, 8-11}
         hd[0] = *reinterpret_cast<const uint4 *>(row0 + 144 * sb);
         hd[1] = *reinterpret_cast<const uint4 *>(row1 + 144 * sb);
-        float dsup[2], msup[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            dsup[h] = half_bits_to_float(hd[h].x);
-            msup[h] = half_bits_to_float(hd[h].x >> 16);
-        }
+        // the 4 lanes of a quad share rows g and g + 8: lane c decodes one of the 4 per-sub-block
+        // values (c = 0: d sc of row g, 1: dmin m of row g, 2 / 3: the same for row g + 8), which a
+        // quad shuffle then hands to the others
+        const uint4 &hsel = (c & 2) ? hd[1] : hd[0];
+        const bool is_min = c & 1;
+        const uint32_t lo6 = is_min ? hsel.z : hsel.y;  // 6-bit values of sub-blocks 0-3, top bits of 4-7
+        const uint32_t hi4 = hsel.w >> (is_min ? 4 : 0);  // low 4 bits of sub-blocks 4-7
+        const float sup = half_bits_to_float(is_min ? (hsel.x >> 16) : hsel.x);
+        const int qbase = (threadIdx.x & 31) & ~3;
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) {
             uint32_t w[2][2];  // rows x (bytes 4c.., bytes 16 + 4c..) of sub-blocks 2pr, 2pr + 1
@@ -291,20 +294,17 @@ __device__ __forceinline__ void pass_q4k(const uint8_t *row0, const uint8_t *row
             for (int hb = 0; hb < 2; ++hb) {
                 const int j = 2 * pr + hb, kb = 8 * sb + j, slot = j % PF;
                 uint32_t A0[4], A1[4];
+                uint32_t v6;  // q4k_scale_min (reference kernel.cu:913-921) for this lane's value
+                if (j < 4) v6 = (lo6 >> (8 * j)) & 63u;
+                else v6 = ((hi4 >> (8 * (j - 4))) & 0xFu) | (((lo6 >> (8 * (j - 4) + 6)) & 3u) << 4);
+                const float mine = sup * (float)v6;  // exact: 11-bit x 6-bit
                 float dsc[2], msc[2];
+                dsc[0] = __shfl_sync(0xffffffffu, mine, qbase);
+                msc[0] = __shfl_sync(0xffffffffu, mine, qbase + 1);
+                dsc[1] = __shfl_sync(0xffffffffu, mine, qbase + 2);
+                msc[1] = __shfl_sync(0xffffffffu, mine, qbase + 3);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    uint32_t scv, mnv;  // q4k_scale_min (reference kernel.cu:913-921)
-                    if (j < 4) {
-                        scv = (hd[h].y >> (8 * j)) & 63u;
-                        mnv = (hd[h].z >> (8 * j)) & 63u;
-                    } else {
-                        const int sj = 8 * (j - 4);
-                        scv = ((hd[h].w >> sj) & 0xFu) | (((hd[h].y >> (sj + 6)) & 3u) << 4);
-                        mnv = ((hd[h].w >> (sj + 4)) & 0xFu) | (((hd[h].z >> (sj + 6)) & 3u) << 4);
-                    }
-                    dsc[h] = dsup[h] * (float)scv;  // exact: 11-bit x 6-bit
-                    msc[h] = msup[h] * (float)mnv;
                     const uint32_t w0 = w[h][0] >> (4 * hb), w1 = w[h][1] >> (4 * hb);
                     A0[h] = int_pair(w0 & 0x000F000Fu, B);
                     A0[2 + h] = int_pair((w0 >> 8) & 0x000F000Fu, B);
