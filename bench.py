@@ -693,6 +693,65 @@ def run_attn_kernel(args):
     return 0
 
 
+def run_q81_kernel(args):
+    """--kernel-only q81_matmul: the opt-in Q8_1 path at a prefill shape (--tokens rows, Q4_K 4096 x
+    4096 and 11008 x 4096): activation quantization + the int8 tensor-core matmul, against the f16
+    tensor-core GEMM (ql_quant_matmul) on the same weights; and the reference's own Q8_1 matmul
+    kernel when it is built.  Weights rotate over > 300 MB."""
+    import torch
+    import blog_b200 as Q
+    torch.cuda.init()
+    Q.init(0)
+    Q.set_stream(torch.cuda.current_stream().cuda_stream)
+    m = args.tokens
+    res = {"kernel_only": "q81_matmul", "tokens": m, "shapes": []}
+    try:
+        import oracle as O
+        R = O.ref_lib()
+    except Exception:
+        R = None
+    for n, k in ((4096, 4096), (11008, 4096)):
+        rb = Q.row_bytes(QK, k)
+        nbuf = max(2, -(-300_000_000 // (n * rb)))
+        ws = []
+        for i in range(nbuf):
+            w = torch.empty((n, rb), dtype=torch.uint8, device="cuda")
+            Q.synth_quantized(QK, 17 * i + n, n, k, 0.02, w.data_ptr())
+            ws.append(w)
+        x = torch.randn(m, k, device="cuda")
+        xq = torch.empty((m, Q.q8_1_row_bytes(k)), dtype=torch.uint8, device="cuda")
+        y = torch.empty(m, n, device="cuda")
+
+        def timed(fn):
+            for i in range(max(args.warmup, 3)):
+                fn(i % nbuf)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(args.steps):
+                fn(i % nbuf)
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / args.steps * 1e3
+
+        def q81(i):
+            Q.quantize_q8_1(x.data_ptr(), xq.data_ptr(), k, m, True)
+            Q.quant_matmul_q8_1(QK, ws[i].data_ptr(), rb, xq.data_ptr(), y.data_ptr(), n, k, m)
+        us = timed(q81)
+        us16 = timed(lambda i: Q.quant_matmul(QK, ws[i].data_ptr(), rb, x.data_ptr(), y.data_ptr(), n, k, m))
+        ent = {"N": n, "K": k, "q81_us": us, "q81_TOPs": 2.0 * m * n * k / us / 1e6, "f16_tensor_us": us16}
+        if R is not None:
+            R.ref_set_stream(torch.cuda.current_stream().cuda_stream)
+            ent["reference_q81_matmul_us"] = timed(lambda i: R.ref_quant_matmul_q8_1(
+                QK, ws[i].data_ptr(), rb, xq.data_ptr(), y.data_ptr(), n, k, m))
+        res["shapes"].append(ent)
+        del ws
+        torch.cuda.empty_cache()
+    Q.check_device()
+    print(json.dumps(res), flush=True)
+    return 0
+
+
 def run_kernel_only(args):
     """Times one kernel of the step at its bench shape (the ncu profiling target):
     swiglu = fused RMSNorm + gate/up SwiGLU (18944 x 3584 x 2), down = down + residual
@@ -705,6 +764,8 @@ def run_kernel_only(args):
         return run_moe_kernel(args)
     if args.kernel_only == "attn":
         return run_attn_kernel(args)
+    if args.kernel_only == "q81_matmul":
+        return run_q81_kernel(args)
     if args.kernel_only in ("chain", "bchain"):
         return run_chain_kernel(args)
     torch.cuda.init()
@@ -1106,7 +1167,7 @@ def main():
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE object of the main line")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--kernel-only", choices=["swiglu", "down", "qkv", "lmhead", "prefill_gateup", "prefill_down",
-                                              "prefill_qkv", "prefill_o", "prefill_swiglu", "chain", "bchain", "moe_swiglu", "moe_down", "attn"],
+                                              "prefill_qkv", "prefill_o", "prefill_swiglu", "chain", "bchain", "moe_swiglu", "moe_down", "attn", "q81_matmul"],
                     help="time one kernel of the step at its bench shape (profiling target)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers for --kernel-only chain")

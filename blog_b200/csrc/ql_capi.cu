@@ -1209,6 +1209,46 @@ int ql_quant_gemv_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_
     return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quant_gemv_q8_1");
 }
 
+int ql_quant_matmul_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_q8_1, float *y, int out_dim,
+                         int in_dim, int m) {
+    t_launches = 0;
+    if (t != kQ4_K && t != kQ6_K && t != kQ5_0 && t != kQ8_0)
+        return fail(QL_EINVAL, "ql_quant_matmul_q8_1: quant_type must be Q4_K, Q6_K, Q5_0 or Q8_0");
+    if (out_dim < 0 || m < 0) return fail(QL_EINVAL, "ql_quant_matmul_q8_1: negative size");
+    if (out_dim == 0 || m == 0) return QL_OK;
+    int st = check_weight(t, w, rb, 0, in_dim, "ql_quant_matmul_q8_1");
+    if (st) return st;
+    if (!x_q8_1 || !y) return fail(QL_EINVAL, "ql_quant_matmul_q8_1: null pointer");
+    if (reinterpret_cast<uintptr_t>(x_q8_1) % 4)
+        return fail(QL_EINVAL, "ql_quant_matmul_q8_1: x_q8_1 must be 4-byte aligned");
+    Workspace *ws = workspace(&st);
+    if (!ws) return st;
+    const int pitch = q81_mm_row_pitch(rb);
+    if (reinterpret_cast<uintptr_t>(w) % 16 || (size_t)64 * pitch > 232448 - 1024) {
+        // rows too long to stage 64 of them (or an unaligned base): the GEMV per token row
+        for (int r = 0; r < m; ++r) {
+            cudaError_t e = gemv_q81_launch(t, w, rb, x_q8_1 + (size_t)r * q81_row_bytes(in_dim), y + (size_t)r * out_dim,
+                                            out_dim, in_dim, g_stream);
+            ++t_launches;
+            if (e != cudaSuccess) return cuda_fail(e, "ql_quant_matmul_q8_1");
+        }
+        return QL_OK;
+    }
+    Q81MmArgs a{};
+    a.w = w;
+    a.rb = rb;
+    a.xq = x_q8_1;
+    a.y = y;
+    a.out_dim = out_dim;
+    a.in_dim = in_dim;
+    a.m = m;
+    a.row_pitch = pitch;
+    a.err = ws->err;
+    cudaError_t e = matmul_q81_launch(t, a, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quant_matmul_q8_1");
+}
+
 int ql_quant_embedding(int32_t t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n) {
     t_launches = 0;
     if (n < 0) return fail(QL_EINVAL, "ql_quant_embedding: negative size");

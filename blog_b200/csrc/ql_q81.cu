@@ -137,7 +137,244 @@ __global__ void __launch_bounds__(32 * kQ81Warps) gemv_q81_kernel(const uint8_t 
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) y[row] = acc;
 }
+// ---------------------------------------------------------------------------------------------
+// Q8_1 matmul for m token rows (the reference's quant_matmul_q8_1_kernel, kernel.cu:2304-2400:
+// the GEMV's per-block formula for every (token, output row)) on the integer tensor cores.  CTA =
+// 64 weight rows (4 warps x 16) x up to 64 tokens; each warp's 16 rows are staged once in shared
+// memory (one bulk copy per row into a slot whose pitch is 16 mod 32 bytes: the 8 rows a quad reads
+// fall in distinct banks); per 32-element block the quants are an exact int8 A fragment, the Q8_1
+// activations the int8 B fragment, one mma.sync.m16n8k32.s8 per 8 tokens (Q6_K: two k16 MMAs, one
+// per 16-element scale group), then acc(row, token) = fmaf(d_w sc d_x, qdot, acc) (- dmin m sum_x)
+// in block order, the reference's expression for each output.
+// ---------------------------------------------------------------------------------------------
+constexpr int kMmThreads = 128;
+constexpr int kMmTokens = 64;  // tokens per CTA: 4 passes of 16 (two n-tiles of 8)
+
+__device__ __forceinline__ void imma_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+
+struct MmBlock {
+    uint32_t a[4];  // int8 quants: {row g: k 4c.., row g+8: k 4c.., row g: k 16 + 4c.., row g+8: k 16 + 4c..}
+    float s[2][2];  // per row (g, g + 8): Q4_K {d sc, dmin m}; Q6_K {d s0, d s1}; Q5_0 / Q8_0 {d, -}
+};
+
+template <int FMT>
+__device__ __forceinline__ void mm_decode(const uint8_t *row0, const uint8_t *row1, int b, int c, MmBlock &o) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t *rp = h ? row1 : row0;
+        if (FMT == kQ4_K) {
+            const int sb = b >> 3, j = b & 7;
+            const uint8_t *base = rp + 144 * sb;
+            const int sh = 4 * (j & 1);
+            o.a[h] = (*reinterpret_cast<const uint32_t *>(base + 16 + 32 * (j >> 1) + 4 * c) >> sh) & 0x0F0F0F0Fu;
+            o.a[2 + h] = (*reinterpret_cast<const uint32_t *>(base + 32 + 32 * (j >> 1) + 4 * c) >> sh) & 0x0F0F0F0Fu;
+            const uint8_t *s = base + 4;  // q4k_scale_min (reference kernel.cu:913-921)
+            uint32_t sc, mn;
+            if (j < 4) {
+                sc = s[j] & 63u;
+                mn = s[j + 4] & 63u;
+            } else {
+                sc = (s[j + 4] & 0xFu) | ((uint32_t)(s[j - 4] >> 6) << 4);
+                mn = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+            }
+            const uint32_t dd = *reinterpret_cast<const uint32_t *>(base);
+            o.s[h][0] = half_bits_to_float(dd) * (float)sc;
+            o.s[h][1] = half_bits_to_float(dd >> 16) * (float)mn;
+        } else if (FMT == kQ6_K) {
+            const int sb = b >> 3, sub = b & 7, hf = sub >> 2, grp = sub & 3;
+            const uint8_t *base = rp + 210 * sb;
+            const uint8_t *ql = base + 64 * hf + ((grp & 1) ? 32 : 0), *qh = base + 128 + 32 * hf;
+            const int lsh = (grp >> 1) ? 4 : 0, hsh = 2 * grp;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int e = 16 * half + 4 * c;
+                const uint32_t l = ld_u16_pair(ql + e), hh = ld_u16_pair(qh + e);
+                o.a[2 * half + h] = __vsub4(((l >> lsh) & 0x0F0F0F0Fu) | (((hh >> hsh) & 0x03030303u) << 4), 0x20202020u);
+            }
+            const int8_t *scl = reinterpret_cast<const int8_t *>(base + 192) + 8 * hf + 2 * grp;
+            const float dw = half_bits_to_float(*reinterpret_cast<const uint16_t *>(base + 208));
+            o.s[h][0] = dw;
+            o.s[h][1] = 0.f;
+            (void)scl;
+        } else if (FMT == kQ5_0) {
+            const uint8_t *base = rp + 22 * b;
+            const uint32_t qh = ld_u16_pair(base + 2), l = ld_u16_pair(base + 6 + 4 * c);
+            o.a[h] = __vsub4((l & 0x0F0F0F0Fu) | bits_to_byte4((qh >> (4 * c)) & 0xFu), 0x10101010u);
+            o.a[2 + h] = __vsub4(((l >> 4) & 0x0F0F0F0Fu) | bits_to_byte4((qh >> (16 + 4 * c)) & 0xFu), 0x10101010u);
+            o.s[h][0] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(base));
+            o.s[h][1] = 0.f;
+        } else {  // Q8_0
+            const uint8_t *base = rp + 34 * b;
+            o.a[h] = ld_u16_pair(base + 2 + 4 * c);
+            o.a[2 + h] = ld_u16_pair(base + 18 + 4 * c);
+            o.s[h][0] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(base));
+            o.s[h][1] = 0.f;
+        }
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kMmThreads) q81_matmul_kernel(const __grid_constant__ Q81MmArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint64_t bar[4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int wrow0 = blockIdx.x * 64 + 16 * warp, tok0 = blockIdx.y * kMmTokens;
+    int nr = min(16, a.out_dim - wrow0);
+    const int P = a.row_pitch, bpr = (a.in_dim + 31) / 32;
+    uint8_t *slab = smem + (size_t)warp * 16 * P;
+    const uint8_t *wbase = a.w + (size_t)wrow0 * a.rb;
+    if (nr > 0) {
+        uintptr_t lo = 0, hi = 0, end = 0;
+        if (lane < nr) {
+            const uintptr_t st = reinterpret_cast<uintptr_t>(wbase + (size_t)lane * a.rb);
+            lo = st & ~uintptr_t(15);
+            end = st + a.rb;
+            hi = end & ~uintptr_t(15);
+        }
+        const uint32_t tx = __reduce_add_sync(0xffffffffu, (uint32_t)(hi - lo));
+        if (lane == 0) {
+            mbar_init(&bar[warp], 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            mbar_arrive_expect_tx(&bar[warp], tx);
+        }
+        __syncwarp();
+        if (lane < nr) {
+            uint8_t *dst = slab + (size_t)lane * P;
+            if (hi > lo)
+                bulk_g2s(dst, reinterpret_cast<const void *>(lo), (uint32_t)(hi - lo), &bar[warp],
+                         l2_evict_first_policy());
+            for (uintptr_t q = hi; q < end; ++q) dst[q - lo] = *reinterpret_cast<const uint8_t *>(q);
+        }
+        __syncwarp();
+        if (!mbar_wait(&bar[warp], 0u, a.err, kErrWaitFull)) {
+            mbar_wait(&bar[warp], 0u, nullptr, 0);  // never leave with the copies in flight
+            nr = 0;
+        }
+    }
+    if (nr <= 0) return;
+    const int sh0 = (int)(reinterpret_cast<uintptr_t>(wbase + (size_t)g * a.rb) & 15);
+    const int sh1 = (int)(reinterpret_cast<uintptr_t>(wbase + (size_t)(g + 8) * a.rb) & 15);
+    const uint8_t *row0 = slab + (size_t)g * P + sh0, *row1 = slab + (size_t)(g + 8) * P + sh1;
+    // all of the CTA's tokens (up to 8 tiles of 8) per weight block: the block is decoded once and the
+    // tiles' activation loads go out together
+    const size_t xrb = (size_t)bpr * 36;
+    const int ntile = (min(kMmTokens, a.m - tok0) + 7) >> 3;
+    int xrow[8], srow[8][2];  // token rows of the B operand (8j + g) and of the scales (8j + 2c, + 1)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        xrow[j] = min(tok0 + 8 * j + g, a.m - 1);
+        srow[j][0] = min(tok0 + 8 * j + 2 * c, a.m - 1);
+        srow[j][1] = min(tok0 + 8 * j + 2 * c + 1, a.m - 1);
+    }
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int b = 0; b < bpr; ++b) {
+        MmBlock blk;
+        mm_decode<FMT>(row0, row1, b, c, blk);
+        const int8_t *scl[2] = {nullptr, nullptr};
+        if (FMT == kQ6_K) {
+            const int sb = b >> 3, sub = b & 7, hf = sub >> 2, grp = sub & 3;
+            scl[0] = reinterpret_cast<const int8_t *>(row0 + 210 * sb + 192) + 8 * hf + 2 * grp;
+            scl[1] = reinterpret_cast<const int8_t *>(row1 + 210 * sb + 192) + 8 * hf + 2 * grp;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j < ntile) {
+                const uint8_t *bb = a.xq + (size_t)xrow[j] * xrb + (size_t)b * 36 + 4;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(bb + 4 * c);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(bb + 16 + 4 * c);
+                float dx[2], sx[2];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const uint32_t ds = *reinterpret_cast<const uint32_t *>(a.xq + (size_t)srow[j][q] * xrb + (size_t)b * 36);
+                    dx[q] = half_bits_to_float(ds);
+                    sx[q] = half_bits_to_float(ds >> 16);
+                }
+                if (FMT == kQ6_K) {
+                    int t0v[4] = {0, 0, 0, 0}, t1v[4] = {0, 0, 0, 0};
+                    imma_k16(t0v, blk.a[0], blk.a[1], b0);
+                    imma_k16(t1v, blk.a[2], blk.a[3], b1);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int h = q >> 1;
+                        acc[j][q] = fmaf(blk.s[h][0] * dx[q & 1],
+                                         (float)scl[h][0] * (float)t0v[q] + (float)scl[h][1] * (float)t1v[q], acc[j][q]);
+                    }
+                } else {
+                    int t[4] = {0, 0, 0, 0};
+                    imma_k32(t, blk.a, b0, b1);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int h = q >> 1;
+                        acc[j][q] = fmaf(blk.s[h][0] * dx[q & 1], (float)t[q], acc[j][q]);
+                        if (FMT == kQ4_K) acc[j][q] -= blk.s[h][1] * sx[q & 1];
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int tok = tok0 + 8 * j + 2 * c + (q & 1), r = g + 8 * (q >> 1);
+            if (j < ntile && tok < a.m && r < nr) a.y[(size_t)tok * a.out_dim + wrow0 + r] = acc[j][q];
+        }
+}
 }  // namespace
+
+int q81_mm_row_pitch(size_t row_bytes) {
+    int p = (int)((row_bytes + 15 + 15) & ~size_t(15));
+    if (p % 32 == 0) p += 16;
+    return p;
+}
+
+cudaError_t matmul_q81_launch(int fmt, const Q81MmArgs &a, cudaStream_t s) {
+    const size_t smem = (size_t)4 * 16 * a.row_pitch;
+    const dim3 grid((a.out_dim + 63) / 64, (a.m + kMmTokens - 1) / kMmTokens);
+    cudaError_t e;
+    switch (fmt) {
+    case kQ4_K:
+        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        q81_matmul_kernel<kQ4_K><<<grid, kMmThreads, smem, s>>>(a);
+        break;
+    case kQ6_K:
+        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        q81_matmul_kernel<kQ6_K><<<grid, kMmThreads, smem, s>>>(a);
+        break;
+    case kQ5_0:
+        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ5_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        q81_matmul_kernel<kQ5_0><<<grid, kMmThreads, smem, s>>>(a);
+        break;
+    case kQ8_0:
+        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        q81_matmul_kernel<kQ8_0><<<grid, kMmThreads, smem, s>>>(a);
+        break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
 
 size_t q81_row_bytes(int in_dim) { return (size_t)((in_dim + 31) / 32) * 36; }
 

@@ -291,6 +291,11 @@ QL_API int ql_quantize_q8_1(const float *x, uint8_t *x_q8_1, int in_dim, int m, 
  * the block scales in fp32 (launch_quant_gemv_q8_1, launch.cu:222-245); Q4_K, Q6_K, Q5_0, Q8_0. */
 QL_API int ql_quant_gemv_q8_1(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const uint8_t *x_q8_1,
                               float *y, int out_dim, int in_dim);
+/* y[m][out_dim] for m Q8_1 activation rows (ql_q8_1_row_bytes(in_dim) apart), the GEMV's per-block
+ * formula for every (token, output row), on the integer tensor cores (launch_quant_matmul_q8_1,
+ * launch.cu:512-531); Q4_K, Q6_K, Q5_0, Q8_0. */
+QL_API int ql_quant_matmul_q8_1(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const uint8_t *x_q8_1,
+                                float *y, int out_dim, int in_dim, int m);
 
 /* ---- embedding, dequant, argmax (reference kernel.cuh:141-142, 244-253, 347) ----- */
 QL_API int ql_quant_embedding(int32_t quant_type, const int *input, float *output, const uint8_t *table, size_t row_bytes,

@@ -383,6 +383,7 @@ def ref_lib():
             "ref_full_attention_attend_batch": (None, [P, P, P, P, I, P, I, I, I, I, I, I]),
             "ref_quantize_q8_1": (None, [P, P, I, I, I]),
             "ref_quant_gemv_q8_1": (None, [I, P, SZ, P, P, I, I]),
+            "ref_quant_matmul_q8_1": (None, [I, P, SZ, P, P, I, I, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

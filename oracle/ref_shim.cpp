@@ -89,4 +89,10 @@ void ref_quant_gemv_q8_1(int t, const uint8_t *w, size_t rb, const uint8_t *xq, 
     launch_quant_gemv_q8_1(static_cast<DType>(t), w, rb, xq, y, out_dim, in_dim);
 }
 
+// kernel.cuh:53-55
+void ref_quant_matmul_q8_1(int t, const uint8_t *w, size_t rb, const uint8_t *xq, float *y, int out_dim, int in_dim,
+                           int m) {
+    launch_quant_matmul_q8_1(static_cast<DType>(t), w, rb, xq, y, out_dim, in_dim, m);
+}
+
 }  // extern "C"

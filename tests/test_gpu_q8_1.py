@@ -77,6 +77,32 @@ def test_gemv_q8_1_matches_oracle_and_reference(t, n, k):
         assert rel_l2(got, host(ref)) < TOL
 
 
+@pytest.mark.parametrize("t,n,k,m", [(O.Q4_K, 1000, 2048, 100), (O.Q6_K, 300, 1024, 37), (O.Q5_0, 520, 1408, 64),
+                                     (O.Q8_0, 777, 896, 16), (O.Q8_0, 64, 4096, 3)])
+def test_matmul_q8_1_matches_oracle_and_reference(t, n, k, m):
+    """The tensor-core Q8_1 matmul (ragged row and token tiles; Q8_0 with in_dim 4096 runs the
+    per-token GEMV) against the oracle's per-token Q8_1 GEMV and the reference's matmul kernel."""
+    import torch
+    w = make_weights(t, n, k, seed=3 * n + k + t)
+    rb = O.row_bytes(t, k)
+    x = np.random.default_rng(m + k).standard_normal((m, k)).astype(np.float32)
+    xq = O.quantize_q8_1(x, t == O.Q4_K)
+    y = torch.full((m, n), float("nan"), device="cuda:0")
+    Q.quant_matmul_q8_1(t, dev(w).data_ptr(), rb, dev(xq).data_ptr(), y.data_ptr(), n, k, m)
+    got = host(y)
+    want = np.stack([O.gemv_q8_1(t, w, rb, xq[i], n, k) for i in range(m)])
+    err = rel_l2(got, want)
+    print(f"Q8_1 matmul type {t} {n}x{k} M={m}: rel_l2 {err:.2e} (launches {Q.last_launch_count()})")
+    assert err < TOL
+    R = O.ref_lib()
+    if R is not None:
+        ref = torch.zeros((m, n), device="cuda:0")
+        R.ref_set_stream(torch.cuda.current_stream().cuda_stream)
+        R.ref_quant_matmul_q8_1(t, dev(w).data_ptr(), rb, dev(xq).data_ptr(), ref.data_ptr(), n, k, m)
+        torch.cuda.synchronize()
+        assert rel_l2(got, host(ref)) < TOL
+
+
 def test_q8_1_rejects_unsupported_types():
     import torch
     x = torch.zeros(64, device="cuda:0")
