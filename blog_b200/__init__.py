@@ -58,6 +58,9 @@ SIGNATURES = {
     "ql_quantize_q8_1": (I, [P, P, I, I, I]),
     "ql_quant_gemv_q8_1": (I, [I32, P, SZ, P, P, I, I]),
     "ql_quant_matmul_q8_1": (I, [I32, P, SZ, P, P, I, I, I]),
+    "ql_q8_1_mmq_row_bytes": (SZ, [I]),
+    "ql_quantize_q8_1_mmq": (I, [P, P, I, I, I]),
+    "ql_quant_matmul_q8_1_mmq": (I, [I32, P, SZ, P, P, I, I, I]),
     "ql_full_attention_attend_batch": (I, [P, P, P, P, I, P, I, I, I, I, I, I]),
     "ql_moe_swiglu_grouped": (I, [I32, P, P, SZ, SZ, SZ, SZ, P, I64, P, I, I, P, I, I, I, I]),
     "ql_moe_down_grouped_accum_ordered": (I, [I32, P, SZ, SZ, P, P, I, I, P, P, I64, I, I, I, I]),
@@ -327,6 +330,18 @@ def quant_gemv_q8_1(t, w, rb, xq, y, out_dim, in_dim):
 
 def quant_matmul_q8_1(t, w, rb, xq, y, out_dim, in_dim, m):
     _call("ql_quant_matmul_q8_1", t, w, rb, xq, y, out_dim, in_dim, m)
+
+
+def q8_1_mmq_row_bytes(in_dim):
+    return lib().ql_q8_1_mmq_row_bytes(in_dim)
+
+
+def quantize_q8_1_mmq(x, xq, in_dim, m, store_raw_sum=False):
+    _call("ql_quantize_q8_1_mmq", x, xq, in_dim, m, int(store_raw_sum))
+
+
+def quant_matmul_q8_1_mmq(t, w, rb, xq, y, out_dim, in_dim, m):
+    _call("ql_quant_matmul_q8_1_mmq", t, w, rb, xq, y, out_dim, in_dim, m)
 
 
 def full_attention_attend(q, gate, kc, vc, kv_bf16, attn, n_heads, kv_heads, head_dim, max_seq_len, pos_dev):

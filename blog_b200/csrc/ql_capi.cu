@@ -1186,9 +1186,25 @@ int ql_quantize_q8_1(const float *x, uint8_t *x_q8_1, int in_dim, int m, int sto
         return fail(QL_EINVAL, "ql_quantize_q8_1: x_q8_1 must be 4-byte aligned");
     int st;
     if (!workspace(&st)) return st;
-    cudaError_t e = quantize_q81_launch(x, x_q8_1, in_dim, m, store_raw_sum != 0, g_stream);
+    cudaError_t e = quantize_q81_launch(x, x_q8_1, in_dim, m, store_raw_sum != 0, false, g_stream);
     ++t_launches;
     return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quantize_q8_1");
+}
+
+size_t ql_q8_1_mmq_row_bytes(int in_dim) { return in_dim > 0 ? q81_mmq_row_bytes(in_dim) : 0; }
+
+int ql_quantize_q8_1_mmq(const float *x, uint8_t *x_mmq, int in_dim, int m, int store_raw_sum) {
+    t_launches = 0;
+    if (in_dim <= 0 || m < 0) return fail(QL_EINVAL, "ql_quantize_q8_1_mmq: need in_dim > 0 and m >= 0");
+    if (m == 0) return QL_OK;
+    if (!x || !x_mmq) return fail(QL_EINVAL, "ql_quantize_q8_1_mmq: null pointer");
+    if (reinterpret_cast<uintptr_t>(x_mmq) % 4)
+        return fail(QL_EINVAL, "ql_quantize_q8_1_mmq: x_q8_1 must be 4-byte aligned");
+    int st;
+    if (!workspace(&st)) return st;
+    cudaError_t e = quantize_q81_launch(x, x_mmq, in_dim, m, store_raw_sum != 0, true, g_stream);
+    ++t_launches;
+    return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quantize_q8_1_mmq");
 }
 
 int ql_quant_gemv_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_q8_1, float *y, int out_dim,
@@ -1209,8 +1225,9 @@ int ql_quant_gemv_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_
     return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quant_gemv_q8_1");
 }
 
-int ql_quant_matmul_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_q8_1, float *y, int out_dim,
-                         int in_dim, int m) {
+namespace {
+int matmul_q81(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_q8_1, float *y, int out_dim, int in_dim,
+               int m, bool mmq) {
     t_launches = 0;
     if (t != kQ4_K && t != kQ6_K && t != kQ5_0 && t != kQ8_0)
         return fail(QL_EINVAL, "ql_quant_matmul_q8_1: quant_type must be Q4_K, Q6_K, Q5_0 or Q8_0");
@@ -1224,6 +1241,9 @@ int ql_quant_matmul_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *
     Workspace *ws = workspace(&st);
     if (!ws) return st;
     const int pitch = q81_mm_row_pitch(rb);
+    if (mmq && (reinterpret_cast<uintptr_t>(w) % 16 || (size_t)64 * pitch > 232448 - 1024))
+        return fail(QL_EINVAL, "ql_quant_matmul_q8_1_mmq: weight rows must be 16-byte aligned and short enough to "
+                               "stage 64 of them (about 3.5 KB)");
     if (reinterpret_cast<uintptr_t>(w) % 16 || (size_t)64 * pitch > 232448 - 1024) {
         // rows too long to stage 64 of them (or an unaligned base): the GEMV per token row
         for (int r = 0; r < m; ++r) {
@@ -1244,9 +1264,21 @@ int ql_quant_matmul_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *
     a.m = m;
     a.row_pitch = pitch;
     a.err = ws->err;
-    cudaError_t e = matmul_q81_launch(t, a, g_stream);
+    cudaError_t e = matmul_q81_launch(t, a, mmq, g_stream);
     ++t_launches;
     return e == cudaSuccess ? QL_OK : cuda_fail(e, "ql_quant_matmul_q8_1");
+}
+}  // namespace
+
+int ql_quant_matmul_q8_1(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_q8_1, float *y, int out_dim,
+                         int in_dim, int m) {
+    return matmul_q81(t, w, rb, x_q8_1, y, out_dim, in_dim, m, false);
+}
+
+int ql_quant_matmul_q8_1_mmq(int32_t t, const uint8_t *w, size_t rb, const uint8_t *x_mmq, float *y, int out_dim,
+                             int in_dim, int m) {
+    if (t != kQ4_K && t != kQ6_K) return fail(QL_EINVAL, "ql_quant_matmul_q8_1_mmq: quant_type must be Q4_K or Q6_K");
+    return matmul_q81(t, w, rb, x_mmq, y, out_dim, in_dim, m, true);
 }
 
 int ql_quant_embedding(int32_t t, const int *ids, float *out, const uint8_t *table, size_t rb, int hidden, int n) {

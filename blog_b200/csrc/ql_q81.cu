@@ -23,6 +23,9 @@ namespace {
 
 constexpr int kQ81Warps = 8;
 
+// MMQ: the reference's packed layout (quantize_q8_1_mmq_kernel, kernel.cu:1724-1765): 144-byte groups
+// of 4 consecutive blocks, group-major ([group][row]), each {4 x (f16 d, f16 sum), 4 x 32 int8}.
+template <bool MMQ>
 __global__ void __launch_bounds__(32 * kQ81Warps) quantize_q81_kernel(const float *__restrict__ x,
                                                                      uint8_t *__restrict__ xq, int in_dim, int m,
                                                                      int bpr, int store_raw_sum) {
@@ -43,13 +46,21 @@ __global__ void __launch_bounds__(32 * kQ81Warps) quantize_q81_kernel(const floa
     q = max(-127, min(127, q));
     int qs = q;
     for (int o = 16; o > 0; o >>= 1) qs += __shfl_down_sync(0xffffffffu, qs, o);
-    uint8_t *dst = xq + (size_t)blk * 36;
-    if (lane == 0) {
-        *reinterpret_cast<uint16_t *>(dst) = __half_as_ushort(__float2half(d));
-        const float s = store_raw_sum ? raw : d * (float)qs;
-        *reinterpret_cast<uint16_t *>(dst + 2) = __half_as_ushort(__float2half(s));
+    uint8_t *ds, *qd;
+    if (MMQ) {
+        uint8_t *grp = xq + ((size_t)(qb >> 2) * m + row) * 144;
+        ds = grp + 4 * (qb & 3);
+        qd = grp + 16 + 32 * (qb & 3);
+    } else {
+        ds = xq + (size_t)blk * 36;
+        qd = ds + 4;
     }
-    reinterpret_cast<int8_t *>(dst + 4)[lane] = (int8_t)q;
+    if (lane == 0) {
+        *reinterpret_cast<uint16_t *>(ds) = __half_as_ushort(__float2half(d));
+        const float s = store_raw_sum ? raw : d * (float)qs;
+        *reinterpret_cast<uint16_t *>(ds + 2) = __half_as_ushort(__float2half(s));
+    }
+    reinterpret_cast<int8_t *>(qd)[lane] = (int8_t)q;
 }
 
 __device__ __forceinline__ uint32_t ld_u16_pair(const uint8_t *p) {  // 4 bytes at a 2-byte-aligned address
@@ -225,7 +236,7 @@ __device__ __forceinline__ void mm_decode(const uint8_t *row0, const uint8_t *ro
     }
 }
 
-template <int FMT>
+template <int FMT, bool MMQ>
 __global__ void __launch_bounds__(kMmThreads) q81_matmul_kernel(const __grid_constant__ Q81MmArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar[4];
@@ -293,13 +304,17 @@ __global__ void __launch_bounds__(kMmThreads) q81_matmul_kernel(const __grid_con
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             if (j < ntile) {
-                const uint8_t *bb = a.xq + (size_t)xrow[j] * xrb + (size_t)b * 36 + 4;
+                // plain rows: block b at b * 36 of the token's row; MMQ: group b / 4 of the token, sub-block b % 4
+                const uint8_t *bb = MMQ ? a.xq + ((size_t)(b >> 2) * a.m + xrow[j]) * 144 + 16 + 32 * (b & 3)
+                                        : a.xq + (size_t)xrow[j] * xrb + (size_t)b * 36 + 4;
                 const uint32_t b0 = *reinterpret_cast<const uint32_t *>(bb + 4 * c);
                 const uint32_t b1 = *reinterpret_cast<const uint32_t *>(bb + 16 + 4 * c);
                 float dx[2], sx[2];
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
-                    const uint32_t ds = *reinterpret_cast<const uint32_t *>(a.xq + (size_t)srow[j][q] * xrb + (size_t)b * 36);
+                    const uint8_t *dsp = MMQ ? a.xq + ((size_t)(b >> 2) * a.m + srow[j][q]) * 144 + 4 * (b & 3)
+                                             : a.xq + (size_t)srow[j][q] * xrb + (size_t)b * 36;
+                    const uint32_t ds = *reinterpret_cast<const uint32_t *>(dsp);
                     dx[q] = half_bits_to_float(ds);
                     sx[q] = half_bits_to_float(ds >> 16);
                 }
@@ -342,46 +357,45 @@ int q81_mm_row_pitch(size_t row_bytes) {
     return p;
 }
 
-cudaError_t matmul_q81_launch(int fmt, const Q81MmArgs &a, cudaStream_t s) {
-    const size_t smem = (size_t)4 * 16 * a.row_pitch;
-    const dim3 grid((a.out_dim + 63) / 64, (a.m + kMmTokens - 1) / kMmTokens);
-    cudaError_t e;
+namespace {
+template <int FMT, bool MMQ>
+cudaError_t mm_launch_t(const Q81MmArgs &a, size_t smem, dim3 grid, cudaStream_t s) {
+    cudaError_t e =
+        cudaFuncSetAttribute(q81_matmul_kernel<FMT, MMQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    q81_matmul_kernel<FMT, MMQ><<<grid, kMmThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+template <bool MMQ>
+cudaError_t mm_launch_fmt(int fmt, const Q81MmArgs &a, size_t smem, dim3 grid, cudaStream_t s) {
     switch (fmt) {
-    case kQ4_K:
-        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem)) != cudaSuccess)
-            return e;
-        q81_matmul_kernel<kQ4_K><<<grid, kMmThreads, smem, s>>>(a);
-        break;
-    case kQ6_K:
-        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem)) != cudaSuccess)
-            return e;
-        q81_matmul_kernel<kQ6_K><<<grid, kMmThreads, smem, s>>>(a);
-        break;
-    case kQ5_0:
-        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ5_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem)) != cudaSuccess)
-            return e;
-        q81_matmul_kernel<kQ5_0><<<grid, kMmThreads, smem, s>>>(a);
-        break;
-    case kQ8_0:
-        if ((e = cudaFuncSetAttribute(q81_matmul_kernel<kQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem)) != cudaSuccess)
-            return e;
-        q81_matmul_kernel<kQ8_0><<<grid, kMmThreads, smem, s>>>(a);
-        break;
+    case kQ4_K: return mm_launch_t<kQ4_K, MMQ>(a, smem, grid, s);
+    case kQ6_K: return mm_launch_t<kQ6_K, MMQ>(a, smem, grid, s);
+    case kQ5_0: return mm_launch_t<kQ5_0, MMQ>(a, smem, grid, s);
+    case kQ8_0: return mm_launch_t<kQ8_0, MMQ>(a, smem, grid, s);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t matmul_q81_launch(int fmt, const Q81MmArgs &a, bool mmq, cudaStream_t s) {
+    const size_t smem = (size_t)4 * 16 * a.row_pitch;
+    const dim3 grid((a.out_dim + 63) / 64, (a.m + kMmTokens - 1) / kMmTokens);
+    return mmq ? mm_launch_fmt<true>(fmt, a, smem, grid, s) : mm_launch_fmt<false>(fmt, a, smem, grid, s);
 }
 
 size_t q81_row_bytes(int in_dim) { return (size_t)((in_dim + 31) / 32) * 36; }
 
-cudaError_t quantize_q81_launch(const float *x, uint8_t *xq, int in_dim, int m, bool store_raw_sum, cudaStream_t s) {
-    const int bpr = (in_dim + 31) / 32;
+size_t q81_mmq_row_bytes(int in_dim) { return (size_t)((in_dim + 127) / 128) * 144; }
+
+cudaError_t quantize_q81_launch(const float *x, uint8_t *xq, int in_dim, int m, bool store_raw_sum, bool mmq,
+                                cudaStream_t s) {
+    const int bpr = mmq ? (in_dim + 127) / 128 * 4 : (in_dim + 31) / 32;  // MMQ: every block of every group
     const long long blocks = ((long long)m * bpr + kQ81Warps - 1) / kQ81Warps;
-    quantize_q81_kernel<<<(unsigned)blocks, 32 * kQ81Warps, 0, s>>>(x, xq, in_dim, m, bpr, store_raw_sum ? 1 : 0);
+    if (mmq)
+        quantize_q81_kernel<true><<<(unsigned)blocks, 32 * kQ81Warps, 0, s>>>(x, xq, in_dim, m, bpr, store_raw_sum ? 1 : 0);
+    else
+        quantize_q81_kernel<false><<<(unsigned)blocks, 32 * kQ81Warps, 0, s>>>(x, xq, in_dim, m, bpr, store_raw_sum ? 1 : 0);
     return cudaGetLastError();
 }
 

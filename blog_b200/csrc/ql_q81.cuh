@@ -17,9 +17,11 @@ struct Q81MmArgs {
 };
 
 size_t q81_row_bytes(int in_dim);
+size_t q81_mmq_row_bytes(int in_dim);
 int q81_mm_row_pitch(size_t row_bytes);
-cudaError_t matmul_q81_launch(int fmt, const Q81MmArgs &a, cudaStream_t s);
-cudaError_t quantize_q81_launch(const float *x, uint8_t *xq, int in_dim, int m, bool store_raw_sum, cudaStream_t s);
+cudaError_t matmul_q81_launch(int fmt, const Q81MmArgs &a, bool mmq, cudaStream_t s);
+cudaError_t quantize_q81_launch(const float *x, uint8_t *xq, int in_dim, int m, bool store_raw_sum, bool mmq,
+                                cudaStream_t s);
 cudaError_t gemv_q81_launch(int fmt, const uint8_t *w, size_t rb, const uint8_t *xq, float *y, int out_dim, int in_dim,
                             cudaStream_t s);
 

@@ -296,6 +296,14 @@ QL_API int ql_quant_gemv_q8_1(int32_t quant_type, const uint8_t *weight, size_t 
  * launch.cu:512-531); Q4_K, Q6_K, Q5_0, Q8_0. */
 QL_API int ql_quant_matmul_q8_1(int32_t quant_type, const uint8_t *weight, size_t row_bytes, const uint8_t *x_q8_1,
                                 float *y, int out_dim, int in_dim, int m);
+/* The reference's packed (MMQ) Q8_1 layout (kernel.cuh:56-61): 144-byte groups of 4 blocks
+ * {4 x (f16 d, f16 sum), 4 x 32 int8}, group-major ([group][row]); ql_q8_1_mmq_row_bytes(in_dim)
+ * per row.  The quantizer's bytes equal launch_quantize_q8_1_mmq's; the matmul computes
+ * ql_quant_matmul_q8_1's result from that layout (Q4_K, Q6_K, as launch_quant_matmul_q8_1_mmq). */
+QL_API size_t ql_q8_1_mmq_row_bytes(int in_dim);
+QL_API int ql_quantize_q8_1_mmq(const float *x, uint8_t *x_q8_1_mmq, int in_dim, int m, int store_raw_sum);
+QL_API int ql_quant_matmul_q8_1_mmq(int32_t quant_type, const uint8_t *weight, size_t row_bytes,
+                                    const uint8_t *x_q8_1_mmq, float *y, int out_dim, int in_dim, int m);
 
 /* ---- embedding, dequant, argmax (reference kernel.cuh:141-142, 244-253, 347) ----- */
 QL_API int ql_quant_embedding(int32_t quant_type, const int *input, float *output, const uint8_t *table, size_t row_bytes,

@@ -185,6 +185,22 @@ def quantize_q8_1(x, store_raw_sum=False):
     return out
 
 
+def q8_1_mmq_from_rows(xq_rows, k):
+    """The packed (MMQ) layout of Q8_1 rows [m][q8_1_row_bytes(k)] (quantize_q8_1_mmq_kernel's
+    layout, kernel.cu:1724-1765): per 128 activations a 144-byte group {4 x (d, sum), 4 x 32 int8},
+    group-major; blocks past the row's last are those of zeros (d = sum = 0, q = 0)."""
+    xq_rows = np.atleast_2d(xq_rows)
+    m = xq_rows.shape[0]
+    bpr, groups = (k + 31) // 32, (k + 127) // 128
+    out = np.zeros((groups, m, 144), np.uint8)
+    for b in range(bpr):
+        blk = xq_rows[:, b * 36:(b + 1) * 36]
+        g, sub = b // 4, b % 4
+        out[g, :, 4 * sub:4 * sub + 4] = blk[:, 0:4]
+        out[g, :, 16 + 32 * sub:48 + 32 * sub] = blk[:, 4:36]
+    return out.reshape(-1)
+
+
 def gemv_q8_1(t, w, rb, xq, n, k):
     """y[n] against one Q8_1 activation row (restates quant_gemv_q8_1_kernel, kernel.cu:1767-1865)."""
     w, xq = _c(w, np.uint8), _c(xq, np.uint8)
@@ -384,6 +400,8 @@ def ref_lib():
             "ref_quantize_q8_1": (None, [P, P, I, I, I]),
             "ref_quant_gemv_q8_1": (None, [I, P, SZ, P, P, I, I]),
             "ref_quant_matmul_q8_1": (None, [I, P, SZ, P, P, I, I, I]),
+            "ref_quantize_q8_1_mmq": (None, [P, P, I, I, I]),
+            "ref_quant_matmul_q8_1_mmq": (None, [I, P, SZ, P, P, I, I, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

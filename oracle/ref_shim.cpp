@@ -95,4 +95,13 @@ void ref_quant_matmul_q8_1(int t, const uint8_t *w, size_t rb, const uint8_t *xq
     launch_quant_matmul_q8_1(static_cast<DType>(t), w, rb, xq, y, out_dim, in_dim, m);
 }
 
+// kernel.cuh:57-61
+void ref_quantize_q8_1_mmq(const float *x, uint8_t *xq, int in_dim, int m, int store_raw_sum) {
+    launch_quantize_q8_1_mmq(x, xq, in_dim, m, store_raw_sum != 0);
+}
+void ref_quant_matmul_q8_1_mmq(int t, const uint8_t *w, size_t rb, const uint8_t *xq, float *y, int out_dim,
+                               int in_dim, int m) {
+    launch_quant_matmul_q8_1_mmq(static_cast<DType>(t), w, rb, xq, y, out_dim, in_dim, m);
+}
+
 }  // extern "C"

@@ -103,6 +103,39 @@ def test_matmul_q8_1_matches_oracle_and_reference(t, n, k, m):
         assert rel_l2(got, host(ref)) < TOL
 
 
+@pytest.mark.parametrize("t,n,k,m,raw", [(O.Q4_K, 600, 2048, 40, True), (O.Q6_K, 300, 1024, 19, False)])
+def test_mmq_layout_quantizer_and_matmul(t, n, k, m, raw):
+    """The packed (MMQ) Q8_1 layout: quantizer bytes equal to the oracle's blocks repacked and to the
+    reference's own MMQ quantizer; the matmul from that layout equal to the plain-layout matmul and
+    within 1e-5 of the reference's MMQ matmul kernel."""
+    import torch
+    x = np.random.default_rng(n + m).standard_normal((m, k)).astype(np.float32)
+    xm = torch.zeros(m * Q.q8_1_mmq_row_bytes(k), dtype=torch.uint8, device="cuda:0")
+    Q.quantize_q8_1_mmq(dev(x).data_ptr(), xm.data_ptr(), k, m, raw)
+    got_bytes = host(xm)
+    rows = O.quantize_q8_1(x, raw)
+    assert np.array_equal(got_bytes, O.q8_1_mmq_from_rows(rows, k))
+    R = O.ref_lib()
+    w = make_weights(t, n, k, seed=n + 5 * k)
+    rb = O.row_bytes(t, k)
+    y = torch.full((m, n), float("nan"), device="cuda:0")
+    Q.quant_matmul_q8_1_mmq(t, dev(w).data_ptr(), rb, xm.data_ptr(), y.data_ptr(), n, k, m)
+    yp = torch.full((m, n), float("nan"), device="cuda:0")
+    Q.quant_matmul_q8_1(t, dev(w).data_ptr(), rb, dev(rows).data_ptr(), yp.data_ptr(), n, k, m)
+    assert np.array_equal(host(y), host(yp))
+    if R is not None:
+        ref = torch.zeros(m * Q.q8_1_mmq_row_bytes(k), dtype=torch.uint8, device="cuda:0")
+        R.ref_set_stream(torch.cuda.current_stream().cuda_stream)
+        R.ref_quantize_q8_1_mmq(dev(x).data_ptr(), ref.data_ptr(), k, m, int(raw))
+        yr = torch.zeros((m, n), device="cuda:0")
+        R.ref_quant_matmul_q8_1_mmq(t, dev(w).data_ptr(), rb, xm.data_ptr(), yr.data_ptr(), n, k, m)
+        torch.cuda.synchronize()
+        assert np.array_equal(got_bytes, host(ref))
+        err = rel_l2(host(y), host(yr))
+        print(f"MMQ matmul type {t}: rel_l2 {err:.2e} vs the reference's MMQ kernel")
+        assert err < TOL
+
+
 def test_q8_1_rejects_unsupported_types():
     import torch
     x = torch.zeros(64, device="cuda:0")
