@@ -528,7 +528,7 @@ __host__ __device__ constexpr int ta_row_bytes(int fmt) { return fmt == kQ8_0 ? 
 // Raw weight ring depth: 4 stages of 128 x 144 B, or 2 of 128 x 272 B (Q8_0), within 227 KB.
 __host__ __device__ constexpr int ta_ring(int fmt) { return fmt == kQ8_0 ? 2 : kTaNR; }
 __host__ __device__ constexpr int ta_smem(int ntok, int fmt) {
-    return 1024 + kTaNX * ntok * 128 + ta_ring(fmt) * 128 * ta_row_bytes(fmt) + 2 * 64 * 33 * 4 + 256;
+    return 1024 + kTaNX * ntok * 128 + ta_ring(fmt) * 128 * ta_row_bytes(fmt) + 256;
 }
 static_assert(ta_smem(256, kQ8_0) <= 232448 && ta_smem(256, kQ4_K) <= 232448, "gemm_ta shared memory");
 
@@ -661,8 +661,7 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sX = smem;
     uint8_t *sR = sX + kTaNX * XB;
-    float *sU = reinterpret_cast<float *>(sR + NR * RBYTES);  // SwiGLU: [2 token halves][64 rows][33]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sU + 2 * 64 * 33);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sR + NR * RBYTES);
     uint64_t *rfull = bars, *rempty = rfull + kTaNR, *xfull = rempty + kTaNR, *xempty = xfull + kTaNX;
     uint64_t *afull = xempty + kTaNX, *aempty = afull + kTaNA, *accfull = aempty + kTaNA;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accfull + 1);
@@ -787,7 +786,10 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
     } else {
         // ------------------- dequantizers, then the epilogue -------------------
         const int q = warp & 3, hf = (warp - 2) >> 2;
-        const int r = 32 * q + lane;  // weight row of the tile = TMEM lane
+        const int r = 32 * q + lane;  // TMEM lane = the MMA's output row
+        // staged weight row this thread decodes: plain = its TMEM lane; SwiGLU = gate row 16q + l (lanes
+        // 0-15) or up row 16q + l - 16 (lanes 16-31), so one warp holds both halves of 16 output columns
+        const int srow = EPI == kGemmSwiglu ? (lane < 16 ? 16 * q + lane : 64 + 16 * q + lane - 16) : r;
         bool ok = true;
         for (int b = 0; b < nsb; ++b) {
             const int rs = b % NR, as = b % kTaNA;
@@ -805,7 +807,7 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
                 break;
             }
             tc_fence_after();
-            const uint8_t *rowp = sR + rs * RBYTES + r * WRB;
+            const uint8_t *rowp = sR + rs * RBYTES + srow * WRB;
             const uint4 hd = FMT == kQ4_K ? *reinterpret_cast<const uint4 *>(rowp) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
@@ -833,24 +835,20 @@ __global__ void __launch_bounds__(kTaThreads, 1) gemm_ta_kernel(const __grid_con
             uint32_t v[32];
             tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col0, v);
             if (EPI == kGemmSwiglu) {
-                // up rows (TMEM lanes 64..127) hand their values to the gate rows (lanes 0..63)
-                float *su = sU + hf * (64 * 33);
-                if (q >= 2)
+                // lanes l and l ^ 16 hold the gate and up sums of output column n0 + 16q + (l & 15):
+                // one exchange, then lanes 0-15 finish tokens col0 .. +15 and lanes 16-31 the rest
+                const int n = n0 + 16 * q + (lane & 15);
+                const bool up = lane >= 16;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) su[(r - 64) * 33 + i] = __uint_as_float(v[i]);
-                named_bar_sync(1, 256);
-                if (q < 2 && ok) {
-                    const int n = n0 + r;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int t = m0 + col0 + i;
-                        if (t < a.M && n < a.N) {
-                            const float sc = a.rinv[t];
-                            a.y[(size_t)t * a.y_stride + n] = silu_mul(__uint_as_float(v[i]) * sc, su[r * 33 + i] * sc);
-                        }
+                for (int i = 0; i < 32; ++i) {
+                    const float mine = __uint_as_float(v[i]);
+                    const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
+                    const int t = m0 + col0 + i;
+                    if (ok && (i >= 16) == up && t < a.M && n < a.N) {
+                        const float sc = a.rinv[t];
+                        a.y[(size_t)t * a.y_stride + n] = silu_mul((up ? other : mine) * sc, (up ? mine : other) * sc);
                     }
                 }
-                named_bar_sync(1, 256);
             } else if (ok) {
                 const int n = n0 + r;
                 if (n < a.N) {
