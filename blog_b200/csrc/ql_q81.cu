@@ -358,6 +358,159 @@ int q81_mm_row_pitch(size_t row_bytes) {
 }
 
 namespace {
+// Staged variant (in_dim a multiple of 128): 8 warps, warps w and w + 4 share slab w and split the
+// K range; each half streams its 128-element activation chunks (64 tokens x 144 bytes: 4 plain blocks
+// or one MMQ group, 16-byte aligned) into shared memory with cp.async, double-buffered, so the B
+// fragments come from shared memory (token records 144 B apart: the 8 tokens x 4 lanes of a load hit
+// 32 distinct banks) instead of an L2 round trip per token tile; the halves' sums meet in shared memory.
+constexpr int kMmsThreads = 256;
+constexpr int kChunk = 64 * 144;  // one activation chunk: 64 tokens x 128 activations
+
+__device__ __forceinline__ void cp_async16_cg(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+template <int FMT, bool MMQ>
+__global__ void __launch_bounds__(kMmsThreads, 1) q81_matmul_staged_kernel(const __grid_constant__ Q81MmArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint64_t bar[4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int slab_i = warp & 3, kh = warp >> 2, gtid = threadIdx.x & 127;
+    const int wrow0 = blockIdx.x * 64 + 16 * slab_i, tok0 = blockIdx.y * kMmTokens;
+    int nr = min(16, a.out_dim - wrow0);
+    const int P = a.row_pitch, bpr = a.in_dim / 32, nch = bpr / 4;
+    uint8_t *slab = smem + (size_t)slab_i * 16 * P;
+    uint8_t *act = smem + (size_t)64 * P + (size_t)kh * 2 * kChunk;  // this half's two chunk buffers
+    const uint8_t *wbase = a.w + (size_t)wrow0 * a.rb;
+    uintptr_t lo = 0, hi = 0, end = 0;
+    if (kh == 0 && nr > 0) {
+        if (lane < nr) {
+            const uintptr_t st = reinterpret_cast<uintptr_t>(wbase + (size_t)lane * a.rb);
+            lo = st & ~uintptr_t(15);
+            end = st + a.rb;
+            hi = end & ~uintptr_t(15);
+        }
+        const uint32_t tx = __reduce_add_sync(0xffffffffu, (uint32_t)(hi - lo));
+        if (lane == 0) {
+            mbar_init(&bar[slab_i], 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            mbar_arrive_expect_tx(&bar[slab_i], tx);
+        }
+    }
+    __syncthreads();  // the slab barriers exist before the other half waits on them
+    if (kh == 0 && lane < nr) {
+        uint8_t *dst = slab + (size_t)lane * P;
+        if (hi > lo)
+            bulk_g2s(dst, reinterpret_cast<const void *>(lo), (uint32_t)(hi - lo), &bar[slab_i], l2_evict_first_policy());
+        for (uintptr_t q = hi; q < end; ++q) dst[q - lo] = *reinterpret_cast<const uint8_t *>(q);
+    }
+    // this half's chunks [c0, c1) (Q4_K: whole super-blocks of 2 chunks)
+    const int unit = FMT == kQ4_K || FMT == kQ6_K ? 2 : 1;
+    const int cmid = (nch / unit) / 2 * unit, c0 = kh ? cmid : 0, c1 = kh ? nch : cmid;
+    const size_t xrb = (size_t)bpr * 36;
+    auto issue = [&](int ch, int buf) {
+        uint8_t *dstb = act + (size_t)buf * kChunk;
+        for (int i = gtid; i < 64 * 9; i += 128) {
+            const int slot = i / 9, piece = i - slot * 9, tok = min(tok0 + slot, a.m - 1);
+            const uint8_t *src = MMQ ? a.xq + ((size_t)ch * a.m + tok) * 144 : a.xq + (size_t)tok * xrb + (size_t)ch * 144;
+            cp_async16_cg(dstb + slot * 144 + 16 * piece, src + 16 * piece);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (c0 < c1) issue(c0, 0);
+    __syncthreads();  // the tails' plain stores, for both halves
+    if (nr > 0 && !mbar_wait(&bar[slab_i], 0u, a.err, kErrWaitFull)) {
+        mbar_wait(&bar[slab_i], 0u, nullptr, 0);  // never leave with the copies in flight
+        nr = 0;
+    }
+    const int sh0 = (int)(reinterpret_cast<uintptr_t>(wbase + (size_t)g * a.rb) & 15);
+    const int sh1 = (int)(reinterpret_cast<uintptr_t>(wbase + (size_t)(g + 8) * a.rb) & 15);
+    const uint8_t *row0 = slab + (size_t)g * P + sh0, *row1 = slab + (size_t)(g + 8) * P + sh1;
+    const int ntile = (min(kMmTokens, a.m - tok0) + 7) >> 3;
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int ch = c0; ch < c1; ++ch) {
+        if (ch + 1 < c1) issue(ch + 1, (ch + 1 - c0) & 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // chunk ch has landed
+        named_bar_sync(1 + kh, 128);
+        const uint8_t *buf = act + (size_t)((ch - c0) & 1) * kChunk;
+        if (nr > 0) {
+#pragma unroll
+            for (int bi = 0; bi < 4; ++bi) {
+                const int b = 4 * ch + bi;
+                MmBlock blk;
+                mm_decode<FMT>(row0, row1, b, c, blk);
+                const int8_t *scl[2] = {nullptr, nullptr};
+                if (FMT == kQ6_K) {
+                    const int sb = b >> 3, sub = b & 7, hf = sub >> 2, grp = sub & 3;
+                    scl[0] = reinterpret_cast<const int8_t *>(row0 + 210 * sb + 192) + 8 * hf + 2 * grp;
+                    scl[1] = reinterpret_cast<const int8_t *>(row1 + 210 * sb + 192) + 8 * hf + 2 * grp;
+                }
+                const int qoff = MMQ ? 16 + 32 * bi : 36 * bi + 4, doff = MMQ ? 4 * bi : 36 * bi;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (j < ntile) {
+                        const uint8_t *rb_ = buf + (8 * j + g) * 144 + qoff;
+                        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(rb_ + 4 * c);
+                        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(rb_ + 16 + 4 * c);
+                        float dx[2], sx[2];
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            const uint32_t ds = *reinterpret_cast<const uint32_t *>(buf + (8 * j + 2 * c + q) * 144 + doff);
+                            dx[q] = half_bits_to_float(ds);
+                            sx[q] = half_bits_to_float(ds >> 16);
+                        }
+                        if (FMT == kQ6_K) {
+                            int t0v[4] = {0, 0, 0, 0}, t1v[4] = {0, 0, 0, 0};
+                            imma_k16(t0v, blk.a[0], blk.a[1], b0);
+                            imma_k16(t1v, blk.a[2], blk.a[3], b1);
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const int h = q >> 1;
+                                acc[j][q] = fmaf(blk.s[h][0] * dx[q & 1],
+                                                 (float)scl[h][0] * (float)t0v[q] + (float)scl[h][1] * (float)t1v[q],
+                                                 acc[j][q]);
+                            }
+                        } else {
+                            int t[4] = {0, 0, 0, 0};
+                            imma_k32(t, blk.a, b0, b1);
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const int h = q >> 1;
+                                acc[j][q] = fmaf(blk.s[h][0] * dx[q & 1], (float)t[q], acc[j][q]);
+                                if (FMT == kQ4_K) acc[j][q] -= blk.s[h][1] * sx[q & 1];
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        named_bar_sync(1 + kh, 128);  // this buffer is refilled two chunks later
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // both halves done with their chunk buffers: they now hold the second half's sums
+    float *red = reinterpret_cast<float *>(smem + (size_t)64 * P);  // [4 slabs][32 lanes][32]
+    if (kh) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) red[(slab_i * 32 + lane) * 32 + 4 * j + q] = acc[j][q];
+    }
+    __syncthreads();
+    if (!kh && nr > 0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int tok = tok0 + 8 * j + 2 * c + (q & 1), r = g + 8 * (q >> 1);
+                if (j < ntile && tok < a.m && r < nr)
+                    a.y[(size_t)tok * a.out_dim + wrow0 + r] = acc[j][q] + red[(slab_i * 32 + lane) * 32 + 4 * j + q];
+            }
+    }
+}
+
 template <int FMT, bool MMQ>
 cudaError_t mm_launch_t(const Q81MmArgs &a, size_t smem, dim3 grid, cudaStream_t s) {
     cudaError_t e =
@@ -366,22 +519,33 @@ cudaError_t mm_launch_t(const Q81MmArgs &a, size_t smem, dim3 grid, cudaStream_t
     q81_matmul_kernel<FMT, MMQ><<<grid, kMmThreads, smem, s>>>(a);
     return cudaGetLastError();
 }
+template <int FMT, bool MMQ>
+cudaError_t mms_launch_t(const Q81MmArgs &a, size_t smem, dim3 grid, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(q81_matmul_staged_kernel<FMT, MMQ>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    q81_matmul_staged_kernel<FMT, MMQ><<<grid, kMmsThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
 template <bool MMQ>
-cudaError_t mm_launch_fmt(int fmt, const Q81MmArgs &a, size_t smem, dim3 grid, cudaStream_t s) {
+cudaError_t mm_launch_fmt(int fmt, const Q81MmArgs &a, size_t smem, dim3 grid, bool staged, cudaStream_t s) {
     switch (fmt) {
-    case kQ4_K: return mm_launch_t<kQ4_K, MMQ>(a, smem, grid, s);
-    case kQ6_K: return mm_launch_t<kQ6_K, MMQ>(a, smem, grid, s);
-    case kQ5_0: return mm_launch_t<kQ5_0, MMQ>(a, smem, grid, s);
-    case kQ8_0: return mm_launch_t<kQ8_0, MMQ>(a, smem, grid, s);
+    case kQ4_K: return staged ? mms_launch_t<kQ4_K, MMQ>(a, smem, grid, s) : mm_launch_t<kQ4_K, MMQ>(a, smem, grid, s);
+    case kQ6_K: return staged ? mms_launch_t<kQ6_K, MMQ>(a, smem, grid, s) : mm_launch_t<kQ6_K, MMQ>(a, smem, grid, s);
+    case kQ5_0: return staged ? mms_launch_t<kQ5_0, MMQ>(a, smem, grid, s) : mm_launch_t<kQ5_0, MMQ>(a, smem, grid, s);
+    case kQ8_0: return staged ? mms_launch_t<kQ8_0, MMQ>(a, smem, grid, s) : mm_launch_t<kQ8_0, MMQ>(a, smem, grid, s);
     default: return cudaErrorInvalidValue;
     }
 }
 }  // namespace
 
 cudaError_t matmul_q81_launch(int fmt, const Q81MmArgs &a, bool mmq, cudaStream_t s) {
-    const size_t smem = (size_t)4 * 16 * a.row_pitch;
+    const size_t wsm = (size_t)4 * 16 * a.row_pitch;
+    const size_t ssm = wsm + 4 * (size_t)kChunk;  // + two chunk buffers per K half (also the halves' sums)
+    const bool staged = a.in_dim % 128 == 0 && ssm <= 232448 - 1024;
+    const size_t smem = staged ? ssm : wsm;
     const dim3 grid((a.out_dim + 63) / 64, (a.m + kMmTokens - 1) / kMmTokens);
-    return mmq ? mm_launch_fmt<true>(fmt, a, smem, grid, s) : mm_launch_fmt<false>(fmt, a, smem, grid, s);
+    return mmq ? mm_launch_fmt<true>(fmt, a, smem, grid, staged, s) : mm_launch_fmt<false>(fmt, a, smem, grid, staged, s);
 }
 
 size_t q81_row_bytes(int in_dim) { return (size_t)((in_dim + 31) / 32) * 36; }
