@@ -1423,7 +1423,12 @@ def main():
         line = {
             "metric": METRIC, "value": toks, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r1["ms"], "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "vs_baseline": None, "dtype": "int8" if r1["chain"] else "f32",
+            "dtype_detail": ("Q4_K nibbles (u8) x activations as 21-bit fixed point in three s8 limbs per "
+                             "256-element block on mma.sync m16n8k32 (s32 sums), block scales and sums in fp32, "
+                             "the fused MLP's residual in 64-bit fixed point; within 1e-5 of the fp32 oracle"
+                             if r1["chain"] else "fp32 activations, exact block decode, fp32 accumulation"),
+            "data": "synthetic",
             "config": bench_config(args.batch, world),
             "hbm_roofline_tokens_per_s": hbm * 1e9 / (total_bytes / world),
             "step_weight_GBps": total_bytes / (r1["ms"] / 1e3) / 1e9,
