@@ -874,8 +874,7 @@ class MoEStack:
         self.h_in = torch.randn((T, DS_H), generator=g).to("cuda")
         self.h = torch.zeros((T, DS_H), device="cuda")
         self.xn = torch.zeros((T, DS_H), device="cuda")
-        self.q = torch.zeros((T, 3072), device="cuda")
-        self.kva = torch.zeros((T, 576), device="cuda")
+        self.qkva = torch.zeros((T, 3072 + 576), device="cuda")
         self.kvb = torch.zeros((T, 4096), device="cuda")
         self.act = torch.zeros((T, max(DS_DENSE, DS_SHARED)), device="cuda")
         self.eact = torch.zeros((T, DS_TOPK, DS_FE), device="cuda")
@@ -924,14 +923,13 @@ class MoEStack:
         self.h.copy_(self.h_in)
         h = self.h.data_ptr()
         for li, L in enumerate(self.layers):
-            # attention stand-in: the MLA projections (fused RMSNorm on q and kv_a)
-            Q.quant_gemv_ex(QK, L["wq"].data_ptr(), rbh, h, DS_H, self.q.data_ptr(), 3072, 3072, DS_H, T,
-                            L["ln1"].data_ptr(), EPS)
-            Q.quant_gemv_ex(QK, L["wkva"].data_ptr(), rbh, h, DS_H, self.kva.data_ptr(), 576, 576, DS_H, T,
-                            L["ln1"].data_ptr(), EPS)
-            Q.quant_gemv_ex(QK, L["wkvb"].data_ptr(), Q.row_bytes(QK, 512), self.kva.data_ptr(), 576,
+            # attention stand-in: the MLA projections; q and kv_a share the normalised input, so they
+            # are one stacked call (fused RMSNorm) into [T][3072 | 576]
+            Q.quant_gemv_stacked_ex(QK, [L["wq"].data_ptr(), L["wkva"].data_ptr()], [rbh, rbh], [3072, 576], h, DS_H,
+                                    self.qkva.data_ptr(), 3648, DS_H, T, L["ln1"].data_ptr(), EPS)
+            Q.quant_gemv_ex(QK, L["wkvb"].data_ptr(), Q.row_bytes(QK, 512), self.qkva.data_ptr() + 4 * 3072, 3648,
                             self.kvb.data_ptr(), 4096, 4096, 512, T)
-            Q.quant_gemv_ex(QK, L["wo"].data_ptr(), rbh, self.q.data_ptr(), 3072, h, DS_H, DS_H, DS_H, T,
+            Q.quant_gemv_ex(QK, L["wo"].data_ptr(), rbh, self.qkva.data_ptr(), 3648, h, DS_H, DS_H, DS_H, T,
                             accumulate=True)
             if li == 0:
                 Q.quant_swiglu_ex(QK, L["wg"].data_ptr(), L["wu"].data_ptr(), rbh, rbh, h, DS_H, self.act.data_ptr(),
