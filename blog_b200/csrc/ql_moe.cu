@@ -15,17 +15,18 @@
 //   5. moe_combine_kernel: out[t, h] += sum over t's routes in route order (fmaf(y, w, total)),
 //      the reference combine's order.
 //
-// Weight rows stream into shared memory as one contiguous range per warp (16 rows of one
-// expert are adjacent in memory): a 1-D bulk copy (TMA engine) from the 16-byte boundary at or
-// before the first byte, plus plain loads of the last < 16 bytes.  This works for any row
-// length, including the 32-element formats whose rows are not 16-byte multiples (Q5_0 with
-// K = 1408: 968 B rows).  Each thread decodes its MMA A fragment straight from the raw bytes in
-// shared memory (no dequantized tile): mma.sync m16n8k16 with the k order of the activation
-// layout (elements 0, 2, 1, 3 | 4, 6, 5, 7 of each group of 8), so lane (g, c) of a 16-element
-// step needs quants 4c..4c+3 of rows g and g + 8: one 32-bit word of nibbles per row, masked
-// into exact integer f16 pairs with the magic-number conversion.  Tokens are the MMA's n = 8
-// columns, up to 32 per pass over the staged rows (decode at batch 64: ~6 tokens per expert,
-// one n-tile).
+// Weight rows stream into shared memory one row per bulk copy (TMA engine), from the 16-byte
+// boundary at or before the row's first byte plus plain loads of its last < 16 bytes, into slots
+// whose pitch is 16 mod 32 bytes (the 8 rows a lane quad reads at once fall in distinct banks).
+// This works for any row length, including the 32-element formats whose rows are not 16-byte
+// multiples (Q5_0 with K = 1408: 968 B rows).  A CTA has 8 warps: 4 slabs of 16 rows, each slab
+// shared by two warps that take one half of K each (their sums meet in shared memory).  Each thread
+// decodes its MMA A fragment straight from the raw bytes (no dequantized tile): mma.sync m16n8k16
+// with the k order of the activation layout (elements 0, 2, 1, 3 | 4, 6, 5, 7 of each group of 8),
+// so lane (g, c) of a 16-element step needs quants 4c..4c+3 of rows g and g + 8: one 32-bit word of
+// nibbles per row, masked into exact integer f16 pairs with the magic-number conversion.  Tokens are
+// the MMA's n = 8 columns, up to 16 per pass over the staged rows (decode at batch 64: ~6 tokens per
+// expert, one n-tile).
 #include "ql_common.cuh"
 #include "ql_gemm.cuh"
 #include "ql_moe.cuh"
