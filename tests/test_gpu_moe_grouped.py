@@ -179,3 +179,33 @@ def test_grouped_no_routes_and_bad_args():
         Q.moe_down_grouped_accum_ordered(t, dev(d).data_ptr(), 32 * rb, rb, y.data_ptr(), y.data_ptr(), 0, 0,
                                          y.data_ptr(), y.data_ptr(), 32, T, k, 32, K)
     assert e.value.status == Q.QL_EINVAL
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_shards_sum_to_the_full_layer(world):
+    """Expert parallelism as the bench runs it, on one GPU: rank r holds experts [r E / W, (r + 1) E / W)
+    (its packed weights and its expert range), computes the routed SwiGLU and down + ordered combine
+    for all tokens, and the ranks' outputs are summed (the all-reduce).  The sum matches the one-call
+    result over all experts (float reassociation of the per-token route sums only) and the oracle."""
+    E, F, H, T, k = 16, 1408, 2048, 64, 6
+    tg, td = O.Q4_K, O.Q5_0
+    g, u = make_weights(tg, E * F, H, seed=341), make_weights(tg, E * F, H, seed=342)
+    d = make_weights(td, E * H, F, seed=343)
+    rbg, rbd = O.row_bytes(tg, H), O.row_bytes(td, F)
+    x = _x(344, T, H)
+    ids = _routes(345, T, k, E)
+    rw = np.abs(_x(346, T, k)).astype(np.float32)
+    zero = np.zeros((T, H), np.float32)
+    full_act = grouped_swiglu(tg, g, u, F * rbg, rbg, x, ids, 0, E, F, H).reshape(T * k, F)
+    full = grouped_down(td, d, H * rbd, rbd, full_act, ids, 0, E, rw, zero, H, F)
+    total = np.zeros((T, H), np.float64)
+    for r in range(world):
+        e0, e1 = r * E // world, (r + 1) * E // world
+        act = grouped_swiglu(tg, g, u, F * rbg, rbg, x, ids, e0, e1 - e0, F, H).reshape(T * k, F)
+        total += grouped_down(td, d, H * rbd, rbd, act, ids, e0, e1 - e0, rw, zero, H, F)
+    err = rel_l2(total, full)
+    print(f"EP{world} shards summed vs one call over all experts: rel_l2 {err:.2e}")
+    assert err < 1e-6
+    want = oracle_down(td, d, H * rbd, rbd, oracle_swiglu(tg, g, u, F * rbg, rbg, x, ids, 0, E, F, H)
+                       .reshape(T * k, F).astype(np.float32), ids, 0, E, rw, zero, H, F)
+    assert rel_l2(total, want) < FP32_CLASS
