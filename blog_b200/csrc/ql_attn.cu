@@ -7,8 +7,9 @@
 // (Qwen2-7B: 28 / 4) each read the group's keys and values, and one CTA per head leaves most SMs
 // idle.  Here a CTA takes one KV head and one split of the keys (flash-decoding): it loads each
 // 64-key tile of K and V into shared memory once for all the group's query heads, keeps a running
-// max / sum / weighted value per head, and writes them as a partial; a second launch merges the
-// splits (max-rescaled sums) and applies the gate.  The split count follows the cache length (so
+// max / sum / weighted value per head, and writes them as a partial; a second launch (programmatic
+// dependent: placed while the first runs, waiting on it in hardware) merges the splits (max-rescaled
+// sums) and applies the gate.  The split count follows the cache length (so
 // the grid is fixed for a CUDA graph) and each CTA sizes its range from the device-side position.
 #include <cuda_bf16.h>
 
@@ -72,6 +73,7 @@ __device__ __forceinline__ void tile_softmax(float *p_s, float *m_s, float *l_s,
 template <typename KvT>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the merge waits for this grid
     const int hd = a.head_dim, G = a.n_heads / a.kv_heads;
     float *q_s = sm, *acc_s = q_s + G * hd, *k_s = acc_s + G * hd, *v_s = k_s + kAttnTile * (hd + 1);
     float *p_s = v_s + kAttnTile * hd, *m_s = p_s + G * kAttnTile, *l_s = m_s + G, *c_s = l_s + G;
@@ -139,34 +141,79 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_c
     }
 }
 
-// The same for a head_dim known at compile time (64, 128, 256) and groups of <= 16 heads: float4
-// tiles (K rows padded by 4 floats, so the 8 lanes of each 16-byte load phase hit distinct banks),
-// scores with lane = key (4 threads per key: heads g0, g0 + 4, ...), weighted values with thread =
-// (head, 4 dims) accumulating in registers.  Shared memory: q[G][HD] | K[kAttnTile][HD + 4] |
+// Scores of one key row for the heads g0, g0 + 4, ... (NH of them): the key row is read from shared
+// memory once for all of them; per head two accumulators (x, z and y, w lanes of each float4).
+template <int NH, int HD>
+__device__ __forceinline__ void score_heads(const float *q_s, const float *k_s, float *p_s, int jj, int g0, int nt,
+                                            float scale) {
+    constexpr int Q4 = HD / 4, KP = HD + 4;
+    const float4 *kr = reinterpret_cast<const float4 *>(k_s + jj * KP);
+    float d0[NH], d1[NH];
+#pragma unroll
+    for (int h = 0; h < NH; ++h) d0[h] = d1[h] = 0.f;
+#pragma unroll 4
+    for (int c4 = 0; c4 < Q4; ++c4) {
+        const float4 kk = kr[c4];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+            const float4 qq = reinterpret_cast<const float4 *>(q_s + (g0 + 4 * h) * HD)[c4];
+            d0[h] = fmaf(qq.x, kk.x, d0[h]);
+            d1[h] = fmaf(qq.y, kk.y, d1[h]);
+            d0[h] = fmaf(qq.z, kk.z, d0[h]);
+            d1[h] = fmaf(qq.w, kk.w, d1[h]);
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < NH; ++h) p_s[(g0 + 4 * h) * kAttnTile + jj] = jj < nt ? (d0[h] + d1[h]) * scale : -INFINITY;
+}
+
+// The same for a head_dim known at compile time (64, 128, 256) and groups of <= MG heads (8 or 16): float4
+// tiles (K rows padded by 4 floats, so the 8 lanes of each 16-byte load phase hit distinct banks).
+// Scores: thread = key (64 per tile) x head phase g0 (0..3), every head g0 + 4i of the group from one
+// read of the key row.  Weighted values: thread = (key parity, head pair, 4 dims): each V piece read
+// once for two heads, the even and odd keys of a tile summed by different threads (running sums in
+// registers, rescaled per tile) and added at the end.  Shared memory: q[G][HD] | K[kAttnTile][HD + 4] |
 // V[kAttnTile][HD] | p[G][kAttnTile] | m, l, corr[G].
-template <typename KvT, int HD>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_hd_kernel(const __grid_constant__ AttnArgs a) {
+template <typename KvT, int HD, int MG>
+__global__ void __launch_bounds__(kAttnThreads, HD <= 128 ? 2 : 1)
+    attn_split_hd_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
     constexpr int Q4 = HD / 4, KP = HD + 4;
-    constexpr int MAXV = (kAttnMaxGroup * Q4 + kAttnThreads - 1) / kAttnThreads;  // float4 accumulators
+    constexpr int QV = (MG * Q4 + kAttnThreads - 1) / kAttnThreads;  // float4 pieces of q per thread
+    constexpr int GPR = kAttnThreads / 2 / Q4;                       // head pairs per value round
+    constexpr int VR = (MG / 2 + GPR - 1) / GPR;                     // value rounds
+    // the merge kernel may be scheduled now; it waits for this grid before reading the partials
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int G = a.n_heads / a.kv_heads;
     float *q_s = sm, *k_s = q_s + G * HD, *v_s = k_s + kAttnTile * KP, *p_s = v_s + kAttnTile * HD;
     float *m_s = p_s + G * kAttnTile, *l_s = m_s + G, *c_s = l_s + G;
     const int split = blockIdx.x, kh = blockIdx.y, tok = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float scale = rsqrtf((float)HD);
+    // the group's queries (adjacent heads) are loaded before the position is read
+    const size_t q_base = ((size_t)tok * a.n_heads + (size_t)kh * G) * HD;
+    float4 qv[QV];
+#pragma unroll
+    for (int u = 0; u < QV; ++u) {
+        const int i = tid + u * kAttnThreads;
+        if (i < G * Q4) qv[u] = reinterpret_cast<const float4 *>(a.q + q_base)[i];
+    }
     int j0, j1;
     split_range(a, split, tok, j0, j1);
-    const float scale = rsqrtf((float)HD);
-    const size_t q_base = ((size_t)tok * a.n_heads + (size_t)kh * G) * HD;
-    for (int i = tid; i < G * Q4; i += kAttnThreads)
-        reinterpret_cast<float4 *>(q_s)[i] = reinterpret_cast<const float4 *>(a.q + q_base)[i];
+#pragma unroll
+    for (int u = 0; u < QV; ++u) {
+        const int i = tid + u * kAttnThreads;
+        if (i < G * Q4) reinterpret_cast<float4 *>(q_s)[i] = qv[u];
+    }
     if (tid < G) {
         m_s[tid] = -INFINITY;
         l_s[tid] = 0.f;
     }
-    float4 acc[MAXV];
+    // value-phase ownership: key parity vh, head pair vgp + GPR r, dims 4 vc4 .. 4 vc4 + 3
+    const int vh = tid / (kAttnThreads / 2), vgp = (tid % (kAttnThreads / 2)) / Q4, vc4 = tid % Q4;
+    float4 acc[VR][2];
 #pragma unroll
-    for (int u = 0; u < MAXV; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < VR; ++r) acc[r][0] = acc[r][1] = make_float4(0.f, 0.f, 0.f, 0.f);
     __syncthreads();
     // Tile loads: NL 4-element pieces of K and of V per thread, all issued before any is stored; the
     // next tile's pieces are loaded while the current tile computes (registers: 2 x NL pieces).
@@ -207,53 +254,75 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_hd_kernel(const __gri
         __syncthreads();
         if (t0 + kAttnTile < j1) issue(t0 + kAttnTile);  // in flight while this tile computes
         {
-            const int jj = tid & (kAttnTile - 1);
-            const float4 *kr = reinterpret_cast<const float4 *>(k_s + jj * KP);
-            for (int g = tid / kAttnTile; g < G; g += kAttnThreads / kAttnTile) {
-                const float4 *qg = reinterpret_cast<const float4 *>(q_s + g * HD);
-                float d0 = 0.f, d1 = 0.f;
-#pragma unroll 8
-                for (int c4 = 0; c4 < Q4; ++c4) {
-                    const float4 kk = kr[c4], qq = qg[c4];
-                    d0 = fmaf(qq.x, kk.x, d0);
-                    d1 = fmaf(qq.y, kk.y, d1);
-                    d0 = fmaf(qq.z, kk.z, d0);
-                    d1 = fmaf(qq.w, kk.w, d1);
-                }
-                p_s[g * kAttnTile + jj] = jj < nt ? (d0 + d1) * scale : -INFINITY;
+            const int jj = tid & (kAttnTile - 1), g0 = tid / kAttnTile;
+            switch (G > g0 ? (G - g0 + 3) / 4 : 0) {
+                case 1: score_heads<1, HD>(q_s, k_s, p_s, jj, g0, nt, scale); break;
+                case 2: score_heads<2, HD>(q_s, k_s, p_s, jj, g0, nt, scale); break;
+                case 3:
+                    if constexpr (MG > 8) score_heads<3, HD>(q_s, k_s, p_s, jj, g0, nt, scale);
+                    break;
+                case 4:
+                    if constexpr (MG > 8) score_heads<4, HD>(q_s, k_s, p_s, jj, g0, nt, scale);
+                    break;
+                default: break;
             }
         }
         __syncthreads();
         tile_softmax(p_s, m_s, l_s, c_s, G, nt, warp, lane);
         __syncthreads();
 #pragma unroll
-        for (int u = 0; u < MAXV; ++u) {
-            const int i = tid + u * kAttnThreads;
-            if (i < G * Q4) {
-                const int g = i / Q4, c4 = i - g * Q4;
-                const float *pg = p_s + g * kAttnTile;
-                const float cr = c_s[g];
-                float4 r = make_float4(acc[u].x * cr, acc[u].y * cr, acc[u].z * cr, acc[u].w * cr);
-                for (int jj = 0; jj < nt; ++jj) {
-                    const float pv = pg[jj];
-                    const float4 vv = *reinterpret_cast<const float4 *>(v_s + jj * HD + 4 * c4);
-                    r.x = fmaf(pv, vv.x, r.x);
-                    r.y = fmaf(pv, vv.y, r.y);
-                    r.z = fmaf(pv, vv.z, r.z);
-                    r.w = fmaf(pv, vv.w, r.w);
+        for (int r = 0; r < VR; ++r) {
+            const int g = 2 * (vgp + GPR * r);
+            if (g < G) {
+                const int g1 = g + 1 < G ? g + 1 : g;  // an odd group's last pair repeats its head
+                const float *p0 = p_s + g * kAttnTile, *p1 = p_s + g1 * kAttnTile;
+                const float c0 = c_s[g], c1 = c_s[g1];
+                float4 r0 = make_float4(acc[r][0].x * c0, acc[r][0].y * c0, acc[r][0].z * c0, acc[r][0].w * c0);
+                float4 r1 = make_float4(acc[r][1].x * c1, acc[r][1].y * c1, acc[r][1].z * c1, acc[r][1].w * c1);
+#pragma unroll 4
+                for (int jj = vh; jj < nt; jj += 2) {
+                    const float4 vv = *reinterpret_cast<const float4 *>(v_s + jj * HD + 4 * vc4);
+                    const float pa = p0[jj], pb = p1[jj];
+                    r0.x = fmaf(pa, vv.x, r0.x);
+                    r0.y = fmaf(pa, vv.y, r0.y);
+                    r0.z = fmaf(pa, vv.z, r0.z);
+                    r0.w = fmaf(pa, vv.w, r0.w);
+                    r1.x = fmaf(pb, vv.x, r1.x);
+                    r1.y = fmaf(pb, vv.y, r1.y);
+                    r1.z = fmaf(pb, vv.z, r1.z);
+                    r1.w = fmaf(pb, vv.w, r1.w);
                 }
-                acc[u] = r;
+                acc[r][0] = r0;
+                acc[r][1] = r1;
             }
         }
         __syncthreads();
     }
-    const size_t pbase = (((size_t)tok * a.n_heads + (size_t)kh * G) * a.splits + split);
+    // the odd-key sums pass through shared memory (the V tile is free) to the even-key threads
+    float4 *odd = reinterpret_cast<float4 *>(v_s);  // [G][Q4]
+    if (vh == 1) {
 #pragma unroll
-    for (int u = 0; u < MAXV; ++u) {
-        const int i = tid + u * kAttnThreads;
-        if (i < G * Q4) {
-            const int g = i / Q4, c4 = i - g * Q4;
-            *reinterpret_cast<float4 *>(a.part_acc + (pbase + (size_t)g * a.splits) * HD + 4 * c4) = acc[u];
+        for (int r = 0; r < VR; ++r) {
+            const int g = 2 * (vgp + GPR * r);
+            if (g < G) odd[g * Q4 + vc4] = acc[r][0];
+            if (g + 1 < G) odd[(g + 1) * Q4 + vc4] = acc[r][1];
+        }
+    }
+    __syncthreads();
+    const size_t pbase = (((size_t)tok * a.n_heads + (size_t)kh * G) * a.splits + split);
+    if (vh == 0) {
+#pragma unroll
+        for (int r = 0; r < VR; ++r) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int g = 2 * (vgp + GPR * r) + e;
+                if (g < G) {
+                    const float4 o = odd[g * Q4 + vc4];
+                    const float4 t = make_float4(acc[r][e].x + o.x, acc[r][e].y + o.y, acc[r][e].z + o.z,
+                                                 acc[r][e].w + o.w);
+                    *reinterpret_cast<float4 *>(a.part_acc + (pbase + (size_t)g * a.splits) * HD + 4 * vc4) = t;
+                }
+            }
         }
     }
     if (tid < G) {
@@ -269,6 +338,14 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnArgs a) {
     __shared__ float inv_l;
     const int h = blockIdx.x, tok = blockIdx.y, hd = a.head_dim;
     const size_t pbase = ((size_t)tok * a.n_heads + h) * a.splits;
+    const size_t o = ((size_t)tok * a.n_heads + h) * hd;
+    const bool vec = hd % 4 == 0 && hd <= 4 * kAttnThreads;
+    // The gate does not come from the split kernel: its sigmoid is taken before waiting for that
+    // kernel (this launch may start while the split kernel runs; the wait covers its stores).
+    float sg[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec && threadIdx.x < hd / 4)
+        for (int e = 0; e < 4; ++e) sg[e] = 1.0f / (1.0f + expf(-a.gate[o + 4 * threadIdx.x + e]));
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         float m = -INFINITY;
@@ -286,8 +363,7 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnArgs a) {
         if (lane == 0) inv_l = 1.0f / l;
     }
     __syncthreads();
-    const size_t o = ((size_t)tok * a.n_heads + h) * hd;
-    if (hd % 4 == 0 && hd <= 4 * kAttnThreads) {
+    if (vec) {
         // thread = (4 dims, split group): float4 loads over the splits of its group, groups summed
         // through shared memory in a fixed order
         __shared__ float4 red[kAttnThreads];
@@ -315,10 +391,7 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnArgs a) {
                 t.w += u.w;
             }
             const float r[4] = {t.x, t.y, t.z, t.w};
-            for (int e = 0; e < 4; ++e) {
-                const float g = a.gate[o + 4 * threadIdx.x + e];
-                a.attn[o + 4 * threadIdx.x + e] = r[e] * inv_l * (1.0f / (1.0f + expf(-g)));
-            }
+            for (int e = 0; e < 4; ++e) a.attn[o + 4 * threadIdx.x + e] = r[e] * inv_l * sg[e];
         }
         return;
     }
@@ -330,16 +403,21 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnArgs a) {
     }
 }
 
+template <typename KvT, int HD, int MG>
+cudaError_t attn_hd_launch_g(const AttnArgs &a, size_t smem, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(attn_split_hd_kernel<KvT, HD, MG>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attn_split_hd_kernel<KvT, HD, MG><<<dim3(a.splits, a.kv_heads, a.tokens), kAttnThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
 template <typename KvT, int HD>
 cudaError_t attn_hd_launch(const AttnArgs &a, cudaStream_t s) {
     const int G = a.n_heads / a.kv_heads;
     const size_t smem = sizeof(float) * ((size_t)G * HD + (size_t)kAttnTile * (HD + 4) + (size_t)kAttnTile * HD +
                                          (size_t)G * kAttnTile + 3 * (size_t)G);
-    cudaError_t e =
-        cudaFuncSetAttribute(attn_split_hd_kernel<KvT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attn_split_hd_kernel<KvT, HD><<<dim3(a.splits, a.kv_heads, a.tokens), kAttnThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    return G <= 8 ? attn_hd_launch_g<KvT, HD, 8>(a, smem, s) : attn_hd_launch_g<KvT, HD, kAttnMaxGroup>(a, smem, s);
 }
 
 template <typename KvT>
@@ -362,8 +440,18 @@ cudaError_t attn_launch_t(const AttnArgs &a, cudaStream_t s) {
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return e;
-    attn_combine_kernel<<<dim3(a.n_heads, a.tokens), kAttnThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    // the merge is a programmatic dependent launch: its CTAs are placed while the split kernel runs
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(a.n_heads, a.tokens);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_combine_kernel, a);
 }
 }  // namespace
 

@@ -81,10 +81,11 @@ def test_decode_attention_matches_reference_kernel(bf16):
     assert err < TOL
 
 
-@pytest.mark.parametrize("nh,kvh,hd", [(8, 8, 64), (32, 4, 256), (16, 2, 96)])
+@pytest.mark.parametrize("nh,kvh,hd", [(8, 8, 64), (32, 4, 256), (16, 2, 96), (13, 1, 128), (32, 2, 64)])
 def test_decode_attention_batch_and_group_shapes(nh, kvh, hd):
-    """Batched queries (causal: token t sees keys 0..start_pos + t), group sizes 1, 8 and 8 with
-    head_dim 64 / 256 / 96, against the oracle and against the reference's batch kernel."""
+    """Batched queries (causal: token t sees keys 0..start_pos + t), group sizes 1, 8, 8, 13 and 16
+    with head_dim 64 / 256 / 96 / 128 / 64 (groups above 8 take the 16-head kernel variant, an odd
+    group ends on a single-head pair), against the oracle and against the reference's batch kernel."""
     import torch
     tokens, ms, start = 5, 300, 37
     q, gate, k, v = _case(450 + hd, tokens, nh, kvh, hd, ms, False)
