@@ -369,15 +369,29 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnArgs a) {
         __shared__ float4 red[kAttnThreads];
         const int q4 = hd / 4, ng = kAttnThreads / q4;
         const int c4 = threadIdx.x % q4, grp = threadIdx.x / q4;
+        // eight partials' loads in flight per batch, summed in split order
+        constexpr int kBatch = 8;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         if (grp < ng)
-            for (int s = grp; s < a.splits; s += ng) {
-                const float4 v = *reinterpret_cast<const float4 *>(a.part_acc + (pbase + s) * hd + 4 * c4);
-                const float w = w_s[s];
-                acc.x = fmaf(v.x, w, acc.x);
-                acc.y = fmaf(v.y, w, acc.y);
-                acc.z = fmaf(v.z, w, acc.z);
-                acc.w = fmaf(v.w, w, acc.w);
+            for (int s0 = grp; s0 < a.splits; s0 += kBatch * ng) {
+                float4 v[kBatch];
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) {
+                    const int s = s0 + u * ng;
+                    v[u] = s < a.splits ? *reinterpret_cast<const float4 *>(a.part_acc + (pbase + s) * hd + 4 * c4)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) {
+                    const int s = s0 + u * ng;
+                    if (s < a.splits) {
+                        const float w = w_s[s];
+                        acc.x = fmaf(v[u].x, w, acc.x);
+                        acc.y = fmaf(v[u].y, w, acc.y);
+                        acc.z = fmaf(v[u].z, w, acc.z);
+                        acc.w = fmaf(v[u].w, w, acc.w);
+                    }
+                }
             }
         red[threadIdx.x] = acc;
         __syncthreads();
