@@ -346,41 +346,57 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnArgs a) {
     if (vec && threadIdx.x < hd / 4)
         for (int e = 0; e < 4; ++e) sg[e] = 1.0f / (1.0f + expf(-a.gate[o + 4 * threadIdx.x + e]));
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // vector path: thread = (4 dims, split group); eight partials' loads per batch, the first batch in
+    // flight while warp 0 computes the split weights
+    constexpr int kBatch = 8;
+    const int q4 = vec ? hd / 4 : 1, ng = kAttnThreads / q4;
+    const int c4 = threadIdx.x % q4, grp = threadIdx.x / q4;
+    float4 v[kBatch];
+    auto load_batch = [&](int s0) {
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int s = s0 + u * ng;
+            v[u] = s < a.splits ? *reinterpret_cast<const float4 *>(a.part_acc + (pbase + s) * hd + 4 * c4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    if (vec && grp < ng) load_batch(grp);
     if (threadIdx.x < 32) {
+        // each lane's (max, sum) pairs loaded once, all in flight
+        constexpr int kPer = kAttnMaxSplits / 32;
         const int lane = threadIdx.x;
+        float2 ml[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int s = lane + 32 * u;
+            ml[u] = s < a.splits ? reinterpret_cast<const float2 *>(a.part_ml)[pbase + s] : make_float2(-INFINITY, 0.f);
+        }
         float m = -INFINITY;
-        for (int s = lane; s < a.splits; s += 32)
-            if (a.part_ml[(pbase + s) * 2 + 1] > 0.f) m = fmaxf(m, a.part_ml[(pbase + s) * 2]);
+#pragma unroll
+        for (int u = 0; u < kPer; ++u)
+            if (ml[u].y > 0.f) m = fmaxf(m, ml[u].x);
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float l = 0.f;
-        for (int s = lane; s < a.splits; s += 32) {
-            const float ls = a.part_ml[(pbase + s) * 2 + 1];
-            const float w = ls > 0.f ? expf(a.part_ml[(pbase + s) * 2] - m) : 0.f;
-            w_s[s] = w;
-            l += w * ls;
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int s = lane + 32 * u;
+            if (s < a.splits) {
+                const float w = ml[u].y > 0.f ? expf(ml[u].x - m) : 0.f;
+                w_s[s] = w;
+                l += w * ml[u].y;
+            }
         }
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         if (lane == 0) inv_l = 1.0f / l;
     }
     __syncthreads();
     if (vec) {
-        // thread = (4 dims, split group): float4 loads over the splits of its group, groups summed
-        // through shared memory in a fixed order
+        // split groups summed through shared memory in a fixed order
         __shared__ float4 red[kAttnThreads];
-        const int q4 = hd / 4, ng = kAttnThreads / q4;
-        const int c4 = threadIdx.x % q4, grp = threadIdx.x / q4;
-        // eight partials' loads in flight per batch, summed in split order
-        constexpr int kBatch = 8;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         if (grp < ng)
             for (int s0 = grp; s0 < a.splits; s0 += kBatch * ng) {
-                float4 v[kBatch];
-#pragma unroll
-                for (int u = 0; u < kBatch; ++u) {
-                    const int s = s0 + u * ng;
-                    v[u] = s < a.splits ? *reinterpret_cast<const float4 *>(a.part_acc + (pbase + s) * hd + 4 * c4)
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
+                if (s0 != grp) load_batch(s0);
 #pragma unroll
                 for (int u = 0; u < kBatch; ++u) {
                     const int s = s0 + u * ng;
