@@ -25,6 +25,9 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnTile = 64;        // keys per shared-memory tile
 constexpr int kAttnMaxGroup = 16;    // query heads per KV head on the head_dim-specialised kernels
 constexpr int kAttnMaxSplits = 512;  // key splits per (token, KV head)
+// CTAs per SM of the head_dim-specialised split kernel (its launch bound; the host sizes the split
+// count by it): f32 caches with head_dim <= 128 stage tiles with cp.async and fit three.
+constexpr int attn_hd_ctas_per_sm(bool kv_bf16, int hd) { return !kv_bf16 && hd <= 128 ? 3 : hd <= 128 ? 2 : 1; }
 
 template <typename KvT>
 __device__ __forceinline__ float kv_f32(KvT v);
@@ -141,6 +144,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_c
     }
 }
 
+// 16-byte global -> shared copy that bypasses the registers (completion by commit / wait groups).
+__device__ __forceinline__ void attn_cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
 // Scores of one key row for the heads g0, g0 + 4, ... (NH of them): the key row is read from shared
 // memory once for all of them; per head two accumulators (x, z and y, w lanes of each float4).
 template <int NH, int HD>
@@ -175,7 +183,7 @@ __device__ __forceinline__ void score_heads(const float *q_s, const float *k_s, 
 // registers, rescaled per tile) and added at the end.  Shared memory: q[G][HD] | K[kAttnTile][HD + 4] |
 // V[kAttnTile][HD] | p[G][kAttnTile] | m, l, corr[G].
 template <typename KvT, int HD, int MG>
-__global__ void __launch_bounds__(kAttnThreads, HD <= 128 ? 2 : 1)
+__global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) == 2, HD))
     attn_split_hd_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
     constexpr int Q4 = HD / 4, KP = HD + 4;
@@ -215,11 +223,25 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 128 ? 2 : 1)
 #pragma unroll
     for (int r = 0; r < VR; ++r) acc[r][0] = acc[r][1] = make_float4(0.f, 0.f, 0.f, 0.f);
     __syncthreads();
-    // Tile loads: NL 4-element pieces of K and of V per thread, all issued before any is stored; the
-    // next tile's pieces are loaded while the current tile computes (registers: 2 x NL pieces).
+    // Tile loads: NL 4-element pieces of K and of V per thread.  f32 caches with head_dim <= 128
+    // (kAsync): cp.async straight into the tiles, K and V in separate groups, each tile's next contents
+    // issued as soon as its last reader is done (K after the scores, V after the values), so no
+    // registers hold pieces and three CTAs share an SM.  Otherwise: all pieces of a tile loaded into
+    // registers before any is stored, the next tile's in flight while the current one computes.
+    constexpr bool kAsync = sizeof(KvT) == 4 && HD <= 128;
     constexpr int NL = kAttnTile * Q4 / kAttnThreads;
     using Piece = typename std::conditional<sizeof(KvT) == 4, float4, uint2>::type;
-    Piece kp[NL], vp[NL];
+    Piece kp[kAsync ? 1 : NL], vp[kAsync ? 1 : NL];
+    auto copy_rows = [&](float *dst, int pitch, const void *cache, int t0) {
+        const int nt = min(kAttnTile, j1 - t0);
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+            const int i = tid + u * kAttnThreads, jj = i / Q4, c4 = i - jj * Q4;
+            if (jj < nt)
+                attn_cp_async16(dst + jj * pitch + 4 * c4,
+                                static_cast<const float *>(cache) + ((size_t)(t0 + jj) * a.kv_heads + kh) * HD + 4 * c4);
+        }
+    };
     auto issue = [&](int t0) {
         const int nt = min(kAttnTile, j1 - t0);
 #pragma unroll
@@ -240,19 +262,32 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 128 ? 2 : 1)
                                __uint_as_float(p.y << 16), __uint_as_float(p.y & 0xFFFF0000u));
         }
     };
-    if (j0 < j1) issue(j0);
+    if constexpr (kAsync) {
+        if (j0 < j1) copy_rows(k_s, KP, a.key_cache, j0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if (j0 < j1) copy_rows(v_s, HD, a.value_cache, j0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    } else {
+        if (j0 < j1) issue(j0);
+    }
     for (int t0 = j0; t0 < j1; t0 += kAttnTile) {
         const int nt = min(kAttnTile, j1 - t0);
+        if constexpr (kAsync) {
+            asm volatile("cp.async.wait_group 1;" ::: "memory");  // this tile's K (its V may be in flight)
+        } else {
 #pragma unroll
-        for (int u = 0; u < NL; ++u) {
-            const int i = tid + u * kAttnThreads, jj = i / Q4, c4 = i - jj * Q4;
-            if (jj < nt) {
-                *reinterpret_cast<float4 *>(k_s + jj * KP + 4 * c4) = widen(kp[u]);
-                *reinterpret_cast<float4 *>(v_s + jj * HD + 4 * c4) = widen(vp[u]);
+            for (int u = 0; u < NL; ++u) {
+                const int i = tid + u * kAttnThreads, jj = i / Q4, c4 = i - jj * Q4;
+                if (jj < nt) {
+                    *reinterpret_cast<float4 *>(k_s + jj * KP + 4 * c4) = widen(kp[u]);
+                    *reinterpret_cast<float4 *>(v_s + jj * HD + 4 * c4) = widen(vp[u]);
+                }
             }
         }
         __syncthreads();
-        if (t0 + kAttnTile < j1) issue(t0 + kAttnTile);  // in flight while this tile computes
+        if constexpr (!kAsync) {
+            if (t0 + kAttnTile < j1) issue(t0 + kAttnTile);  // in flight while this tile computes
+        }
         {
             const int jj = tid & (kAttnTile - 1), g0 = tid / kAttnTile;
             switch (G > g0 ? (G - g0 + 3) / 4 : 0) {
@@ -268,7 +303,12 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 128 ? 2 : 1)
             }
         }
         __syncthreads();
+        if constexpr (kAsync) {  // the K tile is free: the next tile's keys land during softmax and values
+            if (t0 + kAttnTile < j1) copy_rows(k_s, KP, a.key_cache, t0 + kAttnTile);
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
         tile_softmax(p_s, m_s, l_s, c_s, G, nt, warp, lane);
+        if constexpr (kAsync) asm volatile("cp.async.wait_group 1;" ::: "memory");  // this tile's V
         __syncthreads();
 #pragma unroll
         for (int r = 0; r < VR; ++r) {
@@ -297,7 +337,12 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 128 ? 2 : 1)
             }
         }
         __syncthreads();
+        if constexpr (kAsync) {  // the V tile is free: the next tile's values land during its scores
+            if (t0 + kAttnTile < j1) copy_rows(v_s, HD, a.value_cache, t0 + kAttnTile);
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
     }
+    if constexpr (kAsync) asm volatile("cp.async.wait_group 0;" ::: "memory");  // (only empty groups remain)
     // the odd-key sums pass through shared memory (the V tile is free) to the even-key threads
     float4 *odd = reinterpret_cast<float4 *>(v_s);  // [G][Q4]
     if (vh == 1) {
@@ -491,6 +536,9 @@ size_t attn_smem_bytes(int group, int head_dim) {
                             (size_t)kAttnTile * head_dim + (size_t)group * kAttnTile + 3 * (size_t)group);
 }
 int attn_tile() { return kAttnTile; }
+int attn_ctas_per_sm(bool kv_bf16, int head_dim) {
+    return head_dim == 64 || head_dim == 128 || head_dim == 256 ? attn_hd_ctas_per_sm(kv_bf16, head_dim) : 2;
+}
 int attn_max_splits() { return kAttnMaxSplits; }
 
 cudaError_t attn_launch(const AttnArgs &a, bool kv_bf16, cudaStream_t s) {
