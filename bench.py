@@ -641,8 +641,8 @@ def run_moe_kernel(args):
 
 def run_attn_kernel(args):
     """--kernel-only attn: decode attention of one token at position --tokens - 1 over each of 28
-    layers' KV caches in turn (Qwen2-7B: 28 query heads, 4 KV heads, head_dim 128, f32 caches of
-    --tokens positions; 28 caches exceed the L2), through ql_full_attention_attend, and the
+    layers' KV caches in turn (Qwen2-7B: 28 query heads, 4 KV heads, head_dim 128, f32 caches, or bf16
+    with --kv-bf16, of --tokens positions; 28 caches exceed the L2), through ql_full_attention_attend, and the
     reference's own kernel (oracle/_ref) on the same caches when it is built.  Bytes per call =
     the K and V rows of the window."""
     import torch
@@ -652,13 +652,15 @@ def run_attn_kernel(args):
     Q.set_stream(torch.cuda.current_stream().cuda_stream)
     nh, kvh, hd, ms, nl = N_Q, N_KV, HEAD, args.tokens, LAYERS
     pos = ms - 1
-    caches = [(torch.randn(ms, kvh * hd, device="cuda") * 0.5, torch.randn(ms, kvh * hd, device="cuda"))
-              for _ in range(nl)]
+    bf16 = bool(args.kv_bf16)
+    kdt = torch.bfloat16 if bf16 else torch.float32
+    caches = [((torch.randn(ms, kvh * hd, device="cuda") * 0.5).to(kdt),
+               torch.randn(ms, kvh * hd, device="cuda").to(kdt)) for _ in range(nl)]
     q = torch.randn(nh * hd, device="cuda")
     gate = torch.randn(nh * hd, device="cuda")
     out = torch.empty(nh * hd, device="cuda")
     p = torch.full((1,), pos, dtype=torch.int32, device="cuda")
-    nbytes = 2 * (pos + 1) * kvh * hd * 4
+    nbytes = 2 * (pos + 1) * kvh * hd * (2 if bf16 else 4)
 
     def timed(fn):
         for i in range(max(args.warmup, 3)):
@@ -672,11 +674,12 @@ def run_attn_kernel(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / args.steps * 1e3
     us = timed(lambda i: Q.full_attention_attend(q.data_ptr(), gate.data_ptr(), caches[i][0].data_ptr(),
-                                                 caches[i][1].data_ptr(), False, out.data_ptr(), nh, kvh, hd, ms,
+                                                 caches[i][1].data_ptr(), bf16, out.data_ptr(), nh, kvh, hd, ms,
                                                  p.data_ptr()))
     Q.check_device()
     hbm, _ = peaks()
-    res = {"kernel_only": "attn", "positions": pos + 1, "avg_us": us, "kv_bytes": nbytes,
+    res = {"kernel_only": "attn", "kv_dtype": "bf16" if bf16 else "f32", "positions": pos + 1, "avg_us": us,
+           "kv_bytes": nbytes,
            "GBps": nbytes / us / 1e3, "frac_hbm": nbytes / us / 1e3 / hbm, "launches": Q.last_launch_count()}
     try:
         import oracle as O
@@ -686,8 +689,8 @@ def run_attn_kernel(args):
     if R is not None:
         R.ref_set_stream(torch.cuda.current_stream().cuda_stream)
         rus = timed(lambda i: R.ref_full_attention_attend(q.data_ptr(), gate.data_ptr(), caches[i][0].data_ptr(),
-                                                          caches[i][1].data_ptr(), 0, out.data_ptr(), nh, kvh, hd, ms,
-                                                          p.data_ptr()))
+                                                          caches[i][1].data_ptr(), int(bf16), out.data_ptr(), nh, kvh,
+                                                          hd, ms, p.data_ptr()))
         res["reference_kernel_us"] = rus
     print(json.dumps(res), flush=True)
     return 0
@@ -1169,6 +1172,7 @@ def main():
                     help="time one kernel of the step at its bench shape (profiling target)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens for the prefill_* kernel-only modes")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers for --kernel-only chain")
+    ap.add_argument("--kv-bf16", action="store_true", help="bf16 KV caches for --kernel-only attn")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -26,8 +26,8 @@ constexpr int kAttnTile = 64;        // keys per shared-memory tile
 constexpr int kAttnMaxGroup = 16;    // query heads per KV head on the head_dim-specialised kernels
 constexpr int kAttnMaxSplits = 512;  // key splits per (token, KV head)
 // CTAs per SM of the head_dim-specialised split kernel (its launch bound; the host sizes the split
-// count by it): f32 caches with head_dim <= 128 stage tiles with cp.async and fit three.
-constexpr int attn_hd_ctas_per_sm(bool kv_bf16, int hd) { return !kv_bf16 && hd <= 128 ? 3 : hd <= 128 ? 2 : 1; }
+// count by it): with head_dim <= 128 tiles are staged by cp.async and three fit.
+constexpr int attn_hd_ctas_per_sm(int hd) { return hd <= 128 ? 3 : 1; }
 
 template <typename KvT>
 __device__ __forceinline__ float kv_f32(KvT v);
@@ -149,19 +149,41 @@ __device__ __forceinline__ void attn_cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
+// Shared-memory K/V tiles, read in 4-element pieces as float4.  f32 rows padded by 4 floats (the 8
+// lanes of a 16-byte load phase, reading 8 rows, hit distinct banks); bf16 rows (cp.async-staged, raw)
+// padded by 8 elements, widened on read.
+template <typename TileT, int HD>
+struct AttnTile;
+template <int HD>
+struct AttnTile<float, HD> {
+    static constexpr int kPitch = HD + 4;
+    static __device__ __forceinline__ float4 get4(const float *t, int i) {
+        return *reinterpret_cast<const float4 *>(t + i);
+    }
+};
+template <int HD>
+struct AttnTile<__nv_bfloat16, HD> {
+    static constexpr int kPitch = HD + 8;
+    static __device__ __forceinline__ float4 get4(const __nv_bfloat16 *t, int i) {
+        const uint2 p = *reinterpret_cast<const uint2 *>(t + i);  // bf16: the top 16 bits of an f32
+        return make_float4(__uint_as_float(p.x << 16), __uint_as_float(p.x & 0xFFFF0000u), __uint_as_float(p.y << 16),
+                           __uint_as_float(p.y & 0xFFFF0000u));
+    }
+};
+
 // Scores of one key row for the heads g0, g0 + 4, ... (NH of them): the key row is read from shared
 // memory once for all of them; per head two accumulators (x, z and y, w lanes of each float4).
-template <int NH, int HD>
-__device__ __forceinline__ void score_heads(const float *q_s, const float *k_s, float *p_s, int jj, int g0, int nt,
+template <int NH, int HD, typename TileT>
+__device__ __forceinline__ void score_heads(const float *q_s, const TileT *k_t, float *p_s, int jj, int g0, int nt,
                                             float scale) {
-    constexpr int Q4 = HD / 4, KP = HD + 4;
-    const float4 *kr = reinterpret_cast<const float4 *>(k_s + jj * KP);
+    constexpr int Q4 = HD / 4, KP = AttnTile<TileT, HD>::kPitch;
+    const TileT *kr = k_t + jj * KP;
     float d0[NH], d1[NH];
 #pragma unroll
     for (int h = 0; h < NH; ++h) d0[h] = d1[h] = 0.f;
 #pragma unroll 4
     for (int c4 = 0; c4 < Q4; ++c4) {
-        const float4 kk = kr[c4];
+        const float4 kk = AttnTile<TileT, HD>::get4(kr, 4 * c4);
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
             const float4 qq = reinterpret_cast<const float4 *>(q_s + (g0 + 4 * h) * HD)[c4];
@@ -175,25 +197,33 @@ __device__ __forceinline__ void score_heads(const float *q_s, const float *k_s, 
     for (int h = 0; h < NH; ++h) p_s[(g0 + 4 * h) * kAttnTile + jj] = jj < nt ? (d0[h] + d1[h]) * scale : -INFINITY;
 }
 
-// The same for a head_dim known at compile time (64, 128, 256) and groups of <= MG heads (8 or 16): float4
-// tiles (K rows padded by 4 floats, so the 8 lanes of each 16-byte load phase hit distinct banks).
+// Tile element type of the head_dim-specialised kernel: the cache's own type where tiles are staged
+// by cp.async (head_dim <= 128), f32 (widened through registers) for head_dim 256.
+template <typename KvT, int HD>
+using AttnTileT = typename std::conditional<(HD <= 128), KvT, float>::type;
+
+// The same for a head_dim known at compile time (64, 128, 256) and groups of <= MG heads (8 or 16).
 // Scores: thread = key (64 per tile) x head phase g0 (0..3), every head g0 + 4i of the group from one
 // read of the key row.  Weighted values: thread = (key parity, head pair, 4 dims): each V piece read
 // once for two heads, the even and odd keys of a tile summed by different threads (running sums in
-// registers, rescaled per tile) and added at the end.  Shared memory: q[G][HD] | K[kAttnTile][HD + 4] |
-// V[kAttnTile][HD] | p[G][kAttnTile] | m, l, corr[G].
+// registers, rescaled per tile) and added at the end.  Shared memory: q[G][HD] f32 | K[kAttnTile][pitch] |
+// V[kAttnTile][HD] (tile type) | p[G][kAttnTile] | m, l, corr[G].
 template <typename KvT, int HD, int MG>
-__global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) == 2, HD))
+__global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(HD))
     attn_split_hd_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
-    constexpr int Q4 = HD / 4, KP = HD + 4;
+    using TileT = AttnTileT<KvT, HD>;
+    using Tile = AttnTile<TileT, HD>;
+    constexpr int Q4 = HD / 4, KP = Tile::kPitch;
     constexpr int QV = (MG * Q4 + kAttnThreads - 1) / kAttnThreads;  // float4 pieces of q per thread
     constexpr int GPR = kAttnThreads / 2 / Q4;                       // head pairs per value round
     constexpr int VR = (MG / 2 + GPR - 1) / GPR;                     // value rounds
     // the merge kernel may be scheduled now; it waits for this grid before reading the partials
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int G = a.n_heads / a.kv_heads;
-    float *q_s = sm, *k_s = q_s + G * HD, *v_s = k_s + kAttnTile * KP, *p_s = v_s + kAttnTile * HD;
+    float *q_s = sm;
+    TileT *k_t = reinterpret_cast<TileT *>(q_s + G * HD), *v_t = k_t + kAttnTile * KP;
+    float *p_s = reinterpret_cast<float *>(v_t + kAttnTile * HD);
     float *m_s = p_s + G * kAttnTile, *l_s = m_s + G, *c_s = l_s + G;
     const int split = blockIdx.x, kh = blockIdx.y, tok = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -223,23 +253,24 @@ __global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) 
 #pragma unroll
     for (int r = 0; r < VR; ++r) acc[r][0] = acc[r][1] = make_float4(0.f, 0.f, 0.f, 0.f);
     __syncthreads();
-    // Tile loads: NL 4-element pieces of K and of V per thread.  f32 caches with head_dim <= 128
-    // (kAsync): cp.async straight into the tiles, K and V in separate groups, each tile's next contents
-    // issued as soon as its last reader is done (K after the scores, V after the values), so no
-    // registers hold pieces and three CTAs share an SM.  Otherwise: all pieces of a tile loaded into
-    // registers before any is stored, the next tile's in flight while the current one computes.
-    constexpr bool kAsync = sizeof(KvT) == 4 && HD <= 128;
+    // Tile loads.  head_dim <= 128 (kAsync): 16-byte cp.async chunks straight into the tiles in the
+    // cache's type, K and V in separate groups, each tile's next contents issued as soon as its last
+    // reader is done (K after the scores, V after the values), so no registers hold pieces and three CTAs
+    // share an SM.  head_dim 256: NL 4-element pieces of K and of V per thread loaded into registers
+    // before any is stored (widened to f32), the next tile's in flight while the current one computes.
+    constexpr bool kAsync = HD <= 128;
     constexpr int NL = kAttnTile * Q4 / kAttnThreads;
+    constexpr int CE = 16 / sizeof(TileT), QC = HD / CE, NC = kAttnTile * QC / kAttnThreads;  // chunks
     using Piece = typename std::conditional<sizeof(KvT) == 4, float4, uint2>::type;
     Piece kp[kAsync ? 1 : NL], vp[kAsync ? 1 : NL];
-    auto copy_rows = [&](float *dst, int pitch, const void *cache, int t0) {
+    auto copy_rows = [&](TileT *dst, int pitch, const void *cache, int t0) {
         const int nt = min(kAttnTile, j1 - t0);
 #pragma unroll
-        for (int u = 0; u < NL; ++u) {
-            const int i = tid + u * kAttnThreads, jj = i / Q4, c4 = i - jj * Q4;
+        for (int u = 0; u < NC; ++u) {
+            const int i = tid + u * kAttnThreads, jj = i / QC, c = i - jj * QC;
             if (jj < nt)
-                attn_cp_async16(dst + jj * pitch + 4 * c4,
-                                static_cast<const float *>(cache) + ((size_t)(t0 + jj) * a.kv_heads + kh) * HD + 4 * c4);
+                attn_cp_async16(dst + jj * pitch + CE * c,
+                                static_cast<const TileT *>(cache) + ((size_t)(t0 + jj) * a.kv_heads + kh) * HD + CE * c);
         }
     };
     auto issue = [&](int t0) {
@@ -263,9 +294,9 @@ __global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) 
         }
     };
     if constexpr (kAsync) {
-        if (j0 < j1) copy_rows(k_s, KP, a.key_cache, j0);
+        if (j0 < j1) copy_rows(k_t, KP, a.key_cache, j0);
         asm volatile("cp.async.commit_group;" ::: "memory");
-        if (j0 < j1) copy_rows(v_s, HD, a.value_cache, j0);
+        if (j0 < j1) copy_rows(v_t, HD, a.value_cache, j0);
         asm volatile("cp.async.commit_group;" ::: "memory");
     } else {
         if (j0 < j1) issue(j0);
@@ -279,8 +310,10 @@ __global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) 
             for (int u = 0; u < NL; ++u) {
                 const int i = tid + u * kAttnThreads, jj = i / Q4, c4 = i - jj * Q4;
                 if (jj < nt) {
-                    *reinterpret_cast<float4 *>(k_s + jj * KP + 4 * c4) = widen(kp[u]);
-                    *reinterpret_cast<float4 *>(v_s + jj * HD + 4 * c4) = widen(vp[u]);
+                    if constexpr (!kAsync) {  // f32 tiles
+                        *reinterpret_cast<float4 *>(k_t + jj * KP + 4 * c4) = widen(kp[u]);
+                        *reinterpret_cast<float4 *>(v_t + jj * HD + 4 * c4) = widen(vp[u]);
+                    }
                 }
             }
         }
@@ -291,20 +324,20 @@ __global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) 
         {
             const int jj = tid & (kAttnTile - 1), g0 = tid / kAttnTile;
             switch (G > g0 ? (G - g0 + 3) / 4 : 0) {
-                case 1: score_heads<1, HD>(q_s, k_s, p_s, jj, g0, nt, scale); break;
-                case 2: score_heads<2, HD>(q_s, k_s, p_s, jj, g0, nt, scale); break;
+                case 1: score_heads<1, HD>(q_s, k_t, p_s, jj, g0, nt, scale); break;
+                case 2: score_heads<2, HD>(q_s, k_t, p_s, jj, g0, nt, scale); break;
                 case 3:
-                    if constexpr (MG > 8) score_heads<3, HD>(q_s, k_s, p_s, jj, g0, nt, scale);
+                    if constexpr (MG > 8) score_heads<3, HD>(q_s, k_t, p_s, jj, g0, nt, scale);
                     break;
                 case 4:
-                    if constexpr (MG > 8) score_heads<4, HD>(q_s, k_s, p_s, jj, g0, nt, scale);
+                    if constexpr (MG > 8) score_heads<4, HD>(q_s, k_t, p_s, jj, g0, nt, scale);
                     break;
                 default: break;
             }
         }
         __syncthreads();
         if constexpr (kAsync) {  // the K tile is free: the next tile's keys land during softmax and values
-            if (t0 + kAttnTile < j1) copy_rows(k_s, KP, a.key_cache, t0 + kAttnTile);
+            if (t0 + kAttnTile < j1) copy_rows(k_t, KP, a.key_cache, t0 + kAttnTile);
             asm volatile("cp.async.commit_group;" ::: "memory");
         }
         tile_softmax(p_s, m_s, l_s, c_s, G, nt, warp, lane);
@@ -321,7 +354,7 @@ __global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) 
                 float4 r1 = make_float4(acc[r][1].x * c1, acc[r][1].y * c1, acc[r][1].z * c1, acc[r][1].w * c1);
 #pragma unroll 4
                 for (int jj = vh; jj < nt; jj += 2) {
-                    const float4 vv = *reinterpret_cast<const float4 *>(v_s + jj * HD + 4 * vc4);
+                    const float4 vv = Tile::get4(v_t, jj * HD + 4 * vc4);
                     const float pa = p0[jj], pb = p1[jj];
                     r0.x = fmaf(pa, vv.x, r0.x);
                     r0.y = fmaf(pa, vv.y, r0.y);
@@ -338,13 +371,13 @@ __global__ void __launch_bounds__(kAttnThreads, attn_hd_ctas_per_sm(sizeof(KvT) 
         }
         __syncthreads();
         if constexpr (kAsync) {  // the V tile is free: the next tile's values land during its scores
-            if (t0 + kAttnTile < j1) copy_rows(v_s, HD, a.value_cache, t0 + kAttnTile);
+            if (t0 + kAttnTile < j1) copy_rows(v_t, HD, a.value_cache, t0 + kAttnTile);
             asm volatile("cp.async.commit_group;" ::: "memory");
         }
     }
     if constexpr (kAsync) asm volatile("cp.async.wait_group 0;" ::: "memory");  // (only empty groups remain)
     // the odd-key sums pass through shared memory (the V tile is free) to the even-key threads
-    float4 *odd = reinterpret_cast<float4 *>(v_s);  // [G][Q4]
+    float4 *odd = reinterpret_cast<float4 *>(v_t);  // [G][Q4] (G HD floats fit in the V tile)
     if (vh == 1) {
 #pragma unroll
         for (int r = 0; r < VR; ++r) {
@@ -490,8 +523,9 @@ cudaError_t attn_hd_launch_g(const AttnArgs &a, size_t smem, cudaStream_t s) {
 template <typename KvT, int HD>
 cudaError_t attn_hd_launch(const AttnArgs &a, cudaStream_t s) {
     const int G = a.n_heads / a.kv_heads;
-    const size_t smem = sizeof(float) * ((size_t)G * HD + (size_t)kAttnTile * (HD + 4) + (size_t)kAttnTile * HD +
-                                         (size_t)G * kAttnTile + 3 * (size_t)G);
+    using TileT = AttnTileT<KvT, HD>;
+    const size_t smem = sizeof(float) * ((size_t)G * HD + (size_t)G * kAttnTile + 3 * (size_t)G) +
+                        sizeof(TileT) * ((size_t)kAttnTile * AttnTile<TileT, HD>::kPitch + (size_t)kAttnTile * HD);
     return G <= 8 ? attn_hd_launch_g<KvT, HD, 8>(a, smem, s) : attn_hd_launch_g<KvT, HD, kAttnMaxGroup>(a, smem, s);
 }
 
@@ -537,7 +571,8 @@ size_t attn_smem_bytes(int group, int head_dim) {
 }
 int attn_tile() { return kAttnTile; }
 int attn_ctas_per_sm(bool kv_bf16, int head_dim) {
-    return head_dim == 64 || head_dim == 128 || head_dim == 256 ? attn_hd_ctas_per_sm(kv_bf16, head_dim) : 2;
+    (void)kv_bf16;
+    return head_dim == 64 || head_dim == 128 || head_dim == 256 ? attn_hd_ctas_per_sm(head_dim) : 2;
 }
 int attn_max_splits() { return kAttnMaxSplits; }
 

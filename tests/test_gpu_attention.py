@@ -81,26 +81,29 @@ def test_decode_attention_matches_reference_kernel(bf16):
     assert err < TOL
 
 
+@pytest.mark.parametrize("bf16", [False, True])
 @pytest.mark.parametrize("nh,kvh,hd", [(8, 8, 64), (32, 4, 256), (16, 2, 96), (13, 1, 128), (32, 2, 64)])
-def test_decode_attention_batch_and_group_shapes(nh, kvh, hd):
+def test_decode_attention_batch_and_group_shapes(nh, kvh, hd, bf16):
     """Batched queries (causal: token t sees keys 0..start_pos + t), group sizes 1, 8, 8, 13 and 16
     with head_dim 64 / 256 / 96 / 128 / 64 (groups above 8 take the 16-head kernel variant, an odd
-    group ends on a single-head pair), against the oracle and against the reference's batch kernel."""
+    group ends on a single-head pair; head_dim <= 128 stages tiles by cp.async, 256 through
+    registers), f32 and bf16 caches, against the oracle and against the reference's batch kernel."""
     import torch
     tokens, ms, start = 5, 300, 37
-    q, gate, k, v = _case(450 + hd, tokens, nh, kvh, hd, ms, False)
+    q, gate, k, v = _case(450 + hd, tokens, nh, kvh, hd, ms, bf16)
     out = torch.full((tokens, nh * hd), float("nan"), device="cuda:0")
     Q.full_attention_attend_batch(dev(q).data_ptr(), dev(gate).data_ptr(), dev(k).data_ptr(), dev(v).data_ptr(),
-                                  False, out.data_ptr(), tokens, nh, kvh, hd, ms, start)
+                                  bf16, out.data_ptr(), tokens, nh, kvh, hd, ms, start)
     got = host(out)
-    ref = O.attention_attend(q, gate, k, v, False, tokens, nh, kvh, hd, start)
+    ref = O.attention_attend(q, gate, k, v, bf16, tokens, nh, kvh, hd, start)
     assert rel_l2(got, ref) < TOL
     R = O.ref_lib()
     if R is not None:
         out2 = torch.zeros((tokens, nh * hd), device="cuda:0")
         R.ref_set_stream(torch.cuda.current_stream().cuda_stream)
         R.ref_full_attention_attend_batch(dev(q).data_ptr(), dev(gate).data_ptr(), dev(k).data_ptr(),
-                                          dev(v).data_ptr(), 0, out2.data_ptr(), tokens, nh, kvh, hd, ms, start)
+                                          dev(v).data_ptr(), int(bf16), out2.data_ptr(), tokens, nh, kvh, hd, ms,
+                                          start)
         torch.cuda.synchronize()
         assert rel_l2(got, host(out2)) < TOL
 
