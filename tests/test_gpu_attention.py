@@ -124,6 +124,41 @@ def test_decode_attention_position_is_read_on_the_device():
         assert rel_l2(host(out), O.attention_attend(q, gate, k, v, False, 1, nh, kvh, hd, pos)[0]) < TOL
 
 
+def test_decode_attention_replays_in_a_cuda_graph():
+    """The single-token call (key splits, then the merge as a programmatic dependent launch) captured
+    once in a CUDA graph and replayed with the device position moved between replays, f32 and bf16."""
+    import torch
+    nh, kvh, hd, ms = 28, 4, 128, 512
+    for bf16 in (False, True):
+        q, gate, k, v = _case(480 + int(bf16), 1, nh, kvh, hd, ms, bf16)
+        qd, gd, kd, vd = dev(q), dev(gate), dev(k), dev(v)
+        p = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+        out = torch.empty(nh * hd, device="cuda:0")
+
+        def call():
+            Q.full_attention_attend(qd.data_ptr(), gd.data_ptr(), kd.data_ptr(), vd.data_ptr(), bf16, out.data_ptr(),
+                                    nh, kvh, hd, ms, p.data_ptr())
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                Q.set_stream(s.cuda_stream)
+                p.fill_(3)
+                call()  # workspace sized outside the capture
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    call()
+                for pos in (10, 300, 511):
+                    p.fill_(pos)
+                    g.replay()
+                    torch.cuda.synchronize()
+                    err = rel_l2(host(out), O.attention_attend(q, gate, k, v, bf16, 1, nh, kvh, hd, pos)[0])
+                    assert err < TOL, (bf16, pos, err)
+            del g
+        finally:
+            Q.set_stream(torch.cuda.current_stream().cuda_stream)
+
+
 def test_decode_attention_rejects_bad_shapes():
     import torch
     x = torch.zeros(64, device="cuda:0")
