@@ -570,8 +570,7 @@ size_t attn_smem_bytes(int group, int head_dim) {
                             (size_t)kAttnTile * head_dim + (size_t)group * kAttnTile + 3 * (size_t)group);
 }
 int attn_tile() { return kAttnTile; }
-int attn_ctas_per_sm(bool kv_bf16, int head_dim) {
-    (void)kv_bf16;
+int attn_ctas_per_sm(int head_dim) {
     return head_dim == 64 || head_dim == 128 || head_dim == 256 ? attn_hd_ctas_per_sm(head_dim) : 2;
 }
 int attn_max_splits() { return kAttnMaxSplits; }

@@ -21,7 +21,7 @@ struct AttnArgs {
 
 size_t attn_smem_bytes(int group, int head_dim);
 int attn_tile();
-int attn_ctas_per_sm(bool kv_bf16, int head_dim);  // resident split CTAs per SM
+int attn_ctas_per_sm(int head_dim);  // resident split CTAs per SM
 int attn_max_splits();
 cudaError_t attn_launch(const AttnArgs &a, bool kv_bf16, cudaStream_t s);
 

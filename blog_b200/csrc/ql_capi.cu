@@ -1128,7 +1128,7 @@ int attention(const float *q, const float *gate, const void *kc, const void *vc,
     // depend on the position, so a captured launch replays for any position)
     const int keys = pos_dev != nullptr ? max_seq_len : std::min(max_seq_len, start_pos + tokens);
     const int by_len = (keys + attn_tile() - 1) / attn_tile();
-    const int by_sms = std::max(1, attn_ctas_per_sm(kv_bf16 != 0, head_dim) * ws->sms / (kv_heads * tokens));
+    const int by_sms = std::max(1, attn_ctas_per_sm(head_dim) * ws->sms / (kv_heads * tokens));
     const int splits = std::max(1, std::min(std::min(by_len, by_sms), attn_max_splits()));
     const size_t per = (size_t)tokens * n_heads * splits;
     const size_t acc_off = (per * 2 + 3) & ~size_t(3);  // the accumulators start on 16 bytes (float4 stores)
